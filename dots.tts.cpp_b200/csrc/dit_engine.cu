@@ -1,0 +1,645 @@
+// DiT flow-matching velocity head on sm_100a, behind the C ABI in dtts.h.
+//
+// Per velocity forward over `rows` sequences of L tokens (M = rows * L):
+//   adaLN GEMM    a = SiLU(c) W_ada^T + b for every block and the output layer
+//                 at once (one GEMM, N = 6144 * n_layers + 2048)
+//   input GEMM    h = x_in W_in^T + b_in                       (fp32 residual)
+//   per block     LN+modulate -> QKV GEMM (+qk-norm, RoPE epilogue) ->
+//                 attention -> O GEMM (+gated residual epilogue) ->
+//                 LN+modulate -> FFN1 GEMM (+GELU-tanh) -> FFN2 GEMM (+gated residual)
+//   output head   LN+modulate + out_proj on the last P tokens of each row
+// The Euler solve wraps it: per step the time MLP, the CFG combine, the Euler
+// update and the coordinate projection of z into the noise tokens, all on the
+// device, and the whole solve is captured once into a CUDA graph.
+#include "kernels.cuh"
+#include "runtime.h"
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+using namespace dtts;
+
+namespace {
+
+constexpr int kAdaPerLayer = 6 * kD;
+constexpr int kBN = 256;
+
+// ---------------------------------------------------------------- host tables
+// RoPE (cos, sin) per token for the half-split rotation of
+// include/dit_manual.h:111-128: theta_d = (1e4^(-2/64))^d advanced by repeated
+// multiplication, angle = pos * theta_d, evaluated with the host's cosf/sinf
+// exactly as the reference does.
+void rope_half_table(const float *pos, int L, std::vector<float2> &tab) {
+    tab.resize((size_t)L * 32);
+    const float ts = powf(10000.0f, -2.0f / 64.0f);
+    for (int t = 0; t < L; t++) {
+        const float p = pos ? pos[t] : (float)t;
+        float theta = 1.0f;
+        for (int d = 0; d < 32; d++) {
+            tab[(size_t)t * 32 + d] = make_float2(cosf(p * theta), sinf(p * theta));
+            theta *= ts;
+        }
+    }
+}
+
+// Sinusoidal time embedding [cos(t f_i) | sin(t f_i)], f_i = exp(-ln(1e4) i / 128)
+// (src/e2e_pipeline_v4.cpp:58-60).
+void sinusoid(float t, float *se) {
+    for (int i = 0; i < 128; i++) {
+        const float f = expf(-logf(10000.0f) * (float)i / 128.0f);
+        se[i] = cosf(t * f);
+        se[128 + i] = sinf(t * f);
+    }
+}
+
+// Attention mask of the FM sequence (src/e2e_pipeline_v4.cpp:120-146): causal
+// history, the last history block and the latent queries see all history and
+// all latents, padding positions only themselves.
+void fm_mask(uint8_t *mask, int total, int fm_len, int patch, int hidden_patch) {
+    const int latent_start = total - patch;
+    const int block_start = fm_len > hidden_patch ? fm_len - hidden_patch : 0;
+    std::memset(mask, 0, (size_t)total * total);
+    for (int i = 0; i < block_start; i++)
+        for (int j = 0; j <= i; j++) mask[(size_t)i * total + j] = 1;
+    for (int i = block_start; i < fm_len; i++) {
+        for (int j = 0; j < fm_len; j++) mask[(size_t)i * total + j] = 1;
+        for (int j = latent_start; j < total; j++) mask[(size_t)i * total + j] = 1;
+    }
+    for (int i = latent_start; i < total; i++) {
+        for (int j = 0; j < fm_len; j++) mask[(size_t)i * total + j] = 1;
+        for (int j = latent_start; j < total; j++) mask[(size_t)i * total + j] = 1;
+    }
+    for (int i = fm_len; i < latent_start; i++) mask[(size_t)i * total + i] = 1;
+}
+
+// Position ids (src/e2e_pipeline_v4.cpp:149-155).
+void fm_pos(float *pos, int total, int fm_len, int patch) {
+    const int latent_start = total - patch;
+    for (int i = 0; i < fm_len; i++) pos[i] = (float)i;
+    for (int i = latent_start; i < total; i++) pos[i] = (float)(fm_len + i - latent_start);
+    for (int i = fm_len; i < latent_start; i++) pos[i] = 0.0f;
+}
+
+int upload_f32(DeviceArena &a, const float *h, size_t n, float **out, cudaStream_t s) {
+    *out = nullptr;
+    if (!h) return DTTS_OK;
+    void *d = a.alloc(n * sizeof(float));
+    if (!d) { set_error("cudaMalloc of %zu bytes failed", n * sizeof(float)); return DTTS_ERR_OOM; }
+    DTTS_CUDA(cudaMemcpyAsync(d, h, n * sizeof(float), cudaMemcpyHostToDevice, s));
+    *out = static_cast<float *>(d);
+    return DTTS_OK;
+}
+
+// Uploads the row-concatenation of `parts` (each rows_i x cols fp32) as bf16.
+int upload_bf16_concat(DeviceArena &a, const std::vector<std::pair<const float *, size_t>> &parts, size_t cols,
+                       bf16 **out, cudaStream_t s) {
+    size_t rows = 0;
+    for (auto &p : parts) rows += p.second;
+    std::vector<uint16_t> tmp(rows * cols);
+    size_t r0 = 0;
+    for (auto &p : parts) {
+        if (p.first) f32_to_bf16_host(p.first, tmp.data() + r0 * cols, p.second * cols);
+        else std::memset(tmp.data() + r0 * cols, 0, p.second * cols * 2);
+        r0 += p.second;
+    }
+    void *d = a.alloc(tmp.size() * 2);
+    if (!d) { set_error("cudaMalloc of %zu bytes failed", tmp.size() * 2); return DTTS_ERR_OOM; }
+    DTTS_CUDA(cudaMemcpyAsync(d, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice, s));
+    DTTS_CUDA(cudaStreamSynchronize(s));  // tmp goes out of scope
+    *out = static_cast<bf16 *>(d);
+    return DTTS_OK;
+}
+
+GemmOp make_op(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int epi, int *err) {
+    GemmOp op;
+    std::memset(&op, 0, sizeof(op));
+    op.ta = ta;
+    op.tb = tb;
+    op.M = M; op.N = N; op.K = K;
+    op.bn = kBN;
+    op.epi = epi;
+    op.ep.err = err;
+    op.ep.tok_per_row = 1;
+    return op;
+}
+
+}  // namespace
+
+struct dtts_dit {
+    int device = 0, dtype = DTTS_DTYPE_BF16, num_sms = 148;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    DeviceArena wts, ws;
+    int n_layers = 0, n_ada = 0;
+
+    struct Layer {
+        bf16 *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr;
+        float *bo = nullptr, *b1 = nullptr, *b2 = nullptr, *qn = nullptr, *kn = nullptr;
+        CUtensorMap tqkv, to, t1, t2;
+    };
+    std::vector<Layer> layers;
+    bf16 *w_ada = nullptr, *w_in = nullptr;
+    float *b_ada = nullptr, *b_in = nullptr;
+    CUtensorMap t_ada, t_in;
+    float *t_w1 = nullptr, *t_b1 = nullptr, *t_w2 = nullptr, *t_b2 = nullptr;
+    float *spk_w1 = nullptr, *spk_b1 = nullptr, *spk_lw = nullptr, *spk_lb = nullptr;
+    float *out_w = nullptr, *out_b = nullptr, *coord_w = nullptr, *coord_b = nullptr;
+    int *d_err = nullptr;
+
+    // workspace
+    int cap_tok = 0, cap_rows = 0, cap_L = 0, cap_nfe = 0;
+    bf16 *x_in = nullptr, *act = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+         *ffn = nullptr, *a_cond = nullptr;
+    float *h = nullptr, *ada = nullptr, *vel = nullptr, *temb = nullptr, *h1 = nullptr, *spk_c = nullptr,
+          *z = nullptr, *in_a = nullptr, *in_b = nullptr, *cond_f32 = nullptr, *se_tab = nullptr,
+          *spk_in = nullptr;
+    float2 *rope = nullptr;
+    uint8_t *mask = nullptr;
+    CUtensorMap t_x_in, t_act, t_att, t_ffn, t_acond;
+
+    // shapes of the last forward (for profiling) and launch accounting
+    int last_rows = 0, last_L = 0, last_P = 0;
+    bool last_mask = false;
+    int launches = 0;
+
+    // solve graph
+    cudaGraphExec_t gexec = nullptr;
+    std::string gkey;
+
+    ~dtts_dit() {
+        if (gexec) cudaGraphExecDestroy(gexec);
+        ws.free_all();
+        wts.free_all();
+        if (own_stream) cudaStreamDestroy(own_stream);
+    }
+
+    int ensure_workspace(int rows, int L, int nfe);
+    int gemm(const GemmOp &op) {
+        launches++;
+        DTTS_CUDA(launch_gemm(op, num_sms, stream));
+        return DTTS_OK;
+    }
+    int enqueue_forward(int rows, int L, int P);
+    int enqueue_block_op(int kind, int l, int rows, int L);
+    int enqueue_solve(const dtts_solve_args *a);
+    int finish(bool host_wait);
+};
+
+int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
+    const long long tok = (long long)rows * L;
+    if (tok <= cap_tok && rows <= cap_rows && L <= cap_L && nfe <= cap_nfe) return DTTS_OK;
+    if (gexec) { cudaGraphExecDestroy(gexec); gexec = nullptr; gkey.clear(); }
+    DTTS_CUDA(cudaStreamSynchronize(stream));
+    ws.free_all();
+    cap_tok = (int)std::max<long long>(tok, cap_tok);
+    cap_rows = std::max(rows, cap_rows);
+    cap_L = std::max(L, cap_L);
+    cap_nfe = std::max(std::max(nfe, cap_nfe), 1);
+    const size_t T = (size_t)cap_tok, R = (size_t)std::max(cap_rows, 1);
+    auto A = [&](size_t bytes) { return ws.alloc(bytes); };
+    x_in = (bf16 *)A(T * kD * 2);
+    act = (bf16 *)A(T * kD * 2);
+    q = (bf16 *)A(T * kD * 2);
+    k = (bf16 *)A(T * kD * 2);
+    v = (bf16 *)A(T * kD * 2);
+    att = (bf16 *)A(T * kD * 2);
+    ffn = (bf16 *)A(T * kF * 2);
+    h = (float *)A(T * kD * 4);
+    in_a = (float *)A(T * kD * 4);
+    in_b = (float *)A(T * kD * 4);
+    a_cond = (bf16 *)A(R * kD * 2);
+    ada = (float *)A(R * (size_t)n_ada * 4);
+    vel = (float *)A(T * kLat * 4);
+    z = (float *)A(T * kLat * 4);
+    cond_f32 = (float *)A(R * kD * 4);
+    spk_c = (float *)A(R * kD * 4);
+    spk_in = (float *)A(R * kSpk * 4);
+    temb = (float *)A(kD * 4);
+    h1 = (float *)A(kD * 4);
+    se_tab = (float *)A((size_t)cap_nfe * 256 * 4);
+    rope = (float2 *)A((size_t)cap_L * 32 * sizeof(float2));
+    mask = (uint8_t *)A((size_t)cap_L * cap_L);
+    for (void *p : ws.ptrs)
+        if (!p) { set_error("workspace allocation failed (%lld tokens)", tok); cap_tok = cap_rows = cap_L = 0; ws.free_all(); return DTTS_ERR_OOM; }
+    bool ok = make_tmap_bf16(&t_x_in, x_in, T, kD, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
+              make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
+              make_tmap_bf16(&t_acond, a_cond, R, kD, 128);
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace buffer");
+    return DTTS_OK;
+}
+
+// One launch of a per-block operation (used by the forward and by profiling).
+// kind: 0 QKV, 1 O, 2 FFN1, 3 FFN2, 4 attention, 5 LN1, 6 LN2
+int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
+    const int M = rows * L;
+    const Layer &Ly = layers[l];
+    const long long base = (long long)l * kAdaPerLayer;
+    switch (kind) {
+        case 5:
+        case 6: {
+            const long long off = kind == 5 ? 0 : 3 * kD;
+            launches++;
+            launch_ln_modulate(h, act, M, ada + base + off, ada + base + off + kD, n_ada, L, stream);
+            return DTTS_OK;
+        }
+        case 0: {
+            GemmOp op = make_op(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
+            op.ep.q = q; op.ep.k = k; op.ep.v = v;
+            op.ep.ldq = kD; op.ep.ldkv = kD;
+            op.ep.tok_per_row = L; op.ep.kv_cap = L; op.ep.kv_start = 0;
+            op.ep.qk_norm = 1; op.ep.qn = Ly.qn; op.ep.kn = Ly.kn;
+            op.ep.rope = rope; op.ep.rope_mode = ROPE_HALF;
+            return gemm(op);
+        }
+        case 4: {
+            AttnArgs a;
+            a.q = q; a.ldq = kD; a.k = k; a.v = v; a.ldkv = kD; a.o = att; a.ldo = kD;
+            a.rows = rows; a.Tq = L; a.kv_len = L; a.kv_cap = L; a.q_pos0 = 0; a.causal = 0;
+            a.mask = last_mask ? mask : nullptr;
+            a.scale = 1.0f / sqrtf(64.0f);
+            launches++;
+            launch_attention_bf16(a, stream);
+            return DTTS_OK;
+        }
+        case 1: {
+            GemmOp op = make_op(t_att, Ly.to, M, kD, kD, EPI_RESID_GATED, d_err);
+            op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
+            op.ep.gate = ada + base + 2 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = L;
+            return gemm(op);
+        }
+        case 2: {
+            GemmOp op = make_op(t_act, Ly.t1, M, kF, kD, EPI_GELU_BF16, d_err);
+            op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
+            return gemm(op);
+        }
+        case 3: {
+            GemmOp op = make_op(t_ffn, Ly.t2, M, kD, kF, EPI_RESID_GATED, d_err);
+            op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
+            op.ep.gate = ada + base + 5 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = L;
+            return gemm(op);
+        }
+    }
+    set_error("unknown block op %d", kind);
+    return DTTS_ERR_ARG;
+}
+
+// Expects x_in (bf16), a_cond (bf16), rope and mask filled.
+int dtts_dit::enqueue_forward(int rows, int L, int P) {
+    const int M = rows * L;
+    last_rows = rows; last_L = L; last_P = P;
+    {   // adaLN for every block + output layer
+        GemmOp op = make_op(t_acond, t_ada, rows, n_ada, kD, EPI_F32, d_err);
+        op.ep.bias = b_ada; op.ep.out = ada; op.ep.ldo = n_ada;
+        int st = gemm(op);
+        if (st) return st;
+    }
+    {   // input layer
+        GemmOp op = make_op(t_x_in, t_in, M, kD, kD, EPI_F32, d_err);
+        op.ep.bias = b_in; op.ep.out = h; op.ep.ldo = kD;
+        int st = gemm(op);
+        if (st) return st;
+    }
+    static const int order[7] = {5, 0, 4, 1, 6, 2, 3};
+    for (int l = 0; l < n_layers; l++)
+        for (int i = 0; i < 7; i++) {
+            int st = enqueue_block_op(order[i], l, rows, L);
+            if (st) return st;
+        }
+    const long long oo = (long long)n_layers * kAdaPerLayer;
+    launches++;
+    launch_out_head(h, rows, L, P, ada + oo, ada + oo + kD, n_ada, out_w, out_b, vel, d_err, stream);
+    DTTS_CUDA(cudaGetLastError());
+    return DTTS_OK;
+}
+
+int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
+    const int rows = 2 * a->n_utt, L = a->fm_len + a->patch;
+    launches += 2;
+    launch_history_rows(in_a, a->n_utt, a->fm_len, x_in, L, 2, 0, stream);
+    launch_history_rows(in_b, a->n_utt, a->fm_len, x_in, L, 2, 1, stream);
+    if (a->spk) {
+        launches++;
+        launch_speaker_cond(spk_in, a->n_utt, spk_w1, spk_b1, spk_lw, spk_lb, a->spk_scale, spk_c, stream);
+    }
+    const float dt = 1.0f / (float)a->nfe;
+    launches++;
+    launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 0, coord_w, coord_b, x_in, L, stream);
+    for (int step = 0; step < a->nfe; step++) {
+        launches += 3;
+        launch_time_mlp(se_tab + (size_t)step * 256, t_w1, t_b1, t_w2, t_b2, h1, temb, stream);
+        launch_cond_rows(temb, a->spk ? spk_c : nullptr, rows, 2, a_cond, stream);
+        int st = enqueue_forward(rows, L, a->patch);
+        if (st) return st;
+        launches++;
+        launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 1, coord_w, coord_b, x_in, L,
+                         stream);
+    }
+    DTTS_CUDA(cudaGetLastError());
+    return DTTS_OK;
+}
+
+int dtts_dit::finish(bool host_wait) {
+    if (!host_wait) return DTTS_OK;
+    int st = stream_wait(stream, 300.0);
+    if (st) return st;
+    int err = 0;
+    DTTS_CUDA(cudaMemcpy(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        cudaMemset(d_err, 0, sizeof(int));
+        if (err == DEVERR_NONFINITE) { set_error("non-finite velocity"); return DTTS_ERR_NONFINITE; }
+        set_error("device wait limit reached (code %d)", err);
+        return DTTS_ERR_TIMEOUT;
+    }
+    return DTTS_OK;
+}
+
+// =========================================================================
+// C ABI
+// =========================================================================
+extern "C" {
+
+int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit **out) {
+    DTTS_CHECK(w && out, DTTS_ERR_ARG, "null argument");
+    *out = nullptr;
+    DTTS_CHECK(w->n_layers >= 1 && w->n_layers <= 64 && w->blocks, DTTS_ERR_ARG, "n_layers %d invalid", w->n_layers);
+    DTTS_CHECK(dtype == DTTS_DTYPE_BF16, DTTS_ERR_UNSUPPORTED, "DiT dtype %d not supported by this build", dtype);
+    DTTS_CHECK(w->t_w1 && w->t_w2 && w->oada_w && w->out_w && w->in_w && w->coord_w, DTTS_ERR_ARG,
+               "missing a required global DiT weight");
+    for (int l = 0; l < w->n_layers; l++) {
+        const dtts_dit_block_weights &b = w->blocks[l];
+        DTTS_CHECK(b.wq && b.wk && b.wv && b.wo && b.w1 && b.w2 && b.ada_w, DTTS_ERR_ARG,
+                   "missing a required weight in block %d", l);
+    }
+    int nsm = 0;
+    int st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    std::unique_ptr<dtts_dit> e(new dtts_dit());
+    e->device = device; e->dtype = dtype; e->num_sms = nsm; e->n_layers = w->n_layers;
+    DTTS_CUDA(cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking));
+    e->stream = e->own_stream;
+    DTTS_CUDA(gemm_prepare_attributes());
+    cudaStream_t s = e->stream;
+    e->d_err = (int *)e->wts.alloc(sizeof(int));
+    DTTS_CHECK(e->d_err, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemsetAsync(e->d_err, 0, sizeof(int), s));
+
+    e->layers.resize(w->n_layers);
+    for (int l = 0; l < w->n_layers; l++) {
+        const dtts_dit_block_weights &b = w->blocks[l];
+        dtts_dit::Layer &L = e->layers[l];
+        if ((st = upload_bf16_concat(e->wts, {{b.wq, kD}, {b.wk, kD}, {b.wv, kD}}, kD, &L.wqkv, s))) return st;
+        if ((st = upload_bf16_concat(e->wts, {{b.wo, kD}}, kD, &L.wo, s))) return st;
+        if ((st = upload_bf16_concat(e->wts, {{b.w1, kF}}, kD, &L.w1, s))) return st;
+        if ((st = upload_bf16_concat(e->wts, {{b.w2, kD}}, kF, &L.w2, s))) return st;
+        if ((st = upload_f32(e->wts, b.bo, kD, &L.bo, s))) return st;
+        if ((st = upload_f32(e->wts, b.b1, kF, &L.b1, s))) return st;
+        if ((st = upload_f32(e->wts, b.b2, kD, &L.b2, s))) return st;
+        if ((st = upload_f32(e->wts, b.qn, kHD, &L.qn, s))) return st;
+        if ((st = upload_f32(e->wts, b.kn, kHD, &L.kn, s))) return st;
+        bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, kBN) && make_tmap_bf16(&L.to, L.wo, kD, kD, kBN) &&
+                  make_tmap_bf16(&L.t1, L.w1, kF, kD, kBN) && make_tmap_bf16(&L.t2, L.w2, kD, kF, kBN);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for block %d", l);
+    }
+    // adaLN of all blocks followed by the output adaLN: one [n_ada][1024] matrix
+    e->n_ada = w->n_layers * kAdaPerLayer + 2 * kD;
+    {
+        std::vector<std::pair<const float *, size_t>> parts;
+        std::vector<float> bias((size_t)e->n_ada, 0.f);
+        for (int l = 0; l < w->n_layers; l++) {
+            parts.push_back({w->blocks[l].ada_w, (size_t)kAdaPerLayer});
+            if (w->blocks[l].ada_b)
+                std::memcpy(&bias[(size_t)l * kAdaPerLayer], w->blocks[l].ada_b, kAdaPerLayer * 4);
+        }
+        parts.push_back({w->oada_w, (size_t)2 * kD});
+        if (w->oada_b) std::memcpy(&bias[(size_t)w->n_layers * kAdaPerLayer], w->oada_b, 2 * kD * 4);
+        if ((st = upload_bf16_concat(e->wts, parts, kD, &e->w_ada, s))) return st;
+        if ((st = upload_f32(e->wts, bias.data(), bias.size(), &e->b_ada, s))) return st;
+        DTTS_CUDA(cudaStreamSynchronize(s));
+        DTTS_CHECK(make_tmap_bf16(&e->t_ada, e->w_ada, e->n_ada, kD, kBN), DTTS_ERR_CUDA, "tensor map (adaLN)");
+    }
+    if ((st = upload_bf16_concat(e->wts, {{w->in_w, kD}}, kD, &e->w_in, s))) return st;
+    DTTS_CHECK(make_tmap_bf16(&e->t_in, e->w_in, kD, kD, kBN), DTTS_ERR_CUDA, "tensor map (input_layer)");
+    if ((st = upload_f32(e->wts, w->in_b, kD, &e->b_in, s))) return st;
+    if ((st = upload_f32(e->wts, w->t_w1, (size_t)kD * 256, &e->t_w1, s))) return st;
+    if ((st = upload_f32(e->wts, w->t_b1, kD, &e->t_b1, s))) return st;
+    if ((st = upload_f32(e->wts, w->t_w2, (size_t)kD * kD, &e->t_w2, s))) return st;
+    if ((st = upload_f32(e->wts, w->t_b2, kD, &e->t_b2, s))) return st;
+    if ((st = upload_f32(e->wts, w->spk_w1, (size_t)kD * kSpk, &e->spk_w1, s))) return st;
+    if ((st = upload_f32(e->wts, w->spk_b1, kD, &e->spk_b1, s))) return st;
+    if ((st = upload_f32(e->wts, w->spk_ln_w, kD, &e->spk_lw, s))) return st;
+    if ((st = upload_f32(e->wts, w->spk_ln_b, kD, &e->spk_lb, s))) return st;
+    if ((st = upload_f32(e->wts, w->out_w, (size_t)kLat * kD, &e->out_w, s))) return st;
+    if ((st = upload_f32(e->wts, w->out_b, kLat, &e->out_b, s))) return st;
+    if ((st = upload_f32(e->wts, w->coord_w, (size_t)kD * kLat, &e->coord_w, s))) return st;
+    if ((st = upload_f32(e->wts, w->coord_b, kD, &e->coord_b, s))) return st;
+    DTTS_CUDA(cudaStreamSynchronize(s));
+    *out = e.release();
+    return DTTS_OK;
+}
+
+int dtts_dit_destroy(dtts_dit *e) {
+    if (!e) return DTTS_OK;
+    DeviceGuard g(e->device);
+    cudaStreamSynchronize(e->stream);
+    delete e;
+    return DTTS_OK;
+}
+
+int dtts_dit_set_stream(dtts_dit *e, void *stream) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
+    e->stream = stream ? static_cast<cudaStream_t>(stream) : e->own_stream;
+    return DTTS_OK;
+}
+
+int dtts_dit_sync(dtts_dit *e) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
+    DeviceGuard g(e->device);
+    return e->finish(true);
+}
+
+int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const uint8_t *mask, const float *pos,
+                      int rows, int L, int n_out, float *out, int mem) {
+    DTTS_CHECK(e && x_in && cond && out, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(rows >= 1 && L >= 1 && L <= 4096 && n_out >= 1 && n_out <= L, DTTS_ERR_ARG,
+               "bad shape rows=%d L=%d n_out=%d", rows, L, n_out);
+    DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind %d", mem);
+    DeviceGuard g(e->device);
+    int st = e->ensure_workspace(rows, L, 1);
+    if (st) return st;
+    // this call overwrites the RoPE / mask tables a captured solve reads
+    if (e->gexec) { DTTS_CUDA(cudaStreamSynchronize(e->stream)); cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
+    e->gkey.clear();
+    e->launches = 0;
+    const cudaMemcpyKind in_kind = mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    cudaStream_t s = e->stream;
+    const size_t ntok = (size_t)rows * L;
+    DTTS_CUDA(cudaMemcpyAsync(e->in_a, x_in, ntok * kD * 4, in_kind, s));
+    DTTS_CUDA(cudaMemcpyAsync(e->cond_f32, cond, (size_t)rows * kD * 4, in_kind, s));
+    std::vector<float2> rt;
+    rope_half_table(nullptr, L, rt);
+    std::vector<float> hpos;
+    if (pos) {
+        hpos.resize(L);
+        DTTS_CUDA(cudaMemcpy(hpos.data(), pos, L * 4, mem == DTTS_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToHost));
+        rope_half_table(hpos.data(), L, rt);
+    }
+    DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
+    e->last_mask = mask != nullptr;
+    if (mask) DTTS_CUDA(cudaMemcpyAsync(e->mask, mask, (size_t)L * L, in_kind, s));
+    e->launches += 2;
+    launch_f32_to_bf16(e->in_a, e->x_in, (long long)ntok * kD, s);
+    launch_silu_bf16(e->cond_f32, e->a_cond, (long long)rows * kD, s);
+    if ((st = e->enqueue_forward(rows, L, n_out))) return st;
+    const cudaMemcpyKind out_kind = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    DTTS_CUDA(cudaMemcpyAsync(out, e->vel, (size_t)rows * n_out * kLat * 4, out_kind, s));
+    return e->finish(mem == DTTS_MEM_HOST);
+}
+
+int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
+    DTTS_CHECK(e && a, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(a->fm_cond && a->fm_uncond && a->z0 && a->z_out, DTTS_ERR_ARG, "null buffer in solve args");
+    DTTS_CHECK(a->n_utt >= 1 && a->fm_len >= 0 && a->patch >= 1 && a->nfe >= 1 && a->nfe <= 1000, DTTS_ERR_ARG,
+               "bad solve shape n_utt=%d fm_len=%d patch=%d nfe=%d", a->n_utt, a->fm_len, a->patch, a->nfe);
+    DTTS_CHECK(a->fm_len + a->patch <= 4096, DTTS_ERR_ARG, "sequence too long");
+    DTTS_CHECK(a->cfg_form == DTTS_CFG_V4 || a->cfg_form == DTTS_CFG_V3, DTTS_ERR_ARG, "bad cfg_form");
+    DTTS_CHECK(a->layout == DTTS_LAYOUT_FM_MASK || a->layout == DTTS_LAYOUT_FULL, DTTS_ERR_ARG, "bad layout");
+    DTTS_CHECK(a->mem == DTTS_MEM_HOST || a->mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
+    DTTS_CHECK(!a->spk || (e->spk_w1 && e->spk_lw), DTTS_ERR_ARG, "speaker vectors given but xvec_proj weights absent");
+    DeviceGuard g(e->device);
+    const int rows = 2 * a->n_utt, L = a->fm_len + a->patch;
+    int st = e->ensure_workspace(rows, L, a->nfe);
+    if (st) return st;
+    cudaStream_t s = e->stream;
+    const cudaMemcpyKind in_kind = a->mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    const size_t hist = (size_t)a->n_utt * a->fm_len * kD * 4;
+    if (hist) {
+        DTTS_CUDA(cudaMemcpyAsync(e->in_a, a->fm_cond, hist, in_kind, s));
+        DTTS_CUDA(cudaMemcpyAsync(e->in_b, a->fm_uncond, hist, in_kind, s));
+    }
+    DTTS_CUDA(cudaMemcpyAsync(e->z, a->z0, (size_t)a->n_utt * a->patch * kLat * 4, in_kind, s));
+    if (a->spk) DTTS_CUDA(cudaMemcpyAsync(e->spk_in, a->spk, (size_t)a->n_utt * kSpk * 4, in_kind, s));
+
+    char keybuf[256];
+    snprintf(keybuf, sizeof(keybuf), "%d/%d/%d/%d/%a/%d/%d/%d/%a/%p", a->n_utt, a->fm_len, a->patch, a->nfe,
+             a->cfg_scale, a->cfg_form, a->layout, a->spk != nullptr, a->spk_scale, (void *)s);
+    const std::string key(keybuf);
+    const bool tables_current = (key == e->gkey);
+    if (!tables_current) {
+        // constant tables for this shape: mask, RoPE, sinusoids
+        std::vector<float> pos(L);
+        std::vector<uint8_t> m;
+        if (a->layout == DTTS_LAYOUT_FM_MASK) {
+            m.resize((size_t)L * L);
+            fm_mask(m.data(), L, a->fm_len, a->patch, 1);
+            fm_pos(pos.data(), L, a->fm_len, a->patch);
+        } else {
+            for (int i = 0; i < L; i++) pos[i] = (float)i;
+        }
+        std::vector<float2> rt;
+        rope_half_table(pos.data(), L, rt);
+        std::vector<float> se((size_t)a->nfe * 256);
+        const float dt = 1.0f / (float)a->nfe;
+        for (int k = 0; k < a->nfe; k++) sinusoid((float)k * dt, &se[(size_t)k * 256]);
+        DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaMemcpyAsync(e->se_tab, se.data(), se.size() * 4, cudaMemcpyHostToDevice, s));
+        if (!m.empty()) DTTS_CUDA(cudaMemcpyAsync(e->mask, m.data(), m.size(), cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaStreamSynchronize(s));  // host tables go out of scope
+        if (e->gexec) { cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
+        e->gkey = key;
+    }
+    e->last_mask = a->layout == DTTS_LAYOUT_FM_MASK;
+    if (a->use_graph) {
+        if (!e->gexec) {
+            e->launches = 0;
+            cudaGraph_t graph = nullptr;
+            DTTS_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+            st = e->enqueue_solve(a);
+            cudaError_t ce = cudaStreamEndCapture(s, &graph);
+            if (st) { if (graph) cudaGraphDestroy(graph); return st; }
+            DTTS_CUDA(ce);
+            ce = cudaGraphInstantiate(&e->gexec, graph, 0);
+            cudaGraphDestroy(graph);
+            DTTS_CUDA(ce);
+        }
+        DTTS_CUDA(cudaGraphLaunch(e->gexec, s));
+    } else {
+        e->launches = 0;
+        if ((st = e->enqueue_solve(a))) return st;
+    }
+    const cudaMemcpyKind out_kind = a->mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    DTTS_CUDA(cudaMemcpyAsync(a->z_out, e->z, (size_t)a->n_utt * a->patch * kLat * 4, out_kind, s));
+    return e->finish(a->mem == DTTS_MEM_HOST);
+}
+
+int dtts_dit_last_launch_count(dtts_dit *e, int *n) {
+    DTTS_CHECK(e && n, DTTS_ERR_ARG, "null argument");
+    *n = e->launches;
+    return DTTS_OK;
+}
+
+int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us, double *flops, double *bytes) {
+    DTTS_CHECK(e && us, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(e->last_rows > 0, DTTS_ERR_ARG, "run a solve or velocity call first");
+    DTTS_CHECK(kind >= 0 && kind <= 7 && iters >= 1, DTTS_ERR_ARG, "bad kind/iters");
+    DeviceGuard g(e->device);
+    const int rows = e->last_rows, L = e->last_L;
+    const double M = (double)rows * L;
+    auto one = [&]() -> int {
+        switch (kind) {
+            case 0: return e->enqueue_block_op(0, 0, rows, L);
+            case 1: return e->enqueue_block_op(1, 0, rows, L);
+            case 2: return e->enqueue_block_op(2, 0, rows, L);
+            case 3: return e->enqueue_block_op(3, 0, rows, L);
+            case 4: return e->enqueue_block_op(4, 0, rows, L);
+            case 5: return e->enqueue_block_op(5, 0, rows, L);
+            case 6: {
+                GemmOp op = make_op(e->t_acond, e->t_ada, rows, e->n_ada, kD, EPI_F32, e->d_err);
+                op.ep.bias = e->b_ada; op.ep.out = e->ada; op.ep.ldo = e->n_ada;
+                return e->gemm(op);
+            }
+            case 7: {
+                GemmOp op = make_op(e->t_x_in, e->t_in, (int)M, kD, kD, EPI_F32, e->d_err);
+                op.ep.bias = e->b_in; op.ep.out = e->h; op.ep.ldo = kD;
+                return e->gemm(op);
+            }
+        }
+        return DTTS_ERR_ARG;
+    };
+    cudaStream_t s = e->stream;
+    int st;
+    for (int i = 0; i < 3; i++)
+        if ((st = one())) return st;
+    cudaEvent_t e0, e1;
+    DTTS_CUDA(cudaEventCreate(&e0));
+    DTTS_CUDA(cudaEventCreate(&e1));
+    DTTS_CUDA(cudaEventRecord(e0, s));
+    for (int i = 0; i < iters; i++)
+        if ((st = one())) return st;
+    DTTS_CUDA(cudaEventRecord(e1, s));
+    if ((st = stream_wait(s, 120.0))) return st;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *us = ms * 1000.0f / iters;
+    double f = 0, b = 0;
+    const double W = 2.0;  // bytes per bf16
+    switch (kind) {
+        case 0: f = 2 * M * 3 * kD * kD; b = W * (M * kD + 3.0 * kD * kD + 3 * M * kD); break;
+        case 1: f = 2 * M * kD * kD; b = W * (M * kD + 1.0 * kD * kD) + 8 * M * kD; break;
+        case 2: f = 2 * M * kF * kD; b = W * (M * kD + 1.0 * kF * kD + M * kF); break;
+        case 3: f = 2 * M * kD * kF; b = W * (M * kF + 1.0 * kF * kD) + 8 * M * kD; break;
+        case 4: f = 4.0 * rows * kH * (double)L * L * kHD; b = W * 4 * M * kD; break;
+        case 5: f = 0; b = M * kD * 4 + M * kD * 2; break;
+        case 6: f = 2.0 * rows * e->n_ada * kD; b = W * ((double)e->n_ada * kD + rows * kD) + 4.0 * rows * e->n_ada; break;
+        case 7: f = 2 * M * kD * kD; b = W * (M * kD + 1.0 * kD * kD) + 4 * M * kD; break;
+    }
+    if (flops) *flops = f;
+    if (bytes) *bytes = b;
+    return e->finish(true);
+}
+
+}  // extern "C"

@@ -1,0 +1,723 @@
+// Non-GEMM kernels: norms, attention (bf16 mma.sync and fp32), fp32 SIMT
+// projections, conditioning, DiT output head, PatchEncoder conv/pairing.
+#include "kernels.cuh"
+#include <math.h>
+
+namespace dtts {
+
+// =========================================================================
+// norms: one warp per token row of 1024 fp32 values (8 x float4 per lane)
+// =========================================================================
+__global__ void __launch_bounds__(256) ln_modulate_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
+                                                          const float *__restrict__ shift,
+                                                          const float *__restrict__ scale, long long ada_ld,
+                                                          int tok_per_row) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
+    float4 v[8];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        v[j] = xr[lane + 32 * j];
+        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    const float mean = warp_sum(s) * (1.0f / kD);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
+    const long long r = row / tok_per_row;
+    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
+    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
+    uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int c4 = lane + 32 * j;
+        float4 a = __ldg(sh + c4), b = __ldg(sc + c4);
+        float o0 = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
+        float o1 = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
+        float o2 = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
+        float o3 = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
+        yr[c4] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+    }
+}
+
+void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale, long long ada_ld,
+                        int tok_per_row, cudaStream_t s) {
+    ln_modulate_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, shift, scale, ada_ld, tok_per_row);
+}
+
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
+                                                       const float *__restrict__ w) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
+    float4 v[8];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        v[j] = xr[lane + 32 * j];
+        s += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(s) * (1.0f / kD) + 1e-6f);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int c4 = lane + 32 * j;
+        float4 g = w ? __ldg(w4 + c4) : make_float4(1.f, 1.f, 1.f, 1.f);
+        yr[c4] = make_uint2(pack_bf16x2(v[j].x * inv * g.x, v[j].y * inv * g.y),
+                            pack_bf16x2(v[j].z * inv * g.z, v[j].w * inv * g.w));
+    }
+}
+
+void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s) {
+    rms_norm_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, w);
+}
+
+// =========================================================================
+// bf16 attention, mma.sync m16n8k16, one CTA per (64-query tile, head, row).
+// Q/K/V tiles of 64 x 64 bf16 staged in shared memory with a 16-byte-chunk XOR
+// swizzle; scores and the online softmax in fp32; P rounded to bf16 for P.V.
+// =========================================================================
+DTTS_DEV uint32_t swz(int row, int chunk) { return row * 64 + ((chunk ^ (row & 7)) << 3); }
+
+DTTS_DEV void cp_async16(void *smem, const void *gmem, bool valid) {
+    const uint32_t sz = valid ? 16u : 0u;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(sz)
+                 : "memory");
+}
+DTTS_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+DTTS_DEV void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+DTTS_DEV void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+DTTS_DEV void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Loads a 64 x 64 bf16 tile (rows >= valid_rows are zero-filled).
+DTTS_DEV void load_tile64(bf16 *sm, const bf16 *g, long long ld, int valid_rows) {
+    for (int idx = threadIdx.x; idx < 64 * 8; idx += 128) {
+        const int row = idx >> 3, ch = idx & 7;
+        const bool ok = row < valid_rows;
+        const bf16 *src = ok ? g + (long long)row * ld + ch * 8 : g;
+        cp_async16(sm + swz(row, ch), src, ok);
+    }
+}
+
+__global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
+    __shared__ __align__(128) bf16 Qs[64 * 64];
+    __shared__ __align__(128) bf16 Ks[64 * 64];
+    __shared__ __align__(128) bf16 Vs[64 * 64];
+    const int qt = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int q0 = qt * 64;
+    const bf16 *qg = reinterpret_cast<const bf16 *>(a.q) + ((long long)r * a.Tq + q0) * a.ldq + h * kHD;
+    const bf16 *kg = reinterpret_cast<const bf16 *>(a.k) + (long long)r * a.kv_cap * a.ldkv + h * kHD;
+    const bf16 *vg = reinterpret_cast<const bf16 *>(a.v) + (long long)r * a.kv_cap * a.ldkv + h * kHD;
+
+    load_tile64(Qs, qg, a.ldq, a.Tq - q0);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+
+    // row indices of this thread's two query rows (within the tile)
+    const int wr0 = warp * 16 + g, wr1 = wr0 + 8;
+    const int qi0 = q0 + wr0, qi1 = q0 + wr1;
+
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    uint32_t qf[4][4];
+
+    // keys beyond the causal limit of the last query of this tile are never needed
+    int kv_end = a.kv_len;
+    if (a.causal) kv_end = min(kv_end, a.q_pos0 + min(q0 + 64, a.Tq));
+    const int nkb = (kv_end + 63) / 64;
+
+    for (int kb = 0; kb < nkb; kb++) {
+        const int k0 = kb * 64;
+        __syncthreads();  // previous K/V tile fully consumed
+        load_tile64(Ks, kg + (long long)k0 * a.ldkv, a.ldkv, a.kv_len - k0);
+        load_tile64(Vs, vg + (long long)k0 * a.ldkv, a.ldkv, a.kv_len - k0);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        cp_async_wait_all();
+        __syncthreads();
+        if (kb == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int ch = 2 * kk + (lane >> 4);
+                ldsm_x4(qf[kk], Qs + swz(row, ch));
+            }
+        }
+        // S = Q K^T for 16 rows x 64 keys
+        float sc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                uint32_t b[4];
+                const int key = np * 16 + (lane & 7) + 8 * (lane >> 4);
+                const int ch = 2 * kk + ((lane >> 3) & 1);
+                ldsm_x4(b, Ks + swz(key, ch));
+                mma_bf16_16816(sc[2 * np], qf[kk], b[0], b[1]);
+                mma_bf16_16816(sc[2 * np + 1], qf[kk], b[2], b[3]);
+            }
+        }
+        // scale + mask
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int key = k0 + nt * 8 + 2 * t + (c & 1);
+                const int qi = (c < 2) ? qi0 : qi1;
+                float s = sc[nt][c] * a.scale;
+                bool ok = key < a.kv_len;
+                if (a.causal) ok = ok && (key <= a.q_pos0 + qi);
+                if (a.mask && ok && qi < a.Tq) ok = a.mask[(long long)qi * a.kv_len + key] != 0;
+                s = ok ? s : -INFINITY;
+                sc[nt][c] = s;
+                if (c < 2) mx0 = fmaxf(mx0, s); else mx1 = fmaxf(mx1, s);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float u0 = (n0 == -INFINITY) ? 0.f : n0, u1 = (n1 == -INFINITY) ? 0.f : n1;
+        const float corr0 = expf(m0 - u0), corr1 = expf(m1 - u1);
+        m0 = n0; m1 = n1;
+        float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+            sc[nt][0] = expf(sc[nt][0] - u0); sc[nt][1] = expf(sc[nt][1] - u0);
+            sc[nt][2] = expf(sc[nt][2] - u1); sc[nt][3] = expf(sc[nt][3] - u1);
+            rs0 += sc[nt][0] + sc[nt][1];
+            rs1 += sc[nt][2] + sc[nt][3];
+        }
+        rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
+        rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
+        rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
+        rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
+        l0 = l0 * corr0 + rs0;
+        l1 = l1 * corr1 + rs1;
+#pragma unroll
+        for (int i = 0; i < 8; i++) { o[i][0] *= corr0; o[i][1] *= corr0; o[i][2] *= corr1; o[i][3] *= corr1; }
+        // O += P V
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            uint32_t pa[4];
+            pa[0] = pack_bf16x2(sc[2 * kk][0], sc[2 * kk][1]);
+            pa[1] = pack_bf16x2(sc[2 * kk][2], sc[2 * kk][3]);
+            pa[2] = pack_bf16x2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+            pa[3] = pack_bf16x2(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; dp++) {
+                uint32_t b[4];
+                const int key = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+                const int ch = 2 * dp + (lane >> 4);
+                ldsm_x4_t(b, Vs + swz(key, ch));
+                mma_bf16_16816(o[2 * dp], pa, b[0], b[1]);
+                mma_bf16_16816(o[2 * dp + 1], pa, b[2], b[3]);
+            }
+        }
+    }
+    const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f;
+    const float inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+    bf16 *og = reinterpret_cast<bf16 *>(a.o) + (long long)r * a.Tq * a.ldo + h * kHD;
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++) {
+        const int d = nt * 8 + 2 * t;
+        if (qi0 < a.Tq)
+            *reinterpret_cast<uint32_t *>(og + (long long)qi0 * a.ldo + d) = pack_bf16x2(o[nt][0] * inv0, o[nt][1] * inv0);
+        if (qi1 < a.Tq)
+            *reinterpret_cast<uint32_t *>(og + (long long)qi1 * a.ldo + d) = pack_bf16x2(o[nt][2] * inv1, o[nt][3] * inv1);
+    }
+}
+
+void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
+    dim3 grid((a.Tq + 63) / 64, kH, a.rows);
+    attn_bf16_kernel<<<grid, 128, 0, s>>>(a);
+}
+
+// =========================================================================
+// fp32 attention (SIMT), one CTA per (head, row); K and V of the row/head in
+// shared memory; each thread owns one query at a time.  Softmax as
+// include/dit_manual.h:83-86 (max, exp, sum), then P.V.
+// =========================================================================
+__global__ void __launch_bounds__(128) attn_f32_kernel(AttnArgs a) {
+    extern __shared__ float kvs[];
+    float *Ks = kvs;
+    float *Vs = kvs + (long long)a.kv_len * kHD;
+    const int h = blockIdx.x, r = blockIdx.y;
+    const float *kg = reinterpret_cast<const float *>(a.k) + (long long)r * a.kv_cap * a.ldkv + h * kHD;
+    const float *vg = reinterpret_cast<const float *>(a.v) + (long long)r * a.kv_cap * a.ldkv + h * kHD;
+    for (int idx = threadIdx.x; idx < a.kv_len * kHD; idx += blockDim.x) {
+        const int j = idx / kHD, d = idx % kHD;
+        Ks[idx] = kg[(long long)j * a.ldkv + d];
+        Vs[idx] = vg[(long long)j * a.ldkv + d];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.Tq; i += blockDim.x) {
+        const float *qg = reinterpret_cast<const float *>(a.q) + ((long long)r * a.Tq + i) * a.ldq + h * kHD;
+        float q[kHD];
+#pragma unroll
+        for (int d = 0; d < kHD; d++) q[d] = qg[d];
+        float mx = -INFINITY;
+        for (int j = 0; j < a.kv_len; j++) {
+            bool ok = true;
+            if (a.causal) ok = j <= a.q_pos0 + i;
+            if (a.mask) ok = ok && a.mask[(long long)i * a.kv_len + j] != 0;
+            if (!ok) continue;
+            float s = 0.f;
+#pragma unroll
+            for (int d = 0; d < kHD; d++) s += q[d] * Ks[j * kHD + d];
+            mx = fmaxf(mx, s * a.scale);
+        }
+        float acc[kHD];
+#pragma unroll
+        for (int d = 0; d < kHD; d++) acc[d] = 0.f;
+        float sum = 0.f;
+        for (int j = 0; j < a.kv_len; j++) {
+            bool ok = true;
+            if (a.causal) ok = j <= a.q_pos0 + i;
+            if (a.mask) ok = ok && a.mask[(long long)i * a.kv_len + j] != 0;
+            if (!ok) continue;
+            float s = 0.f;
+#pragma unroll
+            for (int d = 0; d < kHD; d++) s += q[d] * Ks[j * kHD + d];
+            const float p = expf(s * a.scale - mx);
+            sum += p;
+#pragma unroll
+            for (int d = 0; d < kHD; d++) acc[d] += p * Vs[j * kHD + d];
+        }
+        const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+        float *og = reinterpret_cast<float *>(a.o) + ((long long)r * a.Tq + i) * a.ldo + h * kHD;
+#pragma unroll
+        for (int d = 0; d < kHD; d++) og[d] = acc[d] * inv;
+    }
+}
+
+cudaError_t attention_f32_prepare() {
+    return cudaFuncSetAttribute(attn_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+cudaError_t launch_attention_f32(const AttnArgs &a, cudaStream_t s) {
+    const size_t smem = (size_t)a.kv_len * kHD * 2 * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    attn_f32_kernel<<<dim3(kH, a.rows), 128, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+// =========================================================================
+// fp32 SIMT GEMM: 64x64 tile, BK 16, 256 threads, 4x4 outputs per thread.
+// Each output accumulates over k in increasing order; bias added last.
+// =========================================================================
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const float *__restrict__ A, const float *__restrict__ B,
+                                                       const float *__restrict__ bias, float *__restrict__ C, int M,
+                                                       int N, int K) {
+    __shared__ float As[16][64 + 4];
+    __shared__ float Bs[16][64 + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int idx = threadIdx.x; idx < 64 * 16; idx += 256) {
+            const int rr = idx >> 4, kk = idx & 15;
+            const int gm = m0 + rr, gn = n0 + rr, gk = k0 + kk;
+            As[kk][rr] = (gm < M && gk < K) ? A[(long long)gm * K + gk] : 0.f;
+            Bs[kk][rr] = (gn < N && gk < K) ? B[(long long)gn * K + gk] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++) {
+            float av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) { av[i] = As[kk][ty * 4 + i]; bv[i] = Bs[kk][tx * 4 + i]; }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] += av[i] * bv[j];
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int gm = m0 + ty * 4 + i;
+        if (gm >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int gn = n0 + tx * 4 + j;
+            if (gn < N) C[(long long)gm * N + gn] = acc[i][j] + (bias ? bias[gn] : 0.f);
+        }
+    }
+}
+
+void launch_gemm_f32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K,
+                     cudaStream_t s) {
+    dim3 grid((N + 63) / 64, (M + 63) / 64);
+    gemm_f32_kernel<<<grid, 256, 0, s>>>(A, B, bias, C, M, N, K);
+}
+
+__global__ void qk_norm_rope_f32_kernel(float *q, float *k, int M, int tok_per_row, int qk_norm,
+                                        const float *qn, const float *kn, const float2 *rope, int rope_mode,
+                                        int pos_start) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // (token, head)
+    if (idx >= (long long)M * kH) return;
+    const int m = (int)(idx / kH), h = (int)(idx % kH);
+    const int t = m % tok_per_row;
+    const float2 *cs = rope + (long long)(pos_start + t) * 32;
+    for (int which = 0; which < 2; which++) {
+        float *p = (which == 0 ? q : k) + (long long)m * kD + h * kHD;
+        const float *g = which == 0 ? qn : kn;
+        float v[kHD];
+#pragma unroll
+        for (int d = 0; d < kHD; d++) v[d] = p[d];
+        if (qk_norm) {
+            float ss = 0.f;
+#pragma unroll
+            for (int d = 0; d < kHD; d++) ss += v[d] * v[d];
+            const float inv = 1.0f / sqrtf(ss / kHD + 1e-6f);
+#pragma unroll
+            for (int d = 0; d < kHD; d++) { float y = v[d] * inv; if (g) y *= g[d]; v[d] = y; }
+        }
+        if (rope_mode == ROPE_HALF) {
+#pragma unroll
+            for (int d = 0; d < 32; d++) {
+                const float2 e = cs[d];
+                const float x1 = v[d], x2 = v[d + 32];
+                v[d] = x1 * e.x - x2 * e.y;
+                v[d + 32] = x2 * e.x + x1 * e.y;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float2 e = cs[i];
+                const float x0 = v[2 * i], x1 = v[2 * i + 1];
+                v[2 * i] = x0 * e.x - x1 * e.y;
+                v[2 * i + 1] = x0 * e.y + x1 * e.x;
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < kHD; d++) p[d] = v[d];
+    }
+}
+
+void launch_qk_norm_rope_f32(float *q, float *k, int M, int tok_per_row, int qk_norm, const float *qn,
+                             const float *kn, const float2 *rope, int rope_mode, int pos_start, cudaStream_t s) {
+    const long long n = (long long)M * kH;
+    qk_norm_rope_f32_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(q, k, M, tok_per_row, qk_norm, qn, kn, rope,
+                                                                         rope_mode, pos_start);
+}
+
+// =========================================================================
+// conversions
+// =========================================================================
+__global__ void f32_to_bf16_kernel(const float *__restrict__ x, bf16 *__restrict__ y, long long n) {
+    const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 v = *reinterpret_cast<const float4 *>(x + i);
+        *reinterpret_cast<uint2 *>(y + i) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    } else {
+        for (long long j = i; j < n; j++) y[j] = __float2bfloat16_rn(x[j]);
+    }
+}
+void launch_f32_to_bf16(const float *x, bf16 *y, long long n, cudaStream_t s) {
+    const long long threads = (n + 3) / 4;
+    f32_to_bf16_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, y, n);
+}
+
+__global__ void silu_bf16_kernel(const float *__restrict__ x, bf16 *__restrict__ y, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) { const float c = x[i]; y[i] = __float2bfloat16_rn(c / (1.0f + expf(-c))); }
+}
+void launch_silu_bf16(const float *x, bf16 *y, long long n, cudaStream_t s) {
+    silu_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, y, n);
+}
+
+__global__ void history_rows_kernel(const float *__restrict__ src, int n_seq, int src_len, bf16 *__restrict__ dst,
+                                    int L, int row_stride, int row_off) {
+    const long long i4 = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
+    const long long total4 = (long long)n_seq * src_len * (kD / 4);
+    if (i4 >= total4) return;
+    const long long tok = i4 / (kD / 4);
+    const int c4 = (int)(i4 % (kD / 4));
+    const int u = (int)(tok / src_len), t = (int)(tok % src_len);
+    const float4 v = reinterpret_cast<const float4 *>(src)[i4];
+    const long long drow = ((long long)u * row_stride + row_off) * L + t;
+    reinterpret_cast<uint2 *>(dst + drow * kD)[c4] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+void launch_history_rows(const float *src, int n_seq, int src_len, bf16 *dst, int L, int row_stride, int row_off,
+                         cudaStream_t s) {
+    const long long total4 = (long long)n_seq * src_len * (kD / 4);
+    if (total4 == 0) return;
+    history_rows_kernel<<<(unsigned)((total4 + 255) / 256), 256, 0, s>>>(src, n_seq, src_len, dst, L, row_stride,
+                                                                          row_off);
+}
+
+// =========================================================================
+// conditioning
+// =========================================================================
+// y[o] = act(W[o] . x + b[o]); one warp per output, lanes split the input.
+template <int IN, bool SILU>
+__global__ void __launch_bounds__(256) warp_gemv_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                        const float *__restrict__ b, float *__restrict__ y, int out) {
+    const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (o >= out) return;
+    const float *wr = w + (long long)o * IN;
+    float s = 0.f;
+#pragma unroll 4
+    for (int i = lane; i < IN; i += 32) s += wr[i] * x[i];
+    s = warp_sum(s);
+    if (lane == 0) {
+        float v = s + (b ? b[o] : 0.f);
+        if (SILU) v = v / (1.0f + expf(-v));
+        y[o] = v;
+    }
+}
+
+void launch_time_mlp(const float *se, const float *w1, const float *b1, const float *w2, const float *b2,
+                     float *h1_scratch, float *temb, cudaStream_t s) {
+    warp_gemv_kernel<256, true><<<kD / 8, 256, 0, s>>>(se, w1, b1, h1_scratch, kD);
+    warp_gemv_kernel<kD, false><<<kD / 8, 256, 0, s>>>(h1_scratch, w2, b2, temb, kD);
+}
+
+__global__ void __launch_bounds__(1024) speaker_cond_kernel(const float *__restrict__ spk, const float *__restrict__ w,
+                                                            const float *__restrict__ b, const float *__restrict__ lw,
+                                                            const float *__restrict__ lb, float scale,
+                                                            float *__restrict__ out) {
+    __shared__ float xs[kSpk];
+    __shared__ float red[32];
+    const int u = blockIdx.x, o = threadIdx.x;
+    for (int i = threadIdx.x; i < kSpk; i += blockDim.x) xs[i] = spk[(long long)u * kSpk + i];
+    __syncthreads();
+    float y = b ? b[o] : 0.f;
+    {
+        const float *wr = w + (long long)o * kSpk;
+        float s = 0.f;
+        for (int i = 0; i < kSpk; i++) s += wr[i] * xs[i];
+        y += s;
+    }
+    // block mean / variance over 1024 outputs
+    float v = warp_sum(y);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float mean = 0.f;
+    for (int i = 0; i < 32; i++) mean += red[i];
+    mean /= kD;
+    __syncthreads();
+    const float d = y - mean;
+    v = warp_sum(d * d);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float var = 0.f;
+    for (int i = 0; i < 32; i++) var += red[i];
+    const float istd = 1.0f / sqrtf(var / kD + 1e-5f);
+    float xo = d * istd;
+    if (lw) xo *= lw[o];
+    if (lb) xo += lb[o];
+    out[(long long)u * kD + o] = xo * scale;
+}
+
+void launch_speaker_cond(const float *spk, int n_utt, const float *w, const float *b, const float *ln_w,
+                         const float *ln_b, float scale, float *spk_c, cudaStream_t s) {
+    speaker_cond_kernel<<<n_utt, kD, 0, s>>>(spk, w, b, ln_w, ln_b, scale, spk_c);
+}
+
+__global__ void cond_rows_kernel(const float *__restrict__ temb, const float *__restrict__ spk_c, int rows,
+                                 int rows_per_utt, bf16 *__restrict__ a) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * kD) return;
+    const int r = (int)(i / kD), c = (int)(i % kD);
+    float v = temb[c];
+    if (spk_c) v += spk_c[(long long)(r / rows_per_utt) * kD + c];
+    a[i] = __float2bfloat16_rn(v / (1.0f + expf(-v)));
+}
+
+void launch_cond_rows(const float *temb, const float *spk_c, int rows, int rows_per_utt, bf16 *a_cond,
+                      cudaStream_t s) {
+    const long long n = (long long)rows * kD;
+    cond_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(temb, spk_c, rows, rows_per_utt, a_cond);
+}
+
+// =========================================================================
+// DiT output head
+// =========================================================================
+__global__ void __launch_bounds__(256) out_head_kernel(const float *__restrict__ h, int L, int P,
+                                                       const float *__restrict__ shift,
+                                                       const float *__restrict__ scale, long long ada_ld,
+                                                       const float *__restrict__ w, const float *__restrict__ b,
+                                                       float *__restrict__ vel, int *err) {
+    __shared__ float u[kD];
+    __shared__ float red[8];
+    const int r = blockIdx.x / P, p = blockIdx.x % P;
+    const int tok = L - P + p;
+    const float *x = h + ((long long)r * L + tok) * kD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float v[4];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) { v[j] = x[threadIdx.x + 256 * j]; s += v[j]; }
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    float mean = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) mean += red[i];
+    mean *= (1.0f / kD);
+    __syncthreads();
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) { const float d = v[j] - mean; q += d * d; }
+    q = warp_sum(q);
+    if (lane == 0) red[warp] = q;
+    __syncthreads();
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) var += red[i];
+    const float inv = 1.0f / sqrtf(var * (1.0f / kD) + 1e-5f);
+    const float *sh = shift + (long long)r * ada_ld;
+    const float *sc = scale + (long long)r * ada_ld;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int c = threadIdx.x + 256 * j;
+        u[c] = (v[j] - mean) * inv * (1.0f + sc[c]) + sh[c];
+    }
+    __syncthreads();
+    // 128 outputs, 16 per warp; lanes split the 1024 inputs
+    for (int oo = 0; oo < kLat / 8; oo++) {
+        const int o = warp * (kLat / 8) + oo;
+        const float *wr = w + (long long)o * kD;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int i = lane; i < kD; i += 32) acc += wr[i] * u[i];
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            const float y = acc + (b ? b[o] : 0.f);
+            if (!isfinite(y) && err) atomicCAS(err, 0, DEVERR_NONFINITE);
+            vel[((long long)r * P + p) * kLat + o] = y;
+        }
+    }
+}
+
+void launch_out_head(const float *h, int rows, int L, int P, const float *shift, const float *scale,
+                     long long ada_ld, const float *w_out, const float *b_out, float *vel, int *err, cudaStream_t s) {
+    out_head_kernel<<<rows * P, 256, 0, s>>>(h, L, P, shift, scale, ada_ld, w_out, b_out, vel, err);
+}
+
+__global__ void __launch_bounds__(256) cfg_euler_kernel(const float *__restrict__ vel, float *__restrict__ z, int P,
+                                                        float cfg_scale, int cfg_form, float dt, int update,
+                                                        const float *__restrict__ wc, const float *__restrict__ bc,
+                                                        bf16 *__restrict__ x_in, int L) {
+    __shared__ float zs[kLat];
+    const int u = blockIdx.x / P, p = blockIdx.x % P;
+    float *zp = z + ((long long)u * P + p) * kLat;
+    if (threadIdx.x < kLat) {
+        float zv = zp[threadIdx.x];
+        if (update) {
+            const float vc = vel[((long long)(2 * u) * P + p) * kLat + threadIdx.x];
+            const float vu = vel[((long long)(2 * u + 1) * P + p) * kLat + threadIdx.x];
+            const float v = cfg_form == 0 ? vc + cfg_scale * (vc - vu) : vu + cfg_scale * (vc - vu);
+            zv += v * dt;
+            zp[threadIdx.x] = zv;
+        }
+        zs[threadIdx.x] = zv;
+    }
+    __syncthreads();
+    const long long tok = L - P + p;
+    bf16 *xc = x_in + ((long long)(2 * u) * L + tok) * kD;
+    bf16 *xu = x_in + ((long long)(2 * u + 1) * L + tok) * kD;
+    for (int o = threadIdx.x; o < kD; o += blockDim.x) {
+        const float *wr = wc + (long long)o * kLat;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int i = 0; i < kLat; i++) acc += wr[i] * zs[i];
+        const bf16 y = __float2bfloat16_rn(acc + (bc ? bc[o] : 0.f));
+        xc[o] = y;
+        xu[o] = y;
+    }
+}
+
+void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_scale, int cfg_form, float dt,
+                      int update, const float *w_coord, const float *b_coord, bf16 *x_in, int L, cudaStream_t s) {
+    cfg_euler_kernel<<<n_utt * P, 256, 0, s>>>(vel, z, P, cfg_scale, cfg_form, dt, update, w_coord, b_coord, x_in, L);
+}
+
+// =========================================================================
+// PatchEncoder
+// =========================================================================
+__global__ void __launch_bounds__(128) pe_conv_kernel(const float *__restrict__ frames, int n_frames,
+                                                      const float *__restrict__ tail, const float *__restrict__ w,
+                                                      const float *__restrict__ bias, bf16 *__restrict__ out,
+                                                      float *__restrict__ new_tail) {
+    __shared__ float f0[kLat], f1[kLat];
+    const int T = n_frames / 2;
+    const int b = blockIdx.x / T, t = blockIdx.x % T;
+    const float *fb = frames + (long long)b * n_frames * kLat;
+    const int i0 = 2 * t - 1, i1 = 2 * t;
+    const int c = threadIdx.x;
+    f0[c] = i0 >= 0 ? fb[(long long)i0 * kLat + c] : (tail ? tail[(long long)b * kLat + c] : 0.f);
+    f1[c] = fb[(long long)i1 * kLat + c];
+    __syncthreads();
+    float s = bias ? bias[c] : 0.f;
+    const float *wr = w + (long long)c * kLat * 2;
+    for (int ic = 0; ic < kLat; ic++) {
+        s += f0[ic] * wr[2 * ic + 0];
+        s += f1[ic] * wr[2 * ic + 1];
+    }
+    out[((long long)b * T + t) * kLat + c] = __float2bfloat16_rn(s);
+    if (new_tail && t == T - 1) new_tail[(long long)b * kLat + c] = fb[(long long)(n_frames - 1) * kLat + c];
+}
+
+void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *w, const float *bias,
+                    bf16 *out, float *new_tail, cudaStream_t s) {
+    const int T = n_frames / 2;
+    pe_conv_kernel<<<B * T, kLat, 0, s>>>(frames, n_frames, tail, w, bias, out, new_tail);
+}
+
+__global__ void pe_pairs_kernel(const float *__restrict__ h, int T, int pair_mode, bf16 *__restrict__ out) {
+    const int n = T / 2;
+    const int bq = blockIdx.x;             // b * n + q
+    const int b = bq / n, q = bq % n;
+    for (int c = threadIdx.x; c < 2 * kD; c += blockDim.x) {
+        const int s = c / kD, i = c % kD;
+        int tok;
+        if (pair_mode == 0) {
+            tok = 2 * q + s;
+        } else {
+            const int g = 2 * q + s;
+            tok = 2 * (g % n) + g / n;
+        }
+        out[(long long)bq * 2 * kD + c] = __float2bfloat16_rn(h[((long long)b * T + tok) * kD + i]);
+    }
+}
+
+void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s) {
+    pe_pairs_kernel<<<B * (T / 2), 256, 0, s>>>(h, T, pair_mode, out);
+}
+
+}  // namespace dtts

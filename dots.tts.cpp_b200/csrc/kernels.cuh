@@ -1,0 +1,96 @@
+// Launchers for the non-GEMM kernels of the DiT / PatchEncoder engines.
+#pragma once
+#include "common.cuh"
+#include "gemm_tc.cuh"
+
+namespace dtts {
+
+constexpr int kD = 1024, kH = 16, kHD = 64, kF = 4096, kLat = 128, kLLM = 1536, kSpk = 512;
+
+// ------------------------------------------------------------ GEMM (tcgen05)
+struct GemmOp {
+    CUtensorMap ta, tb;
+    int M, N, K;
+    int bn;       // 128 or 256
+    int epi;      // EpiKind
+    EpiParams ep;
+};
+// A K-major bf16 matrix [rows][cols] seen by TMA as 64-column x box_rows boxes
+// with 128-byte swizzle.
+bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
+                    unsigned int box_rows);
+cudaError_t launch_gemm(const GemmOp &op, int num_sms, cudaStream_t s);
+cudaError_t gemm_prepare_attributes();
+
+// ------------------------------------------------------------ norms
+// y = bf16( LN(x) * (1 + scale[row]) + shift[row] ), LN without affine, eps 1e-5.
+void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale,
+                        long long ada_ld, int tok_per_row, cudaStream_t s);
+// y = bf16( x / sqrt(mean(x^2) + 1e-6) * w )
+void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s);
+
+// ------------------------------------------------------------ attention
+struct AttnArgs {
+    const void *q; long long ldq;          // row (r, i) = r*Tq + i
+    const void *k; const void *v; long long ldkv;  // row (r, j) = r*kv_cap + j
+    void *o; long long ldo;                // row (r, i) = r*Tq + i
+    int rows, Tq, kv_len, kv_cap;
+    int q_pos0;          // absolute position of query 0 (causal masking)
+    int causal;
+    const uint8_t *mask; // [Tq][kv_len] (1 = attend) or nullptr
+    float scale;
+};
+void launch_attention_bf16(const AttnArgs &a, cudaStream_t s);
+cudaError_t launch_attention_f32(const AttnArgs &a, cudaStream_t s);  // kv_len <= 400
+cudaError_t attention_f32_prepare();  // per device, before the first fp32 launch
+
+// ------------------------------------------------------------ fp32 SIMT path
+// C[M][N] = A[M][K] * B[N][K]^T + bias (fp32 everywhere).
+void launch_gemm_f32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K,
+                     cudaStream_t s);
+// In-place per-head RMS norm (optional) + RoPE on q and k, fp32 [M][1024].
+void launch_qk_norm_rope_f32(float *q, float *k, int M, int tok_per_row, int qk_norm, const float *qn,
+                             const float *kn, const float2 *rope, int rope_mode, int pos_start,
+                             cudaStream_t s);
+
+// ------------------------------------------------------------ conversions
+void launch_f32_to_bf16(const float *x, bf16 *y, long long n, cudaStream_t s);
+// SiLU(x) -> bf16 (the A operand of the adaLN GEMM)
+void launch_silu_bf16(const float *x, bf16 *y, long long n, cudaStream_t s);
+// Copy rows of a [n_seq][src_len][1024] fp32 tensor into tokens 0..src_len-1 of
+// sequence rows (row_stride*u + row_off) of a [rows][L][1024] bf16 buffer.
+void launch_history_rows(const float *src, int n_seq, int src_len, bf16 *dst, int L, int row_stride, int row_off,
+                         cudaStream_t s);
+
+// ------------------------------------------------------------ conditioning
+// temb = W2 SiLU(W1 se + b1) + b2 (se: 256-entry sinusoid computed on the host)
+void launch_time_mlp(const float *se, const float *w1, const float *b1, const float *w2, const float *b2,
+                     float *h1_scratch, float *temb, cudaStream_t s);
+// spk_c[u] = scale * LN_affine(Wx spk[u] + bx), eps 1e-5
+void launch_speaker_cond(const float *spk, int n_utt, const float *w, const float *b, const float *ln_w,
+                         const float *ln_b, float scale, float *spk_c, cudaStream_t s);
+// a_cond[r] = bf16(SiLU(temb + spk_c[r / rows_per_utt]))  (spk_c may be null)
+void launch_cond_rows(const float *temb, const float *spk_c, int rows, int rows_per_utt, bf16 *a_cond,
+                      cudaStream_t s);
+
+// ------------------------------------------------------------ DiT output head
+// vel[r][p] = W_out (LN(h[r, L-P+p]) (1 + scale_r) + shift_r) + b_out
+void launch_out_head(const float *h, int rows, int L, int P, const float *shift, const float *scale,
+                     long long ada_ld, const float *w_out, const float *b_out, float *vel, int *err,
+                     cudaStream_t s);
+// CFG combine + Euler update + coord_proj of the new z into the noise tokens of
+// both rows of each utterance (update = 0: only the coord_proj of z).
+void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_scale, int cfg_form, float dt,
+                      int update, const float *w_coord, const float *b_coord, bf16 *x_in, int L,
+                      cudaStream_t s);
+
+// ------------------------------------------------------------ PatchEncoder
+// causal Conv1d(128->128, k=2, s=2); tokens t of sequence b use frames 2t-1, 2t
+// of the concatenation [tail[b] | frames[b]]; writes bf16 [B*T][128] and, if
+// new_tail != nullptr, stores the last frame of each sequence there.
+void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *w, const float *bias,
+                    bf16 *out, float *new_tail, cudaStream_t s);
+// out[b*n + p] = bf16([h[b, tok0] | h[b, tok1]]) with the pairing rule
+void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s);
+
+}  // namespace dtts

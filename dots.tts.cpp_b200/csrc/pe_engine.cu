@@ -1,0 +1,340 @@
+// PatchEncoder (src/modules/backbone/patchenc.cpp:146-239) on sm_100a, with
+// the streaming decode the reference declares but never defines
+// (include/patchenc.h:78-90): a per-sequence KV cache of post-RoPE keys and
+// values for every layer plus the last input frame (the causal conv tail).
+//
+// One call appends n_frames (a multiple of 4) to B streams:
+//   conv (k=2, s=2, taps 2t-1, 2t of [tail | frames]) -> in_proj GEMM ->
+//   24 x [RMSNorm*w -> QKV GEMM (RoPE epilogue, K/V written into the cache) ->
+//         causal attention over cache + new tokens -> O GEMM (+residual) ->
+//         RMSNorm*w -> FFN1 GEMM (+SiLU) -> FFN2 GEMM (+residual)] ->
+//   token pairs -> out_proj GEMM.
+// Attention and conv are causal, so any split of a sequence into calls gives
+// the stateless forward over the whole prefix.
+#include "kernels.cuh"
+#include "runtime.h"
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+using namespace dtts;
+
+namespace {
+constexpr int kBN = 256;
+
+int up_f32(DeviceArena &a, const float *h, size_t n, float **out) {
+    *out = nullptr;
+    if (!h) return DTTS_OK;
+    void *d = a.alloc(n * 4);
+    DTTS_CHECK(d, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(d, h, n * 4, cudaMemcpyHostToDevice));
+    *out = (float *)d;
+    return DTTS_OK;
+}
+
+int up_bf16(DeviceArena &a, const std::vector<const float *> &parts, size_t rows_each, size_t cols, bf16 **out) {
+    std::vector<uint16_t> tmp(parts.size() * rows_each * cols);
+    for (size_t i = 0; i < parts.size(); i++) f32_to_bf16_host(parts[i], tmp.data() + i * rows_each * cols, rows_each * cols);
+    void *d = a.alloc(tmp.size() * 2);
+    DTTS_CHECK(d, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(d, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice));
+    *out = (bf16 *)d;
+    return DTTS_OK;
+}
+
+GemmOp op0(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int epi, int *err) {
+    GemmOp op;
+    std::memset(&op, 0, sizeof(op));
+    op.ta = ta; op.tb = tb; op.M = M; op.N = N; op.K = K; op.bn = kBN; op.epi = epi;
+    op.ep.err = err; op.ep.tok_per_row = 1;
+    return op;
+}
+}  // namespace
+
+struct dtts_pe {
+    int device = 0, dtype = DTTS_DTYPE_BF16, num_sms = 148;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    DeviceArena wts, cache, ws;
+    int n_layers = 0, max_batch = 0, max_tokens = 0;
+    struct Layer {
+        bf16 *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr;
+        float *bo = nullptr, *b1 = nullptr, *b2 = nullptr, *an = nullptr, *fn = nullptr;
+        CUtensorMap tqkv, to, t1, t2;
+    };
+    std::vector<Layer> layers;
+    float *conv_w = nullptr, *conv_b = nullptr, *in_b = nullptr, *out_b = nullptr;
+    bf16 *in_w = nullptr, *out_w = nullptr;
+    CUtensorMap t_inw, t_outw;
+    bf16 *kc = nullptr, *vc = nullptr;   // [n_layers][max_batch][max_tokens][1024]
+    float *tail[2] = {nullptr, nullptr}; // [max_batch][128], double-buffered
+    int tail_cur = 0;
+    float2 *rope = nullptr;              // [max_tokens][32], adjacent-pair rotation
+    int *d_err = nullptr;
+    int cur_B = 0, cur_len = 0;
+    // workspace
+    long long cap_tok = 0;
+    float *frames = nullptr, *h = nullptr, *outf = nullptr;
+    bf16 *conv = nullptr, *act = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *pairs = nullptr;
+    CUtensorMap t_conv, t_act, t_att, t_ffn, t_pairs;
+    int launches = 0;
+
+    ~dtts_pe() {
+        ws.free_all();
+        cache.free_all();
+        wts.free_all();
+        if (own_stream) cudaStreamDestroy(own_stream);
+    }
+
+    int ensure(long long tok) {
+        if (tok <= cap_tok) return DTTS_OK;
+        DTTS_CUDA(cudaStreamSynchronize(stream));
+        ws.free_all();
+        cap_tok = std::max<long long>(tok, 64);
+        const size_t T = (size_t)cap_tok;
+        frames = (float *)ws.alloc(T * 2 * kLat * 4);
+        conv = (bf16 *)ws.alloc(T * kLat * 2);
+        h = (float *)ws.alloc(T * kD * 4);
+        act = (bf16 *)ws.alloc(T * kD * 2);
+        q = (bf16 *)ws.alloc(T * kD * 2);
+        att = (bf16 *)ws.alloc(T * kD * 2);
+        ffn = (bf16 *)ws.alloc(T * kF * 2);
+        pairs = (bf16 *)ws.alloc(T * kD * 2);   // [T/2][2048]
+        outf = (float *)ws.alloc((T / 2 + 1) * kLLM * 4);
+        for (void *p : ws.ptrs)
+            if (!p) { ws.free_all(); cap_tok = 0; set_error("workspace allocation failed"); return DTTS_ERR_OOM; }
+        bool ok = make_tmap_bf16(&t_conv, conv, T, kLat, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
+                  make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
+                  make_tmap_bf16(&t_pairs, pairs, T / 2 > 0 ? T / 2 : 1, 2 * kD, 128);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder workspace)");
+        return DTTS_OK;
+    }
+
+    int gemm(const GemmOp &op) {
+        launches++;
+        DTTS_CUDA(launch_gemm(op, num_sms, stream));
+        return DTTS_OK;
+    }
+
+    // frames already in `this->frames` ([B][n_frames][128]); output in outf.
+    int enqueue_append(int B, int n_frames, int pair_mode) {
+        const int T = n_frames / 2, M = B * T, n_out = n_frames / 4;
+        const float *tail_in = cur_len > 0 ? tail[tail_cur] : nullptr;
+        float *tail_out = tail[tail_cur ^ 1];
+        launches++;
+        launch_pe_conv(frames, B, n_frames, tail_in, conv_w, conv_b, conv, tail_out, stream);
+        int st;
+        {
+            GemmOp op = op0(t_conv, t_inw, M, kD, kLat, EPI_F32, d_err);
+            op.ep.bias = in_b; op.ep.out = h; op.ep.ldo = kD;
+            if ((st = gemm(op))) return st;
+        }
+        const size_t layer_stride = (size_t)max_batch * max_tokens * kD;
+        for (int l = 0; l < n_layers; l++) {
+            const Layer &Ly = layers[l];
+            launches++;
+            launch_rms_norm(h, act, M, Ly.an, stream);
+            {
+                GemmOp op = op0(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
+                op.ep.q = q; op.ep.ldq = kD;
+                op.ep.k = kc + l * layer_stride; op.ep.v = vc + l * layer_stride; op.ep.ldkv = kD;
+                op.ep.tok_per_row = T; op.ep.kv_cap = max_tokens; op.ep.kv_start = cur_len;
+                op.ep.qk_norm = 0; op.ep.rope = rope; op.ep.rope_mode = ROPE_ADJACENT;
+                if ((st = gemm(op))) return st;
+            }
+            {
+                AttnArgs a;
+                a.q = q; a.ldq = kD; a.k = kc + l * layer_stride; a.v = vc + l * layer_stride; a.ldkv = kD;
+                a.o = att; a.ldo = kD; a.rows = B; a.Tq = T; a.kv_len = cur_len + T; a.kv_cap = max_tokens;
+                a.q_pos0 = cur_len; a.causal = 1; a.mask = nullptr; a.scale = 1.0f / sqrtf(64.0f);
+                launches++;
+                launch_attention_bf16(a, stream);
+            }
+            {
+                GemmOp op = op0(t_att, Ly.to, M, kD, kD, EPI_RESID, d_err);
+                op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
+                if ((st = gemm(op))) return st;
+            }
+            launches++;
+            launch_rms_norm(h, act, M, Ly.fn, stream);
+            {
+                GemmOp op = op0(t_act, Ly.t1, M, kF, kD, EPI_SILU_BF16, d_err);
+                op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
+                if ((st = gemm(op))) return st;
+            }
+            {
+                GemmOp op = op0(t_ffn, Ly.t2, M, kD, kF, EPI_RESID, d_err);
+                op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
+                if ((st = gemm(op))) return st;
+            }
+        }
+        launches++;
+        launch_pe_pairs(h, B, T, pair_mode, pairs, stream);
+        {
+            GemmOp op = op0(t_pairs, t_outw, B * n_out, kLLM, 2 * kD, EPI_F32, d_err);
+            op.ep.bias = out_b; op.ep.out = outf; op.ep.ldo = kLLM;
+            if ((st = gemm(op))) return st;
+        }
+        DTTS_CUDA(cudaGetLastError());
+        return DTTS_OK;
+    }
+
+    int finish(bool host_wait) {
+        if (!host_wait) return DTTS_OK;
+        int st = stream_wait(stream, 300.0);
+        if (st) return st;
+        int err = 0;
+        DTTS_CUDA(cudaMemcpy(&err, d_err, 4, cudaMemcpyDeviceToHost));
+        if (err) { cudaMemset(d_err, 0, 4); set_error("device wait limit reached (code %d)", err); return DTTS_ERR_TIMEOUT; }
+        return DTTS_OK;
+    }
+
+    int append(const float *frames_in, int B, int n_frames, int pair_mode, float *out, int mem) {
+        DTTS_CHECK(frames_in && out, DTTS_ERR_ARG, "null argument");
+        DTTS_CHECK(n_frames >= 4 && n_frames % 4 == 0, DTTS_ERR_ARG, "n_frames %d must be a positive multiple of 4", n_frames);
+        DTTS_CHECK(B == cur_B && B >= 1, DTTS_ERR_ARG, "batch %d does not match the %d open streams", B, cur_B);
+        DTTS_CHECK(cur_len + n_frames / 2 <= max_tokens, DTTS_ERR_ARG, "KV cache full (%d + %d > %d tokens)", cur_len,
+                   n_frames / 2, max_tokens);
+        DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
+        DeviceGuard g(device);
+        const long long tok = (long long)B * (n_frames / 2);
+        int st = ensure(tok);
+        if (st) return st;
+        launches = 0;
+        const cudaMemcpyKind ik = mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+        DTTS_CUDA(cudaMemcpyAsync(frames, frames_in, (size_t)B * n_frames * kLat * 4, ik, stream));
+        if ((st = enqueue_append(B, n_frames, pair_mode))) return st;
+        const cudaMemcpyKind ok = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+        DTTS_CUDA(cudaMemcpyAsync(out, outf, (size_t)B * (n_frames / 4) * kLLM * 4, ok, stream));
+        cur_len += n_frames / 2;
+        tail_cur ^= 1;
+        return finish(mem == DTTS_MEM_HOST);
+    }
+};
+
+extern "C" {
+
+int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batch, int max_tokens, dtts_pe **out) {
+    DTTS_CHECK(w && out, DTTS_ERR_ARG, "null argument");
+    *out = nullptr;
+    DTTS_CHECK(w->n_layers >= 1 && w->n_layers <= 64 && w->layers, DTTS_ERR_ARG, "n_layers %d invalid", w->n_layers);
+    DTTS_CHECK(max_batch >= 1 && max_tokens >= 2 && max_tokens <= 65536, DTTS_ERR_ARG, "bad capacity %d x %d",
+               max_batch, max_tokens);
+    DTTS_CHECK(dtype == DTTS_DTYPE_BF16, DTTS_ERR_UNSUPPORTED, "PatchEncoder dtype %d not supported", dtype);
+    DTTS_CHECK(w->conv_w && w->in_w && w->out_w, DTTS_ERR_ARG, "missing a required PatchEncoder weight");
+    for (int l = 0; l < w->n_layers; l++) {
+        const dtts_pe_layer_weights &L = w->layers[l];
+        DTTS_CHECK(L.wq && L.wk && L.wv && L.wo && L.w1 && L.w2, DTTS_ERR_ARG, "missing weight in layer %d", l);
+    }
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    std::unique_ptr<dtts_pe> p(new dtts_pe());
+    p->device = device; p->dtype = dtype; p->num_sms = nsm; p->n_layers = w->n_layers;
+    p->max_batch = max_batch; p->max_tokens = max_tokens;
+    DTTS_CUDA(cudaStreamCreateWithFlags(&p->own_stream, cudaStreamNonBlocking));
+    p->stream = p->own_stream;
+    DTTS_CUDA(gemm_prepare_attributes());
+    p->d_err = (int *)p->wts.alloc(4);
+    DTTS_CHECK(p->d_err, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemset(p->d_err, 0, 4));
+    p->layers.resize(w->n_layers);
+    for (int l = 0; l < w->n_layers; l++) {
+        const dtts_pe_layer_weights &s = w->layers[l];
+        dtts_pe::Layer &L = p->layers[l];
+        if ((st = up_bf16(p->wts, {s.wq, s.wk, s.wv}, kD, kD, &L.wqkv))) return st;
+        if ((st = up_bf16(p->wts, {s.wo}, kD, kD, &L.wo))) return st;
+        if ((st = up_bf16(p->wts, {s.w1}, kF, kD, &L.w1))) return st;
+        if ((st = up_bf16(p->wts, {s.w2}, kD, kF, &L.w2))) return st;
+        if ((st = up_f32(p->wts, s.bo, kD, &L.bo))) return st;
+        if ((st = up_f32(p->wts, s.b1, kF, &L.b1))) return st;
+        if ((st = up_f32(p->wts, s.b2, kD, &L.b2))) return st;
+        if ((st = up_f32(p->wts, s.attn_norm_w, kD, &L.an))) return st;
+        if ((st = up_f32(p->wts, s.ffn_norm_w, kD, &L.fn))) return st;
+        bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, kBN) && make_tmap_bf16(&L.to, L.wo, kD, kD, kBN) &&
+                  make_tmap_bf16(&L.t1, L.w1, kF, kD, kBN) && make_tmap_bf16(&L.t2, L.w2, kD, kF, kBN);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder layer %d)", l);
+    }
+    if ((st = up_f32(p->wts, w->conv_w, (size_t)kLat * kLat * 2, &p->conv_w))) return st;
+    if ((st = up_f32(p->wts, w->conv_b, kLat, &p->conv_b))) return st;
+    if ((st = up_bf16(p->wts, {w->in_w}, kD, kLat, &p->in_w))) return st;
+    if ((st = up_f32(p->wts, w->in_b, kD, &p->in_b))) return st;
+    if ((st = up_bf16(p->wts, {w->out_w}, kLLM, 2 * kD, &p->out_w))) return st;
+    if ((st = up_f32(p->wts, w->out_b, kLLM, &p->out_b))) return st;
+    bool ok = make_tmap_bf16(&p->t_inw, p->in_w, kD, kLat, kBN) && make_tmap_bf16(&p->t_outw, p->out_w, kLLM, 2 * kD, kBN);
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder projections)");
+    // KV cache and conv tails
+    const size_t cache_elems = (size_t)w->n_layers * max_batch * max_tokens * kD;
+    p->kc = (bf16 *)p->cache.alloc(cache_elems * 2);
+    p->vc = (bf16 *)p->cache.alloc(cache_elems * 2);
+    p->tail[0] = (float *)p->cache.alloc((size_t)max_batch * kLat * 4);
+    p->tail[1] = (float *)p->cache.alloc((size_t)max_batch * kLat * 4);
+    p->rope = (float2 *)p->cache.alloc((size_t)max_tokens * 32 * sizeof(float2));
+    DTTS_CHECK(p->kc && p->vc && p->tail[0] && p->tail[1] && p->rope, DTTS_ERR_OOM,
+               "KV cache allocation failed (%zu MB)", cache_elems * 4 >> 20);
+    // ggml_rope mode 0: theta starts at the position and is multiplied by
+    // 1e4^(-2/64) for each successive adjacent pair.
+    std::vector<float2> rt((size_t)max_tokens * 32);
+    const float theta_scale = powf(10000.0f, -2.0f / 64.0f);
+    for (int pos = 0; pos < max_tokens; pos++) {
+        float theta = (float)pos;
+        for (int i = 0; i < 32; i++) {
+            rt[(size_t)pos * 32 + i] = make_float2(cosf(theta), sinf(theta));
+            theta *= theta_scale;
+        }
+    }
+    DTTS_CUDA(cudaMemcpy(p->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    *out = p.release();
+    return DTTS_OK;
+}
+
+int dtts_pe_destroy(dtts_pe *p) {
+    if (!p) return DTTS_OK;
+    DeviceGuard g(p->device);
+    cudaStreamSynchronize(p->stream);
+    delete p;
+    return DTTS_OK;
+}
+
+int dtts_pe_set_stream(dtts_pe *p, void *stream) {
+    DTTS_CHECK(p, DTTS_ERR_ARG, "null engine");
+    p->stream = stream ? static_cast<cudaStream_t>(stream) : p->own_stream;
+    return DTTS_OK;
+}
+
+int dtts_pe_sync(dtts_pe *p) {
+    DTTS_CHECK(p, DTTS_ERR_ARG, "null engine");
+    DeviceGuard g(p->device);
+    return p->finish(true);
+}
+
+int dtts_pe_stream_reset(dtts_pe *p, int B) {
+    DTTS_CHECK(p, DTTS_ERR_ARG, "null engine");
+    DTTS_CHECK(B >= 1 && B <= p->max_batch, DTTS_ERR_ARG, "batch %d out of [1, %d]", B, p->max_batch);
+    p->cur_B = B;
+    p->cur_len = 0;
+    p->tail_cur = 0;
+    return DTTS_OK;
+}
+
+int dtts_pe_forward(dtts_pe *p, const float *frames, int B, int n_frames, int pair_mode, float *out, int mem) {
+    DTTS_CHECK(p, DTTS_ERR_ARG, "null engine");
+    DTTS_CHECK(pair_mode == DTTS_PAIR_ADJACENT || pair_mode == DTTS_PAIR_AS_WRITTEN, DTTS_ERR_ARG, "bad pair_mode");
+    int st = dtts_pe_stream_reset(p, B);
+    if (st) return st;
+    return p->append(frames, B, n_frames, pair_mode, out, mem);
+}
+
+int dtts_pe_decode(dtts_pe *p, const float *frames, int B, int n_frames, float *out, int mem) {
+    DTTS_CHECK(p, DTTS_ERR_ARG, "null engine");
+    return p->append(frames, B, n_frames, DTTS_PAIR_ADJACENT, out, mem);
+}
+
+int dtts_pe_stream_length(dtts_pe *p, int *tokens) {
+    DTTS_CHECK(p && tokens, DTTS_ERR_ARG, "null argument");
+    *tokens = p->cur_len;
+    return DTTS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+// Self-test entry points: run one engine kernel in isolation on host data so
+// tests can check it against a CPU reference (bf16 rounding is applied to the
+// inputs on the host, exactly as the engine stores them).
+#include "kernels.cuh"
+#include "runtime.h"
+
+#include <cstring>
+#include <vector>
+
+using namespace dtts;
+
+namespace {
+struct Scratch {
+    DeviceArena a;
+    ~Scratch() { a.free_all(); }
+};
+}  // namespace
+
+extern "C" {
+
+// C[M][N] = A[M][K] B[N][K]^T (+ bias[N]) through the tcgen05 GEMM kernel with
+// the fp32-output epilogue; bn = 128 or 256.
+int dtts_selftest_gemm(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, int bn,
+                       int device) {
+    DTTS_CHECK(A && B && C, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(M >= 1 && K >= 64 && K % 64 == 0 && (bn == 128 || bn == 256) && N % bn == 0, DTTS_ERR_ARG,
+               "bad GEMM shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    DTTS_CUDA(gemm_prepare_attributes());
+    Scratch s;
+    std::vector<uint16_t> ha((size_t)M * K), hb((size_t)N * K);
+    f32_to_bf16_host(A, ha.data(), ha.size());
+    f32_to_bf16_host(B, hb.data(), hb.size());
+    void *da = s.a.alloc(ha.size() * 2), *db = s.a.alloc(hb.size() * 2), *dc = s.a.alloc((size_t)M * N * 4);
+    void *dbias = bias ? s.a.alloc((size_t)N * 4) : nullptr;
+    int *derr = (int *)s.a.alloc(4);
+    DTTS_CHECK(da && db && dc && derr && (!bias || dbias), DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(da, ha.data(), ha.size() * 2, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemcpy(db, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice));
+    if (bias) DTTS_CUDA(cudaMemcpy(dbias, bias, (size_t)N * 4, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemset(dc, 0xff, (size_t)M * N * 4));
+    DTTS_CUDA(cudaMemset(derr, 0, 4));
+    GemmOp op;
+    std::memset(&op, 0, sizeof(op));
+    bool ok = make_tmap_bf16(&op.ta, da, M, K, 128) && make_tmap_bf16(&op.tb, db, N, K, bn);
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map encode failed");
+    op.M = M; op.N = N; op.K = K; op.bn = bn; op.epi = EPI_F32;
+    op.ep.out = dc; op.ep.ldo = N; op.ep.bias = (const float *)dbias; op.ep.err = derr; op.ep.tok_per_row = 1;
+    DTTS_CUDA(launch_gemm(op, nsm, 0));
+    if ((st = stream_wait(0, 60.0))) return st;
+    int err = 0;
+    DTTS_CUDA(cudaMemcpy(&err, derr, 4, cudaMemcpyDeviceToHost));
+    DTTS_CHECK(err == 0, DTTS_ERR_TIMEOUT, "GEMM kernel wait limit reached (code %d)", err);
+    DTTS_CUDA(cudaMemcpy(C, dc, (size_t)M * N * 4, cudaMemcpyDeviceToHost));
+    return DTTS_OK;
+}
+
+// Attention core alone: q [rows][Tq][1024], k/v [rows][kv_len][1024] (fp32,
+// rounded to bf16 on upload), out [rows][Tq][1024] fp32.  mask [Tq][kv_len] or
+// NULL; causal with the first query at absolute position q_pos0.
+int dtts_selftest_attention(const float *q, const float *k, const float *v, float *out, int rows, int Tq,
+                            int kv_len, const uint8_t *mask, int causal, int q_pos0, int use_f32, int device) {
+    DTTS_CHECK(q && k && v && out, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(rows >= 1 && Tq >= 1 && kv_len >= 1, DTTS_ERR_ARG, "bad attention shape");
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    Scratch s;
+    const size_t nq = (size_t)rows * Tq * kD, nk = (size_t)rows * kv_len * kD;
+    const size_t esz = use_f32 ? 4 : 2;
+    void *dq = s.a.alloc(nq * esz), *dk = s.a.alloc(nk * esz), *dv = s.a.alloc(nk * esz), *dout = s.a.alloc(nq * esz);
+    void *dm = mask ? s.a.alloc((size_t)Tq * kv_len) : nullptr;
+    DTTS_CHECK(dq && dk && dv && dout && (!mask || dm), DTTS_ERR_OOM, "cudaMalloc failed");
+    if (use_f32) {
+        DTTS_CUDA(attention_f32_prepare());
+        DTTS_CUDA(cudaMemcpy(dq, q, nq * 4, cudaMemcpyHostToDevice));
+        DTTS_CUDA(cudaMemcpy(dk, k, nk * 4, cudaMemcpyHostToDevice));
+        DTTS_CUDA(cudaMemcpy(dv, v, nk * 4, cudaMemcpyHostToDevice));
+    } else {
+        std::vector<uint16_t> t(std::max(nq, nk));
+        f32_to_bf16_host(q, t.data(), nq);
+        DTTS_CUDA(cudaMemcpy(dq, t.data(), nq * 2, cudaMemcpyHostToDevice));
+        f32_to_bf16_host(k, t.data(), nk);
+        DTTS_CUDA(cudaMemcpy(dk, t.data(), nk * 2, cudaMemcpyHostToDevice));
+        f32_to_bf16_host(v, t.data(), nk);
+        DTTS_CUDA(cudaMemcpy(dv, t.data(), nk * 2, cudaMemcpyHostToDevice));
+    }
+    if (mask) DTTS_CUDA(cudaMemcpy(dm, mask, (size_t)Tq * kv_len, cudaMemcpyHostToDevice));
+    AttnArgs a;
+    a.q = dq; a.k = dk; a.v = dv; a.o = dout; a.ldq = a.ldkv = a.ldo = kD;
+    a.rows = rows; a.Tq = Tq; a.kv_len = kv_len; a.kv_cap = kv_len; a.q_pos0 = q_pos0; a.causal = causal;
+    a.mask = (const uint8_t *)dm; a.scale = 0.125f;
+    if (use_f32) DTTS_CUDA(launch_attention_f32(a, 0));
+    else launch_attention_bf16(a, 0);
+    DTTS_CUDA(cudaGetLastError());
+    if ((st = stream_wait(0, 60.0))) return st;
+    if (use_f32) {
+        DTTS_CUDA(cudaMemcpy(out, dout, nq * 4, cudaMemcpyDeviceToHost));
+    } else {
+        std::vector<uint16_t> t(nq);
+        DTTS_CUDA(cudaMemcpy(t.data(), dout, nq * 2, cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < nq; i++) { uint32_t u = (uint32_t)t[i] << 16; std::memcpy(&out[i], &u, 4); }
+    }
+    return DTTS_OK;
+}
+
+}  // extern "C"

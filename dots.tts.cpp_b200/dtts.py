@@ -1,0 +1,460 @@
+"""ctypes binding of libdtts.so (include/dtts.h) for tests and the benchmark.
+
+Loads the in-tree library built by build.py and fails loudly if it is
+missing: there is no CPU fallback.  Weights are dicts of float32 numpy arrays
+keyed by the reference's safetensors tensor names (see synth.py)."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdtts.so")
+
+OK, ERR_ARG, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_NONFINITE, ERR_UNSUPPORTED, ERR_IO, ERR_NO_DEVICE = \
+    0, -1, -2, -3, -4, -5, -6, -7, -8
+DTYPE_BF16, DTYPE_FP8, DTYPE_F32 = 0, 1, 2
+MEM_HOST, MEM_DEVICE = 0, 1
+CFG_V4, CFG_V3 = 0, 1
+LAYOUT_FM_MASK, LAYOUT_FULL = 0, 1
+PAIR_ADJACENT, PAIR_AS_WRITTEN = 0, 1
+
+_fp = C.POINTER(C.c_float)
+_u8p = C.POINTER(C.c_uint8)
+_vp = C.c_void_p
+
+
+class DitBlockW(C.Structure):
+    _fields_ = [(n, _fp) for n in ("wq", "wk", "wv", "wo", "bo", "qn", "kn", "w1", "b1", "w2", "b2",
+                                   "ada_w", "ada_b")]
+
+
+class DitW(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("blocks", C.POINTER(DitBlockW))] + [
+        (n, _fp) for n in ("t_w1", "t_b1", "t_w2", "t_b2", "spk_w1", "spk_b1", "spk_ln_w", "spk_ln_b",
+                           "oada_w", "oada_b", "out_w", "out_b", "in_w", "in_b", "hid_w", "hid_b", "lat_w",
+                           "lat_b", "coord_w", "coord_b")]
+
+
+class AttnW(C.Structure):
+    _fields_ = [(n, _fp) for n in ("wq", "wk", "wv", "wo", "bo", "qn", "kn")]
+
+
+class PeLayerW(C.Structure):
+    _fields_ = [(n, _fp) for n in ("attn_norm_w", "wq", "wk", "wv", "wo", "bo", "ffn_norm_w", "w1", "b1",
+                                   "w2", "b2")]
+
+
+class PeW(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("layers", C.POINTER(PeLayerW))] + [
+        (n, _fp) for n in ("conv_w", "conv_b", "in_w", "in_b", "out_w", "out_b")]
+
+
+class SolveArgs(C.Structure):
+    _fields_ = [("n_utt", C.c_int), ("fm_len", C.c_int), ("patch", C.c_int),
+                ("fm_cond", _vp), ("fm_uncond", _vp), ("z0", _vp), ("spk", _vp),
+                ("spk_scale", C.c_float), ("nfe", C.c_int), ("cfg_scale", C.c_float), ("cfg_form", C.c_int),
+                ("layout", C.c_int), ("z_out", _vp), ("mem", C.c_int), ("use_graph", C.c_int)]
+
+
+DIT_BLOCK_NAMES = {
+    "wq": "attn.q_proj.weight", "wk": "attn.k_proj.weight", "wv": "attn.v_proj.weight",
+    "wo": "attn.o_proj.weight", "bo": "attn.o_proj.bias", "qn": "attn.q_norm.weight",
+    "kn": "attn.k_norm.weight", "w1": "ffn.fc1.weight", "b1": "ffn.fc1.bias",
+    "w2": "ffn.fc2.weight", "b2": "ffn.fc2.bias", "ada_w": "adaLN_modulation.1.weight",
+    "ada_b": "adaLN_modulation.1.bias",
+}
+DIT_GLOBAL_NAMES = {
+    "t_w1": "velocity_field_predictor.time_embedder.mlp.0.weight",
+    "t_b1": "velocity_field_predictor.time_embedder.mlp.0.bias",
+    "t_w2": "velocity_field_predictor.time_embedder.mlp.2.weight",
+    "t_b2": "velocity_field_predictor.time_embedder.mlp.2.bias",
+    "spk_w1": "xvec_proj.0.weight", "spk_b1": "xvec_proj.0.bias",
+    "spk_ln_w": "xvec_proj.1.weight", "spk_ln_b": "xvec_proj.1.bias",
+    "oada_w": "velocity_field_predictor.output_layer.adaLN_modulation.1.weight",
+    "oada_b": "velocity_field_predictor.output_layer.adaLN_modulation.1.bias",
+    "out_w": "velocity_field_predictor.output_layer.linear.weight",
+    "out_b": "velocity_field_predictor.output_layer.linear.bias",
+    "in_w": "velocity_field_predictor.input_layer.weight",
+    "in_b": "velocity_field_predictor.input_layer.bias",
+    "hid_w": "hidden_proj.weight", "hid_b": "hidden_proj.bias",
+    "lat_w": "latent_proj.weight", "lat_b": "latent_proj.bias",
+    "coord_w": "coordinate_proj.weight", "coord_b": "coordinate_proj.bias",
+}
+PE_LAYER_NAMES = {
+    "attn_norm_w": "attn_norm.weight", "wq": "attn.q_proj.weight", "wk": "attn.k_proj.weight",
+    "wv": "attn.v_proj.weight", "wo": "attn.o_proj.weight", "bo": "attn.o_proj.bias",
+    "ffn_norm_w": "ffn_norm.weight", "w1": "ffn.fc1.weight", "b1": "ffn.fc1.bias",
+    "w2": "ffn.fc2.weight", "b2": "ffn.fc2.bias",
+}
+PE_GLOBAL_NAMES = {
+    "conv_w": "patch_encoder.ds_proj.weight", "conv_b": "patch_encoder.ds_proj.bias",
+    "in_w": "patch_encoder.in_proj.weight", "in_b": "patch_encoder.in_proj.bias",
+    "out_w": "patch_encoder.out_proj.weight", "out_b": "patch_encoder.out_proj.bias",
+}
+
+# every symbol include/dtts.h declares (checked against the library by the CPU tests)
+EXPORTS = [
+    "dtts_version", "dtts_status_string", "dtts_last_error", "dtts_device_count",
+    "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
+    "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_euler_solve", "dtts_dit_profile_kernel",
+    "dtts_dit_last_launch_count", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
+    "dtts_attn_profile_core", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
+    "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
+    "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_st_open",
+    "dtts_st_close", "dtts_st_count", "dtts_st_shape", "dtts_st_read_f32",
+]
+
+
+class DttsError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"dtts status {status}: {msg}")
+        self.status = status
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous, "float32 C-contiguous expected"
+    return a.ctypes.data_as(_fp)
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+_LIB = None
+
+
+def lib(path: str = LIB_PATH):
+    """The loaded libdtts.so (raises if it was not built)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} is missing: run `python {os.path.join(HERE, 'build.py')}`")
+    L = C.CDLL(path)
+    L.dtts_version.restype = C.c_char_p
+    L.dtts_status_string.restype = C.c_char_p
+    L.dtts_last_error.restype = C.c_char_p
+    L.dtts_device_count.argtypes = [C.POINTER(C.c_int)]
+    L.dtts_dit_create.argtypes = [C.POINTER(DitW), C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_dit_create_from_safetensors.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_dit_destroy.argtypes = [_vp]
+    L.dtts_dit_set_stream.argtypes = [_vp, _vp]
+    L.dtts_dit_sync.argtypes = [_vp]
+    L.dtts_dit_velocity.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, C.c_int]
+    L.dtts_dit_euler_solve.argtypes = [_vp, C.POINTER(SolveArgs)]
+    L.dtts_dit_profile_kernel.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double),
+                                          C.POINTER(C.c_double)]
+    L.dtts_dit_last_launch_count.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_attn_create.argtypes = [C.POINTER(AttnW), C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_attn_destroy.argtypes = [_vp]
+    L.dtts_attn_forward.argtypes = [_vp, _fp, C.c_int, C.c_int, _u8p, _fp, _fp]
+    L.dtts_attn_profile_core.argtypes = [_vp, C.c_int, C.POINTER(C.c_float)]
+    L.dtts_pe_create.argtypes = [C.POINTER(PeW), C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_pe_create_from_safetensors.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                  C.POINTER(_vp)]
+    L.dtts_pe_destroy.argtypes = [_vp]
+    L.dtts_pe_set_stream.argtypes = [_vp, _vp]
+    L.dtts_pe_sync.argtypes = [_vp]
+    L.dtts_pe_forward.argtypes = [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp, C.c_int]
+    L.dtts_pe_stream_reset.argtypes = [_vp, C.c_int]
+    L.dtts_pe_decode.argtypes = [_vp, _vp, C.c_int, C.c_int, _vp, C.c_int]
+    L.dtts_pe_stream_length.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_selftest_gemm.argtypes = [_fp, _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+    L.dtts_selftest_attention.argtypes = [_fp, _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, _u8p, C.c_int,
+                                          C.c_int, C.c_int, C.c_int]
+    L.dtts_st_open.argtypes = [C.c_char_p, C.POINTER(_vp)]
+    L.dtts_st_close.argtypes = [_vp]
+    L.dtts_st_count.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_st_shape.argtypes = [_vp, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int64)]
+    L.dtts_st_read_f32.argtypes = [_vp, C.c_char_p, _fp, C.c_size_t]
+    _LIB = L
+    return L
+
+
+def check(status):
+    if status != OK:
+        raise DttsError(status, lib().dtts_last_error().decode())
+    return status
+
+
+def device_count():
+    n = C.c_int(0)
+    check(lib().dtts_device_count(C.byref(n)))
+    return n.value
+
+
+# ------------------------------------------------------------------ weights -> structs
+class _Keep:
+    def __init__(self):
+        self.refs = []
+
+
+def dit_struct(w: dict, n_layers: int):
+    keep = _Keep()
+    arr = (DitBlockW * n_layers)()
+    for i in range(n_layers):
+        pre = f"velocity_field_predictor.blocks.{i}."
+        for f, n in DIT_BLOCK_NAMES.items():
+            a = _f32(w.get(pre + n))
+            keep.refs.append(a)
+            setattr(arr[i], f, _ptr(a))
+    s = DitW()
+    s.n_layers = n_layers
+    s.blocks = arr
+    keep.refs.append(arr)
+    for f, n in DIT_GLOBAL_NAMES.items():
+        a = _f32(w.get(n))
+        keep.refs.append(a)
+        setattr(s, f, _ptr(a))
+    return s, keep
+
+
+def pe_struct(w: dict, n_layers: int):
+    keep = _Keep()
+    arr = (PeLayerW * n_layers)()
+    for i in range(n_layers):
+        pre = f"patch_encoder.encoder.layers.{i}."
+        for f, n in PE_LAYER_NAMES.items():
+            a = _f32(w.get(pre + n))
+            keep.refs.append(a)
+            setattr(arr[i], f, _ptr(a))
+    s = PeW()
+    s.n_layers = n_layers
+    s.layers = arr
+    keep.refs.append(arr)
+    for f, n in PE_GLOBAL_NAMES.items():
+        a = _f32(w.get(n))
+        keep.refs.append(a)
+        setattr(s, f, _ptr(a))
+    return s, keep
+
+
+def _addr(a):
+    """Host numpy array -> pointer; anything with data_ptr() (device tensor) -> its address."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+# ------------------------------------------------------------------ engines
+class DiT:
+    """The velocity head on one device."""
+
+    def __init__(self, weights: dict, n_layers: int = 18, dtype=DTYPE_BF16, device=0):
+        s, keep = dit_struct(weights, n_layers)
+        h = _vp()
+        check(lib().dtts_dit_create(C.byref(s), dtype, device, C.byref(h)))
+        self.h = h
+        self.n_layers = n_layers
+
+    @classmethod
+    def from_safetensors(cls, path, n_layers=18, dtype=DTYPE_BF16, device=0):
+        self = cls.__new__(cls)
+        h = _vp()
+        check(lib().dtts_dit_create_from_safetensors(path.encode(), n_layers, dtype, device, C.byref(h)))
+        self.h = h
+        self.n_layers = n_layers
+        return self
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_dit_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr):
+        check(lib().dtts_dit_set_stream(self.h, stream_ptr))
+
+    def sync(self):
+        check(lib().dtts_dit_sync(self.h))
+
+    def velocity(self, x_in, cond, mask=None, pos=None, n_out=None):
+        x_in = _f32(x_in)
+        rows, L = x_in.shape[0], x_in.shape[1]
+        n_out = L if n_out is None else n_out
+        cond = _f32(cond)
+        mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        pos = _f32(pos)
+        out = np.zeros((rows, n_out, 128), np.float32)
+        check(lib().dtts_dit_velocity(self.h, _addr(x_in), _addr(cond), _addr(mask), _addr(pos), rows, L, n_out,
+                                      _addr(out), MEM_HOST))
+        return out
+
+    def solve(self, fm_cond, fm_uncond, z0, spk=None, spk_scale=1.5, nfe=10, cfg_scale=2.0, cfg_form=CFG_V4,
+              layout=LAYOUT_FM_MASK, use_graph=True, z_out=None, mem=MEM_HOST):
+        """Euler + CFG solve.  With mem=MEM_DEVICE every buffer is a device
+        tensor (anything with data_ptr()) and the call only enqueues."""
+        if mem == MEM_HOST:
+            fm_cond, fm_uncond, z0, spk = _f32(fm_cond), _f32(fm_uncond), _f32(z0), _f32(spk)
+            if z_out is None:
+                z_out = np.zeros_like(z0)
+        a = SolveArgs()
+        a.n_utt, a.fm_len, a.patch = z0.shape[0], fm_cond.shape[1], z0.shape[1]
+        a.fm_cond, a.fm_uncond, a.z0, a.spk = _addr(fm_cond), _addr(fm_uncond), _addr(z0), _addr(spk)
+        a.spk_scale, a.nfe, a.cfg_scale, a.cfg_form = spk_scale, nfe, cfg_scale, cfg_form
+        a.layout, a.z_out, a.mem, a.use_graph = layout, _addr(z_out), mem, int(use_graph)
+        check(lib().dtts_dit_euler_solve(self.h, C.byref(a)))
+        return z_out
+
+    def profile(self, kind, iters=20):
+        us, fl, by = C.c_float(), C.c_double(), C.c_double()
+        check(lib().dtts_dit_profile_kernel(self.h, kind, iters, C.byref(us), C.byref(fl), C.byref(by)))
+        return us.value, fl.value, by.value
+
+    def last_launch_count(self):
+        n = C.c_int()
+        check(lib().dtts_dit_last_launch_count(self.h, C.byref(n)))
+        return n.value
+
+
+class Attention:
+    """The DiT attention sublayer alone (manual_attention)."""
+
+    def __init__(self, wq, wk, wv, wo, bo=None, qn=None, kn=None, dtype=DTYPE_F32, device=0):
+        self._keep = [_f32(a) for a in (wq, wk, wv, wo, bo, qn, kn)]
+        s = AttnW(*[_ptr(a) for a in self._keep])
+        h = _vp()
+        check(lib().dtts_attn_create(C.byref(s), dtype, device, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_attn_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, x, mask=None, pos=None):
+        x = _f32(x)
+        rows, L = x.shape[0], x.shape[1]
+        out = np.zeros_like(x)
+        mk = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        pos = _f32(pos)
+        check(lib().dtts_attn_forward(self.h, _ptr(x), rows, L, None if mk is None else mk.ctypes.data_as(_u8p),
+                                      _ptr(pos), _ptr(out)))
+        return out
+
+    def profile_core(self, iters=50):
+        us = C.c_float()
+        check(lib().dtts_attn_profile_core(self.h, iters, C.byref(us)))
+        return us.value
+
+
+class PatchEncoder:
+    def __init__(self, weights: dict, n_layers=24, max_batch=32, max_tokens=512, dtype=DTYPE_BF16, device=0):
+        s, keep = pe_struct(weights, n_layers)
+        h = _vp()
+        check(lib().dtts_pe_create(C.byref(s), dtype, device, max_batch, max_tokens, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_pe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr):
+        check(lib().dtts_pe_set_stream(self.h, stream_ptr))
+
+    def sync(self):
+        check(lib().dtts_pe_sync(self.h))
+
+    def forward(self, frames, pair_mode=PAIR_ADJACENT):
+        frames = _f32(frames)
+        B, n = frames.shape[0], frames.shape[1]
+        out = np.zeros((B, n // 4, 1536), np.float32)
+        check(lib().dtts_pe_forward(self.h, _addr(frames), B, n, pair_mode, _addr(out), MEM_HOST))
+        return out
+
+    def reset(self, B):
+        check(lib().dtts_pe_stream_reset(self.h, B))
+
+    def decode(self, frames, out=None, mem=MEM_HOST):
+        if mem == MEM_HOST:
+            frames = _f32(frames)
+        B, n = frames.shape[0], frames.shape[1]
+        if out is None:
+            out = np.zeros((B, n // 4, 1536), np.float32)
+        check(lib().dtts_pe_decode(self.h, _addr(frames), B, n, _addr(out), mem))
+        return out
+
+    def length(self):
+        n = C.c_int()
+        check(lib().dtts_pe_stream_length(self.h, C.byref(n)))
+        return n.value
+
+
+def selftest_gemm(A, B, bias=None, bn=256, device=0):
+    A, B, bias = _f32(A), _f32(B), _f32(bias)
+    M, K = A.shape
+    N = B.shape[0]
+    Cm = np.zeros((M, N), np.float32)
+    check(lib().dtts_selftest_gemm(_ptr(A), _ptr(B), _ptr(bias), _ptr(Cm), M, N, K, bn, device))
+    return Cm
+
+
+def selftest_attention(q, k, v, mask=None, causal=False, q_pos0=0, use_f32=False, device=0):
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    rows, Tq, kv = q.shape[0], q.shape[1], k.shape[1]
+    out = np.zeros_like(q)
+    mk = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+    check(lib().dtts_selftest_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), rows, Tq, kv,
+                                        None if mk is None else mk.ctypes.data_as(_u8p), int(causal), q_pos0,
+                                        int(use_f32), device))
+    return out
+
+
+class SafeTensors:
+    def __init__(self, path):
+        h = _vp()
+        check(lib().dtts_st_open(path.encode(), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_st_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def count(self):
+        n = C.c_int()
+        check(lib().dtts_st_count(self.h, C.byref(n)))
+        return n.value
+
+    def shape(self, name):
+        nd = C.c_int()
+        shp = (C.c_int64 * 8)()
+        check(lib().dtts_st_shape(self.h, name.encode(), C.byref(nd), shp))
+        return tuple(shp[i] for i in range(nd.value))
+
+    def read(self, name):
+        shp = self.shape(name)
+        out = np.zeros(shp, np.float32)
+        check(lib().dtts_st_read_f32(self.h, name.encode(), _ptr(out), out.size))
+        return out

@@ -1,0 +1,138 @@
+"""Seeded synthetic weights and inputs in the reference's checkpoint layout.
+
+No checkpoint of the real model is available, so every workload runs on
+random-init weights of the real architecture: matrices and biases drawn from
+N(0, 0.02), norm gains from 1 + N(0, 0.02).  Tensor names and shapes are the
+reference's safetensors names (src/utils/dit_loader.cpp:47-115,
+src/utils/patchenc_loader.cpp:175-208); shapes are PyTorch [out, in].
+
+Each tensor gets its own generator seeded by (seed, crc32(name)), so a
+2-layer test model is exactly the first two layers of the 18-layer one."""
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+
+D, H, HD, F, LAT, LLM, SPK = 1024, 16, 64, 4096, 128, 1536, 512
+DIT_LAYERS, PE_LAYERS = 18, 24
+
+
+def _rng(seed: int, name: str):
+    return np.random.default_rng([int(seed), zlib.crc32(name.encode())])
+
+
+def normal(seed, name, shape, std=0.02, mean=0.0):
+    a = _rng(seed, name).standard_normal(size=shape, dtype=np.float32)
+    if std != 1.0:
+        a *= np.float32(std)
+    if mean != 0.0:
+        a += np.float32(mean)
+    return a
+
+
+def dit_shapes(n_layers=DIT_LAYERS):
+    s = {}
+    for i in range(n_layers):
+        p = f"velocity_field_predictor.blocks.{i}."
+        for n in ("q", "k", "v", "o"):
+            s[p + f"attn.{n}_proj.weight"] = (D, D)
+        s[p + "attn.o_proj.bias"] = (D,)
+        s[p + "attn.q_norm.weight"] = (HD,)
+        s[p + "attn.k_norm.weight"] = (HD,)
+        s[p + "ffn.fc1.weight"] = (F, D)
+        s[p + "ffn.fc1.bias"] = (F,)
+        s[p + "ffn.fc2.weight"] = (D, F)
+        s[p + "ffn.fc2.bias"] = (D,)
+        s[p + "adaLN_modulation.1.weight"] = (6 * D, D)
+        s[p + "adaLN_modulation.1.bias"] = (6 * D,)
+    v = "velocity_field_predictor."
+    s[v + "time_embedder.mlp.0.weight"] = (D, 256)
+    s[v + "time_embedder.mlp.0.bias"] = (D,)
+    s[v + "time_embedder.mlp.2.weight"] = (D, D)
+    s[v + "time_embedder.mlp.2.bias"] = (D,)
+    s["xvec_proj.0.weight"] = (D, SPK)
+    s["xvec_proj.0.bias"] = (D,)
+    s["xvec_proj.1.weight"] = (D,)
+    s["xvec_proj.1.bias"] = (D,)
+    s[v + "output_layer.adaLN_modulation.1.weight"] = (2 * D, D)
+    s[v + "output_layer.adaLN_modulation.1.bias"] = (2 * D,)
+    s[v + "output_layer.linear.weight"] = (LAT, D)
+    s[v + "output_layer.linear.bias"] = (LAT,)
+    s[v + "input_layer.weight"] = (D, D)
+    s[v + "input_layer.bias"] = (D,)
+    s["hidden_proj.weight"] = (D, LLM)
+    s["hidden_proj.bias"] = (D,)
+    s["latent_proj.weight"] = (D, LAT)
+    s["latent_proj.bias"] = (D,)
+    s["coordinate_proj.weight"] = (D, LAT)
+    s["coordinate_proj.bias"] = (D,)
+    return s
+
+
+def pe_shapes(n_layers=PE_LAYERS):
+    s = {}
+    for i in range(n_layers):
+        p = f"patch_encoder.encoder.layers.{i}."
+        for n in ("q", "k", "v", "o"):
+            s[p + f"attn.{n}_proj.weight"] = (D, D)
+        s[p + "attn.o_proj.bias"] = (D,)
+        s[p + "attn_norm.weight"] = (D,)
+        s[p + "ffn_norm.weight"] = (D,)
+        s[p + "ffn.fc1.weight"] = (F, D)
+        s[p + "ffn.fc1.bias"] = (F,)
+        s[p + "ffn.fc2.weight"] = (D, F)
+        s[p + "ffn.fc2.bias"] = (D,)
+    s["patch_encoder.ds_proj.weight"] = (LAT, LAT, 2)
+    s["patch_encoder.ds_proj.bias"] = (LAT,)
+    s["patch_encoder.in_proj.weight"] = (D, LAT)
+    s["patch_encoder.in_proj.bias"] = (D,)
+    s["patch_encoder.out_proj.weight"] = (LLM, 2 * D)
+    s["patch_encoder.out_proj.bias"] = (LLM,)
+    return s
+
+
+def _is_gain(name):
+    return name.endswith(("q_norm.weight", "k_norm.weight", "xvec_proj.1.weight",
+                          "attn_norm.weight", "ffn_norm.weight"))
+
+
+def dit_weights(seed=1, n_layers=DIT_LAYERS, ada_bias_std=0.02):
+    """DiT weights.  ada_bias_std > 0.02 makes shift/scale/gate O(1) so that the
+    attention and FFN branches dominate a block's output (used by block tests)."""
+    w = {}
+    for name, shape in dit_shapes(n_layers).items():
+        if _is_gain(name):
+            w[name] = normal(seed, name, shape, 0.02, 1.0)
+        elif name.endswith("adaLN_modulation.1.bias"):
+            w[name] = normal(seed, name, shape, ada_bias_std)
+        else:
+            w[name] = normal(seed, name, shape, 0.02)
+    return w
+
+
+def pe_weights(seed=2, n_layers=PE_LAYERS):
+    w = {}
+    for name, shape in pe_shapes(n_layers).items():
+        w[name] = normal(seed, name, shape, 0.02, 1.0 if _is_gain(name) else 0.0)
+    return w
+
+
+def fm_history(seed, n_utt, fm_len, w=None, hidden_every=5):
+    """FM history buffers like src/e2e_pipeline_v4.cpp:331-340,551-588: a
+    hidden_proj row at every position p with p % hidden_every == 0 (from
+    h ~ N(0,1) [1536]; the unconditional buffer uses hidden_proj(0)) and
+    latent_proj rows of z ~ N(0,1) [128] elsewhere (shared by both buffers).
+    Projections are computed in fp64 and rounded to fp32 (inputs, not the
+    path under test).  Returns (fm_cond, fm_uncond), each [n_utt][fm_len][1024]."""
+    hw, hb = w["hidden_proj.weight"].astype(np.float64), w["hidden_proj.bias"].astype(np.float64)
+    lw, lb = w["latent_proj.weight"].astype(np.float64), w["latent_proj.bias"].astype(np.float64)
+    hid = normal(seed, "fm.hidden", (n_utt, fm_len, LLM), 1.0).astype(np.float64)
+    lat = normal(seed, "fm.latent", (n_utt, fm_len, LAT), 1.0).astype(np.float64)
+    is_hidden = (np.arange(fm_len) % hidden_every) == 0
+    hproj = hid @ hw.T + hb
+    lproj = lat @ lw.T + lb
+    cond = np.where(is_hidden[None, :, None], hproj, lproj).astype(np.float32)
+    null_h = np.broadcast_to(hb, (n_utt, fm_len, D))
+    uncond = np.where(is_hidden[None, :, None], null_h, lproj).astype(np.float32)
+    return np.ascontiguousarray(cond), np.ascontiguousarray(uncond)

@@ -1,0 +1,232 @@
+/* dtts.h - C ABI of the B200 (sm_100a) engine for the dots.tts DiT flow-matching
+ * head and PatchEncoder.
+ *
+ * Plain pointers and sizes only.  Every function returns an int status
+ * (DTTS_OK = 0, negative DTTS_ERR_* on failure); dtts_last_error() gives a
+ * one-line reason for the calling thread's last failure.  The engine never
+ * falls back to the CPU: without a usable sm_100 device, create calls fail
+ * with DTTS_ERR_NO_DEVICE.
+ *
+ * Memory conventions (all fp32 unless noted, row-major, weights PyTorch
+ * [out][in] as in the reference's safetensors checkpoint):
+ *   DTTS_MEM_HOST    pointers are host memory; the call is synchronous and
+ *                    copies in and out itself.
+ *   DTTS_MEM_DEVICE  pointers are device memory on the engine's device; the
+ *                    call only enqueues work on the engine's stream
+ *                    (dtts_*_set_stream), dtts_*_sync() waits and reports
+ *                    device-side errors.
+ * One engine serves one device; calls on one engine must be serialised by
+ * the caller (the reference is single-threaded host code).  Independent
+ * engines (one per GPU, one host thread each) run concurrently.
+ *
+ * Reference interfaces replaced (paths in MaurerAnton/dots.tts.cpp):
+ *   dtts_dit_create*          load_dit_weights        src/utils/dit_loader.cpp:15
+ *                                                     (+ dit_model, include/dit.h:74-126)
+ *   dtts_dit_velocity         manual_dit_block x18 + output layer
+ *                                                     include/dit_manual.h:148,
+ *                                                     src/e2e_pipeline_v4.cpp:438-478
+ *                             dit_forward_raw         include/dit.h:152
+ *   dtts_dit_euler_solve      Euler + CFG loop        src/e2e_pipeline_v4.cpp:402-533
+ *   dtts_attn_*               manual_attention        include/dit_manual.h:88
+ *   dtts_pe_create*           load_patchenc_weights   src/utils/patchenc_loader.cpp:14
+ *   dtts_pe_forward           patchenc_forward        include/patchenc.h:70
+ *   dtts_pe_stream_reset      patchenc_stream_init    include/patchenc.h:80 (declared only)
+ *   dtts_pe_decode            patchenc_decode_step    include/patchenc.h:85 (declared only)
+ *   dtts_st_*                 SafeTensorsFile         include/safetensors.h:23
+ */
+#ifndef DTTS_H
+#define DTTS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DTTS_OK                0
+#define DTTS_ERR_ARG          -1   /* bad argument or shape                          */
+#define DTTS_ERR_CUDA         -2   /* CUDA runtime / launch error                     */
+#define DTTS_ERR_OOM          -3   /* device allocation failed                        */
+#define DTTS_ERR_TIMEOUT      -4   /* a kernel wait or a host wait hit its limit       */
+#define DTTS_ERR_NONFINITE    -5   /* the velocity contained NaN/Inf                   */
+#define DTTS_ERR_UNSUPPORTED  -6   /* valid request this build does not implement      */
+#define DTTS_ERR_IO           -7   /* file missing / malformed / tensor absent          */
+#define DTTS_ERR_NO_DEVICE    -8   /* no sm_100 device with that ordinal                */
+
+#define DTTS_DTYPE_BF16  0   /* bf16 weights and activations, fp32 accumulate/residual */
+#define DTTS_DTYPE_FP8   1   /* e4m3 weights, per-output-channel fp32 scales           */
+#define DTTS_DTYPE_F32   2   /* fp32 everywhere (attention sublayer only)              */
+
+#define DTTS_MEM_HOST    0
+#define DTTS_MEM_DEVICE  1
+
+#define DTTS_CFG_V4      0   /* v = v_c + s (v_c - v_u)  src/e2e_pipeline_v4.cpp:511 */
+#define DTTS_CFG_V3      1   /* v = v_u + s (v_c - v_u)  src/e2e_pipeline.cpp:444    */
+
+#define DTTS_LAYOUT_FM_MASK  0 /* v4 FM mask + position ids, src/e2e_pipeline_v4.cpp:120-155 */
+#define DTTS_LAYOUT_FULL     1 /* no mask, positions 0..L-1                                  */
+
+#define DTTS_PAIR_ADJACENT   0 /* PE output p = out_proj([h_2p | h_2p+1])                       */
+#define DTTS_PAIR_AS_WRITTEN 1 /* patchenc.cpp:230-232 reshape/permute as written (n_patches > 1) */
+
+/* ------------------------------------------------------------------ weights */
+typedef struct dtts_dit_block_weights {
+    const float *wq, *wk, *wv, *wo;   /* [1024][1024]                          */
+    const float *bo;                  /* [1024] or NULL                        */
+    const float *qn, *kn;             /* [64] per-head RMS gains or NULL       */
+    const float *w1, *b1;             /* [4096][1024], [4096]                  */
+    const float *w2, *b2;             /* [1024][4096], [1024]                  */
+    const float *ada_w, *ada_b;       /* [6144][1024], [6144]                  */
+} dtts_dit_block_weights;
+
+typedef struct dtts_dit_weights {
+    int n_layers;                     /* 18 for the real model                 */
+    const dtts_dit_block_weights *blocks;
+    const float *t_w1, *t_b1;         /* time MLP [1024][256], [1024]          */
+    const float *t_w2, *t_b2;         /* [1024][1024], [1024]                  */
+    const float *spk_w1, *spk_b1;     /* xvec_proj.0 [1024][512], [1024]       */
+    const float *spk_ln_w, *spk_ln_b; /* xvec_proj.1 LayerNorm [1024]          */
+    const float *oada_w, *oada_b;     /* output adaLN [2048][1024], [2048]     */
+    const float *out_w, *out_b;       /* output linear [128][1024], [128]      */
+    const float *in_w, *in_b;         /* input_layer [1024][1024], [1024]      */
+    const float *hid_w, *hid_b;       /* hidden_proj [1024][1536], [1024]      */
+    const float *lat_w, *lat_b;       /* latent_proj [1024][128], [1024]       */
+    const float *coord_w, *coord_b;   /* coordinate_proj [1024][128], [1024]   */
+} dtts_dit_weights;
+
+typedef struct dtts_attn_weights {
+    const float *wq, *wk, *wv, *wo;   /* [1024][1024] */
+    const float *bo;                  /* [1024] or NULL */
+    const float *qn, *kn;             /* [64] or NULL */
+} dtts_attn_weights;
+
+typedef struct dtts_pe_layer_weights {
+    const float *attn_norm_w;         /* [1024] or NULL */
+    const float *wq, *wk, *wv, *wo;   /* [1024][1024]   */
+    const float *bo;                  /* [1024] or NULL */
+    const float *ffn_norm_w;          /* [1024] or NULL */
+    const float *w1, *b1;             /* [4096][1024], [4096] */
+    const float *w2, *b2;             /* [1024][4096], [1024] */
+} dtts_pe_layer_weights;
+
+typedef struct dtts_pe_weights {
+    int n_layers;                     /* 24 for the real model */
+    const dtts_pe_layer_weights *layers;
+    const float *conv_w, *conv_b;     /* ds_proj [128][128][2], [128] */
+    const float *in_w, *in_b;         /* in_proj [1024][128], [1024]  */
+    const float *out_w, *out_b;       /* out_proj [1536][2048], [1536] */
+} dtts_pe_weights;
+
+typedef struct dtts_dit dtts_dit;
+typedef struct dtts_attn dtts_attn;
+typedef struct dtts_pe dtts_pe;
+
+/* ------------------------------------------------------------------ general */
+const char *dtts_version(void);
+const char *dtts_status_string(int status);
+const char *dtts_last_error(void);
+int dtts_device_count(int *n);       /* number of sm_100 devices visible */
+
+/* ------------------------------------------------------------------ DiT */
+int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit **out);
+/* Loads the velocity head from a safetensors checkpoint using the reference's
+ * tensor names (src/utils/dit_loader.cpp:47-115); F32, F16 and BF16 tensors. */
+int dtts_dit_create_from_safetensors(const char *path, int n_layers, int dtype, int device, dtts_dit **out);
+int dtts_dit_destroy(dtts_dit *e);
+int dtts_dit_set_stream(dtts_dit *e, void *cuda_stream);  /* NULL: the engine's own stream */
+int dtts_dit_sync(dtts_dit *e);
+
+/* One velocity forward for `rows` independent sequences of L tokens:
+ *   x_in  [rows][L][1024]  DiT input sequence (before input_layer)
+ *   cond  [rows][1024]     raw conditioning c (SiLU is applied inside)
+ *   mask  [L][L] uint8 (1 = attend) or NULL (bidirectional)
+ *   pos   [L] position ids or NULL (0..L-1)
+ *   out   [rows][n_out][128] output-layer rows L-n_out .. L-1 (n_out = L: all)
+ * == manual_dit_block over all layers + output layer, with the FFN applied to
+ * every token. */
+int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const uint8_t *mask, const float *pos,
+                      int rows, int L, int n_out, float *out, int mem);
+
+typedef struct dtts_solve_args {
+    int n_utt;                 /* utterances; 2*n_utt CFG rows run per step        */
+    int fm_len;                /* history tokens; L = fm_len + patch                */
+    int patch;                 /* noise frames (4 in the model)                     */
+    const float *fm_cond;      /* [n_utt][fm_len][1024]  fm_buffer                  */
+    const float *fm_uncond;    /* [n_utt][fm_len][1024]  fm_cfg_buffer              */
+    const float *z0;           /* [n_utt][patch][128]    initial noise              */
+    const float *spk;          /* [n_utt][512] x-vectors or NULL                    */
+    float spk_scale;           /* speaker_scale (1.5 in v4)                         */
+    int nfe;                   /* Euler steps, t_k = k / nfe                        */
+    float cfg_scale;
+    int cfg_form;              /* DTTS_CFG_V4 / DTTS_CFG_V3                         */
+    int layout;                /* DTTS_LAYOUT_FM_MASK / DTTS_LAYOUT_FULL            */
+    float *z_out;              /* [n_utt][patch][128]                               */
+    int mem;                   /* DTTS_MEM_HOST / DTTS_MEM_DEVICE                   */
+    int use_graph;             /* capture the whole solve in one CUDA graph         */
+} dtts_solve_args;
+int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a);
+
+/* Kernel-level timing of one launch type at the shapes of the last solve or
+ * velocity call, on the engine stream with CUDA events (after 3 warm-up
+ * launches).  kind: 0 QKV GEMM, 1 O GEMM, 2 FFN1 GEMM, 3 FFN2 GEMM,
+ * 4 attention, 5 LayerNorm+modulate, 6 adaLN GEMM, 7 input_layer GEMM.
+ * Reports the mean device time of one launch and its algorithmic FLOPs and
+ * bytes (operands read once, results written once). */
+int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us_per_launch, double *flops, double *bytes);
+/* Kernel launches enqueued by the last solve / velocity call (all engine kernels). */
+int dtts_dit_last_launch_count(dtts_dit *e, int *n);
+
+/* ------------------------------------------------------------------ attention sublayer */
+int dtts_attn_create(const dtts_attn_weights *w, int dtype, int device, dtts_attn **out);
+int dtts_attn_destroy(dtts_attn *a);
+/* out = manual_attention(x): x, out [rows][L][1024]; mask [L][L] or NULL; pos [L] or NULL */
+int dtts_attn_forward(dtts_attn *a, const float *x, int rows, int L, const uint8_t *mask, const float *pos,
+                      float *out);
+/* mean device time (us) of the attention core kernel (post-QKV, pre-O) of the last forward */
+int dtts_attn_profile_core(dtts_attn *a, int iters, float *us_per_launch);
+
+/* ------------------------------------------------------------------ PatchEncoder */
+/* max_batch sequences, each with a KV cache of max_tokens tokens (2 per patch). */
+int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batch, int max_tokens, dtts_pe **out);
+int dtts_pe_create_from_safetensors(const char *path, int n_layers, int dtype, int device, int max_batch,
+                                    int max_tokens, dtts_pe **out);
+int dtts_pe_destroy(dtts_pe *p);
+int dtts_pe_set_stream(dtts_pe *p, void *cuda_stream);
+int dtts_pe_sync(dtts_pe *p);
+/* Stateless full forward (patchenc_forward): frames [B][n_frames][128],
+ * n_frames a multiple of 4; out [B][n_frames/4][1536]. Resets the streams. */
+int dtts_pe_forward(dtts_pe *p, const float *frames, int B, int n_frames, int pair_mode, float *out, int mem);
+/* Starts B empty streams (no history, zero conv tail). */
+int dtts_pe_stream_reset(dtts_pe *p, int B);
+/* Appends n_frames (multiple of 4) to each of the B streams: one patch = one
+ * decode step; a prefill is the same call with many patches.  out
+ * [B][n_frames/4][1536].  Causal, so equal to the stateless forward over the
+ * whole prefix (adjacent pairing). */
+int dtts_pe_decode(dtts_pe *p, const float *frames, int B, int n_frames, float *out, int mem);
+int dtts_pe_stream_length(dtts_pe *p, int *tokens);
+
+/* ------------------------------------------------------------------ self-test
+ * One engine kernel in isolation on host data (no reference counterpart):
+ * inputs are rounded to bf16 on the host exactly as the engine stores them. */
+/* C[M][N] = A[M][K] B[N][K]^T (+ bias) with the tcgen05 GEMM; bn = 128 or 256 */
+int dtts_selftest_gemm(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, int bn,
+                       int device);
+/* attention core: q [rows][Tq][1024], k/v [rows][kv_len][1024], out like q */
+int dtts_selftest_attention(const float *q, const float *k, const float *v, float *out, int rows, int Tq,
+                            int kv_len, const uint8_t *mask, int causal, int q_pos0, int use_f32, int device);
+
+/* ------------------------------------------------------------------ safetensors (host only) */
+typedef struct dtts_st dtts_st;
+int dtts_st_open(const char *path, dtts_st **out);
+int dtts_st_close(dtts_st *f);
+int dtts_st_count(dtts_st *f, int *n);
+/* shape of tensor `name` (ndim <= 8); returns DTTS_ERR_IO if absent */
+int dtts_st_shape(dtts_st *f, const char *name, int *ndim, int64_t *shape);
+/* reads tensor `name` converted to fp32 into dst (n elements exactly) */
+int dtts_st_read_f32(dtts_st *f, const char *name, float *dst, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DTTS_H */

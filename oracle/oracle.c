@@ -1,0 +1,491 @@
+/* CPU oracle: fp32 restatement of the reference's DiT / PatchEncoder math.
+ * TEST INFRASTRUCTURE ONLY (see oracle.h).  Paths in citations are relative
+ * to the MaurerAnton/dots.tts.cpp source tree. */
+#include "oracle.h"
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+/* --------------------------------------------------------------------------
+ * primitives
+ * ------------------------------------------------------------------------ */
+
+/* LayerNorm without affine, eps 1e-5 (include/dit_manual.h:16-21). */
+static void ln_noaffine(float *out, const float *x, int n) {
+    float mean = 0.0f;
+    for (int i = 0; i < n; i++) mean += x[i];
+    mean /= (float)n;
+    float var = 0.0f;
+    for (int i = 0; i < n; i++) { float d = x[i] - mean; var += d * d; }
+    float inv = 1.0f / sqrtf(var / (float)n + 1e-5f);
+    for (int i = 0; i < n; i++) out[i] = (x[i] - mean) * inv;
+}
+
+/* y = W x + b for one row, accumulated in input order (include/dit_manual.h:30-61). */
+static void linear1(float *y, const float *x, const float *w, const float *b, int in, int out) {
+    for (int o = 0; o < out; o++) {
+        const float *wr = w + (size_t)o * in;
+        float s = 0.0f;
+        for (int i = 0; i < in; i++) s += wr[i] * x[i];
+        y[o] = b ? b[o] + s : s;
+    }
+}
+
+void orc_linear_rows(float *y, const float *x, int rows, const float *w, const float *b, int in, int out) {
+    #pragma omp parallel for schedule(static)
+    for (int o = 0; o < out; o++) {
+        const float *wr = w + (size_t)o * in;
+        for (int r = 0; r < rows; r++) {
+            const float *xr = x + (size_t)r * in;
+            float s = 0.0f;
+            for (int i = 0; i < in; i++) s += wr[i] * xr[i];
+            y[(size_t)r * out + o] = b ? b[o] + s : s;
+        }
+    }
+}
+
+static float silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* GELU, tanh approximation (include/dit_manual.h:186-192). */
+static float gelu_tanh(float x) {
+    const float c1 = 0.7978845608028654f, c2 = 0.044715f;
+    float x3 = x * x * x;
+    return 0.5f * x * (1.0f + tanhf(c1 * (x + c2 * x3)));
+}
+
+/* --------------------------------------------------------------------------
+ * conditioning
+ * ------------------------------------------------------------------------ */
+
+/* Sinusoid [cos(t f_i) | sin(t f_i)], f_i = exp(-ln(1e4) i / 128)
+ * (src/e2e_pipeline_v4.cpp:58-60, src/modules/backbone/dit_forward.cpp:23-25). */
+void orc_sinusoid(float t, float *se) {
+    const int half = 128;
+    for (int i = 0; i < half; i++) {
+        float f = expf(-logf(10000.0f) * (float)i / (float)half);
+        se[i] = cosf(t * f);
+        se[half + i] = sinf(t * f);
+    }
+}
+
+/* compute_cond with speaker_scale (src/e2e_pipeline_v4.cpp:57-71). */
+void orc_compute_cond(const orc_dit *m, float t, const float *spk, float spk_scale, float *cond) {
+    float se[256], h1[ORC_D];
+    orc_sinusoid(t, se);
+    linear1(h1, se, m->t_w1, m->t_b1, 256, ORC_D);
+    for (int o = 0; o < ORC_D; o++) h1[o] = h1[o] / (1.0f + expf(-h1[o]));
+    linear1(cond, h1, m->t_w2, m->t_b2, ORC_D, ORC_D);
+    if (spk) {
+        float tt[ORC_D];
+        linear1(tt, spk, m->spk_w1, m->spk_b1, ORC_SPK, ORC_D);
+        float mean = 0.0f;
+        for (int i = 0; i < ORC_D; i++) mean += tt[i];
+        mean /= ORC_D;
+        float var = 0.0f;
+        for (int i = 0; i < ORC_D; i++) { float d = tt[i] - mean; var += d * d; }
+        var = var / ORC_D + 1e-5f;
+        float istd = 1.0f / sqrtf(var);
+        for (int i = 0; i < ORC_D; i++) {
+            float x = (tt[i] - mean) * istd;
+            if (m->spk_ln_w) x *= m->spk_ln_w[i];
+            if (m->spk_ln_b) x += m->spk_ln_b[i];
+            cond[i] += x * spk_scale;
+        }
+    }
+}
+
+/* --------------------------------------------------------------------------
+ * attention (include/dit_manual.h:88-146)
+ * Q,K,V without bias; per-head RMS qk-norm eps 1e-6 with a [64] gain; RoPE
+ * half-split on pos (or 0..L-1), theta advanced multiplicatively; scores
+ * scaled by 1/sqrt(64); masked entries -inf; softmax; P.V; O projection.
+ * ------------------------------------------------------------------------ */
+static void rms_head(float *v, const float *g) {
+    float ss = 0.0f;
+    for (int d = 0; d < ORC_HD; d++) ss += v[d] * v[d];
+    float inv = 1.0f / sqrtf(ss / ORC_HD + 1e-6f);
+    for (int d = 0; d < ORC_HD; d++) { float y = v[d] * inv; if (g) y *= g[d]; v[d] = y; }
+}
+
+static void rope_half(float *q, float *k, float pos) {
+    const int half = ORC_HD / 2;
+    float theta = 1.0f;
+    float ts = powf(10000.0f, -2.0f / (float)ORC_HD);
+    for (int d = 0; d < half; d++) {
+        float cs = cosf(pos * theta), sn = sinf(pos * theta);
+        float q0 = q[d], q1 = q[d + half], k0 = k[d], k1 = k[d + half];
+        q[d] = q0 * cs - q1 * sn; q[d + half] = q1 * cs + q0 * sn;
+        k[d] = k0 * cs - k1 * sn; k[d + half] = k1 * cs + k0 * sn;
+        theta *= ts;
+    }
+}
+
+void orc_attention(float *out, const float *x, int L,
+                   const float *wq, const float *wk, const float *wv, const float *wo,
+                   const float *bo, const float *qn, const float *kn,
+                   const uint8_t *mask, const float *pos) {
+    size_t n = (size_t)L * ORC_D;
+    float *q = (float *)malloc(n * sizeof(float));
+    float *k = (float *)malloc(n * sizeof(float));
+    float *v = (float *)malloc(n * sizeof(float));
+    float *ctx = (float *)malloc(n * sizeof(float));
+    orc_linear_rows(q, x, L, wq, NULL, ORC_D, ORC_D);
+    orc_linear_rows(k, x, L, wk, NULL, ORC_D, ORC_D);
+    orc_linear_rows(v, x, L, wv, NULL, ORC_D, ORC_D);
+    /* per (token, head): norm + rope (the reference copies heads out, normalises
+     * then rotates; per-token order is identical) */
+    #pragma omp parallel for schedule(static)
+    for (int t = 0; t < L; t++) {
+        for (int h = 0; h < ORC_H; h++) {
+            float *qh = q + (size_t)t * ORC_D + h * ORC_HD;
+            float *kh = k + (size_t)t * ORC_D + h * ORC_HD;
+            rms_head(qh, qn);
+            rms_head(kh, kn);
+            rope_half(qh, kh, pos ? pos[t] : (float)t);
+        }
+    }
+    const float scale = 1.0f / sqrtf((float)ORC_HD);
+    #pragma omp parallel
+    {
+        float *s = (float *)malloc((size_t)L * sizeof(float));
+        #pragma omp for collapse(2) schedule(static)
+        for (int h = 0; h < ORC_H; h++) {
+            for (int i = 0; i < L; i++) {
+                const float *qi = q + (size_t)i * ORC_D + h * ORC_HD;
+                for (int j = 0; j < L; j++) {
+                    const float *kj = k + (size_t)j * ORC_D + h * ORC_HD;
+                    float acc = 0.0f;
+                    for (int d = 0; d < ORC_HD; d++) acc += qi[d] * kj[d];
+                    s[j] = acc * scale;
+                    if (mask && !mask[(size_t)i * L + j]) s[j] = -INFINITY;
+                }
+                /* manual_softmax (include/dit_manual.h:83-86) */
+                float mx = s[0];
+                for (int j = 1; j < L; j++) if (s[j] > mx) mx = s[j];
+                float sum = 0.0f;
+                for (int j = 0; j < L; j++) { s[j] = expf(s[j] - mx); sum += s[j]; }
+                for (int j = 0; j < L; j++) s[j] /= sum;
+                float *ci = ctx + (size_t)i * ORC_D + h * ORC_HD;
+                for (int d = 0; d < ORC_HD; d++) {
+                    float acc = 0.0f;
+                    for (int j = 0; j < L; j++) acc += s[j] * v[(size_t)j * ORC_D + h * ORC_HD + d];
+                    ci[d] = acc;
+                }
+            }
+        }
+        free(s);
+    }
+    orc_linear_rows(out, ctx, L, wo, bo, ORC_D, ORC_D);
+    free(q); free(k); free(v); free(ctx);
+}
+
+/* --------------------------------------------------------------------------
+ * DiT block (include/dit_manual.h:148-199)
+ * ada = W_ada SiLU(c) + b -> shift_msa, scale_msa, gate_msa, shift_mlp,
+ * scale_mlp, gate_mlp; h = x + g_msa * Attn(LN(x)(1+s)+sh);
+ * out = h + g_mlp * FFN(LN(h)(1+s')+sh'), FFN = W2 GELU_tanh(W1 u + b1) + b2.
+ * ffn_mode ORC_FFN_AS_WRITTEN reproduces the shipped code, whose FFN projects
+ * token 0 only and leaves rows 1.. of the GELU input at whatever the
+ * thread_local scratch held (zero on the first call of a fresh thread); this
+ * restatement uses zeros for those rows.
+ * ------------------------------------------------------------------------ */
+static void dit_adaln(float *ada, const float *cond, const float *w, const float *b, int nout) {
+    float cs[ORC_D];
+    for (int i = 0; i < ORC_D; i++) cs[i] = cond[i] / (1.0f + expf(-cond[i]));
+    #pragma omp parallel for schedule(static)
+    for (int o = 0; o < nout; o++) {
+        float s = b ? b[o] : 0.0f;
+        const float *wr = w + (size_t)o * ORC_D;
+        for (int i = 0; i < ORC_D; i++) s += wr[i] * cs[i];
+        ada[o] = s;
+    }
+}
+
+void orc_dit_block_fwd(float *out, const float *x, const float *cond, const orc_dit_block *b,
+                       int L, const uint8_t *mask, const float *pos, int ffn_mode) {
+    const int D = ORC_D;
+    float *ada = (float *)malloc(6 * D * sizeof(float));
+    dit_adaln(ada, cond, b->ada_w, b->ada_b, 6 * D);
+    const float *sm = ada, *scm = ada + D, *gm = ada + 2 * D;
+    const float *sml = ada + 3 * D, *scl = ada + 4 * D, *gml = ada + 5 * D;
+    size_t n = (size_t)L * D;
+    float *mod = (float *)malloc(n * sizeof(float));
+    float *ao = (float *)malloc(n * sizeof(float));
+    float *h = (float *)malloc(n * sizeof(float));
+    for (int t = 0; t < L; t++) {
+        float *mr = mod + (size_t)t * D;
+        ln_noaffine(mr, x + (size_t)t * D, D);
+        for (int i = 0; i < D; i++) mr[i] = mr[i] * (1.0f + scm[i]) + sm[i];
+    }
+    orc_attention(ao, mod, L, b->wq, b->wk, b->wv, b->wo, b->bo, b->qn, b->kn, mask, pos);
+    for (size_t i = 0; i < n; i++) h[i] = x[i] + gm[i % D] * ao[i];
+    for (int t = 0; t < L; t++) {
+        float *mr = mod + (size_t)t * D;
+        ln_noaffine(mr, h + (size_t)t * D, D);
+        for (int i = 0; i < D; i++) mr[i] = mr[i] * (1.0f + scl[i]) + sml[i];
+    }
+    float *f1 = (float *)calloc((size_t)L * ORC_F, sizeof(float));
+    float *f2 = (float *)calloc(n, sizeof(float));
+    int rows = (ffn_mode == ORC_FFN_AS_WRITTEN) ? 1 : L;
+    orc_linear_rows(f1, mod, rows, b->w1, b->b1, D, ORC_F);
+    for (size_t i = 0; i < (size_t)L * ORC_F; i++) f1[i] = gelu_tanh(f1[i]);
+    orc_linear_rows(f2, f1, rows, b->w2, b->b2, ORC_F, D);
+    for (size_t i = 0; i < n; i++) out[i] = h[i] + gml[i % D] * f2[i];
+    free(ada); free(mod); free(ao); free(h); free(f1); free(f2);
+}
+
+/* --------------------------------------------------------------------------
+ * Velocity forward: input_layer -> blocks -> output adaLN + LN + out_proj
+ * (src/e2e_pipeline_v4.cpp:441-478).  Writes the last n_out tokens of
+ * out_all [L][128] (n_out = L gives every row).
+ * ------------------------------------------------------------------------ */
+void orc_dit_velocity(const orc_dit *m, const float *x_in, int L, const float *cond,
+                      const uint8_t *mask, const float *pos, int ffn_mode,
+                      int n_out, float *out) {
+    const int D = ORC_D;
+    size_t n = (size_t)L * D;
+    float *h = (float *)malloc(n * sizeof(float));
+    float *bo = (float *)malloc(n * sizeof(float));
+    orc_linear_rows(h, x_in, L, m->in_w, m->in_b, D, D);
+    for (int i = 0; i < m->n_layers; i++) {
+        orc_dit_block_fwd(bo, h, cond, &m->blocks[i], L, mask, pos, ffn_mode);
+        float *tmp = h; h = bo; bo = tmp;
+    }
+    float mod_raw[2 * ORC_D];
+    dit_adaln(mod_raw, cond, m->oada_w, m->oada_b, 2 * D);
+    const float *shift = mod_raw, *scale = mod_raw + D;
+    int t0 = L - n_out;
+    for (int t = t0; t < L; t++) {
+        float ln[ORC_D];
+        ln_noaffine(ln, h + (size_t)t * D, D);
+        for (int j = 0; j < D; j++) ln[j] = ln[j] * (1.0f + scale[j]) + shift[j];
+        linear1(out + (size_t)(t - t0) * ORC_LAT, ln, m->out_w, m->out_b, D, ORC_LAT);
+    }
+    free(h); free(bo);
+}
+
+/* --------------------------------------------------------------------------
+ * FM mask / position ids (src/e2e_pipeline_v4.cpp:120-155).
+ * ------------------------------------------------------------------------ */
+void orc_build_fm_mask(uint8_t *mask, int total_len, int fm_len, int patch, int hidden_patch) {
+    int latent_start = total_len - patch;
+    int block_start = fm_len > hidden_patch ? fm_len - hidden_patch : 0;
+    memset(mask, 0, (size_t)total_len * total_len);
+    for (int i = 0; i < block_start; i++)
+        for (int j = 0; j <= i; j++) mask[(size_t)i * total_len + j] = 1;
+    for (int i = block_start; i < fm_len; i++) {
+        for (int j = 0; j < fm_len; j++) mask[(size_t)i * total_len + j] = 1;
+        for (int j = latent_start; j < total_len; j++) mask[(size_t)i * total_len + j] = 1;
+    }
+    for (int i = latent_start; i < total_len; i++) {
+        for (int j = 0; j < fm_len; j++) mask[(size_t)i * total_len + j] = 1;
+        for (int j = latent_start; j < total_len; j++) mask[(size_t)i * total_len + j] = 1;
+    }
+    for (int i = fm_len; i < latent_start; i++) mask[(size_t)i * total_len + i] = 1;
+}
+
+void orc_build_fm_pos(float *pos, int total_len, int fm_len, int patch) {
+    int latent_start = total_len - patch;
+    for (int i = 0; i < fm_len; i++) pos[i] = (float)i;
+    for (int i = latent_start; i < total_len; i++) pos[i] = (float)(fm_len + i - latent_start);
+    for (int i = fm_len; i < latent_start; i++) pos[i] = 0.0f;
+}
+
+/* --------------------------------------------------------------------------
+ * Euler + CFG solve for one latent patch per utterance
+ * (src/e2e_pipeline_v4.cpp:395-526).  layout 0: v4 mask + pos ids;
+ * layout 1: no mask, positions 0..L-1.  cfg_form 0: v = vc + s (vc - vu)
+ * (v4, :509-512); cfg_form 1: v = vu + s (vc - vu) (src/e2e_pipeline.cpp:444).
+ * ------------------------------------------------------------------------ */
+void orc_euler_solve(const orc_dit *m, int n_utt, int fm_len, int patch,
+                     const float *fm_cond, const float *fm_uncond,
+                     const float *z0, const float *spk, float spk_scale,
+                     int nfe, float cfg_scale, int cfg_form, int layout, int ffn_mode,
+                     float *z_out) {
+    const int D = ORC_D;
+    int total = fm_len + patch;
+    int pf = patch * ORC_LAT;
+    uint8_t *mask = NULL;
+    float *pos = NULL;
+    if (layout == 0) {
+        mask = (uint8_t *)malloc((size_t)total * total);
+        pos = (float *)malloc((size_t)total * sizeof(float));
+        orc_build_fm_mask(mask, total, fm_len, patch, 1);
+        orc_build_fm_pos(pos, total, fm_len, patch);
+    }
+    float *xc = (float *)malloc((size_t)total * D * sizeof(float));
+    float *xu = (float *)malloc((size_t)total * D * sizeof(float));
+    float *vc = (float *)malloc((size_t)pf * sizeof(float));
+    float *vu = (float *)malloc((size_t)pf * sizeof(float));
+    const float dt = 1.0f / (float)nfe;
+    for (int u = 0; u < n_utt; u++) {
+        float *z = z_out + (size_t)u * pf;
+        memcpy(z, z0 + (size_t)u * pf, (size_t)pf * sizeof(float));
+        memcpy(xc, fm_cond + (size_t)u * fm_len * D, (size_t)fm_len * D * sizeof(float));
+        memcpy(xu, fm_uncond + (size_t)u * fm_len * D, (size_t)fm_len * D * sizeof(float));
+        for (int step = 0; step < nfe; step++) {
+            float t = (float)step * dt;
+            for (int p = 0; p < patch; p++) {
+                float *dst = xc + (size_t)(total - patch + p) * D;
+                linear1(dst, z + p * ORC_LAT, m->coord_w, m->coord_b, ORC_LAT, D);
+                memcpy(xu + (size_t)(total - patch + p) * D, dst, D * sizeof(float));
+            }
+            float cond[ORC_D];
+            orc_compute_cond(m, t, spk ? spk + (size_t)u * ORC_SPK : NULL, spk_scale, cond);
+            orc_dit_velocity(m, xc, total, cond, mask, pos, ffn_mode, patch, vc);
+            orc_dit_velocity(m, xu, total, cond, mask, pos, ffn_mode, patch, vu);
+            for (int i = 0; i < pf; i++) {
+                float v = (cfg_form == 0) ? vc[i] + cfg_scale * (vc[i] - vu[i])
+                                          : vu[i] + cfg_scale * (vc[i] - vu[i]);
+                z[i] += v * dt;
+            }
+        }
+    }
+    free(mask); free(pos); free(xc); free(xu); free(vc); free(vu);
+}
+
+/* --------------------------------------------------------------------------
+ * PatchEncoder (src/modules/backbone/patchenc.cpp:146-239)
+ * ------------------------------------------------------------------------ */
+
+/* ggml_rms_norm (sum of squares in double, scale = 1/sqrtf(mean + eps)) then
+ * optional elementwise weight (patchenc.cpp:172-173,210-211). */
+static void rms_norm_w(float *out, const float *x, const float *w, int n, float eps) {
+    double ss = 0.0;
+    for (int i = 0; i < n; i++) ss += (double)x[i] * (double)x[i];
+    float mean = (float)(ss / n);
+    float scale = 1.0f / sqrtf(mean + eps);
+    for (int i = 0; i < n; i++) { float y = x[i] * scale; if (w) y *= w[i]; out[i] = y; }
+}
+
+/* ggml_rope mode 0 (adjacent pairs) with freq_base 1e4, freq_scale 1:
+ * theta starts at p and is multiplied by 1e4^(-2/64) per pair. */
+static void rope_adjacent(float *v, int p) {
+    float theta_scale = powf(10000.0f, -2.0f / (float)ORC_HD);
+    float theta = (float)p;
+    for (int i = 0; i < ORC_HD; i += 2) {
+        float c = cosf(theta), s = sinf(theta);
+        float x0 = v[i], x1 = v[i + 1];
+        v[i] = x0 * c - x1 * s;
+        v[i + 1] = x0 * s + x1 * c;
+        theta *= theta_scale;
+    }
+}
+
+void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pair_mode,
+                    float *out, float *h_last) {
+    const int D = ORC_D, C = ORC_LAT;
+    int seq = n_patches * 4;
+    int T = seq / 2;
+    /* causal Conv1d(128->128, k=2, s=2), taps at frames 2o-1 and 2o (patchenc.cpp:19-39) */
+    float *xc = (float *)malloc((size_t)T * C * sizeof(float));
+    for (int o = 0; o < T; o++)
+        for (int oc = 0; oc < C; oc++) {
+            float s = m->conv_b ? m->conv_b[oc] : 0.0f;
+            for (int ic = 0; ic < C; ic++) {
+                int wb = (oc * C + ic) * 2;
+                int i0 = 2 * o - 1;
+                if (i0 >= 0 && i0 < seq) s += frames[(size_t)i0 * C + ic] * m->conv_w[wb + 0];
+                int i1 = 2 * o;
+                if (i1 >= 0 && i1 < seq) s += frames[(size_t)i1 * C + ic] * m->conv_w[wb + 1];
+            }
+            xc[(size_t)o * C + oc] = s;
+        }
+    size_t n = (size_t)T * D;
+    float *h = (float *)malloc(n * sizeof(float));
+    orc_linear_rows(h, xc, T, m->in_w, m->in_b, C, D);
+    float *xn = (float *)malloc(n * sizeof(float));
+    float *q = (float *)malloc(n * sizeof(float));
+    float *k = (float *)malloc(n * sizeof(float));
+    float *v = (float *)malloc(n * sizeof(float));
+    float *ctx = (float *)malloc(n * sizeof(float));
+    float *ao = (float *)malloc(n * sizeof(float));
+    float *f1 = (float *)malloc((size_t)T * ORC_F * sizeof(float));
+    float *f2 = (float *)malloc(n * sizeof(float));
+    const float scale = 1.0f / sqrtf((float)ORC_HD);
+    for (int li = 0; li < m->n_layers; li++) {
+        const orc_pe_layer *l = &m->layers[li];
+        for (int t = 0; t < T; t++) rms_norm_w(xn + (size_t)t * D, h + (size_t)t * D, l->attn_norm_w, D, 1e-6f);
+        orc_linear_rows(q, xn, T, l->wq, NULL, D, D);
+        orc_linear_rows(k, xn, T, l->wk, NULL, D, D);
+        orc_linear_rows(v, xn, T, l->wv, NULL, D, D);
+        /* no qk-norm (patchenc.cpp:283-284); rope on q and k, positions 0..T-1 */
+        for (int t = 0; t < T; t++)
+            for (int hh = 0; hh < ORC_H; hh++) {
+                rope_adjacent(q + (size_t)t * D + hh * ORC_HD, t);
+                rope_adjacent(k + (size_t)t * D + hh * ORC_HD, t);
+            }
+        /* causal per-head attention (patchenc.cpp:59-101) */
+        #pragma omp parallel
+        {
+            float *s = (float *)malloc((size_t)T * sizeof(float));
+            #pragma omp for collapse(2) schedule(static)
+            for (int hh = 0; hh < ORC_H; hh++)
+                for (int ti = 0; ti < T; ti++) {
+                    for (int tj = 0; tj < T; tj++) {
+                        float acc = 0.0f;
+                        for (int d = 0; d < ORC_HD; d++)
+                            acc += q[(size_t)ti * D + hh * ORC_HD + d] * k[(size_t)tj * D + hh * ORC_HD + d];
+                        s[tj] = acc * scale;
+                    }
+                    for (int tj = ti + 1; tj < T; tj++) s[tj] = -INFINITY;
+                    float mx = s[0];
+                    for (int tj = 1; tj < T; tj++) if (s[tj] > mx) mx = s[tj];
+                    float sum = 0.0f;
+                    for (int tj = 0; tj < T; tj++) { s[tj] = expf(s[tj] - mx); sum += s[tj]; }
+                    for (int tj = 0; tj < T; tj++) s[tj] /= sum;
+                    for (int d = 0; d < ORC_HD; d++) {
+                        float acc = 0.0f;
+                        for (int tj = 0; tj < T; tj++) acc += s[tj] * v[(size_t)tj * D + hh * ORC_HD + d];
+                        ctx[(size_t)ti * D + hh * ORC_HD + d] = acc;
+                    }
+                }
+            free(s);
+        }
+        orc_linear_rows(ao, ctx, T, l->wo, l->bo, D, D);
+        for (size_t i = 0; i < n; i++) h[i] += ao[i];
+        for (int t = 0; t < T; t++) rms_norm_w(xn + (size_t)t * D, h + (size_t)t * D, l->ffn_norm_w, D, 1e-6f);
+        orc_linear_rows(f1, xn, T, l->w1, l->b1, D, ORC_F);
+        for (size_t i = 0; i < (size_t)T * ORC_F; i++) f1[i] = silu(f1[i]);
+        orc_linear_rows(f2, f1, T, l->w2, l->b2, ORC_F, D);
+        for (size_t i = 0; i < n; i++) h[i] += f2[i];
+    }
+    if (h_last) memcpy(h_last, h, n * sizeof(float));
+    /* output pairs -> out_proj(2048 -> 1536) (patchenc.cpp:225-238) */
+    float *cat = (float *)malloc((size_t)n_patches * 2 * D * sizeof(float));
+    for (int qi = 0; qi < n_patches; qi++)
+        for (int s = 0; s < 2; s++) {
+            int tok;
+            if (pair_mode == ORC_PAIR_ADJACENT) {
+                tok = 2 * qi + s;
+            } else {
+                /* reshape [D,2,n] -> permute(0,2,1,3) -> [D,n,2] -> [2D,n]:
+                 * flat index f = i + D*p + D*n*j, output row qi covers
+                 * f in [2D qi, 2D qi + 2D), i.e. g = 2 qi + s -> p = g % n, j = g / n */
+                int g = 2 * qi + s;
+                tok = 2 * (g % n_patches) + g / n_patches;
+            }
+            memcpy(cat + (size_t)qi * 2 * D + s * D, h + (size_t)tok * D, D * sizeof(float));
+        }
+    orc_linear_rows(out, cat, n_patches, m->out_w, m->out_b, 2 * D, ORC_LLM);
+    free(cat); free(xc); free(h); free(xn); free(q); free(k); free(v); free(ctx); free(ao); free(f1); free(f2);
+}

@@ -1,0 +1,120 @@
+/* CPU oracle for the DiT flow-matching head and the PatchEncoder.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference legs of bench.py load this library, and only as
+ * the checker or the CPU baseline; the CUDA engine never calls it.
+ *
+ * It restates, in plain fp32 C, the reference's CPU arithmetic for this path
+ * (MaurerAnton/dots.tts.cpp; file:line citations are on each function in
+ * oracle.c).  The DiT half is pinned against the reference's own
+ * include/dit_manual.h compiled into oracle/_ref (see oracle/Makefile); the
+ * PatchEncoder half restates src/modules/backbone/patchenc.cpp, whose ggml
+ * operators (rms_norm, rope mode 0, silu) are not vendored in the reference,
+ * so their exact numerics are restated from ggml's published definitions.
+ *
+ * Layouts: every matrix is row-major [out][in] (PyTorch Linear), activations
+ * are row-major [tokens][features], all fp32. */
+#pragma once
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORC_D      1024   /* DIT_HIDDEN_SIZE / PATCHENC_HIDDEN            */
+#define ORC_H      16     /* heads                                         */
+#define ORC_HD     64     /* head dim                                      */
+#define ORC_F      4096   /* FFN size                                      */
+#define ORC_LAT    128    /* VAE latent dim                                */
+#define ORC_LLM    1536   /* LLM hidden (hidden_proj input, PE output)     */
+#define ORC_SPK    512    /* speaker x-vector dim                          */
+
+/* One DiT block (include/dit.h:47-72 field meanings). */
+typedef struct {
+    const float *wq, *wk, *wv, *wo;  /* [1024][1024] */
+    const float *bo;                 /* [1024] or NULL */
+    const float *qn, *kn;            /* [64] per-head RMS gains, or NULL */
+    const float *w1, *b1;            /* [4096][1024], [4096] */
+    const float *w2, *b2;            /* [1024][4096], [1024] */
+    const float *ada_w, *ada_b;      /* [6144][1024], [6144] */
+} orc_dit_block;
+
+/* Whole DiT (include/dit.h:74-126). */
+typedef struct {
+    int n_layers;
+    const orc_dit_block *blocks;
+    const float *t_w1, *t_b1;        /* [1024][256], [1024] */
+    const float *t_w2, *t_b2;        /* [1024][1024], [1024] */
+    const float *spk_w1, *spk_b1;    /* [1024][512], [1024] */
+    const float *spk_ln_w, *spk_ln_b;/* [1024] */
+    const float *oada_w, *oada_b;    /* [2048][1024], [2048] */
+    const float *out_w, *out_b;      /* [128][1024], [128] */
+    const float *in_w, *in_b;        /* [1024][1024], [1024] */
+    const float *hid_w, *hid_b;      /* [1024][1536], [1024] */
+    const float *lat_w, *lat_b;      /* [1024][128], [1024] */
+    const float *coord_w, *coord_b;  /* [1024][128], [1024] */
+} orc_dit;
+
+typedef struct {
+    const float *attn_norm_w;        /* [1024] or NULL */
+    const float *wq, *wk, *wv, *wo;  /* [1024][1024] */
+    const float *bo;                 /* [1024] or NULL */
+    const float *ffn_norm_w;         /* [1024] or NULL */
+    const float *w1, *b1;            /* [4096][1024], [4096] */
+    const float *w2, *b2;            /* [1024][4096], [1024] */
+} orc_pe_layer;
+
+typedef struct {
+    int n_layers;
+    const orc_pe_layer *layers;
+    const float *conv_w, *conv_b;    /* [128][128][2], [128] */
+    const float *in_w, *in_b;        /* [1024][128], [1024] */
+    const float *out_w, *out_b;      /* [1536][2048], [1536] */
+} orc_pe;
+
+/* rope pairing */
+#define ORC_ROPE_HALF      0   /* (d, d+32): dit_manual.h:111-128            */
+#define ORC_ROPE_ADJACENT  1   /* (2i, 2i+1): ggml_rope mode 0, patchenc.cpp:115-116 */
+
+/* FFN variants of the DiT block */
+#define ORC_FFN_PER_TOKEN  0   /* every token (what the model means)          */
+#define ORC_FFN_AS_WRITTEN 1   /* token 0 only, rows 1.. read a zeroed scratch, dit_manual.h:173-196 */
+
+/* PatchEncoder output pairing */
+#define ORC_PAIR_ADJACENT  0   /* output p = out_proj([h_2p | h_2p+1])        */
+#define ORC_PAIR_AS_WRITTEN 1  /* ggml permute as written, patchenc.cpp:230-232 */
+
+int  orc_num_threads(void);
+void orc_set_threads(int n);
+
+void orc_sinusoid(float t, float *se256);
+void orc_compute_cond(const orc_dit *m, float t, const float *spk, float spk_scale, float *cond);
+void orc_linear_rows(float *y, const float *x, int rows, const float *w, const float *b, int in, int out);
+
+void orc_attention(float *out, const float *x, int L,
+                   const float *wq, const float *wk, const float *wv, const float *wo,
+                   const float *bo, const float *qn, const float *kn,
+                   const uint8_t *mask, const float *pos);
+
+void orc_dit_block_fwd(float *out, const float *x, const float *cond, const orc_dit_block *b,
+                       int L, const uint8_t *mask, const float *pos, int ffn_mode);
+
+void orc_dit_velocity(const orc_dit *m, const float *x_in, int L, const float *cond,
+                      const uint8_t *mask, const float *pos, int ffn_mode,
+                      int n_out, float *out);
+
+void orc_build_fm_mask(uint8_t *mask, int total_len, int fm_len, int patch, int hidden_patch);
+void orc_build_fm_pos(float *pos, int total_len, int fm_len, int patch);
+
+void orc_euler_solve(const orc_dit *m, int n_utt, int fm_len, int patch,
+                     const float *fm_cond, const float *fm_uncond,
+                     const float *z0, const float *spk, float spk_scale,
+                     int nfe, float cfg_scale, int cfg_form, int layout, int ffn_mode,
+                     float *z_out);
+
+void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pair_mode,
+                    float *out, float *h_last);
+
+#ifdef __cplusplus
+}
+#endif

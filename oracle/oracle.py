@@ -1,0 +1,334 @@
+"""ctypes binding for the CPU oracle (oracle.c) and the reference build
+(_ref/libdtts_ref.so, the reference's include/dit_manual.h compiled in place).
+
+TEST INFRASTRUCTURE ONLY.  tests/, __graft_entry__.smoke() and bench.py's
+CPU-baseline / reference legs load this module, as the checker or as the CPU
+timing baseline; the CUDA engine never routes through it.
+
+Weights are passed as dicts of float32 numpy arrays named exactly as in the
+reference's safetensors checkpoint (src/utils/dit_loader.cpp:47-115,
+src/utils/patchenc_loader.cpp:175-208)."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libdtts_ref.so")
+
+FFN_PER_TOKEN = 0
+FFN_AS_WRITTEN = 1
+PAIR_ADJACENT = 0
+PAIR_AS_WRITTEN = 1
+
+_fp = C.POINTER(C.c_float)
+_u8p = C.POINTER(C.c_uint8)
+
+
+class DitBlock(C.Structure):
+    _fields_ = [(n, _fp) for n in ("wq", "wk", "wv", "wo", "bo", "qn", "kn", "w1", "b1",
+                                   "w2", "b2", "ada_w", "ada_b")]
+
+
+class Dit(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("blocks", C.POINTER(DitBlock))] + [
+        (n, _fp) for n in ("t_w1", "t_b1", "t_w2", "t_b2", "spk_w1", "spk_b1", "spk_ln_w",
+                           "spk_ln_b", "oada_w", "oada_b", "out_w", "out_b", "in_w", "in_b",
+                           "hid_w", "hid_b", "lat_w", "lat_b", "coord_w", "coord_b")]
+
+
+class PeLayer(C.Structure):
+    _fields_ = [(n, _fp) for n in ("attn_norm_w", "wq", "wk", "wv", "wo", "bo", "ffn_norm_w",
+                                   "w1", "b1", "w2", "b2")]
+
+
+class Pe(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("layers", C.POINTER(PeLayer))] + [
+        (n, _fp) for n in ("conv_w", "conv_b", "in_w", "in_b", "out_w", "out_b")]
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous, "float32 C-contiguous expected"
+    return a.ctypes.data_as(_fp)
+
+
+def _u8(a):
+    if a is None:
+        return None
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    return a.ctypes.data_as(_u8p), a
+
+
+DIT_BLOCK_NAMES = {
+    "wq": "attn.q_proj.weight", "wk": "attn.k_proj.weight", "wv": "attn.v_proj.weight",
+    "wo": "attn.o_proj.weight", "bo": "attn.o_proj.bias", "qn": "attn.q_norm.weight",
+    "kn": "attn.k_norm.weight", "w1": "ffn.fc1.weight", "b1": "ffn.fc1.bias",
+    "w2": "ffn.fc2.weight", "b2": "ffn.fc2.bias", "ada_w": "adaLN_modulation.1.weight",
+    "ada_b": "adaLN_modulation.1.bias",
+}
+DIT_GLOBAL_NAMES = {
+    "t_w1": "velocity_field_predictor.time_embedder.mlp.0.weight",
+    "t_b1": "velocity_field_predictor.time_embedder.mlp.0.bias",
+    "t_w2": "velocity_field_predictor.time_embedder.mlp.2.weight",
+    "t_b2": "velocity_field_predictor.time_embedder.mlp.2.bias",
+    "spk_w1": "xvec_proj.0.weight", "spk_b1": "xvec_proj.0.bias",
+    "spk_ln_w": "xvec_proj.1.weight", "spk_ln_b": "xvec_proj.1.bias",
+    "oada_w": "velocity_field_predictor.output_layer.adaLN_modulation.1.weight",
+    "oada_b": "velocity_field_predictor.output_layer.adaLN_modulation.1.bias",
+    "out_w": "velocity_field_predictor.output_layer.linear.weight",
+    "out_b": "velocity_field_predictor.output_layer.linear.bias",
+    "in_w": "velocity_field_predictor.input_layer.weight",
+    "in_b": "velocity_field_predictor.input_layer.bias",
+    "hid_w": "hidden_proj.weight", "hid_b": "hidden_proj.bias",
+    "lat_w": "latent_proj.weight", "lat_b": "latent_proj.bias",
+    "coord_w": "coordinate_proj.weight", "coord_b": "coordinate_proj.bias",
+}
+PE_LAYER_NAMES = {
+    "attn_norm_w": "attn_norm.weight", "wq": "attn.q_proj.weight", "wk": "attn.k_proj.weight",
+    "wv": "attn.v_proj.weight", "wo": "attn.o_proj.weight", "bo": "attn.o_proj.bias",
+    "ffn_norm_w": "ffn_norm.weight", "w1": "ffn.fc1.weight", "b1": "ffn.fc1.bias",
+    "w2": "ffn.fc2.weight", "b2": "ffn.fc2.bias",
+}
+PE_GLOBAL_NAMES = {
+    "conv_w": "patch_encoder.ds_proj.weight", "conv_b": "patch_encoder.ds_proj.bias",
+    "in_w": "patch_encoder.in_proj.weight", "in_b": "patch_encoder.in_proj.bias",
+    "out_w": "patch_encoder.out_proj.weight", "out_b": "patch_encoder.out_proj.bias",
+}
+
+
+def dit_block_prefix(i):
+    return f"velocity_field_predictor.blocks.{i}."
+
+
+def pe_layer_prefix(i):
+    return f"patch_encoder.encoder.layers.{i}."
+
+
+class _Keep:
+    """Holds the ctypes structs and the arrays they point into."""
+
+    def __init__(self):
+        self.refs = []
+
+
+def make_block_struct(w: dict, i: int, keep: _Keep) -> DitBlock:
+    b = DitBlock()
+    pre = dit_block_prefix(i)
+    for f, n in DIT_BLOCK_NAMES.items():
+        a = w.get(pre + n)
+        keep.refs.append(a)
+        setattr(b, f, _ptr(a))
+    return b
+
+
+def make_dit_struct(w: dict, n_layers: int):
+    keep = _Keep()
+    arr = (DitBlock * n_layers)()
+    for i in range(n_layers):
+        arr[i] = make_block_struct(w, i, keep)
+    m = Dit()
+    m.n_layers = n_layers
+    m.blocks = arr
+    keep.refs.append(arr)
+    for f, n in DIT_GLOBAL_NAMES.items():
+        a = w.get(n)
+        keep.refs.append(a)
+        setattr(m, f, _ptr(a))
+    return m, keep
+
+
+def make_pe_struct(w: dict, n_layers: int):
+    keep = _Keep()
+    arr = (PeLayer * n_layers)()
+    for i in range(n_layers):
+        pre = pe_layer_prefix(i)
+        for f, n in PE_LAYER_NAMES.items():
+            a = w.get(pre + n)
+            keep.refs.append(a)
+            setattr(arr[i], f, _ptr(a))
+    m = Pe()
+    m.n_layers = n_layers
+    m.layers = arr
+    keep.refs.append(arr)
+    for f, n in PE_GLOBAL_NAMES.items():
+        a = w.get(n)
+        keep.refs.append(a)
+        setattr(m, f, _ptr(a))
+    return m, keep
+
+
+class Oracle:
+    """The fp32 C restatement (liboracle.so)."""
+
+    def __init__(self, path: str = LIB_PATH):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle`")
+        self.lib = C.CDLL(path)
+        L = self.lib
+        L.orc_num_threads.restype = C.c_int
+        L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_sinusoid.argtypes = [C.c_float, _fp]
+        L.orc_compute_cond.argtypes = [C.POINTER(Dit), C.c_float, _fp, C.c_float, _fp]
+        L.orc_attention.argtypes = [_fp, _fp, C.c_int] + [_fp] * 7 + [_u8p, _fp]
+        L.orc_dit_block_fwd.argtypes = [_fp, _fp, _fp, C.POINTER(DitBlock), C.c_int, _u8p, _fp, C.c_int]
+        L.orc_dit_velocity.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp, _u8p, _fp, C.c_int, C.c_int, _fp]
+        L.orc_build_fm_mask.argtypes = [_u8p, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.orc_build_fm_pos.argtypes = [_fp, C.c_int, C.c_int, C.c_int]
+        L.orc_euler_solve.argtypes = [C.POINTER(Dit), C.c_int, C.c_int, C.c_int, _fp, _fp, _fp, _fp,
+                                      C.c_float, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, _fp]
+        L.orc_pe_forward.argtypes = [C.POINTER(Pe), _fp, C.c_int, C.c_int, _fp, _fp]
+        L.orc_linear_rows.argtypes = [_fp, _fp, C.c_int, _fp, _fp, C.c_int, C.c_int]
+
+    def set_threads(self, n):
+        self.lib.orc_set_threads(int(n))
+
+    def num_threads(self):
+        return self.lib.orc_num_threads()
+
+    def sinusoid(self, t):
+        se = np.zeros(256, np.float32)
+        self.lib.orc_sinusoid(C.c_float(t), _ptr(se))
+        return se
+
+    def compute_cond(self, w, t, spk=None, spk_scale=1.0, n_layers=0):
+        m, keep = make_dit_struct(w, n_layers)
+        out = np.zeros(1024, np.float32)
+        spk = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        self.lib.orc_compute_cond(C.byref(m), C.c_float(t), _ptr(spk), C.c_float(spk_scale), _ptr(out))
+        return out
+
+    def attention(self, x, wq, wk, wv, wo, bo=None, qn=None, kn=None, mask=None, pos=None):
+        x = np.ascontiguousarray(x, np.float32)
+        L = x.shape[0]
+        out = np.zeros((L, 1024), np.float32)
+        mk = _u8(mask)
+        pos = None if pos is None else np.ascontiguousarray(pos, np.float32)
+        self.lib.orc_attention(_ptr(out), _ptr(x), L, _ptr(wq), _ptr(wk), _ptr(wv), _ptr(wo), _ptr(bo),
+                               _ptr(qn), _ptr(kn), mk[0] if mk else None, _ptr(pos))
+        return out
+
+    def dit_block(self, w, i, x, cond, mask=None, pos=None, ffn_mode=FFN_PER_TOKEN):
+        keep = _Keep()
+        b = make_block_struct(w, i, keep)
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        mk = _u8(mask)
+        pos = None if pos is None else np.ascontiguousarray(pos, np.float32)
+        cond = np.ascontiguousarray(cond, np.float32)
+        self.lib.orc_dit_block_fwd(_ptr(out), _ptr(x), _ptr(cond), C.byref(b), x.shape[0],
+                                   mk[0] if mk else None, _ptr(pos), ffn_mode)
+        return out
+
+    def dit_velocity(self, w, n_layers, x_in, cond, mask=None, pos=None, ffn_mode=FFN_PER_TOKEN, n_out=None):
+        m, keep = make_dit_struct(w, n_layers)
+        x_in = np.ascontiguousarray(x_in, np.float32)
+        L = x_in.shape[0]
+        n_out = L if n_out is None else n_out
+        out = np.zeros((n_out, 128), np.float32)
+        mk = _u8(mask)
+        pos = None if pos is None else np.ascontiguousarray(pos, np.float32)
+        cond = np.ascontiguousarray(cond, np.float32)
+        self.lib.orc_dit_velocity(C.byref(m), _ptr(x_in), L, _ptr(cond), mk[0] if mk else None, _ptr(pos),
+                                  ffn_mode, n_out, _ptr(out))
+        return out
+
+    def fm_mask(self, total, fm_len, patch, hidden_patch=1):
+        m = np.zeros((total, total), np.uint8)
+        self.lib.orc_build_fm_mask(m.ctypes.data_as(_u8p), total, fm_len, patch, hidden_patch)
+        return m
+
+    def fm_pos(self, total, fm_len, patch):
+        p = np.zeros(total, np.float32)
+        self.lib.orc_build_fm_pos(_ptr(p), total, fm_len, patch)
+        return p
+
+    def euler_solve(self, w, n_layers, fm_cond, fm_uncond, z0, spk=None, spk_scale=1.5, nfe=10,
+                    cfg_scale=2.0, cfg_form=0, layout=0, ffn_mode=FFN_PER_TOKEN):
+        m, keep = make_dit_struct(w, n_layers)
+        fm_cond = np.ascontiguousarray(fm_cond, np.float32)
+        fm_uncond = np.ascontiguousarray(fm_uncond, np.float32)
+        z0 = np.ascontiguousarray(z0, np.float32)
+        n_utt, fm_len = fm_cond.shape[0], fm_cond.shape[1]
+        patch = z0.shape[1]
+        out = np.zeros_like(z0)
+        spk = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        self.lib.orc_euler_solve(C.byref(m), n_utt, fm_len, patch, _ptr(fm_cond), _ptr(fm_uncond), _ptr(z0),
+                                 _ptr(spk), C.c_float(spk_scale), nfe, C.c_float(cfg_scale), cfg_form,
+                                 layout, ffn_mode, _ptr(out))
+        return out
+
+    def pe_forward(self, w, n_layers, frames, pair_mode=PAIR_ADJACENT, want_hidden=False):
+        m, keep = make_pe_struct(w, n_layers)
+        frames = np.ascontiguousarray(frames, np.float32)
+        n_patches = frames.shape[0] // 4
+        out = np.zeros((n_patches, 1536), np.float32)
+        h = np.zeros((n_patches * 2, 1024), np.float32) if want_hidden else None
+        self.lib.orc_pe_forward(C.byref(m), _ptr(frames), n_patches, pair_mode, _ptr(out), _ptr(h))
+        return (out, h) if want_hidden else out
+
+    def linear_rows(self, x, w, b=None):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros((x.shape[0], w.shape[0]), np.float32)
+        self.lib.orc_linear_rows(_ptr(out), _ptr(x), x.shape[0], _ptr(w), _ptr(b), w.shape[1], w.shape[0])
+        return out
+
+
+class Reference:
+    """The reference's own include/dit_manual.h, compiled in place (_ref/)."""
+
+    def __init__(self, path: str = REF_PATH):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle` where the reference tree exists")
+        self.lib = C.CDLL(path)
+        L = self.lib
+        L.ref_num_threads.restype = C.c_int
+        L.ref_manual_attention.argtypes = [_fp, _fp, C.c_int] + [_fp] * 7 + [_u8p, _fp]
+        L.ref_dit_block.argtypes = [_fp, _fp, _fp, C.POINTER(DitBlock), C.c_int, _u8p, _fp, C.c_int]
+        L.ref_dit_velocity.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp, _u8p, _fp, C.c_int, C.c_int, _fp]
+
+    @staticmethod
+    def available(path: str = REF_PATH) -> bool:
+        return os.path.exists(path)
+
+    def num_threads(self):
+        return self.lib.ref_num_threads()
+
+    def manual_attention(self, x, wq, wk, wv, wo, bo=None, qn=None, kn=None, mask=None, pos=None):
+        x = np.ascontiguousarray(x, np.float32)
+        L = x.shape[0]
+        out = np.zeros((L, 1024), np.float32)
+        mk = _u8(mask)
+        pos = None if pos is None else np.ascontiguousarray(pos, np.float32)
+        self.lib.ref_manual_attention(_ptr(out), _ptr(x), L, _ptr(wq), _ptr(wk), _ptr(wv), _ptr(wo), _ptr(bo),
+                                      _ptr(qn), _ptr(kn), mk[0] if mk else None, _ptr(pos))
+        return out
+
+    def dit_block(self, w, i, x, cond, mask=None, pos=None, ffn_mode=FFN_PER_TOKEN):
+        keep = _Keep()
+        b = make_block_struct(w, i, keep)
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        mk = _u8(mask)
+        pos = None if pos is None else np.ascontiguousarray(pos, np.float32)
+        cond = np.ascontiguousarray(cond, np.float32)
+        self.lib.ref_dit_block(_ptr(out), _ptr(x), _ptr(cond), C.byref(b), x.shape[0],
+                               mk[0] if mk else None, _ptr(pos), ffn_mode)
+        return out
+
+    def dit_velocity(self, w, n_layers, x_in, cond, mask=None, pos=None, ffn_mode=FFN_PER_TOKEN, n_out=None):
+        m, keep = make_dit_struct(w, n_layers)
+        x_in = np.ascontiguousarray(x_in, np.float32)
+        L = x_in.shape[0]
+        n_out = L if n_out is None else n_out
+        out = np.zeros((n_out, 128), np.float32)
+        mk = _u8(mask)
+        pos = None if pos is None else np.ascontiguousarray(pos, np.float32)
+        cond = np.ascontiguousarray(cond, np.float32)
+        self.lib.ref_dit_velocity(C.byref(m), _ptr(x_in), L, _ptr(cond), mk[0] if mk else None, _ptr(pos),
+                                  ffn_mode, n_out, _ptr(out))
+        return out
