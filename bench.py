@@ -1,0 +1,363 @@
+#!/usr/bin/env python3
+"""Benchmark: DiT ODE-step evals/s of the B200 engine (or of the reference CPU path).
+
+Workload (default): one Euler flow-matching solve per utterance for one latent
+patch -- 10 steps of the 18-layer DiT velocity forward with classifier-free
+guidance (cond + uncond rows in one launch), CFG scale 2.0 (v4 form),
+64 utterances (128 CFG rows) per GPU, L = 64 tokens per row (60 FM-history
+tokens in the v4 layout with its attention mask and position ids, plus 4 noise
+frames), speaker x-vectors, bf16 weights with fp32 accumulation, the whole
+solve captured in one CUDA graph.  Weights are random-init N(0, 0.02) (seed 1)
+in the real architecture; inputs are seeded synthetic tensors of the real
+shapes.  One "eval" = one CFG-pair velocity evaluation, so a solve is
+n_utt * nfe evals.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs one process per GPU under torch.distributed.run (launched here if
+not already); every rank solves its own shard of utterances (weak scaling, no
+collective on the data path); times are CUDA-event device times, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(HERE, "dots.tts.cpp_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "DiT ODE-step evals/sec"
+UNIT = "evals/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n-utt", type=int, default=64, help="utterances per GPU")
+    ap.add_argument("--fm-len", type=int, default=60, help="FM history tokens (L = fm_len + patch)")
+    ap.add_argument("--patch", type=int, default=4)
+    ap.add_argument("--nfe", type=int, default=10)
+    ap.add_argument("--layers", type=int, default=18)
+    ap.add_argument("--cfg-scale", type=float, default=2.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
+    return ap.parse_args()
+
+
+def maybe_relaunch(args):
+    """--gpus N > 1 outside torchrun: relaunch this script under it."""
+    if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={args.gpus}",
+               "--master-addr", "127.0.0.1", "--master-port", str(29500 + os.getpid() % 1000)] + sys.argv
+        sys.exit(subprocess.call(cmd))
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- workload
+def make_inputs(args, rank):
+    import synth
+    seed = 1000 + rank
+    w = synth.dit_weights(1, n_layers=args.layers)
+    fc, fu = synth.fm_history(seed, args.n_utt, args.fm_len, w)
+    z0 = synth.normal(seed, "z0", (args.n_utt, args.patch, 128), 1.0)
+    spk = synth.normal(seed, "spk", (args.n_utt, 512), 1.0 / np.sqrt(512.0))
+    return w, fc, fu, z0, spk
+
+
+def workload_config(args, n):
+    L = args.fm_len + args.patch
+    return {"workload": f"DiT Euler solve, {args.layers} layers, CFG pair, v4 FM layout",
+            "n_utt_per_gpu": args.n_utt, "cfg_rows_per_gpu": 2 * args.n_utt, "seq_len": L,
+            "fm_len": args.fm_len, "patch": args.patch, "nfe": args.nfe, "cfg_scale": args.cfg_scale,
+            "weights": "bf16 (fp32 accumulate, fp32 residual)", "global_utterances": args.n_utt * n,
+            "parallelism": f"utterance shards x{n}, no collective",
+            "l2": "working set > L2: 0.69 GB of weights streamed per forward",
+            "graph": "whole solve in one CUDA graph"}
+
+
+def cpu_reference_eval(args, w, fc, fu, z0, spk, ffn_mode):
+    """One CFG-pair velocity eval (cond row + uncond row, step t = 0) through the
+    reference's own include/dit_manual.h built in oracle/_ref, wired like
+    src/e2e_pipeline_v4.cpp:438-506.  Returns seconds."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    orc, ref = O.Oracle(), O.Reference()
+    L = args.fm_len + args.patch
+    mask = orc.fm_mask(L, args.fm_len, args.patch)
+    pos = orc.fm_pos(L, args.fm_len, args.patch)
+    cond = orc.compute_cond(w, 0.0, spk[0], 1.5, n_layers=args.layers)
+    coord = orc.linear_rows(z0[0], w["coordinate_proj.weight"], w["coordinate_proj.bias"])
+    xs = []
+    for buf in (fc, fu):
+        x = np.zeros((L, 1024), np.float32)
+        x[:args.fm_len] = buf[0]
+        x[args.fm_len:] = coord
+        xs.append(x)
+    t = time.perf_counter()
+    for x in xs:
+        ref.dit_velocity(w, args.layers, x, cond, mask, pos, ffn_mode=ffn_mode, n_out=args.patch)
+    return time.perf_counter() - t, ref.num_threads()
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference CPU path (as shipped) on the host cores."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    if not O.Reference.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdtts_ref.so was not built"}))
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+    w, fc, fu, z0, spk = make_inputs(args, 0)
+    for _ in range(args.warmup):
+        cpu_reference_eval(args, w, fc, fu, z0, spk, O.FFN_AS_WRITTEN)
+    tot, cores = 0.0, 1
+    for _ in range(args.steps):
+        dt, cores = cpu_reference_eval(args, w, fc, fu, z0, spk, O.FFN_AS_WRITTEN)
+        tot += dt
+    value = args.steps / tot
+    sample = ("one CFG-pair velocity eval per step (cond + uncond row, L=%d, %d layers) through the "
+              "reference's manual_dit_block as shipped (include/dit_manual.h; FFN on token 0 only)"
+              % (args.fm_len + args.patch, args.layers))
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def load_traffic():
+    """Per-launch DRAM traffic of the dominant GEMM from the committed ncu summary."""
+    p = os.path.join(HERE, "profiles", "gemm_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import dtts
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    w, fc, fu, z0, spk = make_inputs(args, rank)
+    eng = dtts.DiT(w, n_layers=args.layers, device=local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    eng.set_stream(stream.cuda_stream)
+    kw = dict(spk_scale=1.5, nfe=args.nfe, cfg_scale=args.cfg_scale, cfg_form=dtts.CFG_V4,
+              layout=dtts.LAYOUT_FM_MASK, use_graph=True)
+
+    # ---- resident inputs (value)
+    d_fc, d_fu = torch.from_numpy(fc).to(dev), torch.from_numpy(fu).to(dev)
+    d_z0, d_spk = torch.from_numpy(z0).to(dev), torch.from_numpy(spk).to(dev)
+    d_z = torch.empty_like(d_z0)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            eng.solve(d_fc, d_fu, d_z0, d_spk, z_out=d_z, mem=dtts.MEM_DEVICE, **kw)
+        eng.sync()
+        launches_per_solve = eng.last_launch_count()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk = ClockSampler(local_rank)
+        clk.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            eng.solve(d_fc, d_fu, d_z0, d_spk, z_out=d_z, mem=dtts.MEM_DEVICE, **kw)
+        e1.record(stream)
+        eng.sync()
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            dist.barrier()
+
+    # ---- end to end through the public API with pinned host buffers (e2e)
+    e2e_ms = None
+    h2d = fc.nbytes + fu.nbytes + z0.nbytes + spk.nbytes
+    d2h = z0.nbytes
+    if not args.no_e2e:
+        p_fc, p_fu = torch.from_numpy(fc).pin_memory(), torch.from_numpy(fu).pin_memory()
+        p_z0, p_spk = torch.from_numpy(z0).pin_memory(), torch.from_numpy(spk).pin_memory()
+        p_z = torch.empty_like(p_z0).pin_memory()
+        hfc, hfu, hz0, hspk, hz = (t.numpy() for t in (p_fc, p_fu, p_z0, p_spk, p_z))
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                eng.solve(hfc, hfu, hz0, hspk, z_out=hz, mem=dtts.MEM_HOST, **kw)
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+            for _ in range(args.steps):
+                eng.solve(hfc, hfu, hz0, hspk, z_out=hz, mem=dtts.MEM_HOST, **kw)
+            e3.record(stream)
+            torch.cuda.synchronize()
+            e2e_ms = e2.elapsed_time(e3)
+            if dist:
+                dist.barrier()
+
+    # ---- max over ranks
+    t = torch.tensor([ms, e2e_ms if e2e_ms is not None else 0.0], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms_max = float(t[0]), float(t[1])
+
+    evals = args.n_utt * args.nfe * args.steps * world
+    value = evals / (ms / 1000.0)
+    e2e_value = evals / (e2e_ms_max / 1000.0) if e2e_ms is not None else None
+
+    # ---- roofline of the dominant kernel (tcgen05 GEMM, live CUDA events)
+    roof, attn_us, kernels = None, None, {}
+    if not args.no_roofline:
+        with torch.cuda.stream(stream):
+            names = {0: "gemm_qkv", 1: "gemm_o", 2: "gemm_ffn1", 3: "gemm_ffn2", 4: "attention", 5: "ln_modulate",
+                     6: "gemm_adaln", 7: "gemm_input"}
+            for kind, name in names.items():
+                us, fl, by = eng.profile(kind, iters=20)
+                kernels[name] = {"us": us, "flops": fl, "bytes": by}
+        f = sum(kernels[n]["flops"] for n in ("gemm_qkv", "gemm_o", "gemm_ffn1", "gemm_ffn2"))
+        tt = sum(kernels[n]["us"] for n in ("gemm_qkv", "gemm_o", "gemm_ffn1", "gemm_ffn2"))
+        achieved = f / (tt * 1e-6) / 1e12
+        peaks = {}
+        try:
+            with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as fh:
+                peaks = json.load(fh)
+        except (OSError, ValueError):
+            pass
+        peak = peaks.get("bf16_tflops", 1590.0)
+        src = "measured (burst, kernel timed alone)" if "bf16_tflops" in peaks else "fallback"
+        tr = load_traffic()
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": tr.get("bytes_per_launch") if tr else None,
+                "kernel": "gemm_tc_kernel (tcgen05, the four per-block GEMMs, FLOP-weighted)",
+                "peak_source": src,
+                "algorithmic_flops_per_block": f}
+        attn_us = kernels["attention"]["us"]
+
+    # ---- CPU baseline: reference code (per-token FFN) on the host, rank 0, N = 1
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(HERE, "oracle"))
+        import oracle as O
+        if O.Reference.available():
+            os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+            secs, cores = cpu_reference_eval(args, w, fc, fu, z0, spk, O.FFN_PER_TOKEN)
+            cpu = {"value": 1.0 / secs, "unit": UNIT, "cores": cores, "kind": "reference",
+                   "sample": "one CFG-pair eval (2 rows, L=%d, %d layers) through the reference's "
+                             "include/dit_manual.h (FFN per token) built in oracle/_ref, %.1f s"
+                             % (args.fm_len + args.patch, args.layers, secs)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights)",
+            "config": workload_config(args, world),
+            "e2e": None if e2e_value is None else {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                                                    "d2h_bytes_per_step": d2h},
+            "roofline": roof,
+            "attention_us_per_layer": attn_us,
+            "kernels_us": {k: round(v["us"], 2) for k, v in kernels.items()},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": launches_per_solve * args.steps,
+        }
+        print(json.dumps(line))
+    eng.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    maybe_relaunch(args)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()
