@@ -25,7 +25,11 @@ using namespace dtts;
 namespace {
 
 constexpr int kAdaPerLayer = 6 * kD;
-constexpr int kBN = 256;
+
+// Tile configuration of one GEMM: tile width BN, epilogue warps, K splits.
+struct GemmTune {
+    int bn, nw, ks;
+};
 
 // ---------------------------------------------------------------- host tables
 // RoPE (cos, sin) per token for the half-split rotation of
@@ -113,16 +117,19 @@ int upload_bf16_concat(DeviceArena &a, const std::vector<std::pair<const float *
     return DTTS_OK;
 }
 
-GemmOp make_op(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int epi, int *err) {
+GemmOp make_op(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int epi, int *err,
+               const GemmTune &t) {
     GemmOp op;
     std::memset(&op, 0, sizeof(op));
     op.ta = ta;
     op.tb = tb;
     op.M = M; op.N = N; op.K = K;
-    op.bn = kBN;
+    op.bn = t.bn;
+    op.nw = t.nw;
     op.epi = epi;
     op.ep.err = err;
     op.ep.tok_per_row = 1;
+    op.ep.ksplit = t.ks;
     return op;
 }
 
@@ -143,6 +150,10 @@ struct dtts_dit {
     bf16 *w_ada = nullptr, *w_in = nullptr;
     float *b_ada = nullptr, *b_in = nullptr;
     CUtensorMap t_ada, t_in;
+    // tile configurations (tunable, see dtts_dit_tune)
+    // defaults from a sweep on B200 at 128 CFG rows x L = 64 (8192 tokens)
+    GemmTune tu_qkv{192, 8, 1}, tu_o{256, 4, 1}, tu_ffn1{256, 4, 1}, tu_ffn2{256, 4, 2}, tu_ada{256, 8, 1},
+        tu_in{256, 4, 1};
     float *t_w1 = nullptr, *t_b1 = nullptr, *t_w2 = nullptr, *t_b2 = nullptr;
     float *spk_w1 = nullptr, *spk_b1 = nullptr, *spk_lw = nullptr, *spk_lb = nullptr;
     float *out_w = nullptr, *out_b = nullptr, *coord_w = nullptr, *coord_b = nullptr;
@@ -157,7 +168,7 @@ struct dtts_dit {
           *spk_in = nullptr;
     float2 *rope = nullptr;
     uint8_t *mask = nullptr;
-    CUtensorMap t_x_in, t_act, t_att, t_ffn, t_acond;
+    CUtensorMap t_x_in, t_act, t_att, t_ffn, t_acond, t_h;
 
     // shapes of the last forward (for profiling) and launch accounting
     int last_rows = 0, last_L = 0, last_P = 0;
@@ -176,11 +187,17 @@ struct dtts_dit {
     }
 
     int ensure_workspace(int rows, int L, int nfe);
+    int build_weight_maps();
     int gemm(const GemmOp &op) {
         launches++;
         DTTS_CUDA(launch_gemm(op, num_sms, stream));
         return DTTS_OK;
     }
+    // modulation source of the current forward: row r of sequence tokens uses
+    // ada_cur + (r / rows_per_ada) * n_ada
+    const float *ada_cur = nullptr;
+    int rows_per_ada = 1;
+    int last_ada_rows = 0;
     int enqueue_forward(int rows, int L, int P);
     int enqueue_block_op(int kind, int l, int rows, int L);
     int enqueue_solve(const dtts_solve_args *a);
@@ -209,15 +226,15 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
     h = (float *)A(T * kD * 4);
     in_a = (float *)A(T * kD * 4);
     in_b = (float *)A(T * kD * 4);
-    a_cond = (bf16 *)A(R * kD * 2);
-    ada = (float *)A(R * (size_t)n_ada * 4);
+    a_cond = (bf16 *)A(R * (size_t)cap_nfe * kD * 2);
+    ada = (float *)A(R * (size_t)cap_nfe * n_ada * 4);
     vel = (float *)A(T * kLat * 4);
     z = (float *)A(T * kLat * 4);
     cond_f32 = (float *)A(R * kD * 4);
     spk_c = (float *)A(R * kD * 4);
     spk_in = (float *)A(R * kSpk * 4);
-    temb = (float *)A(kD * 4);
-    h1 = (float *)A(kD * 4);
+    temb = (float *)A((size_t)cap_nfe * kD * 4);
+    h1 = (float *)A((size_t)cap_nfe * kD * 4);
     se_tab = (float *)A((size_t)cap_nfe * 256 * 4);
     rope = (float2 *)A((size_t)cap_L * 32 * sizeof(float2));
     mask = (uint8_t *)A((size_t)cap_L * cap_L);
@@ -225,8 +242,22 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
         if (!p) { set_error("workspace allocation failed (%lld tokens)", tok); cap_tok = cap_rows = cap_L = 0; ws.free_all(); return DTTS_ERR_OOM; }
     bool ok = make_tmap_bf16(&t_x_in, x_in, T, kD, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
               make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
-              make_tmap_bf16(&t_acond, a_cond, R, kD, 128);
+              make_tmap_bf16(&t_acond, a_cond, R * (size_t)cap_nfe, kD, 128) && make_tmap_f32_resid(&t_h, h, T, kD);
     DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace buffer");
+    return DTTS_OK;
+}
+
+// Weight tensor maps: the TMA box height of B is the GEMM's tile width.
+int dtts_dit::build_weight_maps() {
+    for (int l = 0; l < n_layers; l++) {
+        Layer &L = layers[l];
+        bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, tu_qkv.bn) &&
+                  make_tmap_bf16(&L.to, L.wo, kD, kD, tu_o.bn) && make_tmap_bf16(&L.t1, L.w1, kF, kD, tu_ffn1.bn) &&
+                  make_tmap_bf16(&L.t2, L.w2, kD, kF, tu_ffn2.bn);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for block %d", l);
+    }
+    bool ok = make_tmap_bf16(&t_ada, w_ada, n_ada, kD, tu_ada.bn) && make_tmap_bf16(&t_in, w_in, kD, kD, tu_in.bn);
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed (adaLN / input_layer)");
     return DTTS_OK;
 }
 
@@ -235,17 +266,18 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
 int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
     const int M = rows * L;
     const Layer &Ly = layers[l];
-    const long long base = (long long)l * kAdaPerLayer;
+    const float *ada_l = ada_cur + (long long)l * kAdaPerLayer;
+    const int tpr = L * rows_per_ada;   // tokens sharing one modulation row
     switch (kind) {
         case 5:
         case 6: {
             const long long off = kind == 5 ? 0 : 3 * kD;
             launches++;
-            launch_ln_modulate(h, act, M, ada + base + off, ada + base + off + kD, n_ada, L, stream);
+            launch_ln_modulate(h, act, M, ada_l + off, ada_l + off + kD, n_ada, tpr, stream);
             return DTTS_OK;
         }
         case 0: {
-            GemmOp op = make_op(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
+            GemmOp op = make_op(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err, tu_qkv);
             op.ep.q = q; op.ep.k = k; op.ep.v = v;
             op.ep.ldq = kD; op.ep.ldkv = kD;
             op.ep.tok_per_row = L; op.ep.kv_cap = L; op.ep.kv_start = 0;
@@ -264,20 +296,22 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             return DTTS_OK;
         }
         case 1: {
-            GemmOp op = make_op(t_att, Ly.to, M, kD, kD, EPI_RESID_GATED, d_err);
+            GemmOp op = make_op(t_att, Ly.to, M, kD, kD, EPI_RESID_GATED, d_err, tu_o);
+            op.tr = t_h;
             op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
-            op.ep.gate = ada + base + 2 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = L;
+            op.ep.gate = ada_l + 2 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = tpr;
             return gemm(op);
         }
         case 2: {
-            GemmOp op = make_op(t_act, Ly.t1, M, kF, kD, EPI_GELU_BF16, d_err);
+            GemmOp op = make_op(t_act, Ly.t1, M, kF, kD, EPI_GELU_BF16, d_err, tu_ffn1);
             op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
             return gemm(op);
         }
         case 3: {
-            GemmOp op = make_op(t_ffn, Ly.t2, M, kD, kF, EPI_RESID_GATED, d_err);
+            GemmOp op = make_op(t_ffn, Ly.t2, M, kD, kF, EPI_RESID_GATED, d_err, tu_ffn2);
+            op.tr = t_h;
             op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
-            op.ep.gate = ada + base + 5 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = L;
+            op.ep.gate = ada_l + 5 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = tpr;
             return gemm(op);
         }
     }
@@ -285,18 +319,12 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
     return DTTS_ERR_ARG;
 }
 
-// Expects x_in (bf16), a_cond (bf16), rope and mask filled.
+// Expects x_in (bf16), the modulation rows at ada_cur, rope and mask filled.
 int dtts_dit::enqueue_forward(int rows, int L, int P) {
     const int M = rows * L;
     last_rows = rows; last_L = L; last_P = P;
-    {   // adaLN for every block + output layer
-        GemmOp op = make_op(t_acond, t_ada, rows, n_ada, kD, EPI_F32, d_err);
-        op.ep.bias = b_ada; op.ep.out = ada; op.ep.ldo = n_ada;
-        int st = gemm(op);
-        if (st) return st;
-    }
     {   // input layer
-        GemmOp op = make_op(t_x_in, t_in, M, kD, kD, EPI_F32, d_err);
+        GemmOp op = make_op(t_x_in, t_in, M, kD, kD, EPI_F32, d_err, tu_in);
         op.ep.bias = b_in; op.ep.out = h; op.ep.ldo = kD;
         int st = gemm(op);
         if (st) return st;
@@ -309,7 +337,8 @@ int dtts_dit::enqueue_forward(int rows, int L, int P) {
         }
     const long long oo = (long long)n_layers * kAdaPerLayer;
     launches++;
-    launch_out_head(h, rows, L, P, ada + oo, ada + oo + kD, n_ada, out_w, out_b, vel, d_err, stream);
+    launch_out_head(h, rows, L, P, ada_cur + oo, ada_cur + oo + kD, n_ada, rows_per_ada, out_w, out_b, vel, d_err,
+                    stream);
     DTTS_CUDA(cudaGetLastError());
     return DTTS_OK;
 }
@@ -324,12 +353,24 @@ int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
         launch_speaker_cond(spk_in, a->n_utt, spk_w1, spk_b1, spk_lw, spk_lb, a->spk_scale, spk_c, stream);
     }
     const float dt = 1.0f / (float)a->nfe;
+    // Conditioning of every step up front: c depends only on t_k and the
+    // speaker, so one adaLN GEMM covers all steps and utterances (cond and
+    // uncond rows of an utterance share c).
+    launches += 3;
+    launch_time_mlp(se_tab, a->nfe, t_w1, t_b1, t_w2, t_b2, h1, temb, stream);
+    launch_cond_rows(temb, a->nfe, a->spk ? spk_c : nullptr, a->n_utt, a_cond, stream);
+    {
+        GemmOp op = make_op(t_acond, t_ada, a->nfe * a->n_utt, n_ada, kD, EPI_F32, d_err, tu_ada);
+        op.ep.bias = b_ada; op.ep.out = ada; op.ep.ldo = n_ada;
+        int st = gemm(op);
+        if (st) return st;
+        last_ada_rows = a->nfe * a->n_utt;
+    }
     launches++;
     launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 0, coord_w, coord_b, x_in, L, stream);
+    rows_per_ada = 2;
     for (int step = 0; step < a->nfe; step++) {
-        launches += 3;
-        launch_time_mlp(se_tab + (size_t)step * 256, t_w1, t_b1, t_w2, t_b2, h1, temb, stream);
-        launch_cond_rows(temb, a->spk ? spk_c : nullptr, rows, 2, a_cond, stream);
+        ada_cur = ada + (size_t)step * a->n_utt * n_ada;
         int st = enqueue_forward(rows, L, a->patch);
         if (st) return st;
         launches++;
@@ -399,9 +440,6 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
         if ((st = upload_f32(e->wts, b.b2, kD, &L.b2, s))) return st;
         if ((st = upload_f32(e->wts, b.qn, kHD, &L.qn, s))) return st;
         if ((st = upload_f32(e->wts, b.kn, kHD, &L.kn, s))) return st;
-        bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, kBN) && make_tmap_bf16(&L.to, L.wo, kD, kD, kBN) &&
-                  make_tmap_bf16(&L.t1, L.w1, kF, kD, kBN) && make_tmap_bf16(&L.t2, L.w2, kD, kF, kBN);
-        DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for block %d", l);
     }
     // adaLN of all blocks followed by the output adaLN: one [n_ada][1024] matrix
     e->n_ada = w->n_layers * kAdaPerLayer + 2 * kD;
@@ -418,10 +456,8 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
         if ((st = upload_bf16_concat(e->wts, parts, kD, &e->w_ada, s))) return st;
         if ((st = upload_f32(e->wts, bias.data(), bias.size(), &e->b_ada, s))) return st;
         DTTS_CUDA(cudaStreamSynchronize(s));
-        DTTS_CHECK(make_tmap_bf16(&e->t_ada, e->w_ada, e->n_ada, kD, kBN), DTTS_ERR_CUDA, "tensor map (adaLN)");
     }
     if ((st = upload_bf16_concat(e->wts, {{w->in_w, kD}}, kD, &e->w_in, s))) return st;
-    DTTS_CHECK(make_tmap_bf16(&e->t_in, e->w_in, kD, kD, kBN), DTTS_ERR_CUDA, "tensor map (input_layer)");
     if ((st = upload_f32(e->wts, w->in_b, kD, &e->b_in, s))) return st;
     if ((st = upload_f32(e->wts, w->t_w1, (size_t)kD * 256, &e->t_w1, s))) return st;
     if ((st = upload_f32(e->wts, w->t_b1, kD, &e->t_b1, s))) return st;
@@ -436,6 +472,7 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     if ((st = upload_f32(e->wts, w->coord_w, (size_t)kD * kLat, &e->coord_w, s))) return st;
     if ((st = upload_f32(e->wts, w->coord_b, kD, &e->coord_b, s))) return st;
     DTTS_CUDA(cudaStreamSynchronize(s));
+    if ((st = e->build_weight_maps())) return st;
     *out = e.release();
     return DTTS_OK;
 }
@@ -492,6 +529,14 @@ int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const u
     e->launches += 2;
     launch_f32_to_bf16(e->in_a, e->x_in, (long long)ntok * kD, s);
     launch_silu_bf16(e->cond_f32, e->a_cond, (long long)rows * kD, s);
+    {
+        GemmOp op = make_op(e->t_acond, e->t_ada, rows, e->n_ada, kD, EPI_F32, e->d_err, e->tu_ada);
+        op.ep.bias = e->b_ada; op.ep.out = e->ada; op.ep.ldo = e->n_ada;
+        if ((st = e->gemm(op))) return st;
+    }
+    e->last_ada_rows = rows;
+    e->ada_cur = e->ada;
+    e->rows_per_ada = 1;
     if ((st = e->enqueue_forward(rows, L, n_out))) return st;
     const cudaMemcpyKind out_kind = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
     DTTS_CUDA(cudaMemcpyAsync(out, e->vel, (size_t)rows * n_out * kLat * 4, out_kind, s));
@@ -574,6 +619,28 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
     return e->finish(a->mem == DTTS_MEM_HOST);
 }
 
+int dtts_dit_tune(dtts_dit *e, const char *gemm, int bn, int epi_warps, int ksplit) {
+    DTTS_CHECK(e && gemm, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(bn == 128 || bn == 192 || bn == 256, DTTS_ERR_ARG, "bn must be 128, 192 or 256");
+    DTTS_CHECK(epi_warps == 4 || epi_warps == 8, DTTS_ERR_ARG, "epi_warps must be 4 or 8");
+    DTTS_CHECK(ksplit == 1 || ksplit == 2 || ksplit == 4 || ksplit == 8, DTTS_ERR_ARG, "ksplit must be 1, 2, 4 or 8");
+    const std::string g(gemm);
+    GemmTune t{bn, epi_warps, ksplit};
+    GemmTune *dst = g == "qkv" ? &e->tu_qkv : g == "o" ? &e->tu_o : g == "ffn1" ? &e->tu_ffn1 : g == "ffn2" ? &e->tu_ffn2
+                  : g == "adaln" ? &e->tu_ada : g == "input" ? &e->tu_in : nullptr;
+    DTTS_CHECK(dst, DTTS_ERR_ARG, "unknown GEMM '%s' (qkv, o, ffn1, ffn2, adaln, input)", gemm);
+    const int n = g == "qkv" ? 3 * kD : g == "ffn1" ? kF : g == "adaln" ? e->n_ada : kD;
+    DTTS_CHECK(n % bn == 0, DTTS_ERR_ARG, "N = %d is not a multiple of bn %d", n, bn);
+    const bool resid = g == "o" || g == "ffn2";
+    DTTS_CHECK(ksplit == 1 || resid, DTTS_ERR_ARG, "ksplit > 1 only for the residual GEMMs (o, ffn2)");
+    DeviceGuard gd(e->device);
+    DTTS_CUDA(cudaStreamSynchronize(e->stream));
+    *dst = t;
+    if (e->gexec) { cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
+    e->gkey.clear();
+    return e->build_weight_maps();
+}
+
 int dtts_dit_last_launch_count(dtts_dit *e, int *n) {
     DTTS_CHECK(e && n, DTTS_ERR_ARG, "null argument");
     *n = e->launches;
@@ -596,12 +663,12 @@ int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us, double 
             case 4: return e->enqueue_block_op(4, 0, rows, L);
             case 5: return e->enqueue_block_op(5, 0, rows, L);
             case 6: {
-                GemmOp op = make_op(e->t_acond, e->t_ada, rows, e->n_ada, kD, EPI_F32, e->d_err);
+                GemmOp op = make_op(e->t_acond, e->t_ada, e->last_ada_rows, e->n_ada, kD, EPI_F32, e->d_err, e->tu_ada);
                 op.ep.bias = e->b_ada; op.ep.out = e->ada; op.ep.ldo = e->n_ada;
                 return e->gemm(op);
             }
             case 7: {
-                GemmOp op = make_op(e->t_x_in, e->t_in, (int)M, kD, kD, EPI_F32, e->d_err);
+                GemmOp op = make_op(e->t_x_in, e->t_in, (int)M, kD, kD, EPI_F32, e->d_err, e->tu_in);
                 op.ep.bias = e->b_in; op.ep.out = e->h; op.ep.ldo = kD;
                 return e->gemm(op);
             }
@@ -634,7 +701,11 @@ int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us, double 
         case 3: f = 2 * M * kD * kF; b = W * (M * kF + 1.0 * kF * kD) + 8 * M * kD; break;
         case 4: f = 4.0 * rows * kH * (double)L * L * kHD; b = W * 4 * M * kD; break;
         case 5: f = 0; b = M * kD * 4 + M * kD * 2; break;
-        case 6: f = 2.0 * rows * e->n_ada * kD; b = W * ((double)e->n_ada * kD + rows * kD) + 4.0 * rows * e->n_ada; break;
+        case 6: {
+            const double ar = e->last_ada_rows;
+            f = 2.0 * ar * e->n_ada * kD; b = W * ((double)e->n_ada * kD + ar * kD) + 4.0 * ar * e->n_ada;
+            break;
+        }
         case 7: f = 2 * M * kD * kD; b = W * (M * kD + 1.0 * kD * kD) + 4 * M * kD; break;
     }
     if (flops) *flops = f;

@@ -24,43 +24,46 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int NW>
 cudaError_t launch_one(const GemmOp &op, int num_sms, cudaStream_t s) {
-    using Cfg = GemmCfg<BN>;
-    const int tiles = ((op.M + Cfg::BM - 1) / Cfg::BM) * (op.N / BN);
-    const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_tc_kernel<BN, EPI><<<grid, 192, Cfg::SMEM_BYTES, s>>>(op.ta, op.tb, op.M, op.N, op.K, op.ep);
+    using Cfg = GemmCfg<BN, NW, EPI>;
+    const int units = ((op.M + Cfg::BM - 1) / Cfg::BM) * (op.N / BN) * (op.ep.ksplit > 0 ? op.ep.ksplit : 1);
+    const int grid = units < num_sms ? units : num_sms;
+    gemm_tc_kernel<BN, EPI, NW><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(op.ta, op.tb, op.tr, op.M, op.N, op.K,
+                                                                            op.ep);
     return cudaGetLastError();
 }
 
-template <int BN>
+template <int BN, int NW>
 cudaError_t dispatch_epi(const GemmOp &op, int num_sms, cudaStream_t s) {
     switch (op.epi) {
-        case EPI_BF16: return launch_one<BN, EPI_BF16>(op, num_sms, s);
-        case EPI_GELU_BF16: return launch_one<BN, EPI_GELU_BF16>(op, num_sms, s);
-        case EPI_SILU_BF16: return launch_one<BN, EPI_SILU_BF16>(op, num_sms, s);
-        case EPI_F32: return launch_one<BN, EPI_F32>(op, num_sms, s);
-        case EPI_RESID: return launch_one<BN, EPI_RESID>(op, num_sms, s);
-        case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED>(op, num_sms, s);
-        case EPI_QKV: return launch_one<BN, EPI_QKV>(op, num_sms, s);
+        case EPI_BF16: return launch_one<BN, EPI_BF16, NW>(op, num_sms, s);
+        case EPI_GELU_BF16: return launch_one<BN, EPI_GELU_BF16, NW>(op, num_sms, s);
+        case EPI_SILU_BF16: return launch_one<BN, EPI_SILU_BF16, NW>(op, num_sms, s);
+        case EPI_F32: return launch_one<BN, EPI_F32, NW>(op, num_sms, s);
+        case EPI_RESID: return launch_one<BN, EPI_RESID, NW>(op, num_sms, s);
+        case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED, NW>(op, num_sms, s);
+        case EPI_QKV: return launch_one<BN, EPI_QKV, NW>(op, num_sms, s);
         default: return cudaErrorInvalidValue;
     }
 }
 
-template <int BN>
+template <int BN, int NW, int EPI>
+cudaError_t prepare_one() {
+    return cudaFuncSetAttribute((const void *)gemm_tc_kernel<BN, EPI, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                GemmCfg<BN, NW, EPI>::SMEM_BYTES);
+}
+
+template <int BN, int NW>
 cudaError_t prepare_bn() {
-    using Cfg = GemmCfg<BN>;
-    const void *fns[] = {
-        (const void *)gemm_tc_kernel<BN, EPI_BF16>,        (const void *)gemm_tc_kernel<BN, EPI_GELU_BF16>,
-        (const void *)gemm_tc_kernel<BN, EPI_SILU_BF16>,   (const void *)gemm_tc_kernel<BN, EPI_F32>,
-        (const void *)gemm_tc_kernel<BN, EPI_RESID>,       (const void *)gemm_tc_kernel<BN, EPI_RESID_GATED>,
-        (const void *)gemm_tc_kernel<BN, EPI_QKV>,
-    };
-    for (const void *f : fns) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-    }
-    return cudaSuccess;
+    cudaError_t e;
+    if ((e = prepare_one<BN, NW, EPI_BF16>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_GELU_BF16>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_SILU_BF16>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_F32>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_RESID>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_RESID_GATED>()) != cudaSuccess) return e;
+    return prepare_one<BN, NW, EPI_QKV>();
 }
 
 }  // namespace
@@ -68,9 +71,27 @@ cudaError_t prepare_bn() {
 // Opts every GEMM instantiation into its dynamic shared-memory size on the
 // current device (attributes are per device; called when an engine is created).
 cudaError_t gemm_prepare_attributes() {
-    cudaError_t e = prepare_bn<128>();
-    if (e != cudaSuccess) return e;
-    return prepare_bn<256>();
+    cudaError_t e;
+    if ((e = prepare_bn<128, 4>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<192, 4>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<256, 4>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<128, 8>()) != cudaSuccess) return e;
+    if ((e = prepare_bn<192, 8>()) != cudaSuccess) return e;
+    return prepare_bn<256, 8>();
+}
+
+bool make_tmap_f32_resid(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || !base || rows == 0 || cols % 32 != 0) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 4};
+    cuuint32_t box[2] = {32, 32};        // 32 fp32 = 128 bytes per row, 32 rows: one warp's staging tile
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
@@ -89,11 +110,17 @@ bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, u
 }
 
 cudaError_t launch_gemm(const GemmOp &op, int num_sms, cudaStream_t s) {
-    if (op.M < 1 || op.K % 64 != 0 || op.K < 64 || op.N % op.bn != 0) return cudaErrorInvalidValue;
-    if (op.epi == EPI_QKV && op.N % 64 != 0) return cudaErrorInvalidValue;
-    switch (op.bn) {
-        case 128: return dispatch_epi<128>(op, num_sms, s);
-        case 256: return dispatch_epi<256>(op, num_sms, s);
+    const int ks = op.ep.ksplit > 0 ? op.ep.ksplit : 1;
+    if (op.M < 1 || op.K < 64 * ks || op.K % (64 * ks) != 0 || op.N % op.bn != 0) return cudaErrorInvalidValue;
+    if (ks > 1 && !is_resid(op.epi)) return cudaErrorInvalidValue;
+    const int nw = op.nw == 8 ? 8 : 4;
+    switch (op.bn * 16 + nw) {
+        case 128 * 16 + 4: return dispatch_epi<128, 4>(op, num_sms, s);
+        case 192 * 16 + 4: return dispatch_epi<192, 4>(op, num_sms, s);
+        case 256 * 16 + 4: return dispatch_epi<256, 4>(op, num_sms, s);
+        case 128 * 16 + 8: return dispatch_epi<128, 8>(op, num_sms, s);
+        case 192 * 16 + 8: return dispatch_epi<192, 8>(op, num_sms, s);
+        case 256 * 16 + 8: return dispatch_epi<256, 8>(op, num_sms, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -3,19 +3,28 @@
 //   C[M, N] = A[M, K] * B[N, K]^T     A, B bf16 K-major (PyTorch Linear: B is
 //                                      the [out, in] weight), fp32 accumulate
 //
-// One persistent CTA per SM, 6 warps:
+// One persistent CTA per SM:
 //   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage,
 //               128-byte swizzle, mbarrier complete_tx
 //   warp 1      TMEM allocator + MMA issuer (one thread): 4 x
 //               tcgen05.mma.cta_group::1.kind::f16 (128 x BN x 16) per stage,
 //               tcgen05.commit frees the stage
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fused op, store
-// Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i run
-// while the MMAs of tile i+1 accumulate.  Every mbarrier wait is bounded
-// (common.cuh); on expiry the CTA drains and returns with an error code.
+//   warps 2..   NW epilogue warps: tcgen05.ld 32 lanes x 32 columns, fused op,
+//               then each warp stages its 32 rows x 128 bytes in shared memory
+//               (16-byte chunks XOR-swizzled by row) and writes them back with
+//               8 lanes per row, 4 full 128-byte row segments per instruction.
+// Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of one tile run
+// while the MMAs of the next accumulate.  Work units are (tile, K split).  The
+// residual epilogues never read the residual: each warp stages gate * (acc +
+// bias) and adds it into the fp32 residual with a TMA bulk reduce-add
+// (cp.reduce.async.bulk.tensor ... .add), double-buffered, so K splits simply
+// add their partials.  Every
+// mbarrier wait is bounded (common.cuh); on expiry the CTA drains and returns
+// with an error code in the device error word.
 //
-// Shape rules (checked on the host): N % BN == 0, K % 64 == 0, M >= 1; rows
-// past M are zero-filled by TMA and never stored.
+// Shape rules (checked on the host): N % BN == 0, K % (64 * ksplit) == 0,
+// ksplit > 1 only for EPI_RESID / EPI_RESID_GATED; rows past M are
+// zero-filled by TMA and never stored.
 #pragma once
 #include "common.cuh"
 
@@ -35,13 +44,15 @@ enum RopeMode : int { ROPE_HALF = 0, ROPE_ADJACENT = 1 };
 
 struct EpiParams {
     const float *bias;        // [N] or nullptr
+    // EPI_RESID*: the residual is also described by the third tensor map of the
+    // kernel (fp32, box 32 x 32, 128-byte swizzle) for the bulk reduce-add
     void *out;                // EPI_BF16/GELU/SILU: bf16; EPI_F32: f32
     long long ldo;
     float *resid;             // EPI_RESID*: fp32 [M][ldr]
     long long ldr;
     const float *gate;        // EPI_RESID_GATED: gate[(m / tok_per_row) * gate_ld + n]
     long long gate_ld;
-    int tok_per_row;          // tokens per sequence row (L); maps token m -> (row, t)
+    int tok_per_row;          // tokens per gate row / per sequence; maps token m -> (row, t)
     // EPI_QKV: columns [0,1024) -> q, [1024,2048) -> k, [2048,3072) -> v
     bf16 *q, *k, *v;
     long long ldq, ldkv;      // q[m*ldq + c]; k/v[((m/T)*kv_cap + kv_start + m%T) * ldkv + c]
@@ -50,22 +61,32 @@ struct EpiParams {
     const float *qn, *kn;     // its gains [64], or nullptr for none
     const float2 *rope;       // [positions][32] (cos, sin); row index = kv_start + m%T
     int rope_mode;
+    int ksplit;               // K splits (>= 1)
     int *err;                 // device error word
 };
 
-template <int BN>
+__host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || epi == EPI_RESID_GATED; }
+
+template <int BN, int NW, int EPI>
 struct GemmCfg {
     static constexpr int BM = 128, BK = 64;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
-    static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+    static constexpr int STAGE_BUFS = is_resid(EPI) ? 2 : 1;  // staging buffers per epilogue warp
+    static constexpr int STAGE_STAGING = NW * STAGE_BUFS * 32 * 128;  // 32 rows x 128 bytes each
+    static constexpr int SMEM_MAX = 227 * 1024;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
+    static constexpr int STAGES_FIT = (SMEM_MAX - STAGE_STAGING - BAR_BYTES - 1024) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+    static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGE_STAGING + BAR_BYTES + 1024;  // +1024 alignment slack
+    static constexpr int THREADS = 64 + NW * 32;
     static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
-    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
+    static_assert(NW == 4 || NW == 8, "epilogue warps");
+    static_assert(STAGES >= 3, "pipeline depth");
 };
 
 DTTS_DEV float gelu_tanh_fast(float x) {
@@ -74,21 +95,28 @@ DTTS_DEV float gelu_tanh_fast(float x) {
 }
 DTTS_DEV float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-// Stores 32 consecutive bf16 values (64 bytes, 16-byte aligned).
-DTTS_DEV void store_bf16x32(bf16 *dst, const float (&v)[32]) {
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
+// ---- per-warp staging buffer: 32 rows x 128 bytes, 16-byte chunks swizzled by row
+DTTS_DEV uint32_t stage_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+
+DTTS_DEV void stage_put(uint8_t *wbuf, int lane, const float (&v)[32]) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+    for (int c = 0; c < 8; c++)
+        *reinterpret_cast<float4 *>(wbuf + stage_off(lane, c)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+DTTS_DEV void stage_put_bf16(uint8_t *wbuf, int lane, const float (&lo)[32], const float (&hi)[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
         uint4 u;
-        u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
-        u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
-        u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
-        u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-        d[i] = u;
+        u.x = pack_bf16x2(lo[8 * c + 0], lo[8 * c + 1]); u.y = pack_bf16x2(lo[8 * c + 2], lo[8 * c + 3]);
+        u.z = pack_bf16x2(lo[8 * c + 4], lo[8 * c + 5]); u.w = pack_bf16x2(lo[8 * c + 6], lo[8 * c + 7]);
+        *reinterpret_cast<uint4 *>(wbuf + stage_off(lane, c)) = u;
+        u.x = pack_bf16x2(hi[8 * c + 0], hi[8 * c + 1]); u.y = pack_bf16x2(hi[8 * c + 2], hi[8 * c + 3]);
+        u.z = pack_bf16x2(hi[8 * c + 4], hi[8 * c + 5]); u.w = pack_bf16x2(hi[8 * c + 6], hi[8 * c + 7]);
+        *reinterpret_cast<uint4 *>(wbuf + stage_off(lane, 4 + c)) = u;
     }
 }
 
-DTTS_DEV void add_bias32(float (&v)[32], const float *bias, int n0) {
+DTTS_DEV void load_bias32(float (&v)[32], const float *bias, int n0) {
     if (!bias) return;
     const float4 *b4 = reinterpret_cast<const float4 *>(bias + n0);
 #pragma unroll
@@ -98,120 +126,74 @@ DTTS_DEV void add_bias32(float (&v)[32], const float *bias, int n0) {
     }
 }
 
-// One 32-column chunk for the non-QKV epilogues.  m < M is guaranteed.
-template <int EPI>
-DTTS_DEV void epilogue_chunk(const EpiParams &ep, int m, int n0, float (&v)[32]) {
-    add_bias32(v, ep.bias, n0);
-    if constexpr (EPI == EPI_BF16 || EPI == EPI_GELU_BF16 || EPI == EPI_SILU_BF16) {
-        if constexpr (EPI == EPI_GELU_BF16) {
+// Per-thread head transform for EPI_QKV: lo = head columns [0,32), hi = [32,64).
+DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&lo)[32], float (&hi)[32]) {
+    if (sect == 2) return;  // v: plain
+    if (ep.qk_norm) {
+        const float *g = sect == 0 ? ep.qn : ep.kn;
+        float ss = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = gelu_tanh_fast(v[i]);
+        for (int i = 0; i < 32; i++) ss += lo[i] * lo[i] + hi[i] * hi[i];
+        const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+#pragma unroll
+        for (int i = 0; i < 32; i++) { lo[i] *= inv; hi[i] *= inv; }
+        if (g) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) { lo[i] *= __ldg(g + i); hi[i] *= __ldg(g + 32 + i); }
         }
-        if constexpr (EPI == EPI_SILU_BF16) {
+    }
+    const int t = m % ep.tok_per_row;
+    const float4 *cs = reinterpret_cast<const float4 *>(ep.rope + (long long)(ep.kv_start + t) * 32);
+    if (ep.rope_mode == ROPE_HALF) {
+        // pairs (d, d + 32), frequency index d
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = silu_f(v[i]);
+        for (int i = 0; i < 16; i++) {
+            const float4 e = __ldg(cs + i);  // (cos_2i, sin_2i, cos_2i+1, sin_2i+1)
+            float x1 = lo[2 * i], x2 = hi[2 * i];
+            lo[2 * i] = x1 * e.x - x2 * e.y;
+            hi[2 * i] = x2 * e.x + x1 * e.y;
+            x1 = lo[2 * i + 1]; x2 = hi[2 * i + 1];
+            lo[2 * i + 1] = x1 * e.z - x2 * e.w;
+            hi[2 * i + 1] = x2 * e.z + x1 * e.w;
         }
-        store_bf16x32(reinterpret_cast<bf16 *>(ep.out) + (long long)m * ep.ldo + n0, v);
-    } else if constexpr (EPI == EPI_F32) {
-        float4 *d = reinterpret_cast<float4 *>(reinterpret_cast<float *>(ep.out) + (long long)m * ep.ldo + n0);
-#pragma unroll
-        for (int i = 0; i < 8; i++) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    } else if constexpr (EPI == EPI_RESID || EPI == EPI_RESID_GATED) {
-        float4 *r = reinterpret_cast<float4 *>(ep.resid + (long long)m * ep.ldr + n0);
-        const float4 *g4 = nullptr;
-        if constexpr (EPI == EPI_RESID_GATED)
-            g4 = reinterpret_cast<const float4 *>(ep.gate + (long long)(m / ep.tok_per_row) * ep.gate_ld + n0);
+    } else {
+        // adjacent pairs (2i, 2i + 1), frequency index i
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            float4 x = r[i];
-            if constexpr (EPI == EPI_RESID_GATED) {
-                float4 g = __ldg(g4 + i);
-                x.x += g.x * v[4 * i + 0]; x.y += g.y * v[4 * i + 1];
-                x.z += g.z * v[4 * i + 2]; x.w += g.w * v[4 * i + 3];
-            } else {
-                x.x += v[4 * i + 0]; x.y += v[4 * i + 1]; x.z += v[4 * i + 2]; x.w += v[4 * i + 3];
-            }
-            r[i] = x;
+            const float4 e = __ldg(cs + i);  // frequencies 2i, 2i+1
+            float x0 = lo[4 * i], x1 = lo[4 * i + 1];
+            lo[4 * i] = x0 * e.x - x1 * e.y;
+            lo[4 * i + 1] = x0 * e.y + x1 * e.x;
+            x0 = lo[4 * i + 2]; x1 = lo[4 * i + 3];
+            lo[4 * i + 2] = x0 * e.z - x1 * e.w;
+            lo[4 * i + 3] = x0 * e.w + x1 * e.z;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 e = __ldg(cs + 8 + i);  // frequencies 16 + 2i, 16 + 2i + 1
+            float x0 = hi[4 * i], x1 = hi[4 * i + 1];
+            hi[4 * i] = x0 * e.x - x1 * e.y;
+            hi[4 * i + 1] = x0 * e.y + x1 * e.x;
+            x0 = hi[4 * i + 2]; x1 = hi[4 * i + 3];
+            hi[4 * i + 2] = x0 * e.z - x1 * e.w;
+            hi[4 * i + 3] = x0 * e.w + x1 * e.z;
         }
     }
 }
 
-// One 64-column head for EPI_QKV: lo = columns [0,32), hi = [32,64).
-DTTS_DEV void epilogue_head(const EpiParams &ep, int m, int n0, float (&lo)[32], float (&hi)[32]) {
-    const int sect = n0 >> 10;          // 0 q, 1 k, 2 v
-    const int c = n0 & 1023;
-    const int t = m % ep.tok_per_row;
-    const int r = m / ep.tok_per_row;
-    if (sect < 2) {
-        if (ep.qk_norm) {
-            const float *g = sect == 0 ? ep.qn : ep.kn;
-            float ss = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; i++) ss += lo[i] * lo[i] + hi[i] * hi[i];
-            const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
-                lo[i] *= inv;
-                hi[i] *= inv;
-            }
-            if (g) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    lo[i] *= __ldg(g + i);
-                    hi[i] *= __ldg(g + 32 + i);
-                }
-            }
-        }
-        const float2 *cs = ep.rope + (long long)(ep.kv_start + t) * 32;
-        if (ep.rope_mode == ROPE_HALF) {
-            // pairs (d, d + 32), frequency index d
-#pragma unroll
-            for (int d = 0; d < 32; d++) {
-                float2 e = __ldg(cs + d);
-                float x1 = lo[d], x2 = hi[d];
-                lo[d] = x1 * e.x - x2 * e.y;
-                hi[d] = x2 * e.x + x1 * e.y;
-            }
-        } else {
-            // adjacent pairs (2i, 2i + 1), frequency index i
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                float2 e = __ldg(cs + i);
-                float x0 = lo[2 * i], x1 = lo[2 * i + 1];
-                lo[2 * i] = x0 * e.x - x1 * e.y;
-                lo[2 * i + 1] = x0 * e.y + x1 * e.x;
-            }
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                float2 e = __ldg(cs + 16 + i);
-                float x0 = hi[2 * i], x1 = hi[2 * i + 1];
-                hi[2 * i] = x0 * e.x - x1 * e.y;
-                hi[2 * i + 1] = x0 * e.y + x1 * e.x;
-            }
-        }
-    }
-    bf16 *dst;
-    if (sect == 0) {
-        dst = ep.q + (long long)m * ep.ldq + c;
-    } else {
-        long long row = (long long)r * ep.kv_cap + ep.kv_start + t;
-        dst = (sect == 1 ? ep.k : ep.v) + row * ep.ldkv + c;
-    }
-    store_bf16x32(dst, lo);
-    store_bf16x32(dst + 32, hi);
-}
-
-template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, EpiParams ep) {
-    using Cfg = GemmCfg<BN>;
+template <int BN, int EPI, int NW>
+__global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmR, int M, int N, int K, EpiParams ep) {
+    using Cfg = GemmCfg<BN, NW, EPI>;
     constexpr int STAGES = Cfg::STAGES;
+    constexpr int EPI_THREADS = NW * 32;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * Cfg::A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint8_t *sStage = smem + STAGES * Cfg::STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sStage + Cfg::STAGE_STAGING);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *tfull = bars + 2 * STAGES;
@@ -224,11 +206,13 @@ __global__ void __launch_bounds__(192, 1)
     const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
     const int num_n = N / BN;
     const int num_tiles = num_m * num_n;
-    const int kblocks = K / Cfg::BK;
+    const int ksplit = ep.ksplit > 0 ? ep.ksplit : 1;
+    const int num_units = num_tiles * ksplit;
+    const int kblocks = K / Cfg::BK / ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int a = 0; a < 2; a++) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
+        for (int a = 0; a < 2; a++) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], EPI_THREADS); }
         mbar_init(fin_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -249,13 +233,15 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int s = 0; s < STAGES; s++) last_par[s] = -1;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const int tile = u % num_tiles, split = u / num_tiles;
                 const int mb = tile % num_m, nb = tile / num_m;
+                const int kb0 = split * kblocks;
                 for (int kb = 0; kb < kblocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-                    tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
-                    tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * Cfg::BK, nb * BN);
+                    tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], (kb0 + kb) * Cfg::BK, mb * Cfg::BM);
+                    tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], (kb0 + kb) * Cfg::BK, nb * BN);
                     last_par[stage] = static_cast<int>(phase);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
@@ -280,7 +266,7 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             int it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, it++) {
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, it++) {
                 const int acc = it & 1;
                 const uint32_t acc_phase = (it >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, ep.err, DEVERR_TIMEOUT_MMA)) { ok = false; break; }
@@ -310,35 +296,135 @@ __global__ void __launch_bounds__(192, 1)
                 if (globaltimer_ns() - t0 > kWaitLimitNs) break;
         }
     } else {
-        // ---------------- epilogue (warps 2..5 -> TMEM lane quadrant warp % 4)
+        // ---------------- epilogue: warps 2.. ; TMEM lane quadrant = warp % 4,
+        // with 8 warps the two warps of a quadrant take alternate column chunks
+        const int ew = warp - 2;
         const int quad = warp & 3;
+        const int half = (NW == 8) ? (ew >> 2) : 0;
+        constexpr int CSTEP = (NW == 8) ? 2 : 1;
+        uint8_t *wbuf = sStage + ew * Cfg::STAGE_BUFS * 32 * 128;
+        int cc = 0;                   // chunks issued by this warp (staging buffer parity)
+        const int rsub = lane >> 3;   // row within a group of 4 (write-back phase)
+        const int chunk = lane & 7;   // 16-byte chunk of the 128-byte row segment
         int it = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, it++) {
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x, it++) {
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.err, DEVERR_TIMEOUT_EPILOGUE)) break;
             tc_fence_after();
+            const int tile = u % num_tiles, split = u / num_tiles;
             const int mb = tile % num_m, nb = tile / num_m;
-            const int m = mb * Cfg::BM + quad * 32 + lane;
+            const int m_base = mb * Cfg::BM + quad * 32;
             const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(quad * 32) << 16);
-            if constexpr (EPI == EPI_QKV) {
+            if constexpr (EPI == EPI_QKV || EPI == EPI_BF16 || EPI == EPI_GELU_BF16 || EPI == EPI_SILU_BF16) {
+                // 64 columns (one head / 128 bytes of bf16) per chunk
 #pragma unroll 1
-                for (int h = 0; h < BN / 64; h++) {
+                for (int c = half; c < BN / 64; c += CSTEP) {
+                    const int n0 = nb * BN + c * 64;
                     float lo[32], hi[32];
-                    tmem_ld32(tbase + h * 64, lo);
-                    tmem_ld32(tbase + h * 64 + 32, hi);
-                    if (m < M) epilogue_head(ep, m, nb * BN + h * 64, lo, hi);
+                    tmem_ld32(tbase + c * 64, lo);
+                    tmem_ld32(tbase + c * 64 + 32, hi);
+                    const int m_self = m_base + lane;
+                    if constexpr (EPI == EPI_QKV) {
+                        if (m_self < M) qkv_head_transform(ep, m_self, n0 >> 10, lo, hi);
+                    } else {
+                        load_bias32(lo, ep.bias, n0);
+                        load_bias32(hi, ep.bias, n0 + 32);
+                        if constexpr (EPI == EPI_GELU_BF16) {
+#pragma unroll
+                            for (int i = 0; i < 32; i++) { lo[i] = gelu_tanh_fast(lo[i]); hi[i] = gelu_tanh_fast(hi[i]); }
+                        }
+                        if constexpr (EPI == EPI_SILU_BF16) {
+#pragma unroll
+                            for (int i = 0; i < 32; i++) { lo[i] = silu_f(lo[i]); hi[i] = silu_f(hi[i]); }
+                        }
+                    }
+                    __syncwarp();
+                    stage_put_bf16(wbuf, lane, lo, hi);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r = rsub + 4 * i;
+                        const int m = m_base + r;
+                        const uint4 val = *reinterpret_cast<const uint4 *>(wbuf + stage_off(r, chunk));
+                        if (m >= M) continue;
+                        bf16 *dst;
+                        if constexpr (EPI == EPI_QKV) {
+                            const int sect = n0 >> 10, col = (n0 & 1023) + chunk * 8;
+                            if (sect == 0) {
+                                dst = ep.q + (long long)m * ep.ldq + col;
+                            } else {
+                                const long long row = (long long)(m / ep.tok_per_row) * ep.kv_cap + ep.kv_start +
+                                                      (m % ep.tok_per_row);
+                                dst = (sect == 1 ? ep.k : ep.v) + row * ep.ldkv + col;
+                            }
+                        } else {
+                            dst = reinterpret_cast<bf16 *>(ep.out) + (long long)m * ep.ldo + n0 + chunk * 8;
+                        }
+                        *reinterpret_cast<uint4 *>(dst) = val;
+                    }
                 }
-            } else {
+            } else if constexpr (EPI == EPI_F32) {
+                // fp32 results: 32 columns (128 bytes) per chunk
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; c++) {
+                for (int c = half; c < BN / 32; c += CSTEP) {
+                    const int n0 = nb * BN + c * 32;
                     float v[32];
                     tmem_ld32(tbase + c * 32, v);
-                    if (m < M) epilogue_chunk<EPI>(ep, m, nb * BN + c * 32, v);
+                    load_bias32(v, ep.bias, n0);
+                    __syncwarp();
+                    stage_put(wbuf, lane, v);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r = rsub + 4 * i;
+                        const int m = m_base + r;
+                        const float4 val = *reinterpret_cast<const float4 *>(wbuf + stage_off(r, chunk));
+                        if (m >= M) continue;
+                        *reinterpret_cast<float4 *>(reinterpret_cast<float *>(ep.out) + (long long)m * ep.ldo + n0 +
+                                                    chunk * 4) = val;
+                    }
+                }
+            } else {
+                // residual: stage gate * (acc + bias) and bulk-reduce it into the
+                // fp32 residual (32 rows x 32 columns per warp per chunk)
+                const int m_self = m_base + lane;
+                const float4 *g4 = nullptr;
+                if constexpr (EPI == EPI_RESID_GATED)
+                    if (m_self < M) g4 = reinterpret_cast<const float4 *>(ep.gate + (long long)(m_self / ep.tok_per_row) * ep.gate_ld);
+#pragma unroll 1
+                for (int c = half; c < BN / 32; c += CSTEP, cc++) {
+                    const int n0 = nb * BN + c * 32;
+                    float v[32];
+                    tmem_ld32(tbase + c * 32, v);
+                    if (split == 0) load_bias32(v, ep.bias, n0);
+                    if (m_self >= M) {
+#pragma unroll
+                        for (int i = 0; i < 32; i++) v[i] = 0.f;
+                    } else if constexpr (EPI == EPI_RESID_GATED) {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float4 g = __ldg(g4 + (n0 >> 2) + i);
+                            v[4 * i + 0] *= g.x; v[4 * i + 1] *= g.y; v[4 * i + 2] *= g.z; v[4 * i + 3] *= g.w;
+                        }
+                    }
+                    uint8_t *buf = wbuf + (cc & 1) * 32 * 128;
+                    if (lane == 0) bulk_wait_read<1>();   // the reduce that last read this buffer is done
+                    __syncwarp();
+                    stage_put(buf, lane, v);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && m_base < M) {
+                        tma_reduce_add_2d(&tmR, buf, n0, m_base);
+                        bulk_commit();
+                    }
                 }
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+        }
+        if constexpr (is_resid(EPI)) {
+            if (lane == 0) bulk_wait<0>();   // every reduce of this warp has landed
         }
     }
 

@@ -481,56 +481,54 @@ void launch_history_rows(const float *src, int n_seq, int src_len, bf16 *dst, in
 // =========================================================================
 // conditioning
 // =========================================================================
-// y[o] = act(W[o] . x + b[o]); one warp per output, lanes split the input.
+// y[k][o] = act(W[o] . x[k] + b[o]) for nx input vectors; one warp per output
+// row o (the row is read once, coalesced, for all nx inputs).
 template <int IN, bool SILU>
-__global__ void __launch_bounds__(256) warp_gemv_kernel(const float *__restrict__ x, const float *__restrict__ w,
-                                                        const float *__restrict__ b, float *__restrict__ y, int out) {
+__global__ void __launch_bounds__(256) warp_gemv_kernel(const float *__restrict__ x, int nx,
+                                                        const float *__restrict__ w, const float *__restrict__ b,
+                                                        float *__restrict__ y, int out) {
+    constexpr int PER = IN / 32;
     const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (o >= out) return;
-    const float *wr = w + (long long)o * IN;
-    float s = 0.f;
-#pragma unroll 4
-    for (int i = lane; i < IN; i += 32) s += wr[i] * x[i];
-    s = warp_sum(s);
-    if (lane == 0) {
-        float v = s + (b ? b[o] : 0.f);
-        if (SILU) v = v / (1.0f + expf(-v));
-        y[o] = v;
+    float wr[PER];
+    const float *wrow = w + (long long)o * IN;
+#pragma unroll
+    for (int j = 0; j < PER; j++) wr[j] = wrow[lane + 32 * j];
+    for (int k = 0; k < nx; k++) {
+        const float *xk = x + (long long)k * IN;
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) s += wr[j] * xk[lane + 32 * j];
+        s = warp_sum(s);
+        if (lane == 0) {
+            float v = s + (b ? b[o] : 0.f);
+            if (SILU) v = v / (1.0f + expf(-v));
+            y[(long long)k * out + o] = v;
+        }
     }
 }
 
-void launch_time_mlp(const float *se, const float *w1, const float *b1, const float *w2, const float *b2,
+void launch_time_mlp(const float *se, int n, const float *w1, const float *b1, const float *w2, const float *b2,
                      float *h1_scratch, float *temb, cudaStream_t s) {
-    warp_gemv_kernel<256, true><<<kD / 8, 256, 0, s>>>(se, w1, b1, h1_scratch, kD);
-    warp_gemv_kernel<kD, false><<<kD / 8, 256, 0, s>>>(h1_scratch, w2, b2, temb, kD);
+    warp_gemv_kernel<256, true><<<kD / 8, 256, 0, s>>>(se, n, w1, b1, h1_scratch, kD);
+    warp_gemv_kernel<kD, false><<<kD / 8, 256, 0, s>>>(h1_scratch, n, w2, b2, temb, kD);
 }
 
-__global__ void __launch_bounds__(1024) speaker_cond_kernel(const float *__restrict__ spk, const float *__restrict__ w,
-                                                            const float *__restrict__ b, const float *__restrict__ lw,
-                                                            const float *__restrict__ lb, float scale,
-                                                            float *__restrict__ out) {
-    __shared__ float xs[kSpk];
+// LayerNorm (affine, eps 1e-5) of y[u] in place, times scale: one block per row.
+__global__ void __launch_bounds__(1024) speaker_ln_kernel(float *__restrict__ y, const float *__restrict__ lw,
+                                                          const float *__restrict__ lb, float scale) {
     __shared__ float red[32];
     const int u = blockIdx.x, o = threadIdx.x;
-    for (int i = threadIdx.x; i < kSpk; i += blockDim.x) xs[i] = spk[(long long)u * kSpk + i];
-    __syncthreads();
-    float y = b ? b[o] : 0.f;
-    {
-        const float *wr = w + (long long)o * kSpk;
-        float s = 0.f;
-        for (int i = 0; i < kSpk; i++) s += wr[i] * xs[i];
-        y += s;
-    }
-    // block mean / variance over 1024 outputs
-    float v = warp_sum(y);
+    const float v0 = y[(long long)u * kD + o];
+    float v = warp_sum(v0);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     float mean = 0.f;
     for (int i = 0; i < 32; i++) mean += red[i];
     mean /= kD;
     __syncthreads();
-    const float d = y - mean;
+    const float d = v0 - mean;
     v = warp_sum(d * d);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
@@ -540,95 +538,116 @@ __global__ void __launch_bounds__(1024) speaker_cond_kernel(const float *__restr
     float xo = d * istd;
     if (lw) xo *= lw[o];
     if (lb) xo += lb[o];
-    out[(long long)u * kD + o] = xo * scale;
+    y[(long long)u * kD + o] = xo * scale;
 }
 
 void launch_speaker_cond(const float *spk, int n_utt, const float *w, const float *b, const float *ln_w,
                          const float *ln_b, float scale, float *spk_c, cudaStream_t s) {
-    speaker_cond_kernel<<<n_utt, kD, 0, s>>>(spk, w, b, ln_w, ln_b, scale, spk_c);
+    warp_gemv_kernel<kSpk, false><<<kD / 8, 256, 0, s>>>(spk, n_utt, w, b, spk_c, kD);
+    speaker_ln_kernel<<<n_utt, kD, 0, s>>>(spk_c, ln_w, ln_b, scale);
 }
 
-__global__ void cond_rows_kernel(const float *__restrict__ temb, const float *__restrict__ spk_c, int rows,
-                                 int rows_per_utt, bf16 *__restrict__ a) {
+// a[k*n + u][c] = bf16(SiLU(temb[k][c] + spk_c[u][c]))
+__global__ void cond_rows_kernel(const float *__restrict__ temb, int n_t, const float *__restrict__ spk_c, int n,
+                                 bf16 *__restrict__ a) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)rows * kD) return;
-    const int r = (int)(i / kD), c = (int)(i % kD);
-    float v = temb[c];
-    if (spk_c) v += spk_c[(long long)(r / rows_per_utt) * kD + c];
+    if (i >= (long long)n_t * n * kD) return;
+    const long long row = i / kD;
+    const int c = (int)(i % kD);
+    const int k = (int)(row / n), u = (int)(row % n);
+    float v = temb[(long long)k * kD + c];
+    if (spk_c) v += spk_c[(long long)u * kD + c];
     a[i] = __float2bfloat16_rn(v / (1.0f + expf(-v)));
 }
 
-void launch_cond_rows(const float *temb, const float *spk_c, int rows, int rows_per_utt, bf16 *a_cond,
-                      cudaStream_t s) {
-    const long long n = (long long)rows * kD;
-    cond_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(temb, spk_c, rows, rows_per_utt, a_cond);
+void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf16 *a_cond, cudaStream_t s) {
+    const long long tot = (long long)n_t * n * kD;
+    cond_rows_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(temb, n_t, spk_c, n, a_cond);
 }
 
 // =========================================================================
-// DiT output head
+// DiT output head: 8 tokens per block.  LN + modulation of the 8 token rows
+// into shared memory, then 128 outputs, each warp owning 16 output rows of
+// W_out (read once, coalesced) against the 8 tokens.
 // =========================================================================
-__global__ void __launch_bounds__(256) out_head_kernel(const float *__restrict__ h, int L, int P,
+constexpr int kOutTok = 8;
+
+__global__ void __launch_bounds__(256) out_head_kernel(const float *__restrict__ h, int rows, int L, int P,
                                                        const float *__restrict__ shift,
                                                        const float *__restrict__ scale, long long ada_ld,
-                                                       const float *__restrict__ w, const float *__restrict__ b,
-                                                       float *__restrict__ vel, int *err) {
-    __shared__ float u[kD];
-    __shared__ float red[8];
-    const int r = blockIdx.x / P, p = blockIdx.x % P;
-    const int tok = L - P + p;
-    const float *x = h + ((long long)r * L + tok) * kD;
+                                                       int rows_per_ada, const float *__restrict__ w,
+                                                       const float *__restrict__ b, float *__restrict__ vel,
+                                                       int *err) {
+    __shared__ float u[kOutTok][kD];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float v[4];
-    float s = 0.f;
+    const int tok0 = blockIdx.x * kOutTok;
+    const int ntok = rows * P;
+    // each warp normalises one token row
+    {
+        const int tk = tok0 + warp;
+        if (tk < ntok) {
+            const int r = tk / P, p = tk % P;
+            const float4 *x = reinterpret_cast<const float4 *>(h + ((long long)r * L + (L - P + p)) * kD);
+            float4 v[8];
+            float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; j++) { v[j] = x[threadIdx.x + 256 * j]; s += v[j]; }
-    s = warp_sum(s);
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    float mean = 0.f;
+            for (int j = 0; j < 8; j++) { v[j] = x[lane + 32 * j]; sum += (v[j].x + v[j].y) + (v[j].z + v[j].w); }
+            const float mean = warp_sum(sum) * (1.0f / kD);
+            float q = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; i++) mean += red[i];
-    mean *= (1.0f / kD);
-    __syncthreads();
-    float q = 0.f;
+            for (int j = 0; j < 8; j++) {
+                const float a0 = v[j].x - mean, a1 = v[j].y - mean, a2 = v[j].z - mean, a3 = v[j].w - mean;
+                q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+            }
+            const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
+            const long long ar = (long long)(r / rows_per_ada) * ada_ld;
+            const float4 *sh = reinterpret_cast<const float4 *>(shift + ar);
+            const float4 *sc = reinterpret_cast<const float4 *>(scale + ar);
 #pragma unroll
-    for (int j = 0; j < 4; j++) { const float d = v[j] - mean; q += d * d; }
-    q = warp_sum(q);
-    if (lane == 0) red[warp] = q;
-    __syncthreads();
-    float var = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) var += red[i];
-    const float inv = 1.0f / sqrtf(var * (1.0f / kD) + 1e-5f);
-    const float *sh = shift + (long long)r * ada_ld;
-    const float *sc = scale + (long long)r * ada_ld;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int c = threadIdx.x + 256 * j;
-        u[c] = (v[j] - mean) * inv * (1.0f + sc[c]) + sh[c];
+            for (int j = 0; j < 8; j++) {
+                const int c4 = lane + 32 * j;
+                const float4 a = __ldg(sh + c4), g = __ldg(sc + c4);
+                u[warp][4 * c4 + 0] = (v[j].x - mean) * inv * (1.0f + g.x) + a.x;
+                u[warp][4 * c4 + 1] = (v[j].y - mean) * inv * (1.0f + g.y) + a.y;
+                u[warp][4 * c4 + 2] = (v[j].z - mean) * inv * (1.0f + g.z) + a.z;
+                u[warp][4 * c4 + 3] = (v[j].w - mean) * inv * (1.0f + g.w) + a.w;
+            }
+        }
     }
     __syncthreads();
-    // 128 outputs, 16 per warp; lanes split the 1024 inputs
     for (int oo = 0; oo < kLat / 8; oo++) {
         const int o = warp * (kLat / 8) + oo;
         const float *wr = w + (long long)o * kD;
-        float acc = 0.f;
-#pragma unroll 8
-        for (int i = lane; i < kD; i += 32) acc += wr[i] * u[i];
-        acc = warp_sum(acc);
-        if (lane == 0) {
-            const float y = acc + (b ? b[o] : 0.f);
+        float acc[kOutTok] = {};
+#pragma unroll 4
+        for (int i = lane; i < kD; i += 32) {
+            const float wv = wr[i];
+#pragma unroll
+            for (int t = 0; t < kOutTok; t++) acc[t] += wv * u[t][i];
+        }
+#pragma unroll
+        for (int t = 0; t < kOutTok; t++) acc[t] = warp_sum(acc[t]);
+        if (lane < kOutTok && tok0 + lane < ntok) {
+            float y = 0.f;
+#pragma unroll
+            for (int t = 0; t < kOutTok; t++) y = (lane == t) ? acc[t] : y;
+            y += b ? b[o] : 0.f;
             if (!isfinite(y) && err) atomicCAS(err, 0, DEVERR_NONFINITE);
-            vel[((long long)r * P + p) * kLat + o] = y;
+            vel[(long long)(tok0 + lane) * kLat + o] = y;
         }
     }
 }
 
 void launch_out_head(const float *h, int rows, int L, int P, const float *shift, const float *scale,
-                     long long ada_ld, const float *w_out, const float *b_out, float *vel, int *err, cudaStream_t s) {
-    out_head_kernel<<<rows * P, 256, 0, s>>>(h, L, P, shift, scale, ada_ld, w_out, b_out, vel, err);
+                     long long ada_ld, int rows_per_ada, const float *w_out, const float *b_out, float *vel, int *err,
+                     cudaStream_t s) {
+    const int ntok = rows * P;
+    out_head_kernel<<<(ntok + kOutTok - 1) / kOutTok, 256, 0, s>>>(h, rows, L, P, shift, scale, ada_ld, rows_per_ada,
+                                                                   w_out, b_out, vel, err);
 }
 
+// CFG combine + Euler update + coordinate projection, one block per
+// (utterance, frame): 8 warps x 128 outputs, lanes split the 128 inputs.
 __global__ void __launch_bounds__(256) cfg_euler_kernel(const float *__restrict__ vel, float *__restrict__ z, int P,
                                                         float cfg_scale, int cfg_form, float dt, int update,
                                                         const float *__restrict__ wc, const float *__restrict__ bc,
@@ -648,17 +667,20 @@ __global__ void __launch_bounds__(256) cfg_euler_kernel(const float *__restrict_
         zs[threadIdx.x] = zv;
     }
     __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float z0 = zs[lane], z1 = zs[lane + 32], z2 = zs[lane + 64], z3 = zs[lane + 96];
     const long long tok = L - P + p;
     bf16 *xc = x_in + ((long long)(2 * u) * L + tok) * kD;
     bf16 *xu = x_in + ((long long)(2 * u + 1) * L + tok) * kD;
-    for (int o = threadIdx.x; o < kD; o += blockDim.x) {
+    for (int o = warp; o < kD; o += 8) {
         const float *wr = wc + (long long)o * kLat;
-        float acc = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < kLat; i++) acc += wr[i] * zs[i];
-        const bf16 y = __float2bfloat16_rn(acc + (bc ? bc[o] : 0.f));
-        xc[o] = y;
-        xu[o] = y;
+        float acc = wr[lane] * z0 + wr[lane + 32] * z1 + wr[lane + 64] * z2 + wr[lane + 96] * z3;
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            const bf16 y = __float2bfloat16_rn(acc + (bc ? bc[o] : 0.f));
+            xc[o] = y;
+            xu[o] = y;
+        }
     }
 }
 

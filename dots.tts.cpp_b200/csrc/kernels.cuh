@@ -10,8 +10,10 @@ constexpr int kD = 1024, kH = 16, kHD = 64, kF = 4096, kLat = 128, kLLM = 1536, 
 // ------------------------------------------------------------ GEMM (tcgen05)
 struct GemmOp {
     CUtensorMap ta, tb;
+    CUtensorMap tr;   // residual (EPI_RESID*), from make_tmap_f32_resid
     int M, N, K;
-    int bn;       // 128 or 256
+    int bn;       // 128, 192 or 256
+    int nw;       // epilogue warps: 4 or 8
     int epi;      // EpiKind
     EpiParams ep;
 };
@@ -19,6 +21,8 @@ struct GemmOp {
 // with 128-byte swizzle.
 bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
                     unsigned int box_rows);
+// The fp32 residual [rows][cols] as the target of the epilogue's bulk reduce-add.
+bool make_tmap_f32_resid(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols);
 cudaError_t launch_gemm(const GemmOp &op, int num_sms, cudaStream_t s);
 cudaError_t gemm_prepare_attributes();
 
@@ -63,20 +67,21 @@ void launch_history_rows(const float *src, int n_seq, int src_len, bf16 *dst, in
                          cudaStream_t s);
 
 // ------------------------------------------------------------ conditioning
-// temb = W2 SiLU(W1 se + b1) + b2 (se: 256-entry sinusoid computed on the host)
-void launch_time_mlp(const float *se, const float *w1, const float *b1, const float *w2, const float *b2,
+// temb[k] = W2 SiLU(W1 se[k] + b1) + b2 for n sinusoids se[k] (256 entries,
+// computed on the host); h1_scratch holds n x 1024.
+void launch_time_mlp(const float *se, int n, const float *w1, const float *b1, const float *w2, const float *b2,
                      float *h1_scratch, float *temb, cudaStream_t s);
 // spk_c[u] = scale * LN_affine(Wx spk[u] + bx), eps 1e-5
 void launch_speaker_cond(const float *spk, int n_utt, const float *w, const float *b, const float *ln_w,
                          const float *ln_b, float scale, float *spk_c, cudaStream_t s);
-// a_cond[r] = bf16(SiLU(temb + spk_c[r / rows_per_utt]))  (spk_c may be null)
-void launch_cond_rows(const float *temb, const float *spk_c, int rows, int rows_per_utt, bf16 *a_cond,
-                      cudaStream_t s);
+// a_cond[k*n + u] = bf16(SiLU(temb[k] + spk_c[u])) for k < n_t, u < n  (spk_c may be null)
+void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf16 *a_cond, cudaStream_t s);
 
 // ------------------------------------------------------------ DiT output head
-// vel[r][p] = W_out (LN(h[r, L-P+p]) (1 + scale_r) + shift_r) + b_out
+// vel[r][p] = W_out (LN(h[r, L-P+p]) (1 + scale) + shift) + b_out, with the
+// modulation of row r at shift/scale + (r / rows_per_ada) * ada_ld
 void launch_out_head(const float *h, int rows, int L, int P, const float *shift, const float *scale,
-                     long long ada_ld, const float *w_out, const float *b_out, float *vel, int *err,
+                     long long ada_ld, int rows_per_ada, const float *w_out, const float *b_out, float *vel, int *err,
                      cudaStream_t s);
 // CFG combine + Euler update + coord_proj of the new z into the noise tokens of
 // both rows of each utterance (update = 0: only the coord_proj of z).

@@ -77,7 +77,7 @@ struct dtts_pe {
     long long cap_tok = 0;
     float *frames = nullptr, *h = nullptr, *outf = nullptr;
     bf16 *conv = nullptr, *act = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *pairs = nullptr;
-    CUtensorMap t_conv, t_act, t_att, t_ffn, t_pairs;
+    CUtensorMap t_conv, t_act, t_att, t_ffn, t_pairs, t_h;
     int launches = 0;
 
     ~dtts_pe() {
@@ -106,7 +106,8 @@ struct dtts_pe {
             if (!p) { ws.free_all(); cap_tok = 0; set_error("workspace allocation failed"); return DTTS_ERR_OOM; }
         bool ok = make_tmap_bf16(&t_conv, conv, T, kLat, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
                   make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
-                  make_tmap_bf16(&t_pairs, pairs, T / 2 > 0 ? T / 2 : 1, 2 * kD, 128);
+                  make_tmap_bf16(&t_pairs, pairs, T / 2 > 0 ? T / 2 : 1, 2 * kD, 128) &&
+                  make_tmap_f32_resid(&t_h, h, T, kD);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder workspace)");
         return DTTS_OK;
     }
@@ -153,6 +154,7 @@ struct dtts_pe {
             }
             {
                 GemmOp op = op0(t_att, Ly.to, M, kD, kD, EPI_RESID, d_err);
+                op.tr = t_h;
                 op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
             }
@@ -165,6 +167,7 @@ struct dtts_pe {
             }
             {
                 GemmOp op = op0(t_ffn, Ly.t2, M, kD, kF, EPI_RESID, d_err);
+                op.tr = t_h;
                 op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
             }

@@ -100,7 +100,7 @@ EXPORTS = [
     "dtts_version", "dtts_status_string", "dtts_last_error", "dtts_device_count",
     "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
     "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_euler_solve", "dtts_dit_profile_kernel",
-    "dtts_dit_last_launch_count", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
+    "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
     "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_st_open",
@@ -150,6 +150,7 @@ def lib(path: str = LIB_PATH):
     L.dtts_dit_profile_kernel.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double),
                                           C.POINTER(C.c_double)]
     L.dtts_dit_last_launch_count.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_dit_tune.argtypes = [_vp, C.c_char_p, C.c_int, C.c_int, C.c_int]
     L.dtts_attn_create.argtypes = [C.POINTER(AttnW), C.c_int, C.c_int, C.POINTER(_vp)]
     L.dtts_attn_destroy.argtypes = [_vp]
     L.dtts_attn_forward.argtypes = [_vp, _fp, C.c_int, C.c_int, _u8p, _fp, _fp]
@@ -312,6 +313,9 @@ class DiT:
         us, fl, by = C.c_float(), C.c_double(), C.c_double()
         check(lib().dtts_dit_profile_kernel(self.h, kind, iters, C.byref(us), C.byref(fl), C.byref(by)))
         return us.value, fl.value, by.value
+
+    def tune(self, gemm, bn, epi_warps=4, ksplit=1):
+        check(lib().dtts_dit_tune(self.h, gemm.encode(), bn, epi_warps, ksplit))
 
     def last_launch_count(self):
         n = C.c_int()

@@ -174,6 +174,11 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a);
  * Reports the mean device time of one launch and its algorithmic FLOPs and
  * bytes (operands read once, results written once). */
 int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us_per_launch, double *flops, double *bytes);
+/* Tile configuration of one GEMM of the block stack ("qkv", "o", "ffn1",
+ * "ffn2", "adaln", "input"): tile width bn (128/192/256, dividing N),
+ * epi_warps (4/8) epilogue warps, ksplit (1/2/4/8, residual GEMMs only).
+ * Results are identical up to fp32 summation order; defaults are tuned for B200. */
+int dtts_dit_tune(dtts_dit *e, const char *gemm, int bn, int epi_warps, int ksplit);
 /* Kernel launches enqueued by the last solve / velocity call (all engine kernels). */
 int dtts_dit_last_launch_count(dtts_dit *e, int *n);
 
