@@ -177,7 +177,9 @@ int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us_per_laun
 /* Tile configuration of one GEMM of the block stack ("qkv", "o", "ffn1",
  * "ffn2", "adaln", "input"): tile width bn (128/192/256, dividing N),
  * epi_warps (4/8) epilogue warps, ksplit (1/2/4/8, residual GEMMs only).
- * Results are identical up to fp32 summation order; defaults are tuned for B200. */
+ * Results are identical up to fp32 summation order; with ksplit > 1 the
+ * partial sums reach the residual in run-dependent order, so repeated runs
+ * may differ in the last bits.  Defaults (ksplit 1) are tuned for B200. */
 int dtts_dit_tune(dtts_dit *e, const char *gemm, int bn, int epi_warps, int ksplit);
 /* Kernel launches enqueued by the last solve / velocity call (all engine kernels). */
 int dtts_dit_last_launch_count(dtts_dit *e, int *n);
@@ -190,7 +192,6 @@ int dtts_attn_forward(dtts_attn *a, const float *x, int rows, int L, const uint8
                       float *out);
 /* mean device time (us) of the attention core kernel (post-QKV, pre-O) of the last forward */
 int dtts_attn_profile_core(dtts_attn *a, int iters, float *us_per_launch);
-
 /* ------------------------------------------------------------------ PatchEncoder */
 /* max_batch sequences, each with a KV cache of max_tokens tokens (2 per patch). */
 int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batch, int max_tokens, dtts_pe **out);
