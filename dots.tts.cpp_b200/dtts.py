@@ -101,7 +101,7 @@ EXPORTS = [
     "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
     "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_euler_solve", "dtts_dit_profile_kernel",
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
-    "dtts_attn_profile_core", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
+    "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
     "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_st_open",
     "dtts_st_close", "dtts_st_count", "dtts_st_shape", "dtts_st_read_f32",
@@ -155,6 +155,7 @@ def lib(path: str = LIB_PATH):
     L.dtts_attn_destroy.argtypes = [_vp]
     L.dtts_attn_forward.argtypes = [_vp, _fp, C.c_int, C.c_int, _u8p, _fp, _fp]
     L.dtts_attn_profile_core.argtypes = [_vp, C.c_int, C.POINTER(C.c_float)]
+    L.dtts_attn_forward_f32_noalloc.argtypes = [_vp] * 10 + [C.c_int, C.c_int, _vp, _vp]
     L.dtts_pe_create.argtypes = [C.POINTER(PeW), C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
     L.dtts_pe_create_from_safetensors.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                                   C.POINTER(_vp)]

@@ -192,6 +192,27 @@ int dtts_attn_forward(dtts_attn *a, const float *x, int rows, int L, const uint8
                       float *out);
 /* mean device time (us) of the attention core kernel (post-QKV, pre-O) of the last forward */
 int dtts_attn_profile_core(dtts_attn *a, int iters, float *us_per_launch);
+
+/* fp32 attention sublayer that performs no device allocation (no counterpart
+ * in the reference).  For callers that may not allocate GPU memory while they
+ * run -- a host that gives the library a fixed memory budget, a plugin whose
+ * runtime forbids allocation during execution, a real-time audio thread where
+ * an allocation could block -- every argument is a device pointer the caller
+ * owns (x, out [rows][L][1024]; weights as in dtts_attn_weights; mask [L][L]
+ * and pos [L] or NULL) and the intermediates live in one fixed array compiled
+ * into the library (4.06 MiB, held by every GPU that loads it until exit).
+ * Limits: rows * L <= DTTS_NOALLOC_MAX_TOKENS and L <= 256; larger shapes
+ * return DTTS_ERR_ARG.  Work is enqueued on `cuda_stream` (NULL: the default
+ * stream) on the current device; the call returns without waiting.  The first
+ * call on a device looks up the array's address and sets a kernel attribute,
+ * so make that first call before any stream capture.  All calls on a device
+ * share the array: calls whose work overlaps on the GPU race and must be
+ * serialised by the caller.  Nothing in the array needs to start at zero. */
+#define DTTS_NOALLOC_MAX_TOKENS 256
+int dtts_attn_forward_f32_noalloc(const float *x, const float *wq, const float *wk, const float *wv, const float *wo,
+                                  const float *bo, const float *qn, const float *kn, const uint8_t *mask,
+                                  const float *pos, int rows, int L, float *out, void *cuda_stream);
+
 /* ------------------------------------------------------------------ PatchEncoder */
 /* max_batch sequences, each with a KV cache of max_tokens tokens (2 per patch). */
 int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batch, int max_tokens, dtts_pe **out);
