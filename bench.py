@@ -42,7 +42,7 @@ UNIT = "evals/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--n-utt", type=int, default=64, help="utterances per GPU")
@@ -148,6 +148,10 @@ def cpu_reference_eval(args, w, fc, fu, z0, spk, ffn_mode):
     sys.path.insert(0, os.path.join(HERE, "oracle"))
     import oracle as O
     orc, ref = O.Oracle(), O.Reference()
+    # all host threads (torch.distributed.run sets OMP_NUM_THREADS=1 per process)
+    ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    orc.set_threads(ncpu)
+    ref.set_threads(ncpu)
     L = args.fm_len + args.patch
     mask = orc.fm_mask(L, args.fm_len, args.patch)
     pos = orc.fm_pos(L, args.fm_len, args.patch)
@@ -174,7 +178,6 @@ def run_reference(args, rank, world):
     if not O.Reference.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdtts_ref.so was not built"}))
         return
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
     w, fc, fu, z0, spk = make_inputs(args, 0)
     for _ in range(args.warmup):
         cpu_reference_eval(args, w, fc, fu, z0, spk, O.FFN_AS_WRITTEN)
@@ -319,7 +322,6 @@ def run_ours(args, rank, world, local_rank):
         sys.path.insert(0, os.path.join(HERE, "oracle"))
         import oracle as O
         if O.Reference.available():
-            os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
             secs, cores = cpu_reference_eval(args, w, fc, fu, z0, spk, O.FFN_PER_TOKEN)
             cpu = {"value": 1.0 / secs, "unit": UNIT, "cores": cores, "kind": "reference",
                    "sample": "one CFG-pair eval (2 rows, L=%d, %d layers) through the reference's "

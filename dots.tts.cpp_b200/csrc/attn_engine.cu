@@ -27,6 +27,7 @@ struct dtts_attn {
     bf16 *x16 = nullptr, *q16 = nullptr, *k16 = nullptr, *v16 = nullptr, *ctx16 = nullptr;
     float2 *rope = nullptr;
     uint8_t *mask = nullptr;
+    uint32_t *mask_bits = nullptr;
     CUtensorMap t_x16, t_ctx16;
     // last shapes
     int last_rows = 0, last_L = 0;
@@ -50,6 +51,7 @@ struct dtts_attn {
         out = (float *)ws.alloc(T * kD * 4);
         rope = (float2 *)ws.alloc((size_t)cap_L * 32 * sizeof(float2));
         mask = (uint8_t *)ws.alloc((size_t)cap_L * cap_L);
+        mask_bits = (uint32_t *)ws.alloc((size_t)cap_L * ((cap_L + 31) / 32) * 4);
         if (dtype == DTTS_DTYPE_F32) {
             qf = (float *)ws.alloc(T * kD * 4);
             kf = (float *)ws.alloc(T * kD * 4);
@@ -72,9 +74,10 @@ struct dtts_attn {
     }
 
     void enqueue_core(int rows, int L) {
-        AttnArgs a;
+        AttnArgs a{};
         a.rows = rows; a.Tq = L; a.kv_len = L; a.kv_cap = L; a.q_pos0 = 0; a.causal = 0;
         a.mask = last_mask ? mask : nullptr;
+        a.mask_bits = last_mask ? mask_bits : nullptr;
         a.scale = 1.0f / sqrtf(64.0f);
         a.ldq = a.ldkv = a.ldo = kD;
         if (dtype == DTTS_DTYPE_F32) {
@@ -149,6 +152,7 @@ int dtts_attn_create(const dtts_attn_weights *w, int dtype, int device, dtts_att
         if ((st = up_f32(a->wts, w->wo, (size_t)kD * kD, &a->wo))) return st;
     } else {
         DTTS_CUDA(gemm_prepare_attributes());
+        DTTS_CUDA(attention_short_prepare());
         if ((st = up_bf16(a->wts, {w->wq, w->wk, w->wv}, kD, kD, &a->wqkv16))) return st;
         if ((st = up_bf16(a->wts, {w->wo}, kD, kD, &a->wo16))) return st;
         bool ok = make_tmap_bf16(&a->t_wqkv, a->wqkv16, 3 * kD, kD, 256) && make_tmap_bf16(&a->t_wo, a->wo16, kD, kD, 256);
@@ -180,7 +184,13 @@ int dtts_attn_forward(dtts_attn *a, const float *x, int rows, int L, const uint8
     rope_half(pos, L, rt);
     DTTS_CUDA(cudaMemcpyAsync(a->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
     a->last_mask = mask != nullptr;
-    if (mask) DTTS_CUDA(cudaMemcpyAsync(a->mask, mask, (size_t)L * L, cudaMemcpyHostToDevice, s));
+    std::vector<uint32_t> bits;
+    if (mask) {
+        bits.resize((size_t)L * ((L + 31) / 32));
+        pack_mask_bits(mask, L, L, bits.data());
+        DTTS_CUDA(cudaMemcpyAsync(a->mask, mask, (size_t)L * L, cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaMemcpyAsync(a->mask_bits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice, s));
+    }
     DTTS_CUDA(cudaMemcpyAsync(a->x, x, (size_t)M * kD * 4, cudaMemcpyHostToDevice, s));
     if (a->dtype == DTTS_DTYPE_F32) {
         launch_gemm_f32(a->x, a->wq, nullptr, a->qf, M, kD, kD, s);

@@ -170,6 +170,7 @@ struct dtts_dit {
           *spk_in = nullptr;
     float2 *rope = nullptr;
     uint8_t *mask = nullptr;
+    uint32_t *mask_bits = nullptr;   // [L][ceil(L/32)]
     CUtensorMap t_x_in, t_act, t_att, t_ffn, t_acond, t_h;
 
     // shapes of the last forward (for profiling) and launch accounting
@@ -240,6 +241,7 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
     se_tab = (float *)A((size_t)cap_nfe * 256 * 4);
     rope = (float2 *)A((size_t)cap_L * 32 * sizeof(float2));
     mask = (uint8_t *)A((size_t)cap_L * cap_L);
+    mask_bits = (uint32_t *)A((size_t)cap_L * ((cap_L + 31) / 32) * 4);
     for (void *p : ws.ptrs)
         if (!p) { set_error("workspace allocation failed (%lld tokens)", tok); cap_tok = cap_rows = cap_L = 0; ws.free_all(); return DTTS_ERR_OOM; }
     bool ok = make_tmap_bf16(&t_x_in, x_in, T, kD, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
@@ -288,10 +290,11 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             return gemm(op);
         }
         case 4: {
-            AttnArgs a;
+            AttnArgs a{};
             a.q = q; a.ldq = kD; a.k = k; a.v = v; a.ldkv = kD; a.o = att; a.ldo = kD;
             a.rows = rows; a.Tq = L; a.kv_len = L; a.kv_cap = L; a.q_pos0 = 0; a.causal = 0;
             a.mask = last_mask ? mask : nullptr;
+            a.mask_bits = last_mask ? mask_bits : nullptr;
             a.scale = 1.0f / sqrtf(64.0f);
             launches++;
             launch_attention_bf16(a, stream);
@@ -424,6 +427,7 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     DTTS_CUDA(cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking));
     e->stream = e->own_stream;
     DTTS_CUDA(gemm_prepare_attributes());
+    DTTS_CUDA(attention_short_prepare());
     cudaStream_t s = e->stream;
     e->d_err = (int *)e->wts.alloc(sizeof(int));
     DTTS_CHECK(e->d_err, DTTS_ERR_OOM, "cudaMalloc failed");
@@ -527,7 +531,16 @@ int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const u
     }
     DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
     e->last_mask = mask != nullptr;
-    if (mask) DTTS_CUDA(cudaMemcpyAsync(e->mask, mask, (size_t)L * L, in_kind, s));
+    std::vector<uint32_t> bits;
+    if (mask) {
+        std::vector<uint8_t> hm((size_t)L * L);
+        DTTS_CUDA(cudaMemcpy(hm.data(), mask, hm.size(), mem == DTTS_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToHost));
+        bits.resize((size_t)L * ((L + 31) / 32));
+        pack_mask_bits(hm.data(), L, L, bits.data());
+        DTTS_CUDA(cudaMemcpyAsync(e->mask, hm.data(), hm.size(), cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaMemcpyAsync(e->mask_bits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaStreamSynchronize(s));   // host copies go out of scope
+    }
     e->launches += 2;
     launch_f32_to_bf16(e->in_a, e->x_in, (long long)ntok * kD, s);
     launch_silu_bf16(e->cond_f32, e->a_cond, (long long)rows * kD, s);
@@ -592,7 +605,13 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
         for (int k = 0; k < a->nfe; k++) sinusoid((float)k * dt, &se[(size_t)k * 256]);
         DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
         DTTS_CUDA(cudaMemcpyAsync(e->se_tab, se.data(), se.size() * 4, cudaMemcpyHostToDevice, s));
-        if (!m.empty()) DTTS_CUDA(cudaMemcpyAsync(e->mask, m.data(), m.size(), cudaMemcpyHostToDevice, s));
+        std::vector<uint32_t> bits;
+        if (!m.empty()) {
+            bits.resize((size_t)L * ((L + 31) / 32));
+            pack_mask_bits(m.data(), L, L, bits.data());
+            DTTS_CUDA(cudaMemcpyAsync(e->mask, m.data(), m.size(), cudaMemcpyHostToDevice, s));
+            DTTS_CUDA(cudaMemcpyAsync(e->mask_bits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice, s));
+        }
         DTTS_CUDA(cudaStreamSynchronize(s));  // host tables go out of scope
         if (e->gexec) { cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
         e->gkey = key;

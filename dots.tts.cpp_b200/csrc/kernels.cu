@@ -2,6 +2,7 @@
 // projections, conditioning, DiT output head, PatchEncoder conv/pairing.
 #include "kernels.cuh"
 #include <math.h>
+#include <algorithm>
 
 namespace dtts {
 
@@ -15,35 +16,35 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const float *__restric
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
+    const long long r = row / tok_per_row;
     const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
-    float4 v[8];
+    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
+    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
+    // all loads first: the row, its shift and its scale are independent
+    float4 v[8], a[8], b[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < 8; j++) { a[j] = __ldg(sh + lane + 32 * j); b[j] = __ldg(sc + lane + 32 * j); }
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        v[j] = xr[lane + 32 * j];
-        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    }
+    for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
     const float mean = warp_sum(s) * (1.0f / kD);
     float q = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
-        q += (a * a + b * b) + (c * c + d * d);
+        const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
+        q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
     }
     const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
-    const long long r = row / tok_per_row;
-    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
-    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
     uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        const int c4 = lane + 32 * j;
-        float4 a = __ldg(sh + c4), b = __ldg(sc + c4);
-        float o0 = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
-        float o1 = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
-        float o2 = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
-        float o3 = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
-        yr[c4] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+        const float o0 = (v[j].x - mean) * inv * (1.0f + b[j].x) + a[j].x;
+        const float o1 = (v[j].y - mean) * inv * (1.0f + b[j].y) + a[j].y;
+        const float o2 = (v[j].z - mean) * inv * (1.0f + b[j].z) + a[j].z;
+        const float o3 = (v[j].w - mean) * inv * (1.0f + b[j].w) + a[j].w;
+        yr[lane + 32 * j] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
     }
 }
 
@@ -186,17 +187,24 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
             }
         }
         // scale + mask
+        uint32_t mb[2][2] = {{~0u, ~0u}, {~0u, ~0u}};   // [row g / g+8][key word within the block]
+        if (a.mask_bits) {
+            const int mw = (a.kv_len + 31) >> 5, w0 = k0 >> 5;
+            if (qi0 < a.Tq) { mb[0][0] = a.mask_bits[(long long)qi0 * mw + w0]; if (w0 + 1 < mw) mb[0][1] = a.mask_bits[(long long)qi0 * mw + w0 + 1]; }
+            if (qi1 < a.Tq) { mb[1][0] = a.mask_bits[(long long)qi1 * mw + w0]; if (w0 + 1 < mw) mb[1][1] = a.mask_bits[(long long)qi1 * mw + w0 + 1]; }
+        }
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int nt = 0; nt < 8; nt++) {
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                const int key = k0 + nt * 8 + 2 * t + (c & 1);
+                const int kl = nt * 8 + 2 * t + (c & 1);
+                const int key = k0 + kl;
                 const int qi = (c < 2) ? qi0 : qi1;
                 float s = sc[nt][c] * a.scale;
                 bool ok = key < a.kv_len;
                 if (a.causal) ok = ok && (key <= a.q_pos0 + qi);
-                if (a.mask && ok && qi < a.Tq) ok = a.mask[(long long)qi * a.kv_len + key] != 0;
+                ok = ok && ((mb[c >> 1][kl >> 5] >> (kl & 31)) & 1u);
                 s = ok ? s : -INFINITY;
                 sc[nt][c] = s;
                 if (c < 2) mx0 = fmaxf(mx0, s); else mx1 = fmaxf(mx1, s);
@@ -258,7 +266,164 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
     }
 }
 
+// Short-sequence attention (Tq <= 64 and kv_len <= 64, the DiT at L <= 64):
+// every CTA walks `per_cta` consecutive (row, head) pairs, prefetching the next
+// pair's Q, K and V tiles with cp.async while it computes the current one; one
+// key block, so the softmax is exact in one pass (exp2 of pre-scaled scores).
+__global__ void __launch_bounds__(128, 4) attn_short_kernel(AttnArgs a, int n_pairs, int per_cta) {
+    extern __shared__ __align__(128) uint8_t attn_smem[];
+    bf16 *sm = reinterpret_cast<bf16 *>(attn_smem);   // [2 buffers][Q, K, V][64 * 64]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int p0 = blockIdx.x * per_cta;
+    const int pend = min(p0 + per_cta, n_pairs);
+    const float kLog2e = 1.4426950408889634f;
+    const float sc = a.scale * kLog2e;
+    auto issue = [&](int p, int buf) {
+        const int r = p / kH, h = p % kH;
+        bf16 *base = sm + buf * 3 * 64 * 64;
+        load_tile64(base, reinterpret_cast<const bf16 *>(a.q) + (long long)r * a.Tq * a.ldq + h * kHD, a.ldq, a.Tq);
+        load_tile64(base + 64 * 64, reinterpret_cast<const bf16 *>(a.k) + (long long)r * a.kv_cap * a.ldkv + h * kHD,
+                    a.ldkv, a.kv_len);
+        load_tile64(base + 2 * 64 * 64, reinterpret_cast<const bf16 *>(a.v) + (long long)r * a.kv_cap * a.ldkv + h * kHD,
+                    a.ldkv, a.kv_len);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    if (p0 < pend) issue(p0, 0);
+    const int qi0 = warp * 16 + g, qi1 = qi0 + 8;
+    // the mask is shared by every (row, head): this thread's two query rows, keys 0..63
+    uint32_t mb[2][2] = {{~0u, ~0u}, {~0u, ~0u}};
+    if (a.mask_bits) {
+        const int mw = (a.kv_len + 31) >> 5;
+        if (qi0 < a.Tq) { mb[0][0] = a.mask_bits[qi0 * mw]; if (mw > 1) mb[0][1] = a.mask_bits[qi0 * mw + 1]; }
+        if (qi1 < a.Tq) { mb[1][0] = a.mask_bits[qi1 * mw]; if (mw > 1) mb[1][1] = a.mask_bits[qi1 * mw + 1]; }
+    }
+    for (int p = p0, it = 0; p < pend; p++, it++) {
+        const int buf = it & 1;
+        if (p + 1 < pend) {
+            issue(p + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        }
+        __syncthreads();
+        const bf16 *Qs = sm + buf * 3 * 64 * 64, *Ks = Qs + 64 * 64, *Vs = Qs + 2 * 64 * 64;
+        uint32_t qf[4][4];
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+            ldsm_x4(qf[kk], Qs + swz(row, 2 * kk + (lane >> 4)));
+        }
+        float s[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                uint32_t b[4];
+                ldsm_x4(b, Ks + swz(np * 16 + (lane & 7) + 8 * (lane >> 4), 2 * kk + ((lane >> 3) & 1)));
+                mma_bf16_16816(s[2 * np], qf[kk], b[0], b[1]);
+                mma_bf16_16816(s[2 * np + 1], qf[kk], b[2], b[3]);
+            }
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int key = nt * 8 + 2 * t + (c & 1);
+                const int qi = (c < 2) ? qi0 : qi1;
+                bool ok = key < a.kv_len;
+                if (a.causal) ok = ok && (key <= a.q_pos0 + qi);
+                ok = ok && ((mb[c >> 1][key >> 5] >> (key & 31)) & 1u);
+                const float v = ok ? s[nt][c] * sc : -INFINITY;
+                s[nt][c] = v;
+                if (c < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float u0 = mx0 == -INFINITY ? 0.f : mx0, u1 = mx1 == -INFINITY ? 0.f : mx1;
+        float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+            s[nt][0] = exp2f(s[nt][0] - u0); s[nt][1] = exp2f(s[nt][1] - u0);
+            s[nt][2] = exp2f(s[nt][2] - u1); s[nt][3] = exp2f(s[nt][3] - u1);
+            l0 += s[nt][0] + s[nt][1];
+            l1 += s[nt][2] + s[nt][3];
+        }
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        float o[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            uint32_t pa[4];
+            pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; dp++) {
+                uint32_t b[4];
+                ldsm_x4_t(b, Vs + swz(kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * dp + (lane >> 4)));
+                mma_bf16_16816(o[2 * dp], pa, b[0], b[1]);
+                mma_bf16_16816(o[2 * dp + 1], pa, b[2], b[3]);
+            }
+        }
+        const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+        const int r = p / kH, h = p % kH;
+        bf16 *og = reinterpret_cast<bf16 *>(a.o) + (long long)r * a.Tq * a.ldo + h * kHD;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+            const int d = nt * 8 + 2 * t;
+            if (qi0 < a.Tq)
+                *reinterpret_cast<uint32_t *>(og + (long long)qi0 * a.ldo + d) = pack_bf16x2(o[nt][0] * inv0, o[nt][1] * inv0);
+            if (qi1 < a.Tq)
+                *reinterpret_cast<uint32_t *>(og + (long long)qi1 * a.ldo + d) = pack_bf16x2(o[nt][2] * inv1, o[nt][3] * inv1);
+        }
+        __syncthreads();   // buffer `buf` is refilled two pairs from now
+    }
+}
+
+constexpr int kShortSmem = 2 * 3 * 64 * 64 * 2;
+
+void pack_mask_bits(const uint8_t *mask, int Tq, int kv_len, uint32_t *bits) {
+    const int mw = (kv_len + 31) / 32;
+    for (int i = 0; i < Tq; i++)
+        for (int w = 0; w < mw; w++) {
+            uint32_t v = 0;
+            for (int b = 0; b < 32; b++) {
+                const int j = 32 * w + b;
+                if (j < kv_len && mask[(long long)i * kv_len + j]) v |= 1u << b;
+            }
+            bits[(long long)i * mw + w] = v;
+        }
+}
+
+cudaError_t attention_short_prepare() {
+    return cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kShortSmem);
+}
+
 void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
+    if (a.Tq <= 64 && a.kv_len <= 64) {
+        const int n_pairs = a.rows * kH;
+        int dev = 0, nsm = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        // about 4 resident CTAs per SM, each with a few pairs to pipeline
+        const int target = nsm * 4;
+        const int per_cta = std::max(1, (n_pairs + target - 1) / target);
+        const int grid = (n_pairs + per_cta - 1) / per_cta;
+        attn_short_kernel<<<grid, 128, kShortSmem, s>>>(a, n_pairs, per_cta);
+        return;
+    }
     dim3 grid((a.Tq + 63) / 64, kH, a.rows);
     attn_bf16_kernel<<<grid, 128, 0, s>>>(a);
 }

@@ -41,10 +41,17 @@ struct AttnArgs {
     int rows, Tq, kv_len, kv_cap;
     int q_pos0;          // absolute position of query 0 (causal masking)
     int causal;
-    const uint8_t *mask; // [Tq][kv_len] (1 = attend) or nullptr
+    const uint8_t *mask; // [Tq][kv_len] (1 = attend) or nullptr (fp32 kernel)
+    const uint32_t *mask_bits;  // the same mask bit-packed, [Tq][ceil(kv_len/32)] words,
+                                // bit k of word w = key 32w + k (bf16 kernels); nullptr: none
     float scale;
 };
+// Tq <= 64 and kv_len <= 64 take the pipelined short-sequence kernel (call
+// attention_short_prepare() once per device first); longer ones the tiled kernel.
 void launch_attention_bf16(const AttnArgs &a, cudaStream_t s);
+cudaError_t attention_short_prepare();
+// Host helper: bit-packs a [Tq][kv_len] uint8 mask into [Tq][ceil(kv_len/32)] words.
+void pack_mask_bits(const uint8_t *mask, int Tq, int kv_len, uint32_t *bits);
 cudaError_t launch_attention_f32(const AttnArgs &a, cudaStream_t s);  // kv_len <= 400
 cudaError_t attention_f32_prepare();  // per device, before the first fp32 launch
 

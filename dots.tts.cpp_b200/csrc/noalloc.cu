@@ -91,7 +91,7 @@ extern "C" int dtts_attn_forward_f32_noalloc(const float *x, const float *wq, co
     launch_gemm_f32(x, wk, nullptr, k, M, kD, kD, s);
     launch_gemm_f32(x, wv, nullptr, v, M, kD, kD, s);
     launch_qk_norm_rope_f32(q, k, M, L, 1, qn, kn, rope, ROPE_HALF, 0, s);
-    AttnArgs a;
+    AttnArgs a{};
     a.q = q; a.k = k; a.v = v; a.o = ctx; a.ldq = a.ldkv = a.ldo = kD;
     a.rows = rows; a.Tq = L; a.kv_len = L; a.kv_cap = L; a.q_pos0 = 0; a.causal = 0;
     a.mask = mask; a.scale = 1.0f / sqrtf(64.0f);

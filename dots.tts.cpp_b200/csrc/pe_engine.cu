@@ -145,7 +145,7 @@ struct dtts_pe {
                 if ((st = gemm(op))) return st;
             }
             {
-                AttnArgs a;
+                AttnArgs a{};
                 a.q = q; a.ldq = kD; a.k = kc + l * layer_stride; a.v = vc + l * layer_stride; a.ldkv = kD;
                 a.o = att; a.ldo = kD; a.rows = B; a.Tq = T; a.kv_len = cur_len + T; a.kv_cap = max_tokens;
                 a.q_pos0 = cur_len; a.causal = 1; a.mask = nullptr; a.scale = 1.0f / sqrtf(64.0f);
@@ -239,6 +239,7 @@ int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batc
     DTTS_CUDA(cudaStreamCreateWithFlags(&p->own_stream, cudaStreamNonBlocking));
     p->stream = p->own_stream;
     DTTS_CUDA(gemm_prepare_attributes());
+    DTTS_CUDA(attention_short_prepare());
     p->d_err = (int *)p->wts.alloc(4);
     DTTS_CHECK(p->d_err, DTTS_ERR_OOM, "cudaMalloc failed");
     DTTS_CUDA(cudaMemset(p->d_err, 0, 4));

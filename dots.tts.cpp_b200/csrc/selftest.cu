@@ -72,13 +72,16 @@ int dtts_selftest_attention(const float *q, const float *k, const float *v, floa
     const size_t esz = use_f32 ? 4 : 2;
     void *dq = s.a.alloc(nq * esz), *dk = s.a.alloc(nk * esz), *dv = s.a.alloc(nk * esz), *dout = s.a.alloc(nq * esz);
     void *dm = mask ? s.a.alloc((size_t)Tq * kv_len) : nullptr;
-    DTTS_CHECK(dq && dk && dv && dout && (!mask || dm), DTTS_ERR_OOM, "cudaMalloc failed");
+    const int mw = (kv_len + 31) / 32;
+    void *dbits = mask ? s.a.alloc((size_t)Tq * mw * 4) : nullptr;
+    DTTS_CHECK(dq && dk && dv && dout && (!mask || (dm && dbits)), DTTS_ERR_OOM, "cudaMalloc failed");
     if (use_f32) {
         DTTS_CUDA(attention_f32_prepare());
         DTTS_CUDA(cudaMemcpy(dq, q, nq * 4, cudaMemcpyHostToDevice));
         DTTS_CUDA(cudaMemcpy(dk, k, nk * 4, cudaMemcpyHostToDevice));
         DTTS_CUDA(cudaMemcpy(dv, v, nk * 4, cudaMemcpyHostToDevice));
     } else {
+        DTTS_CUDA(attention_short_prepare());
         std::vector<uint16_t> t(std::max(nq, nk));
         f32_to_bf16_host(q, t.data(), nq);
         DTTS_CUDA(cudaMemcpy(dq, t.data(), nq * 2, cudaMemcpyHostToDevice));
@@ -87,11 +90,16 @@ int dtts_selftest_attention(const float *q, const float *k, const float *v, floa
         f32_to_bf16_host(v, t.data(), nk);
         DTTS_CUDA(cudaMemcpy(dv, t.data(), nk * 2, cudaMemcpyHostToDevice));
     }
-    if (mask) DTTS_CUDA(cudaMemcpy(dm, mask, (size_t)Tq * kv_len, cudaMemcpyHostToDevice));
-    AttnArgs a;
+    if (mask) {
+        DTTS_CUDA(cudaMemcpy(dm, mask, (size_t)Tq * kv_len, cudaMemcpyHostToDevice));
+        std::vector<uint32_t> bits((size_t)Tq * mw);
+        pack_mask_bits(mask, Tq, kv_len, bits.data());
+        DTTS_CUDA(cudaMemcpy(dbits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice));
+    }
+    AttnArgs a{};
     a.q = dq; a.k = dk; a.v = dv; a.o = dout; a.ldq = a.ldkv = a.ldo = kD;
     a.rows = rows; a.Tq = Tq; a.kv_len = kv_len; a.kv_cap = kv_len; a.q_pos0 = q_pos0; a.causal = causal;
-    a.mask = (const uint8_t *)dm; a.scale = 0.125f;
+    a.mask = (const uint8_t *)dm; a.mask_bits = (const uint32_t *)dbits; a.scale = 0.125f;
     if (use_f32) DTTS_CUDA(launch_attention_f32(a, 0));
     else launch_attention_bf16(a, 0);
     DTTS_CUDA(cudaGetLastError());

@@ -287,6 +287,7 @@ class Reference:
         self.lib = C.CDLL(path)
         L = self.lib
         L.ref_num_threads.restype = C.c_int
+        L.ref_set_threads.argtypes = [C.c_int]
         L.ref_manual_attention.argtypes = [_fp, _fp, C.c_int] + [_fp] * 7 + [_u8p, _fp]
         L.ref_dit_block.argtypes = [_fp, _fp, _fp, C.POINTER(DitBlock), C.c_int, _u8p, _fp, C.c_int]
         L.ref_dit_velocity.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp, _u8p, _fp, C.c_int, C.c_int, _fp]
@@ -297,6 +298,9 @@ class Reference:
 
     def num_threads(self):
         return self.lib.ref_num_threads()
+
+    def set_threads(self, n):
+        self.lib.ref_set_threads(int(n))
 
     def manual_attention(self, x, wq, wk, wv, wo, bo=None, qn=None, kn=None, mask=None, pos=None):
         x = np.ascontiguousarray(x, np.float32)

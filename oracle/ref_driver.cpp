@@ -104,6 +104,7 @@ void dit_block_per_token_ffn(const float *x_in, const float *cond, const dit_blo
 extern "C" {
 
 int ref_num_threads(void) { return omp_get_max_threads(); }
+void ref_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
 
 void ref_manual_attention(float *out, const float *x, int n_tokens,
                           const float *wq, const float *wk, const float *wv, const float *wo,
