@@ -160,6 +160,7 @@ struct dtts_dit {
     float *spk_w1 = nullptr, *spk_b1 = nullptr, *spk_lw = nullptr, *spk_lb = nullptr;
     float *out_w = nullptr, *out_b = nullptr, *coord_w = nullptr, *coord_b = nullptr;
     int *d_err = nullptr;
+    bool has_in = false, has_out = false;
 
     // workspace
     int cap_tok = 0, cap_rows = 0, cap_L = 0, cap_nfe = 0;
@@ -411,8 +412,8 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     *out = nullptr;
     DTTS_CHECK(w->n_layers >= 1 && w->n_layers <= 64 && w->blocks, DTTS_ERR_ARG, "n_layers %d invalid", w->n_layers);
     DTTS_CHECK(dtype == DTTS_DTYPE_BF16, DTTS_ERR_UNSUPPORTED, "DiT dtype %d not supported by this build", dtype);
-    DTTS_CHECK(w->t_w1 && w->t_w2 && w->oada_w && w->out_w && w->in_w && w->coord_w, DTTS_ERR_ARG,
-               "missing a required global DiT weight");
+    // Global weights are checked by the calls that need them: a model with
+    // only blocks serves dtts_dit_blocks (manual_dit_block).
     for (int l = 0; l < w->n_layers; l++) {
         const dtts_dit_block_weights &b = w->blocks[l];
         DTTS_CHECK(b.wq && b.wk && b.wv && b.wo && b.w1 && b.w2 && b.ada_w, DTTS_ERR_ARG,
@@ -463,7 +464,9 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
         if ((st = upload_f32(e->wts, bias.data(), bias.size(), &e->b_ada, s))) return st;
         DTTS_CUDA(cudaStreamSynchronize(s));
     }
-    if ((st = upload_bf16_concat(e->wts, {{w->in_w, kD}}, kD, &e->w_in, s))) return st;
+    if ((st = upload_bf16_concat(e->wts, {{w->in_w, kD}}, kD, &e->w_in, s))) return st;   // zeros if absent
+    e->has_in = w->in_w != nullptr;
+    e->has_out = w->out_w != nullptr && w->oada_w != nullptr;
     if ((st = upload_f32(e->wts, w->in_b, kD, &e->b_in, s))) return st;
     if ((st = upload_f32(e->wts, w->t_w1, (size_t)kD * 256, &e->t_w1, s))) return st;
     if ((st = upload_f32(e->wts, w->t_b1, kD, &e->t_b1, s))) return st;
@@ -509,6 +512,7 @@ int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const u
     DTTS_CHECK(rows >= 1 && L >= 1 && L <= 4096 && n_out >= 1 && n_out <= L, DTTS_ERR_ARG,
                "bad shape rows=%d L=%d n_out=%d", rows, L, n_out);
     DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind %d", mem);
+    DTTS_CHECK(e->has_in && e->has_out, DTTS_ERR_ARG, "model lacks input_layer / output layer weights");
     DeviceGuard g(e->device);
     int st = e->ensure_workspace(rows, L, 1);
     if (st) return st;
@@ -568,6 +572,8 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
     DTTS_CHECK(a->layout == DTTS_LAYOUT_FM_MASK || a->layout == DTTS_LAYOUT_FULL, DTTS_ERR_ARG, "bad layout");
     DTTS_CHECK(a->mem == DTTS_MEM_HOST || a->mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
     DTTS_CHECK(!a->spk || (e->spk_w1 && e->spk_lw), DTTS_ERR_ARG, "speaker vectors given but xvec_proj weights absent");
+    DTTS_CHECK(e->has_in && e->has_out && e->coord_w && e->t_w1 && e->t_w2, DTTS_ERR_ARG,
+               "model lacks input/output/coordinate/time-embedding weights needed by the solve");
     DeviceGuard g(e->device);
     const int rows = 2 * a->n_utt, L = a->fm_len + a->patch;
     int st = e->ensure_workspace(rows, L, a->nfe);
@@ -638,6 +644,85 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
     const cudaMemcpyKind out_kind = a->mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
     DTTS_CUDA(cudaMemcpyAsync(a->z_out, e->z, (size_t)a->n_utt * a->patch * kLat * 4, out_kind, s));
     return e->finish(a->mem == DTTS_MEM_HOST);
+}
+
+int dtts_dit_blocks(dtts_dit *e, const float *h_in, const float *cond, const uint8_t *mask, const float *pos, int rows,
+                    int L, float *h_out, int mem) {
+    DTTS_CHECK(e && h_in && cond && h_out, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(rows >= 1 && L >= 1 && L <= 4096, DTTS_ERR_ARG, "bad shape rows=%d L=%d", rows, L);
+    DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind %d", mem);
+    DeviceGuard g(e->device);
+    int st = e->ensure_workspace(rows, L, 1);
+    if (st) return st;
+    if (e->gexec) { DTTS_CUDA(cudaStreamSynchronize(e->stream)); cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
+    e->gkey.clear();
+    e->launches = 0;
+    const cudaMemcpyKind in_kind = mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    cudaStream_t s = e->stream;
+    const size_t ntok = (size_t)rows * L;
+    DTTS_CUDA(cudaMemcpyAsync(e->h, h_in, ntok * kD * 4, in_kind, s));
+    DTTS_CUDA(cudaMemcpyAsync(e->cond_f32, cond, (size_t)rows * kD * 4, in_kind, s));
+    std::vector<float> hpos;
+    std::vector<float2> rt;
+    if (pos) {
+        hpos.resize(L);
+        DTTS_CUDA(cudaMemcpy(hpos.data(), pos, L * 4, mem == DTTS_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToHost));
+    }
+    rope_half_table(pos ? hpos.data() : nullptr, L, rt);
+    DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
+    e->last_mask = mask != nullptr;
+    std::vector<uint8_t> hm;
+    std::vector<uint32_t> bits;
+    if (mask) {
+        hm.resize((size_t)L * L);
+        DTTS_CUDA(cudaMemcpy(hm.data(), mask, hm.size(), mem == DTTS_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToHost));
+        bits.resize((size_t)L * ((L + 31) / 32));
+        pack_mask_bits(hm.data(), L, L, bits.data());
+        DTTS_CUDA(cudaMemcpyAsync(e->mask, hm.data(), hm.size(), cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaMemcpyAsync(e->mask_bits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice, s));
+    }
+    e->launches++;
+    launch_silu_bf16(e->cond_f32, e->a_cond, (long long)rows * kD, s);
+    {
+        GemmOp op = make_op(e->t_acond, e->t_ada, rows, e->n_ada, kD, EPI_F32, e->d_err, e->tu_ada);
+        op.ep.bias = e->b_ada; op.ep.out = e->ada; op.ep.ldo = e->n_ada;
+        if ((st = e->gemm(op))) return st;
+    }
+    e->last_ada_rows = rows;
+    e->ada_cur = e->ada;
+    e->rows_per_ada = 1;
+    e->last_rows = rows; e->last_L = L; e->last_P = 0;
+    static const int order[7] = {5, 0, 4, 1, 6, 2, 3};
+    for (int l = 0; l < e->n_layers; l++)
+        for (int i = 0; i < 7; i++)
+            if ((st = e->enqueue_block_op(order[i], l, rows, L))) return st;
+    const cudaMemcpyKind out_kind = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    DTTS_CUDA(cudaMemcpyAsync(h_out, e->h, ntok * kD * 4, out_kind, s));
+    return e->finish(mem == DTTS_MEM_HOST);
+}
+
+int dtts_dit_cond(dtts_dit *e, float t, const float *spk, float spk_scale, float *cond) {
+    DTTS_CHECK(e && cond, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(e->t_w1 && e->t_w2, DTTS_ERR_ARG, "model lacks time-embedding weights");
+    DTTS_CHECK(!spk || (e->spk_w1 && e->spk_lw), DTTS_ERR_ARG, "speaker vector given but xvec_proj weights absent");
+    DeviceGuard g(e->device);
+    int st = e->ensure_workspace(1, 1, 1);
+    if (st) return st;
+    cudaStream_t s = e->stream;
+    float se[256];
+    sinusoid(t, se);
+    DTTS_CUDA(cudaMemcpyAsync(e->se_tab, se, sizeof(se), cudaMemcpyHostToDevice, s));
+    launch_time_mlp(e->se_tab, 1, e->t_w1, e->t_b1, e->t_w2, e->t_b2, e->h1, e->temb, s);
+    if (spk) {
+        DTTS_CUDA(cudaMemcpyAsync(e->spk_in, spk, kSpk * 4, cudaMemcpyHostToDevice, s));
+        launch_speaker_cond(e->spk_in, 1, e->spk_w1, e->spk_b1, e->spk_lw, e->spk_lb, spk_scale, e->spk_c, s);
+        launch_add_f32(e->temb, e->spk_c, e->cond_f32, kD, s);
+        DTTS_CUDA(cudaMemcpyAsync(cond, e->cond_f32, kD * 4, cudaMemcpyDeviceToHost, s));
+    } else {
+        DTTS_CUDA(cudaMemcpyAsync(cond, e->temb, kD * 4, cudaMemcpyDeviceToHost, s));
+    }
+    DTTS_CUDA(cudaGetLastError());
+    return e->finish(true);
 }
 
 int dtts_dit_tune(dtts_dit *e, const char *gemm, int bn, int epi_warps, int ksplit) {

@@ -9,10 +9,10 @@ namespace dtts {
 // =========================================================================
 // norms: one warp per token row of 1024 fp32 values (8 x float4 per lane)
 // =========================================================================
-__global__ void __launch_bounds__(256) ln_modulate_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
-                                                          const float *__restrict__ shift,
-                                                          const float *__restrict__ scale, long long ada_ld,
-                                                          int tok_per_row) {
+__global__ void __launch_bounds__(256, 3) ln_modulate_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
+                                                             const float *__restrict__ shift,
+                                                             const float *__restrict__ scale, long long ada_ld,
+                                                             int tok_per_row) {
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -20,12 +20,9 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const float *__restric
     const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
     const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
     const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
-    // all loads first: the row, its shift and its scale are independent
-    float4 v[8], a[8], b[8];
+    float4 v[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
-#pragma unroll
-    for (int j = 0; j < 8; j++) { a[j] = __ldg(sh + lane + 32 * j); b[j] = __ldg(sc + lane + 32 * j); }
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
@@ -40,10 +37,11 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(const float *__restric
     uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        const float o0 = (v[j].x - mean) * inv * (1.0f + b[j].x) + a[j].x;
-        const float o1 = (v[j].y - mean) * inv * (1.0f + b[j].y) + a[j].y;
-        const float o2 = (v[j].z - mean) * inv * (1.0f + b[j].z) + a[j].z;
-        const float o3 = (v[j].w - mean) * inv * (1.0f + b[j].w) + a[j].w;
+        const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
+        const float o0 = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
+        const float o1 = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
+        const float o2 = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
+        const float o3 = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
         yr[lane + 32 * j] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
     }
 }
@@ -270,7 +268,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
 // every CTA walks `per_cta` consecutive (row, head) pairs, prefetching the next
 // pair's Q, K and V tiles with cp.async while it computes the current one; one
 // key block, so the softmax is exact in one pass (exp2 of pre-scaled scores).
-__global__ void __launch_bounds__(128, 4) attn_short_kernel(AttnArgs a, int n_pairs, int per_cta) {
+__global__ void __launch_bounds__(128, 5) attn_short_kernel(AttnArgs a, int n_pairs, int per_cta) {
     extern __shared__ __align__(128) uint8_t attn_smem[];
     bf16 *sm = reinterpret_cast<bf16 *>(attn_smem);   // [2 buffers][Q, K, V][64 * 64]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -417,8 +415,8 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
         int dev = 0, nsm = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-        // about 4 resident CTAs per SM, each with a few pairs to pipeline
-        const int target = nsm * 4;
+        // about 5 resident CTAs per SM, each with a few pairs to pipeline
+        const int target = nsm * 5;
         const int per_cta = std::max(1, (n_pairs + target - 1) / target);
         const int grid = (n_pairs + per_cta - 1) / per_cta;
         attn_short_kernel<<<grid, 128, kShortSmem, s>>>(a, n_pairs, per_cta);
@@ -621,6 +619,15 @@ __global__ void silu_bf16_kernel(const float *__restrict__ x, bf16 *__restrict__
 }
 void launch_silu_bf16(const float *x, bf16 *y, long long n, cudaStream_t s) {
     silu_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, y, n);
+}
+
+__global__ void add_f32_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c,
+                               long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) c[i] = a[i] + b[i];
+}
+void launch_add_f32(const float *a, const float *b, float *c, long long n, cudaStream_t s) {
+    add_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a, b, c, n);
 }
 
 __global__ void history_rows_kernel(const float *__restrict__ src, int n_seq, int src_len, bf16 *__restrict__ dst,

@@ -68,6 +68,8 @@ void launch_qk_norm_rope_f32(float *q, float *k, int M, int tok_per_row, int qk_
 void launch_f32_to_bf16(const float *x, bf16 *y, long long n, cudaStream_t s);
 // SiLU(x) -> bf16 (the A operand of the adaLN GEMM)
 void launch_silu_bf16(const float *x, bf16 *y, long long n, cudaStream_t s);
+// c = a + b (fp32, n elements)
+void launch_add_f32(const float *a, const float *b, float *c, long long n, cudaStream_t s);
 // Copy rows of a [n_seq][src_len][1024] fp32 tensor into tokens 0..src_len-1 of
 // sequence rows (row_stride*u + row_off) of a [rows][L][1024] bf16 buffer.
 void launch_history_rows(const float *src, int n_seq, int src_len, bf16 *dst, int L, int row_stride, int row_off,

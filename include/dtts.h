@@ -148,6 +148,18 @@ int dtts_dit_sync(dtts_dit *e);
 int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const uint8_t *mask, const float *pos,
                       int rows, int L, int n_out, float *out, int mem);
 
+/* The block stack alone on `rows` sequences of L tokens: h_out = block_{n-1}(...
+ * block_0(h_in)), each block = manual_dit_block (include/dit_manual.h:148) with
+ * the FFN applied to every token.  h_in, h_out [rows][L][1024], cond
+ * [rows][1024] raw c.  A model created with only block weights serves this
+ * call (the drop-in manual_dit_block uses one such engine per block). */
+int dtts_dit_blocks(dtts_dit *e, const float *h_in, const float *cond, const uint8_t *mask, const float *pos,
+                    int rows, int L, float *h_out, int mem);
+/* c = compute_cond(t, spk) on the device (src/e2e_pipeline_v4.cpp:57-71):
+ * time MLP of the sinusoid of t, plus speaker_scale * LN(xvec_proj(spk)) when
+ * spk != NULL.  Host pointers (spk [512], cond [1024]); synchronous. */
+int dtts_dit_cond(dtts_dit *e, float t, const float *spk, float spk_scale, float *cond);
+
 typedef struct dtts_solve_args {
     int n_utt;                 /* utterances; 2*n_utt CFG rows run per step        */
     int fm_len;                /* history tokens; L = fm_len + patch                */
