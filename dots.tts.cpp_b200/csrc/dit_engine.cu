@@ -49,6 +49,21 @@ void rope_half_table(const float *pos, int L, std::vector<float2> &tab) {
     }
 }
 
+// (cos, sin) per token for ggml_rope mode 0 (adjacent pairs), the pairing of
+// the reference's ggml DiT path (src/modules/backbone/dit_attention.cpp:53-54):
+// theta starts at the position and is multiplied by 1e4^(-2/64) per pair.
+void rope_adjacent_table(const float *pos, int L, std::vector<float2> &tab) {
+    tab.resize((size_t)L * 32);
+    const float ts = powf(10000.0f, -2.0f / 64.0f);
+    for (int t = 0; t < L; t++) {
+        float theta = pos ? (float)(int)pos[t] : (float)t;
+        for (int d = 0; d < 32; d++) {
+            tab[(size_t)t * 32 + d] = make_float2(cosf(theta), sinf(theta));
+            theta *= ts;
+        }
+    }
+}
+
 // Sinusoidal time embedding [cos(t f_i) | sin(t f_i)], f_i = exp(-ln(1e4) i / 128)
 // (src/e2e_pipeline_v4.cpp:58-60).
 void sinusoid(float t, float *se) {
@@ -161,6 +176,11 @@ struct dtts_dit {
     float *out_w = nullptr, *out_b = nullptr, *coord_w = nullptr, *coord_b = nullptr;
     int *d_err = nullptr;
     bool has_in = false, has_out = false;
+    int rope_mode = ROPE_HALF;   // DTTS_ROPE_HALF / DTTS_ROPE_ADJACENT
+    void rope_table(const float *pos, int L, std::vector<float2> &tab) const {
+        if (rope_mode == ROPE_ADJACENT) rope_adjacent_table(pos, L, tab);
+        else rope_half_table(pos, L, tab);
+    }
 
     // workspace
     int cap_tok = 0, cap_rows = 0, cap_L = 0, cap_nfe = 0;
@@ -287,7 +307,7 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             op.ep.ldq = kD; op.ep.ldkv = kD;
             op.ep.tok_per_row = L; op.ep.kv_cap = L; op.ep.kv_start = 0;
             op.ep.qk_norm = 1; op.ep.qn = Ly.qn; op.ep.kn = Ly.kn;
-            op.ep.rope = rope; op.ep.rope_mode = ROPE_HALF;
+            op.ep.rope = rope; op.ep.rope_mode = rope_mode;
             return gemm(op);
         }
         case 4: {
@@ -526,13 +546,12 @@ int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const u
     DTTS_CUDA(cudaMemcpyAsync(e->in_a, x_in, ntok * kD * 4, in_kind, s));
     DTTS_CUDA(cudaMemcpyAsync(e->cond_f32, cond, (size_t)rows * kD * 4, in_kind, s));
     std::vector<float2> rt;
-    rope_half_table(nullptr, L, rt);
     std::vector<float> hpos;
     if (pos) {
         hpos.resize(L);
         DTTS_CUDA(cudaMemcpy(hpos.data(), pos, L * 4, mem == DTTS_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToHost));
-        rope_half_table(hpos.data(), L, rt);
     }
+    e->rope_table(pos ? hpos.data() : nullptr, L, rt);
     DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
     e->last_mask = mask != nullptr;
     std::vector<uint32_t> bits;
@@ -605,7 +624,7 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
             for (int i = 0; i < L; i++) pos[i] = (float)i;
         }
         std::vector<float2> rt;
-        rope_half_table(pos.data(), L, rt);
+        e->rope_table(pos.data(), L, rt);
         std::vector<float> se((size_t)a->nfe * 256);
         const float dt = 1.0f / (float)a->nfe;
         for (int k = 0; k < a->nfe; k++) sinusoid((float)k * dt, &se[(size_t)k * 256]);
@@ -668,7 +687,7 @@ int dtts_dit_blocks(dtts_dit *e, const float *h_in, const float *cond, const uin
         hpos.resize(L);
         DTTS_CUDA(cudaMemcpy(hpos.data(), pos, L * 4, mem == DTTS_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToHost));
     }
-    rope_half_table(pos ? hpos.data() : nullptr, L, rt);
+    e->rope_table(pos ? hpos.data() : nullptr, L, rt);
     DTTS_CUDA(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, s));
     e->last_mask = mask != nullptr;
     std::vector<uint8_t> hm;
@@ -699,6 +718,15 @@ int dtts_dit_blocks(dtts_dit *e, const float *h_in, const float *cond, const uin
     const cudaMemcpyKind out_kind = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
     DTTS_CUDA(cudaMemcpyAsync(h_out, e->h, ntok * kD * 4, out_kind, s));
     return e->finish(mem == DTTS_MEM_HOST);
+}
+
+int dtts_dit_set_rope(dtts_dit *e, int mode) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
+    DTTS_CHECK(mode == DTTS_ROPE_HALF || mode == DTTS_ROPE_ADJACENT, DTTS_ERR_ARG, "bad rope mode %d", mode);
+    if (e->gexec) { DeviceGuard g(e->device); DTTS_CUDA(cudaStreamSynchronize(e->stream)); cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
+    e->gkey.clear();
+    e->rope_mode = mode;
+    return DTTS_OK;
 }
 
 int dtts_dit_cond(dtts_dit *e, float t, const float *spk, float spk_scale, float *cond) {

@@ -20,6 +20,7 @@ MEM_HOST, MEM_DEVICE = 0, 1
 CFG_V4, CFG_V3 = 0, 1
 LAYOUT_FM_MASK, LAYOUT_FULL = 0, 1
 PAIR_ADJACENT, PAIR_AS_WRITTEN = 0, 1
+ROPE_HALF, ROPE_ADJACENT = 0, 1
 
 _fp = C.POINTER(C.c_float)
 _u8p = C.POINTER(C.c_uint8)
@@ -99,7 +100,7 @@ PE_GLOBAL_NAMES = {
 EXPORTS = [
     "dtts_version", "dtts_status_string", "dtts_last_error", "dtts_device_count",
     "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
-    "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_euler_solve", "dtts_dit_profile_kernel",
+    "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_profile_kernel",
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
@@ -147,6 +148,9 @@ def lib(path: str = LIB_PATH):
     L.dtts_dit_sync.argtypes = [_vp]
     L.dtts_dit_velocity.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, C.c_int]
     L.dtts_dit_euler_solve.argtypes = [_vp, C.POINTER(SolveArgs)]
+    L.dtts_dit_blocks.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp, C.c_int]
+    L.dtts_dit_cond.argtypes = [_vp, C.c_float, _vp, C.c_float, _vp]
+    L.dtts_dit_set_rope.argtypes = [_vp, C.c_int]
     L.dtts_dit_profile_kernel.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double),
                                           C.POINTER(C.c_double)]
     L.dtts_dit_last_launch_count.argtypes = [_vp, C.POINTER(C.c_int)]
@@ -292,6 +296,26 @@ class DiT:
         out = np.zeros((rows, n_out, 128), np.float32)
         check(lib().dtts_dit_velocity(self.h, _addr(x_in), _addr(cond), _addr(mask), _addr(pos), rows, L, n_out,
                                       _addr(out), MEM_HOST))
+        return out
+
+    def blocks(self, h_in, cond, mask=None, pos=None):
+        h_in = _f32(h_in)
+        rows, L = h_in.shape[0], h_in.shape[1]
+        cond = _f32(cond)
+        mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        pos = _f32(pos)
+        out = np.zeros_like(h_in)
+        check(lib().dtts_dit_blocks(self.h, _addr(h_in), _addr(cond), _addr(mask), _addr(pos), rows, L, _addr(out),
+                                    MEM_HOST))
+        return out
+
+    def set_rope(self, mode):
+        check(lib().dtts_dit_set_rope(self.h, mode))
+
+    def cond(self, t, spk=None, spk_scale=1.5):
+        spk = _f32(spk)
+        out = np.zeros(1024, np.float32)
+        check(lib().dtts_dit_cond(self.h, C.c_float(t), _addr(spk), C.c_float(spk_scale), _addr(out)))
         return out
 
     def solve(self, fm_cond, fm_uncond, z0, spk=None, spk_scale=1.5, nfe=10, cfg_scale=2.0, cfg_form=CFG_V4,

@@ -67,6 +67,9 @@ extern "C" {
 #define DTTS_LAYOUT_FM_MASK  0 /* v4 FM mask + position ids, src/e2e_pipeline_v4.cpp:120-155 */
 #define DTTS_LAYOUT_FULL     1 /* no mask, positions 0..L-1                                  */
 
+#define DTTS_ROPE_HALF       0 /* pairs (d, d+32): manual_attention, include/dit_manual.h:111-128  */
+#define DTTS_ROPE_ADJACENT   1 /* pairs (2i, 2i+1): ggml_rope mode 0, src/modules/backbone/dit_attention.cpp:53-54 */
+
 #define DTTS_PAIR_ADJACENT   0 /* PE output p = out_proj([h_2p | h_2p+1])                       */
 #define DTTS_PAIR_AS_WRITTEN 1 /* patchenc.cpp:230-232 reshape/permute as written (n_patches > 1) */
 
@@ -155,6 +158,9 @@ int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const u
  * call (the drop-in manual_dit_block uses one such engine per block). */
 int dtts_dit_blocks(dtts_dit *e, const float *h_in, const float *cond, const uint8_t *mask, const float *pos,
                     int rows, int L, float *h_out, int mem);
+/* RoPE pairing of the DiT (default DTTS_ROPE_HALF, the live manual_dit_block
+ * path; DTTS_ROPE_ADJACENT reproduces the ggml DiT path behind dit_forward_raw). */
+int dtts_dit_set_rope(dtts_dit *e, int mode);
 /* c = compute_cond(t, spk) on the device (src/e2e_pipeline_v4.cpp:57-71):
  * time MLP of the sinusoid of t, plus speaker_scale * LN(xvec_proj(spk)) when
  * spk != NULL.  Host pointers (spk [512], cond [1024]); synchronous. */

@@ -126,6 +126,14 @@ static void rms_head(float *v, const float *g) {
     for (int d = 0; d < ORC_HD; d++) { float y = v[d] * inv; if (g) y *= g[d]; v[d] = y; }
 }
 
+/* DiT RoPE pairing: ORC_ROPE_HALF (manual_attention, include/dit_manual.h:111-128)
+ * or ORC_ROPE_ADJACENT (ggml_rope mode 0 as called by the hybrid DiT path,
+ * src/modules/backbone/dit_attention.cpp:53-54). */
+static int g_dit_rope = ORC_ROPE_HALF;
+void orc_set_dit_rope(int mode) { g_dit_rope = mode; }
+
+static void rope_adjacent(float *v, int p);
+
 static void rope_half(float *q, float *k, float pos) {
     const int half = ORC_HD / 2;
     float theta = 1.0f;
@@ -160,7 +168,12 @@ void orc_attention(float *out, const float *x, int L,
             float *kh = k + (size_t)t * ORC_D + h * ORC_HD;
             rms_head(qh, qn);
             rms_head(kh, kn);
-            rope_half(qh, kh, pos ? pos[t] : (float)t);
+            if (g_dit_rope == ORC_ROPE_ADJACENT) {
+                rope_adjacent(qh, pos ? (int)pos[t] : t);
+                rope_adjacent(kh, pos ? (int)pos[t] : t);
+            } else {
+                rope_half(qh, kh, pos ? pos[t] : (float)t);
+            }
         }
     }
     const float scale = 1.0f / sqrtf((float)ORC_HD);

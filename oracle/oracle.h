@@ -85,6 +85,7 @@ typedef struct {
 #define ORC_PAIR_AS_WRITTEN 1  /* ggml permute as written, patchenc.cpp:230-232 */
 
 int  orc_num_threads(void);
+void orc_set_dit_rope(int mode);
 void orc_set_threads(int n);
 
 void orc_sinusoid(float t, float *se256);

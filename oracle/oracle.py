@@ -23,6 +23,8 @@ FFN_PER_TOKEN = 0
 FFN_AS_WRITTEN = 1
 PAIR_ADJACENT = 0
 PAIR_AS_WRITTEN = 1
+ROPE_HALF = 0       # (d, d+32) pairs: manual_attention, include/dit_manual.h:111-128
+ROPE_ADJACENT = 1   # (2i, 2i+1) pairs: ggml_rope mode 0 behind dit_forward_raw
 
 _fp = C.POINTER(C.c_float)
 _u8p = C.POINTER(C.c_uint8)
@@ -172,6 +174,7 @@ class Oracle:
         L = self.lib
         L.orc_num_threads.restype = C.c_int
         L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_set_dit_rope.argtypes = [C.c_int]
         L.orc_sinusoid.argtypes = [C.c_float, _fp]
         L.orc_compute_cond.argtypes = [C.POINTER(Dit), C.c_float, _fp, C.c_float, _fp]
         L.orc_attention.argtypes = [_fp, _fp, C.c_int] + [_fp] * 7 + [_u8p, _fp]
@@ -186,6 +189,10 @@ class Oracle:
 
     def set_threads(self, n):
         self.lib.orc_set_threads(int(n))
+
+    def set_dit_rope(self, mode):
+        """0: half-split (manual_attention), 1: adjacent pairs (ggml mode 0, dit_forward_raw)."""
+        self.lib.orc_set_dit_rope(int(mode))
 
     def num_threads(self):
         return self.lib.orc_num_threads()

@@ -2,6 +2,9 @@
   bf16 paths      max relative error <= 2e-2 and cosine >= 0.999
   fp32 attention  max relative error <= 1e-3
 where max relative error = max|got - ref| / max|ref| over the whole tensor."""
+import json
+import struct
+
 import numpy as np
 
 BF16_REL, BF16_COS = 2e-2, 0.999
@@ -31,3 +34,22 @@ def bf16(a):
 def assert_bf16_close(got, want, what=""):
     r, c = rel(got, want), cos(got, want)
     assert r <= BF16_REL and c >= BF16_COS, f"{what}: max rel {r:.3e} (<= {BF16_REL}), cos {c:.6f} (>= {BF16_COS})"
+
+
+def write_safetensors(path, tensors, metadata=None):
+    """Minimal writer of the safetensors layout: u64 header length, JSON header,
+    raw little-endian data."""
+    hdr, blobs, off = {}, [], 0
+    if metadata:
+        hdr["__metadata__"] = metadata
+    for name, (dtype, arr) in tensors.items():
+        raw = np.ascontiguousarray(arr).tobytes()
+        hdr[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    h = json.dumps(hdr).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)

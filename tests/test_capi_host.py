@@ -3,7 +3,6 @@ every symbol include/dtts.h declares, validates arguments before touching a
 device, and its safetensors reader (F32/F16/BF16, the reference's format,
 include/safetensors.h) parses files and rejects malformed ones."""
 import ctypes as C
-import json
 import os
 import re
 import struct
@@ -12,6 +11,7 @@ import numpy as np
 import pytest
 
 import dtts
+from helpers import write_safetensors
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -68,25 +68,6 @@ def _f16(a):
 def _bf16_bits(a):
     u = np.asarray(a, np.float32).view(np.uint32)
     return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
-
-
-def write_safetensors(path, tensors, metadata=None):
-    """Minimal writer of the safetensors layout: u64 header length, JSON header,
-    raw little-endian data."""
-    hdr, blobs, off = {}, [], 0
-    if metadata:
-        hdr["__metadata__"] = metadata
-    for name, (dtype, arr) in tensors.items():
-        raw = np.ascontiguousarray(arr).tobytes()
-        hdr[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [off, off + len(raw)]}
-        blobs.append(raw)
-        off += len(raw)
-    h = json.dumps(hdr).encode()
-    with open(path, "wb") as f:
-        f.write(struct.pack("<Q", len(h)))
-        f.write(h)
-        for b in blobs:
-            f.write(b)
 
 
 def test_safetensors_reader_dtypes(tmp_path, dtts_mod):
