@@ -26,6 +26,14 @@ namespace {
 
 constexpr int kAdaPerLayer = 6 * kD;
 
+// launch kinds of the solve timeline (DTTS_TL_* in include/dtts.h); 0..4 are
+// the block-op codes of enqueue_block_op
+constexpr int TL_LN = DTTS_TL_LN_MODULATE, TL_GEMM_ADALN = DTTS_TL_GEMM_ADALN, TL_GEMM_INPUT = DTTS_TL_GEMM_INPUT,
+              TL_OUT_HEAD = DTTS_TL_OUT_HEAD, TL_EULER = DTTS_TL_CFG_EULER, TL_COND = DTTS_TL_CONDITIONING;
+static_assert(DTTS_TL_GEMM_QKV == 0 && DTTS_TL_GEMM_O == 1 && DTTS_TL_GEMM_FFN1 == 2 && DTTS_TL_GEMM_FFN2 == 3 &&
+                  DTTS_TL_ATTENTION == 4,
+              "timeline kinds 0..4 are the block-op codes");
+
 // Tile configuration of one GEMM: tile width BN, epilogue warps, K splits.
 struct GemmTune {
     int bn, nw, ks;
@@ -203,11 +211,33 @@ struct dtts_dit {
     cudaGraphExec_t gexec = nullptr;
     std::string gkey;
 
+    // launch timeline (dtts_dit_solve_timeline): one timing event before and
+    // one after every launch of a captured solve; tl_kind[i] is the kind of
+    // launch i, timed by events 2i and 2i+1
+    bool tl_on = false;
+    std::vector<cudaEvent_t> tl_ev;
+    std::vector<int> tl_kind;
+    int tl_begin(int kind) {
+        const size_t i = tl_kind.size();
+        if (2 * i + 1 >= tl_ev.size()) return -1;   // pool exhausted: launch not timed
+        cudaEventRecordWithFlags(tl_ev[2 * i], stream, cudaEventRecordExternal);
+        tl_kind.push_back(kind);
+        return (int)i;
+    }
+    void tl_end(int i) { cudaEventRecordWithFlags(tl_ev[2 * (size_t)i + 1], stream, cudaEventRecordExternal); }
+    struct TlScope {
+        dtts_dit *e;
+        int idx;
+        TlScope(dtts_dit *e_, int kind) : e(e_), idx(e_->tl_on ? e_->tl_begin(kind) : -1) {}
+        ~TlScope() { if (idx >= 0) e->tl_end(idx); }
+    };
+
     ~dtts_dit() {
         if (gexec) cudaGraphExecDestroy(gexec);
         ws.free_all();
         wts.free_all();
         if (own_stream) cudaStreamDestroy(own_stream);
+        for (cudaEvent_t ev : tl_ev) cudaEventDestroy(ev);
     }
 
     int ensure_workspace(int rows, int L, int nfe);
@@ -293,6 +323,7 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
     const Layer &Ly = layers[l];
     const float *ada_l = ada_cur + (long long)l * kAdaPerLayer;
     const int tpr = L * rows_per_ada;   // tokens sharing one modulation row
+    TlScope tl_scope(this, kind == 6 ? TL_LN : kind);
     switch (kind) {
         case 5:
         case 6: {
@@ -350,6 +381,7 @@ int dtts_dit::enqueue_forward(int rows, int L, int P) {
     const int M = rows * L;
     last_rows = rows; last_L = L; last_P = P;
     {   // input layer
+        TlScope tl_scope(this, TL_GEMM_INPUT);
         GemmOp op = make_op(t_x_in, t_in, M, kD, kD, EPI_F32, d_err, tu_in);
         op.ep.bias = b_in; op.ep.out = h; op.ep.ldo = kD;
         int st = gemm(op);
@@ -363,6 +395,7 @@ int dtts_dit::enqueue_forward(int rows, int L, int P) {
         }
     const long long oo = (long long)n_layers * kAdaPerLayer;
     launches++;
+    TlScope tl_scope(this, TL_OUT_HEAD);
     launch_out_head(h, rows, L, P, ada_cur + oo, ada_cur + oo + kD, n_ada, rows_per_ada, out_w, out_b, vel, d_err,
                     stream);
     DTTS_CUDA(cudaGetLastError());
@@ -372,10 +405,17 @@ int dtts_dit::enqueue_forward(int rows, int L, int P) {
 int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
     const int rows = 2 * a->n_utt, L = a->fm_len + a->patch;
     launches += 2;
-    launch_history_rows(in_a, a->n_utt, a->fm_len, x_in, L, 2, 0, stream);
-    launch_history_rows(in_b, a->n_utt, a->fm_len, x_in, L, 2, 1, stream);
+    {
+        TlScope tl_scope(this, TL_COND);
+        launch_history_rows(in_a, a->n_utt, a->fm_len, x_in, L, 2, 0, stream);
+    }
+    {
+        TlScope tl_scope(this, TL_COND);
+        launch_history_rows(in_b, a->n_utt, a->fm_len, x_in, L, 2, 1, stream);
+    }
     if (a->spk) {
         launches++;
+        TlScope tl_scope(this, TL_COND);
         launch_speaker_cond(spk_in, a->n_utt, spk_w1, spk_b1, spk_lw, spk_lb, a->spk_scale, spk_c, stream);
     }
     const float dt = 1.0f / (float)a->nfe;
@@ -383,9 +423,16 @@ int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
     // speaker, so one adaLN GEMM covers all steps and utterances (cond and
     // uncond rows of an utterance share c).
     launches += 3;
-    launch_time_mlp(se_tab, a->nfe, t_w1, t_b1, t_w2, t_b2, h1, temb, stream);
-    launch_cond_rows(temb, a->nfe, a->spk ? spk_c : nullptr, a->n_utt, a_cond, stream);
     {
+        TlScope tl_scope(this, TL_COND);
+        launch_time_mlp(se_tab, a->nfe, t_w1, t_b1, t_w2, t_b2, h1, temb, stream);
+    }
+    {
+        TlScope tl_scope(this, TL_COND);
+        launch_cond_rows(temb, a->nfe, a->spk ? spk_c : nullptr, a->n_utt, a_cond, stream);
+    }
+    {
+        TlScope tl_scope(this, TL_GEMM_ADALN);
         GemmOp op = make_op(t_acond, t_ada, a->nfe * a->n_utt, n_ada, kD, EPI_F32, d_err, tu_ada);
         op.ep.bias = b_ada; op.ep.out = ada; op.ep.ldo = n_ada;
         int st = gemm(op);
@@ -393,13 +440,18 @@ int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
         last_ada_rows = a->nfe * a->n_utt;
     }
     launches++;
-    launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 0, coord_w, coord_b, x_in, L, stream);
+    {
+        TlScope tl_scope(this, TL_EULER);
+        launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 0, coord_w, coord_b, x_in, L,
+                         stream);
+    }
     rows_per_ada = 2;
     for (int step = 0; step < a->nfe; step++) {
         ada_cur = ada + (size_t)step * a->n_utt * n_ada;
         int st = enqueue_forward(rows, L, a->patch);
         if (st) return st;
         launches++;
+        TlScope tl_scope(this, TL_EULER);
         launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 1, coord_w, coord_b, x_in, L,
                          stream);
     }
@@ -779,6 +831,61 @@ int dtts_dit_last_launch_count(dtts_dit *e, int *n) {
     DTTS_CHECK(e && n, DTTS_ERR_ARG, "null argument");
     *n = e->launches;
     return DTTS_OK;
+}
+
+int dtts_dit_solve_timeline(dtts_dit *e, const dtts_solve_args *a, int reps, float *us_total, int *counts) {
+    DTTS_CHECK(e && a && us_total && counts, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(a->mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "the timeline takes device buffers");
+    DTTS_CHECK(reps >= 1 && reps <= 100, DTTS_ERR_ARG, "reps %d out of range", reps);
+    // one ordinary solve: validates the arguments, sizes the workspace and
+    // uploads this shape's tables
+    int st = dtts_dit_euler_solve(e, a);
+    if (st) return st;
+    DeviceGuard g(e->device);
+    cudaStream_t s = e->stream;
+    const int saved_launches = e->launches;
+    const size_t need = 2 * (size_t)(saved_launches + 16);
+    while (e->tl_ev.size() < need) {
+        cudaEvent_t ev;
+        DTTS_CUDA(cudaEventCreate(&ev));
+        e->tl_ev.push_back(ev);
+    }
+    e->tl_kind.clear();
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    DTTS_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    e->tl_on = true;
+    cudaError_t ce = cudaMemcpyAsync(e->z, a->z0, (size_t)a->n_utt * a->patch * kLat * 4, cudaMemcpyDeviceToDevice, s);
+    st = ce == cudaSuccess ? e->enqueue_solve(a) : DTTS_ERR_CUDA;
+    e->tl_on = false;
+    cudaError_t ce2 = cudaStreamEndCapture(s, &graph);
+    e->launches = saved_launches;
+    if (st || ce != cudaSuccess || ce2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        if (st) return st;
+        DTTS_CUDA(ce != cudaSuccess ? ce : ce2);
+    }
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    DTTS_CUDA(ce);
+    for (int k = 0; k < DTTS_TL_KINDS; k++) { us_total[k] = 0.f; counts[k] = 0; }
+    for (size_t i = 0; i < e->tl_kind.size(); i++) counts[e->tl_kind[i]]++;
+    std::vector<double> acc(DTTS_TL_KINDS, 0.0);
+    for (int r = 0; r < reps && !st; r++) {
+        ce = cudaGraphLaunch(exec, s);
+        if (ce != cudaSuccess) { st = DTTS_ERR_CUDA; set_error("timeline graph launch: %s", cudaGetErrorString(ce)); break; }
+        if ((st = stream_wait(s, 120.0))) break;
+        for (size_t i = 0; i < e->tl_kind.size(); i++) {
+            float ms = 0.f;
+            ce = cudaEventElapsedTime(&ms, e->tl_ev[2 * i], e->tl_ev[2 * i + 1]);
+            if (ce != cudaSuccess) { st = DTTS_ERR_CUDA; set_error("timeline event: %s", cudaGetErrorString(ce)); break; }
+            acc[e->tl_kind[i]] += ms;
+        }
+    }
+    cudaGraphExecDestroy(exec);
+    if (st) return st;
+    for (int k = 0; k < DTTS_TL_KINDS; k++) us_total[k] = (float)(acc[k] * 1000.0 / reps);
+    return e->finish(true);
 }
 
 int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us, double *flops, double *bytes) {

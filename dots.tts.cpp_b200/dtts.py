@@ -96,11 +96,17 @@ PE_GLOBAL_NAMES = {
     "out_w": "patch_encoder.out_proj.weight", "out_b": "patch_encoder.out_proj.bias",
 }
 
+# launch kinds of dtts_dit_solve_timeline (DTTS_TL_*)
+TL_NAMES = ["gemm_qkv", "gemm_o", "gemm_ffn1", "gemm_ffn2", "attention", "ln_modulate", "gemm_adaln", "gemm_input",
+            "out_head", "cfg_euler", "conditioning"]
+TL_KINDS = len(TL_NAMES)
+
 # every symbol include/dtts.h declares (checked against the library by the CPU tests)
 EXPORTS = [
     "dtts_version", "dtts_status_string", "dtts_last_error", "dtts_device_count",
     "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
-    "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_profile_kernel",
+    "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_solve_timeline",
+    "dtts_dit_profile_kernel",
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
@@ -333,6 +339,21 @@ class DiT:
         a.layout, a.z_out, a.mem, a.use_graph = layout, _addr(z_out), mem, int(use_graph)
         check(lib().dtts_dit_euler_solve(self.h, C.byref(a)))
         return z_out
+
+    def solve_timeline(self, fm_cond, fm_uncond, z0, z_out, spk=None, spk_scale=1.5, nfe=10, cfg_scale=2.0,
+                       cfg_form=CFG_V4, layout=LAYOUT_FM_MASK, reps=3):
+        """Device time of every launch kind in one solve (device buffers), measured
+        in place with events around each launch of the captured solve.  Returns
+        {kind name: (summed us per solve, launches per solve)}."""
+        a = SolveArgs()
+        a.n_utt, a.fm_len, a.patch = z0.shape[0], fm_cond.shape[1], z0.shape[1]
+        a.fm_cond, a.fm_uncond, a.z0, a.spk = _addr(fm_cond), _addr(fm_uncond), _addr(z0), _addr(spk)
+        a.spk_scale, a.nfe, a.cfg_scale, a.cfg_form = spk_scale, nfe, cfg_scale, cfg_form
+        a.layout, a.z_out, a.mem, a.use_graph = layout, _addr(z_out), MEM_DEVICE, 1
+        us = (C.c_float * TL_KINDS)()
+        n = (C.c_int * TL_KINDS)()
+        check(lib().dtts_dit_solve_timeline(self.h, C.byref(a), reps, us, n))
+        return {TL_NAMES[k]: (us[k], n[k]) for k in range(TL_KINDS)}
 
     def profile(self, kind, iters=20):
         us, fl, by = C.c_float(), C.c_double(), C.c_double()

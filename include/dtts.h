@@ -185,6 +185,26 @@ typedef struct dtts_solve_args {
 } dtts_solve_args;
 int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a);
 
+/* Launch kinds of dtts_dit_solve_timeline. */
+#define DTTS_TL_GEMM_QKV       0   /* QKV projection + qk-norm + RoPE epilogue  */
+#define DTTS_TL_GEMM_O         1   /* attention output projection, gated residual */
+#define DTTS_TL_GEMM_FFN1      2   /* FFN up projection + GELU                   */
+#define DTTS_TL_GEMM_FFN2      3   /* FFN down projection, gated residual        */
+#define DTTS_TL_ATTENTION      4   /* softmax(QK^T/8)V core                      */
+#define DTTS_TL_LN_MODULATE    5   /* LayerNorm + shift/scale (both per block)   */
+#define DTTS_TL_GEMM_ADALN     6   /* adaLN of every step, once per solve        */
+#define DTTS_TL_GEMM_INPUT     7   /* input_layer                                */
+#define DTTS_TL_OUT_HEAD       8   /* output adaLN-LN + out_proj                 */
+#define DTTS_TL_CFG_EULER      9   /* CFG combine + Euler update + coord_proj    */
+#define DTTS_TL_CONDITIONING  10   /* history rows, time MLP, speaker, c rows    */
+#define DTTS_TL_KINDS         11
+/* Device time of every launch of one solve, in place: the solve of `a` (device
+ * buffers) is captured into a CUDA graph with a timing event before and after
+ * each launch and replayed `reps` times.  us_total[k] = summed device time (us)
+ * of kind-k launches in one solve (mean over reps), counts[k] = kind-k launches
+ * per solve.  Runs one ordinary solve first; a->z_out receives its result. */
+int dtts_dit_solve_timeline(dtts_dit *e, const dtts_solve_args *a, int reps, float *us_total, int *counts);
+
 /* Kernel-level timing of one launch type at the shapes of the last solve or
  * velocity call, on the engine stream with CUDA events (after 3 warm-up
  * launches).  kind: 0 QKV GEMM, 1 O GEMM, 2 FFN1 GEMM, 3 FFN2 GEMM,

@@ -144,3 +144,45 @@ def test_bad_arguments(eng18):
     fc = np.zeros((1, 4, 1024), np.float32)
     with pytest.raises(dtts.DttsError):
         eng18.solve(fc, fc, np.zeros((1, 4, 128), np.float32), nfe=0)
+
+
+def test_solve_timeline_counts_and_result(eng18, w18):
+    """The in-place launch timeline used for the benchmark's roofline: launch
+    counts per kind follow the solve's structure, the captured solve computes
+    the same result as an ordinary one, and the per-kind totals add up to the
+    solve's own device time."""
+    import torch
+    n_utt, fm_len, nfe = 8, 60, 3
+    fc, fu = synth.fm_history(14, n_utt, fm_len, w18)
+    z0 = synth.normal(14, "z0", (n_utt, 4, 128), 1.0)
+    spk = synth.normal(14, "spk", (n_utt, 512), 1.0 / np.sqrt(512))
+    want = eng18.solve(fc, fu, z0, spk, nfe=nfe, cfg_scale=2.0)
+    dev = torch.device("cuda", 0)
+    d = [torch.from_numpy(a).to(dev) for a in (fc, fu, z0, spk)]
+    d_z = torch.empty_like(d[2])
+    torch.cuda.synchronize()
+    tl = eng18.solve_timeline(d[0], d[1], d[2], d_z, spk=d[3], nfe=nfe, cfg_scale=2.0, reps=2)
+    assert np.array_equal(d_z.cpu().numpy(), want)
+    n = {k: v[1] for k, v in tl.items()}
+    assert n["gemm_qkv"] == n["gemm_o"] == n["gemm_ffn1"] == n["gemm_ffn2"] == n["attention"] == 18 * nfe
+    assert n["ln_modulate"] == 2 * 18 * nfe and n["gemm_input"] == nfe and n["out_head"] == nfe
+    assert n["gemm_adaln"] == 1 and n["cfg_euler"] == nfe + 1
+    assert all(v[0] > 0 for v in tl.values() if v[1])
+    # whole-solve device time of the ordinary graph, for comparison
+    s = torch.cuda.Stream(device=dev)
+    eng18.set_stream(s.cuda_stream)
+    try:
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                eng18.solve(d[0], d[1], d[2], d[3], nfe=nfe, cfg_scale=2.0, z_out=d_z, mem=dtts.MEM_DEVICE)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(3):
+                eng18.solve(d[0], d[1], d[2], d[3], nfe=nfe, cfg_scale=2.0, z_out=d_z, mem=dtts.MEM_DEVICE)
+            e1.record(s)
+            eng18.sync()
+        solve_us = e0.elapsed_time(e1) * 1000.0 / 3
+    finally:
+        eng18.set_stream(None)
+    total = sum(v[0] for v in tl.values())
+    assert 0.7 * solve_us < total < 1.3 * solve_us, (total, solve_us)
