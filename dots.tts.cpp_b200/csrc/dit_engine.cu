@@ -120,6 +120,18 @@ int upload_f32(DeviceArena &a, const float *h, size_t n, float **out, cudaStream
     return DTTS_OK;
 }
 
+// Uploads h [rows][cols] as its transpose [cols][rows]; `keep` holds the host
+// copy until the stream has been synchronised.
+int upload_f32_transposed(DeviceArena &a, const float *h, size_t rows, size_t cols, float **out, cudaStream_t s,
+                          std::vector<float> &keep) {
+    *out = nullptr;
+    if (!h) return DTTS_OK;
+    keep.resize(rows * cols);
+    for (size_t r = 0; r < rows; r++)
+        for (size_t c = 0; c < cols; c++) keep[c * rows + r] = h[r * cols + c];
+    return upload_f32(a, keep.data(), keep.size(), out, s);
+}
+
 // Uploads the row-concatenation of `parts` (each rows_i x cols fp32) as bf16.
 int upload_bf16_concat(DeviceArena &a, const std::vector<std::pair<const float *, size_t>> &parts, size_t cols,
                        bf16 **out, cudaStream_t s) {
@@ -181,7 +193,8 @@ struct dtts_dit {
         tu_in{256, 4, 1};
     float *t_w1 = nullptr, *t_b1 = nullptr, *t_w2 = nullptr, *t_b2 = nullptr;
     float *spk_w1 = nullptr, *spk_b1 = nullptr, *spk_lw = nullptr, *spk_lb = nullptr;
-    float *out_w = nullptr, *out_b = nullptr, *coord_w = nullptr, *coord_b = nullptr;
+    // output and coordinate projections stored transposed: out_wt [1024][128], coord_wt [128][1024]
+    float *out_wt = nullptr, *out_b = nullptr, *coord_wt = nullptr, *coord_b = nullptr;
     int *d_err = nullptr;
     bool has_in = false, has_out = false;
     int rope_mode = ROPE_HALF;   // DTTS_ROPE_HALF / DTTS_ROPE_ADJACENT
@@ -396,7 +409,7 @@ int dtts_dit::enqueue_forward(int rows, int L, int P) {
     const long long oo = (long long)n_layers * kAdaPerLayer;
     launches++;
     TlScope tl_scope(this, TL_OUT_HEAD);
-    launch_out_head(h, rows, L, P, ada_cur + oo, ada_cur + oo + kD, n_ada, rows_per_ada, out_w, out_b, vel, d_err,
+    launch_out_head(h, rows, L, P, ada_cur + oo, ada_cur + oo + kD, n_ada, rows_per_ada, out_wt, out_b, vel, d_err,
                     stream);
     DTTS_CUDA(cudaGetLastError());
     return DTTS_OK;
@@ -442,7 +455,7 @@ int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
     launches++;
     {
         TlScope tl_scope(this, TL_EULER);
-        launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 0, coord_w, coord_b, x_in, L,
+        launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 0, coord_wt, coord_b, x_in, L,
                          stream);
     }
     rows_per_ada = 2;
@@ -452,7 +465,7 @@ int dtts_dit::enqueue_solve(const dtts_solve_args *a) {
         if (st) return st;
         launches++;
         TlScope tl_scope(this, TL_EULER);
-        launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 1, coord_w, coord_b, x_in, L,
+        launch_cfg_euler(vel, z, a->n_utt, a->patch, a->cfg_scale, a->cfg_form, dt, 1, coord_wt, coord_b, x_in, L,
                          stream);
     }
     DTTS_CUDA(cudaGetLastError());
@@ -548,9 +561,10 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     if ((st = upload_f32(e->wts, w->spk_b1, kD, &e->spk_b1, s))) return st;
     if ((st = upload_f32(e->wts, w->spk_ln_w, kD, &e->spk_lw, s))) return st;
     if ((st = upload_f32(e->wts, w->spk_ln_b, kD, &e->spk_lb, s))) return st;
-    if ((st = upload_f32(e->wts, w->out_w, (size_t)kLat * kD, &e->out_w, s))) return st;
+    std::vector<float> out_wt_host, coord_wt_host;
+    if ((st = upload_f32_transposed(e->wts, w->out_w, kLat, kD, &e->out_wt, s, out_wt_host))) return st;
     if ((st = upload_f32(e->wts, w->out_b, kLat, &e->out_b, s))) return st;
-    if ((st = upload_f32(e->wts, w->coord_w, (size_t)kD * kLat, &e->coord_w, s))) return st;
+    if ((st = upload_f32_transposed(e->wts, w->coord_w, kD, kLat, &e->coord_wt, s, coord_wt_host))) return st;
     if ((st = upload_f32(e->wts, w->coord_b, kD, &e->coord_b, s))) return st;
     DTTS_CUDA(cudaStreamSynchronize(s));
     if ((st = e->build_weight_maps())) return st;
@@ -643,7 +657,7 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
     DTTS_CHECK(a->layout == DTTS_LAYOUT_FM_MASK || a->layout == DTTS_LAYOUT_FULL, DTTS_ERR_ARG, "bad layout");
     DTTS_CHECK(a->mem == DTTS_MEM_HOST || a->mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
     DTTS_CHECK(!a->spk || (e->spk_w1 && e->spk_lw), DTTS_ERR_ARG, "speaker vectors given but xvec_proj weights absent");
-    DTTS_CHECK(e->has_in && e->has_out && e->coord_w && e->t_w1 && e->t_w2, DTTS_ERR_ARG,
+    DTTS_CHECK(e->has_in && e->has_out && e->coord_wt && e->t_w1 && e->t_w2, DTTS_ERR_ARG,
                "model lacks input/output/coordinate/time-embedding weights needed by the solve");
     DeviceGuard g(e->device);
     const int rows = 2 * a->n_utt, L = a->fm_len + a->patch;

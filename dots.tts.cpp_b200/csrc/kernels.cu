@@ -738,23 +738,24 @@ void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf1
 }
 
 // =========================================================================
-// DiT output head: 8 tokens per block.  LN + modulation of the 8 token rows
-// into shared memory, then 128 outputs, each warp owning 16 output rows of
-// W_out (read once, coalesced) against the 8 tokens.
+// DiT output head: 8 tokens per block.  Each warp normalises and modulates one
+// token row into shared memory; then thread (kg, c4) accumulates outputs
+// 4c4..4c4+3 of the 8 tokens over k in [128 kg, 128 kg + 128), reading
+// W_out^T [1024][128] as coalesced float4 rows, and the 8 K-group partials are
+// summed through shared memory.
 // =========================================================================
 constexpr int kOutTok = 8;
 
 __global__ void __launch_bounds__(256) out_head_kernel(const float *__restrict__ h, int rows, int L, int P,
                                                        const float *__restrict__ shift,
                                                        const float *__restrict__ scale, long long ada_ld,
-                                                       int rows_per_ada, const float *__restrict__ w,
+                                                       int rows_per_ada, const float *__restrict__ wt,
                                                        const float *__restrict__ b, float *__restrict__ vel,
                                                        int *err) {
-    __shared__ float u[kOutTok][kD];
+    __shared__ __align__(16) float u[kOutTok][kD];   // modulated rows; later the K-group partials
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tok0 = blockIdx.x * kOutTok;
     const int ntok = rows * P;
-    // each warp normalises one token row
     {
         const int tk = tok0 + warp;
         if (tk < ntok) {
@@ -775,90 +776,138 @@ __global__ void __launch_bounds__(256) out_head_kernel(const float *__restrict__
             const long long ar = (long long)(r / rows_per_ada) * ada_ld;
             const float4 *sh = reinterpret_cast<const float4 *>(shift + ar);
             const float4 *sc = reinterpret_cast<const float4 *>(scale + ar);
+            float4 *ur = reinterpret_cast<float4 *>(u[warp]);
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int c4 = lane + 32 * j;
                 const float4 a = __ldg(sh + c4), g = __ldg(sc + c4);
-                u[warp][4 * c4 + 0] = (v[j].x - mean) * inv * (1.0f + g.x) + a.x;
-                u[warp][4 * c4 + 1] = (v[j].y - mean) * inv * (1.0f + g.y) + a.y;
-                u[warp][4 * c4 + 2] = (v[j].z - mean) * inv * (1.0f + g.z) + a.z;
-                u[warp][4 * c4 + 3] = (v[j].w - mean) * inv * (1.0f + g.w) + a.w;
+                ur[c4] = make_float4((v[j].x - mean) * inv * (1.0f + g.x) + a.x,
+                                     (v[j].y - mean) * inv * (1.0f + g.y) + a.y,
+                                     (v[j].z - mean) * inv * (1.0f + g.z) + a.z,
+                                     (v[j].w - mean) * inv * (1.0f + g.w) + a.w);
             }
+        } else {
+            float4 *ur = reinterpret_cast<float4 *>(u[warp]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) ur[lane + 32 * j] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     __syncthreads();
-    for (int oo = 0; oo < kLat / 8; oo++) {
-        const int o = warp * (kLat / 8) + oo;
-        const float *wr = w + (long long)o * kD;
-        float acc[kOutTok] = {};
-#pragma unroll 4
-        for (int i = lane; i < kD; i += 32) {
-            const float wv = wr[i];
+    const int c4 = lane, kg = warp;
+    float4 acc[kOutTok];
 #pragma unroll
-            for (int t = 0; t < kOutTok; t++) acc[t] += wv * u[t][i];
+    for (int t = 0; t < kOutTok; t++) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *w4 = reinterpret_cast<const float4 *>(wt) + c4;
+#pragma unroll 16
+    for (int kk = 0; kk < kD / 8; kk++) {
+        const int k = kg * (kD / 8) + kk;
+        const float4 w = __ldg(w4 + (long long)k * (kLat / 4));
+#pragma unroll
+        for (int t = 0; t < kOutTok; t++) {
+            const float xv = u[t][k];
+            acc[t].x += w.x * xv; acc[t].y += w.y * xv; acc[t].z += w.z * xv; acc[t].w += w.w * xv;
         }
+    }
+    __syncthreads();   // every thread is done with u: reuse it for the partials [kg][t][c4]
+    float4 *part = reinterpret_cast<float4 *>(&u[0][0]);
 #pragma unroll
-        for (int t = 0; t < kOutTok; t++) acc[t] = warp_sum(acc[t]);
-        if (lane < kOutTok && tok0 + lane < ntok) {
-            float y = 0.f;
+    for (int t = 0; t < kOutTok; t++) part[(kg * kOutTok + t) * 32 + c4] = acc[t];
+    __syncthreads();
+    {
+        const int t = warp;
+        float4 y = part[t * 32 + c4];
 #pragma unroll
-            for (int t = 0; t < kOutTok; t++) y = (lane == t) ? acc[t] : y;
-            y += b ? b[o] : 0.f;
-            if (!isfinite(y) && err) atomicCAS(err, 0, DEVERR_NONFINITE);
-            vel[(long long)(tok0 + lane) * kLat + o] = y;
+        for (int g = 1; g < 8; g++) {
+            const float4 o = part[(g * kOutTok + t) * 32 + c4];
+            y.x += o.x; y.y += o.y; y.z += o.z; y.w += o.w;
+        }
+        if (b) {
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(b) + c4);
+            y.x += bb.x; y.y += bb.y; y.z += bb.z; y.w += bb.w;
+        }
+        const int tok = tok0 + t;
+        if (tok < ntok) {
+            if (err && !(isfinite(y.x) && isfinite(y.y) && isfinite(y.z) && isfinite(y.w)))
+                atomicCAS(err, 0, DEVERR_NONFINITE);
+            reinterpret_cast<float4 *>(vel + (long long)tok * kLat)[c4] = y;
         }
     }
 }
 
 void launch_out_head(const float *h, int rows, int L, int P, const float *shift, const float *scale,
-                     long long ada_ld, int rows_per_ada, const float *w_out, const float *b_out, float *vel, int *err,
+                     long long ada_ld, int rows_per_ada, const float *w_out_t, const float *b_out, float *vel, int *err,
                      cudaStream_t s) {
     const int ntok = rows * P;
     out_head_kernel<<<(ntok + kOutTok - 1) / kOutTok, 256, 0, s>>>(h, rows, L, P, shift, scale, ada_ld, rows_per_ada,
-                                                                   w_out, b_out, vel, err);
+                                                                   w_out_t, b_out, vel, err);
 }
 
-// CFG combine + Euler update + coordinate projection, one block per
-// (utterance, frame): 8 warps x 128 outputs, lanes split the 128 inputs.
-__global__ void __launch_bounds__(256) cfg_euler_kernel(const float *__restrict__ vel, float *__restrict__ z, int P,
-                                                        float cfg_scale, int cfg_form, float dt, int update,
-                                                        const float *__restrict__ wc, const float *__restrict__ bc,
+// CFG combine + Euler update + coordinate projection, kEulerRows z rows
+// (utterance, frame) per block.  The block updates its own rows of z in place
+// (each row belongs to one block), then thread t computes outputs 4t..4t+3 of
+// every row from coordinate_proj^T [128][1024] read as coalesced float4 rows.
+constexpr int kEulerRows = 4;
+
+__global__ void __launch_bounds__(256) cfg_euler_kernel(const float *__restrict__ vel, float *__restrict__ z, int nrows,
+                                                        int P, float cfg_scale, int cfg_form, float dt, int update,
+                                                        const float *__restrict__ wct, const float *__restrict__ bc,
                                                         bf16 *__restrict__ x_in, int L) {
-    __shared__ float zs[kLat];
-    const int u = blockIdx.x / P, p = blockIdx.x % P;
-    float *zp = z + ((long long)u * P + p) * kLat;
-    if (threadIdx.x < kLat) {
-        float zv = zp[threadIdx.x];
-        if (update) {
-            const float vc = vel[((long long)(2 * u) * P + p) * kLat + threadIdx.x];
-            const float vu = vel[((long long)(2 * u + 1) * P + p) * kLat + threadIdx.x];
-            const float v = cfg_form == 0 ? vc + cfg_scale * (vc - vu) : vu + cfg_scale * (vc - vu);
-            zv += v * dt;
-            zp[threadIdx.x] = zv;
+    __shared__ float zs[kEulerRows][kLat];
+    const int r0 = blockIdx.x * kEulerRows;
+    for (int i = threadIdx.x; i < kEulerRows * kLat; i += blockDim.x) {
+        const int rr = i / kLat, c = i % kLat, r = r0 + rr;
+        float zv = 0.f;
+        if (r < nrows) {
+            const int u = r / P, p = r % P;
+            float *zp = z + (long long)r * kLat;
+            zv = zp[c];
+            if (update) {
+                const float vc = vel[((long long)(2 * u) * P + p) * kLat + c];
+                const float vu = vel[((long long)(2 * u + 1) * P + p) * kLat + c];
+                const float v = cfg_form == 0 ? vc + cfg_scale * (vc - vu) : vu + cfg_scale * (vc - vu);
+                zv += v * dt;
+                zp[c] = zv;
+            }
         }
-        zs[threadIdx.x] = zv;
+        zs[rr][c] = zv;
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float z0 = zs[lane], z1 = zs[lane + 32], z2 = zs[lane + 64], z3 = zs[lane + 96];
-    const long long tok = L - P + p;
-    bf16 *xc = x_in + ((long long)(2 * u) * L + tok) * kD;
-    bf16 *xu = x_in + ((long long)(2 * u + 1) * L + tok) * kD;
-    for (int o = warp; o < kD; o += 8) {
-        const float *wr = wc + (long long)o * kLat;
-        float acc = wr[lane] * z0 + wr[lane + 32] * z1 + wr[lane + 64] * z2 + wr[lane + 96] * z3;
-        acc = warp_sum(acc);
-        if (lane == 0) {
-            const bf16 y = __float2bfloat16_rn(acc + (bc ? bc[o] : 0.f));
-            xc[o] = y;
-            xu[o] = y;
+    const int o4 = threadIdx.x;   // outputs 4 o4 .. 4 o4 + 3
+    float4 acc[kEulerRows];
+#pragma unroll
+    for (int rr = 0; rr < kEulerRows; rr++) acc[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *w4 = reinterpret_cast<const float4 *>(wct) + o4;
+#pragma unroll 16
+    for (int k = 0; k < kLat; k++) {
+        const float4 w = __ldg(w4 + (long long)k * (kD / 4));
+#pragma unroll
+        for (int rr = 0; rr < kEulerRows; rr++) {
+            const float xv = zs[rr][k];
+            acc[rr].x += w.x * xv; acc[rr].y += w.y * xv; acc[rr].z += w.z * xv; acc[rr].w += w.w * xv;
         }
+    }
+    const float4 bb = bc ? __ldg(reinterpret_cast<const float4 *>(bc) + o4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int rr = 0; rr < kEulerRows; rr++) {
+        const int r = r0 + rr;
+        if (r >= nrows) break;
+        const int u = r / P, p = r % P;
+        const long long tok = L - P + p;
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc[rr].x + bb.x, acc[rr].y + bb.y);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(acc[rr].z + bb.z, acc[rr].w + bb.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t *>(&lo);
+        pk.y = *reinterpret_cast<uint32_t *>(&hi);
+        *reinterpret_cast<uint2 *>(x_in + ((long long)(2 * u) * L + tok) * kD + 4 * o4) = pk;
+        *reinterpret_cast<uint2 *>(x_in + ((long long)(2 * u + 1) * L + tok) * kD + 4 * o4) = pk;
     }
 }
 
 void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_scale, int cfg_form, float dt,
-                      int update, const float *w_coord, const float *b_coord, bf16 *x_in, int L, cudaStream_t s) {
-    cfg_euler_kernel<<<n_utt * P, 256, 0, s>>>(vel, z, P, cfg_scale, cfg_form, dt, update, w_coord, b_coord, x_in, L);
+                      int update, const float *w_coord_t, const float *b_coord, bf16 *x_in, int L, cudaStream_t s) {
+    const int nrows = n_utt * P;
+    cfg_euler_kernel<<<(nrows + kEulerRows - 1) / kEulerRows, kD / 4, 0, s>>>(
+        vel, z, nrows, P, cfg_scale, cfg_form, dt, update, w_coord_t, b_coord, x_in, L);
 }
 
 // =========================================================================

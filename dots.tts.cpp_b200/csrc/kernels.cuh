@@ -88,14 +88,16 @@ void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf1
 
 // ------------------------------------------------------------ DiT output head
 // vel[r][p] = W_out (LN(h[r, L-P+p]) (1 + scale) + shift) + b_out, with the
-// modulation of row r at shift/scale + (r / rows_per_ada) * ada_ld
+// modulation of row r at shift/scale + (r / rows_per_ada) * ada_ld; w_out_t is
+// W_out transposed, [1024][128]
 void launch_out_head(const float *h, int rows, int L, int P, const float *shift, const float *scale,
-                     long long ada_ld, int rows_per_ada, const float *w_out, const float *b_out, float *vel, int *err,
+                     long long ada_ld, int rows_per_ada, const float *w_out_t, const float *b_out, float *vel, int *err,
                      cudaStream_t s);
 // CFG combine + Euler update + coord_proj of the new z into the noise tokens of
-// both rows of each utterance (update = 0: only the coord_proj of z).
+// both rows of each utterance (update = 0: only the coord_proj of z); w_coord_t
+// is coordinate_proj's weight transposed, [128][1024]
 void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_scale, int cfg_form, float dt,
-                      int update, const float *w_coord, const float *b_coord, bf16 *x_in, int L,
+                      int update, const float *w_coord_t, const float *b_coord, bf16 *x_in, int L,
                       cudaStream_t s);
 
 // ------------------------------------------------------------ PatchEncoder

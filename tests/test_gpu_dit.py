@@ -150,7 +150,7 @@ def test_solve_timeline_counts_and_result(eng18, w18):
     """The in-place launch timeline used for the benchmark's roofline: launch
     counts per kind follow the solve's structure, the captured solve computes
     the same result as an ordinary one, and the per-kind totals add up to the
-    solve's own device time."""
+    solve's own device time plus the event latency per launch."""
     import torch
     n_utt, fm_len, nfe = 8, 60, 3
     fc, fu = synth.fm_history(14, n_utt, fm_len, w18)
@@ -185,4 +185,7 @@ def test_solve_timeline_counts_and_result(eng18, w18):
     finally:
         eng18.set_stream(None)
     total = sum(v[0] for v in tl.values())
-    assert 0.7 * solve_us < total < 1.3 * solve_us, (total, solve_us)
+    launches = sum(v[1] for v in tl.values())
+    # each timed launch also carries the latency its two event nodes add (a few
+    # microseconds), which dominates at this small size
+    assert 0.7 * solve_us < total < 1.1 * solve_us + 6.0 * launches, (total, solve_us, launches)
