@@ -123,6 +123,12 @@ const char *dtts_status_string(int s) {
 
 const char *dtts_last_error(void) { return dtts::last_error(); }
 
+int dtts_fp8_quantize_rows(const float *w, int rows, int cols, uint8_t *q, float *scale) {
+    DTTS_CHECK(w && q && scale && rows >= 1 && cols >= 1, DTTS_ERR_ARG, "bad fp8 quantisation arguments");
+    dtts::e4m3_quantize_rows(w, (size_t)rows, (size_t)cols, q, scale, nullptr);
+    return DTTS_OK;
+}
+
 int dtts_device_count(int *n) {
     if (!n) return DTTS_ERR_ARG;
     *n = 0;

@@ -14,6 +14,7 @@
 #include "kernels.cuh"
 #include "runtime.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -180,6 +181,13 @@ struct dtts_dit {
         bf16 *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr;
         float *bo = nullptr, *b1 = nullptr, *b2 = nullptr, *qn = nullptr, *kn = nullptr;
         CUtensorMap tqkv, to, t1, t2;
+        // FP8 path: e4m3 weights with one scale per output channel, and the
+        // bounds that size the attention-output and GELU-output scales
+        uint8_t *qkv8 = nullptr, *o8 = nullptr, *w18 = nullptr, *w28 = nullptr;
+        float *sqkv = nullptr, *so = nullptr, *s1 = nullptr, *s2 = nullptr;
+        float vbound = 0.f;    // largest |row| of the dequantised Wv
+        float w1n = 0.f;       // largest |row| of the dequantised W1
+        float b1max = 0.f;     // largest |b1|
     };
     std::vector<Layer> layers;
     bf16 *w_ada = nullptr, *w_in = nullptr;
@@ -214,6 +222,11 @@ struct dtts_dit {
     uint8_t *mask = nullptr;
     uint32_t *mask_bits = nullptr;   // [L][ceil(L/32)]
     CUtensorMap t_x_in, t_act, t_att, t_ffn, t_acond, t_h;
+    // FP8 path workspace: e4m3 operands and their per-row scales
+    uint8_t *act8 = nullptr, *att8 = nullptr, *ffn8 = nullptr;
+    float *s_act = nullptr, *s_att = nullptr, *s_ffn = nullptr, *inv_ffn = nullptr, *unorm = nullptr;
+    CUtensorMap t_act8, t_att8, t_ffn8;
+    bool fp8() const { return dtype == DTTS_DTYPE_FP8; }
 
     // shapes of the last forward (for profiling) and launch accounting
     int last_rows = 0, last_L = 0, last_P = 0;
@@ -306,12 +319,27 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
     rope = (float2 *)A((size_t)cap_L * 32 * sizeof(float2));
     mask = (uint8_t *)A((size_t)cap_L * cap_L);
     mask_bits = (uint32_t *)A((size_t)cap_L * ((cap_L + 31) / 32) * 4);
+    if (fp8()) {
+        act8 = (uint8_t *)A(T * kD);
+        att8 = (uint8_t *)A(T * kD);
+        ffn8 = (uint8_t *)A(T * kF);
+        s_act = (float *)A(T * 4);
+        s_att = (float *)A(T * 4);
+        s_ffn = (float *)A(T * 4);
+        inv_ffn = (float *)A(T * 4);
+        unorm = (float *)A(T * 4);
+    }
     for (void *p : ws.ptrs)
         if (!p) { set_error("workspace allocation failed (%lld tokens)", tok); cap_tok = cap_rows = cap_L = 0; ws.free_all(); return DTTS_ERR_OOM; }
     bool ok = make_tmap_bf16(&t_x_in, x_in, T, kD, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
               make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
               make_tmap_bf16(&t_acond, a_cond, R * (size_t)cap_nfe, kD, 128) && make_tmap_f32_resid(&t_h, h, T, kD);
     DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace buffer");
+    if (fp8()) {
+        ok = make_tmap_e4m3(&t_act8, act8, T, kD, 128) && make_tmap_e4m3(&t_att8, att8, T, kD, 128) &&
+             make_tmap_e4m3(&t_ffn8, ffn8, T, kF, 128);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for an e4m3 workspace buffer");
+    }
     return DTTS_OK;
 }
 
@@ -319,9 +347,15 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
 int dtts_dit::build_weight_maps() {
     for (int l = 0; l < n_layers; l++) {
         Layer &L = layers[l];
-        bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, tu_qkv.bn) &&
-                  make_tmap_bf16(&L.to, L.wo, kD, kD, tu_o.bn) && make_tmap_bf16(&L.t1, L.w1, kF, kD, tu_ffn1.bn) &&
-                  make_tmap_bf16(&L.t2, L.w2, kD, kF, tu_ffn2.bn);
+        bool ok;
+        if (fp8())
+            ok = make_tmap_e4m3(&L.tqkv, L.qkv8, 3 * kD, kD, tu_qkv.bn) &&
+                 make_tmap_e4m3(&L.to, L.o8, kD, kD, tu_o.bn) && make_tmap_e4m3(&L.t1, L.w18, kF, kD, tu_ffn1.bn) &&
+                 make_tmap_e4m3(&L.t2, L.w28, kD, kF, tu_ffn2.bn);
+        else
+            ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, tu_qkv.bn) &&
+                 make_tmap_bf16(&L.to, L.wo, kD, kD, tu_o.bn) && make_tmap_bf16(&L.t1, L.w1, kF, kD, tu_ffn1.bn) &&
+                 make_tmap_bf16(&L.t2, L.w2, kD, kF, tu_ffn2.bn);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for block %d", l);
     }
     bool ok = make_tmap_bf16(&t_ada, w_ada, n_ada, kD, tu_ada.bn) && make_tmap_bf16(&t_in, w_in, kD, kD, tu_in.bn);
@@ -342,11 +376,21 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
         case 6: {
             const long long off = kind == 5 ? 0 : 3 * kD;
             launches++;
+            if (fp8()) {
+                if (kind == 5)
+                    launch_ln_modulate_f8(h, act8, M, ada_l + off, ada_l + off + kD, n_ada, tpr, s_act, unorm, nullptr,
+                                          nullptr, 0.f, 0.f, stream);
+                else
+                    launch_ln_modulate_f8(h, act8, M, ada_l + off, ada_l + off + kD, n_ada, tpr, s_act, nullptr, s_ffn,
+                                          inv_ffn, Ly.w1n, Ly.b1max, stream);
+                return DTTS_OK;
+            }
             launch_ln_modulate(h, act, M, ada_l + off, ada_l + off + kD, n_ada, tpr, stream);
             return DTTS_OK;
         }
         case 0: {
-            GemmOp op = make_op(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err, tu_qkv);
+            GemmOp op = make_op(fp8() ? t_act8 : t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err, tu_qkv);
+            if (fp8()) { op.f8 = 1; op.ep.row_scale = s_act; op.ep.col_scale = Ly.sqkv; }
             op.ep.q = q; op.ep.k = k; op.ep.v = v;
             op.ep.ldq = kD; op.ep.ldkv = kD;
             op.ep.tok_per_row = L; op.ep.kv_cap = L; op.ep.kv_start = 0;
@@ -361,24 +405,33 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             a.mask = last_mask ? mask : nullptr;
             a.mask_bits = last_mask ? mask_bits : nullptr;
             a.scale = 1.0f / sqrtf(64.0f);
+            if (fp8()) { a.o8 = att8; a.o_scale = s_att; a.unorm = unorm; a.vbound = Ly.vbound; }
             launches++;
             launch_attention_bf16(a, stream);
             return DTTS_OK;
         }
         case 1: {
-            GemmOp op = make_op(t_att, Ly.to, M, kD, kD, EPI_RESID_GATED, d_err, tu_o);
+            GemmOp op = make_op(fp8() ? t_att8 : t_att, Ly.to, M, kD, kD, EPI_RESID_GATED, d_err, tu_o);
+            if (fp8()) { op.f8 = 1; op.ep.row_scale = s_att; op.ep.col_scale = Ly.so; }
             op.tr = t_h;
             op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
             op.ep.gate = ada_l + 2 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = tpr;
             return gemm(op);
         }
         case 2: {
+            if (fp8()) {
+                GemmOp op = make_op(t_act8, Ly.t1, M, kF, kD, EPI_GELU_F8, d_err, tu_ffn1);
+                op.f8 = 1; op.ep.row_scale = s_act; op.ep.col_scale = Ly.s1; op.ep.out_inv = inv_ffn;
+                op.ep.bias = Ly.b1; op.ep.out = ffn8; op.ep.ldo = kF;
+                return gemm(op);
+            }
             GemmOp op = make_op(t_act, Ly.t1, M, kF, kD, EPI_GELU_BF16, d_err, tu_ffn1);
             op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
             return gemm(op);
         }
         case 3: {
-            GemmOp op = make_op(t_ffn, Ly.t2, M, kD, kF, EPI_RESID_GATED, d_err, tu_ffn2);
+            GemmOp op = make_op(fp8() ? t_ffn8 : t_ffn, Ly.t2, M, kD, kF, EPI_RESID_GATED, d_err, tu_ffn2);
+            if (fp8()) { op.f8 = 1; op.ep.row_scale = s_ffn; op.ep.col_scale = Ly.s2; }
             op.tr = t_h;
             op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
             op.ep.gate = ada_l + 5 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = tpr;
@@ -487,6 +540,47 @@ int dtts_dit::finish(bool host_wait) {
     return DTTS_OK;
 }
 
+// FP8 weights of one block: e4m3 with one scale per output channel (the rows
+// of the PyTorch [out][in] matrices), plus the bounds the FP8 forward needs:
+// the largest dequantised row norm of Wv and of W1, and max |b1|.
+int upload_block_e4m3(DeviceArena &a, const dtts_dit_block_weights &b, dtts_dit::Layer &L, cudaStream_t s) {
+    struct Part { const float *w; size_t rows, cols; };
+    auto upload = [&](std::initializer_list<Part> parts, uint8_t **dq, float **dsc, float *max_norm_last) -> int {
+        size_t rows = 0, cols = parts.begin()->cols;
+        for (const Part &p : parts) rows += p.rows;
+        std::vector<uint8_t> q(rows * cols);
+        std::vector<float> sc(rows), nrm(rows);
+        size_t r0 = 0;
+        for (const Part &p : parts) {
+            e4m3_quantize_rows(p.w, p.rows, p.cols, q.data() + r0 * cols, sc.data() + r0, nrm.data() + r0);
+            r0 += p.rows;
+        }
+        if (max_norm_last) {   // bound over the rows of the last part
+            const Part &p = *(parts.end() - 1);
+            float m = 0.f;
+            for (size_t r = rows - p.rows; r < rows; r++) m = std::max(m, nrm[r]);
+            *max_norm_last = m;
+        }
+        void *d = a.alloc(q.size()), *ds = a.alloc(sc.size() * 4);
+        if (!d || !ds) { set_error("cudaMalloc of e4m3 weights failed"); return DTTS_ERR_OOM; }
+        DTTS_CUDA(cudaMemcpyAsync(d, q.data(), q.size(), cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaMemcpyAsync(ds, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice, s));
+        DTTS_CUDA(cudaStreamSynchronize(s));   // host copies go out of scope
+        *dq = static_cast<uint8_t *>(d);
+        *dsc = static_cast<float *>(ds);
+        return DTTS_OK;
+    };
+    int st;
+    if ((st = upload({{b.wq, kD, kD}, {b.wk, kD, kD}, {b.wv, kD, kD}}, &L.qkv8, &L.sqkv, &L.vbound))) return st;
+    if ((st = upload({{b.wo, kD, kD}}, &L.o8, &L.so, nullptr))) return st;
+    if ((st = upload({{b.w1, kF, kD}}, &L.w18, &L.s1, &L.w1n))) return st;
+    if ((st = upload({{b.w2, kD, kF}}, &L.w28, &L.s2, nullptr))) return st;
+    L.b1max = 0.f;
+    if (b.b1)
+        for (int j = 0; j < kF; j++) L.b1max = std::max(L.b1max, std::fabs(b.b1[j]));
+    return DTTS_OK;
+}
+
 // =========================================================================
 // C ABI
 // =========================================================================
@@ -496,7 +590,8 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     DTTS_CHECK(w && out, DTTS_ERR_ARG, "null argument");
     *out = nullptr;
     DTTS_CHECK(w->n_layers >= 1 && w->n_layers <= 64 && w->blocks, DTTS_ERR_ARG, "n_layers %d invalid", w->n_layers);
-    DTTS_CHECK(dtype == DTTS_DTYPE_BF16, DTTS_ERR_UNSUPPORTED, "DiT dtype %d not supported by this build", dtype);
+    DTTS_CHECK(dtype == DTTS_DTYPE_BF16 || dtype == DTTS_DTYPE_FP8, DTTS_ERR_UNSUPPORTED,
+               "DiT dtype %d not supported (bf16 or fp8)", dtype);
     // Global weights are checked by the calls that need them: a model with
     // only blocks serves dtts_dit_blocks (manual_dit_block).
     for (int l = 0; l < w->n_layers; l++) {
@@ -510,6 +605,12 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     DeviceGuard g(device);
     std::unique_ptr<dtts_dit> e(new dtts_dit());
     e->device = device; e->dtype = dtype; e->num_sms = nsm; e->n_layers = w->n_layers;
+    if (dtype == DTTS_DTYPE_FP8) {
+        // e4m3 mainloops take half the time, so the epilogue decides: eight
+        // epilogue warps for the O and FFN1 tiles (sweep at 8192 tokens)
+        e->tu_o = {256, 8, 1};
+        e->tu_ffn1 = {256, 8, 1};
+    }
     DTTS_CUDA(cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking));
     e->stream = e->own_stream;
     DTTS_CUDA(gemm_prepare_attributes());
@@ -523,10 +624,14 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     for (int l = 0; l < w->n_layers; l++) {
         const dtts_dit_block_weights &b = w->blocks[l];
         dtts_dit::Layer &L = e->layers[l];
-        if ((st = upload_bf16_concat(e->wts, {{b.wq, kD}, {b.wk, kD}, {b.wv, kD}}, kD, &L.wqkv, s))) return st;
-        if ((st = upload_bf16_concat(e->wts, {{b.wo, kD}}, kD, &L.wo, s))) return st;
-        if ((st = upload_bf16_concat(e->wts, {{b.w1, kF}}, kD, &L.w1, s))) return st;
-        if ((st = upload_bf16_concat(e->wts, {{b.w2, kD}}, kF, &L.w2, s))) return st;
+        if (dtype == DTTS_DTYPE_FP8) {
+            if ((st = upload_block_e4m3(e->wts, b, L, s))) return st;
+        } else {
+            if ((st = upload_bf16_concat(e->wts, {{b.wq, kD}, {b.wk, kD}, {b.wv, kD}}, kD, &L.wqkv, s))) return st;
+            if ((st = upload_bf16_concat(e->wts, {{b.wo, kD}}, kD, &L.wo, s))) return st;
+            if ((st = upload_bf16_concat(e->wts, {{b.w1, kF}}, kD, &L.w1, s))) return st;
+            if ((st = upload_bf16_concat(e->wts, {{b.w2, kD}}, kF, &L.w2, s))) return st;
+        }
         if ((st = upload_f32(e->wts, b.bo, kD, &L.bo, s))) return st;
         if ((st = upload_f32(e->wts, b.b1, kF, &L.b1, s))) return st;
         if ((st = upload_f32(e->wts, b.b2, kD, &L.b2, s))) return st;

@@ -24,14 +24,28 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int BN, int EPI, int NW>
+template <int BN, int EPI, int NW, int F8 = 0>
 cudaError_t launch_one(const GemmOp &op, int num_sms, cudaStream_t s) {
-    using Cfg = GemmCfg<BN, NW, EPI>;
+    using Cfg = GemmCfg<BN, NW, EPI, F8>;
     const int units = ((op.M + Cfg::BM - 1) / Cfg::BM) * (op.N / BN) * (op.ep.ksplit > 0 ? op.ep.ksplit : 1);
     const int grid = units < num_sms ? units : num_sms;
-    gemm_tc_kernel<BN, EPI, NW><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(op.ta, op.tb, op.tr, op.M, op.N, op.K,
-                                                                            op.ep);
+    gemm_tc_kernel<BN, EPI, NW, F8><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(op.ta, op.tb, op.tr, op.M, op.N,
+                                                                                op.K, op.ep);
     return cudaGetLastError();
+}
+
+// e4m3 operands: the three epilogues of the DiT block's FP8 path, and fp32 output
+template <int BN, int NW>
+cudaError_t dispatch_epi_f8(const GemmOp &op, int num_sms, cudaStream_t s) {
+    switch (op.epi) {
+        case EPI_QKV: return launch_one<BN, EPI_QKV, NW, 1>(op, num_sms, s);
+        case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED, NW, 1>(op, num_sms, s);
+        case EPI_F32: return launch_one<BN, EPI_F32, NW, 1>(op, num_sms, s);
+        case EPI_GELU_F8:
+            if constexpr (BN % 128 == 0) return launch_one<BN, EPI_GELU_F8, NW, 1>(op, num_sms, s);
+            return cudaErrorInvalidValue;
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 template <int BN, int NW>
@@ -48,10 +62,20 @@ cudaError_t dispatch_epi(const GemmOp &op, int num_sms, cudaStream_t s) {
     }
 }
 
-template <int BN, int NW, int EPI>
+template <int BN, int NW, int EPI, int F8 = 0>
 cudaError_t prepare_one() {
-    return cudaFuncSetAttribute((const void *)gemm_tc_kernel<BN, EPI, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                GemmCfg<BN, NW, EPI>::SMEM_BYTES);
+    return cudaFuncSetAttribute((const void *)gemm_tc_kernel<BN, EPI, NW, F8>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, NW, EPI, F8>::SMEM_BYTES);
+}
+
+template <int BN, int NW>
+cudaError_t prepare_bn_f8() {
+    cudaError_t e;
+    if ((e = prepare_one<BN, NW, EPI_QKV, 1>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_F32, 1>()) != cudaSuccess) return e;
+    if constexpr (BN % 128 == 0)
+        if ((e = prepare_one<BN, NW, EPI_GELU_F8, 1>()) != cudaSuccess) return e;
+    return prepare_one<BN, NW, EPI_RESID_GATED, 1>();
 }
 
 template <int BN, int NW>
@@ -77,7 +101,28 @@ cudaError_t gemm_prepare_attributes() {
     if ((e = prepare_bn<256, 4>()) != cudaSuccess) return e;
     if ((e = prepare_bn<128, 8>()) != cudaSuccess) return e;
     if ((e = prepare_bn<192, 8>()) != cudaSuccess) return e;
-    return prepare_bn<256, 8>();
+    if ((e = prepare_bn<256, 8>()) != cudaSuccess) return e;
+    if ((e = prepare_bn_f8<128, 4>()) != cudaSuccess) return e;
+    if ((e = prepare_bn_f8<192, 4>()) != cudaSuccess) return e;
+    if ((e = prepare_bn_f8<256, 4>()) != cudaSuccess) return e;
+    if ((e = prepare_bn_f8<128, 8>()) != cudaSuccess) return e;
+    if ((e = prepare_bn_f8<192, 8>()) != cudaSuccess) return e;
+    return prepare_bn_f8<256, 8>();
+}
+
+bool make_tmap_e4m3(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
+                    unsigned int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || !base || rows == 0 || cols % 128 != 0 || box_rows == 0 || box_rows > 256) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};      // bytes between rows
+    cuuint32_t box[2] = {128, box_rows}; // 128 e4m3 = 128 bytes: one swizzle atom row
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 bool make_tmap_f32_resid(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols) {
@@ -111,9 +156,24 @@ bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, u
 
 cudaError_t launch_gemm(const GemmOp &op, int num_sms, cudaStream_t s) {
     const int ks = op.ep.ksplit > 0 ? op.ep.ksplit : 1;
-    if (op.M < 1 || op.K < 64 * ks || op.K % (64 * ks) != 0 || op.N % op.bn != 0) return cudaErrorInvalidValue;
+    const int bk = op.f8 ? 128 : 64;
+    if (op.M < 1 || op.K < bk * ks || op.K % (bk * ks) != 0 || op.N % op.bn != 0) return cudaErrorInvalidValue;
     if (ks > 1 && !is_resid(op.epi)) return cudaErrorInvalidValue;
     const int nw = op.nw == 8 ? 8 : 4;
+    if (op.f8) {
+        if (!op.ep.row_scale || !op.ep.col_scale) return cudaErrorInvalidValue;
+        if (op.epi == EPI_GELU_F8 && (!op.ep.out_inv || op.bn % 128 != 0)) return cudaErrorInvalidValue;
+        switch (op.bn * 16 + nw) {
+            case 128 * 16 + 4: return dispatch_epi_f8<128, 4>(op, num_sms, s);
+            case 192 * 16 + 4: return dispatch_epi_f8<192, 4>(op, num_sms, s);
+            case 256 * 16 + 4: return dispatch_epi_f8<256, 4>(op, num_sms, s);
+            case 128 * 16 + 8: return dispatch_epi_f8<128, 8>(op, num_sms, s);
+            case 192 * 16 + 8: return dispatch_epi_f8<192, 8>(op, num_sms, s);
+            case 256 * 16 + 8: return dispatch_epi_f8<256, 8>(op, num_sms, s);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (op.epi == EPI_GELU_F8) return cudaErrorInvalidValue;
     switch (op.bn * 16 + nw) {
         case 128 * 16 + 4: return dispatch_epi<128, 4>(op, num_sms, s);
         case 192 * 16 + 4: return dispatch_epi<192, 4>(op, num_sms, s);

@@ -2,9 +2,12 @@
 //
 //   C[M, N] = A[M, K] * B[N, K]^T     A, B bf16 K-major (PyTorch Linear: B is
 //                                      the [out, in] weight), fp32 accumulate
+//   F8 = 1: A, B e4m3 (kind::f8f6f4), C = row_scale[m] * col_scale[n] * acc,
+//           so A carries one scale per row and B one per output channel
 //
 // One persistent CTA per SM:
-//   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage,
+//   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage (bf16;
+//               128x128 and BNx128 for e4m3, the same 128-byte rows),
 //               128-byte swizzle, mbarrier complete_tx
 //   warp 1      TMEM allocator + MMA issuer (one thread): 4 x
 //               tcgen05.mma.cta_group::1.kind::f16 (128 x BN x 16) per stage,
@@ -22,7 +25,7 @@
 // mbarrier wait is bounded (common.cuh); on expiry the CTA drains and returns
 // with an error code in the device error word.
 //
-// Shape rules (checked on the host): N % BN == 0, K % (64 * ksplit) == 0,
+// Shape rules (checked on the host): N % BN == 0, K % (BK * ksplit) == 0,
 // ksplit > 1 only for EPI_RESID / EPI_RESID_GATED; rows past M are
 // zero-filled by TMA and never stored.
 #pragma once
@@ -38,6 +41,7 @@ enum EpiKind : int {
     EPI_RESID,        // resid   += acc + bias                     (PE residual)
     EPI_RESID_GATED,  // resid   += gate[row] * (acc + bias)       (DiT gated residual)
     EPI_QKV,          // q/k/v split, optional per-head RMS norm, RoPE, bf16 stores
+    EPI_GELU_F8,      // out_e4m3 = e4m3(gelu_tanh(acc + bias) * out_inv[row])  (DiT FFN1, FP8 path)
 };
 
 enum RopeMode : int { ROPE_HALF = 0, ROPE_ADJACENT = 1 };
@@ -63,30 +67,41 @@ struct EpiParams {
     int rope_mode;
     int ksplit;               // K splits (>= 1)
     int *err;                 // device error word
+    // e4m3 operands (F8 = 1): acc * row_scale[m] * col_scale[n] before the bias
+    const float *row_scale;   // [M]
+    const float *col_scale;   // [N]
+    const float *out_inv;     // EPI_GELU_F8: per-row factor applied before the e4m3 conversion
 };
 
 __host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || epi == EPI_RESID_GATED; }
 
-template <int BN, int NW, int EPI>
+constexpr int kRopeSmemRows = 64;   // sequences up to this length read RoPE from shared memory
+
+template <int BN, int NW, int EPI, int F8 = 0>
 struct GemmCfg {
-    static constexpr int BM = 128, BK = 64;
-    static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int BM = 128;
+    static constexpr int BK = F8 ? 128 : 64;   // elements per stage: 128 bytes of K either way
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_BUFS = is_resid(EPI) ? 2 : 1;  // staging buffers per epilogue warp
     static constexpr int STAGE_STAGING = NW * STAGE_BUFS * 32 * 128;  // 32 rows x 128 bytes each
     static constexpr int SMEM_MAX = 227 * 1024;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int STAGES_FIT = (SMEM_MAX - STAGE_STAGING - BAR_BYTES - 1024) / STAGE_BYTES;
+    // EPI_QKV: the q/k RMS gains (128 floats) and up to kRopeSmemRows rows of
+    // the RoPE table staged in shared memory once per CTA
+    static constexpr int CONST_BYTES = EPI == EPI_QKV ? 512 + kRopeSmemRows * 256 : 0;
+    static constexpr int STAGES_FIT = (SMEM_MAX - STAGE_STAGING - CONST_BYTES - BAR_BYTES - 1024) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGE_STAGING + BAR_BYTES + 1024;  // +1024 alignment slack
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGE_STAGING + CONST_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
     static constexpr int THREADS = 64 + NW * 32;
-    static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+    static constexpr uint32_t IDESC = F8 ? idesc_e4m3(BM, BN) : idesc_bf16(BM, BN);
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
     static_assert(NW == 4 || NW == 8, "epilogue warps");
     static_assert(STAGES >= 3, "pipeline depth");
+    static_assert(EPI != EPI_GELU_F8 || (F8 && BN % 128 == 0), "e4m3 output tiles are whole 128-byte rows");
 };
 
 DTTS_DEV float gelu_tanh_fast(float x) {
@@ -116,6 +131,44 @@ DTTS_DEV void stage_put_bf16(uint8_t *wbuf, int lane, const float (&lo)[32], con
     }
 }
 
+// Per-column constants of one 32-column chunk (e4m3 column scale, bias),
+// loaded into registers BEFORE the chunk's TMEM read so that their latency
+// overlaps it instead of following it.
+struct Col32 {
+    float4 s[8], b[8];
+};
+template <bool SCALE>
+DTTS_DEV void col32_load(Col32 &c, const float *cs, const float *bias, int n0) {
+    if constexpr (SCALE) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(cs + n0);
+#pragma unroll
+        for (int i = 0; i < 8; i++) c.s[i] = __ldg(s4 + i);
+    }
+    if (bias) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(bias + n0);
+#pragma unroll
+        for (int i = 0; i < 8; i++) c.b[i] = __ldg(b4 + i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) c.b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+// v = v * rs * scale + bias (SCALE) or v + bias
+template <bool SCALE>
+DTTS_DEV void col32_apply(float (&v)[32], const Col32 &c, float rs) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        if constexpr (SCALE) {
+            v[4 * i + 0] = fmaf(v[4 * i + 0], rs * c.s[i].x, c.b[i].x);
+            v[4 * i + 1] = fmaf(v[4 * i + 1], rs * c.s[i].y, c.b[i].y);
+            v[4 * i + 2] = fmaf(v[4 * i + 2], rs * c.s[i].z, c.b[i].z);
+            v[4 * i + 3] = fmaf(v[4 * i + 3], rs * c.s[i].w, c.b[i].w);
+        } else {
+            v[4 * i + 0] += c.b[i].x; v[4 * i + 1] += c.b[i].y; v[4 * i + 2] += c.b[i].z; v[4 * i + 3] += c.b[i].w;
+        }
+    }
+}
+
 DTTS_DEV void load_bias32(float (&v)[32], const float *bias, int n0) {
     if (!bias) return;
     const float4 *b4 = reinterpret_cast<const float4 *>(bias + n0);
@@ -127,28 +180,36 @@ DTTS_DEV void load_bias32(float (&v)[32], const float *bias, int n0) {
 }
 
 // Per-thread head transform for EPI_QKV: lo = head columns [0,32), hi = [32,64).
-DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&lo)[32], float (&hi)[32]) {
+// sgain: the q gains then the k gains (shared memory, ones where absent);
+// srope: RoPE rows kv_start.. in shared memory, or nullptr to read ep.rope.
+// The RoPE rows are read with generic loads: they may be shared or global.
+DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&lo)[32], float (&hi)[32],
+                                 const float *sgain, const float4 *srope) {
     if (sect == 2) return;  // v: plain
+    const int t = m % ep.tok_per_row;
     if (ep.qk_norm) {
-        const float *g = sect == 0 ? ep.qn : ep.kn;
-        float ss = 0.f;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; i++) ss += lo[i] * lo[i] + hi[i] * hi[i];
-        const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+        for (int i = 0; i < 32; i += 2) {
+            s0 = fmaf(lo[i], lo[i], s0); s1 = fmaf(hi[i], hi[i], s1);
+            s2 = fmaf(lo[i + 1], lo[i + 1], s2); s3 = fmaf(hi[i + 1], hi[i + 1], s3);
+        }
+        const float inv = 1.0f / sqrtf(((s0 + s1) + (s2 + s3)) / 64.0f + 1e-6f);
+        const float4 *g4 = reinterpret_cast<const float4 *>(sgain + sect * 64);
 #pragma unroll
-        for (int i = 0; i < 32; i++) { lo[i] *= inv; hi[i] *= inv; }
-        if (g) {
-#pragma unroll
-            for (int i = 0; i < 32; i++) { lo[i] *= __ldg(g + i); hi[i] *= __ldg(g + 32 + i); }
+        for (int i = 0; i < 8; i++) {
+            const float4 a = g4[i], b = g4[8 + i];
+            lo[4 * i + 0] *= inv * a.x; lo[4 * i + 1] *= inv * a.y; lo[4 * i + 2] *= inv * a.z; lo[4 * i + 3] *= inv * a.w;
+            hi[4 * i + 0] *= inv * b.x; hi[4 * i + 1] *= inv * b.y; hi[4 * i + 2] *= inv * b.z; hi[4 * i + 3] *= inv * b.w;
         }
     }
-    const int t = m % ep.tok_per_row;
-    const float4 *cs = reinterpret_cast<const float4 *>(ep.rope + (long long)(ep.kv_start + t) * 32);
+    const float4 *cs = srope ? srope + t * 16
+                             : reinterpret_cast<const float4 *>(ep.rope + (long long)(ep.kv_start + t) * 32);
     if (ep.rope_mode == ROPE_HALF) {
         // pairs (d, d + 32), frequency index d
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-            const float4 e = __ldg(cs + i);  // (cos_2i, sin_2i, cos_2i+1, sin_2i+1)
+            const float4 e = cs[i];  // (cos_2i, sin_2i, cos_2i+1, sin_2i+1)
             float x1 = lo[2 * i], x2 = hi[2 * i];
             lo[2 * i] = x1 * e.x - x2 * e.y;
             hi[2 * i] = x2 * e.x + x1 * e.y;
@@ -160,7 +221,7 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
         // adjacent pairs (2i, 2i + 1), frequency index i
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const float4 e = __ldg(cs + i);  // frequencies 2i, 2i+1
+            const float4 e = cs[i];  // frequencies 2i, 2i+1
             float x0 = lo[4 * i], x1 = lo[4 * i + 1];
             lo[4 * i] = x0 * e.x - x1 * e.y;
             lo[4 * i + 1] = x0 * e.y + x1 * e.x;
@@ -170,7 +231,7 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
         }
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const float4 e = __ldg(cs + 8 + i);  // frequencies 16 + 2i, 16 + 2i + 1
+            const float4 e = cs[8 + i];  // frequencies 16 + 2i, 16 + 2i + 1
             float x0 = hi[4 * i], x1 = hi[4 * i + 1];
             hi[4 * i] = x0 * e.x - x1 * e.y;
             hi[4 * i + 1] = x0 * e.y + x1 * e.x;
@@ -181,11 +242,11 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
     }
 }
 
-template <int BN, int EPI, int NW>
-__global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
+template <int BN, int EPI, int NW, int F8 = 0>
+__global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmR, int M, int N, int K, EpiParams ep) {
-    using Cfg = GemmCfg<BN, NW, EPI>;
+    using Cfg = GemmCfg<BN, NW, EPI, F8>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr int EPI_THREADS = NW * 32;
     extern __shared__ uint8_t smem_raw[];
@@ -193,7 +254,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * Cfg::A_BYTES;
     uint8_t *sStage = smem + STAGES * Cfg::STAGE_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sStage + Cfg::STAGE_STAGING);
+    uint8_t *sConst = sStage + Cfg::STAGE_STAGING;   // EPI_QKV: gains, RoPE rows
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sConst + Cfg::CONST_BYTES);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *tfull = bars + 2 * STAGES;
@@ -277,10 +339,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+                    // four MMAs of 32 bytes of K (16 bf16 or 32 e4m3 elements)
 #pragma unroll
-                    for (int k = 0; k < Cfg::BK / 16; k++) {
-                        tc_mma_bf16(d_tmem, sdesc_k128(a0 + k * 32), sdesc_k128(b0 + k * 32), Cfg::IDESC,
-                                    (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < 4; k++) {
+                        if constexpr (F8)
+                            tc_mma_f8(d_tmem, sdesc_k128(a0 + k * 32), sdesc_k128(b0 + k * 32), Cfg::IDESC,
+                                      (kb | k) != 0 ? 1u : 0u);
+                        else
+                            tc_mma_bf16(d_tmem, sdesc_k128(a0 + k * 32), sdesc_k128(b0 + k * 32), Cfg::IDESC,
+                                        (kb | k) != 0 ? 1u : 0u);
                     }
                     tc_commit(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -300,6 +367,23 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
         // with 8 warps the two warps of a quadrant take alternate column chunks
         const int ew = warp - 2;
         const int quad = warp & 3;
+        float *sgain = nullptr;
+        const float4 *srope = nullptr;
+        if constexpr (EPI == EPI_QKV) {
+            sgain = reinterpret_cast<float *>(sConst);
+            float2 *rp = reinterpret_cast<float2 *>(sConst + 512);
+            const int et = threadIdx.x - 64;
+            for (int i = et; i < 128; i += EPI_THREADS) {
+                const float *g = i < 64 ? ep.qn : ep.kn;
+                sgain[i] = g ? __ldg(g + (i & 63)) : 1.0f;
+            }
+            const bool rope_smem = ep.rope != nullptr && ep.tok_per_row <= kRopeSmemRows;
+            if (rope_smem)
+                for (int i = et; i < ep.tok_per_row * 32; i += EPI_THREADS)
+                    rp[i] = __ldg(ep.rope + (long long)ep.kv_start * 32 + i);
+            asm volatile("bar.sync 1, %0;\n" ::"r"(EPI_THREADS) : "memory");
+            if (rope_smem) srope = reinterpret_cast<const float4 *>(rp);
+        }
         const int half = (NW == 8) ? (ew >> 2) : 0;
         constexpr int CSTEP = (NW == 8) ? 2 : 1;
         uint8_t *wbuf = sStage + ew * Cfg::STAGE_BUFS * 32 * 128;
@@ -316,20 +400,32 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
             const int mb = tile % num_m, nb = tile / num_m;
             const int m_base = mb * Cfg::BM + quad * 32;
             const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(quad * 32) << 16);
+            float rs = 0.f;   // e4m3 row scale of this thread's row
+            if constexpr (F8)
+                if (m_base + lane < M) rs = __ldg(ep.row_scale + m_base + lane);
             if constexpr (EPI == EPI_QKV || EPI == EPI_BF16 || EPI == EPI_GELU_BF16 || EPI == EPI_SILU_BF16) {
                 // 64 columns (one head / 128 bytes of bf16) per chunk
 #pragma unroll 1
                 for (int c = half; c < BN / 64; c += CSTEP) {
                     const int n0 = nb * BN + c * 64;
+                    // the DiT QKV projection has no bias: bf16 QKV needs no column constants
+                    constexpr bool kCols = F8 || EPI != EPI_QKV;
+                    Col32 cl, ch;
+                    if constexpr (kCols) {
+                        col32_load<F8 != 0>(cl, ep.col_scale, EPI == EPI_QKV ? nullptr : ep.bias, n0);
+                        col32_load<F8 != 0>(ch, ep.col_scale, EPI == EPI_QKV ? nullptr : ep.bias, n0 + 32);
+                    }
                     float lo[32], hi[32];
                     tmem_ld32(tbase + c * 64, lo);
                     tmem_ld32(tbase + c * 64 + 32, hi);
+                    if constexpr (kCols) {
+                        col32_apply<F8 != 0>(lo, cl, rs);
+                        col32_apply<F8 != 0>(hi, ch, rs);
+                    }
                     const int m_self = m_base + lane;
                     if constexpr (EPI == EPI_QKV) {
-                        if (m_self < M) qkv_head_transform(ep, m_self, n0 >> 10, lo, hi);
+                        if (m_self < M) qkv_head_transform(ep, m_self, n0 >> 10, lo, hi, sgain, srope);
                     } else {
-                        load_bias32(lo, ep.bias, n0);
-                        load_bias32(hi, ep.bias, n0 + 32);
                         if constexpr (EPI == EPI_GELU_BF16) {
 #pragma unroll
                             for (int i = 0; i < 32; i++) { lo[i] = gelu_tanh_fast(lo[i]); hi[i] = gelu_tanh_fast(hi[i]); }
@@ -364,14 +460,63 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
                         *reinterpret_cast<uint4 *>(dst) = val;
                     }
                 }
+            } else if constexpr (EPI == EPI_GELU_F8) {
+                // e4m3 results: 128 columns (one 128-byte row segment) per pass,
+                // built from four 32-column TMEM loads
+                const float oinv = (m_base + lane < M) ? __ldg(ep.out_inv + m_base + lane) : 0.f;
+#pragma unroll 1
+                for (int sg = half; sg < BN / 128; sg += CSTEP) {
+                    const int n_seg = nb * BN + sg * 128;
+                    __syncwarp();
+#pragma unroll 1
+                    for (int sub = 0; sub < 4; sub++) {
+                        const int n0 = n_seg + sub * 32;
+                        Col32 cv;
+                        col32_load<true>(cv, ep.col_scale, ep.bias, n0);
+                        float v[32];
+                        tmem_ld32(tbase + sg * 128 + sub * 32, v);
+                        col32_apply<true>(v, cv, rs);
+                        uint4 w0, w1;
+                        w0.x = pack_e4m3x4(gelu_tanh_fast(v[0]) * oinv, gelu_tanh_fast(v[1]) * oinv,
+                                           gelu_tanh_fast(v[2]) * oinv, gelu_tanh_fast(v[3]) * oinv);
+                        w0.y = pack_e4m3x4(gelu_tanh_fast(v[4]) * oinv, gelu_tanh_fast(v[5]) * oinv,
+                                           gelu_tanh_fast(v[6]) * oinv, gelu_tanh_fast(v[7]) * oinv);
+                        w0.z = pack_e4m3x4(gelu_tanh_fast(v[8]) * oinv, gelu_tanh_fast(v[9]) * oinv,
+                                           gelu_tanh_fast(v[10]) * oinv, gelu_tanh_fast(v[11]) * oinv);
+                        w0.w = pack_e4m3x4(gelu_tanh_fast(v[12]) * oinv, gelu_tanh_fast(v[13]) * oinv,
+                                           gelu_tanh_fast(v[14]) * oinv, gelu_tanh_fast(v[15]) * oinv);
+                        w1.x = pack_e4m3x4(gelu_tanh_fast(v[16]) * oinv, gelu_tanh_fast(v[17]) * oinv,
+                                           gelu_tanh_fast(v[18]) * oinv, gelu_tanh_fast(v[19]) * oinv);
+                        w1.y = pack_e4m3x4(gelu_tanh_fast(v[20]) * oinv, gelu_tanh_fast(v[21]) * oinv,
+                                           gelu_tanh_fast(v[22]) * oinv, gelu_tanh_fast(v[23]) * oinv);
+                        w1.z = pack_e4m3x4(gelu_tanh_fast(v[24]) * oinv, gelu_tanh_fast(v[25]) * oinv,
+                                           gelu_tanh_fast(v[26]) * oinv, gelu_tanh_fast(v[27]) * oinv);
+                        w1.w = pack_e4m3x4(gelu_tanh_fast(v[28]) * oinv, gelu_tanh_fast(v[29]) * oinv,
+                                           gelu_tanh_fast(v[30]) * oinv, gelu_tanh_fast(v[31]) * oinv);
+                        *reinterpret_cast<uint4 *>(wbuf + stage_off(lane, 2 * sub)) = w0;
+                        *reinterpret_cast<uint4 *>(wbuf + stage_off(lane, 2 * sub + 1)) = w1;
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int r = rsub + 4 * i;
+                        const int m = m_base + r;
+                        const uint4 val = *reinterpret_cast<const uint4 *>(wbuf + stage_off(r, chunk));
+                        if (m >= M) continue;
+                        *reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(ep.out) + (long long)m * ep.ldo + n_seg +
+                                                   chunk * 16) = val;
+                    }
+                }
             } else if constexpr (EPI == EPI_F32) {
                 // fp32 results: 32 columns (128 bytes) per chunk
 #pragma unroll 1
                 for (int c = half; c < BN / 32; c += CSTEP) {
                     const int n0 = nb * BN + c * 32;
+                    Col32 cv;
+                    col32_load<F8 != 0>(cv, ep.col_scale, ep.bias, n0);
                     float v[32];
                     tmem_ld32(tbase + c * 32, v);
-                    load_bias32(v, ep.bias, n0);
+                    col32_apply<F8 != 0>(v, cv, rs);
                     __syncwarp();
                     stage_put(wbuf, lane, v);
                     __syncwarp();
@@ -395,17 +540,23 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI>::THREADS, 1)
 #pragma unroll 1
                 for (int c = half; c < BN / 32; c += CSTEP, cc++) {
                     const int n0 = nb * BN + c * 32;
+                    Col32 cv;
+                    col32_load<F8 != 0>(cv, ep.col_scale, split == 0 ? ep.bias : nullptr, n0);
+                    float4 gq[8];
+                    if constexpr (EPI == EPI_RESID_GATED) {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) gq[i] = g4 ? __ldg(g4 + (n0 >> 2) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                     float v[32];
                     tmem_ld32(tbase + c * 32, v);
-                    if (split == 0) load_bias32(v, ep.bias, n0);
+                    col32_apply<F8 != 0>(v, cv, rs);
                     if (m_self >= M) {
 #pragma unroll
                         for (int i = 0; i < 32; i++) v[i] = 0.f;
                     } else if constexpr (EPI == EPI_RESID_GATED) {
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
-                            const float4 g = __ldg(g4 + (n0 >> 2) + i);
-                            v[4 * i + 0] *= g.x; v[4 * i + 1] *= g.y; v[4 * i + 2] *= g.z; v[4 * i + 3] *= g.w;
+                            v[4 * i + 0] *= gq[i].x; v[4 * i + 1] *= gq[i].y; v[4 * i + 2] *= gq[i].z; v[4 * i + 3] *= gq[i].w;
                         }
                     }
                     uint8_t *buf = wbuf + (cc & 1) * 32 * 128;

@@ -51,6 +51,90 @@ void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, cons
     ln_modulate_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, shift, scale, ada_ld, tok_per_row);
 }
 
+// The same LayerNorm + modulation with an e4m3 output row: the row is scaled
+// by 448 / absmax before the conversion and row_scale = absmax / 448 is
+// written beside it.  unorm (if given) receives 1.08 |u| and, when g_scale is
+// given, the row's bound on |gelu(W1 u + b1)|, B = 1.02 max(1.08 |u| w1n +
+// b1max, 0.17), is stored as g_scale = B / 448 and g_inv = 448 / B.
+__global__ void __launch_bounds__(256, 3) ln_modulate_f8_kernel(const float *__restrict__ x, uint8_t *__restrict__ y,
+                                                                int M, const float *__restrict__ shift,
+                                                                const float *__restrict__ scale, long long ada_ld,
+                                                                int tok_per_row, float *__restrict__ row_scale,
+                                                                float *__restrict__ unorm, float *__restrict__ g_scale,
+                                                                float *__restrict__ g_inv, float w1n, float b1max) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const long long r = row / tok_per_row;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
+    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
+    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    const float mean = warp_sum(s) * (1.0f / kD);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
+        q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
+    float amax = 0.f, ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
+        v[j].x = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
+        v[j].y = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
+        v[j].z = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
+        v[j].w = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+        ss += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
+    }
+    amax = warp_max(amax);
+    const float qinv = amax > 0.f ? 448.0f / amax : 0.f;
+    uint32_t *yr = reinterpret_cast<uint32_t *>(y + (long long)row * kD);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        yr[lane + 32 * j] = pack_e4m3x4(v[j].x * qinv, v[j].y * qinv, v[j].z * qinv, v[j].w * qinv);
+    const float nrm = sqrtf(warp_sum(ss));
+    if (lane == 0) {
+        row_scale[row] = amax / 448.0f;
+        if (unorm) unorm[row] = 1.08f * nrm;
+        if (g_scale) {
+            const float bnd = 1.02f * fmaxf(1.08f * nrm * w1n + b1max, 0.17f);
+            g_scale[row] = bnd / 448.0f;
+            g_inv[row] = 448.0f / bnd;
+        }
+    }
+}
+
+void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
+                           long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
+                           float *g_inv, float w1n, float b1max, cudaStream_t s) {
+    ln_modulate_f8_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, shift, scale, ada_ld, tok_per_row, row_scale, unorm,
+                                                      g_scale, g_inv, w1n, b1max);
+}
+
+// e4m3 conversion of n values (device self-test of the rounding).
+__global__ void e4m3_selftest_kernel(const float *__restrict__ x, uint8_t *__restrict__ y, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (4 * i + 3 < n) {
+        const uint32_t p = pack_e4m3x4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+        y[4 * i] = p & 0xff; y[4 * i + 1] = (p >> 8) & 0xff; y[4 * i + 2] = (p >> 16) & 0xff; y[4 * i + 3] = p >> 24;
+    } else {
+        for (int k = 4 * i; k < n; k++) y[k] = pack_e4m3x4(x[k], 0.f, 0.f, 0.f) & 0xff;
+    }
+}
+
+void launch_e4m3_selftest(const float *x, uint8_t *y, int n, cudaStream_t s) {
+    const int quads = (n + 3) / 4;
+    e4m3_selftest_kernel<<<(quads + 127) / 128, 128, 0, s>>>(x, y, n);
+}
+
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
                                                        const float *__restrict__ w) {
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -119,6 +203,49 @@ DTTS_DEV void load_tile64(bf16 *sm, const bf16 *g, long long ld, int valid_rows)
         const bool ok = row < valid_rows;
         const bf16 *src = ok ? g + (long long)row * ld + ch * 8 : g;
         cp_async16(sm + swz(row, ch), src, ok);
+    }
+}
+
+// Bound on |softmax . V| of sequence r for the e4m3 output (see AttnArgs).
+DTTS_DEV float attn_seq_bound(const AttnArgs &a, int r) {
+    float m = 0.f;
+    for (int j = threadIdx.x & 31; j < a.kv_len; j += 32) m = fmaxf(m, __ldg(a.unorm + (long long)r * a.kv_cap + j));
+    return 1.02f * warp_max(m) * a.vbound;
+}
+
+// Stores this thread's part of a 64-column head output (query rows qi0, qi1;
+// columns nt*8 + 2t, +1): bf16 into a.o, or e4m3 into a.o8 when it is set.
+DTTS_DEV void attn_store(const AttnArgs &a, int r, int h, int qi0, int qi1, int t, const float (&o)[8][4],
+                         float inv0, float inv1) {
+    if (a.o8) {
+        const float bnd = attn_seq_bound(a, r);
+        const float qs = bnd > 0.f ? 448.0f / bnd : 0.f;
+        const float f0 = inv0 * qs, f1 = inv1 * qs;
+        uint8_t *og = a.o8 + (long long)r * a.Tq * a.ldo + h * kHD;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+            const int d = nt * 8 + 2 * t;
+            if (qi0 < a.Tq)
+                *reinterpret_cast<__nv_fp8x2_storage_t *>(og + (long long)qi0 * a.ldo + d) =
+                    __nv_cvt_float2_to_fp8x2(make_float2(o[nt][0] * f0, o[nt][1] * f0), __NV_SATFINITE, __NV_E4M3);
+            if (qi1 < a.Tq)
+                *reinterpret_cast<__nv_fp8x2_storage_t *>(og + (long long)qi1 * a.ldo + d) =
+                    __nv_cvt_float2_to_fp8x2(make_float2(o[nt][2] * f1, o[nt][3] * f1), __NV_SATFINITE, __NV_E4M3);
+        }
+        if (h == 0 && t == 0) {
+            if (qi0 < a.Tq) a.o_scale[(long long)r * a.Tq + qi0] = bnd / 448.0f;
+            if (qi1 < a.Tq) a.o_scale[(long long)r * a.Tq + qi1] = bnd / 448.0f;
+        }
+        return;
+    }
+    bf16 *og = reinterpret_cast<bf16 *>(a.o) + (long long)r * a.Tq * a.ldo + h * kHD;
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++) {
+        const int d = nt * 8 + 2 * t;
+        if (qi0 < a.Tq)
+            *reinterpret_cast<uint32_t *>(og + (long long)qi0 * a.ldo + d) = pack_bf16x2(o[nt][0] * inv0, o[nt][1] * inv0);
+        if (qi1 < a.Tq)
+            *reinterpret_cast<uint32_t *>(og + (long long)qi1 * a.ldo + d) = pack_bf16x2(o[nt][2] * inv1, o[nt][3] * inv1);
     }
 }
 
@@ -253,15 +380,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
     }
     const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f;
     const float inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
-    bf16 *og = reinterpret_cast<bf16 *>(a.o) + (long long)r * a.Tq * a.ldo + h * kHD;
-#pragma unroll
-    for (int nt = 0; nt < 8; nt++) {
-        const int d = nt * 8 + 2 * t;
-        if (qi0 < a.Tq)
-            *reinterpret_cast<uint32_t *>(og + (long long)qi0 * a.ldo + d) = pack_bf16x2(o[nt][0] * inv0, o[nt][1] * inv0);
-        if (qi1 < a.Tq)
-            *reinterpret_cast<uint32_t *>(og + (long long)qi1 * a.ldo + d) = pack_bf16x2(o[nt][2] * inv1, o[nt][3] * inv1);
-    }
+    attn_store(a, r, h, qi0, qi1, t, o, inv0, inv1);
 }
 
 // Short-sequence attention (Tq <= 64 and kv_len <= 64, the DiT at L <= 64):
@@ -376,16 +495,7 @@ __global__ void __launch_bounds__(128, 5) attn_short_kernel(AttnArgs a, int n_pa
             }
         }
         const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
-        const int r = p / kH, h = p % kH;
-        bf16 *og = reinterpret_cast<bf16 *>(a.o) + (long long)r * a.Tq * a.ldo + h * kHD;
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            const int d = nt * 8 + 2 * t;
-            if (qi0 < a.Tq)
-                *reinterpret_cast<uint32_t *>(og + (long long)qi0 * a.ldo + d) = pack_bf16x2(o[nt][0] * inv0, o[nt][1] * inv0);
-            if (qi1 < a.Tq)
-                *reinterpret_cast<uint32_t *>(og + (long long)qi1 * a.ldo + d) = pack_bf16x2(o[nt][2] * inv1, o[nt][3] * inv1);
-        }
+        attn_store(a, p / kH, p % kH, qi0, qi1, t, o, inv0, inv1);
         __syncthreads();   // buffer `buf` is refilled two pairs from now
     }
 }

@@ -15,11 +15,16 @@ struct GemmOp {
     int bn;       // 128, 192 or 256
     int nw;       // epilogue warps: 4 or 8
     int epi;      // EpiKind
+    int f8;       // 1: A and B are e4m3 (tensor maps from make_tmap_e4m3)
     EpiParams ep;
 };
 // A K-major bf16 matrix [rows][cols] seen by TMA as 64-column x box_rows boxes
 // with 128-byte swizzle.
 bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
+                    unsigned int box_rows);
+// A K-major e4m3 matrix [rows][cols] (one byte per element) seen by TMA as
+// 128-column x box_rows boxes with 128-byte swizzle.
+bool make_tmap_e4m3(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
                     unsigned int box_rows);
 // The fp32 residual [rows][cols] as the target of the epilogue's bulk reduce-add.
 bool make_tmap_f32_resid(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols);
@@ -45,6 +50,15 @@ struct AttnArgs {
     const uint32_t *mask_bits;  // the same mask bit-packed, [Tq][ceil(kv_len/32)] words,
                                 // bit k of word w = key 32w + k (bf16 kernels); nullptr: none
     float scale;
+    // e4m3 output (DiT FP8 path), used instead of `o` when o8 is set:
+    // o8[(r*Tq + i) * ldo + c] = e4m3(out * 448 / B_r) with the bound
+    // B_r = 1.02 * max_{j < kv_len} unorm[r*kv_cap + j] * vbound on |out|
+    // (softmax . V is a convex mix of V rows, |V_j,d| <= |u_j| |Wv_d|), and the
+    // head-0 pass writes o_scale[r*Tq + i] = B_r / 448
+    uint8_t *o8;
+    float *o_scale;
+    const float *unorm;
+    float vbound;
 };
 // Tq <= 64 and kv_len <= 64 take the pipelined short-sequence kernel (call
 // attention_short_prepare() once per device first); longer ones the tiled kernel.
@@ -85,6 +99,12 @@ void launch_speaker_cond(const float *spk, int n_utt, const float *w, const floa
                          const float *ln_b, float scale, float *spk_c, cudaStream_t s);
 // a_cond[k*n + u] = bf16(SiLU(temb[k] + spk_c[u])) for k < n_t, u < n  (spk_c may be null)
 void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf16 *a_cond, cudaStream_t s);
+
+// LayerNorm + modulation to e4m3 rows (DiT FP8 path), see kernels.cu.
+void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
+                           long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
+                           float *g_inv, float w1n, float b1max, cudaStream_t s);
+void launch_e4m3_selftest(const float *x, uint8_t *y, int n, cudaStream_t s);
 
 // ------------------------------------------------------------ DiT output head
 // vel[r][p] = W_out (LN(h[r, L-P+p]) (1 + scale) + shift) + b_out, with the

@@ -1,6 +1,8 @@
 // Host runtime helpers (see runtime.h).
 #include "runtime.h"
 
+#include <cmath>
+
 #include <algorithm>
 #include <chrono>
 #include <cstdarg>
@@ -54,6 +56,72 @@ void f32_to_bf16_host(const float *src, uint16_t *dst, size_t n) {
         th.emplace_back([=] {
             for (size_t i = b; i < e; i++) dst[i] = bf16_rne(src[i]);
         });
+    }
+    for (auto &x : th) x.join();
+}
+
+// e4m3: 1 sign bit, 4 exponent bits (bias 7), 3 mantissa bits, largest finite
+// 448, subnormals m * 2^-9, no infinities.  Round to nearest even, saturating.
+uint8_t e4m3_encode_host(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    const uint8_t sign = static_cast<uint8_t>((u >> 24) & 0x80u);
+    const uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return sign | 0x7f;    // NaN
+    if (a >= 0x43e00000u) return sign | 0x7e;   // |x| >= 448 (or inf): saturate
+    if (a < 0x3c800000u) {                      // |x| < 2^-6: multiples of 2^-9
+        float f;
+        std::memcpy(&f, &a, 4);
+        return sign | static_cast<uint8_t>(std::nearbyint(f * 512.0f));   // 8 = 2^-6, the smallest normal
+    }
+    // keep 3 of the 23 mantissa bits, rounding to nearest even at bit 20 (a
+    // carry moves into the exponent), then rebias the exponent from 127 to 7
+    const uint32_t r = (a + 0x7ffffu + ((a >> 20) & 1u)) >> 20;
+    return sign | static_cast<uint8_t>(r - (120u << 3));
+}
+
+float e4m3_decode_host(uint8_t b) {
+    const int E = (b >> 3) & 15, m = b & 7;
+    if (E == 15 && m == 7) return std::nanf("");
+    const float v = E == 0 ? std::ldexp(static_cast<float>(m), -9) : std::ldexp(static_cast<float>(8 + m), E - 10);
+    return (b & 0x80) ? -v : v;
+}
+
+void e4m3_quantize_rows(const float *w, size_t rows, size_t cols, uint8_t *q, float *scale, float *row_norm) {
+    float dec[256];
+    for (int i = 0; i < 256; i++) dec[i] = e4m3_decode_host(static_cast<uint8_t>(i));
+    auto work = [&](size_t r0, size_t r1) {
+        for (size_t r = r0; r < r1; r++) {
+            const float *src = w + r * cols;
+            uint8_t *dst = q + r * cols;
+            float amax = 0.f;
+            for (size_t c = 0; c < cols; c++) amax = std::max(amax, std::fabs(src[c]));
+            if (amax == 0.f) {
+                std::memset(dst, 0, cols);
+                scale[r] = 0.f;
+                if (row_norm) row_norm[r] = 0.f;
+                continue;
+            }
+            const float inv = 448.0f / amax, s = amax / 448.0f;
+            float ss = 0.f;
+            for (size_t c = 0; c < cols; c++) {
+                dst[c] = e4m3_encode_host(src[c] * inv);
+                const float d = dec[dst[c]] * s;
+                ss += d * d;
+            }
+            scale[r] = s;
+            if (row_norm) row_norm[r] = std::sqrt(ss);
+        }
+    };
+    const size_t total = rows * cols;
+    unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    if (total < (size_t(1) << 20) || nt == 1) { work(0, rows); return; }
+    std::vector<std::thread> th;
+    const size_t per = (rows + nt - 1) / nt;
+    for (unsigned t = 0; t < nt; t++) {
+        const size_t b = t * per, e = std::min(rows, b + per);
+        if (b >= e) break;
+        th.emplace_back(work, b, e);
     }
     for (auto &x : th) x.join();
 }

@@ -72,6 +72,14 @@ struct DeviceArena {
 // Host fp32 -> bf16 (round to nearest even), multithreaded for large arrays.
 void f32_to_bf16_host(const float *src, uint16_t *dst, size_t n);
 
+// e4m3 (round to nearest even, saturating at +-448) on the host.
+uint8_t e4m3_encode_host(float x);
+float e4m3_decode_host(uint8_t b);
+// Per-row (output-channel) e4m3 quantisation of w [rows][cols]:
+// scale[r] = amax_r / 448, q = e4m3(w * 448 / amax_r); row_norm (optional)
+// receives the L2 norm of each dequantised row.
+void e4m3_quantize_rows(const float *w, size_t rows, size_t cols, uint8_t *q, float *scale, float *row_norm);
+
 // Checks that a device with this ordinal exists and is sm_100; fills num_sms.
 int check_device(int device, int *num_sms);
 

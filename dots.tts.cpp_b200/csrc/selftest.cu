@@ -57,6 +57,46 @@ int dtts_selftest_gemm(const float *A, const float *B, const float *bias, float 
     return DTTS_OK;
 }
 
+// C[M][N] = a_scale[m] b_scale[n] (A[M][K] B[N][K]^T) (+ bias[N]) with e4m3
+// A and B (bytes) through the kind::f8f6f4 GEMM; bn = 128 or 256, K % 128 == 0.
+int dtts_selftest_gemm_e4m3(const uint8_t *A, const float *a_scale, const uint8_t *B, const float *b_scale,
+                            const float *bias, float *C, int M, int N, int K, int bn, int device) {
+    DTTS_CHECK(A && a_scale && B && b_scale && C, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(M >= 1 && K >= 128 && K % 128 == 0 && (bn == 128 || bn == 256) && N % bn == 0, DTTS_ERR_ARG,
+               "bad GEMM shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    DTTS_CUDA(gemm_prepare_attributes());
+    Scratch s;
+    void *da = s.a.alloc((size_t)M * K), *db = s.a.alloc((size_t)N * K), *dc = s.a.alloc((size_t)M * N * 4);
+    float *dsa = (float *)s.a.alloc((size_t)M * 4), *dsb = (float *)s.a.alloc((size_t)N * 4);
+    void *dbias = bias ? s.a.alloc((size_t)N * 4) : nullptr;
+    int *derr = (int *)s.a.alloc(4);
+    DTTS_CHECK(da && db && dc && dsa && dsb && derr && (!bias || dbias), DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(da, A, (size_t)M * K, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemcpy(db, B, (size_t)N * K, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemcpy(dsa, a_scale, (size_t)M * 4, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemcpy(dsb, b_scale, (size_t)N * 4, cudaMemcpyHostToDevice));
+    if (bias) DTTS_CUDA(cudaMemcpy(dbias, bias, (size_t)N * 4, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemset(dc, 0xff, (size_t)M * N * 4));
+    DTTS_CUDA(cudaMemset(derr, 0, 4));
+    GemmOp op;
+    std::memset(&op, 0, sizeof(op));
+    bool ok = make_tmap_e4m3(&op.ta, da, M, K, 128) && make_tmap_e4m3(&op.tb, db, N, K, bn);
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map encode failed");
+    op.M = M; op.N = N; op.K = K; op.bn = bn; op.epi = EPI_F32; op.f8 = 1;
+    op.ep.out = dc; op.ep.ldo = N; op.ep.bias = (const float *)dbias; op.ep.err = derr; op.ep.tok_per_row = 1;
+    op.ep.row_scale = dsa; op.ep.col_scale = dsb;
+    DTTS_CUDA(launch_gemm(op, nsm, 0));
+    if ((st = stream_wait(0, 60.0))) return st;
+    int err = 0;
+    DTTS_CUDA(cudaMemcpy(&err, derr, 4, cudaMemcpyDeviceToHost));
+    DTTS_CHECK(err == 0, DTTS_ERR_TIMEOUT, "GEMM kernel wait limit reached (code %d)", err);
+    DTTS_CUDA(cudaMemcpy(C, dc, (size_t)M * N * 4, cudaMemcpyDeviceToHost));
+    return DTTS_OK;
+}
+
 // Attention core alone: q [rows][Tq][1024], k/v [rows][kv_len][1024] (fp32,
 // rounded to bf16 on upload), out [rows][Tq][1024] fp32.  mask [Tq][kv_len] or
 // NULL; causal with the first query at absolute position q_pos0.
@@ -111,6 +151,23 @@ int dtts_selftest_attention(const float *q, const float *k, const float *v, floa
         DTTS_CUDA(cudaMemcpy(t.data(), dout, nq * 2, cudaMemcpyDeviceToHost));
         for (size_t i = 0; i < nq; i++) { uint32_t u = (uint32_t)t[i] << 16; std::memcpy(&out[i], &u, 4); }
     }
+    return DTTS_OK;
+}
+
+int dtts_selftest_e4m3(const float *x, uint8_t *out, int n, int device) {
+    DTTS_CHECK(x && out && n >= 1, DTTS_ERR_ARG, "bad e4m3 self-test arguments");
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    Scratch s;
+    float *dx = (float *)s.a.alloc((size_t)n * 4);
+    uint8_t *dy = (uint8_t *)s.a.alloc((size_t)n);
+    DTTS_CHECK(dx && dy, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice));
+    launch_e4m3_selftest(dx, dy, n, 0);
+    DTTS_CUDA(cudaGetLastError());
+    DTTS_CUDA(cudaDeviceSynchronize());
+    DTTS_CUDA(cudaMemcpy(out, dy, (size_t)n, cudaMemcpyDeviceToHost));
     return DTTS_OK;
 }
 

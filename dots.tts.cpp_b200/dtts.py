@@ -110,7 +110,9 @@ EXPORTS = [
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
-    "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_st_open",
+    "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_selftest_e4m3",
+    "dtts_selftest_gemm_e4m3",
+    "dtts_fp8_quantize_rows", "dtts_st_open",
     "dtts_st_close", "dtts_st_count", "dtts_st_shape", "dtts_st_read_f32",
 ]
 
@@ -473,6 +475,37 @@ def selftest_attention(q, k, v, mask=None, causal=False, q_pos0=0, use_f32=False
                                         None if mk is None else mk.ctypes.data_as(_u8p), int(causal), q_pos0,
                                         int(use_f32), device))
     return out
+
+
+def selftest_e4m3(x, device=0):
+    """Device e4m3 conversion (round to nearest even, saturating) of x."""
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    out = np.zeros(x.size, np.uint8)
+    check(lib().dtts_selftest_e4m3(_ptr(x), out.ctypes.data_as(_u8p), x.size, device))
+    return out
+
+
+def selftest_gemm_e4m3(A, a_scale, B, b_scale, bias=None, bn=128, device=0):
+    """C = diag(a_scale) (A B^T) diag(b_scale) + bias with e4m3 byte matrices
+    A [M][K], B [N][K] on the tcgen05 kind::f8f6f4 GEMM."""
+    A, B = np.ascontiguousarray(A, np.uint8), np.ascontiguousarray(B, np.uint8)
+    a_scale, b_scale, bias = _f32(a_scale), _f32(b_scale), _f32(bias)
+    M, K = A.shape
+    N = B.shape[0]
+    C_ = np.zeros((M, N), np.float32)
+    check(lib().dtts_selftest_gemm_e4m3(A.ctypes.data_as(_u8p), _ptr(a_scale), B.ctypes.data_as(_u8p),
+                                        _ptr(b_scale), _ptr(bias), _ptr(C_), M, N, K, bn, device))
+    return C_
+
+
+def fp8_quantize_rows(w):
+    """The FP8 engine's per-output-channel weight quantisation (host only):
+    returns (e4m3 bytes [rows][cols], scale [rows])."""
+    w = np.ascontiguousarray(w, np.float32)
+    q = np.zeros(w.shape, np.uint8)
+    sc = np.zeros(w.shape[0], np.float32)
+    check(lib().dtts_fp8_quantize_rows(_ptr(w), w.shape[0], w.shape[1], q.ctypes.data_as(_u8p), _ptr(sc)))
+    return q, sc
 
 
 class SafeTensors:

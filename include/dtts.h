@@ -55,7 +55,12 @@ extern "C" {
 #define DTTS_ERR_NO_DEVICE    -8   /* no sm_100 device with that ordinal                */
 
 #define DTTS_DTYPE_BF16  0   /* bf16 weights and activations, fp32 accumulate/residual */
-#define DTTS_DTYPE_FP8   1   /* e4m3 weights, per-output-channel fp32 scales           */
+#define DTTS_DTYPE_FP8   1   /* DiT only: the four block projections in e4m3 x e4m3 ->
+                                 fp32 (tcgen05 kind::f8f6f4); weights with one fp32 scale per
+                                 output channel, activations with one scale per token row
+                                 (LayerNorm outputs: row absmax; attention and GELU outputs:
+                                 a per-row bound, see dtts_fp8_quantize_rows); adaLN,
+                                 input/output layers, attention core and residual as bf16 */
 #define DTTS_DTYPE_F32   2   /* fp32 everywhere (attention sublayer only)              */
 
 #define DTTS_MEM_HOST    0
@@ -277,9 +282,24 @@ int dtts_pe_stream_length(dtts_pe *p, int *tokens);
 /* C[M][N] = A[M][K] B[N][K]^T (+ bias) with the tcgen05 GEMM; bn = 128 or 256 */
 int dtts_selftest_gemm(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, int bn,
                        int device);
+/* C[M][N] = a_scale[m] b_scale[n] sum_k A[m][k] B[n][k] (+ bias) with e4m3 bytes A
+ * [M][K], B [N][K] through the kind::f8f6f4 GEMM; bn = 128 or 256, K % 128 == 0 */
+int dtts_selftest_gemm_e4m3(const uint8_t *A, const float *a_scale, const uint8_t *B, const float *b_scale,
+                            const float *bias, float *C, int M, int N, int K, int bn, int device);
 /* attention core: q [rows][Tq][1024], k/v [rows][kv_len][1024], out like q */
 int dtts_selftest_attention(const float *q, const float *k, const float *v, float *out, int rows, int Tq,
                             int kv_len, const uint8_t *mask, int causal, int q_pos0, int use_f32, int device);
+
+/* e4m3 conversion (round to nearest even, saturating at +-448) of n floats on
+ * the device, the conversion every FP8 kernel uses for its activations. */
+int dtts_selftest_e4m3(const float *x, uint8_t *out, int n, int device);
+
+/* Host only: the FP8 engine's weight quantisation (no counterpart in the
+ * reference, whose DiT is fp32).  w [rows][cols] row-major, one scale per row
+ * (output channel): scale[r] = max_c |w[r][c]| / 448 and q[r][c] =
+ * e4m3(w[r][c] * 448 / max_c |w[r][c]|); an all-zero row gets scale 0.
+ * Dequantised weight = e4m3 value * scale. */
+int dtts_fp8_quantize_rows(const float *w, int rows, int cols, uint8_t *q, float *scale);
 
 /* ------------------------------------------------------------------ safetensors (host only) */
 typedef struct dtts_st dtts_st;

@@ -233,8 +233,13 @@ static void dit_adaln(float *ada, const float *cond, const float *w, const float
     }
 }
 
+static void dit_block_fwd_fp8(float *out, const float *x, const float *cond, const orc_dit_block *b,
+                              int L, const uint8_t *mask, const float *pos);
+static int g_dit_fp8;
+
 void orc_dit_block_fwd(float *out, const float *x, const float *cond, const orc_dit_block *b,
                        int L, const uint8_t *mask, const float *pos, int ffn_mode) {
+    if (g_dit_fp8 && ffn_mode == ORC_FFN_PER_TOKEN) { dit_block_fwd_fp8(out, x, cond, b, L, mask, pos); return; }
     const int D = ORC_D;
     float *ada = (float *)malloc(6 * D * sizeof(float));
     dit_adaln(ada, cond, b->ada_w, b->ada_b, 6 * D);
@@ -264,6 +269,212 @@ void orc_dit_block_fwd(float *out, const float *x, const float *cond, const orc_
     orc_linear_rows(f2, f1, rows, b->w2, b->b2, ORC_F, D);
     for (size_t i = 0; i < n; i++) out[i] = h[i] + gml[i % D] * f2[i];
     free(ada); free(mod); free(ao); free(h); free(f1); free(f2);
+}
+
+/* --------------------------------------------------------------------------
+ * FP8 (e4m3) arithmetic of the engine's FP8 weight path, restated on the CPU.
+ * This path has no counterpart in the reference (whose DiT is fp32): it is the
+ * exact quantisation recipe of the engine's DTTS_DTYPE_FP8 mode, so the engine
+ * can be checked against it at the bf16 tolerance, and against the fp32 block
+ * at the FP8 tolerance.
+ *   e4m3: 1 sign, 4 exponent (bias 7), 3 mantissa bits; largest finite 448;
+ *   subnormals m * 2^-9; round to nearest even, saturating at +-448.
+ *   weights: per output channel, s_w = amax / 448, q = e4m3(w * (448 / amax)).
+ *   LN outputs (QKV and FFN1 inputs): per row, s = amax / 448.
+ *   attention output (O input): per row s_o = B / 448 with
+ *     B = 1.02 * max_{j in sequence} unorm_j * max_d |Wv_d|,  unorm = 1.08 |u|,
+ *     a bound on |softmax . V| (a convex mix of V rows).
+ *   GELU output (FFN2 input): per row s_g = 1.02 * max(unorm2 * max_j |W1_j|
+ *     + max_j |b1_j|, 0.17) / 448, a bound on |gelu(W1 u + b1)|.
+ * ------------------------------------------------------------------------ */
+uint8_t orc_e4m3_encode(float x) {
+    const uint8_t sign = signbit(x) ? 0x80 : 0;
+    if (isnan(x)) return 0x7F;
+    const float a = fabsf(x);
+    if (a >= 448.0f) return sign | 0x7E;
+    if (a < 0.015625f) return sign | (uint8_t)rintf(a * 512.0f);   /* subnormal; 8 -> 2^-6 */
+    int e;
+    frexpf(a, &e);
+    int E = e - 1;                                   /* a in [2^E, 2^(E+1)) */
+    float q = rintf(ldexpf(a, 3 - E));               /* 1.mmm scaled to [8, 16] */
+    if (q >= 16.0f) { q = 8.0f; E += 1; }
+    if (E > 8 || (E == 8 && q > 14.0f)) return sign | 0x7E;
+    return sign | (uint8_t)(((E + 7) << 3) | ((int)q - 8));
+}
+
+float orc_e4m3_decode(uint8_t b) {
+    const int E = (b >> 3) & 15, m = b & 7;
+    if (E == 15 && m == 7) return NAN;
+    const float v = E == 0 ? ldexpf((float)m, -9) : ldexpf((float)(8 + m), E - 10);
+    return (b & 0x80) ? -v : v;
+}
+
+static float fq(float x, float inv, float s) { return orc_e4m3_decode(orc_e4m3_encode(x * inv)) * s; }
+
+static float row_amax(const float *x, int n) {
+    float m = 0.0f;
+    for (int i = 0; i < n; i++) m = fmaxf(m, fabsf(x[i]));
+    return m;
+}
+
+static float row_norm(const float *x, int n) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s += x[i] * x[i];
+    return sqrtf(s);
+}
+
+/* per-row quantise-dequantise with the row's own absmax */
+static void fq_row_amax(float *x, int n) {
+    const float amax = row_amax(x, n);
+    if (amax == 0.0f) return;
+    const float inv = 448.0f / amax, s = amax / 448.0f;
+    for (int i = 0; i < n; i++) x[i] = fq(x[i], inv, s);
+}
+
+/* fake-quantised copy of one [rows][cols] weight, per output row; also the
+ * largest dequantised row norm */
+typedef struct { const float *src; size_t n; float probe; float *w; float max_norm; } fq_weight;
+#define FQ_CACHE 160
+static fq_weight g_fq[FQ_CACHE];
+static int g_fq_n = 0;
+static int g_dit_fp8 = 0;
+
+void orc_set_dit_fp8(int on) {
+    for (int i = 0; i < g_fq_n; i++) free(g_fq[i].w);
+    g_fq_n = 0;
+    g_dit_fp8 = on;
+}
+
+static const fq_weight *fq_weight_get(const float *w, int rows, int cols) {
+    const size_t n = (size_t)rows * cols;
+    const float probe = w[0] + w[n / 2] + w[n - 1];
+    for (int i = 0; i < g_fq_n; i++)
+        if (g_fq[i].src == w && g_fq[i].n == n && g_fq[i].probe == probe) return &g_fq[i];
+    fq_weight *e = &g_fq[g_fq_n++];
+    e->src = w; e->n = n; e->probe = probe;
+    e->w = (float *)malloc(n * sizeof(float));
+    float mn = 0.0f;
+    #pragma omp parallel for schedule(static) reduction(max:mn)
+    for (int r = 0; r < rows; r++) {
+        const float *src = w + (size_t)r * cols;
+        float *dst = e->w + (size_t)r * cols;
+        const float amax = row_amax(src, cols);
+        if (amax == 0.0f) {
+            memset(dst, 0, (size_t)cols * sizeof(float));
+        } else {
+            const float inv = 448.0f / amax, sc = amax / 448.0f;
+            for (int c = 0; c < cols; c++) dst[c] = fq(src[c], inv, sc);
+        }
+        mn = fmaxf(mn, row_norm(dst, cols));
+    }
+    e->max_norm = mn;
+    return e;
+}
+
+/* DiT block with the engine's FP8 arithmetic (FFN on every token). */
+static void dit_block_fwd_fp8(float *out, const float *x, const float *cond, const orc_dit_block *b,
+                              int L, const uint8_t *mask, const float *pos) {
+    const int D = ORC_D;
+    float *ada = (float *)malloc(6 * D * sizeof(float));
+    dit_adaln(ada, cond, b->ada_w, b->ada_b, 6 * D);
+    const float *sm = ada, *scm = ada + D, *gm = ada + 2 * D;
+    const float *sml = ada + 3 * D, *scl = ada + 4 * D, *gml = ada + 5 * D;
+    if (g_fq_n + 6 > FQ_CACHE) orc_set_dit_fp8(g_dit_fp8);   /* cache full: start over */
+    const fq_weight *wq = fq_weight_get(b->wq, D, D), *wk = fq_weight_get(b->wk, D, D);
+    const fq_weight *wv = fq_weight_get(b->wv, D, D), *wo = fq_weight_get(b->wo, D, D);
+    const fq_weight *w1 = fq_weight_get(b->w1, ORC_F, D), *w2 = fq_weight_get(b->w2, D, ORC_F);
+    float b1max = 0.0f;
+    for (int j = 0; j < ORC_F; j++) b1max = fmaxf(b1max, fabsf(b->b1 ? b->b1[j] : 0.0f));
+    size_t n = (size_t)L * D;
+    float *mod = (float *)malloc(n * sizeof(float));
+    float *h = (float *)malloc(n * sizeof(float));
+    float *q = (float *)malloc(n * sizeof(float));
+    float *k = (float *)malloc(n * sizeof(float));
+    float *v = (float *)malloc(n * sizeof(float));
+    float *ctx = (float *)malloc(n * sizeof(float));
+    float *ao = (float *)malloc(n * sizeof(float));
+    float *unorm = (float *)malloc((size_t)L * sizeof(float));
+    for (int t = 0; t < L; t++) {
+        float *mr = mod + (size_t)t * D;
+        ln_noaffine(mr, x + (size_t)t * D, D);
+        for (int i = 0; i < D; i++) mr[i] = mr[i] * (1.0f + scm[i]) + sm[i];
+        unorm[t] = 1.08f * row_norm(mr, D);
+        fq_row_amax(mr, D);
+    }
+    orc_linear_rows(q, mod, L, wq->w, NULL, D, D);
+    orc_linear_rows(k, mod, L, wk->w, NULL, D, D);
+    orc_linear_rows(v, mod, L, wv->w, NULL, D, D);
+    for (int t = 0; t < L; t++)
+        for (int hh = 0; hh < ORC_H; hh++) {
+            float *qh = q + (size_t)t * D + hh * ORC_HD, *kh = k + (size_t)t * D + hh * ORC_HD;
+            rms_head(qh, b->qn);
+            rms_head(kh, b->kn);
+            if (g_dit_rope == ORC_ROPE_ADJACENT) {
+                rope_adjacent(qh, pos ? (int)pos[t] : t);
+                rope_adjacent(kh, pos ? (int)pos[t] : t);
+            } else {
+                rope_half(qh, kh, pos ? pos[t] : (float)t);
+            }
+        }
+    const float scale = 1.0f / sqrtf((float)ORC_HD);
+    #pragma omp parallel
+    {
+        float *sc = (float *)malloc((size_t)L * sizeof(float));
+        #pragma omp for collapse(2) schedule(static)
+        for (int hh = 0; hh < ORC_H; hh++)
+            for (int i = 0; i < L; i++) {
+                const float *qi = q + (size_t)i * D + hh * ORC_HD;
+                for (int j = 0; j < L; j++) {
+                    const float *kj = k + (size_t)j * D + hh * ORC_HD;
+                    float acc = 0.0f;
+                    for (int d = 0; d < ORC_HD; d++) acc += qi[d] * kj[d];
+                    sc[j] = acc * scale;
+                    if (mask && !mask[(size_t)i * L + j]) sc[j] = -INFINITY;
+                }
+                float mx = sc[0];
+                for (int j = 1; j < L; j++) if (sc[j] > mx) mx = sc[j];
+                float sum = 0.0f;
+                for (int j = 0; j < L; j++) { sc[j] = expf(sc[j] - mx); sum += sc[j]; }
+                for (int j = 0; j < L; j++) sc[j] /= sum;
+                float *ci = ctx + (size_t)i * D + hh * ORC_HD;
+                for (int d = 0; d < ORC_HD; d++) {
+                    float acc = 0.0f;
+                    for (int j = 0; j < L; j++) acc += sc[j] * v[(size_t)j * D + hh * ORC_HD + d];
+                    ci[d] = acc;
+                }
+            }
+        free(sc);
+    }
+    /* attention output: one scale per sequence from the bound on |V| */
+    float umax = 0.0f;
+    for (int t = 0; t < L; t++) umax = fmaxf(umax, unorm[t]);
+    const float bo_ = 1.02f * umax * wv->max_norm;
+    if (bo_ > 0.0f) {
+        const float inv = 448.0f / bo_, s = bo_ / 448.0f;
+        for (size_t i = 0; i < n; i++) ctx[i] = fq(ctx[i], inv, s);
+    }
+    orc_linear_rows(ao, ctx, L, wo->w, b->bo, D, D);
+    for (size_t i = 0; i < n; i++) h[i] = x[i] + gm[i % D] * ao[i];
+    float *sg = (float *)malloc((size_t)L * sizeof(float));
+    for (int t = 0; t < L; t++) {
+        float *mr = mod + (size_t)t * D;
+        ln_noaffine(mr, h + (size_t)t * D, D);
+        for (int i = 0; i < D; i++) mr[i] = mr[i] * (1.0f + scl[i]) + sml[i];
+        sg[t] = 1.02f * fmaxf(1.08f * row_norm(mr, D) * w1->max_norm + b1max, 0.17f);
+        fq_row_amax(mr, D);
+    }
+    float *f1 = (float *)malloc((size_t)L * ORC_F * sizeof(float));
+    float *f2 = (float *)malloc(n * sizeof(float));
+    orc_linear_rows(f1, mod, L, w1->w, b->b1, D, ORC_F);
+    for (int t = 0; t < L; t++) {
+        const float inv = 448.0f / sg[t], s = sg[t] / 448.0f;
+        float *fr = f1 + (size_t)t * ORC_F;
+        for (int j = 0; j < ORC_F; j++) fr[j] = fq(gelu_tanh(fr[j]), inv, s);
+    }
+    orc_linear_rows(f2, f1, L, w2->w, b->b2, ORC_F, D);
+    for (size_t i = 0; i < n; i++) out[i] = h[i] + gml[i % D] * f2[i];
+    free(ada); free(mod); free(h); free(q); free(k); free(v); free(ctx); free(ao); free(unorm);
+    free(sg); free(f1); free(f2);
 }
 
 /* --------------------------------------------------------------------------

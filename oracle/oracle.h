@@ -84,6 +84,14 @@ typedef struct {
 #define ORC_PAIR_ADJACENT  0   /* output p = out_proj([h_2p | h_2p+1])        */
 #define ORC_PAIR_AS_WRITTEN 1  /* ggml permute as written, patchenc.cpp:230-232 */
 
+/* FP8 (e4m3) quantisation recipe of the engine's FP8 weight path (no
+ * counterpart in the reference, whose DiT is fp32): orc_set_dit_fp8(1) makes
+ * every DiT block (FFN per token) use it; (0) restores fp32.  Both calls drop
+ * the cache of fake-quantised weights. */
+void    orc_set_dit_fp8(int on);
+uint8_t orc_e4m3_encode(float x);
+float   orc_e4m3_decode(uint8_t b);
+
 int  orc_num_threads(void);
 void orc_set_dit_rope(int mode);
 void orc_set_threads(int n);

@@ -175,6 +175,11 @@ class Oracle:
         L.orc_num_threads.restype = C.c_int
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_set_dit_rope.argtypes = [C.c_int]
+        L.orc_set_dit_fp8.argtypes = [C.c_int]
+        L.orc_e4m3_encode.argtypes = [C.c_float]
+        L.orc_e4m3_encode.restype = C.c_uint8
+        L.orc_e4m3_decode.argtypes = [C.c_uint8]
+        L.orc_e4m3_decode.restype = C.c_float
         L.orc_sinusoid.argtypes = [C.c_float, _fp]
         L.orc_compute_cond.argtypes = [C.POINTER(Dit), C.c_float, _fp, C.c_float, _fp]
         L.orc_attention.argtypes = [_fp, _fp, C.c_int] + [_fp] * 7 + [_u8p, _fp]
@@ -196,6 +201,18 @@ class Oracle:
 
     def num_threads(self):
         return self.lib.orc_num_threads()
+
+    def set_dit_fp8(self, on):
+        """1: DiT blocks use the engine's FP8 (e4m3) recipe; 0: fp32."""
+        self.lib.orc_set_dit_fp8(int(on))
+
+    def e4m3_encode(self, x):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        return np.array([self.lib.orc_e4m3_encode(C.c_float(float(v))) for v in x], np.uint8)
+
+    def e4m3_decode(self, b):
+        b = np.ascontiguousarray(b, np.uint8).ravel()
+        return np.array([self.lib.orc_e4m3_decode(C.c_uint8(int(v))) for v in b], np.float32)
 
     def sinusoid(self, t):
         se = np.zeros(256, np.float32)

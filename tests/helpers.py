@@ -53,3 +53,43 @@ def write_safetensors(path, tensors, metadata=None):
         f.write(h)
         for b in blobs:
             f.write(b)
+
+
+# FP8 (e4m3) path against the fp32 reference: the quantisation itself moves the
+# velocity by a few percent (3.8% max relative error, cosine 0.9993 on a
+# 2-layer model), so this bar is wider; against the oracle's restatement of the
+# same FP8 recipe the engine meets the bf16 bar above.
+FP8_REL, FP8_COS = 1e-1, 0.995
+# FP8 engine against the oracle's restatement of the same recipe: tiny
+# upstream differences (bf16 intermediates) flip single e4m3 roundings, each a
+# whole quantum (6-12%), so the two agree to cosine 0.999 but not element-wise
+# to the bf16 bar.  The GEMM itself is pinned tightly by the e4m3 GEMM test.
+FP8_ORACLE_REL, FP8_ORACLE_COS = 5e-2, 0.999
+# A whole Euler solve (18 layers, CFG scale 2 amplifies velocity differences
+# threefold): the recipe's own displacement error against fp32 is 14% max
+# relative, cosine 0.993, and the engine is held to the same order.
+FP8_SOLVE_REL, FP8_SOLVE_COS = 2.5e-1, 0.985
+
+
+def assert_fp8_close(got, want, what=""):
+    r, c = rel(got, want), cos(got, want)
+    assert r <= FP8_REL and c >= FP8_COS, f"{what}: max rel {r:.3e} (<= {FP8_REL}), cos {c:.6f} (>= {FP8_COS})"
+
+
+def assert_fp8_recipe_close(got, want, what=""):
+    r, c = rel(got, want), cos(got, want)
+    assert r <= FP8_ORACLE_REL and c >= FP8_ORACLE_COS, \
+        f"{what}: max rel {r:.3e} (<= {FP8_ORACLE_REL}), cos {c:.6f} (>= {FP8_ORACLE_COS})"
+
+
+def assert_fp8_solve_close(got, want, what=""):
+    r, c = rel(got, want), cos(got, want)
+    assert r <= FP8_SOLVE_REL and c >= FP8_SOLVE_COS, \
+        f"{what}: max rel {r:.3e} (<= {FP8_SOLVE_REL}), cos {c:.6f} (>= {FP8_SOLVE_COS})"
+
+
+def assert_no_worse_than_recipe(got, recipe, exact, what=""):
+    """The engine's distance from the fp32 result is of the order of the FP8
+    recipe's own: 1 - cos(got, exact) <= 1.5 (1 - cos(recipe, exact)) + 1e-4."""
+    e_got, e_rec = 1.0 - cos(got, exact), 1.0 - cos(recipe, exact)
+    assert e_got <= 1.5 * e_rec + 1e-4, f"{what}: 1-cos {e_got:.3e} against the recipe's {e_rec:.3e}"
