@@ -50,8 +50,9 @@ def parse():
     ap.add_argument("--patch", type=int, default=4)
     ap.add_argument("--nfe", type=int, default=10)
     ap.add_argument("--layers", type=int, default=18)
-    ap.add_argument("--dtype", choices=["bf16", "fp8"], default="bf16",
-                    help="block projection weights: bf16, or e4m3 with per-channel scales")
+    ap.add_argument("--dtype", choices=["both", "bf16", "fp8"], default="both",
+                    help="block projection weights: bf16, e4m3 with per-channel scales, or both "
+                         "(bf16 is the headline line, the e4m3 run is added under the key fp8)")
     ap.add_argument("--cfg-scale", type=float, default=2.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -132,17 +133,17 @@ def make_inputs(args, rank):
     return w, fc, fu, z0, spk
 
 
-def workload_config(args, n):
+def workload_config(args, n, dtype="bf16"):
     L = args.fm_len + args.patch
     return {"workload": f"DiT Euler solve, {args.layers} layers, CFG pair, v4 FM layout",
             "n_utt_per_gpu": args.n_utt, "cfg_rows_per_gpu": 2 * args.n_utt, "seq_len": L,
             "fm_len": args.fm_len, "patch": args.patch, "nfe": args.nfe, "cfg_scale": args.cfg_scale,
-            "weights": ("bf16 (fp32 accumulate, fp32 residual)" if args.dtype == "bf16" else
+            "weights": ("bf16 (fp32 accumulate, fp32 residual)" if dtype == "bf16" else
                         "block projections e4m3 x e4m3 (per-channel weight scales, per-row activation scales), "
                         "fp32 accumulate; adaLN/input/output bf16; fp32 residual"),
             "global_utterances": args.n_utt * n,
             "parallelism": f"utterance shards x{n}, no collective",
-            "l2": "working set > L2: %s of weights streamed per forward" % ("0.69 GB" if args.dtype == "bf16" else "0.36 GB"),
+            "l2": "working set > L2: %s of weights streamed per forward" % ("0.69 GB" if dtype == "bf16" else "0.36 GB"),
             "graph": "whole solve in one CUDA graph"}
 
 
@@ -214,20 +215,17 @@ def load_traffic():
         return None
 
 
-def run_ours(args, rank, world, local_rank):
+def measure(args, dtype, world, local_rank, dist, inputs):
+    """Times one engine (dtype "bf16" or "fp8") on this rank: the resident-input
+    solve loop (value), the same through host buffers (e2e), then the in-place
+    launch timeline and each GEMM alone (roofline).  Every rank takes the same
+    collective steps."""
     import torch
     import dtts
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    w, fc, fu, z0, spk = make_inputs(args, rank)
+    w, fc, fu, z0, spk = inputs
     eng = dtts.DiT(w, n_layers=args.layers, device=local_rank,
-                   dtype=dtts.DTYPE_FP8 if args.dtype == "fp8" else dtts.DTYPE_BF16)
+                   dtype=dtts.DTYPE_FP8 if dtype == "fp8" else dtts.DTYPE_BF16)
     stream = torch.cuda.Stream(device=dev)
     eng.set_stream(stream.cuda_stream)
     kw = dict(spk_scale=1.5, nfe=args.nfe, cfg_scale=args.cfg_scale, cfg_form=dtts.CFG_V4,
@@ -328,12 +326,12 @@ def run_ours(args, rank, world, local_rank):
         burst = peaks.get("bf16_tflops", 1590.0)
         src = ("measured bf16_tflops_sustained (kernels timed inside the long solve)" if "bf16_tflops_sustained" in peaks
                else "fallback sustained figure")
-        if args.dtype == "fp8":
+        if dtype == "fp8":
             # no e4m3 measurement exists for this pool: the dense e4m3 tensor
             # rate of B200 is twice its bf16 rate, so twice the measured figure
             peak, burst = 2 * peak, 2 * burst
             src = "2 x " + src + " (dense e4m3 = 2 x bf16 tensor rate)"
-        tr = load_traffic()
+        tr = load_traffic() if dtype == "bf16" else None
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": tr.get("bytes_per_launch") if tr else None,
                 "kernel": "gemm_tc_kernel (tcgen05): QKV + O + FFN1 + FFN2 of one block, FLOP-weighted",
@@ -341,6 +339,28 @@ def run_ours(args, rank, world, local_rank):
                 "algorithmic_flops_per_launch": f,
                 "traffic_source": tr.get("source") if tr else None}
         attn_us = kernels["attention"]["us_per_launch"]
+    eng.close()
+    return {"value": value, "ms_per_step": ms / args.steps,
+            "e2e": None if e2e_value is None else {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                                                    "d2h_bytes_per_step": d2h},
+            "roofline": roof, "attention_us_per_layer": attn_us, "kernels_in_place": kernels,
+            "timeline_solve_ms": timeline_ms, "kernels_alone_us": alone, "clocks": clocks,
+            "gpu_launches": launches_per_solve * args.steps}
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    inputs = make_inputs(args, rank)
+    head_dtype = "fp8" if args.dtype == "fp8" else "bf16"
+    head = measure(args, head_dtype, world, local_rank, dist, inputs)
+    extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
 
     # ---- CPU baseline: reference code (per-token FFN) on the host, rank 0, N = 1
     cpu = None
@@ -348,6 +368,7 @@ def run_ours(args, rank, world, local_rank):
         sys.path.insert(0, os.path.join(HERE, "oracle"))
         import oracle as O
         if O.Reference.available():
+            w, fc, fu, z0, spk = inputs
             secs, cores = cpu_reference_eval(args, w, fc, fu, z0, spk, O.FFN_PER_TOKEN)
             cpu = {"value": 1.0 / secs, "unit": UNIT, "cores": cores, "kind": "reference",
                    "sample": "one CFG-pair eval (2 rows, L=%d, %d layers) through the reference's "
@@ -356,24 +377,23 @@ def run_ours(args, rank, world, local_rank):
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if args.dtype == "bf16" else "e4m3",
+            "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if head_dtype == "bf16" else "e4m3",
             "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights)",
-            "config": workload_config(args, world),
-            "e2e": None if e2e_value is None else {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                                                    "d2h_bytes_per_step": d2h},
-            "roofline": roof,
-            "attention_us_per_layer": attn_us,
-            "kernels_in_place": kernels,
-            "timeline_solve_ms": timeline_ms,
-            "kernels_alone_us": alone,
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-            "gpu_launches": launches_per_solve * args.steps,
+            "config": workload_config(args, world, head_dtype),
         }
+        for k in ("e2e", "roofline", "attention_us_per_layer", "kernels_in_place", "timeline_solve_ms",
+                  "kernels_alone_us"):
+            line[k] = head[k]
+        line["cpu_baseline"] = cpu
+        line["clocks"] = head["clocks"]
+        line["gpu_launches"] = head["gpu_launches"]
+        if extra:
+            line["fp8"] = {"dtype": "e4m3", "weights": workload_config(args, world, "fp8")["weights"],
+                           **{k: extra[k] for k in ("value", "ms_per_step", "e2e", "roofline", "attention_us_per_layer",
+                                                    "kernels_in_place", "clocks", "gpu_launches")}}
         print(json.dumps(line))
-    eng.close()
     if dist:
         dist.destroy_process_group()
 

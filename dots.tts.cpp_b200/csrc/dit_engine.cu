@@ -197,7 +197,7 @@ struct dtts_dit {
     // defaults from a sweep on B200 at 128 CFG rows x L = 64 (8192 tokens); no
     // K split by default, so every result is bit-reproducible (split partials
     // reach the residual in run-dependent order)
-    GemmTune tu_qkv{192, 8, 1}, tu_o{256, 4, 1}, tu_ffn1{256, 4, 1}, tu_ffn2{256, 4, 1}, tu_ada{256, 8, 1},
+    GemmTune tu_qkv{256, 8, 1}, tu_o{256, 4, 1}, tu_ffn1{256, 4, 1}, tu_ffn2{256, 4, 1}, tu_ada{256, 8, 1},
         tu_in{256, 4, 1};
     float *t_w1 = nullptr, *t_b1 = nullptr, *t_w2 = nullptr, *t_b2 = nullptr;
     float *spk_w1 = nullptr, *spk_b1 = nullptr, *spk_lw = nullptr, *spk_lb = nullptr;

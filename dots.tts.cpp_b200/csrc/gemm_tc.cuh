@@ -369,6 +369,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
         const int quad = warp & 3;
         float *sgain = nullptr;
         const float4 *srope = nullptr;
+        const bool kv_dense = ep.kv_cap == ep.tok_per_row && ep.kv_start == 0;
         if constexpr (EPI == EPI_QKV) {
             sgain = reinterpret_cast<float *>(sConst);
             float2 *rp = reinterpret_cast<float2 *>(sConst + 512);
@@ -450,8 +451,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                             if (sect == 0) {
                                 dst = ep.q + (long long)m * ep.ldq + col;
                             } else {
-                                const long long row = (long long)(m / ep.tok_per_row) * ep.kv_cap + ep.kv_start +
-                                                      (m % ep.tok_per_row);
+                                // token m of sequence m / T sits at row m of a dense cache (the DiT)
+                                const long long row = kv_dense ? (long long)m
+                                                               : (long long)(m / ep.tok_per_row) * ep.kv_cap +
+                                                                     ep.kv_start + (m % ep.tok_per_row);
                                 dst = (sect == 1 ? ep.k : ep.v) + row * ep.ldkv + col;
                             }
                         } else {
