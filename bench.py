@@ -135,16 +135,22 @@ def make_inputs(args, rank):
 
 def workload_config(args, n, dtype="bf16"):
     L = args.fm_len + args.patch
-    return {"workload": f"DiT Euler solve, {args.layers} layers, CFG pair, v4 FM layout",
-            "n_utt_per_gpu": args.n_utt, "cfg_rows_per_gpu": 2 * args.n_utt, "seq_len": L,
-            "fm_len": args.fm_len, "patch": args.patch, "nfe": args.nfe, "cfg_scale": args.cfg_scale,
-            "weights": ("bf16 (fp32 accumulate, fp32 residual)" if dtype == "bf16" else
-                        "block projections e4m3 x e4m3 (per-channel weight scales, per-row activation scales), "
-                        "fp32 accumulate; adaLN/input/output bf16; fp32 residual"),
-            "global_utterances": args.n_utt * n,
-            "parallelism": f"utterance shards x{n}, no collective",
-            "l2": "working set > L2: %s of weights streamed per forward" % ("0.69 GB" if dtype == "bf16" else "0.36 GB"),
-            "graph": "whole solve in one CUDA graph"}
+    cfg = {"workload": f"DiT Euler solve, {args.layers} layers, CFG pair, v4 FM layout",
+           "n_utt_per_gpu": args.n_utt, "cfg_rows_per_gpu": 2 * args.n_utt, "seq_len": L,
+           "fm_len": args.fm_len, "patch": args.patch, "nfe": args.nfe, "cfg_scale": args.cfg_scale}
+    if dtype == "f32":
+        cfg.update({"weights": "fp32 (the reference's host arithmetic)",
+                    "sample": "CFG-pair evals of this workload's first utterance at step t = 0"})
+        return cfg
+    cfg.update({
+        "weights": ("bf16 (fp32 accumulate, fp32 residual)" if dtype == "bf16" else
+                    "block projections e4m3 x e4m3 (per-channel weight scales, per-row activation scales), "
+                    "fp32 accumulate; adaLN/input/output bf16; fp32 residual"),
+        "global_utterances": args.n_utt * n,
+        "parallelism": f"utterance shards x{n}, no collective",
+        "l2": "working set > L2: %s of weights streamed per forward" % ("0.69 GB" if dtype == "bf16" else "0.36 GB"),
+        "graph": "whole solve in one CUDA graph"})
+    return cfg
 
 
 def cpu_reference_eval(args, w, fc, fu, z0, spk, ffn_mode):
@@ -199,7 +205,7 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args, 1),
+        "config": workload_config(args, 1, "f32"),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))

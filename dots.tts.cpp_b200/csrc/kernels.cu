@@ -222,15 +222,18 @@ DTTS_DEV void attn_store(const AttnArgs &a, int r, int h, int qi0, int qi1, int 
         const float qs = bnd > 0.f ? 448.0f / bnd : 0.f;
         const float f0 = inv0 * qs, f1 = inv1 * qs;
         uint8_t *og = a.o8 + (long long)r * a.Tq * a.ldo + h * kHD;
+        // lanes t and t^1 swap halves so that each writes 4 consecutive bytes:
+        // even t row qi0, columns 2t..2t+3; odd t row qi1, columns 2t-2..2t+1
+        const bool even = (t & 1) == 0;
 #pragma unroll
         for (int nt = 0; nt < 8; nt++) {
-            const int d = nt * 8 + 2 * t;
-            if (qi0 < a.Tq)
-                *reinterpret_cast<__nv_fp8x2_storage_t *>(og + (long long)qi0 * a.ldo + d) =
-                    __nv_cvt_float2_to_fp8x2(make_float2(o[nt][0] * f0, o[nt][1] * f0), __NV_SATFINITE, __NV_E4M3);
-            if (qi1 < a.Tq)
-                *reinterpret_cast<__nv_fp8x2_storage_t *>(og + (long long)qi1 * a.ldo + d) =
-                    __nv_cvt_float2_to_fp8x2(make_float2(o[nt][2] * f1, o[nt][3] * f1), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(o[nt][0] * f0, o[nt][1] * f0), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(o[nt][2] * f1, o[nt][3] * f1), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, even ? p1 : p0, 1);
+            const int qi = even ? qi0 : qi1;
+            const int d = nt * 8 + 2 * (t & ~1);
+            const uint32_t word = even ? (p0 | (other << 16)) : (other | (p1 << 16));
+            if (qi < a.Tq) *reinterpret_cast<uint32_t *>(og + (long long)qi * a.ldo + d) = word;
         }
         if (h == 0 && t == 0) {
             if (qi0 < a.Tq) a.o_scale[(long long)r * a.Tq + qi0] = bnd / 448.0f;
