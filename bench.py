@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--no-pe", action="store_true", help="skip the PatchEncoder stream measurement")
     return ap.parse_args()
 
 
@@ -354,6 +355,48 @@ def measure(args, dtype, world, local_rank, dist, inputs):
             "gpu_launches": launches_per_solve * args.steps}
 
 
+def measure_pe(args, local_rank):
+    """PatchEncoder stream at the PatchEncoder workload: 32 streams, a 500-frame
+    prefill (250 tokens each), then 125 one-patch decode steps against the KV
+    cache; 24 layers, bf16, device-resident frames, CUDA events on the engine
+    stream.  The decode steps are launched one host call at a time, as a
+    streaming caller would, so launch gaps count."""
+    import torch
+    import dtts
+    import synth
+    dev = torch.device("cuda", local_rank)
+    B, prefill, steps = 32, 500, 125
+    w = synth.pe_weights(2, n_layers=24)
+    pe = dtts.PatchEncoder(w, n_layers=24, max_batch=B, max_tokens=512, device=local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    pe.set_stream(stream.cuda_stream)
+    fr = torch.from_numpy(synth.normal(2, "pe.bench", (B, prefill + 4 * steps, 128), 1.0)).to(dev)
+    pre_in = fr[:, :prefill].contiguous()
+    steps_in = [fr[:, prefill + 4 * i:prefill + 4 * i + 4].contiguous() for i in range(steps)]
+    out_pre = torch.empty((B, prefill // 4, 1536), device=dev)
+    out_step = torch.empty((B, 1, 1536), device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with torch.cuda.stream(stream):
+        for rep in range(2):   # the first pass warms up
+            pe.reset(B)
+            ev[0].record(stream)
+            pe.decode(pre_in, out=out_pre, mem=dtts.MEM_DEVICE)
+            ev[1].record(stream)
+            for i in range(steps):
+                pe.decode(steps_in[i], out=out_step, mem=dtts.MEM_DEVICE)
+            ev[2].record(stream)
+            pe.sync()
+    torch.cuda.synchronize()
+    pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    pe.close()
+    flop_pre = B * 24 * (prefill // 2) * 2 * (4 * 1024 * 1024 + 2 * 1024 * 4096)
+    return {"workload": "PatchEncoder, 24 layers, 32 streams: 500-frame prefill, then 125 decode steps",
+            "prefill_ms": pre_ms, "prefill_frames_per_s": B * prefill / (pre_ms / 1000.0),
+            "prefill_gemm_tflops": flop_pre / (pre_ms / 1000.0) / 1e12,
+            "decode_ms_per_step": dec_ms / steps, "decode_patches_per_s": B * steps / (dec_ms / 1000.0),
+            "dtype": "bf16"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     dist = None
@@ -367,6 +410,7 @@ def run_ours(args, rank, world, local_rank):
     head_dtype = "fp8" if args.dtype == "fp8" else "bf16"
     head = measure(args, head_dtype, world, local_rank, dist, inputs)
     extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
+    pe = measure_pe(args, local_rank) if (world == 1 and not args.no_pe) else None
 
     # ---- CPU baseline: reference code (per-token FFN) on the host, rank 0, N = 1
     cpu = None
@@ -395,6 +439,8 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_baseline"] = cpu
         line["clocks"] = head["clocks"]
         line["gpu_launches"] = head["gpu_launches"]
+        if pe:
+            line["patch_encoder"] = pe
         if extra:
             line["fp8"] = {"dtype": "e4m3", "weights": workload_config(args, world, "fp8")["weights"],
                            **{k: extra[k] for k in ("value", "ms_per_step", "e2e", "roofline", "attention_us_per_layer",
