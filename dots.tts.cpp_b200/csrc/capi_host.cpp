@@ -320,6 +320,10 @@ int dtts_dit_create_from_safetensors(const char *path, int n_layers, int dtype, 
     w.lat_b = H.get(f, "latent_proj.bias", D, false, &st);
     w.coord_w = H.get(f, "coordinate_proj.weight", D * 128, true, &st);
     w.coord_b = H.get(f, "coordinate_proj.bias", D, false, &st);
+    w.eos_w1 = H.get(f, "eos_proj.0.weight", 1536 * 1536, false, &st);   // src/utils/dit_loader.cpp:109-112
+    w.eos_b1 = H.get(f, "eos_proj.0.bias", 1536, false, &st);
+    w.eos_w2 = H.get(f, "eos_proj.2.weight", 2 * 1536, false, &st);
+    w.eos_b2 = H.get(f, "eos_proj.2.bias", 2, false, &st);
     if (st) return st;
     return dtts_dit_create(&w, dtype, device, out);
 }

@@ -26,6 +26,7 @@ using namespace dtts;
 namespace {
 
 constexpr int kAdaPerLayer = 6 * kD;
+constexpr int kFmMaxPatch = 16;   // latent frames per dtts_fm_append_latents call
 
 // launch kinds of the solve timeline (DTTS_TL_* in include/dtts.h); 0..4 are
 // the block-op codes of enqueue_block_op
@@ -203,6 +204,9 @@ struct dtts_dit {
     float *spk_w1 = nullptr, *spk_b1 = nullptr, *spk_lw = nullptr, *spk_lb = nullptr;
     // output and coordinate projections stored transposed: out_wt [1024][128], coord_wt [128][1024]
     float *out_wt = nullptr, *out_b = nullptr, *coord_wt = nullptr, *coord_b = nullptr;
+    // FM history projections and the EOS head (fp32, dtts_fm_*)
+    float *hid_w = nullptr, *hid_b = nullptr, *lat_w = nullptr, *lat_b = nullptr;
+    float *eos_w1 = nullptr, *eos_b1 = nullptr, *eos_w2 = nullptr, *eos_b2 = nullptr;
     int *d_err = nullptr;
     bool has_in = false, has_out = false;
     int rope_mode = ROPE_HALF;   // DTTS_ROPE_HALF / DTTS_ROPE_ADJACENT
@@ -671,6 +675,14 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     if ((st = upload_f32(e->wts, w->out_b, kLat, &e->out_b, s))) return st;
     if ((st = upload_f32_transposed(e->wts, w->coord_w, kD, kLat, &e->coord_wt, s, coord_wt_host))) return st;
     if ((st = upload_f32(e->wts, w->coord_b, kD, &e->coord_b, s))) return st;
+    if ((st = upload_f32(e->wts, w->hid_w, (size_t)kD * kLLM, &e->hid_w, s))) return st;
+    if ((st = upload_f32(e->wts, w->hid_b, kD, &e->hid_b, s))) return st;
+    if ((st = upload_f32(e->wts, w->lat_w, (size_t)kD * kLat, &e->lat_w, s))) return st;
+    if ((st = upload_f32(e->wts, w->lat_b, kD, &e->lat_b, s))) return st;
+    if ((st = upload_f32(e->wts, w->eos_w1, (size_t)kLLM * kLLM, &e->eos_w1, s))) return st;
+    if ((st = upload_f32(e->wts, w->eos_b1, kLLM, &e->eos_b1, s))) return st;
+    if ((st = upload_f32(e->wts, w->eos_w2, (size_t)2 * kLLM, &e->eos_w2, s))) return st;
+    if ((st = upload_f32(e->wts, w->eos_b2, 2, &e->eos_b2, s))) return st;
     DTTS_CUDA(cudaStreamSynchronize(s));
     if ((st = e->build_weight_maps())) return st;
     *out = e.release();
@@ -752,7 +764,12 @@ int dtts_dit_velocity(dtts_dit *e, const float *x_in, const float *cond, const u
     return e->finish(mem == DTTS_MEM_HOST);
 }
 
-int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
+}  // extern "C"
+
+// The solve; fm_stride > 0: fm_cond / fm_uncond are device buffers holding
+// each utterance's rows fm_stride rows apart (the FM history of dtts_fm),
+// whatever a->mem says about the other buffers.
+static int euler_solve_impl(dtts_dit *e, const dtts_solve_args *a, long long fm_stride) {
     DTTS_CHECK(e && a, DTTS_ERR_ARG, "null argument");
     DTTS_CHECK(a->fm_cond && a->fm_uncond && a->z0 && a->z_out, DTTS_ERR_ARG, "null buffer in solve args");
     DTTS_CHECK(a->n_utt >= 1 && a->fm_len >= 0 && a->patch >= 1 && a->nfe >= 1 && a->nfe <= 1000, DTTS_ERR_ARG,
@@ -771,7 +788,11 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
     cudaStream_t s = e->stream;
     const cudaMemcpyKind in_kind = a->mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
     const size_t hist = (size_t)a->n_utt * a->fm_len * kD * 4;
-    if (hist) {
+    if (hist && fm_stride > 0) {
+        const size_t w = (size_t)a->fm_len * kD * 4, sp = (size_t)fm_stride * kD * 4;
+        DTTS_CUDA(cudaMemcpy2DAsync(e->in_a, w, a->fm_cond, sp, w, a->n_utt, cudaMemcpyDeviceToDevice, s));
+        DTTS_CUDA(cudaMemcpy2DAsync(e->in_b, w, a->fm_uncond, sp, w, a->n_utt, cudaMemcpyDeviceToDevice, s));
+    } else if (hist) {
         DTTS_CUDA(cudaMemcpyAsync(e->in_a, a->fm_cond, hist, in_kind, s));
         DTTS_CUDA(cudaMemcpyAsync(e->in_b, a->fm_uncond, hist, in_kind, s));
     }
@@ -835,6 +856,10 @@ int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) {
     DTTS_CUDA(cudaMemcpyAsync(a->z_out, e->z, (size_t)a->n_utt * a->patch * kLat * 4, out_kind, s));
     return e->finish(a->mem == DTTS_MEM_HOST);
 }
+
+extern "C" {
+
+int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a) { return euler_solve_impl(e, a, 0); }
 
 int dtts_dit_blocks(dtts_dit *e, const float *h_in, const float *cond, const uint8_t *mask, const float *pos, int rows,
                     int L, float *h_out, int mem) {
@@ -1071,6 +1096,151 @@ int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us, double 
     if (flops) *flops = f;
     if (bytes) *bytes = b;
     return e->finish(true);
+}
+
+// ---------------------------------------------------------------- FM history
+struct dtts_fm {
+    dtts_dit *e = nullptr;
+    int n_utt = 0, cap = 0, len = 0;
+    DeviceArena mem;
+    float *cond = nullptr, *uncond = nullptr;   // [n_utt][cap][1024]
+    float *tmp = nullptr;                       // [n_utt * kFmMaxPatch][1024] projected rows
+    float *hin = nullptr;                       // [n_utt][1536]
+    float *zin = nullptr;                       // [n_utt][kFmMaxPatch][128]
+    float *h1 = nullptr, *logits = nullptr, *prob = nullptr;   // EOS head
+    float *null_row = nullptr;                  // hidden_proj(0) = its bias
+    ~dtts_fm() { mem.free_all(); }
+};
+
+int dtts_fm_create(dtts_dit *e, int n_utt, int capacity, dtts_fm **out) {
+    DTTS_CHECK(e && out, DTTS_ERR_ARG, "null argument");
+    *out = nullptr;
+    DTTS_CHECK(n_utt >= 1 && capacity >= 1 && capacity <= 4096, DTTS_ERR_ARG, "bad FM history shape %d x %d", n_utt,
+               capacity);
+    DTTS_CHECK(e->hid_w && e->lat_w, DTTS_ERR_ARG, "the model lacks hidden_proj / latent_proj weights");
+    DeviceGuard g(e->device);
+    std::unique_ptr<dtts_fm> f(new dtts_fm());
+    f->e = e; f->n_utt = n_utt; f->cap = capacity;
+    const size_t rows = (size_t)n_utt * capacity;
+    auto A = [&](size_t bytes) { return (float *)f->mem.alloc(bytes); };
+    f->cond = A(rows * kD * 4);
+    f->uncond = A(rows * kD * 4);
+    f->tmp = A((size_t)n_utt * kFmMaxPatch * kD * 4);
+    f->hin = A((size_t)n_utt * kLLM * 4);
+    f->zin = A((size_t)n_utt * kFmMaxPatch * kLat * 4);
+    f->h1 = A((size_t)n_utt * kLLM * 4);
+    f->logits = A((size_t)n_utt * 2 * 4);
+    f->prob = A((size_t)n_utt * 4);
+    f->null_row = A((size_t)kD * 4);
+    DTTS_CHECK(f->cond && f->uncond && f->tmp && f->hin && f->zin && f->h1 && f->logits && f->prob && f->null_row,
+               DTTS_ERR_OOM, "FM history allocation failed");
+    // hidden_proj of a zero vector is its bias (src/e2e_pipeline_v4.cpp:338-339)
+    if (e->hid_b)
+        DTTS_CUDA(cudaMemcpyAsync(f->null_row, e->hid_b, (size_t)kD * 4, cudaMemcpyDeviceToDevice, e->stream));
+    else
+        DTTS_CUDA(cudaMemsetAsync(f->null_row, 0, (size_t)kD * 4, e->stream));
+    DTTS_CUDA(cudaStreamSynchronize(e->stream));
+    *out = f.release();
+    return DTTS_OK;
+}
+
+int dtts_fm_destroy(dtts_fm *f) {
+    if (!f) return DTTS_OK;
+    DeviceGuard g(f->e->device);
+    cudaStreamSynchronize(f->e->stream);
+    delete f;
+    return DTTS_OK;
+}
+
+static int fm_copy_in(dtts_fm *f, float *dst, const float *src, size_t bytes, int mem) {
+    DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
+    DTTS_CUDA(cudaMemcpyAsync(dst, src, bytes, mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                              f->e->stream));
+    return DTTS_OK;
+}
+
+int dtts_fm_start(dtts_fm *f, const float *hidden0, int mem) {
+    DTTS_CHECK(f && hidden0, DTTS_ERR_ARG, "null argument");
+    dtts_dit *e = f->e;
+    DeviceGuard g(e->device);
+    int st = fm_copy_in(f, f->hin, hidden0, (size_t)f->n_utt * kLLM * 4, mem);
+    if (st) return st;
+    launch_gemm_f32(f->hin, e->hid_w, e->hid_b, f->tmp, f->n_utt, kD, kLLM, e->stream);
+    launch_fm_place_rows(f->tmp, f->cond, f->n_utt, 1, f->cap, 0, 0, e->stream);
+    launch_fm_place_rows(f->null_row, f->uncond, f->n_utt, 1, f->cap, 0, 1, e->stream);
+    DTTS_CUDA(cudaGetLastError());
+    f->len = 1;
+    return e->finish(mem == DTTS_MEM_HOST);
+}
+
+int dtts_fm_append_latents(dtts_fm *f, const float *z, int patch, int mem) {
+    DTTS_CHECK(f && z, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(f->len >= 1, DTTS_ERR_ARG, "call dtts_fm_start first");
+    DTTS_CHECK(patch >= 1 && patch <= kFmMaxPatch, DTTS_ERR_ARG, "patch %d out of [1, %d]", patch, kFmMaxPatch);
+    DTTS_CHECK(f->len + patch <= f->cap, DTTS_ERR_ARG, "FM history full (%d + %d > %d rows)", f->len, patch, f->cap);
+    dtts_dit *e = f->e;
+    DeviceGuard g(e->device);
+    int st = fm_copy_in(f, f->zin, z, (size_t)f->n_utt * patch * kLat * 4, mem);
+    if (st) return st;
+    launch_gemm_f32(f->zin, e->lat_w, e->lat_b, f->tmp, f->n_utt * patch, kD, kLat, e->stream);
+    launch_fm_place_rows(f->tmp, f->cond, f->n_utt, patch, f->cap, f->len, 0, e->stream);
+    launch_fm_place_rows(f->tmp, f->uncond, f->n_utt, patch, f->cap, f->len, 0, e->stream);
+    DTTS_CUDA(cudaGetLastError());
+    f->len += patch;
+    return e->finish(mem == DTTS_MEM_HOST);
+}
+
+int dtts_fm_append_hidden(dtts_fm *f, const float *h, float *eos_prob, int eos_act, int mem) {
+    DTTS_CHECK(f && h, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(f->len >= 1, DTTS_ERR_ARG, "call dtts_fm_start first");
+    DTTS_CHECK(f->len + 1 <= f->cap, DTTS_ERR_ARG, "FM history full (%d rows)", f->cap);
+    DTTS_CHECK(eos_act == DTTS_EOS_SILU || eos_act == DTTS_EOS_AS_WRITTEN, DTTS_ERR_ARG, "bad eos_act %d", eos_act);
+    dtts_dit *e = f->e;
+    DTTS_CHECK(!eos_prob || (e->eos_w1 && e->eos_w2), DTTS_ERR_ARG, "the model lacks eos_proj weights");
+    DeviceGuard g(e->device);
+    int st = fm_copy_in(f, f->hin, h, (size_t)f->n_utt * kLLM * 4, mem);
+    if (st) return st;
+    launch_gemm_f32(f->hin, e->hid_w, e->hid_b, f->tmp, f->n_utt, kD, kLLM, e->stream);
+    launch_fm_place_rows(f->tmp, f->cond, f->n_utt, 1, f->cap, f->len, 0, e->stream);
+    launch_fm_place_rows(f->null_row, f->uncond, f->n_utt, 1, f->cap, f->len, 1, e->stream);
+    if (eos_prob) {
+        launch_gemm_f32(f->hin, e->eos_w1, e->eos_b1, f->h1, f->n_utt, kLLM, kLLM, e->stream);
+        launch_eos_act(f->h1, f->n_utt, eos_act == DTTS_EOS_AS_WRITTEN, e->stream);
+        launch_gemm_f32(f->h1, e->eos_w2, e->eos_b2, f->logits, f->n_utt, 2, kLLM, e->stream);
+        launch_eos_prob(f->logits, f->n_utt, f->prob, e->stream);
+        DTTS_CUDA(cudaMemcpyAsync(eos_prob, f->prob, (size_t)f->n_utt * 4,
+                                  mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, e->stream));
+    }
+    DTTS_CUDA(cudaGetLastError());
+    f->len += 1;
+    return e->finish(mem == DTTS_MEM_HOST);
+}
+
+int dtts_fm_length(dtts_fm *f, int *rows) {
+    DTTS_CHECK(f && rows, DTTS_ERR_ARG, "null argument");
+    *rows = f->len;
+    return DTTS_OK;
+}
+
+int dtts_fm_read(dtts_fm *f, float *cond, float *uncond) {
+    DTTS_CHECK(f && cond && uncond, DTTS_ERR_ARG, "null argument");
+    dtts_dit *e = f->e;
+    DeviceGuard g(e->device);
+    const size_t w = (size_t)f->len * kD * 4, sp = (size_t)f->cap * kD * 4;
+    DTTS_CUDA(cudaMemcpy2DAsync(cond, w, f->cond, sp, w, f->n_utt, cudaMemcpyDeviceToHost, e->stream));
+    DTTS_CUDA(cudaMemcpy2DAsync(uncond, w, f->uncond, sp, w, f->n_utt, cudaMemcpyDeviceToHost, e->stream));
+    return e->finish(true);
+}
+
+int dtts_fm_solve(dtts_fm *f, const dtts_solve_args *a) {
+    DTTS_CHECK(f && a, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(f->len >= 1, DTTS_ERR_ARG, "empty FM history");
+    dtts_solve_args b = *a;
+    b.n_utt = f->n_utt;
+    b.fm_len = f->len;
+    b.fm_cond = f->cond;
+    b.fm_uncond = f->uncond;
+    return euler_solve_impl(f->e, &b, f->cap);
 }
 
 }  // extern "C"

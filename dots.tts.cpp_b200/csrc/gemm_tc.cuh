@@ -61,6 +61,7 @@ struct EpiParams {
     bf16 *q, *k, *v;
     long long ldq, ldkv;      // q[m*ldq + c]; k/v[((m/T)*kv_cap + kv_start + m%T) * ldkv + c]
     int kv_cap, kv_start;
+    const int *kv_start_dev;  // if set, kv_start is read from device memory (graph-captured decode)
     int qk_norm;              // per-head RMS norm (eps 1e-6) of q and k before RoPE
     const float *qn, *kn;     // its gains [64], or nullptr for none
     const float2 *rope;       // [positions][32] (cos, sin); row index = kv_start + m%T
@@ -184,7 +185,7 @@ DTTS_DEV void load_bias32(float (&v)[32], const float *bias, int n0) {
 // srope: RoPE rows kv_start.. in shared memory, or nullptr to read ep.rope.
 // The RoPE rows are read with generic loads: they may be shared or global.
 DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&lo)[32], float (&hi)[32],
-                                 const float *sgain, const float4 *srope) {
+                                 const float *sgain, const float4 *srope, int kv_start) {
     if (sect == 2) return;  // v: plain
     const int t = m % ep.tok_per_row;
     if (ep.qk_norm) {
@@ -204,7 +205,7 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
         }
     }
     const float4 *cs = srope ? srope + t * 16
-                             : reinterpret_cast<const float4 *>(ep.rope + (long long)(ep.kv_start + t) * 32);
+                             : reinterpret_cast<const float4 *>(ep.rope + (long long)(kv_start + t) * 32);
     if (ep.rope_mode == ROPE_HALF) {
         // pairs (d, d + 32), frequency index d
 #pragma unroll
@@ -369,7 +370,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
         const int quad = warp & 3;
         float *sgain = nullptr;
         const float4 *srope = nullptr;
-        const bool kv_dense = ep.kv_cap == ep.tok_per_row && ep.kv_start == 0;
+        const int kv_start = ep.kv_start_dev ? *ep.kv_start_dev : ep.kv_start;
+        const bool kv_dense = ep.kv_cap == ep.tok_per_row && kv_start == 0;
         if constexpr (EPI == EPI_QKV) {
             sgain = reinterpret_cast<float *>(sConst);
             float2 *rp = reinterpret_cast<float2 *>(sConst + 512);
@@ -381,7 +383,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             const bool rope_smem = ep.rope != nullptr && ep.tok_per_row <= kRopeSmemRows;
             if (rope_smem)
                 for (int i = et; i < ep.tok_per_row * 32; i += EPI_THREADS)
-                    rp[i] = __ldg(ep.rope + (long long)ep.kv_start * 32 + i);
+                    rp[i] = __ldg(ep.rope + (long long)kv_start * 32 + i);
             asm volatile("bar.sync 1, %0;\n" ::"r"(EPI_THREADS) : "memory");
             if (rope_smem) srope = reinterpret_cast<const float4 *>(rp);
         }
@@ -425,7 +427,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                     }
                     const int m_self = m_base + lane;
                     if constexpr (EPI == EPI_QKV) {
-                        if (m_self < M) qkv_head_transform(ep, m_self, n0 >> 10, lo, hi, sgain, srope);
+                        if (m_self < M) qkv_head_transform(ep, m_self, n0 >> 10, lo, hi, sgain, srope, kv_start);
                     } else {
                         if constexpr (EPI == EPI_GELU_BF16) {
 #pragma unroll
@@ -454,7 +456,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                                 // token m of sequence m / T sits at row m of a dense cache (the DiT)
                                 const long long row = kv_dense ? (long long)m
                                                                : (long long)(m / ep.tok_per_row) * ep.kv_cap +
-                                                                     ep.kv_start + (m % ep.tok_per_row);
+                                                                     kv_start + (m % ep.tok_per_row);
                                 dst = (sect == 1 ? ep.k : ep.v) + row * ep.ldkv + col;
                             }
                         } else {

@@ -252,7 +252,15 @@ DTTS_DEV void attn_store(const AttnArgs &a, int r, int h, int qi0, int qi1, int 
     }
 }
 
+__global__ void advance_len_kernel(int *len, int add) { *len += add; }
+
+void launch_advance_len(int *len, int add, cudaStream_t s) { advance_len_kernel<<<1, 1, 0, s>>>(len, add); }
+
 __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
+    if (a.kv_base_dev) {   // graph-captured decode: positions from device memory
+        a.q_pos0 = *a.kv_base_dev;
+        a.kv_len = a.q_pos0 + a.Tq;
+    }
     __shared__ __align__(128) bf16 Qs[64 * 64];
     __shared__ __align__(128) bf16 Ks[64 * 64];
     __shared__ __align__(128) bf16 Vs[64 * 64];
@@ -523,7 +531,7 @@ cudaError_t attention_short_prepare() {
 }
 
 void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
-    if (a.Tq <= 64 && a.kv_len <= 64) {
+    if (a.Tq <= 64 && a.kv_len <= 64 && !a.kv_base_dev) {
         const int n_pairs = a.rows * kH;
         int dev = 0, nsm = 148;
         cudaGetDevice(&dev);
@@ -1021,6 +1029,53 @@ void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_sc
     const int nrows = n_utt * P;
     cfg_euler_kernel<<<(nrows + kEulerRows - 1) / kEulerRows, kD / 4, 0, s>>>(
         vel, z, nrows, P, cfg_scale, cfg_form, dt, update, w_coord_t, b_coord, x_in, L);
+}
+
+// =========================================================================
+// FM history on the device
+// =========================================================================
+// Row (u, p) of src ([n_utt * P][1024], or one row broadcast to every (u, p)
+// when broadcast != 0) to row u * cap + start + p of dst.
+__global__ void fm_place_rows_kernel(const float *__restrict__ src, float *__restrict__ dst, int P, int cap, int start,
+                                     int broadcast) {
+    const int r = blockIdx.x, u = r / P, p = r % P;
+    const float4 *s4 = reinterpret_cast<const float4 *>(src + (broadcast ? 0 : (long long)r * kD));
+    float4 *d4 = reinterpret_cast<float4 *>(dst + ((long long)u * cap + start + p) * kD);
+    for (int i = threadIdx.x; i < kD / 4; i += blockDim.x) d4[i] = s4[i];
+}
+
+void launch_fm_place_rows(const float *src, float *dst, int n_utt, int P, int cap, int start, int broadcast,
+                          cudaStream_t s) {
+    fm_place_rows_kernel<<<n_utt * P, 256, 0, s>>>(src, dst, P, cap, start, broadcast);
+}
+
+// EOS head activation in place: SiLU(s) = s sigmoid(s) (eos_proj.1), or the
+// shipped code's s * (s / (1 + exp(-s))) (src/e2e_pipeline_v4.cpp:608-609).
+__global__ void eos_act_kernel(float *__restrict__ x, long long n, int as_written) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = x[i];
+    const float silu = v / (1.0f + expf(-v));
+    x[i] = as_written ? v * silu : silu;
+}
+
+// p = softmax(logits[u][0..1])[1], as src/e2e_pipeline_v4.cpp:617-619.
+__global__ void eos_prob_kernel(const float *__restrict__ logits, int n, float *__restrict__ prob) {
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= n) return;
+    const float a = logits[2 * u], b = logits[2 * u + 1];
+    const float mx = fmaxf(a, b);
+    const float sum = expf(a - mx) + expf(b - mx);
+    prob[u] = expf(b - mx) / sum;
+}
+
+void launch_eos_act(float *h1, int n, int as_written, cudaStream_t s) {
+    const long long tot = (long long)n * kLLM;
+    eos_act_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(h1, tot, as_written);
+}
+
+void launch_eos_prob(const float *logits, int n, float *prob, cudaStream_t s) {
+    eos_prob_kernel<<<(n + 127) / 128, 128, 0, s>>>(logits, n, prob);
 }
 
 // =========================================================================

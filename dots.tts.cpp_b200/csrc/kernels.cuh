@@ -59,10 +59,15 @@ struct AttnArgs {
     float *o_scale;
     const float *unorm;
     float vbound;
+    // if set (tiled kernel only): the cache length before this call is read
+    // from device memory, q_pos0 = *kv_base_dev and kv_len = *kv_base_dev + Tq
+    const int *kv_base_dev;
 };
 // Tq <= 64 and kv_len <= 64 take the pipelined short-sequence kernel (call
 // attention_short_prepare() once per device first); longer ones the tiled kernel.
 void launch_attention_bf16(const AttnArgs &a, cudaStream_t s);
+// *len += add on the device (KV length of a graph-captured decode step)
+void launch_advance_len(int *len, int add, cudaStream_t s);
 cudaError_t attention_short_prepare();
 // Host helper: bit-packs a [Tq][kv_len] uint8 mask into [Tq][ceil(kv_len/32)] words.
 void pack_mask_bits(const uint8_t *mask, int Tq, int kv_len, uint32_t *bits);
@@ -105,6 +110,12 @@ void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
                            float *g_inv, float w1n, float b1max, cudaStream_t s);
 void launch_e4m3_selftest(const float *x, uint8_t *y, int n, cudaStream_t s);
+
+// ------------------------------------------------------------ FM history
+void launch_fm_place_rows(const float *src, float *dst, int n_utt, int P, int cap, int start, int broadcast,
+                          cudaStream_t s);
+void launch_eos_act(float *h1, int n, int as_written, cudaStream_t s);   // h1 [n][1536] in place
+void launch_eos_prob(const float *logits, int n, float *prob, cudaStream_t s);
 
 // ------------------------------------------------------------ DiT output head
 // vel[r][p] = W_out (LN(h[r, L-P+p]) (1 + scale) + shift) + b_out, with the

@@ -23,6 +23,12 @@ using namespace dtts;
 
 namespace {
 constexpr int kBN = 256;
+// Calls of at most kSmallTok tokens (decode steps) use 128-wide tiles, split
+// the two residual GEMMs along K (more CTAs stream the weights; the partial
+// sums reach the residual in run-dependent order), read the cache position
+// from device memory and replay one CUDA graph per shape.
+constexpr int kBNs = 128;
+constexpr long long kSmallTok = 256;
 
 int up_f32(DeviceArena &a, const float *h, size_t n, float **out) {
     *out = nullptr;
@@ -62,14 +68,15 @@ struct dtts_pe {
         bf16 *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr;
         float *bo = nullptr, *b1 = nullptr, *b2 = nullptr, *an = nullptr, *fn = nullptr;
         CUtensorMap tqkv, to, t1, t2;
+        CUtensorMap tqkv_s, to_s, t1_s, t2_s;   // 128-row boxes for kBNs tiles
     };
     std::vector<Layer> layers;
     float *conv_w = nullptr, *conv_b = nullptr, *in_b = nullptr, *out_b = nullptr;
     bf16 *in_w = nullptr, *out_w = nullptr;
-    CUtensorMap t_inw, t_outw;
+    CUtensorMap t_inw, t_outw, t_inw_s, t_outw_s;
     bf16 *kc = nullptr, *vc = nullptr;   // [n_layers][max_batch][max_tokens][1024]
-    float *tail[2] = {nullptr, nullptr}; // [max_batch][128], double-buffered
-    int tail_cur = 0;
+    float *tail[2] = {nullptr, nullptr}; // [max_batch][128]: tail[0] read, tail[1] written then copied back
+    int *d_len = nullptr;                // cache length on the device (graph-captured steps)
     float2 *rope = nullptr;              // [max_tokens][32], adjacent-pair rotation
     int *d_err = nullptr;
     int cur_B = 0, cur_len = 0;
@@ -79,8 +86,16 @@ struct dtts_pe {
     bf16 *conv = nullptr, *act = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *pairs = nullptr;
     CUtensorMap t_conv, t_act, t_att, t_ffn, t_pairs, t_h;
     int launches = 0;
+    // decode graphs, keyed by (B, n_frames); dropped when the workspace moves
+    struct Graph { int B, n_frames; cudaGraphExec_t exec; };
+    std::vector<Graph> graphs;
+    void drop_graphs() {
+        for (Graph &g : graphs) cudaGraphExecDestroy(g.exec);
+        graphs.clear();
+    }
 
     ~dtts_pe() {
+        drop_graphs();
         ws.free_all();
         cache.free_all();
         wts.free_all();
@@ -90,6 +105,7 @@ struct dtts_pe {
     int ensure(long long tok) {
         if (tok <= cap_tok) return DTTS_OK;
         DTTS_CUDA(cudaStreamSynchronize(stream));
+        drop_graphs();
         ws.free_all();
         cap_tok = std::max<long long>(tok, 64);
         const size_t T = (size_t)cap_tok;
@@ -119,15 +135,18 @@ struct dtts_pe {
     }
 
     // frames already in `this->frames` ([B][n_frames][128]); output in outf.
-    int enqueue_append(int B, int n_frames, int pair_mode) {
+    // dev_pos: positions come from d_len (graph capture) instead of cur_len.
+    int enqueue_append(int B, int n_frames, int pair_mode, bool dev_pos) {
         const int T = n_frames / 2, M = B * T, n_out = n_frames / 4;
-        const float *tail_in = cur_len > 0 ? tail[tail_cur] : nullptr;
-        float *tail_out = tail[tail_cur ^ 1];
+        const bool small = (long long)M <= kSmallTok;
+        const int bn = small ? kBNs : kBN;
         launches++;
-        launch_pe_conv(frames, B, n_frames, tail_in, conv_w, conv_b, conv, tail_out, stream);
+        launch_pe_conv(frames, B, n_frames, tail[0], conv_w, conv_b, conv, tail[1], stream);
+        DTTS_CUDA(cudaMemcpyAsync(tail[0], tail[1], (size_t)B * kLat * 4, cudaMemcpyDeviceToDevice, stream));
         int st;
         {
-            GemmOp op = op0(t_conv, t_inw, M, kD, kLat, EPI_F32, d_err);
+            GemmOp op = op0(t_conv, small ? t_inw_s : t_inw, M, kD, kLat, EPI_F32, d_err);
+            op.bn = bn;
             op.ep.bias = in_b; op.ep.out = h; op.ep.ldo = kD;
             if ((st = gemm(op))) return st;
         }
@@ -137,10 +156,12 @@ struct dtts_pe {
             launches++;
             launch_rms_norm(h, act, M, Ly.an, stream);
             {
-                GemmOp op = op0(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
+                GemmOp op = op0(t_act, small ? Ly.tqkv_s : Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
+                op.bn = bn;
                 op.ep.q = q; op.ep.ldq = kD;
                 op.ep.k = kc + l * layer_stride; op.ep.v = vc + l * layer_stride; op.ep.ldkv = kD;
                 op.ep.tok_per_row = T; op.ep.kv_cap = max_tokens; op.ep.kv_start = cur_len;
+                op.ep.kv_start_dev = dev_pos ? d_len : nullptr;
                 op.ep.qk_norm = 0; op.ep.rope = rope; op.ep.rope_mode = ROPE_ADJACENT;
                 if ((st = gemm(op))) return st;
             }
@@ -149,11 +170,14 @@ struct dtts_pe {
                 a.q = q; a.ldq = kD; a.k = kc + l * layer_stride; a.v = vc + l * layer_stride; a.ldkv = kD;
                 a.o = att; a.ldo = kD; a.rows = B; a.Tq = T; a.kv_len = cur_len + T; a.kv_cap = max_tokens;
                 a.q_pos0 = cur_len; a.causal = 1; a.mask = nullptr; a.scale = 1.0f / sqrtf(64.0f);
+                a.kv_base_dev = dev_pos ? d_len : nullptr;
                 launches++;
                 launch_attention_bf16(a, stream);
             }
             {
-                GemmOp op = op0(t_att, Ly.to, M, kD, kD, EPI_RESID, d_err);
+                GemmOp op = op0(t_att, small ? Ly.to_s : Ly.to, M, kD, kD, EPI_RESID, d_err);
+                op.bn = bn;
+                op.ep.ksplit = small ? 2 : 1;
                 op.tr = t_h;
                 op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
@@ -161,12 +185,15 @@ struct dtts_pe {
             launches++;
             launch_rms_norm(h, act, M, Ly.fn, stream);
             {
-                GemmOp op = op0(t_act, Ly.t1, M, kF, kD, EPI_SILU_BF16, d_err);
+                GemmOp op = op0(t_act, small ? Ly.t1_s : Ly.t1, M, kF, kD, EPI_SILU_BF16, d_err);
+                op.bn = bn;
                 op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
                 if ((st = gemm(op))) return st;
             }
             {
-                GemmOp op = op0(t_ffn, Ly.t2, M, kD, kF, EPI_RESID, d_err);
+                GemmOp op = op0(t_ffn, small ? Ly.t2_s : Ly.t2, M, kD, kF, EPI_RESID, d_err);
+                op.bn = bn;
+                op.ep.ksplit = small ? 4 : 1;
                 op.tr = t_h;
                 op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
@@ -175,10 +202,13 @@ struct dtts_pe {
         launches++;
         launch_pe_pairs(h, B, T, pair_mode, pairs, stream);
         {
-            GemmOp op = op0(t_pairs, t_outw, B * n_out, kLLM, 2 * kD, EPI_F32, d_err);
+            GemmOp op = op0(t_pairs, small ? t_outw_s : t_outw, B * n_out, kLLM, 2 * kD, EPI_F32, d_err);
+            op.bn = bn;
             op.ep.bias = out_b; op.ep.out = outf; op.ep.ldo = kLLM;
             if ((st = gemm(op))) return st;
         }
+        launches++;
+        launch_advance_len(d_len, T, stream);
         DTTS_CUDA(cudaGetLastError());
         return DTTS_OK;
     }
@@ -204,14 +234,34 @@ struct dtts_pe {
         const long long tok = (long long)B * (n_frames / 2);
         int st = ensure(tok);
         if (st) return st;
-        launches = 0;
         const cudaMemcpyKind ik = mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
         DTTS_CUDA(cudaMemcpyAsync(frames, frames_in, (size_t)B * n_frames * kLat * 4, ik, stream));
-        if ((st = enqueue_append(B, n_frames, pair_mode))) return st;
+        if (tok <= kSmallTok && pair_mode == DTTS_PAIR_ADJACENT) {
+            // decode step: one graph per (B, n_frames), positions from d_len
+            cudaGraphExec_t exec = nullptr;
+            for (Graph &g : graphs)
+                if (g.B == B && g.n_frames == n_frames) exec = g.exec;
+            if (!exec) {
+                launches = 0;
+                cudaGraph_t graph = nullptr;
+                DTTS_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+                st = enqueue_append(B, n_frames, pair_mode, true);
+                cudaError_t ce = cudaStreamEndCapture(stream, &graph);
+                if (st) { if (graph) cudaGraphDestroy(graph); return st; }
+                DTTS_CUDA(ce);
+                ce = cudaGraphInstantiate(&exec, graph, 0);
+                cudaGraphDestroy(graph);
+                DTTS_CUDA(ce);
+                graphs.push_back({B, n_frames, exec});
+            }
+            DTTS_CUDA(cudaGraphLaunch(exec, stream));
+        } else {
+            launches = 0;
+            if ((st = enqueue_append(B, n_frames, pair_mode, false))) return st;
+        }
         const cudaMemcpyKind ok = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
         DTTS_CUDA(cudaMemcpyAsync(out, outf, (size_t)B * (n_frames / 4) * kLLM * 4, ok, stream));
         cur_len += n_frames / 2;
-        tail_cur ^= 1;
         return finish(mem == DTTS_MEM_HOST);
     }
 };
@@ -257,7 +307,9 @@ int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batc
         if ((st = up_f32(p->wts, s.attn_norm_w, kD, &L.an))) return st;
         if ((st = up_f32(p->wts, s.ffn_norm_w, kD, &L.fn))) return st;
         bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, 3 * kD, kD, kBN) && make_tmap_bf16(&L.to, L.wo, kD, kD, kBN) &&
-                  make_tmap_bf16(&L.t1, L.w1, kF, kD, kBN) && make_tmap_bf16(&L.t2, L.w2, kD, kF, kBN);
+                  make_tmap_bf16(&L.t1, L.w1, kF, kD, kBN) && make_tmap_bf16(&L.t2, L.w2, kD, kF, kBN) &&
+                  make_tmap_bf16(&L.tqkv_s, L.wqkv, 3 * kD, kD, kBNs) && make_tmap_bf16(&L.to_s, L.wo, kD, kD, kBNs) &&
+                  make_tmap_bf16(&L.t1_s, L.w1, kF, kD, kBNs) && make_tmap_bf16(&L.t2_s, L.w2, kD, kF, kBNs);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder layer %d)", l);
     }
     if ((st = up_f32(p->wts, w->conv_w, (size_t)kLat * kLat * 2, &p->conv_w))) return st;
@@ -266,7 +318,9 @@ int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batc
     if ((st = up_f32(p->wts, w->in_b, kD, &p->in_b))) return st;
     if ((st = up_bf16(p->wts, {w->out_w}, kLLM, 2 * kD, &p->out_w))) return st;
     if ((st = up_f32(p->wts, w->out_b, kLLM, &p->out_b))) return st;
-    bool ok = make_tmap_bf16(&p->t_inw, p->in_w, kD, kLat, kBN) && make_tmap_bf16(&p->t_outw, p->out_w, kLLM, 2 * kD, kBN);
+    bool ok = make_tmap_bf16(&p->t_inw, p->in_w, kD, kLat, kBN) && make_tmap_bf16(&p->t_outw, p->out_w, kLLM, 2 * kD, kBN) &&
+              make_tmap_bf16(&p->t_inw_s, p->in_w, kD, kLat, kBNs) &&
+              make_tmap_bf16(&p->t_outw_s, p->out_w, kLLM, 2 * kD, kBNs);
     DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder projections)");
     // KV cache and conv tails
     const size_t cache_elems = (size_t)w->n_layers * max_batch * max_tokens * kD;
@@ -275,7 +329,8 @@ int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batc
     p->tail[0] = (float *)p->cache.alloc((size_t)max_batch * kLat * 4);
     p->tail[1] = (float *)p->cache.alloc((size_t)max_batch * kLat * 4);
     p->rope = (float2 *)p->cache.alloc((size_t)max_tokens * 32 * sizeof(float2));
-    DTTS_CHECK(p->kc && p->vc && p->tail[0] && p->tail[1] && p->rope, DTTS_ERR_OOM,
+    p->d_len = (int *)p->cache.alloc(sizeof(int));
+    DTTS_CHECK(p->kc && p->vc && p->tail[0] && p->tail[1] && p->rope && p->d_len, DTTS_ERR_OOM,
                "KV cache allocation failed (%zu MB)", cache_elems * 4 >> 20);
     // ggml_rope mode 0: theta starts at the position and is multiplied by
     // 1e4^(-2/64) for each successive adjacent pair.
@@ -316,9 +371,13 @@ int dtts_pe_sync(dtts_pe *p) {
 int dtts_pe_stream_reset(dtts_pe *p, int B) {
     DTTS_CHECK(p, DTTS_ERR_ARG, "null engine");
     DTTS_CHECK(B >= 1 && B <= p->max_batch, DTTS_ERR_ARG, "batch %d out of [1, %d]", B, p->max_batch);
+    DeviceGuard g(p->device);
     p->cur_B = B;
     p->cur_len = 0;
-    p->tail_cur = 0;
+    // empty streams: zero conv tail (tap 2t-1 of the first token reads nothing)
+    // and cache length 0, in stream order with the calls that follow
+    DTTS_CUDA(cudaMemsetAsync(p->tail[0], 0, (size_t)p->max_batch * kLat * 4, p->stream));
+    DTTS_CUDA(cudaMemsetAsync(p->d_len, 0, sizeof(int), p->stream));
     return DTTS_OK;
 }
 

@@ -72,6 +72,8 @@ dtts_dit *model_engine(dit_model &m) {
     w.hid_w = td(m.hidden_proj_w); w.hid_b = td(m.hidden_proj_b);
     w.lat_w = td(m.latent_proj_w); w.lat_b = td(m.latent_proj_b);
     w.coord_w = td(m.coord_proj_w); w.coord_b = td(m.coord_proj_b);
+    w.eos_w1 = td(m.eos_proj_w1); w.eos_b1 = td(m.eos_proj_b1);
+    w.eos_w2 = td(m.eos_proj_w2); w.eos_b2 = td(m.eos_proj_b2);
     dtts_dit *e = nullptr;
     check(dtts_dit_create(&w, DTTS_DTYPE_BF16, g_device, &e), "dtts_dit_create");
     g_dit[&m] = e;

@@ -36,7 +36,7 @@ class DitW(C.Structure):
     _fields_ = [("n_layers", C.c_int), ("blocks", C.POINTER(DitBlockW))] + [
         (n, _fp) for n in ("t_w1", "t_b1", "t_w2", "t_b2", "spk_w1", "spk_b1", "spk_ln_w", "spk_ln_b",
                            "oada_w", "oada_b", "out_w", "out_b", "in_w", "in_b", "hid_w", "hid_b", "lat_w",
-                           "lat_b", "coord_w", "coord_b")]
+                           "lat_b", "coord_w", "coord_b", "eos_w1", "eos_b1", "eos_w2", "eos_b2")]
 
 
 class AttnW(C.Structure):
@@ -83,6 +83,8 @@ DIT_GLOBAL_NAMES = {
     "hid_w": "hidden_proj.weight", "hid_b": "hidden_proj.bias",
     "lat_w": "latent_proj.weight", "lat_b": "latent_proj.bias",
     "coord_w": "coordinate_proj.weight", "coord_b": "coordinate_proj.bias",
+    "eos_w1": "eos_proj.0.weight", "eos_b1": "eos_proj.0.bias",
+    "eos_w2": "eos_proj.2.weight", "eos_b2": "eos_proj.2.bias",
 }
 PE_LAYER_NAMES = {
     "attn_norm_w": "attn_norm.weight", "wq": "attn.q_proj.weight", "wk": "attn.k_proj.weight",
@@ -107,7 +109,8 @@ EXPORTS = [
     "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
     "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_solve_timeline",
     "dtts_dit_profile_kernel",
-    "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
+    "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_fm_create", "dtts_fm_destroy", "dtts_fm_start",
+    "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
     "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_selftest_e4m3",
@@ -369,6 +372,66 @@ class DiT:
         n = C.c_int()
         check(lib().dtts_dit_last_launch_count(self.h, C.byref(n)))
         return n.value
+
+
+EOS_SILU, EOS_AS_WRITTEN = 0, 1
+
+
+class FMHistory:
+    """The autoregressive loop's FM buffers on the device (dtts_fm_*)."""
+
+    def __init__(self, dit, n_utt, capacity):
+        h = _vp()
+        check(lib().dtts_fm_create(dit.h, n_utt, capacity, C.byref(h)))
+        self.h, self.dit, self.n_utt = h, dit, n_utt
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_fm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def start(self, hidden0):
+        check(lib().dtts_fm_start(self.h, _addr(_f32(hidden0)), MEM_HOST))
+
+    def append_latents(self, z):
+        z = _f32(z)
+        check(lib().dtts_fm_append_latents(self.h, _addr(z), z.shape[1], MEM_HOST))
+
+    def append_hidden(self, h, eos=True, eos_act=EOS_SILU):
+        h = _f32(h)
+        p = np.zeros(h.shape[0], np.float32) if eos else None
+        check(lib().dtts_fm_append_hidden(self.h, _addr(h), _addr(p), eos_act, MEM_HOST))
+        return p
+
+    def length(self):
+        n = C.c_int()
+        check(lib().dtts_fm_length(self.h, C.byref(n)))
+        return n.value
+
+    def read(self):
+        L = self.length()
+        c = np.zeros((self.n_utt, L, 1024), np.float32)
+        u = np.zeros_like(c)
+        check(lib().dtts_fm_read(self.h, _addr(c), _addr(u)))
+        return c, u
+
+    def solve(self, z0, spk=None, spk_scale=1.5, nfe=10, cfg_scale=2.0, cfg_form=CFG_V4, layout=LAYOUT_FM_MASK,
+              use_graph=True):
+        z0, spk = _f32(z0), _f32(spk)
+        z_out = np.zeros_like(z0)
+        a = SolveArgs()
+        a.n_utt, a.fm_len, a.patch = z0.shape[0], 0, z0.shape[1]
+        a.fm_cond, a.fm_uncond, a.z0, a.spk = None, None, _addr(z0), _addr(spk)
+        a.spk_scale, a.nfe, a.cfg_scale, a.cfg_form = spk_scale, nfe, cfg_scale, cfg_form
+        a.layout, a.z_out, a.mem, a.use_graph = layout, _addr(z_out), MEM_HOST, int(use_graph)
+        check(lib().dtts_fm_solve(self.h, C.byref(a)))
+        return z_out
 
 
 class Attention:

@@ -67,6 +67,10 @@ def dit_shapes(n_layers=DIT_LAYERS):
     s["latent_proj.bias"] = (D,)
     s["coordinate_proj.weight"] = (D, LAT)
     s["coordinate_proj.bias"] = (D,)
+    s["eos_proj.0.weight"] = (LLM, LLM)
+    s["eos_proj.0.bias"] = (LLM,)
+    s["eos_proj.2.weight"] = (2, LLM)
+    s["eos_proj.2.bias"] = (2,)
     return s
 
 

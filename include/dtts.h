@@ -101,6 +101,8 @@ typedef struct dtts_dit_weights {
     const float *hid_w, *hid_b;       /* hidden_proj [1024][1536], [1024]      */
     const float *lat_w, *lat_b;       /* latent_proj [1024][128], [1024]       */
     const float *coord_w, *coord_b;   /* coordinate_proj [1024][128], [1024]   */
+    const float *eos_w1, *eos_b1;     /* eos_proj.0 [1536][1536], [1536] or NULL */
+    const float *eos_w2, *eos_b2;     /* eos_proj.2 [2][1536], [2]             */
 } dtts_dit_weights;
 
 typedef struct dtts_attn_weights {
@@ -189,6 +191,35 @@ typedef struct dtts_solve_args {
     int use_graph;             /* capture the whole solve in one CUDA graph         */
 } dtts_solve_args;
 int dtts_dit_euler_solve(dtts_dit *e, const dtts_solve_args *a);
+
+/* ------------------------------------------------------------------ FM history on the device
+ * The autoregressive loop's flow-matching buffers (src/e2e_pipeline_v4.cpp:324-340, 551-588),
+ * resident on the engine's device for n_utt utterances: the conditional rows and the CFG rows
+ * (null hidden state), each up to `capacity` rows per utterance.  Projections are fp32 GEMMs
+ * with the model's hidden_proj / latent_proj; the EOS head uses eos_proj.  Host buffers make
+ * the calls synchronous; device buffers enqueue them on the engine stream. */
+typedef struct dtts_fm dtts_fm;
+#define DTTS_EOS_SILU        0   /* eos_proj.0 -> SiLU -> eos_proj.2 (the model's definition)           */
+#define DTTS_EOS_AS_WRITTEN  1   /* s * SiLU(s) between the two layers, as src/e2e_pipeline_v4.cpp:608-609 computes */
+int dtts_fm_create(dtts_dit *e, int n_utt, int capacity, dtts_fm **out);
+int dtts_fm_destroy(dtts_fm *f);
+/* Restarts every utterance with one row: hidden_proj(hidden0[u]) (conditional) and
+ * hidden_proj(0) (CFG).  hidden0 [n_utt][1536]  (src/e2e_pipeline_v4.cpp:329-340) */
+int dtts_fm_start(dtts_fm *f, const float *hidden0, int mem);
+/* Appends latent_proj(z[u][p]) for p < patch (<= 16) to both row sets; z are the solver's raw
+ * latents [n_utt][patch][128]  (src/e2e_pipeline_v4.cpp:551-556) */
+int dtts_fm_append_latents(dtts_fm *f, const float *z, int patch, int mem);
+/* Appends hidden_proj(h[u]) to the conditional rows and hidden_proj(0) to the CFG rows
+ * (:576-586).  If eos_prob is not NULL it also receives, per utterance, the EOS head's
+ * probability softmax(eos_proj.2(act(eos_proj.0(h))))[1] (:598-619); eos_act is
+ * DTTS_EOS_SILU or DTTS_EOS_AS_WRITTEN.  h [n_utt][1536], eos_prob [n_utt]. */
+int dtts_fm_append_hidden(dtts_fm *f, const float *h, float *eos_prob, int eos_act, int mem);
+int dtts_fm_length(dtts_fm *f, int *rows);
+/* Copies the current rows to the host: cond, uncond [n_utt][length][1024]. */
+int dtts_fm_read(dtts_fm *f, float *cond, float *uncond);
+/* The Euler + CFG solve on the current history: a->n_utt, fm_len, fm_cond and fm_uncond are
+ * taken from f; a->z0, spk, z_out (and a->mem, which describes them) as in dtts_dit_euler_solve. */
+int dtts_fm_solve(dtts_fm *f, const dtts_solve_args *a);
 
 /* Launch kinds of dtts_dit_solve_timeline. */
 #define DTTS_TL_GEMM_QKV       0   /* QKV projection + qk-norm + RoPE epilogue  */

@@ -508,6 +508,32 @@ void orc_dit_velocity(const orc_dit *m, const float *x_in, int L, const float *c
 }
 
 /* --------------------------------------------------------------------------
+ * EOS head of the v4 pipeline (src/e2e_pipeline_v4.cpp:598-619):
+ * s = W1 h + b1 (input order), a = s / (1 + e^-s) and, as the shipped code
+ * does, a = s * a when as_written (:608-609); logits = W2 a + b2;
+ * p = softmax(logits)[1].
+ * ------------------------------------------------------------------------ */
+float orc_eos_prob(const float *w1, const float *b1, const float *w2, const float *b2, const float *h,
+                   int as_written) {
+    float a[ORC_LLM];
+    for (int o = 0; o < ORC_LLM; o++) {
+        float s = b1 ? b1[o] : 0.0f;
+        for (int i = 0; i < ORC_LLM; i++) s += w1[(size_t)o * ORC_LLM + i] * h[i];
+        a[o] = s / (1.0f + expf(-s));
+        if (as_written) a[o] = s * a[o];
+    }
+    float lg[2];
+    for (int o = 0; o < 2; o++) {
+        float s = b2 ? b2[o] : 0.0f;
+        for (int i = 0; i < ORC_LLM; i++) s += w2[(size_t)o * ORC_LLM + i] * a[i];
+        lg[o] = s;
+    }
+    const float mx = fmaxf(lg[0], lg[1]);
+    const float sum = expf(lg[0] - mx) + expf(lg[1] - mx);
+    return expf(lg[1] - mx) / sum;
+}
+
+/* --------------------------------------------------------------------------
  * FM mask / position ids (src/e2e_pipeline_v4.cpp:120-155).
  * ------------------------------------------------------------------------ */
 void orc_build_fm_mask(uint8_t *mask, int total_len, int fm_len, int patch, int hidden_patch) {

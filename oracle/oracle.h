@@ -112,6 +112,9 @@ void orc_dit_velocity(const orc_dit *m, const float *x_in, int L, const float *c
                       const uint8_t *mask, const float *pos, int ffn_mode,
                       int n_out, float *out);
 
+float orc_eos_prob(const float *w1, const float *b1, const float *w2, const float *b2, const float *h,
+                   int as_written);
+
 void orc_build_fm_mask(uint8_t *mask, int total_len, int fm_len, int patch, int hidden_patch);
 void orc_build_fm_pos(float *pos, int total_len, int fm_len, int patch);
 

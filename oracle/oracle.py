@@ -176,6 +176,8 @@ class Oracle:
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_set_dit_rope.argtypes = [C.c_int]
         L.orc_set_dit_fp8.argtypes = [C.c_int]
+        L.orc_eos_prob.argtypes = [_fp, _fp, _fp, _fp, _fp, C.c_int]
+        L.orc_eos_prob.restype = C.c_float
         L.orc_e4m3_encode.argtypes = [C.c_float]
         L.orc_e4m3_encode.restype = C.c_uint8
         L.orc_e4m3_decode.argtypes = [C.c_uint8]
@@ -205,6 +207,14 @@ class Oracle:
     def set_dit_fp8(self, on):
         """1: DiT blocks use the engine's FP8 (e4m3) recipe; 0: fp32."""
         self.lib.orc_set_dit_fp8(int(on))
+
+    def eos_prob(self, w, h, as_written=False):
+        """EOS head probability for each row of h [n][1536]."""
+        h = np.ascontiguousarray(h, np.float32)
+        a = [np.ascontiguousarray(w[n], np.float32) for n in
+             ("eos_proj.0.weight", "eos_proj.0.bias", "eos_proj.2.weight", "eos_proj.2.bias")]
+        return np.array([self.lib.orc_eos_prob(*[_ptr(x) for x in a], _ptr(h[i]), int(as_written))
+                         for i in range(h.shape[0])], np.float32)
 
     def e4m3_encode(self, x):
         x = np.ascontiguousarray(x, np.float32).ravel()

@@ -134,6 +134,7 @@ int main(int argc, char **argv) {
     dit.latent_proj_w = nullptr;
     dit.coord_proj_w = nullptr;
     dit.hidden_proj_b = dit.latent_proj_b = dit.coord_proj_b = nullptr;
+    dit.eos_proj_w1 = dit.eos_proj_b1 = dit.eos_proj_w2 = dit.eos_proj_b2 = nullptr;
 
     patch_encoder enc;
     enc.n_layers = 2;

@@ -135,3 +135,22 @@ def test_euler_solve_uses_velocity(orc):
     vu = orc.dit_velocity(w, 1, xu, cond, mask, pos, n_out=4)
     want = z0[0] + (vc + 2.0 * (vc - vu)) * 1.0
     assert rel(z1[0], want) < 1e-6
+
+
+def test_eos_head_restatement(orc):
+    """The EOS head of the v4 pipeline (src/e2e_pipeline_v4.cpp:598-619) against
+    a float64 evaluation: SiLU between the layers, or s * SiLU(s) as the shipped
+    code computes (:608-609)."""
+    import synth
+    w = {k: v for k, v in synth.dit_weights(4, n_layers=1).items() if k.startswith("eos_proj")}
+    h = synth.normal(4, "eos.h", (3, 1536), 1.0)
+    for as_written in (False, True):
+        got = orc.eos_prob(w, h, as_written)
+        s = h.astype(np.float64) @ w["eos_proj.0.weight"].T.astype(np.float64) + w["eos_proj.0.bias"]
+        a = s / (1 + np.exp(-s))
+        if as_written:
+            a = s * a
+        lg = a @ w["eos_proj.2.weight"].T.astype(np.float64) + w["eos_proj.2.bias"]
+        want = np.exp(lg[:, 1] - lg.max(1)) / np.exp(lg - lg.max(1, keepdims=True)).sum(1)
+        assert np.abs(got - want).max() < 1e-5
+    assert np.abs(orc.eos_prob(w, h, False) - orc.eos_prob(w, h, True)).max() > 1e-3
