@@ -1,0 +1,391 @@
+// The LLM decoder step of the autoregressive loop (Qwen2.5-1.5B as run by
+// src/llm_manual.cpp): llm_kv_cache_init (:237) over a prompt and
+// llm_kv_cache_step (:342), one new embedding per sequence, on sm_100a for a
+// batch of sequences advancing together.
+//
+// Per layer: RMSNorm (eps 1e-6, gain) -> q|k|v projection with biases
+// (tcgen05 GEMM, fp32 out) -> RoPE (half-split pairs, theta 1e6, angle
+// pos * theta_d with theta_d advanced by repeated multiplication) on q and k,
+// k and v appended to a bf16 cache -> grouped-query attention (12 query heads
+// over 2 key/value heads of 128, causal) -> o_proj (+bias) into the fp32
+// residual -> RMSNorm -> gate|up projection -> SiLU(gate) * up -> down_proj
+// into the residual; then the final RMSNorm.
+#include "kernels.cuh"
+#include "runtime.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+using namespace dtts;
+
+namespace {
+
+constexpr int kLH = 1536, kLF = 8960, kLNH = 12, kLNKV = 2, kLHD = 128, kLKV = kLNKV * kLHD;
+constexpr int kLQKV = kLH + 2 * kLKV;   // 2048 columns: q | k | v
+
+// ---------------------------------------------------------------- kernels
+// RMSNorm of 1536-wide rows, one warp per row (manual_rms_norm,
+// include/dit_manual.h:23-27): out = x / sqrt(mean(x^2) + 1e-6) * w.
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(256) llm_rms_norm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                           void *__restrict__ out, int M) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kLH);
+    float4 v[12];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+        v[j] = xr[lane + 32 * j];
+        ss += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) / (float)kLH + 1e-6f);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+        const int c4 = lane + 32 * j;
+        const float4 g = w ? __ldg(w4 + c4) : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 o = make_float4(v[j].x * inv * g.x, v[j].y * inv * g.y, v[j].z * inv * g.z, v[j].w * inv * g.w);
+        if constexpr (OUT_BF16)
+            reinterpret_cast<uint2 *>(out)[(long long)row * (kLH / 4) + c4] = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+        else
+            reinterpret_cast<float4 *>(out)[(long long)row * (kLH / 4) + c4] = o;
+    }
+}
+
+// RoPE on q (12 heads) and k (2 heads) of token m = b * T + t at position
+// pos0 + t, q to qout (fp32), k and v appended to the caches
+// [b][kv head][cap][128] (bf16).  One block per token, 128 threads: thread
+// d < 64 rotates pair (d, d + 64) of every head.
+__global__ void __launch_bounds__(128) llm_rope_cache_kernel(const float *__restrict__ qkv, int T, int pos0,
+                                                              const float2 *__restrict__ rope, float *__restrict__ qout,
+                                                              bf16 *__restrict__ kc, bf16 *__restrict__ vc, int cap) {
+    const int m = blockIdx.x, b = m / T, t = m % T, p = pos0 + t;
+    const float *row = qkv + (long long)m * kLQKV;
+    const int d = threadIdx.x;
+    if (d < 64) {
+        const float2 cs = rope[(long long)p * 64 + d];
+        for (int h = 0; h < kLNH; h++) {
+            const float x0 = row[h * kLHD + d], x1 = row[h * kLHD + d + 64];
+            qout[(long long)m * kLH + h * kLHD + d] = x0 * cs.x - x1 * cs.y;
+            qout[(long long)m * kLH + h * kLHD + d + 64] = x1 * cs.x + x0 * cs.y;
+        }
+        for (int h = 0; h < kLNKV; h++) {
+            const float x0 = row[kLH + h * kLHD + d], x1 = row[kLH + h * kLHD + d + 64];
+            bf16 *dst = kc + (((long long)b * kLNKV + h) * cap + p) * kLHD;
+            dst[d] = __float2bfloat16_rn(x0 * cs.x - x1 * cs.y);
+            dst[d + 64] = __float2bfloat16_rn(x1 * cs.x + x0 * cs.y);
+        }
+    }
+    for (int h = 0; h < kLNKV; h++)
+        vc[(((long long)b * kLNKV + h) * cap + p) * kLHD + d] = __float2bfloat16_rn(row[kLH + kLKV + h * kLHD + d]);
+}
+
+// Grouped-query causal attention, one warp per (token m, query head): lane
+// l owns dims 4l..4l+3; keys 0 .. pos0 + t of the token's sequence; online
+// softmax in fp32; the output row goes to ao (bf16, the o_proj input).
+__global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__ q, const bf16 *__restrict__ kc,
+                                                       const bf16 *__restrict__ vc, int T, int pos0, int cap, int M,
+                                                       bf16 *__restrict__ ao) {
+    const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (wid >= M * kLNH) return;
+    const int m = wid / kLNH, h = wid % kLNH, b = m / T, t = m % T;
+    const int kvh = h * kLNKV / kLNH;
+    const int n_keys = pos0 + t + 1;
+    const float scale = 1.0f / sqrtf((float)kLHD);
+    const float4 qv = reinterpret_cast<const float4 *>(q + (long long)m * kLH + h * kLHD)[lane];
+    const bf16 *kb = kc + ((long long)b * kLNKV + kvh) * cap * kLHD + 4 * lane;
+    const bf16 *vb = vc + ((long long)b * kLNKV + kvh) * cap * kLHD + 4 * lane;
+    float mx = -INFINITY, l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < n_keys; j++) {
+        const uint2 kr = *reinterpret_cast<const uint2 *>(kb + (long long)j * kLHD);
+        const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr.x));
+        const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr.y));
+        const float s = warp_sum((qv.x * k01.x + qv.y * k01.y) + (qv.z * k23.x + qv.w * k23.y)) * scale;
+        const float nm = fmaxf(mx, s);
+        const float corr = expf(mx - nm), e = expf(s - nm);
+        const uint2 vr = *reinterpret_cast<const uint2 *>(vb + (long long)j * kLHD);
+        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr.x));
+        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr.y));
+        acc.x = acc.x * corr + e * v01.x; acc.y = acc.y * corr + e * v01.y;
+        acc.z = acc.z * corr + e * v23.x; acc.w = acc.w * corr + e * v23.y;
+        l = l * corr + e;
+        mx = nm;
+    }
+    const float inv = 1.0f / l;
+    reinterpret_cast<uint2 *>(ao + (long long)m * kLH + h * kLHD)[lane] =
+        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+}
+
+// out[m][j] = gate / (1 + e^-gate) * up with gu[m] = gate[8960] | up[8960]
+// (src/llm_manual.cpp:333-334, :468).
+__global__ void llm_swiglu_kernel(const float *__restrict__ gu, bf16 *__restrict__ out, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long m = i / kLF, j = i % kLF;
+    const float g = gu[m * 2 * kLF + j], u = gu[m * 2 * kLF + kLF + j];
+    out[i] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+}
+
+int up_f32(DeviceArena &a, const float *h, size_t n, float **out) {
+    *out = nullptr;
+    if (!h) return DTTS_OK;
+    void *d = a.alloc(n * 4);
+    DTTS_CHECK(d, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(d, h, n * 4, cudaMemcpyHostToDevice));
+    *out = (float *)d;
+    return DTTS_OK;
+}
+
+// row-concatenation of parts (rows_i x cols fp32) uploaded as bf16
+int up_bf16(DeviceArena &a, const std::vector<std::pair<const float *, size_t>> &parts, size_t cols, bf16 **out) {
+    size_t rows = 0;
+    for (auto &p : parts) rows += p.second;
+    std::vector<uint16_t> tmp(rows * cols);
+    size_t r0 = 0;
+    for (auto &p : parts) {
+        f32_to_bf16_host(p.first, tmp.data() + r0 * cols, p.second * cols);
+        r0 += p.second;
+    }
+    void *d = a.alloc(tmp.size() * 2);
+    DTTS_CHECK(d, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(d, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice));
+    *out = (bf16 *)d;
+    return DTTS_OK;
+}
+
+}  // namespace
+
+struct dtts_llm {
+    int device = 0, num_sms = 148, n_layers = 0, max_batch = 0, max_seq = 0;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    DeviceArena wts, cache, ws;
+    struct Layer {
+        bf16 *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+        float *bqkv = nullptr, *bo = nullptr, *an = nullptr, *fn = nullptr;
+        CUtensorMap tqkv, to, tgu, td;             // 256-row boxes
+        CUtensorMap tqkv_s, to_s, tgu_s, td_s;     // 128-row boxes (small batches)
+    };
+    std::vector<Layer> layers;
+    float *final_norm = nullptr;
+    bf16 *kc = nullptr, *vc = nullptr;   // [n_layers][max_batch][2][max_seq][128]
+    float2 *rope = nullptr;              // [max_seq][64]
+    int *d_err = nullptr;
+    int cur_B = 0, cur_len = 0;
+    long long cap_tok = 0;
+    float *h = nullptr, *qkv = nullptr, *q = nullptr, *gu = nullptr;
+    bf16 *act = nullptr, *ao = nullptr, *ffn = nullptr;
+    CUtensorMap t_act, t_ao, t_ffn, t_h;
+
+    ~dtts_llm() {
+        ws.free_all();
+        cache.free_all();
+        wts.free_all();
+        if (own_stream) cudaStreamDestroy(own_stream);
+    }
+
+    int ensure(long long tok) {
+        if (tok <= cap_tok) return DTTS_OK;
+        DTTS_CUDA(cudaStreamSynchronize(stream));
+        ws.free_all();
+        cap_tok = std::max<long long>(tok, 64);
+        const size_t T = (size_t)cap_tok;
+        h = (float *)ws.alloc(T * kLH * 4);
+        qkv = (float *)ws.alloc(T * kLQKV * 4);
+        q = (float *)ws.alloc(T * kLH * 4);
+        gu = (float *)ws.alloc(T * 2 * kLF * 4);
+        act = (bf16 *)ws.alloc(T * kLH * 2);
+        ao = (bf16 *)ws.alloc(T * kLH * 2);
+        ffn = (bf16 *)ws.alloc(T * kLF * 2);
+        DTTS_CHECK(h && qkv && q && gu && act && ao && ffn, DTTS_ERR_OOM, "LLM workspace allocation failed");
+        bool ok = make_tmap_bf16(&t_act, act, T, kLH, 128) && make_tmap_bf16(&t_ao, ao, T, kLH, 128) &&
+                  make_tmap_bf16(&t_ffn, ffn, T, kLF, 128) && make_tmap_f32_resid(&t_h, h, T, kLH);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (LLM workspace)");
+        return DTTS_OK;
+    }
+
+    GemmOp op(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int epi, int bn) {
+        GemmOp o;
+        std::memset(&o, 0, sizeof(o));
+        o.ta = ta; o.tb = tb; o.M = M; o.N = N; o.K = K; o.bn = bn; o.nw = 4; o.epi = epi;
+        o.ep.err = d_err; o.ep.tok_per_row = 1; o.ep.ksplit = 1;
+        return o;
+    }
+
+    // emb already in h ([B * T][1536]); runs every layer and the final norm into `out`
+    int enqueue(int B, int T, int pos0, float *out) {
+        const int M = B * T;
+        const bool small = M <= 256;
+        const int bn = small ? 128 : 256;
+        const size_t layer_stride = (size_t)max_batch * kLNKV * max_seq * kLHD;
+        for (int l = 0; l < n_layers; l++) {
+            const Layer &L = layers[l];
+            llm_rms_norm_kernel<true><<<(M + 7) / 8, 256, 0, stream>>>(h, L.an, act, M);
+            {
+                GemmOp o = op(t_act, small ? L.tqkv_s : L.tqkv, M, kLQKV, kLH, EPI_F32, bn);
+                o.ep.bias = L.bqkv; o.ep.out = qkv; o.ep.ldo = kLQKV;
+                DTTS_CUDA(launch_gemm(o, num_sms, stream));
+            }
+            llm_rope_cache_kernel<<<M, 128, 0, stream>>>(qkv, T, pos0, rope, q, kc + l * layer_stride,
+                                                         vc + l * layer_stride, max_seq);
+            llm_attn_kernel<<<(M * kLNH + 7) / 8, 256, 0, stream>>>(q, kc + l * layer_stride, vc + l * layer_stride, T,
+                                                                    pos0, max_seq, M, ao);
+            {
+                GemmOp o = op(t_ao, small ? L.to_s : L.to, M, kLH, kLH, EPI_RESID, bn);
+                o.tr = t_h; o.ep.bias = L.bo; o.ep.resid = h; o.ep.ldr = kLH;
+                o.ep.ksplit = small ? 4 : 1;
+                DTTS_CUDA(launch_gemm(o, num_sms, stream));
+            }
+            llm_rms_norm_kernel<true><<<(M + 7) / 8, 256, 0, stream>>>(h, L.fn, act, M);
+            {
+                GemmOp o = op(t_act, small ? L.tgu_s : L.tgu, M, 2 * kLF, kLH, EPI_F32, bn);
+                o.ep.out = gu; o.ep.ldo = 2 * kLF;
+                DTTS_CUDA(launch_gemm(o, num_sms, stream));
+            }
+            const long long nf = (long long)M * kLF;
+            llm_swiglu_kernel<<<(unsigned)((nf + 255) / 256), 256, 0, stream>>>(gu, ffn, nf);
+            {
+                GemmOp o = op(t_ffn, small ? L.td_s : L.td, M, kLH, kLF, EPI_RESID, bn);
+                o.tr = t_h; o.ep.resid = h; o.ep.ldr = kLH;
+                o.ep.ksplit = small ? 4 : 1;
+                DTTS_CUDA(launch_gemm(o, num_sms, stream));
+            }
+        }
+        llm_rms_norm_kernel<false><<<(M + 7) / 8, 256, 0, stream>>>(h, final_norm, out, M);
+        DTTS_CUDA(cudaGetLastError());
+        return DTTS_OK;
+    }
+
+    int run(const float *emb, int B, int T, float *hidden, int mem) {
+        DTTS_CHECK(emb && hidden, DTTS_ERR_ARG, "null argument");
+        DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
+        DTTS_CHECK(cur_len + T <= max_seq, DTTS_ERR_ARG, "KV cache full (%d + %d > %d tokens)", cur_len, T, max_seq);
+        DeviceGuard g(device);
+        const long long M = (long long)B * T;
+        int st = ensure(M + 1);
+        if (st) return st;
+        // the final norm writes into qkv's space (fp32, at least M x 1536), then out
+        float *outd = qkv;
+        DTTS_CUDA(cudaMemcpyAsync(h, emb, (size_t)M * kLH * 4,
+                                  mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, stream));
+        if ((st = enqueue(B, T, cur_len, outd))) return st;
+        DTTS_CUDA(cudaMemcpyAsync(hidden, outd, (size_t)M * kLH * 4,
+                                  mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, stream));
+        cur_len += T;
+        if (mem != DTTS_MEM_HOST) return DTTS_OK;
+        if ((st = stream_wait(stream, 300.0))) return st;
+        int err = 0;
+        DTTS_CUDA(cudaMemcpy(&err, d_err, 4, cudaMemcpyDeviceToHost));
+        if (err) { cudaMemset(d_err, 0, 4); set_error("device wait limit reached (code %d)", err); return DTTS_ERR_TIMEOUT; }
+        return DTTS_OK;
+    }
+};
+
+extern "C" {
+
+int dtts_llm_create(const dtts_llm_weights *w, int device, int max_batch, int max_seq, dtts_llm **out) {
+    DTTS_CHECK(w && out, DTTS_ERR_ARG, "null argument");
+    *out = nullptr;
+    DTTS_CHECK(w->n_layers >= 1 && w->n_layers <= 64 && w->layers && w->final_norm, DTTS_ERR_ARG,
+               "n_layers %d invalid or final norm missing", w->n_layers);
+    DTTS_CHECK(max_batch >= 1 && max_seq >= 1 && max_seq <= 32768, DTTS_ERR_ARG, "bad capacity %d x %d", max_batch,
+               max_seq);
+    for (int l = 0; l < w->n_layers; l++) {
+        const dtts_llm_layer_weights &L = w->layers[l];
+        DTTS_CHECK(L.qw && L.kw && L.vw && L.ow && L.gw && L.uw && L.dw, DTTS_ERR_ARG, "missing weight in layer %d", l);
+    }
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    std::unique_ptr<dtts_llm> e(new dtts_llm());
+    e->device = device; e->num_sms = nsm; e->n_layers = w->n_layers; e->max_batch = max_batch; e->max_seq = max_seq;
+    DTTS_CUDA(cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking));
+    e->stream = e->own_stream;
+    DTTS_CUDA(gemm_prepare_attributes());
+    e->d_err = (int *)e->wts.alloc(4);
+    DTTS_CHECK(e->d_err, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemset(e->d_err, 0, 4));
+    e->layers.resize(w->n_layers);
+    std::vector<float> bqkv(kLQKV);
+    for (int l = 0; l < w->n_layers; l++) {
+        const dtts_llm_layer_weights &s = w->layers[l];
+        dtts_llm::Layer &L = e->layers[l];
+        if ((st = up_bf16(e->wts, {{s.qw, kLH}, {s.kw, kLKV}, {s.vw, kLKV}}, kLH, &L.wqkv))) return st;
+        if ((st = up_bf16(e->wts, {{s.ow, kLH}}, kLH, &L.wo))) return st;
+        if ((st = up_bf16(e->wts, {{s.gw, kLF}, {s.uw, kLF}}, kLH, &L.wgu))) return st;
+        if ((st = up_bf16(e->wts, {{s.dw, kLH}}, kLF, &L.wd))) return st;
+        std::fill(bqkv.begin(), bqkv.end(), 0.f);
+        if (s.qb) std::memcpy(bqkv.data(), s.qb, kLH * 4);
+        if (s.kb) std::memcpy(bqkv.data() + kLH, s.kb, kLKV * 4);
+        if (s.vb) std::memcpy(bqkv.data() + kLH + kLKV, s.vb, kLKV * 4);
+        if ((st = up_f32(e->wts, bqkv.data(), kLQKV, &L.bqkv))) return st;
+        if ((st = up_f32(e->wts, s.ob, kLH, &L.bo))) return st;
+        if ((st = up_f32(e->wts, s.an, kLH, &L.an))) return st;
+        if ((st = up_f32(e->wts, s.fn, kLH, &L.fn))) return st;
+        bool ok = make_tmap_bf16(&L.tqkv, L.wqkv, kLQKV, kLH, 256) && make_tmap_bf16(&L.to, L.wo, kLH, kLH, 256) &&
+                  make_tmap_bf16(&L.tgu, L.wgu, 2 * kLF, kLH, 256) && make_tmap_bf16(&L.td, L.wd, kLH, kLF, 256) &&
+                  make_tmap_bf16(&L.tqkv_s, L.wqkv, kLQKV, kLH, 128) && make_tmap_bf16(&L.to_s, L.wo, kLH, kLH, 128) &&
+                  make_tmap_bf16(&L.tgu_s, L.wgu, 2 * kLF, kLH, 128) && make_tmap_bf16(&L.td_s, L.wd, kLH, kLF, 128);
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (LLM layer %d)", l);
+    }
+    if ((st = up_f32(e->wts, w->final_norm, kLH, &e->final_norm))) return st;
+    const size_t cache_elems = (size_t)w->n_layers * max_batch * kLNKV * max_seq * kLHD;
+    e->kc = (bf16 *)e->cache.alloc(cache_elems * 2);
+    e->vc = (bf16 *)e->cache.alloc(cache_elems * 2);
+    e->rope = (float2 *)e->cache.alloc((size_t)max_seq * 64 * sizeof(float2));
+    DTTS_CHECK(e->kc && e->vc && e->rope, DTTS_ERR_OOM, "LLM KV cache allocation failed (%zu MB)", cache_elems * 4 >> 20);
+    // (cos, sin)(pos * theta_d), theta_d = (1e6^(-2/128))^d by repeated
+    // multiplication, as src/llm_manual.cpp:398-403 and :449-451 compute them
+    std::vector<float2> rt((size_t)max_seq * 64);
+    const float ts = powf(1000000.0f, -2.0f / (float)kLHD);
+    for (int p = 0; p < max_seq; p++) {
+        float theta = 1.0f;
+        for (int d = 0; d < 64; d++) {
+            rt[(size_t)p * 64 + d] = make_float2(cosf((float)p * theta), sinf((float)p * theta));
+            theta *= ts;
+        }
+    }
+    DTTS_CUDA(cudaMemcpy(e->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    *out = e.release();
+    return DTTS_OK;
+}
+
+int dtts_llm_destroy(dtts_llm *e) {
+    if (!e) return DTTS_OK;
+    DeviceGuard g(e->device);
+    cudaStreamSynchronize(e->stream);
+    delete e;
+    return DTTS_OK;
+}
+
+int dtts_llm_set_stream(dtts_llm *e, void *stream) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
+    e->stream = stream ? static_cast<cudaStream_t>(stream) : e->own_stream;
+    return DTTS_OK;
+}
+
+int dtts_llm_prefill(dtts_llm *e, const float *emb, int B, int n_tok, float *hidden, int mem) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
+    DTTS_CHECK(B >= 1 && B <= e->max_batch && n_tok >= 1, DTTS_ERR_ARG, "bad prefill shape %d x %d", B, n_tok);
+    e->cur_B = B;
+    e->cur_len = 0;
+    return e->run(emb, B, n_tok, hidden, mem);
+}
+
+int dtts_llm_step(dtts_llm *e, const float *emb, int B, float *hidden, int mem) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
+    DTTS_CHECK(B == e->cur_B && e->cur_len > 0, DTTS_ERR_ARG, "step needs a prefill of the same %d sequences", B);
+    return e->run(emb, B, 1, hidden, mem);
+}
+
+int dtts_llm_length(dtts_llm *e, int *tokens) {
+    DTTS_CHECK(e && tokens, DTTS_ERR_ARG, "null argument");
+    *tokens = e->cur_len;
+    return DTTS_OK;
+}
+
+}  // extern "C"

@@ -110,7 +110,8 @@ EXPORTS = [
     "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_solve_timeline",
     "dtts_dit_profile_kernel",
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_fm_create", "dtts_fm_destroy", "dtts_fm_start",
-    "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
+    "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve",
+    "dtts_llm_create", "dtts_llm_destroy", "dtts_llm_set_stream", "dtts_llm_prefill", "dtts_llm_step", "dtts_llm_length", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
     "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_selftest_e4m3",
@@ -432,6 +433,71 @@ class FMHistory:
         a.layout, a.z_out, a.mem, a.use_graph = layout, _addr(z_out), MEM_HOST, int(use_graph)
         check(lib().dtts_fm_solve(self.h, C.byref(a)))
         return z_out
+
+
+class LLMLayerW(C.Structure):
+    _fields_ = [(n, _fp) for n in ("an", "fn", "qw", "qb", "kw", "kb", "vw", "vb", "ow", "ob", "gw", "uw", "dw")]
+
+
+class LLMW(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("layers", C.POINTER(LLMLayerW)), ("final_norm", _fp)]
+
+
+LLM_LAYER_NAMES = {
+    "an": "input_layernorm.weight", "fn": "post_attention_layernorm.weight",
+    "qw": "self_attn.q_proj.weight", "qb": "self_attn.q_proj.bias",
+    "kw": "self_attn.k_proj.weight", "kb": "self_attn.k_proj.bias",
+    "vw": "self_attn.v_proj.weight", "vb": "self_attn.v_proj.bias",
+    "ow": "self_attn.o_proj.weight", "ob": "self_attn.o_proj.bias",
+    "gw": "mlp.gate_proj.weight", "uw": "mlp.up_proj.weight", "dw": "mlp.down_proj.weight",
+}
+
+
+class LLM:
+    """The LLM decoder step (dtts_llm_*), names as the checkpoint's llm.model.* tensors."""
+
+    def __init__(self, weights: dict, n_layers=28, max_batch=64, max_seq=512, device=0):
+        keep = _Keep()
+        arr = (LLMLayerW * n_layers)()
+        for i in range(n_layers):
+            for f, n in LLM_LAYER_NAMES.items():
+                a = _f32(weights.get(f"llm.model.layers.{i}." + n))
+                keep.refs.append(a)
+                setattr(arr[i], f, _ptr(a))
+        fn = _f32(weights["llm.model.norm.weight"])
+        keep.refs.append(fn)
+        s = LLMW(n_layers, arr, _ptr(fn))
+        h = _vp()
+        check(lib().dtts_llm_create(C.byref(s), device, max_batch, max_seq, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_llm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, emb):
+        emb = _f32(emb)
+        out = np.zeros_like(emb)
+        check(lib().dtts_llm_prefill(self.h, _addr(emb), emb.shape[0], emb.shape[1], _addr(out), MEM_HOST))
+        return out
+
+    def step(self, emb):
+        emb = _f32(emb)
+        out = np.zeros_like(emb)
+        check(lib().dtts_llm_step(self.h, _addr(emb), emb.shape[0], _addr(out), MEM_HOST))
+        return out
+
+    def length(self):
+        n = C.c_int()
+        check(lib().dtts_llm_length(self.h, C.byref(n)))
+        return n.value
 
 
 class Attention:

@@ -140,3 +140,37 @@ def fm_history(seed, n_utt, fm_len, w=None, hidden_every=5):
     null_h = np.broadcast_to(hb, (n_utt, fm_len, D))
     uncond = np.where(is_hidden[None, :, None], null_h, lproj).astype(np.float32)
     return np.ascontiguousarray(cond), np.ascontiguousarray(uncond)
+
+
+LH, LF, LKV = 1536, 8960, 256          # Qwen2.5-1.5B: hidden, MLP, K/V width (2 heads x 128)
+LLM_LAYERS = 28
+
+
+def llm_shapes(n_layers=LLM_LAYERS):
+    """Tensor names and shapes of the LLM's decoder (src/llm_manual.cpp:26-44)."""
+    s = {}
+    for i in range(n_layers):
+        p = f"llm.model.layers.{i}."
+        s[p + "input_layernorm.weight"] = (LH,)
+        s[p + "post_attention_layernorm.weight"] = (LH,)
+        s[p + "self_attn.q_proj.weight"] = (LH, LH)
+        s[p + "self_attn.q_proj.bias"] = (LH,)
+        s[p + "self_attn.k_proj.weight"] = (LKV, LH)
+        s[p + "self_attn.k_proj.bias"] = (LKV,)
+        s[p + "self_attn.v_proj.weight"] = (LKV, LH)
+        s[p + "self_attn.v_proj.bias"] = (LKV,)
+        s[p + "self_attn.o_proj.weight"] = (LH, LH)
+        s[p + "mlp.gate_proj.weight"] = (LF, LH)
+        s[p + "mlp.up_proj.weight"] = (LF, LH)
+        s[p + "mlp.down_proj.weight"] = (LH, LF)
+    s["llm.model.norm.weight"] = (LH,)
+    return s
+
+
+def llm_weights(seed=3, n_layers=LLM_LAYERS):
+    """LLM decoder weights: N(0, 0.02), norm gains 1 + N(0, 0.02)."""
+    w = {}
+    for name, shape in llm_shapes(n_layers).items():
+        gain = name.endswith("norm.weight")
+        w[name] = normal(seed, name, shape, 0.02, 1.0 if gain else 0.0)
+    return w

@@ -307,6 +307,37 @@ int dtts_pe_stream_reset(dtts_pe *p, int B);
 int dtts_pe_decode(dtts_pe *p, const float *frames, int B, int n_frames, float *out, int mem);
 int dtts_pe_stream_length(dtts_pe *p, int *tokens);
 
+/* ------------------------------------------------------------------ LLM decoder step
+ * The autoregressive loop's Qwen2.5-1.5B step (src/llm_manual.cpp): a batch of B sequences
+ * advancing together.  bf16 weights and K/V cache, fp32 residual and attention arithmetic.
+ * Embedding lookup stays with the caller: the calls take embeddings. */
+typedef struct dtts_llm dtts_llm;
+typedef struct dtts_llm_layer_weights {
+    const float *an, *fn;             /* input_layernorm, post_attention_layernorm [1536] */
+    const float *qw, *qb;             /* q_proj [1536][1536], [1536]                     */
+    const float *kw, *kb, *vw, *vb;   /* k_proj, v_proj [256][1536], [256]               */
+    const float *ow, *ob;             /* o_proj [1536][1536], bias or NULL               */
+    const float *gw, *uw;             /* gate_proj, up_proj [8960][1536]                 */
+    const float *dw;                  /* down_proj [1536][8960]                          */
+} dtts_llm_layer_weights;
+typedef struct dtts_llm_weights {
+    int n_layers;                     /* 28 for Qwen2.5-1.5B */
+    const dtts_llm_layer_weights *layers;
+    const float *final_norm;          /* model.norm [1536] */
+} dtts_llm_weights;
+/* Replaces load_llm_weights (src/llm_manual.cpp:13): weights uploaded once; K/V cache for
+ * max_batch sequences of max_seq tokens. */
+int dtts_llm_create(const dtts_llm_weights *w, int device, int max_batch, int max_seq, dtts_llm **out);
+int dtts_llm_destroy(dtts_llm *e);
+int dtts_llm_set_stream(dtts_llm *e, void *cuda_stream);
+/* llm_kv_cache_init (src/llm_manual.cpp:237) for B prompts at once: emb [B][n_tok][1536] ->
+ * hidden [B][n_tok][1536] after the final norm; restarts the caches. */
+int dtts_llm_prefill(dtts_llm *e, const float *emb, int B, int n_tok, float *hidden, int mem);
+/* llm_kv_cache_step (src/llm_manual.cpp:342): one embedding per sequence, emb [B][1536] ->
+ * hidden [B][1536]; B must match the prefill. */
+int dtts_llm_step(dtts_llm *e, const float *emb, int B, float *hidden, int mem);
+int dtts_llm_length(dtts_llm *e, int *tokens);
+
 /* ------------------------------------------------------------------ self-test
  * One engine kernel in isolation on host data (no reference counterpart):
  * inputs are rounded to bf16 on the host exactly as the engine stores them. */

@@ -312,6 +312,10 @@ class Oracle:
         return out
 
 
+class _RefLLMLayer(C.Structure):
+    _fields_ = [(n, _fp) for n in ("an", "fn", "qw", "qb", "kw", "kb", "vw", "vb", "ow", "ob", "gw", "uw", "dw")]
+
+
 class Reference:
     """The reference's own include/dit_manual.h, compiled in place (_ref/)."""
 
@@ -325,6 +329,7 @@ class Reference:
         L.ref_manual_attention.argtypes = [_fp, _fp, C.c_int] + [_fp] * 7 + [_u8p, _fp]
         L.ref_dit_block.argtypes = [_fp, _fp, _fp, C.POINTER(DitBlock), C.c_int, _u8p, _fp, C.c_int]
         L.ref_dit_velocity.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp, _u8p, _fp, C.c_int, C.c_int, _fp]
+        L.ref_llm_run.argtypes = [C.c_int, C.POINTER(_RefLLMLayer), _fp, _fp, C.c_int, _fp, C.c_int, _fp, _fp]
 
     @staticmethod
     def available(path: str = REF_PATH) -> bool:
@@ -357,6 +362,31 @@ class Reference:
         self.lib.ref_dit_block(_ptr(out), _ptr(x), _ptr(cond), C.byref(b), x.shape[0],
                                mk[0] if mk else None, _ptr(pos), ffn_mode)
         return out
+
+    def llm_run(self, w, n_layers, prompt_emb, step_emb):
+        """The reference's llm_kv_cache_init on prompt_emb [n_tok][1536] then one
+        llm_kv_cache_step per row of step_emb [n_steps][1536]; returns the
+        prompt's hidden states and the steps' hidden states."""
+        names = ["input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+                 "self_attn.q_proj.bias", "self_attn.k_proj.weight", "self_attn.k_proj.bias",
+                 "self_attn.v_proj.weight", "self_attn.v_proj.bias", "self_attn.o_proj.weight", None,
+                 "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight"]
+        keep = []
+        arr = (_RefLLMLayer * n_layers)()
+        for i in range(n_layers):
+            vals = []
+            for n in names:
+                a = None if n is None else np.ascontiguousarray(w[f"llm.model.layers.{i}." + n], np.float32)
+                keep.append(a)
+                vals.append(_ptr(a))
+            arr[i] = _RefLLMLayer(*vals)
+        fn = np.ascontiguousarray(w["llm.model.norm.weight"], np.float32)
+        pe = np.ascontiguousarray(prompt_emb, np.float32)
+        se = np.ascontiguousarray(step_emb, np.float32)
+        ph = np.zeros_like(pe)
+        sh = np.zeros_like(se)
+        self.lib.ref_llm_run(n_layers, arr, _ptr(fn), _ptr(pe), pe.shape[0], _ptr(se), se.shape[0], _ptr(ph), _ptr(sh))
+        return ph, sh
 
     def dit_velocity(self, w, n_layers, x_in, cond, mask=None, pos=None, ffn_mode=FFN_PER_TOKEN, n_out=None):
         m, keep = make_dit_struct(w, n_layers)
