@@ -58,6 +58,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-pe", action="store_true", help="skip the PatchEncoder stream measurement")
+    ap.add_argument("--no-llm", action="store_true", help="skip the LLM decoder step measurement")
     return ap.parse_args()
 
 
@@ -397,6 +398,44 @@ def measure_pe(args, local_rank):
             "dtype": "bf16"}
 
 
+def measure_llm(args, local_rank):
+    """LLM decoder step at the autoregressive loop's batch: 28 layers of
+    Qwen2.5-1.5B (synthetic weights), 64 sequences prefilled with 64-token
+    prompts, then 16 steps of one embedding each (device-resident inputs,
+    CUDA events on the engine stream, one host call per step)."""
+    import torch
+    import dtts
+    import synth
+    dev = torch.device("cuda", local_rank)
+    B, n_tok, steps, layers = args.n_utt, 64, 16, 28
+    w = synth.llm_weights(3, n_layers=layers)
+    llm = dtts.LLM(w, n_layers=layers, max_batch=B, max_seq=n_tok + steps + 1, device=local_rank)
+    del w
+    stream = torch.cuda.Stream(device=dev)
+    llm.set_stream(stream.cuda_stream)
+    emb = torch.from_numpy(synth.normal(4, "llm.bench", (B, n_tok + steps, 1536), 1.0)).to(dev)
+    prompt = emb[:, :n_tok].contiguous()
+    step_in = [emb[:, n_tok + i].contiguous() for i in range(steps)]
+    out_p = torch.empty((B, n_tok, 1536), device=dev)
+    out_s = torch.empty((B, 1536), device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with torch.cuda.stream(stream):
+        for rep in range(2):   # the first pass warms up
+            ev[0].record(stream)
+            llm.prefill(prompt, out=out_p, mem=dtts.MEM_DEVICE)
+            ev[1].record(stream)
+            for i in range(steps):
+                llm.step(step_in[i], out=out_s, mem=dtts.MEM_DEVICE)
+            ev[2].record(stream)
+    torch.cuda.synchronize()
+    pre_ms, st_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]) / steps
+    llm.close()
+    weight_bytes = layers * 2 * (1536 * 2048 + 1536 * 1536 + 2 * 8960 * 1536 + 8960 * 1536)
+    return {"workload": f"LLM decoder, {layers} layers, {B} sequences: {n_tok}-token prefill, then {steps} steps",
+            "prefill_ms": pre_ms, "step_ms": st_ms, "steps_per_s": 1000.0 / st_ms,
+            "step_weight_stream_gbs": weight_bytes / (st_ms / 1000.0) / 1e9, "dtype": "bf16"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     dist = None
@@ -411,6 +450,7 @@ def run_ours(args, rank, world, local_rank):
     head = measure(args, head_dtype, world, local_rank, dist, inputs)
     extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
     pe = measure_pe(args, local_rank) if (world == 1 and not args.no_pe) else None
+    llm = measure_llm(args, local_rank) if (world == 1 and not args.no_llm) else None
 
     # ---- CPU baseline: reference code (per-token FFN) on the host, rank 0, N = 1
     cpu = None
@@ -441,6 +481,8 @@ def run_ours(args, rank, world, local_rank):
         line["gpu_launches"] = head["gpu_launches"]
         if pe:
             line["patch_encoder"] = pe
+        if llm:
+            line["llm_step"] = llm
         if extra:
             line["fp8"] = {"dtype": "e4m3", "weights": workload_config(args, world, "fp8")["weights"],
                            **{k: extra[k] for k in ("value", "ms_per_step", "e2e", "roofline", "attention_us_per_layer",

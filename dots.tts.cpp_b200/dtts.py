@@ -150,8 +150,11 @@ def lib(path: str = LIB_PATH):
         raise FileNotFoundError(f"{path} is missing: run `python {os.path.join(HERE, 'build.py')}`")
     L = C.CDLL(path)
     L.dtts_version.restype = C.c_char_p
+    L.dtts_version.argtypes = []
     L.dtts_status_string.restype = C.c_char_p
+    L.dtts_status_string.argtypes = [C.c_int]
     L.dtts_last_error.restype = C.c_char_p
+    L.dtts_last_error.argtypes = []
     L.dtts_device_count.argtypes = [C.POINTER(C.c_int)]
     L.dtts_dit_create.argtypes = [C.POINTER(DitW), C.c_int, C.c_int, C.POINTER(_vp)]
     L.dtts_dit_create_from_safetensors.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
@@ -190,6 +193,26 @@ def lib(path: str = LIB_PATH):
     L.dtts_st_count.argtypes = [_vp, C.POINTER(C.c_int)]
     L.dtts_st_shape.argtypes = [_vp, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int64)]
     L.dtts_st_read_f32.argtypes = [_vp, C.c_char_p, _fp, C.c_size_t]
+    L.dtts_dit_solve_timeline.argtypes = [_vp, C.POINTER(SolveArgs), C.c_int, C.POINTER(C.c_float),
+                                          C.POINTER(C.c_int)]
+    L.dtts_fm_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_fm_destroy.argtypes = [_vp]
+    L.dtts_fm_start.argtypes = [_vp, _vp, C.c_int]
+    L.dtts_fm_append_latents.argtypes = [_vp, _vp, C.c_int, C.c_int]
+    L.dtts_fm_append_hidden.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int]
+    L.dtts_fm_length.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_fm_read.argtypes = [_vp, _vp, _vp]
+    L.dtts_fm_solve.argtypes = [_vp, C.POINTER(SolveArgs)]
+    L.dtts_llm_create.argtypes = [C.POINTER(LLMW), C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_llm_destroy.argtypes = [_vp]
+    L.dtts_llm_set_stream.argtypes = [_vp, _vp]
+    L.dtts_llm_prefill.argtypes = [_vp, _vp, C.c_int, C.c_int, _vp, C.c_int]
+    L.dtts_llm_step.argtypes = [_vp, _vp, C.c_int, _vp, C.c_int]
+    L.dtts_llm_length.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_selftest_e4m3.argtypes = [_fp, _u8p, C.c_int, C.c_int]
+    L.dtts_selftest_gemm_e4m3.argtypes = [_u8p, _fp, _u8p, _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.c_int]
+    L.dtts_fp8_quantize_rows.argtypes = [_fp, C.c_int, C.c_int, _u8p, _fp]
     _LIB = L
     return L
 
@@ -482,16 +505,22 @@ class LLM:
         except Exception:
             pass
 
-    def prefill(self, emb):
-        emb = _f32(emb)
-        out = np.zeros_like(emb)
-        check(lib().dtts_llm_prefill(self.h, _addr(emb), emb.shape[0], emb.shape[1], _addr(out), MEM_HOST))
+    def set_stream(self, stream_ptr):
+        check(lib().dtts_llm_set_stream(self.h, stream_ptr))
+
+    def prefill(self, emb, out=None, mem=MEM_HOST):
+        """mem=MEM_DEVICE: emb and out are device tensors and the call only enqueues."""
+        if mem == MEM_HOST:
+            emb = _f32(emb)
+            out = np.zeros_like(emb) if out is None else out
+        check(lib().dtts_llm_prefill(self.h, _addr(emb), emb.shape[0], emb.shape[1], _addr(out), mem))
         return out
 
-    def step(self, emb):
-        emb = _f32(emb)
-        out = np.zeros_like(emb)
-        check(lib().dtts_llm_step(self.h, _addr(emb), emb.shape[0], _addr(out), MEM_HOST))
+    def step(self, emb, out=None, mem=MEM_HOST):
+        if mem == MEM_HOST:
+            emb = _f32(emb)
+            out = np.zeros_like(emb) if out is None else out
+        check(lib().dtts_llm_step(self.h, _addr(emb), emb.shape[0], _addr(out), mem))
         return out
 
     def length(self):

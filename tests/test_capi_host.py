@@ -31,6 +31,13 @@ def test_library_exports_every_declared_symbol():
     assert sorted(names) == sorted(dtts.EXPORTS)
 
 
+def test_every_export_has_a_ctypes_signature(dtts_mod):
+    """Without argtypes ctypes would pass a 64-bit pointer as a C int."""
+    L = dtts.lib()
+    missing = [n for n in dtts.EXPORTS if getattr(L, n).argtypes is None]
+    assert not missing, missing
+
+
 def test_version_and_status_strings(dtts_mod):
     L = dtts_mod.lib()
     assert b"sm_100a" in L.dtts_version()
