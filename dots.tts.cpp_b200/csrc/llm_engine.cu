@@ -60,9 +60,12 @@ __global__ void __launch_bounds__(256) llm_rms_norm_kernel(const float *__restri
 // pos0 + t, q to qout (fp32), k and v appended to the caches
 // [b][kv head][cap][128] (bf16).  One block per token, 128 threads: thread
 // d < 64 rotates pair (d, d + 64) of every head.
+// pos_dev, if set, holds pos0 on the device (graph-captured steps).
 __global__ void __launch_bounds__(128) llm_rope_cache_kernel(const float *__restrict__ qkv, int T, int pos0,
+                                                              const int *__restrict__ pos_dev,
                                                               const float2 *__restrict__ rope, float *__restrict__ qout,
                                                               bf16 *__restrict__ kc, bf16 *__restrict__ vc, int cap) {
+    if (pos_dev) pos0 = *pos_dev;
     const int m = blockIdx.x, b = m / T, t = m % T, p = pos0 + t;
     const float *row = qkv + (long long)m * kLQKV;
     const int d = threadIdx.x;
@@ -85,11 +88,15 @@ __global__ void __launch_bounds__(128) llm_rope_cache_kernel(const float *__rest
 }
 
 // Grouped-query causal attention, one warp per (token m, query head): lane
-// l owns dims 4l..4l+3; keys 0 .. pos0 + t of the token's sequence; online
-// softmax in fp32; the output row goes to ao (bf16, the o_proj input).
+// l owns dims 4l..4l+3; keys 0 .. pos0 + t of the token's sequence, eight at
+// a time (their K and V rows are loaded together and their dot products
+// reduced together, so the memory latency is paid once per eight keys);
+// online softmax in fp32; the output row goes to ao (bf16, the o_proj input).
 __global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__ q, const bf16 *__restrict__ kc,
-                                                       const bf16 *__restrict__ vc, int T, int pos0, int cap, int M,
+                                                       const bf16 *__restrict__ vc, int T, int pos0,
+                                                       const int *__restrict__ pos_dev, int cap, int M,
                                                        bf16 *__restrict__ ao) {
+    if (pos_dev) pos0 = *pos_dev;
     const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wid >= M * kLNH) return;
     const int m = wid / kLNH, h = wid % kLNH, b = m / T, t = m % T;
@@ -99,22 +106,46 @@ __global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__
     const float4 qv = reinterpret_cast<const float4 *>(q + (long long)m * kLH + h * kLHD)[lane];
     const bf16 *kb = kc + ((long long)b * kLNKV + kvh) * cap * kLHD + 4 * lane;
     const bf16 *vb = vc + ((long long)b * kLNKV + kvh) * cap * kLHD + 4 * lane;
+    constexpr int U = 8;
     float mx = -INFINITY, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < n_keys; j++) {
-        const uint2 kr = *reinterpret_cast<const uint2 *>(kb + (long long)j * kLHD);
-        const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr.x));
-        const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr.y));
-        const float s = warp_sum((qv.x * k01.x + qv.y * k01.y) + (qv.z * k23.x + qv.w * k23.y)) * scale;
-        const float nm = fmaxf(mx, s);
-        const float corr = expf(mx - nm), e = expf(s - nm);
-        const uint2 vr = *reinterpret_cast<const uint2 *>(vb + (long long)j * kLHD);
-        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr.x));
-        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr.y));
-        acc.x = acc.x * corr + e * v01.x; acc.y = acc.y * corr + e * v01.y;
-        acc.z = acc.z * corr + e * v23.x; acc.w = acc.w * corr + e * v23.y;
-        l = l * corr + e;
-        mx = nm;
+    for (int j0 = 0; j0 < n_keys; j0 += U) {
+        uint2 kr[U], vr[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = min(j0 + u, n_keys - 1);   // past the end: a valid row, masked below
+            kr[u] = *reinterpret_cast<const uint2 *>(kb + (long long)j * kLHD);
+            vr[u] = *reinterpret_cast<const uint2 *>(vb + (long long)j * kLHD);
+        }
+        float sc[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[u].x));
+            const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[u].y));
+            sc[u] = (qv.x * k01.x + qv.y * k01.y) + (qv.z * k23.x + qv.w * k23.y);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int u = 0; u < U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+        float bm = mx;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            sc[u] = (j0 + u < n_keys) ? sc[u] * scale : -INFINITY;
+            bm = fmaxf(bm, sc[u]);
+        }
+        const float corr = expf(mx - bm);
+        acc.x *= corr; acc.y *= corr; acc.z *= corr; acc.w *= corr;
+        l *= corr;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const float e = expf(sc[u] - bm);
+            const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr[u].x));
+            const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr[u].y));
+            acc.x += e * v01.x; acc.y += e * v01.y; acc.z += e * v23.x; acc.w += e * v23.y;
+            l += e;
+        }
+        mx = bm;
     }
     const float inv = 1.0f / l;
     reinterpret_cast<uint2 *>(ao + (long long)m * kLH + h * kLHD)[lane] =
@@ -174,14 +205,23 @@ struct dtts_llm {
     float *final_norm = nullptr;
     bf16 *kc = nullptr, *vc = nullptr;   // [n_layers][max_batch][2][max_seq][128]
     float2 *rope = nullptr;              // [max_seq][64]
+    int *d_len = nullptr;                // cache length on the device (graph-captured steps)
     int *d_err = nullptr;
+    // step graphs, one per batch size; dropped when the workspace moves
+    struct Graph { int B; cudaGraphExec_t exec; };
+    std::vector<Graph> graphs;
+    void drop_graphs() {
+        for (Graph &g : graphs) cudaGraphExecDestroy(g.exec);
+        graphs.clear();
+    }
     int cur_B = 0, cur_len = 0;
     long long cap_tok = 0;
     float *h = nullptr, *qkv = nullptr, *q = nullptr, *gu = nullptr;
     bf16 *act = nullptr, *ao = nullptr, *ffn = nullptr;
-    CUtensorMap t_act, t_ao, t_ffn, t_h;
+    CUtensorMap t_act, t_ao, t_ffn, t_h, t_qkv_r, t_gu_r;   // *_r: fp32 reduce-add targets
 
     ~dtts_llm() {
+        drop_graphs();
         ws.free_all();
         cache.free_all();
         wts.free_all();
@@ -191,6 +231,7 @@ struct dtts_llm {
     int ensure(long long tok) {
         if (tok <= cap_tok) return DTTS_OK;
         DTTS_CUDA(cudaStreamSynchronize(stream));
+        drop_graphs();
         ws.free_all();
         cap_tok = std::max<long long>(tok, 64);
         const size_t T = (size_t)cap_tok;
@@ -203,7 +244,8 @@ struct dtts_llm {
         ffn = (bf16 *)ws.alloc(T * kLF * 2);
         DTTS_CHECK(h && qkv && q && gu && act && ao && ffn, DTTS_ERR_OOM, "LLM workspace allocation failed");
         bool ok = make_tmap_bf16(&t_act, act, T, kLH, 128) && make_tmap_bf16(&t_ao, ao, T, kLH, 128) &&
-                  make_tmap_bf16(&t_ffn, ffn, T, kLF, 128) && make_tmap_f32_resid(&t_h, h, T, kLH);
+                  make_tmap_bf16(&t_ffn, ffn, T, kLF, 128) && make_tmap_f32_resid(&t_h, h, T, kLH) &&
+                  make_tmap_f32_resid(&t_qkv_r, qkv, T, kLQKV) && make_tmap_f32_resid(&t_gu_r, gu, T, 2 * kLF);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (LLM workspace)");
         return DTTS_OK;
     }
@@ -216,8 +258,10 @@ struct dtts_llm {
         return o;
     }
 
-    // emb already in h ([B * T][1536]); runs every layer and the final norm into `out`
-    int enqueue(int B, int T, int pos0, float *out) {
+    // emb already in h ([B * T][1536]); runs every layer and the final norm into
+    // `out`, then advances d_len; dev_pos: positions from d_len, not pos0
+    int enqueue(int B, int T, int pos0, bool dev_pos, float *out) {
+        const int *pd = dev_pos ? d_len : nullptr;
         const int M = B * T;
         const bool small = M <= 256;
         const int bn = small ? 128 : 256;
@@ -225,24 +269,36 @@ struct dtts_llm {
         for (int l = 0; l < n_layers; l++) {
             const Layer &L = layers[l];
             llm_rms_norm_kernel<true><<<(M + 7) / 8, 256, 0, stream>>>(h, L.an, act, M);
-            {
-                GemmOp o = op(t_act, small ? L.tqkv_s : L.tqkv, M, kLQKV, kLH, EPI_F32, bn);
+            if (small) {
+                // few rows: split K 8 ways so that 128 CTAs stream the weights,
+                // partial sums reduce-added into the zeroed fp32 output
+                DTTS_CUDA(cudaMemsetAsync(qkv, 0, (size_t)M * kLQKV * 4, stream));
+                GemmOp o = op(t_act, L.tqkv_s, M, kLQKV, kLH, EPI_RESID, bn);
+                o.tr = t_qkv_r; o.ep.bias = L.bqkv; o.ep.resid = qkv; o.ep.ldr = kLQKV; o.ep.ksplit = 8;
+                DTTS_CUDA(launch_gemm(o, num_sms, stream));
+            } else {
+                GemmOp o = op(t_act, L.tqkv, M, kLQKV, kLH, EPI_F32, bn);
                 o.ep.bias = L.bqkv; o.ep.out = qkv; o.ep.ldo = kLQKV;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
-            llm_rope_cache_kernel<<<M, 128, 0, stream>>>(qkv, T, pos0, rope, q, kc + l * layer_stride,
+            llm_rope_cache_kernel<<<M, 128, 0, stream>>>(qkv, T, pos0, pd, rope, q, kc + l * layer_stride,
                                                          vc + l * layer_stride, max_seq);
             llm_attn_kernel<<<(M * kLNH + 7) / 8, 256, 0, stream>>>(q, kc + l * layer_stride, vc + l * layer_stride, T,
-                                                                    pos0, max_seq, M, ao);
+                                                                    pos0, pd, max_seq, M, ao);
             {
                 GemmOp o = op(t_ao, small ? L.to_s : L.to, M, kLH, kLH, EPI_RESID, bn);
                 o.tr = t_h; o.ep.bias = L.bo; o.ep.resid = h; o.ep.ldr = kLH;
-                o.ep.ksplit = small ? 4 : 1;
+                o.ep.ksplit = small ? 8 : 1;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
             llm_rms_norm_kernel<true><<<(M + 7) / 8, 256, 0, stream>>>(h, L.fn, act, M);
-            {
-                GemmOp o = op(t_act, small ? L.tgu_s : L.tgu, M, 2 * kLF, kLH, EPI_F32, bn);
+            if (small) {
+                DTTS_CUDA(cudaMemsetAsync(gu, 0, (size_t)M * 2 * kLF * 4, stream));
+                GemmOp o = op(t_act, L.tgu_s, M, 2 * kLF, kLH, EPI_RESID, bn);
+                o.tr = t_gu_r; o.ep.resid = gu; o.ep.ldr = 2 * kLF; o.ep.ksplit = 2;
+                DTTS_CUDA(launch_gemm(o, num_sms, stream));
+            } else {
+                GemmOp o = op(t_act, L.tgu, M, 2 * kLF, kLH, EPI_F32, bn);
                 o.ep.out = gu; o.ep.ldo = 2 * kLF;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
@@ -251,11 +307,12 @@ struct dtts_llm {
             {
                 GemmOp o = op(t_ffn, small ? L.td_s : L.td, M, kLH, kLF, EPI_RESID, bn);
                 o.tr = t_h; o.ep.resid = h; o.ep.ldr = kLH;
-                o.ep.ksplit = small ? 4 : 1;
+                o.ep.ksplit = small ? 10 : 1;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
         }
         llm_rms_norm_kernel<false><<<(M + 7) / 8, 256, 0, stream>>>(h, final_norm, out, M);
+        launch_advance_len(d_len, T, stream);
         DTTS_CUDA(cudaGetLastError());
         return DTTS_OK;
     }
@@ -272,7 +329,27 @@ struct dtts_llm {
         float *outd = qkv;
         DTTS_CUDA(cudaMemcpyAsync(h, emb, (size_t)M * kLH * 4,
                                   mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, stream));
-        if ((st = enqueue(B, T, cur_len, outd))) return st;
+        if (T == 1) {
+            // decode step: one graph per batch size, positions from d_len
+            cudaGraphExec_t exec = nullptr;
+            for (Graph &g : graphs)
+                if (g.B == B) exec = g.exec;
+            if (!exec) {
+                cudaGraph_t graph = nullptr;
+                DTTS_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+                st = enqueue(B, 1, 0, true, outd);
+                cudaError_t ce = cudaStreamEndCapture(stream, &graph);
+                if (st) { if (graph) cudaGraphDestroy(graph); return st; }
+                DTTS_CUDA(ce);
+                ce = cudaGraphInstantiate(&exec, graph, 0);
+                cudaGraphDestroy(graph);
+                DTTS_CUDA(ce);
+                graphs.push_back({B, exec});
+            }
+            DTTS_CUDA(cudaGraphLaunch(exec, stream));
+        } else if ((st = enqueue(B, T, cur_len, false, outd))) {
+            return st;
+        }
         DTTS_CUDA(cudaMemcpyAsync(hidden, outd, (size_t)M * kLH * 4,
                                   mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, stream));
         cur_len += T;
@@ -337,7 +414,8 @@ int dtts_llm_create(const dtts_llm_weights *w, int device, int max_batch, int ma
     e->kc = (bf16 *)e->cache.alloc(cache_elems * 2);
     e->vc = (bf16 *)e->cache.alloc(cache_elems * 2);
     e->rope = (float2 *)e->cache.alloc((size_t)max_seq * 64 * sizeof(float2));
-    DTTS_CHECK(e->kc && e->vc && e->rope, DTTS_ERR_OOM, "LLM KV cache allocation failed (%zu MB)", cache_elems * 4 >> 20);
+    e->d_len = (int *)e->cache.alloc(sizeof(int));
+    DTTS_CHECK(e->kc && e->vc && e->rope && e->d_len, DTTS_ERR_OOM, "LLM KV cache allocation failed (%zu MB)", cache_elems * 4 >> 20);
     // (cos, sin)(pos * theta_d), theta_d = (1e6^(-2/128))^d by repeated
     // multiplication, as src/llm_manual.cpp:398-403 and :449-451 compute them
     std::vector<float2> rt((size_t)max_seq * 64);
@@ -371,8 +449,10 @@ int dtts_llm_set_stream(dtts_llm *e, void *stream) {
 int dtts_llm_prefill(dtts_llm *e, const float *emb, int B, int n_tok, float *hidden, int mem) {
     DTTS_CHECK(e, DTTS_ERR_ARG, "null engine");
     DTTS_CHECK(B >= 1 && B <= e->max_batch && n_tok >= 1, DTTS_ERR_ARG, "bad prefill shape %d x %d", B, n_tok);
+    DeviceGuard g(e->device);
     e->cur_B = B;
     e->cur_len = 0;
+    DTTS_CUDA(cudaMemsetAsync(e->d_len, 0, sizeof(int), e->stream));
     return e->run(emb, B, n_tok, hidden, mem);
 }
 
