@@ -530,7 +530,88 @@ cudaError_t attention_short_prepare() {
     return cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kShortSmem);
 }
 
+// Decode attention (a few queries per sequence against a long cache, causal,
+// no mask): one CTA of 4 warps per (row, query, head); each warp takes every
+// fourth block of 16 keys, loading their K and V rows together and reducing
+// their 16 dot products together (lane l owns dims 2l, 2l+1 of the 64); the
+// warps' online-softmax states are merged through shared memory.
+constexpr int kDecWarps = 4, kDecKeys = 16;
+
+__global__ void __launch_bounds__(kDecWarps * 32, 8) attn_decode_kernel(const AttnArgs a) {
+    const int q_pos0 = a.kv_base_dev ? *a.kv_base_dev : a.q_pos0;
+    const int kv_len = a.kv_base_dev ? q_pos0 + a.Tq : a.kv_len;
+    const int h = blockIdx.x % kH, qi = (blockIdx.x / kH) % a.Tq, r = blockIdx.x / (kH * a.Tq);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_keys = a.causal ? min(kv_len, q_pos0 + qi + 1) : kv_len;
+    const float sc = a.scale;
+    const bf16 *qg = reinterpret_cast<const bf16 *>(a.q) + ((long long)r * a.Tq + qi) * a.ldq + h * kHD;
+    const float2 qv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162 *>(qg)[lane]);
+    const bf16 *kg = reinterpret_cast<const bf16 *>(a.k) + (long long)r * a.kv_cap * a.ldkv + h * kHD + 2 * lane;
+    const bf16 *vg = reinterpret_cast<const bf16 *>(a.v) + (long long)r * a.kv_cap * a.ldkv + h * kHD + 2 * lane;
+    float mx = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int j0 = warp * kDecKeys; j0 < n_keys; j0 += kDecWarps * kDecKeys) {
+        uint32_t kr[kDecKeys], vr[kDecKeys];
+#pragma unroll
+        for (int u = 0; u < kDecKeys; u++) {
+            const int j = min(j0 + u, n_keys - 1);   // past the end: a valid row, masked below
+            kr[u] = *reinterpret_cast<const uint32_t *>(kg + (long long)j * a.ldkv);
+            vr[u] = *reinterpret_cast<const uint32_t *>(vg + (long long)j * a.ldkv);
+        }
+        float s[kDecKeys];
+#pragma unroll
+        for (int u = 0; u < kDecKeys; u++) {
+            const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[u]));
+            s[u] = qv.x * kk.x + qv.y * kk.y;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int u = 0; u < kDecKeys; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
+        float bm = mx;
+#pragma unroll
+        for (int u = 0; u < kDecKeys; u++) {
+            s[u] = (j0 + u < n_keys) ? s[u] * sc : -INFINITY;
+            bm = fmaxf(bm, s[u]);
+        }
+        const float corr = expf(mx - bm);
+        o0 *= corr; o1 *= corr; l *= corr;
+#pragma unroll
+        for (int u = 0; u < kDecKeys; u++) {
+            const float e = expf(s[u] - bm);
+            const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr[u]));
+            o0 += e * vv.x; o1 += e * vv.y; l += e;
+        }
+        mx = bm;
+    }
+    __shared__ float sm_m[kDecWarps], sm_l[kDecWarps];
+    __shared__ float2 sm_o[kDecWarps][32];
+    if (lane == 0) { sm_m[warp] = mx; sm_l[warp] = l; }
+    sm_o[warp][lane] = make_float2(o0, o1);
+    __syncthreads();
+    if (warp == 0) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; w++) M = fmaxf(M, sm_m[w]);
+        float L = 0.f, x = 0.f, y = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; w++) {
+            if (sm_m[w] == -INFINITY) continue;   // a warp that saw no key
+            const float f = expf(sm_m[w] - M);
+            L += sm_l[w] * f;
+            x += sm_o[w][lane].x * f;
+            y += sm_o[w][lane].y * f;
+        }
+        const float inv = L > 0.f ? 1.0f / L : 0.f;
+        bf16 *og = reinterpret_cast<bf16 *>(a.o) + ((long long)r * a.Tq + qi) * a.ldo + h * kHD;
+        reinterpret_cast<uint32_t *>(og)[lane] = pack_bf16x2(x * inv, y * inv);
+    }
+}
+
 void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
+    if (a.Tq <= 8 && !a.mask && !a.mask_bits && !a.o8 && (a.kv_base_dev || a.kv_len > 64)) {
+        attn_decode_kernel<<<a.rows * a.Tq * kH, kDecWarps * 32, 0, s>>>(a);
+        return;
+    }
     if (a.Tq <= 64 && a.kv_len <= 64 && !a.kv_base_dev) {
         const int n_pairs = a.rows * kH;
         int dev = 0, nsm = 148;

@@ -23,12 +23,49 @@ using namespace dtts;
 
 namespace {
 constexpr int kBN = 256;
-// Calls of at most kSmallTok tokens (decode steps) use 128-wide tiles, split
-// the two residual GEMMs along K (more CTAs stream the weights; the partial
-// sums reach the residual in run-dependent order), read the cache position
-// from device memory and replay one CUDA graph per shape.
+// Calls of at most kSmallTok tokens (decode steps) use 128-wide tiles and split
+// every layer GEMM along K so that about 128 CTAs stream the weights: QKV and
+// FFN1 reduce-add into zeroed fp32 rows (finished by pe_qkv_finish_kernel and
+// pe_silu_kernel, which zero them again behind themselves), O and FFN2 into the
+// residual.  Partial sums arrive in run-dependent order.  These calls read the
+// cache position from device memory and replay one CUDA graph per shape.
 constexpr int kBNs = 128;
 constexpr long long kSmallTok = 256;
+constexpr int kKsQKV = 8, kKsO = 16, kKsF1 = 4, kKsF2 = 16;
+
+// Split-K QKV finish for token m = b * T + t at cache position p = start + t:
+// RoPE on adjacent pairs of q and k (the EPI_QKV epilogue's rotation), q to
+// bf16 rows, k and v into the caches, then the fp32 row is zeroed for the next
+// reduce-add.  One block of 256 threads per token.
+__global__ void __launch_bounds__(256) pe_qkv_finish_kernel(float *__restrict__ qkv, int T, int start,
+                                                            const int *__restrict__ start_dev,
+                                                            const float2 *__restrict__ rope, bf16 *__restrict__ q,
+                                                            bf16 *__restrict__ kc, bf16 *__restrict__ vc, int cap) {
+    if (start_dev) start = *start_dev;
+    const int m = blockIdx.x, b = m / T, t = m % T, p = start + t;
+    float2 *row = reinterpret_cast<float2 *>(qkv + (long long)m * 3 * kD);
+    const long long crow = ((long long)b * cap + p) * kD;
+    for (int i = threadIdx.x; i < kD / 2; i += blockDim.x) {
+        const float2 cs = rope[(long long)p * 32 + (i & 31)];
+        const float2 xq = row[i], xk = row[kD / 2 + i], xv = row[kD + i];
+        row[i] = row[kD / 2 + i] = row[kD + i] = make_float2(0.f, 0.f);
+        reinterpret_cast<uint32_t *>(q + (long long)m * kD)[i] =
+            pack_bf16x2(xq.x * cs.x - xq.y * cs.y, xq.x * cs.y + xq.y * cs.x);
+        reinterpret_cast<uint32_t *>(kc + crow)[i] = pack_bf16x2(xk.x * cs.x - xk.y * cs.y, xk.x * cs.y + xk.y * cs.x);
+        reinterpret_cast<uint32_t *>(vc + crow)[i] = pack_bf16x2(xv.x, xv.y);
+    }
+}
+
+// ffn = bf16(silu(x)) over n4 groups of four, x zeroed behind the read
+__global__ void pe_silu_kernel(float *__restrict__ x, bf16 *__restrict__ ffn, long long n4) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    float4 v = reinterpret_cast<float4 *>(x)[i];
+    reinterpret_cast<float4 *>(x)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    v.x = v.x / (1.0f + __expf(-v.x)); v.y = v.y / (1.0f + __expf(-v.y));
+    v.z = v.z / (1.0f + __expf(-v.z)); v.w = v.w / (1.0f + __expf(-v.w));
+    reinterpret_cast<uint2 *>(ffn)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
 
 int up_f32(DeviceArena &a, const float *h, size_t n, float **out) {
     *out = nullptr;
@@ -85,6 +122,10 @@ struct dtts_pe {
     float *frames = nullptr, *h = nullptr, *outf = nullptr;
     bf16 *conv = nullptr, *act = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *pairs = nullptr;
     CUtensorMap t_conv, t_act, t_att, t_ffn, t_pairs, t_h;
+    // split-K targets of the small path ([kSmallTok][3 * 1024] and
+    // [kSmallTok][4096] fp32), all zero between calls
+    float *qkv32 = nullptr, *ffn32 = nullptr;
+    CUtensorMap t_qkv32, t_ffn32;
     int launches = 0;
     // decode graphs, keyed by (B, n_frames); dropped when the workspace moves
     struct Graph { int B, n_frames; cudaGraphExec_t exec; };
@@ -118,13 +159,18 @@ struct dtts_pe {
         ffn = (bf16 *)ws.alloc(T * kF * 2);
         pairs = (bf16 *)ws.alloc(T * kD * 2);   // [T/2][2048]
         outf = (float *)ws.alloc((T / 2 + 1) * kLLM * 4);
+        qkv32 = (float *)ws.alloc((size_t)kSmallTok * 3 * kD * 4);
+        ffn32 = (float *)ws.alloc((size_t)kSmallTok * kF * 4);
         for (void *p : ws.ptrs)
             if (!p) { ws.free_all(); cap_tok = 0; set_error("workspace allocation failed"); return DTTS_ERR_OOM; }
         bool ok = make_tmap_bf16(&t_conv, conv, T, kLat, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
                   make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
                   make_tmap_bf16(&t_pairs, pairs, T / 2 > 0 ? T / 2 : 1, 2 * kD, 128) &&
-                  make_tmap_f32_resid(&t_h, h, T, kD);
+                  make_tmap_f32_resid(&t_h, h, T, kD) && make_tmap_f32_resid(&t_qkv32, qkv32, kSmallTok, 3 * kD) &&
+                  make_tmap_f32_resid(&t_ffn32, ffn32, kSmallTok, kF);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder workspace)");
+        DTTS_CUDA(cudaMemsetAsync(qkv32, 0, (size_t)kSmallTok * 3 * kD * 4, stream));
+        DTTS_CUDA(cudaMemsetAsync(ffn32, 0, (size_t)kSmallTok * kF * 4, stream));
         return DTTS_OK;
     }
 
@@ -155,8 +201,16 @@ struct dtts_pe {
             const Layer &Ly = layers[l];
             launches++;
             launch_rms_norm(h, act, M, Ly.an, stream);
-            {
-                GemmOp op = op0(t_act, small ? Ly.tqkv_s : Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
+            if (small) {
+                GemmOp op = op0(t_act, Ly.tqkv_s, M, 3 * kD, kD, EPI_RESID, d_err);
+                op.bn = bn; op.tr = t_qkv32;
+                op.ep.resid = qkv32; op.ep.ldr = 3 * kD; op.ep.ksplit = kKsQKV;
+                if ((st = gemm(op))) return st;
+                launches++;
+                pe_qkv_finish_kernel<<<M, 256, 0, stream>>>(qkv32, T, cur_len, dev_pos ? d_len : nullptr, rope, q,
+                                                            kc + l * layer_stride, vc + l * layer_stride, max_tokens);
+            } else {
+                GemmOp op = op0(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
                 op.bn = bn;
                 op.ep.q = q; op.ep.ldq = kD;
                 op.ep.k = kc + l * layer_stride; op.ep.v = vc + l * layer_stride; op.ep.ldkv = kD;
@@ -177,23 +231,30 @@ struct dtts_pe {
             {
                 GemmOp op = op0(t_att, small ? Ly.to_s : Ly.to, M, kD, kD, EPI_RESID, d_err);
                 op.bn = bn;
-                op.ep.ksplit = small ? 2 : 1;
+                op.ep.ksplit = small ? kKsO : 1;
                 op.tr = t_h;
                 op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
             }
             launches++;
             launch_rms_norm(h, act, M, Ly.fn, stream);
-            {
-                GemmOp op = op0(t_act, small ? Ly.t1_s : Ly.t1, M, kF, kD, EPI_SILU_BF16, d_err);
-                op.bn = bn;
+            if (small) {
+                GemmOp op = op0(t_act, Ly.t1_s, M, kF, kD, EPI_RESID, d_err);
+                op.bn = bn; op.tr = t_ffn32;
+                op.ep.bias = Ly.b1; op.ep.resid = ffn32; op.ep.ldr = kF; op.ep.ksplit = kKsF1;
+                if ((st = gemm(op))) return st;
+                launches++;
+                const long long n4 = (long long)M * kF / 4;
+                pe_silu_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(ffn32, ffn, n4);
+            } else {
+                GemmOp op = op0(t_act, Ly.t1, M, kF, kD, EPI_SILU_BF16, d_err);
                 op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
                 if ((st = gemm(op))) return st;
             }
             {
                 GemmOp op = op0(t_ffn, small ? Ly.t2_s : Ly.t2, M, kD, kF, EPI_RESID, d_err);
                 op.bn = bn;
-                op.ep.ksplit = small ? 4 : 1;
+                op.ep.ksplit = small ? kKsF2 : 1;
                 op.tr = t_h;
                 op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
@@ -219,7 +280,14 @@ struct dtts_pe {
         if (st) return st;
         int err = 0;
         DTTS_CUDA(cudaMemcpy(&err, d_err, 4, cudaMemcpyDeviceToHost));
-        if (err) { cudaMemset(d_err, 0, 4); set_error("device wait limit reached (code %d)", err); return DTTS_ERR_TIMEOUT; }
+        if (err) {
+            // an abandoned call may leave partial sums in the split-K targets
+            cudaMemset(d_err, 0, 4);
+            if (qkv32) cudaMemset(qkv32, 0, (size_t)kSmallTok * 3 * kD * 4);
+            if (ffn32) cudaMemset(ffn32, 0, (size_t)kSmallTok * kF * 4);
+            set_error("device wait limit reached (code %d)", err);
+            return DTTS_ERR_TIMEOUT;
+        }
         return DTTS_OK;
     }
 
