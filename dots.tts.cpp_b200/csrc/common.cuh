@@ -27,6 +27,35 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 DTTS_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it in the stream still
+// runs.  Every kernel here calls pdl_wait() in all threads before its first
+// access to memory that an earlier kernel writes or reads (only constant
+// weights may be fetched before it), so memory effects keep the stream
+// order; after an ordinary launch pdl_wait() returns at once.  pdl_trigger()
+// lets the next kernel's CTAs be scheduled once every CTA of this grid has
+// issued it.
+DTTS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+DTTS_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// k<<<grid, block, smem, s>>>(args...), with programmatic stream
+// serialization when pdl is set (the kernel must follow the pdl_wait rule)
+template <typename... P, typename... A>
+inline cudaError_t launch_k(bool pdl, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            A &&...args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<A &&>(args)...);
+}
+
 DTTS_DEV unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

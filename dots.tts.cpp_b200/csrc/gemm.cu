@@ -1,8 +1,18 @@
 // Host side of the tcgen05 GEMM: tensor-map encoding and launch dispatch.
 #include "kernels.cuh"
+
+#include <cstdlib>
 #include <mutex>
 
 namespace dtts {
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("DTTS_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 namespace {
 
@@ -29,9 +39,8 @@ cudaError_t launch_one(const GemmOp &op, int num_sms, cudaStream_t s) {
     using Cfg = GemmCfg<BN, NW, EPI, F8>;
     const int units = ((op.M + Cfg::BM - 1) / Cfg::BM) * (op.N / BN) * (op.ep.ksplit > 0 ? op.ep.ksplit : 1);
     const int grid = units < num_sms ? units : num_sms;
-    gemm_tc_kernel<BN, EPI, NW, F8><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(op.ta, op.tb, op.tr, op.M, op.N,
-                                                                                op.K, op.ep);
-    return cudaGetLastError();
+    return launch_k(op.pdl && pdl_enabled(), gemm_tc_kernel<BN, EPI, NW, F8>, dim3(grid), dim3(Cfg::THREADS),
+                    (size_t)Cfg::SMEM_BYTES, s, op.ta, op.tb, op.tr, op.M, op.N, op.K, op.ep);
 }
 
 // e4m3 operands: the three epilogues of the DiT block's FP8 path, and fp32 output

@@ -286,6 +286,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    const bool producer = warp == 0 && lane == 0;
+    if (!producer) { pdl_wait(); pdl_trigger(); }
 
     if (warp == 0) {
         if (lane == 0) {
@@ -295,16 +297,36 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             int last_par[STAGES];  // parity of the last load issued per stage, -1: none
 #pragma unroll
             for (int s = 0; s < STAGES; s++) last_par[s] = -1;
+            // The first unit's weight (B) tiles do not depend on earlier
+            // kernels: they are requested before the wait on the previous
+            // kernel, into stages 0 .. npre-1, whose A tiles follow after it.
+            int npre = 0;
+            if (blockIdx.x < num_units) {
+                const int tile = blockIdx.x % num_tiles, split = blockIdx.x / num_tiles;
+                const int nb = tile / num_m, kb0 = split * kblocks;
+                npre = kblocks < STAGES ? kblocks : STAGES;
+                for (int kb = 0; kb < npre; kb++) {
+                    mbar_arrive_expect_tx(&full[kb], Cfg::STAGE_BYTES);
+                    tma_load_2d(sB + kb * Cfg::B_BYTES, &tmB, &full[kb], (kb0 + kb) * Cfg::BK, nb * BN);
+                    last_par[kb] = 0;
+                }
+            }
+            pdl_wait();
+            pdl_trigger();
             bool ok = true;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int tile = u % num_tiles, split = u / num_tiles;
                 const int mb = tile % num_m, nb = tile / num_m;
                 const int kb0 = split * kblocks;
                 for (int kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                    const bool pre = u == (int)blockIdx.x && kb < npre;   // stage == kb, phase 0, B in flight
+                    if (!pre) {
+                        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                    }
                     tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], (kb0 + kb) * Cfg::BK, mb * Cfg::BM);
-                    tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], (kb0 + kb) * Cfg::BK, nb * BN);
+                    if (!pre)
+                        tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], (kb0 + kb) * Cfg::BK, nb * BN);
                     last_par[stage] = static_cast<int>(phase);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }

@@ -137,6 +137,8 @@ void launch_e4m3_selftest(const float *x, uint8_t *y, int n, cudaStream_t s) {
 
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
                                                        const float *__restrict__ w) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -160,8 +162,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__
     }
 }
 
-void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s) {
-    rms_norm_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, w);
+void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), rms_norm_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, w);
 }
 
 // =========================================================================
@@ -252,11 +254,19 @@ DTTS_DEV void attn_store(const AttnArgs &a, int r, int h, int qi0, int qi1, int 
     }
 }
 
-__global__ void advance_len_kernel(int *len, int add) { *len += add; }
+__global__ void advance_len_kernel(int *len, int add) {
+    pdl_wait();
+    pdl_trigger();
+    *len += add;
+}
 
-void launch_advance_len(int *len, int add, cudaStream_t s) { advance_len_kernel<<<1, 1, 0, s>>>(len, add); }
+void launch_advance_len(int *len, int add, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), advance_len_kernel, dim3(1), dim3(1), 0, s, len, add);
+}
 
 __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
     if (a.kv_base_dev) {   // graph-captured decode: positions from device memory
         a.q_pos0 = *a.kv_base_dev;
         a.kv_len = a.q_pos0 + a.Tq;
@@ -399,6 +409,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnArgs a) {
 // pair's Q, K and V tiles with cp.async while it computes the current one; one
 // key block, so the softmax is exact in one pass (exp2 of pre-scaled scores).
 __global__ void __launch_bounds__(128, 5) attn_short_kernel(AttnArgs a, int n_pairs, int per_cta) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(128) uint8_t attn_smem[];
     bf16 *sm = reinterpret_cast<bf16 *>(attn_smem);   // [2 buffers][Q, K, V][64 * 64]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -531,85 +543,132 @@ cudaError_t attention_short_prepare() {
 }
 
 // Decode attention (a few queries per sequence against a long cache, causal,
-// no mask): one CTA of 4 warps per (row, query, head); each warp takes every
-// fourth block of 16 keys, loading their K and V rows together and reducing
-// their 16 dot products together (lane l owns dims 2l, 2l+1 of the 64); the
-// warps' online-softmax states are merged through shared memory.
+// no mask): one CTA of 4 warps per (row, query, head).  A warp reads 16 keys
+// per round as four groups of four: lane l takes dims 8(l%8)..8(l%8)+7 of key
+// 4u + l/8, so each 16-byte load instruction reads four whole 128-byte K (or V)
+// rows and a score needs a 3-step shuffle reduction over 8 lanes.  Each group
+// of 8 lanes accumulates its own keys' P.V over its 8 dims; the groups, then
+// the warps (online-softmax states through shared memory), are merged at the
+// end.  Scores are pre-scaled by log2(e) and exponentiated with exp2.
 constexpr int kDecWarps = 4, kDecKeys = 16;
 
 __global__ void __launch_bounds__(kDecWarps * 32, 8) attn_decode_kernel(const AttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int q_pos0 = a.kv_base_dev ? *a.kv_base_dev : a.q_pos0;
     const int kv_len = a.kv_base_dev ? q_pos0 + a.Tq : a.kv_len;
     const int h = blockIdx.x % kH, qi = (blockIdx.x / kH) % a.Tq, r = blockIdx.x / (kH * a.Tq);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 3, c = lane & 7;
     const int n_keys = a.causal ? min(kv_len, q_pos0 + qi + 1) : kv_len;
-    const float sc = a.scale;
-    const bf16 *qg = reinterpret_cast<const bf16 *>(a.q) + ((long long)r * a.Tq + qi) * a.ldq + h * kHD;
-    const float2 qv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162 *>(qg)[lane]);
-    const bf16 *kg = reinterpret_cast<const bf16 *>(a.k) + (long long)r * a.kv_cap * a.ldkv + h * kHD + 2 * lane;
-    const bf16 *vg = reinterpret_cast<const bf16 *>(a.v) + (long long)r * a.kv_cap * a.ldkv + h * kHD + 2 * lane;
-    float mx = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+    const float sc = a.scale * 1.4426950408889634f;
+    const bf16 *qg = reinterpret_cast<const bf16 *>(a.q) + ((long long)r * a.Tq + qi) * a.ldq + h * kHD + 8 * c;
+    float qv[8];
+    {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(qg);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+            qv[2 * i] = f.x * sc; qv[2 * i + 1] = f.y * sc;
+        }
+    }
+    const long long rbase = (long long)r * a.kv_cap * a.ldkv + h * kHD + 8 * c;
+    const bf16 *kg = reinterpret_cast<const bf16 *>(a.k) + rbase;
+    const bf16 *vg = reinterpret_cast<const bf16 *>(a.v) + rbase;
+    float mx = -INFINITY, l = 0.f, acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.f;
     for (int j0 = warp * kDecKeys; j0 < n_keys; j0 += kDecWarps * kDecKeys) {
-        uint32_t kr[kDecKeys], vr[kDecKeys];
+        uint4 kr[4], vr[4];
 #pragma unroll
-        for (int u = 0; u < kDecKeys; u++) {
-            const int j = min(j0 + u, n_keys - 1);   // past the end: a valid row, masked below
-            kr[u] = *reinterpret_cast<const uint32_t *>(kg + (long long)j * a.ldkv);
-            vr[u] = *reinterpret_cast<const uint32_t *>(vg + (long long)j * a.ldkv);
+        for (int u = 0; u < 4; u++) {
+            const int j = min(j0 + 4 * u + g, n_keys - 1);   // past the end: a valid row, masked below
+            kr[u] = *reinterpret_cast<const uint4 *>(kg + (long long)j * a.ldkv);
+            vr[u] = *reinterpret_cast<const uint4 *>(vg + (long long)j * a.ldkv);
         }
-        float s[kDecKeys];
+        float s[4];
 #pragma unroll
-        for (int u = 0; u < kDecKeys; u++) {
-            const float2 kk = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[u]));
-            s[u] = qv.x * kk.x + qv.y * kk.y;
+        for (int u = 0; u < 4; u++) {
+            const uint32_t w[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+            float d = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+                d = fmaf(qv[2 * i], f.x, d);
+                d = fmaf(qv[2 * i + 1], f.y, d);
+            }
+            s[u] = d;
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+        for (int o = 4; o > 0; o >>= 1)
 #pragma unroll
-            for (int u = 0; u < kDecKeys; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
+            for (int u = 0; u < 4; u++) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
         float bm = mx;
 #pragma unroll
-        for (int u = 0; u < kDecKeys; u++) {
-            s[u] = (j0 + u < n_keys) ? s[u] * sc : -INFINITY;
+        for (int u = 0; u < 4; u++) {
+            if (j0 + 4 * u + g >= n_keys) s[u] = -INFINITY;
             bm = fmaxf(bm, s[u]);
         }
-        const float corr = expf(mx - bm);
-        o0 *= corr; o1 *= corr; l *= corr;
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+        const float corr = exp2f(mx - bm);
+        l *= corr;
 #pragma unroll
-        for (int u = 0; u < kDecKeys; u++) {
-            const float e = expf(s[u] - bm);
-            const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr[u]));
-            o0 += e * vv.x; o1 += e * vv.y; l += e;
+        for (int i = 0; i < 8; i++) acc[i] *= corr;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float p = exp2f(s[u] - bm);
+            l += p;
+            const uint32_t w[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+                acc[2 * i] = fmaf(p, f.x, acc[2 * i]);
+                acc[2 * i + 1] = fmaf(p, f.y, acc[2 * i + 1]);
+            }
         }
         mx = bm;
     }
+    // merge the four key groups (lanes c, c + 8, c + 16, c + 24)
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+        l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    }
     __shared__ float sm_m[kDecWarps], sm_l[kDecWarps];
-    __shared__ float2 sm_o[kDecWarps][32];
+    __shared__ float4 sm_o[kDecWarps][16];
     if (lane == 0) { sm_m[warp] = mx; sm_l[warp] = l; }
-    sm_o[warp][lane] = make_float2(o0, o1);
+    if (g == 0) {
+        sm_o[warp][2 * c] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        sm_o[warp][2 * c + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 0 && lane < 16) {
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kDecWarps; w++) M = fmaxf(M, sm_m[w]);
-        float L = 0.f, x = 0.f, y = 0.f;
+        float L = 0.f;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int w = 0; w < kDecWarps; w++) {
             if (sm_m[w] == -INFINITY) continue;   // a warp that saw no key
-            const float f = expf(sm_m[w] - M);
+            const float f = exp2f(sm_m[w] - M);
+            const float4 o = sm_o[w][lane];
             L += sm_l[w] * f;
-            x += sm_o[w][lane].x * f;
-            y += sm_o[w][lane].y * f;
+            x.x += o.x * f; x.y += o.y * f; x.z += o.z * f; x.w += o.w * f;
         }
         const float inv = L > 0.f ? 1.0f / L : 0.f;
         bf16 *og = reinterpret_cast<bf16 *>(a.o) + ((long long)r * a.Tq + qi) * a.ldo + h * kHD;
-        reinterpret_cast<uint32_t *>(og)[lane] = pack_bf16x2(x * inv, y * inv);
+        reinterpret_cast<uint2 *>(og)[lane] = make_uint2(pack_bf16x2(x.x * inv, x.y * inv), pack_bf16x2(x.z * inv, x.w * inv));
     }
 }
 
-void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
+void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl) {
+    pdl = pdl && pdl_enabled();
     if (a.Tq <= 8 && !a.mask && !a.mask_bits && !a.o8 && (a.kv_base_dev || a.kv_len > 64)) {
-        attn_decode_kernel<<<a.rows * a.Tq * kH, kDecWarps * 32, 0, s>>>(a);
+        launch_k(pdl, attn_decode_kernel, dim3(a.rows * a.Tq * kH), dim3(kDecWarps * 32), 0, s, a);
         return;
     }
     if (a.Tq <= 64 && a.kv_len <= 64 && !a.kv_base_dev) {
@@ -621,11 +680,10 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s) {
         const int target = nsm * 5;
         const int per_cta = std::max(1, (n_pairs + target - 1) / target);
         const int grid = (n_pairs + per_cta - 1) / per_cta;
-        attn_short_kernel<<<grid, 128, kShortSmem, s>>>(a, n_pairs, per_cta);
+        launch_k(pdl, attn_short_kernel, dim3(grid), dim3(128), (size_t)kShortSmem, s, a, n_pairs, per_cta);
         return;
     }
-    dim3 grid((a.Tq + 63) / 64, kH, a.rows);
-    attn_bf16_kernel<<<grid, 128, 0, s>>>(a);
+    launch_k(pdl, attn_bf16_kernel, dim3((a.Tq + 63) / 64, kH, a.rows), dim3(128), 0, s, a);
 }
 
 // =========================================================================
@@ -1166,6 +1224,8 @@ __global__ void __launch_bounds__(128) pe_conv_kernel(const float *__restrict__ 
                                                       const float *__restrict__ tail, const float *__restrict__ w,
                                                       const float *__restrict__ bias, bf16 *__restrict__ out,
                                                       float *__restrict__ new_tail) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float f0[kLat], f1[kLat];
     const int T = n_frames / 2;
     const int b = blockIdx.x / T, t = blockIdx.x % T;
@@ -1192,6 +1252,8 @@ void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail,
 }
 
 __global__ void pe_pairs_kernel(const float *__restrict__ h, int T, int pair_mode, bf16 *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int n = T / 2;
     const int bq = blockIdx.x;             // b * n + q
     const int b = bq / n, q = bq % n;
@@ -1208,8 +1270,8 @@ __global__ void pe_pairs_kernel(const float *__restrict__ h, int T, int pair_mod
     }
 }
 
-void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s) {
-    pe_pairs_kernel<<<B * (T / 2), 256, 0, s>>>(h, T, pair_mode, out);
+void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), pe_pairs_kernel, dim3(B * (T / 2)), dim3(256), 0, s, h, T, pair_mode, out);
 }
 
 }  // namespace dtts

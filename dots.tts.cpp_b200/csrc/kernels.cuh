@@ -16,8 +16,11 @@ struct GemmOp {
     int nw;       // epilogue warps: 4 or 8
     int epi;      // EpiKind
     int f8;       // 1: A and B are e4m3 (tensor maps from make_tmap_e4m3)
+    int pdl;      // 1: programmatic launch after the previous kernel (its weight tiles load early)
     EpiParams ep;
 };
+// Programmatic dependent launches on (the default) unless DTTS_PDL=0.
+bool pdl_enabled();
 // A K-major bf16 matrix [rows][cols] seen by TMA as 64-column x box_rows boxes
 // with 128-byte swizzle.
 bool make_tmap_bf16(CUtensorMap *m, const void *base, unsigned long long rows, unsigned long long cols,
@@ -36,7 +39,7 @@ cudaError_t gemm_prepare_attributes();
 void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale,
                         long long ada_ld, int tok_per_row, cudaStream_t s);
 // y = bf16( x / sqrt(mean(x^2) + 1e-6) * w )
-void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s);
+void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s, bool pdl = false);
 
 // ------------------------------------------------------------ attention
 struct AttnArgs {
@@ -65,9 +68,9 @@ struct AttnArgs {
 };
 // Tq <= 64 and kv_len <= 64 take the pipelined short-sequence kernel (call
 // attention_short_prepare() once per device first); longer ones the tiled kernel.
-void launch_attention_bf16(const AttnArgs &a, cudaStream_t s);
+void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl = false);
 // *len += add on the device (KV length of a graph-captured decode step)
-void launch_advance_len(int *len, int add, cudaStream_t s);
+void launch_advance_len(int *len, int add, cudaStream_t s, bool pdl = false);
 cudaError_t attention_short_prepare();
 // Host helper: bit-packs a [Tq][kv_len] uint8 mask into [Tq][ceil(kv_len/32)] words.
 void pack_mask_bits(const uint8_t *mask, int Tq, int kv_len, uint32_t *bits);
@@ -138,6 +141,6 @@ void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_sc
 void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *w, const float *bias,
                     bf16 *out, float *new_tail, cudaStream_t s);
 // out[b*n + p] = bf16([h[b, tok0] | h[b, tok1]]) with the pairing rule
-void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s);
+void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s, bool pdl = false);
 
 }  // namespace dtts

@@ -32,6 +32,8 @@ constexpr int kLQKV = kLH + 2 * kLKV;   // 2048 columns: q | k | v
 template <bool OUT_BF16>
 __global__ void __launch_bounds__(256) llm_rms_norm_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                                            void *__restrict__ out, int M) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= M) return;
     const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kLH);
@@ -58,33 +60,45 @@ __global__ void __launch_bounds__(256) llm_rms_norm_kernel(const float *__restri
 
 // RoPE on q (12 heads) and k (2 heads) of token m = b * T + t at position
 // pos0 + t, q to qout (fp32), k and v appended to the caches
-// [b][kv head][cap][128] (bf16).  One block per token, 128 threads: thread
-// d < 64 rotates pair (d, d + 64) of every head.
-// pos_dev, if set, holds pos0 on the device (graph-captured steps).
-__global__ void __launch_bounds__(128) llm_rope_cache_kernel(const float *__restrict__ qkv, int T, int pos0,
+// [b][kv head][cap][128] (bf16).  One block of 256 threads per token; work
+// item i < 14 * 64 rotates pair (d, d + 64), d = i % 64, of q/k head i / 64,
+// and the 256 v values follow.  pos_dev, if set, holds pos0 on the device
+// (graph-captured steps); zero: each qkv value is cleared by the thread that
+// read it (the next split-K reduce-add target).
+__global__ void __launch_bounds__(256) llm_rope_cache_kernel(float *__restrict__ qkv, int T, int pos0,
                                                               const int *__restrict__ pos_dev,
                                                               const float2 *__restrict__ rope, float *__restrict__ qout,
-                                                              bf16 *__restrict__ kc, bf16 *__restrict__ vc, int cap) {
+                                                              bf16 *__restrict__ kc, bf16 *__restrict__ vc, int cap,
+                                                              int zero) {
+    pdl_wait();
+    pdl_trigger();
     if (pos_dev) pos0 = *pos_dev;
     const int m = blockIdx.x, b = m / T, t = m % T, p = pos0 + t;
-    const float *row = qkv + (long long)m * kLQKV;
-    const int d = threadIdx.x;
-    if (d < 64) {
-        const float2 cs = rope[(long long)p * 64 + d];
-        for (int h = 0; h < kLNH; h++) {
-            const float x0 = row[h * kLHD + d], x1 = row[h * kLHD + d + 64];
-            qout[(long long)m * kLH + h * kLHD + d] = x0 * cs.x - x1 * cs.y;
-            qout[(long long)m * kLH + h * kLHD + d + 64] = x1 * cs.x + x0 * cs.y;
-        }
-        for (int h = 0; h < kLNKV; h++) {
-            const float x0 = row[kLH + h * kLHD + d], x1 = row[kLH + h * kLHD + d + 64];
-            bf16 *dst = kc + (((long long)b * kLNKV + h) * cap + p) * kLHD;
-            dst[d] = __float2bfloat16_rn(x0 * cs.x - x1 * cs.y);
-            dst[d + 64] = __float2bfloat16_rn(x1 * cs.x + x0 * cs.y);
+    float *row = qkv + (long long)m * kLQKV;
+    constexpr int kRot = (kLNH + kLNKV) * 64;
+    for (int i = threadIdx.x; i < kRot + kLKV; i += blockDim.x) {
+        if (i < kRot) {
+            const int hh = i >> 6, d = i & 63;
+            const int c = hh * kLHD + d;   // q heads, then k heads (columns 1536..1791)
+            const float2 cs = rope[(long long)p * 64 + d];
+            const float x0 = row[c], x1 = row[c + 64];
+            if (zero) row[c] = row[c + 64] = 0.f;
+            const float y0 = x0 * cs.x - x1 * cs.y, y1 = x1 * cs.x + x0 * cs.y;
+            if (hh < kLNH) {
+                qout[(long long)m * kLH + c] = y0;
+                qout[(long long)m * kLH + c + 64] = y1;
+            } else {
+                bf16 *dst = kc + (((long long)b * kLNKV + (hh - kLNH)) * cap + p) * kLHD;
+                dst[d] = __float2bfloat16_rn(y0);
+                dst[d + 64] = __float2bfloat16_rn(y1);
+            }
+        } else {
+            const int j = i - kRot, hv = j >> 7, d = j & 127;
+            const float x = row[kLH + kLKV + j];
+            if (zero) row[kLH + kLKV + j] = 0.f;
+            vc[(((long long)b * kLNKV + hv) * cap + p) * kLHD + d] = __float2bfloat16_rn(x);
         }
     }
-    for (int h = 0; h < kLNKV; h++)
-        vc[(((long long)b * kLNKV + h) * cap + p) * kLHD + d] = __float2bfloat16_rn(row[kLH + kLKV + h * kLHD + d]);
 }
 
 // Grouped-query causal attention, one warp per (token m, query head): lane
@@ -96,6 +110,8 @@ __global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__
                                                        const bf16 *__restrict__ vc, int T, int pos0,
                                                        const int *__restrict__ pos_dev, int cap, int M,
                                                        bf16 *__restrict__ ao) {
+    pdl_wait();
+    pdl_trigger();
     if (pos_dev) pos0 = *pos_dev;
     const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wid >= M * kLNH) return;
@@ -153,13 +169,21 @@ __global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__
 }
 
 // out[m][j] = gate / (1 + e^-gate) * up with gu[m] = gate[8960] | up[8960]
-// (src/llm_manual.cpp:333-334, :468).
-__global__ void llm_swiglu_kernel(const float *__restrict__ gu, bf16 *__restrict__ out, long long n) {
+// (src/llm_manual.cpp:333-334, :468), four columns per thread; zero: gu is
+// cleared behind the read.
+__global__ void llm_swiglu_kernel(float *__restrict__ gu, bf16 *__restrict__ out, long long n4, int zero) {
+    pdl_wait();
+    pdl_trigger();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const long long m = i / kLF, j = i % kLF;
-    const float g = gu[m * 2 * kLF + j], u = gu[m * 2 * kLF + kLF + j];
-    out[i] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+    if (i >= n4) return;
+    const long long m = i / (kLF / 4), j4 = i % (kLF / 4);
+    float4 *g4 = reinterpret_cast<float4 *>(gu + m * 2 * kLF) + j4;
+    float4 *u4 = reinterpret_cast<float4 *>(gu + m * 2 * kLF + kLF) + j4;
+    const float4 g = *g4, u = *u4;
+    if (zero) *g4 = *u4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    reinterpret_cast<uint2 *>(out)[i] =
+        make_uint2(pack_bf16x2(g.x / (1.0f + expf(-g.x)) * u.x, g.y / (1.0f + expf(-g.y)) * u.y),
+                   pack_bf16x2(g.z / (1.0f + expf(-g.z)) * u.z, g.w / (1.0f + expf(-g.w)) * u.w));
 }
 
 int up_f32(DeviceArena &a, const float *h, size_t n, float **out) {
@@ -255,6 +279,7 @@ struct dtts_llm {
         std::memset(&o, 0, sizeof(o));
         o.ta = ta; o.tb = tb; o.M = M; o.N = N; o.K = K; o.bn = bn; o.nw = 4; o.epi = epi;
         o.ep.err = d_err; o.ep.tok_per_row = 1; o.ep.ksplit = 1;
+        o.pdl = 1;   // every GEMM follows another kernel
         return o;
     }
 
@@ -266,13 +291,20 @@ struct dtts_llm {
         const bool small = M <= 256;
         const int bn = small ? 128 : 256;
         const size_t layer_stride = (size_t)max_batch * kLNKV * max_seq * kLHD;
+        // few rows: the QKV and gate|up GEMMs split K so that about 128 CTAs
+        // stream the weights, partial sums reduce-added into fp32 rows that are
+        // zeroed here once and then by their readers behind each read
+        if (small) {
+            DTTS_CUDA(cudaMemsetAsync(qkv, 0, (size_t)M * kLQKV * 4, stream));
+            DTTS_CUDA(cudaMemsetAsync(gu, 0, (size_t)M * 2 * kLF * 4, stream));
+        }
+        // every kernel but the first starts programmatically behind the one before it
+        const bool pdl = pdl_enabled();
         for (int l = 0; l < n_layers; l++) {
             const Layer &L = layers[l];
-            llm_rms_norm_kernel<true><<<(M + 7) / 8, 256, 0, stream>>>(h, L.an, act, M);
+            launch_k(pdl && l > 0, llm_rms_norm_kernel<true>, dim3((M + 7) / 8), dim3(256), 0, stream,
+                     (const float *)h, (const float *)L.an, (void *)act, M);
             if (small) {
-                // few rows: split K 8 ways so that 128 CTAs stream the weights,
-                // partial sums reduce-added into the zeroed fp32 output
-                DTTS_CUDA(cudaMemsetAsync(qkv, 0, (size_t)M * kLQKV * 4, stream));
                 GemmOp o = op(t_act, L.tqkv_s, M, kLQKV, kLH, EPI_RESID, bn);
                 o.tr = t_qkv_r; o.ep.bias = L.bqkv; o.ep.resid = qkv; o.ep.ldr = kLQKV; o.ep.ksplit = 8;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
@@ -281,19 +313,20 @@ struct dtts_llm {
                 o.ep.bias = L.bqkv; o.ep.out = qkv; o.ep.ldo = kLQKV;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
-            llm_rope_cache_kernel<<<M, 128, 0, stream>>>(qkv, T, pos0, pd, rope, q, kc + l * layer_stride,
-                                                         vc + l * layer_stride, max_seq);
-            llm_attn_kernel<<<(M * kLNH + 7) / 8, 256, 0, stream>>>(q, kc + l * layer_stride, vc + l * layer_stride, T,
-                                                                    pos0, pd, max_seq, M, ao);
+            launch_k(pdl, llm_rope_cache_kernel, dim3(M), dim3(256), 0, stream, qkv, T, pos0, pd, (const float2 *)rope,
+                     q, kc + l * layer_stride, vc + l * layer_stride, max_seq, small ? 1 : 0);
+            launch_k(pdl, llm_attn_kernel, dim3((M * kLNH + 7) / 8), dim3(256), 0, stream, (const float *)q,
+                     (const bf16 *)(kc + l * layer_stride), (const bf16 *)(vc + l * layer_stride), T, pos0, pd,
+                     max_seq, M, ao);
             {
                 GemmOp o = op(t_ao, small ? L.to_s : L.to, M, kLH, kLH, EPI_RESID, bn);
                 o.tr = t_h; o.ep.bias = L.bo; o.ep.resid = h; o.ep.ldr = kLH;
                 o.ep.ksplit = small ? 8 : 1;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
-            llm_rms_norm_kernel<true><<<(M + 7) / 8, 256, 0, stream>>>(h, L.fn, act, M);
+            launch_k(pdl, llm_rms_norm_kernel<true>, dim3((M + 7) / 8), dim3(256), 0, stream, (const float *)h,
+                     (const float *)L.fn, (void *)act, M);
             if (small) {
-                DTTS_CUDA(cudaMemsetAsync(gu, 0, (size_t)M * 2 * kLF * 4, stream));
                 GemmOp o = op(t_act, L.tgu_s, M, 2 * kLF, kLH, EPI_RESID, bn);
                 o.tr = t_gu_r; o.ep.resid = gu; o.ep.ldr = 2 * kLF; o.ep.ksplit = 2;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
@@ -302,8 +335,9 @@ struct dtts_llm {
                 o.ep.out = gu; o.ep.ldo = 2 * kLF;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
-            const long long nf = (long long)M * kLF;
-            llm_swiglu_kernel<<<(unsigned)((nf + 255) / 256), 256, 0, stream>>>(gu, ffn, nf);
+            const long long nf4 = (long long)M * kLF / 4;
+            launch_k(pdl, llm_swiglu_kernel, dim3((unsigned)((nf4 + 255) / 256)), dim3(256), 0, stream, gu, ffn, nf4,
+                     small ? 1 : 0);
             {
                 GemmOp o = op(t_ffn, small ? L.td_s : L.td, M, kLH, kLF, EPI_RESID, bn);
                 o.tr = t_h; o.ep.resid = h; o.ep.ldr = kLH;
@@ -311,8 +345,9 @@ struct dtts_llm {
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
         }
-        llm_rms_norm_kernel<false><<<(M + 7) / 8, 256, 0, stream>>>(h, final_norm, out, M);
-        launch_advance_len(d_len, T, stream);
+        launch_k(pdl, llm_rms_norm_kernel<false>, dim3((M + 7) / 8), dim3(256), 0, stream, (const float *)h,
+                 (const float *)final_norm, (void *)out, M);
+        launch_advance_len(d_len, T, stream, true);
         DTTS_CUDA(cudaGetLastError());
         return DTTS_OK;
     }

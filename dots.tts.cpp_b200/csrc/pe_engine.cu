@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(256) pe_qkv_finish_kernel(float *__restrict__ 
                                                             const int *__restrict__ start_dev,
                                                             const float2 *__restrict__ rope, bf16 *__restrict__ q,
                                                             bf16 *__restrict__ kc, bf16 *__restrict__ vc, int cap) {
+    pdl_wait();
+    pdl_trigger();
     if (start_dev) start = *start_dev;
     const int m = blockIdx.x, b = m / T, t = m % T, p = start + t;
     float2 *row = reinterpret_cast<float2 *>(qkv + (long long)m * 3 * kD);
@@ -58,6 +60,8 @@ __global__ void __launch_bounds__(256) pe_qkv_finish_kernel(float *__restrict__ 
 
 // ffn = bf16(silu(x)) over n4 groups of four, x zeroed behind the read
 __global__ void pe_silu_kernel(float *__restrict__ x, bf16 *__restrict__ ffn, long long n4) {
+    pdl_wait();
+    pdl_trigger();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     float4 v = reinterpret_cast<float4 *>(x)[i];
@@ -174,8 +178,10 @@ struct dtts_pe {
         return DTTS_OK;
     }
 
-    int gemm(const GemmOp &op) {
+    // every GEMM of a call follows another kernel: programmatic launch
+    int gemm(GemmOp op) {
         launches++;
+        op.pdl = 1;
         DTTS_CUDA(launch_gemm(op, num_sms, stream));
         return DTTS_OK;
     }
@@ -188,7 +194,7 @@ struct dtts_pe {
         const int bn = small ? kBNs : kBN;
         launches++;
         launch_pe_conv(frames, B, n_frames, tail[0], conv_w, conv_b, conv, tail[1], stream);
-        DTTS_CUDA(cudaMemcpyAsync(tail[0], tail[1], (size_t)B * kLat * 4, cudaMemcpyDeviceToDevice, stream));
+        // every kernel after the conv starts programmatically behind the one before it
         int st;
         {
             GemmOp op = op0(t_conv, small ? t_inw_s : t_inw, M, kD, kLat, EPI_F32, d_err);
@@ -200,15 +206,16 @@ struct dtts_pe {
         for (int l = 0; l < n_layers; l++) {
             const Layer &Ly = layers[l];
             launches++;
-            launch_rms_norm(h, act, M, Ly.an, stream);
+            launch_rms_norm(h, act, M, Ly.an, stream, true);
             if (small) {
                 GemmOp op = op0(t_act, Ly.tqkv_s, M, 3 * kD, kD, EPI_RESID, d_err);
                 op.bn = bn; op.tr = t_qkv32;
                 op.ep.resid = qkv32; op.ep.ldr = 3 * kD; op.ep.ksplit = kKsQKV;
                 if ((st = gemm(op))) return st;
                 launches++;
-                pe_qkv_finish_kernel<<<M, 256, 0, stream>>>(qkv32, T, cur_len, dev_pos ? d_len : nullptr, rope, q,
-                                                            kc + l * layer_stride, vc + l * layer_stride, max_tokens);
+                launch_k(pdl_enabled(), pe_qkv_finish_kernel, dim3(M), dim3(256), 0, stream, qkv32, T, cur_len,
+                         (const int *)(dev_pos ? d_len : nullptr), (const float2 *)rope, q, kc + l * layer_stride,
+                         vc + l * layer_stride, max_tokens);
             } else {
                 GemmOp op = op0(t_act, Ly.tqkv, M, 3 * kD, kD, EPI_QKV, d_err);
                 op.bn = bn;
@@ -226,7 +233,7 @@ struct dtts_pe {
                 a.q_pos0 = cur_len; a.causal = 1; a.mask = nullptr; a.scale = 1.0f / sqrtf(64.0f);
                 a.kv_base_dev = dev_pos ? d_len : nullptr;
                 launches++;
-                launch_attention_bf16(a, stream);
+                launch_attention_bf16(a, stream, true);
             }
             {
                 GemmOp op = op0(t_att, small ? Ly.to_s : Ly.to, M, kD, kD, EPI_RESID, d_err);
@@ -237,7 +244,7 @@ struct dtts_pe {
                 if ((st = gemm(op))) return st;
             }
             launches++;
-            launch_rms_norm(h, act, M, Ly.fn, stream);
+            launch_rms_norm(h, act, M, Ly.fn, stream, true);
             if (small) {
                 GemmOp op = op0(t_act, Ly.t1_s, M, kF, kD, EPI_RESID, d_err);
                 op.bn = bn; op.tr = t_ffn32;
@@ -245,7 +252,8 @@ struct dtts_pe {
                 if ((st = gemm(op))) return st;
                 launches++;
                 const long long n4 = (long long)M * kF / 4;
-                pe_silu_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(ffn32, ffn, n4);
+                launch_k(pdl_enabled(), pe_silu_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, stream,
+                         ffn32, ffn, n4);
             } else {
                 GemmOp op = op0(t_act, Ly.t1, M, kF, kD, EPI_SILU_BF16, d_err);
                 op.ep.bias = Ly.b1; op.ep.out = ffn; op.ep.ldo = kF;
@@ -261,7 +269,7 @@ struct dtts_pe {
             }
         }
         launches++;
-        launch_pe_pairs(h, B, T, pair_mode, pairs, stream);
+        launch_pe_pairs(h, B, T, pair_mode, pairs, stream, true);
         {
             GemmOp op = op0(t_pairs, small ? t_outw_s : t_outw, B * n_out, kLLM, 2 * kD, EPI_F32, d_err);
             op.bn = bn;
@@ -269,7 +277,8 @@ struct dtts_pe {
             if ((st = gemm(op))) return st;
         }
         launches++;
-        launch_advance_len(d_len, T, stream);
+        launch_advance_len(d_len, T, stream, true);
+        DTTS_CUDA(cudaMemcpyAsync(tail[0], tail[1], (size_t)B * kLat * 4, cudaMemcpyDeviceToDevice, stream));
         DTTS_CUDA(cudaGetLastError());
         return DTTS_OK;
     }
