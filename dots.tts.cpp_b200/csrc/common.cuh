@@ -20,6 +20,7 @@ enum DeviceError : int {
     DEVERR_TIMEOUT_MMA = 2,
     DEVERR_TIMEOUT_EPILOGUE = 3,
     DEVERR_NONFINITE = 4,
+    DEVERR_TIMEOUT_BARRIER = 5,   // a grid barrier between CTAs of one kernel
 };
 
 // Every spin on an mbarrier gives up after this long (globaltimer ns).

@@ -105,6 +105,7 @@ cudaError_t prepare_bn() {
 // current device (attributes are per device; called when an engine is created).
 cudaError_t gemm_prepare_attributes() {
     cudaError_t e;
+    if ((e = prepare_bn<64, 4>()) != cudaSuccess) return e;
     if ((e = prepare_bn<128, 4>()) != cudaSuccess) return e;
     if ((e = prepare_bn<192, 4>()) != cudaSuccess) return e;
     if ((e = prepare_bn<256, 4>()) != cudaSuccess) return e;
@@ -184,6 +185,7 @@ cudaError_t launch_gemm(const GemmOp &op, int num_sms, cudaStream_t s) {
     }
     if (op.epi == EPI_GELU_F8) return cudaErrorInvalidValue;
     switch (op.bn * 16 + nw) {
+        case 64 * 16 + 4: return dispatch_epi<64, 4>(op, num_sms, s);
         case 128 * 16 + 4: return dispatch_epi<128, 4>(op, num_sms, s);
         case 192 * 16 + 4: return dispatch_epi<192, 4>(op, num_sms, s);
         case 256 * 16 + 4: return dispatch_epi<256, 4>(op, num_sms, s);

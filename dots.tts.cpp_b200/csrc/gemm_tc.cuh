@@ -72,6 +72,12 @@ struct EpiParams {
     const float *row_scale;   // [M]
     const float *col_scale;   // [N]
     const float *out_inv;     // EPI_GELU_F8: per-row factor applied before the e4m3 conversion
+    // Convolution as a GEMM over taps (tap_kb > 0): K is taps x channels, tap-major,
+    // tap_kb k-blocks per tap.  K-block kb of tap j = kb / tap_kb reads A at
+    // column (kb mod tap_kb) * BK and row m + tap_base + j * tap_step; rows
+    // outside [0, M) read as zero (TMA fill), which is the zero padding of a
+    // causal (or centred) time convolution over A = [time][channels].
+    int tap_kb, tap_base, tap_step;
 };
 
 __host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || epi == EPI_RESID_GATED; }
@@ -306,7 +312,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                 const int nb = tile / num_m, kb0 = split * kblocks;
                 npre = kblocks < STAGES ? kblocks : STAGES;
                 for (int kb = 0; kb < npre; kb++) {
-                    mbar_arrive_expect_tx(&full[kb], Cfg::STAGE_BYTES);
+                    mbar_arrive_expect_tx(&full[kb], Cfg::STAGE_BYTES);   // B now, A after the wait
                     tma_load_2d(sB + kb * Cfg::B_BYTES, &tmB, &full[kb], (kb0 + kb) * Cfg::BK, nb * BN);
                     last_par[kb] = 0;
                 }
@@ -324,7 +330,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.err, DEVERR_TIMEOUT_PRODUCER)) { ok = false; break; }
                         mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
                     }
-                    tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], (kb0 + kb) * Cfg::BK, mb * Cfg::BM);
+                    int ax = (kb0 + kb) * Cfg::BK, ay = mb * Cfg::BM;
+                    if (ep.tap_kb > 0) {
+                        const int tap = (kb0 + kb) / ep.tap_kb;
+                        ax = (kb0 + kb - tap * ep.tap_kb) * Cfg::BK;
+                        ay += ep.tap_base + tap * ep.tap_step;
+                    }
+                    tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], ax, ay);
                     if (!pre)
                         tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], (kb0 + kb) * Cfg::BK, nb * BN);
                     last_par[stage] = static_cast<int>(phase);

@@ -12,7 +12,7 @@ struct GemmOp {
     CUtensorMap ta, tb;
     CUtensorMap tr;   // residual (EPI_RESID*), from make_tmap_f32_resid
     int M, N, K;
-    int bn;       // 128, 192 or 256
+    int bn;       // 128, 192 or 256 (64 with 4 epilogue warps)
     int nw;       // epilogue warps: 4 or 8
     int epi;      // EpiKind
     int f8;       // 1: A and B are e4m3 (tensor maps from make_tmap_e4m3)

@@ -1,0 +1,676 @@
+// BigVGAN v2 decoder (src/modules/vocoder/bigvgan_cpp.cpp:325-542 and
+// lstm.cpp of the reference) on sm_100a.
+//
+// Layout: every activation is time-major [time][channels], channels padded to
+// a multiple of 64 (at least 64) with zeros that stay zero: padded weights
+// and biases are zero and SnakeBeta(0) = 0.
+//   bottleneck   post_proj, Linear 128->512, 4 x LSTM(512) with skip,
+//                Linear 512->128: fp32 SIMT GEMMs + one cooperative kernel
+//                per LSTM layer (a grid barrier per time step)
+//   conv_pre     K = 5, centred: tcgen05 GEMM over taps (bf16 out)
+//   6 stages     causal ConvTranspose1d (K = 2 stride) as `stride` GEMMs, one
+//                per output phase r: out[q s + r] = W_r . [x[q] | x[q-1]],
+//                written with row stride s; then three AMP blocks, each
+//                r += c2(act(c1(act(r)))) x 3 with dilations 1, 3, 5:
+//                act = Activation1d (fp32 in, bf16 out), c1 a GEMM over taps
+//                (fp32 out + bias), c2 a GEMM over taps reduce-added into the
+//                fp32 residual r (+ bias); the stage output is the mean of
+//                the three blocks
+//   post         Activation1d with per-channel filters, conv_post (K = 7,
+//                causal, no bias), tanh x 1.92
+// The convolution GEMMs read A = activations through a 2-D tensor map whose
+// rows outside [0, T) are TMA zero fill, shifted per tap (EpiParams::tap_*),
+// so causal padding costs nothing.
+#include "kernels.cuh"
+#include "runtime.h"
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+using namespace dtts;
+
+namespace {
+constexpr int kStages = 6, kRb = 18, kTaps = 12;
+constexpr int kUpIn[kStages] = {1536, 768, 384, 192, 96, 48};
+constexpr int kUpOut[kStages] = {768, 384, 192, 96, 48, 24};
+constexpr int kUpStride[kStages] = {10, 6, 4, 2, 2, 2};
+constexpr int kRbK[3] = {3, 7, 11};
+constexpr int kRbDil[3] = {1, 3, 5};
+constexpr int kHop = 1920;
+constexpr int kLstmH = 512, kLstmCtas = 64, kLstmUnits = kLstmH / kLstmCtas;   // 8 units per CTA
+
+inline int cpad(int c) { return c <= 64 ? 64 : (c + 63) / 64 * 64; }
+
+// ------------------------------------------------------------------ filter
+// BigVGAN's kaiser_sinc_filter1d (the alias-free activation's low-pass
+// filter): Kaiser window with beta from the attenuation
+// A = 2.285 (K/2 - 1) pi (4 half_width) + 7.95, sinc sampled at half-integer
+// times for even K, taps normalised to sum 1.  The reference hard-codes the
+// K = 12, cutoff 0.25, half width 0.3 result (bigvgan_cpp.cpp:27-31).
+constexpr double kPi = 3.14159265358979323846;
+
+double bessel_i0(double x) {
+    double term = 1.0, sum = 1.0;
+    for (int k = 1; k < 200; k++) {
+        term *= (x / (2.0 * k)) * (x / (2.0 * k));
+        sum += term;
+        if (term < 1e-17 * sum) break;
+    }
+    return sum;
+}
+
+void kaiser_sinc(float *f, double cutoff, double half_width, int K) {
+    const int half = K / 2;
+    const double A = 2.285 * (half - 1) * kPi * (4.0 * half_width) + 7.95;
+    const double beta = A > 50.0 ? 0.1102 * (A - 8.7) : A >= 21.0 ? 0.5842 * pow(A - 21.0, 0.4) + 0.07886 * (A - 21.0) : 0.0;
+    std::vector<double> v(K);
+    double sum = 0.0;
+    for (int n = 0; n < K; n++) {
+        const double r = 2.0 * n / (K - 1) - 1.0;
+        const double win = bessel_i0(beta * sqrt(std::max(0.0, 1.0 - r * r))) / bessel_i0(beta);
+        const double t = (K % 2 == 0) ? (n - half + 0.5) : (n - half);
+        const double x = 2.0 * cutoff * t;
+        const double sinc = x == 0.0 ? 1.0 : sin(kPi * x) / (kPi * x);
+        v[n] = 2.0 * cutoff * win * sinc;
+        sum += v[n];
+    }
+    for (int n = 0; n < K; n++) f[n] = (float)(v[n] / sum);
+}
+
+// ------------------------------------------------------------------ kernels
+// Activation1d (bigvgan_cpp.cpp:33-124) on a tile of 64 output times x 32
+// channels: x rows t0-11 .. t0+63 staged in shared memory; then
+//   u[j] = 2 sum_{k = j mod 2, k + 2, .., k <= min(j, 11)} fu[k] x[(j - k) / 2]
+//   s[j] = u + sin^2(a u) * inv_b   (0 for a non-finite u, u for a non-finite s)
+// for j in [2 t0 - 11, 2 t0 + 127] (j < 0 repeats s[0]: the replicate pad),
+// then out[t] = sum_k fd[k] s[2t + k - 11].  Channels >= ch are written as 0.
+constexpr int kActT = 64, kActC = 32;
+struct ActArgs {
+    const float *x; int ldx;
+    void *y; int ldy; int y_bf16;
+    int T, ch;
+    const float *a, *inv_b;          // [ch]: e^clamp(alpha), 1 / (e^clamp(beta) + 1e-9)
+    const float *fu, *fd; int fch;   // [fch][12]
+};
+
+__device__ __forceinline__ float snake(float u, float a, float ib) {
+    if (isnan(u) || isinf(u)) return 0.f;
+    const float sn = sinf(a * u);
+    const float v = u + ib * sn * sn;
+    return (isnan(v) || isinf(v)) ? u : v;
+}
+
+__global__ void __launch_bounds__(256) voc_act_kernel(const ActArgs p) {
+    __shared__ float xs[kActT + 11][kActC];
+    __shared__ float ss[2 * kActT + 11][kActC];
+    const int c0 = blockIdx.x * kActC, t0 = blockIdx.y * kActT;
+    const int tid = threadIdx.x, cl = tid & 31;
+    const int c = c0 + cl;
+    const bool live = c < p.ch;
+    for (int i = tid; i < (kActT + 11) * kActC; i += 256) {
+        const int r = i / kActC, t = t0 - 11 + r;
+        float v = 0.f;
+        if (t >= 0 && t < p.T && c0 + (i % kActC) < p.ch) v = p.x[(long long)t * p.ldx + c0 + (i % kActC)];
+        xs[r][i % kActC] = v;
+    }
+    __syncthreads();
+    float fu[kTaps], fd[kTaps];
+    const float *fup = p.fu + (p.fch == 1 ? 0 : (long long)(live ? c : 0) * kTaps);
+    const float *fdp = p.fd + (p.fch == 1 ? 0 : (long long)(live ? c : 0) * kTaps);
+#pragma unroll
+    for (int k = 0; k < kTaps; k++) { fu[k] = __ldg(fup + k); fd[k] = __ldg(fdp + k); }
+    const float a = live ? __ldg(p.a + c) : 1.f, ib = live ? __ldg(p.inv_b + c) : 1.f;
+    const int j0 = 2 * t0 - 11;
+    for (int jl = tid >> 5; jl < 2 * kActT + 11; jl += 8) {
+        int j = j0 + jl;
+        if (j < 0) j = 0;   // replicate pad: s[j < 0] = s[0]
+        float u = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTaps; k++) {
+            if ((k & 1) != (j & 1) || k > j) continue;
+            u += xs[(j - k) / 2 - (t0 - 11)][cl] * fu[k] * 2.0f;
+        }
+        ss[jl][cl] = snake(u, a, ib);
+    }
+    __syncthreads();
+    for (int tl = tid >> 5; tl < kActT; tl += 8) {
+        const int t = t0 + tl;
+        if (t >= p.T) break;
+        float o = 0.f;
+#pragma unroll
+        for (int k = 0; k < kTaps; k++) o += ss[2 * tl + k][cl] * fd[k];
+        if (!live) o = 0.f;
+        if (c < p.ldy) {
+            if (p.y_bf16) reinterpret_cast<bf16 *>(p.y)[(long long)t * p.ldy + c] = __float2bfloat16_rn(o);
+            else reinterpret_cast<float *>(p.y)[(long long)t * p.ldy + c] = o;
+        }
+    }
+}
+
+void launch_act(const ActArgs &p, int cp, cudaStream_t s) {
+    dim3 grid((cp + kActC - 1) / kActC, (p.T + kActT - 1) / kActT);
+    voc_act_kernel<<<grid, 256, 0, s>>>(p);
+}
+
+// x = (r0 + r1 + r2) / 3 (bigvgan_cpp.cpp:485-494), as bf16 and optionally fp32
+__global__ void voc_mean3_kernel(const float4 *__restrict__ r0, const float4 *__restrict__ r1,
+                                 const float4 *__restrict__ r2, uint2 *__restrict__ xb, float4 *__restrict__ xf,
+                                 long long n4) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const float4 a = r0[i], b = r1[i], c = r2[i];
+    const float4 m = make_float4((a.x + b.x + c.x) / 3.0f, (a.y + b.y + c.y) / 3.0f, (a.z + b.z + c.z) / 3.0f,
+                                 (a.w + b.w + c.w) / 3.0f);
+    if (xb) xb[i] = make_uint2(pack_bf16x2(m.x, m.y), pack_bf16x2(m.z, m.w));
+    if (xf) xf[i] = m;
+}
+
+// conv_post (Conv1d(24, 1, 7), causal, no bias) and tanh x 1.92
+// (bigvgan_cpp.cpp:509-521): one thread per output sample
+__global__ void voc_post_kernel(const float *__restrict__ x, int ldx, int T, int ch, const float *__restrict__ w,
+                                float *__restrict__ audio) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    float s = 0.f;
+    for (int k = 0; k < 7; k++) {
+        const int ts = t + k - 6;
+        if (ts < 0) continue;
+        const float *xr = x + (long long)ts * ldx;
+        for (int c = 0; c < ch; c++) s += xr[c] * __ldg(w + c * 7 + k);
+    }
+    audio[t] = tanhf(s) * 1.92f;
+}
+
+// One LSTM layer's recurrence (lstm.cpp:12-50): gin [T][2048] holds
+// x W_ih^T + b_ih + b_hh for every step; CTA b owns hidden units 8b .. 8b+7,
+// i.e. W_hh rows g * 512 + 8b + i (gates i, f, g, o), kept in shared memory.
+// Each step reads h[t-1] from L2, writes its 8 units of h[t], then meets the
+// other CTAs at a grid barrier (a counter; bounded wait, error code on expiry).
+// Launched cooperatively so that all CTAs are resident.
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(256) voc_lstm_kernel(const float *__restrict__ gin, const float *__restrict__ w_hh,
+                                                       float *h_out, int T, unsigned *bar, int *err) {
+    extern __shared__ float sm[];
+    float *w = sm;                        // [32][512]
+    float *hs = sm + 32 * kLstmH;         // [512]
+    float *gs = hs + kLstmH;              // [32]
+    __shared__ int abort_flag;
+    const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < 32 * kLstmH; i += 256) {
+        const int r = i / kLstmH, k = i % kLstmH;   // r = gate * 8 + unit
+        w[i] = w_hh[(long long)((r >> 3) * kLstmH + b * kLstmUnits + (r & 7)) * kLstmH + k];
+    }
+    if (tid == 0) abort_flag = 0;
+    float cst = 0.f;
+    for (int t = 0; t < T; t++) {
+        for (int k = tid; k < kLstmH; k += 256) hs[k] = t ? __ldcg(h_out + (long long)(t - 1) * kLstmH + k) : 0.f;
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int r = warp * 4 + q;
+            float acc = 0.f;
+            for (int k = lane; k < kLstmH; k += 32) acc += w[r * kLstmH + k] * hs[k];
+            acc = warp_sum(acc);
+            if (lane == 0) gs[r] = acc;
+        }
+        __syncthreads();
+        if (tid < kLstmUnits) {
+            const int j = b * kLstmUnits + tid;
+            const float *g = gin + (long long)t * 4 * kLstmH;
+            const float gi = g[j] + gs[tid], gf = g[kLstmH + j] + gs[8 + tid];
+            const float gg = g[2 * kLstmH + j] + gs[16 + tid], go = g[3 * kLstmH + j] + gs[24 + tid];
+            const float iv = 1.0f / (1.0f + expf(-gi)), fv = 1.0f / (1.0f + expf(-gf));
+            const float gv = tanhf(gg), ov = 1.0f / (1.0f + expf(-go));
+            cst = fv * cst + iv * gv;
+            h_out[(long long)t * kLstmH + j] = ov * tanhf(cst);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(bar, 1u);
+            const unsigned target = (unsigned)(t + 1) * gridDim.x;
+            const unsigned long long t0 = globaltimer_ns();
+            while (ld_acquire_u32(bar) < target) {
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    atomicExch(err, DEVERR_TIMEOUT_BARRIER);
+                    abort_flag = 1;
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        if (abort_flag) return;
+    }
+}
+
+// ------------------------------------------------------------------ host helpers
+int up_f32(DeviceArena &a, const float *h, size_t n, float **out) {
+    *out = nullptr;
+    void *d = a.alloc(n * 4);
+    DTTS_CHECK(d, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(d, h, n * 4, cudaMemcpyHostToDevice));
+    *out = (float *)d;
+    return DTTS_OK;
+}
+
+// zero-padded copy of a [n] vector to [np]
+int up_f32_pad(DeviceArena &a, const float *h, size_t n, size_t np, float **out) {
+    std::vector<float> v(np, 0.f);
+    if (h) std::memcpy(v.data(), h, n * 4);
+    return up_f32(a, v.data(), np, out);
+}
+
+int up_bf16(DeviceArena &a, const std::vector<float> &v, bf16 **out) {
+    std::vector<uint16_t> tmp(v.size());
+    f32_to_bf16_host(v.data(), tmp.data(), v.size());
+    void *d = a.alloc(tmp.size() * 2);
+    DTTS_CHECK(d, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(d, tmp.data(), tmp.size() * 2, cudaMemcpyHostToDevice));
+    *out = (bf16 *)d;
+    return DTTS_OK;
+}
+
+// Activation constants: a = e^clamp(alpha, +-20), inv_b = 1 / (e^clamp(beta, +-20) + 1e-9),
+// in float as the reference evaluates them (bigvgan_cpp.cpp:103-110); padded channels 1, 1.
+void snake_consts(const float *alpha, const float *beta, int ch, int cp, std::vector<float> &a, std::vector<float> &ib) {
+    a.assign(cp, 1.f);
+    ib.assign(cp, 1.f);
+    for (int c = 0; c < ch; c++) {
+        float al = alpha ? alpha[c] : 1.0f, be = beta ? beta[c] : 1.0f;
+        // no alpha/beta tensor: the reference uses 1 and still exponentiates (log scale)
+        al = expf(al > 20.0f ? 20.0f : (al < -20.0f ? -20.0f : al));
+        be = expf(be > 20.0f ? 20.0f : (be < -20.0f ? -20.0f : be));
+        a[c] = al;
+        ib[c] = 1.0f / (be + 1e-9f);
+    }
+}
+
+GemmOp conv_op(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int epi, int bn, int *err) {
+    GemmOp op;
+    std::memset(&op, 0, sizeof(op));
+    op.ta = ta; op.tb = tb; op.M = M; op.N = N; op.K = K; op.bn = bn; op.nw = 4; op.epi = epi;
+    op.ep.err = err; op.ep.tok_per_row = 1; op.ep.ksplit = 1;
+    return op;
+}
+}  // namespace
+
+struct dtts_voc {
+    int device = 0, num_sms = 148, max_frames = 0;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    DeviceArena wts, ws;
+    int *d_err = nullptr;
+    unsigned *d_bar = nullptr;
+    // bottleneck (fp32)
+    float *pp_w = nullptr, *pp_b = nullptr, *mi_w1 = nullptr, *mi_b1 = nullptr, *mi_w2 = nullptr, *mi_b2 = nullptr;
+    float *w_ih[4] = {}, *w_hh[4] = {}, *b_g[4] = {};
+    // convolutions (bf16 B operands [N][taps * cp_in]) and biases (fp32, padded)
+    bf16 *w_pre = nullptr; float *b_pre = nullptr; CUtensorMap t_pre;
+    bf16 *w_up[kStages] = {}; float *b_up[kStages] = {};
+    std::vector<CUtensorMap> t_up[kStages];               // one per output phase
+    bf16 *w_c1[kRb][3] = {}, *w_c2[kRb][3] = {};
+    float *b_c1[kRb][3] = {}, *b_c2[kRb][3] = {};
+    CUtensorMap t_c1[kRb][3], t_c2[kRb][3];
+    float *act_a[kRb][6] = {}, *act_ib[kRb][6] = {};
+    float *aa = nullptr;                                  // [12] AMP filter
+    float *post_a = nullptr, *post_ib = nullptr, *post_fu = nullptr, *post_fd = nullptr, *post_w = nullptr;
+    // workspace
+    float *lat = nullptr, *pp = nullptr, *z = nullptr, *gin = nullptr, *hl[2] = {}, *bott = nullptr, *audio = nullptr;
+    bf16 *bott16 = nullptr, *x0 = nullptr;                // conv_pre in / out
+    float *r[3] = {}, *y = nullptr, *xf = nullptr;        // stage buffers, fp32
+    bf16 *a16 = nullptr, *xin = nullptr;                  // GEMM A operands
+    size_t stage_elems = 0;
+    int maps_T0 = -1;                                     // n_frames the activation maps were encoded for
+    CUtensorMap t_bott, t_x0, t_xin[kStages], t_a[kStages], t_r[kStages][3];
+
+    ~dtts_voc() {
+        ws.free_all();
+        wts.free_all();
+        if (own_stream) cudaStreamDestroy(own_stream);
+    }
+
+    static int bn_for(int n) { return n % 128 == 0 ? 128 : 64; }
+
+    int alloc_ws() {
+        const size_t F = (size_t)max_frames;
+        size_t mx = 0;
+        for (int s = 0; s < kStages; s++) {
+            size_t T = F;
+            for (int q = 0; q <= s; q++) T *= kUpStride[q];
+            mx = std::max(mx, T * (size_t)cpad(kUpOut[s]));
+        }
+        stage_elems = mx;
+        lat = (float *)ws.alloc(F * 128 * 4);
+        pp = (float *)ws.alloc(F * 128 * 4);
+        z = (float *)ws.alloc(F * kLstmH * 4);
+        gin = (float *)ws.alloc(F * 4 * kLstmH * 4);
+        hl[0] = (float *)ws.alloc(F * kLstmH * 4);
+        hl[1] = (float *)ws.alloc(F * kLstmH * 4);
+        bott = (float *)ws.alloc(F * 128 * 4);
+        bott16 = (bf16 *)ws.alloc(F * 128 * 2);
+        x0 = (bf16 *)ws.alloc(F * 1536 * 2);
+        for (int j = 0; j < 3; j++) r[j] = (float *)ws.alloc(mx * 4);
+        y = (float *)ws.alloc(mx * 4);
+        xf = (float *)ws.alloc(mx * 4);
+        a16 = (bf16 *)ws.alloc(mx * 2);
+        xin = (bf16 *)ws.alloc(mx * 2);
+        audio = (float *)ws.alloc(F * kHop * 4);
+        for (void *p : ws.ptrs)
+            DTTS_CHECK(p, DTTS_ERR_OOM, "vocoder workspace allocation failed (%d frames)", max_frames);
+        return DTTS_OK;
+    }
+
+    // tensor maps over the activations for an utterance of T0 frames (rows = exact lengths,
+    // so rows past the end read as zero)
+    int encode_maps(int T0) {
+        if (T0 == maps_T0) return DTTS_OK;
+        bool ok = make_tmap_bf16(&t_bott, bott16, T0, 128, 128) && make_tmap_bf16(&t_x0, x0, T0, 1536, 128);
+        long long Tin = T0;
+        for (int s = 0; s < kStages && ok; s++) {
+            const int cin = s == 0 ? 1536 : cpad(kUpOut[s - 1]), cp = cpad(kUpOut[s]);
+            const long long T = Tin * kUpStride[s];
+            if (s > 0) ok = ok && make_tmap_bf16(&t_xin[s], xin, Tin, cin, 128);
+            ok = ok && make_tmap_bf16(&t_a[s], a16, T, cp, 128);
+            for (int j = 0; j < 3 && ok; j++) ok = make_tmap_f32_resid(&t_r[s][j], r[j], T, cp);
+            Tin = T;
+        }
+        DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (vocoder activations, %d frames)", T0);
+        maps_T0 = T0;
+        return DTTS_OK;
+    }
+
+    int gemm(const GemmOp &op) {
+        DTTS_CUDA(launch_gemm(op, num_sms, stream));
+        return DTTS_OK;
+    }
+
+    int lstm_layer(const float *w_hh_l, float *h_out, int T) {
+        DTTS_CUDA(cudaMemsetAsync(d_bar, 0, sizeof(unsigned), stream));
+        const float *g = gin;
+        unsigned *bar = d_bar;
+        int *err = d_err;
+        void *args[] = {(void *)&g, (void *)&w_hh_l, (void *)&h_out, (void *)&T, (void *)&bar, (void *)&err};
+        const size_t smem = (32 * kLstmH + kLstmH + 32) * sizeof(float);
+        DTTS_CUDA(cudaLaunchCooperativeKernel((const void *)voc_lstm_kernel, dim3(kLstmCtas), dim3(256), args, smem,
+                                              stream));
+        return DTTS_OK;
+    }
+
+    // the whole decode on `stream`, latents already in `lat`, audio to `audio`
+    int enqueue(int T0) {
+        int st;
+        // ---- bottleneck (bigvgan_cpp.cpp:344-377)
+        launch_gemm_f32(lat, pp_w, pp_b, pp, T0, 128, 128, stream);
+        launch_gemm_f32(pp, mi_w1, mi_b1, z, T0, kLstmH, 128, stream);
+        const float *in = z;
+        for (int l = 0; l < 4; l++) {
+            launch_gemm_f32(in, w_ih[l], b_g[l], gin, T0, 4 * kLstmH, kLstmH, stream);
+            if ((st = lstm_layer(w_hh[l], hl[l & 1], T0))) return st;
+            in = hl[l & 1];
+        }
+        launch_add_f32(z, hl[1], hl[0], (long long)T0 * kLstmH, stream);   // skip: z + h of the last layer
+        launch_gemm_f32(hl[0], mi_w2, mi_b2, bott, T0, 128, kLstmH, stream);
+        launch_f32_to_bf16(bott, bott16, (long long)T0 * 128, stream);
+        // ---- conv_pre: centred K = 5 (taps at t - 2 .. t + 2), bf16 out (:384-405)
+        {
+            GemmOp op = conv_op(t_bott, t_pre, T0, 1536, 5 * 128, EPI_BF16, 128, d_err);
+            op.ep.bias = b_pre; op.ep.out = x0; op.ep.ldo = 1536;
+            op.ep.tap_kb = 2; op.ep.tap_base = -2; op.ep.tap_step = 1;
+            if ((st = gemm(op))) return st;
+        }
+        long long Tin = T0;
+        for (int s = 0; s < kStages; s++) {
+            const int cin = s == 0 ? 1536 : cpad(kUpOut[s - 1]), cp = cpad(kUpOut[s]), ch = kUpOut[s];
+            const int str = kUpStride[s];
+            const long long T = Tin * str;
+            const int bn = bn_for(cp);
+            // ---- causal ConvTranspose1d, one GEMM per output phase (:176-205, :415-420)
+            for (int ph = 0; ph < str; ph++) {
+                GemmOp op = conv_op(s == 0 ? t_x0 : t_xin[s], t_up[s][ph], (int)Tin, cp, 2 * cin, EPI_F32, bn, d_err);
+                op.ep.bias = b_up[s]; op.ep.out = r[0] + (size_t)ph * cp; op.ep.ldo = (long long)str * cp;
+                op.ep.tap_kb = cin / 64; op.ep.tap_base = 0; op.ep.tap_step = -1;
+                if ((st = gemm(op))) return st;
+            }
+            const size_t n = (size_t)T * cp;
+            DTTS_CUDA(cudaMemcpyAsync(r[1], r[0], n * 4, cudaMemcpyDeviceToDevice, stream));
+            DTTS_CUDA(cudaMemcpyAsync(r[2], r[0], n * 4, cudaMemcpyDeviceToDevice, stream));
+            // ---- three AMP blocks (:427-483)
+            for (int j = 0; j < 3; j++) {
+                const int rb = s * 3 + j, K = kRbK[j];
+                for (int p = 0; p < 3; p++) {
+                    ActArgs aa1{r[j], cp, a16, cp, 1, (int)T, ch, act_a[rb][2 * p], act_ib[rb][2 * p], aa, aa, 1};
+                    launch_act(aa1, cp, stream);
+                    {
+                        GemmOp op = conv_op(t_a[s], t_c1[rb][p], (int)T, cp, K * cp, EPI_F32, bn, d_err);
+                        op.ep.bias = b_c1[rb][p]; op.ep.out = y; op.ep.ldo = cp;
+                        op.ep.tap_kb = cp / 64; op.ep.tap_base = -kRbDil[p] * (K - 1); op.ep.tap_step = kRbDil[p];
+                        if ((st = gemm(op))) return st;
+                    }
+                    ActArgs aa2{y, cp, a16, cp, 1, (int)T, ch, act_a[rb][2 * p + 1], act_ib[rb][2 * p + 1], aa, aa, 1};
+                    launch_act(aa2, cp, stream);
+                    {
+                        GemmOp op = conv_op(t_a[s], t_c2[rb][p], (int)T, cp, K * cp, EPI_RESID, bn, d_err);
+                        op.tr = t_r[s][j];
+                        op.ep.bias = b_c2[rb][p]; op.ep.resid = r[j]; op.ep.ldr = cp;
+                        op.ep.tap_kb = cp / 64; op.ep.tap_base = -(K - 1); op.ep.tap_step = 1;
+                        if ((st = gemm(op))) return st;
+                    }
+                }
+            }
+            const long long n4 = (long long)(n / 4);
+            const bool last = s == kStages - 1;
+            voc_mean3_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(
+                (const float4 *)r[0], (const float4 *)r[1], (const float4 *)r[2], last ? nullptr : (uint2 *)xin,
+                last ? (float4 *)xf : nullptr, n4);
+            Tin = T;
+        }
+        // ---- activation_post, conv_post, tanh (:499-521)
+        const int cp = cpad(24);
+        ActArgs ap{xf, cp, y, cp, 0, (int)Tin, 24, post_a, post_ib, post_fu, post_fd, 24};
+        launch_act(ap, cp, stream);
+        voc_post_kernel<<<(unsigned)((Tin + 255) / 256), 256, 0, stream>>>(y, cp, (int)Tin, 24, post_w, audio);
+        DTTS_CUDA(cudaGetLastError());
+        return DTTS_OK;
+    }
+
+    int decode(const float *latent, int n_frames, float *audio_out, int mem) {
+        DTTS_CHECK(latent && audio_out, DTTS_ERR_ARG, "null argument");
+        DTTS_CHECK(n_frames >= 1 && n_frames <= max_frames, DTTS_ERR_ARG, "n_frames %d out of [1, %d]", n_frames,
+                   max_frames);
+        DTTS_CHECK(mem == DTTS_MEM_HOST || mem == DTTS_MEM_DEVICE, DTTS_ERR_ARG, "bad mem kind");
+        DeviceGuard g(device);
+        int st = encode_maps(n_frames);
+        if (st) return st;
+        const cudaMemcpyKind ik = mem == DTTS_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+        DTTS_CUDA(cudaMemcpyAsync(lat, latent, (size_t)n_frames * 128 * 4, ik, stream));
+        if ((st = enqueue(n_frames))) return st;
+        const cudaMemcpyKind ok = mem == DTTS_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+        DTTS_CUDA(cudaMemcpyAsync(audio_out, audio, (size_t)n_frames * kHop * 4, ok, stream));
+        if (mem != DTTS_MEM_HOST) return DTTS_OK;
+        if ((st = stream_wait(stream, 300.0))) return st;
+        int err = 0;
+        DTTS_CUDA(cudaMemcpy(&err, d_err, 4, cudaMemcpyDeviceToHost));
+        if (err) { cudaMemset(d_err, 0, 4); set_error("device wait limit reached (code %d)", err); return DTTS_ERR_TIMEOUT; }
+        return DTTS_OK;
+    }
+};
+
+namespace {
+// B operand of a convolution over taps: B[o][tap * cpi + c] = W[o][c][tap] (W [oc][ic][K])
+std::vector<float> conv_b_operand(const float *W, int oc, int ic, int K, int cpo, int cpi) {
+    std::vector<float> v((size_t)cpo * K * cpi, 0.f);
+    for (int o = 0; o < oc; o++)
+        for (int c = 0; c < ic; c++)
+            for (int k = 0; k < K; k++) v[((size_t)o * K + k) * cpi + c] = W[((size_t)o * ic + c) * K + k];
+    return v;
+}
+}  // namespace
+
+extern "C" {
+
+int dtts_voc_aa_filter(float *taps12) {
+    DTTS_CHECK(taps12, DTTS_ERR_ARG, "null argument");
+    kaiser_sinc(taps12, 0.25, 0.3, kTaps);
+    return DTTS_OK;
+}
+
+int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_voc **out) {
+    DTTS_CHECK(w && out, DTTS_ERR_ARG, "null argument");
+    *out = nullptr;
+    DTTS_CHECK(max_frames >= 1 && max_frames <= 100000, DTTS_ERR_ARG, "max_frames %d out of [1, 100000]", max_frames);
+    DTTS_CHECK(w->post_proj_w && w->mi_w1 && w->mi_w2 && w->conv_pre_w && w->conv_post_w && w->post_filt_up &&
+                   w->post_filt_down,
+               DTTS_ERR_ARG, "missing a required vocoder weight");
+    for (int l = 0; l < 4; l++)
+        DTTS_CHECK(w->lstm_w_ih[l] && w->lstm_w_hh[l], DTTS_ERR_ARG, "missing LSTM layer %d weights", l);
+    for (int s = 0; s < kStages; s++) DTTS_CHECK(w->ups_w[s], DTTS_ERR_ARG, "missing decoder.ups.%d", s);
+    for (int rb = 0; rb < kRb; rb++)
+        for (int j = 0; j < 3; j++)
+            DTTS_CHECK(w->c1_w[rb][j] && w->c2_w[rb][j], DTTS_ERR_ARG, "missing resblock %d conv %d", rb, j);
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    std::unique_ptr<dtts_voc> v(new dtts_voc());
+    v->device = device; v->num_sms = nsm; v->max_frames = max_frames;
+    DTTS_CUDA(cudaStreamCreateWithFlags(&v->own_stream, cudaStreamNonBlocking));
+    v->stream = v->own_stream;
+    DTTS_CUDA(gemm_prepare_attributes());
+    DTTS_CUDA(cudaFuncSetAttribute((const void *)voc_lstm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (32 * kLstmH + kLstmH + 32) * (int)sizeof(float)));
+    DeviceArena &A = v->wts;
+    v->d_err = (int *)A.alloc(4);
+    v->d_bar = (unsigned *)A.alloc(4);
+    DTTS_CHECK(v->d_err && v->d_bar, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemset(v->d_err, 0, 4));
+    // bottleneck
+    std::vector<float> zero(4 * kLstmH, 0.f);
+    if ((st = up_f32(A, w->post_proj_w, 128 * 128, &v->pp_w))) return st;
+    if ((st = up_f32_pad(A, w->post_proj_b, 128, 128, &v->pp_b))) return st;
+    if ((st = up_f32(A, w->mi_w1, (size_t)kLstmH * 128, &v->mi_w1))) return st;
+    if ((st = up_f32_pad(A, w->mi_b1, kLstmH, kLstmH, &v->mi_b1))) return st;
+    if ((st = up_f32(A, w->mi_w2, (size_t)128 * kLstmH, &v->mi_w2))) return st;
+    if ((st = up_f32_pad(A, w->mi_b2, 128, 128, &v->mi_b2))) return st;
+    for (int l = 0; l < 4; l++) {
+        if ((st = up_f32(A, w->lstm_w_ih[l], (size_t)4 * kLstmH * kLstmH, &v->w_ih[l]))) return st;
+        if ((st = up_f32(A, w->lstm_w_hh[l], (size_t)4 * kLstmH * kLstmH, &v->w_hh[l]))) return st;
+        // b_ih + b_hh, summed in float as lstm.cpp:26 starts each gate
+        std::vector<float> bg(4 * kLstmH);
+        for (int i = 0; i < 4 * kLstmH; i++)
+            bg[i] = (w->lstm_b_ih[l] ? w->lstm_b_ih[l][i] : 0.f) + (w->lstm_b_hh[l] ? w->lstm_b_hh[l][i] : 0.f);
+        if ((st = up_f32(A, bg.data(), bg.size(), &v->b_g[l]))) return st;
+    }
+    // conv_pre
+    if ((st = up_bf16(A, conv_b_operand(w->conv_pre_w, 1536, 128, 5, 1536, 128), &v->w_pre))) return st;
+    if ((st = up_f32_pad(A, w->conv_pre_b, 1536, 1536, &v->b_pre))) return st;
+    bool ok = make_tmap_bf16(&v->t_pre, v->w_pre, 1536, 5 * 128, 128);
+    // upsampling: phase r, B_r[o][j * cpi + c] = W[c][o][r + j stride] (W [ic][oc][2 stride])
+    for (int s = 0; s < kStages && ok; s++) {
+        const int ic = kUpIn[s], oc = kUpOut[s], cpi = s == 0 ? 1536 : cpad(ic), cpo = cpad(oc), str = kUpStride[s];
+        const int K = 2 * str;
+        std::vector<float> bop((size_t)str * cpo * 2 * cpi, 0.f);
+        for (int ph = 0; ph < str; ph++)
+            for (int o = 0; o < oc; o++)
+                for (int j = 0; j < 2; j++)
+                    for (int c = 0; c < ic; c++)
+                        bop[(((size_t)ph * cpo + o) * 2 + j) * cpi + c] = w->ups_w[s][((size_t)c * oc + o) * K + ph + j * str];
+        if ((st = up_bf16(A, bop, &v->w_up[s]))) return st;
+        if ((st = up_f32_pad(A, w->ups_b[s], oc, cpo, &v->b_up[s]))) return st;
+        v->t_up[s].resize(str);
+        const int bn = dtts_voc::bn_for(cpo);
+        for (int ph = 0; ph < str && ok; ph++)
+            ok = make_tmap_bf16(&v->t_up[s][ph], v->w_up[s] + (size_t)ph * cpo * 2 * cpi, cpo, 2 * cpi, bn);
+    }
+    // AMP blocks
+    for (int rb = 0; rb < kRb && ok; rb++) {
+        const int ch = kUpOut[rb / 3], cp = cpad(ch), K = kRbK[rb % 3], bn = dtts_voc::bn_for(cp);
+        for (int j = 0; j < 3 && ok; j++) {
+            if ((st = up_bf16(A, conv_b_operand(w->c1_w[rb][j], ch, ch, K, cp, cp), &v->w_c1[rb][j]))) return st;
+            if ((st = up_bf16(A, conv_b_operand(w->c2_w[rb][j], ch, ch, K, cp, cp), &v->w_c2[rb][j]))) return st;
+            if ((st = up_f32_pad(A, w->c1_b[rb][j], ch, cp, &v->b_c1[rb][j]))) return st;
+            if ((st = up_f32_pad(A, w->c2_b[rb][j], ch, cp, &v->b_c2[rb][j]))) return st;
+            ok = make_tmap_bf16(&v->t_c1[rb][j], v->w_c1[rb][j], cp, (size_t)K * cp, bn) &&
+                 make_tmap_bf16(&v->t_c2[rb][j], v->w_c2[rb][j], cp, (size_t)K * cp, bn);
+        }
+        for (int a = 0; a < 6; a++) {
+            std::vector<float> av, ib;
+            snake_consts(w->alpha[rb][a], w->beta[rb][a], ch, cp, av, ib);
+            if ((st = up_f32(A, av.data(), cp, &v->act_a[rb][a]))) return st;
+            if ((st = up_f32(A, ib.data(), cp, &v->act_ib[rb][a]))) return st;
+        }
+    }
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (vocoder weights)");
+    // filters, activation_post, conv_post
+    float aa[kTaps];
+    kaiser_sinc(aa, 0.25, 0.3, kTaps);
+    if ((st = up_f32(A, aa, kTaps, &v->aa))) return st;
+    {
+        std::vector<float> av, ib;
+        snake_consts(w->post_alpha, w->post_beta, 24, 24, av, ib);
+        if ((st = up_f32(A, av.data(), 24, &v->post_a))) return st;
+        if ((st = up_f32(A, ib.data(), 24, &v->post_ib))) return st;
+    }
+    if ((st = up_f32(A, w->post_filt_up, 24 * kTaps, &v->post_fu))) return st;
+    if ((st = up_f32(A, w->post_filt_down, 24 * kTaps, &v->post_fd))) return st;
+    if ((st = up_f32(A, w->conv_post_w, 24 * 7, &v->post_w))) return st;
+    if ((st = v->alloc_ws())) return st;
+    *out = v.release();
+    return DTTS_OK;
+}
+
+int dtts_voc_destroy(dtts_voc *v) {
+    if (!v) return DTTS_OK;
+    DeviceGuard g(v->device);
+    cudaStreamSynchronize(v->stream);
+    delete v;
+    return DTTS_OK;
+}
+
+int dtts_voc_set_stream(dtts_voc *v, void *stream) {
+    DTTS_CHECK(v, DTTS_ERR_ARG, "null engine");
+    v->stream = stream ? static_cast<cudaStream_t>(stream) : v->own_stream;
+    return DTTS_OK;
+}
+
+int dtts_voc_decode(dtts_voc *v, const float *latent, int n_frames, float *audio, int mem) {
+    DTTS_CHECK(v, DTTS_ERR_ARG, "null engine");
+    return v->decode(latent, n_frames, audio, mem);
+}
+
+int dtts_selftest_voc_activation(const float *x, int len, int ch, const float *alpha, const float *beta,
+                                 const float *filt_up, const float *filt_down, int fch, float *out) {
+    DTTS_CHECK(x && out && filt_up && filt_down, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(len >= 1 && ch >= 1 && ch <= 4096 && (fch == 1 || fch == ch), DTTS_ERR_ARG, "bad shape");
+    int nsm = 0, st = check_device(0, &nsm);
+    if (st) return st;
+    DeviceGuard g(0);
+    std::vector<float> av, ib;
+    snake_consts(alpha, beta, ch, ch, av, ib);
+    DeviceArena A;
+    float *dx = nullptr, *dy = nullptr, *da = nullptr, *dib = nullptr, *dfu = nullptr, *dfd = nullptr;
+    st = up_f32(A, x, (size_t)len * ch, &dx);
+    if (!st) st = up_f32(A, av.data(), ch, &da);
+    if (!st) st = up_f32(A, ib.data(), ch, &dib);
+    if (!st) st = up_f32(A, filt_up, (size_t)fch * kTaps, &dfu);
+    if (!st) st = up_f32(A, filt_down, (size_t)fch * kTaps, &dfd);
+    if (!st) {
+        dy = (float *)A.alloc((size_t)len * ch * 4);
+        if (!dy) { set_error("cudaMalloc failed"); st = DTTS_ERR_OOM; }
+    }
+    if (!st) {
+        ActArgs p{dx, ch, dy, ch, 0, len, ch, da, dib, dfu, dfd, fch};
+        launch_act(p, ch, 0);
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(out, dy, (size_t)len * ch * 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) { set_error("voc activation selftest: %s", cudaGetErrorString(e)); st = DTTS_ERR_CUDA; }
+    }
+    A.free_all();
+    return st;
+}
+
+}  // extern "C"

@@ -111,7 +111,9 @@ EXPORTS = [
     "dtts_dit_profile_kernel",
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_fm_create", "dtts_fm_destroy", "dtts_fm_start",
     "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve",
-    "dtts_llm_create", "dtts_llm_destroy", "dtts_llm_set_stream", "dtts_llm_prefill", "dtts_llm_step", "dtts_llm_length", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
+    "dtts_llm_create", "dtts_llm_destroy", "dtts_llm_set_stream", "dtts_llm_prefill", "dtts_llm_step", "dtts_llm_length",
+    "dtts_voc_create", "dtts_voc_destroy", "dtts_voc_set_stream", "dtts_voc_decode", "dtts_voc_aa_filter",
+    "dtts_selftest_voc_activation", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
     "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_selftest_e4m3",
@@ -119,6 +121,20 @@ EXPORTS = [
     "dtts_fp8_quantize_rows", "dtts_st_open",
     "dtts_st_close", "dtts_st_count", "dtts_st_shape", "dtts_st_read_f32",
 ]
+
+
+_fp3 = _fp * 3
+_fp6 = _fp * 6
+
+
+class VocW(C.Structure):
+    """dtts_voc_weights (include/dtts.h)."""
+    _fields_ = [(n, _fp) for n in ("post_proj_w", "post_proj_b", "mi_w1", "mi_b1", "mi_w2", "mi_b2")] + [
+        (n, _fp * 4) for n in ("lstm_w_ih", "lstm_w_hh", "lstm_b_ih", "lstm_b_hh")] + [
+        ("conv_pre_w", _fp), ("conv_pre_b", _fp), ("ups_w", _fp * 6), ("ups_b", _fp * 6)] + [
+        (n, _fp3 * 18) for n in ("c1_w", "c1_b", "c2_w", "c2_b")] + [
+        (n, _fp6 * 18) for n in ("alpha", "beta")] + [
+        (n, _fp) for n in ("post_alpha", "post_beta", "post_filt_up", "post_filt_down", "conv_post_w")]
 
 
 class DttsError(RuntimeError):
@@ -209,6 +225,12 @@ def lib(path: str = LIB_PATH):
     L.dtts_llm_prefill.argtypes = [_vp, _vp, C.c_int, C.c_int, _vp, C.c_int]
     L.dtts_llm_step.argtypes = [_vp, _vp, C.c_int, _vp, C.c_int]
     L.dtts_llm_length.argtypes = [_vp, C.POINTER(C.c_int)]
+    L.dtts_voc_create.argtypes = [C.POINTER(VocW), C.c_int, C.c_int, C.POINTER(_vp)]
+    L.dtts_voc_destroy.argtypes = [_vp]
+    L.dtts_voc_set_stream.argtypes = [_vp, _vp]
+    L.dtts_voc_decode.argtypes = [_vp, _vp, C.c_int, _vp, C.c_int]
+    L.dtts_voc_aa_filter.argtypes = [_fp]
+    L.dtts_selftest_voc_activation.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp, _fp, C.c_int, _fp]
     L.dtts_selftest_e4m3.argtypes = [_fp, _u8p, C.c_int, C.c_int]
     L.dtts_selftest_gemm_e4m3.argtypes = [_u8p, _fp, _u8p, _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
                                           C.c_int]
@@ -527,6 +549,93 @@ class LLM:
         n = C.c_int()
         check(lib().dtts_llm_length(self.h, C.byref(n)))
         return n.value
+
+
+def voc_struct(w: dict):
+    """VocW over the checkpoint-named arrays of w (bigvgan_load's names)."""
+    keep = []
+
+    def P(name):
+        a = _f32(w.get(name))
+        keep.append(a)
+        return _ptr(a)
+
+    v = VocW()
+    v.post_proj_w, v.post_proj_b = P("post_proj.weight"), P("post_proj.bias")
+    v.mi_w1, v.mi_b1 = P("dec_mi_layer.0.weight"), P("dec_mi_layer.0.bias")
+    v.mi_w2, v.mi_b2 = P("dec_mi_layer.2.weight"), P("dec_mi_layer.2.bias")
+    for l in range(4):
+        v.lstm_w_ih[l] = P(f"dec_mi_layer.1.lstm.weight_ih_l{l}")
+        v.lstm_w_hh[l] = P(f"dec_mi_layer.1.lstm.weight_hh_l{l}")
+        v.lstm_b_ih[l] = P(f"dec_mi_layer.1.lstm.bias_ih_l{l}")
+        v.lstm_b_hh[l] = P(f"dec_mi_layer.1.lstm.bias_hh_l{l}")
+    v.conv_pre_w, v.conv_pre_b = P("decoder.conv_pre.weight"), P("decoder.conv_pre.bias")
+    for i in range(6):
+        v.ups_w[i], v.ups_b[i] = P(f"decoder.ups.{i}.0.weight"), P(f"decoder.ups.{i}.0.bias")
+    for rb in range(18):
+        p = f"decoder.resblocks.{rb}."
+        for j in range(3):
+            v.c1_w[rb][j], v.c1_b[rb][j] = P(p + f"convs1.{j}.weight"), P(p + f"convs1.{j}.bias")
+            v.c2_w[rb][j], v.c2_b[rb][j] = P(p + f"convs2.{j}.weight"), P(p + f"convs2.{j}.bias")
+        for a in range(6):
+            v.alpha[rb][a] = P(p + f"activations.{a}.act.alpha")
+            v.beta[rb][a] = P(p + f"activations.{a}.act.beta")
+    v.post_alpha = P("decoder.activation_post.act.alpha")
+    v.post_beta = P("decoder.activation_post.act.beta")
+    v.post_filt_up = P("decoder.activation_post.upsample.filter")
+    v.post_filt_down = P("decoder.activation_post.downsample.lowpass.filter")
+    v.conv_post_w = P("decoder.conv_post.weight")
+    return v, keep
+
+
+class Vocoder:
+    """The BigVGAN decoder (dtts_voc_*): latents [n_frames][128] -> audio [n_frames * 1920]."""
+
+    HOP = 1920
+
+    def __init__(self, weights: dict, max_frames=256, device=0):
+        v, keep = voc_struct(weights)
+        h = _vp()
+        check(lib().dtts_voc_create(C.byref(v), device, max_frames, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().dtts_voc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr):
+        check(lib().dtts_voc_set_stream(self.h, stream_ptr))
+
+    def decode(self, latent, out=None, mem=MEM_HOST):
+        """mem=MEM_DEVICE: latent and out are device tensors and the call only enqueues."""
+        if mem == MEM_HOST:
+            latent = _f32(latent)
+            out = np.zeros(latent.shape[0] * self.HOP, np.float32) if out is None else out
+        check(lib().dtts_voc_decode(self.h, _addr(latent), latent.shape[0], _addr(out), mem))
+        return out
+
+
+def voc_aa_filter():
+    f = np.zeros(12, np.float32)
+    check(lib().dtts_voc_aa_filter(_ptr(f)))
+    return f
+
+
+def selftest_voc_activation(x, alpha, beta, filt_up, filt_down):
+    x = _f32(x)
+    fu, fd = _f32(filt_up), _f32(filt_down)
+    fch = 1 if fu.size == 12 else x.shape[1]
+    out = np.zeros_like(x)
+    check(lib().dtts_selftest_voc_activation(_ptr(x), x.shape[0], x.shape[1], _ptr(_f32(alpha)), _ptr(_f32(beta)),
+                                             _ptr(fu), _ptr(fd), fch, _ptr(out)))
+    return out
 
 
 class Attention:

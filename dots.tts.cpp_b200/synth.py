@@ -174,3 +174,73 @@ def llm_weights(seed=3, n_layers=LLM_LAYERS):
         gain = name.endswith("norm.weight")
         w[name] = normal(seed, name, shape, 0.02, 1.0 if gain else 0.0)
     return w
+
+
+# ---------------------------------------------------------------- vocoder
+VOC_UP_IN = (1536, 768, 384, 192, 96, 48)
+VOC_UP_OUT = (768, 384, 192, 96, 48, 24)
+VOC_UP_STRIDE = (10, 6, 4, 2, 2, 2)
+VOC_UP_KERNEL = (20, 12, 8, 4, 4, 4)
+VOC_RB_KERNEL = (3, 7, 11)
+VOC_RB_DIL = (1, 3, 5)
+VOC_HOP = 1920
+
+
+def voc_shapes():
+    """Tensor names and shapes of the BigVGAN decoder checkpoint
+    (src/modules/vocoder/bigvgan_cpp.cpp:203-290)."""
+    s = {"post_proj.weight": (LAT, LAT, 1), "post_proj.bias": (LAT,),
+         "dec_mi_layer.0.weight": (512, LAT), "dec_mi_layer.0.bias": (512,),
+         "dec_mi_layer.2.weight": (LAT, 512), "dec_mi_layer.2.bias": (LAT,),
+         "decoder.conv_pre.weight": (1536, LAT, 5), "decoder.conv_pre.bias": (1536,)}
+    for l in range(4):
+        for k in ("ih", "hh"):
+            s[f"dec_mi_layer.1.lstm.weight_{k}_l{l}"] = (2048, 512)
+            s[f"dec_mi_layer.1.lstm.bias_{k}_l{l}"] = (2048,)
+    for i in range(6):
+        s[f"decoder.ups.{i}.0.weight"] = (VOC_UP_IN[i], VOC_UP_OUT[i], VOC_UP_KERNEL[i])
+        s[f"decoder.ups.{i}.0.bias"] = (VOC_UP_OUT[i],)
+    for rb in range(18):
+        ch, K = VOC_UP_OUT[rb // 3], VOC_RB_KERNEL[rb % 3]
+        p = f"decoder.resblocks.{rb}."
+        for j in range(3):
+            for c in ("convs1", "convs2"):
+                s[p + f"{c}.{j}.weight"] = (ch, ch, K)
+                s[p + f"{c}.{j}.bias"] = (ch,)
+        for a in range(6):
+            s[p + f"activations.{a}.act.alpha"] = (ch,)
+            s[p + f"activations.{a}.act.beta"] = (ch,)
+    s["decoder.activation_post.act.alpha"] = (24,)
+    s["decoder.activation_post.act.beta"] = (24,)
+    s["decoder.activation_post.upsample.filter"] = (24, 1, 12)
+    s["decoder.activation_post.downsample.lowpass.filter"] = (24, 1, 12)
+    s["decoder.conv_post.weight"] = (1, 24, 7)
+    return s
+
+
+def voc_weights(seed=5, aa_filter=None):
+    """BigVGAN decoder weights scaled so that the signal stays of order one
+    through all six stages and tanh stays mostly linear: convolutions
+    N(0, g / sqrt(fan_in)) with g = 0.5 inside the AMP blocks and in conv_post,
+    1 elsewhere, LSTM N(0, 0.5 / sqrt(512)), biases
+    N(0, 0.02), log-scale snake alpha / beta N(0, 0.1).  The activation_post
+    filters are `aa_filter` (12 taps) perturbed per channel by N(0, 1e-3)."""
+    w = {}
+    for name, shape in voc_shapes().items():
+        if name.endswith(".bias") or "lstm.bias" in name:
+            w[name] = normal(seed, name, shape, 0.02)
+        elif name.endswith("act.alpha") or name.endswith("act.beta"):
+            w[name] = normal(seed, name, shape, 0.1)
+        elif name.endswith("filter"):
+            base = np.zeros(12, np.float32) if aa_filter is None else np.asarray(aa_filter, np.float32)
+            w[name] = (base[None, None, :] + normal(seed, name, shape, 1e-3)).astype(np.float32)
+        elif "lstm.weight" in name:
+            w[name] = normal(seed, name, shape, 0.5 / np.sqrt(512.0))
+        elif "ups." in name:
+            ic, oc, K = shape
+            w[name] = normal(seed, name, shape, 1.0 / np.sqrt(2.0 * ic))
+        else:
+            fan_in = int(np.prod(shape[1:]))
+            g = 0.5 if ("resblocks" in name or "conv_post" in name) else 1.0
+            w[name] = normal(seed, name, shape, g / np.sqrt(fan_in))
+    return w

@@ -338,6 +338,45 @@ int dtts_llm_prefill(dtts_llm *e, const float *emb, int B, int n_tok, float *hid
 int dtts_llm_step(dtts_llm *e, const float *emb, int B, float *hidden, int mem);
 int dtts_llm_length(dtts_llm *e, int *tokens);
 
+/* ------------------------------------------------------------------ vocoder
+ * BigVGAN v2 decoder (src/modules/vocoder/bigvgan_cpp.cpp, include/bigvgan_cpp.h): the
+ * latents of an utterance [n_frames][128] to audio [n_frames * 1920] at 24 kHz.  Convolutions
+ * run as tcgen05 GEMMs over taps on bf16 time-major activations (fp32 accumulate, fp32
+ * residual stream); the LSTM bottleneck and the activations are fp32.  Tensor names below
+ * are the checkpoint's (bigvgan_load, bigvgan_cpp.cpp:203-290). */
+typedef struct dtts_voc dtts_voc;
+typedef struct dtts_voc_weights {
+    const float *post_proj_w, *post_proj_b;   /* post_proj.weight [128][128][1], .bias [128]          */
+    const float *mi_w1, *mi_b1;               /* dec_mi_layer.0.weight [512][128], .bias [512]        */
+    const float *mi_w2, *mi_b2;               /* dec_mi_layer.2.weight [128][512], .bias [128]        */
+    const float *lstm_w_ih[4], *lstm_w_hh[4]; /* dec_mi_layer.1.lstm.weight_{ih,hh}_l{0..3} [2048][512] */
+    const float *lstm_b_ih[4], *lstm_b_hh[4]; /* dec_mi_layer.1.lstm.bias_{ih,hh}_l{0..3} [2048]      */
+    const float *conv_pre_w, *conv_pre_b;     /* decoder.conv_pre [1536][128][5], [1536]              */
+    const float *ups_w[6], *ups_b[6];         /* decoder.ups.{s}.0 [in][out][2 stride], [out]          */
+    const float *c1_w[18][3], *c1_b[18][3];   /* decoder.resblocks.{r}.convs1.{j} [ch][ch][k], [ch]    */
+    const float *c2_w[18][3], *c2_b[18][3];   /* decoder.resblocks.{r}.convs2.{j}                      */
+    const float *alpha[18][6], *beta[18][6];  /* decoder.resblocks.{r}.activations.{a}.act.alpha/.beta */
+    const float *post_alpha, *post_beta;      /* decoder.activation_post.act.alpha/.beta [24]          */
+    const float *post_filt_up;                /* decoder.activation_post.upsample.filter [24][1][12]   */
+    const float *post_filt_down;              /* ...downsample.lowpass.filter [24][1][12]              */
+    const float *conv_post_w;                 /* decoder.conv_post.weight [1][24][7] (no bias)         */
+} dtts_voc_weights;
+/* Replaces bigvgan_load (bigvgan_cpp.cpp:203): weights uploaded once; work buffers for
+ * utterances of up to max_frames latent frames. */
+int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_voc **out);
+int dtts_voc_destroy(dtts_voc *v);
+int dtts_voc_set_stream(dtts_voc *v, void *cuda_stream);
+/* bigvgan_decode (bigvgan_cpp.cpp:325): latent [n_frames][128] -> audio [n_frames * 1920]. */
+int dtts_voc_decode(dtts_voc *v, const float *latent, int n_frames, float *audio, int mem);
+/* The 12-tap low-pass filter of the AMP activations (BigVGAN's kaiser_sinc_filter1d with
+ * cutoff 0.25, half width 0.3), as the engine computes it. */
+int dtts_voc_aa_filter(float *taps12);
+/* One Activation1d (up x2, SnakeBeta, down x2) on x [len][ch] fp32 (host), out fp32;
+ * filt_up / filt_down hold 12 taps shared by all channels (fch = 1) or [ch][12] (fch = ch);
+ * alpha / beta are the log-scale parameters [ch]. */
+int dtts_selftest_voc_activation(const float *x, int len, int ch, const float *alpha, const float *beta,
+                                 const float *filt_up, const float *filt_down, int fch, float *out);
+
 /* ------------------------------------------------------------------ self-test
  * One engine kernel in isolation on host data (no reference counterpart):
  * inputs are rounded to bf16 on the host exactly as the engine stores them. */

@@ -127,6 +127,47 @@ void orc_euler_solve(const orc_dit *m, int n_utt, int fm_len, int patch,
 void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pair_mode,
                     float *out, float *h_last);
 
+
+/* ---------------------------------------------------------------- vocoder
+ * BigVGAN v2 decoder as the reference runs it (src/modules/vocoder/
+ * bigvgan_cpp.cpp:325-542, include/bigvgan_cpp.h): post_proj, dec_mi_layer
+ * (Linear 128->512, 4-layer LSTM with skip, Linear 512->128), conv_pre, six
+ * causal upsampling stages of three AMP blocks each, activation_post,
+ * conv_post, tanh x 1.92.  Tensor names in the comments are the checkpoint's. */
+#define ORC_VOC_STAGES 6
+#define ORC_VOC_RB     18
+typedef struct {
+    const float *post_proj_w, *post_proj_b;          /* post_proj.weight [128][128][1], .bias [128]      */
+    const float *mi_w1, *mi_b1;                      /* dec_mi_layer.0.weight [512][128], .bias [512]    */
+    const float *mi_w2, *mi_b2;                      /* dec_mi_layer.2.weight [128][512], .bias [128]    */
+    const float *lstm_w_ih[4], *lstm_w_hh[4];        /* dec_mi_layer.1.lstm.weight_{ih,hh}_l{l} [2048][512] */
+    const float *lstm_b_ih[4], *lstm_b_hh[4];        /* .bias_{ih,hh}_l{l} [2048]                        */
+    const float *conv_pre_w, *conv_pre_b;            /* decoder.conv_pre [1536][128][5], [1536]          */
+    const float *ups_w[ORC_VOC_STAGES];              /* decoder.ups.{s}.0.weight [in][out][2 stride]     */
+    const float *ups_b[ORC_VOC_STAGES];              /* decoder.ups.{s}.0.bias [out]                     */
+    const float *c1_w[ORC_VOC_RB][3], *c1_b[ORC_VOC_RB][3];   /* decoder.resblocks.{r}.convs1.{j} [ch][ch][k] */
+    const float *c2_w[ORC_VOC_RB][3], *c2_b[ORC_VOC_RB][3];   /* decoder.resblocks.{r}.convs2.{j}             */
+    const float *alpha[ORC_VOC_RB][6], *beta[ORC_VOC_RB][6];  /* decoder.resblocks.{r}.activations.{a}.act.{alpha,beta} [ch] */
+    const float *post_alpha, *post_beta;             /* decoder.activation_post.act.{alpha,beta} [24]    */
+    const float *post_filt_up, *post_filt_down;      /* ...upsample.filter, ...downsample.lowpass.filter [24][1][12] */
+    const float *conv_post_w;                        /* decoder.conv_post.weight [1][24][7], no bias     */
+} orc_voc;
+
+/* Stage geometry (bigvgan_cpp.cpp:207-210) and AMP constants (:407, :418). */
+extern const int orc_voc_up_in[ORC_VOC_STAGES], orc_voc_up_out[ORC_VOC_STAGES];
+extern const int orc_voc_up_stride[ORC_VOC_STAGES], orc_voc_up_kernel[ORC_VOC_STAGES];
+extern const int orc_voc_rb_kernel[3], orc_voc_rb_dil[3];
+
+/* aa_filter: the 12-tap low-pass filter the AMP activations use
+ * (bigvgan_cpp.cpp:27-31). audio [n_frames * 1920]. */
+void orc_voc_decode(const orc_voc *m, const float *aa_filter, const float *latent, int n_frames, float *audio);
+/* The pieces, for focused tests: Activation1d (up x2, SnakeBeta with log-scale
+ * alpha/beta, down x2; :33-124) in place on x [len][ch]; filt [fch][12] with
+ * fch = 1 (shared) or ch; and the dec_mi_layer bottleneck (:344-377). */
+void orc_voc_activation(float *x, int len, int ch, const float *alpha, const float *beta,
+                        const float *filt_up, const float *filt_down, int fch);
+void orc_voc_bottleneck(const orc_voc *m, const float *latent, int n_frames, float *out128);
+
 #ifdef __cplusplus
 }
 #endif

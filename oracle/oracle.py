@@ -52,6 +52,85 @@ class Pe(C.Structure):
         (n, _fp) for n in ("conv_w", "conv_b", "in_w", "in_b", "out_w", "out_b")]
 
 
+_fp3 = _fp * 3
+_fp6 = _fp * 6
+
+
+class Voc(C.Structure):
+    """orc_voc (oracle.h) and ref_voc (ref_voc.cpp): BigVGAN decoder weights."""
+    _fields_ = [(n, _fp) for n in ("post_proj_w", "post_proj_b", "mi_w1", "mi_b1", "mi_w2", "mi_b2")] + [
+        (n, _fp * 4) for n in ("lstm_w_ih", "lstm_w_hh", "lstm_b_ih", "lstm_b_hh")] + [
+        ("conv_pre_w", _fp), ("conv_pre_b", _fp), ("ups_w", _fp * 6), ("ups_b", _fp * 6)] + [
+        (n, _fp3 * 18) for n in ("c1_w", "c1_b", "c2_w", "c2_b")] + [
+        (n, _fp6 * 18) for n in ("alpha", "beta")] + [
+        (n, _fp) for n in ("post_alpha", "post_beta", "post_filt_up", "post_filt_down", "conv_post_w")]
+
+
+def aa_filter(cutoff=0.25, half_width=0.3, kernel_size=12):
+    """The AMP activations' low-pass filter: BigVGAN's kaiser_sinc_filter1d
+    (alias-free activation, published with BigVGAN) restated in float64 and
+    rounded to float32.  The reference hard-codes its values
+    (src/modules/vocoder/bigvgan_cpp.cpp:27-31, "kaiser_sinc_filter1d(cutoff=0.25,
+    half_width=0.3, K=12)"); tests/golden/voc_aa_filter.npz pins them.
+    Kaiser window of length K with beta from the attenuation
+    A = 2.285 (K/2 - 1) pi (4 half_width) + 7.95; an even K samples the sinc at
+    half-integer times; the taps are normalised to sum 1."""
+    half = kernel_size // 2
+    A = 2.285 * (half - 1) * np.pi * (4.0 * half_width) + 7.95
+    if A > 50.0:
+        beta = 0.1102 * (A - 8.7)
+    elif A >= 21.0:
+        beta = 0.5842 * (A - 21.0) ** 0.4 + 0.07886 * (A - 21.0)
+    else:
+        beta = 0.0
+    n = np.arange(kernel_size, dtype=np.float64)
+    window = np.i0(beta * np.sqrt(1.0 - (2.0 * n / (kernel_size - 1) - 1.0) ** 2)) / np.i0(beta)
+    if kernel_size % 2 == 0:
+        t = np.arange(-half, half, dtype=np.float64) + 0.5
+    else:
+        t = np.arange(kernel_size, dtype=np.float64) - half
+    f = 2.0 * cutoff * window * np.sinc(2.0 * cutoff * t)
+    f /= f.sum()
+    return f.astype(np.float32)
+
+
+def make_voc_struct(w: dict):
+    """Voc struct over the checkpoint-named arrays of w (synth.voc_shapes)."""
+    keep = []
+
+    def P(name):
+        a = np.ascontiguousarray(w[name], np.float32)
+        keep.append(a)
+        return _ptr(a)
+
+    v = Voc()
+    v.post_proj_w, v.post_proj_b = P("post_proj.weight"), P("post_proj.bias")
+    v.mi_w1, v.mi_b1 = P("dec_mi_layer.0.weight"), P("dec_mi_layer.0.bias")
+    v.mi_w2, v.mi_b2 = P("dec_mi_layer.2.weight"), P("dec_mi_layer.2.bias")
+    for l in range(4):
+        v.lstm_w_ih[l] = P(f"dec_mi_layer.1.lstm.weight_ih_l{l}")
+        v.lstm_w_hh[l] = P(f"dec_mi_layer.1.lstm.weight_hh_l{l}")
+        v.lstm_b_ih[l] = P(f"dec_mi_layer.1.lstm.bias_ih_l{l}")
+        v.lstm_b_hh[l] = P(f"dec_mi_layer.1.lstm.bias_hh_l{l}")
+    v.conv_pre_w, v.conv_pre_b = P("decoder.conv_pre.weight"), P("decoder.conv_pre.bias")
+    for i in range(6):
+        v.ups_w[i], v.ups_b[i] = P(f"decoder.ups.{i}.0.weight"), P(f"decoder.ups.{i}.0.bias")
+    for rb in range(18):
+        p = f"decoder.resblocks.{rb}."
+        for j in range(3):
+            v.c1_w[rb][j], v.c1_b[rb][j] = P(p + f"convs1.{j}.weight"), P(p + f"convs1.{j}.bias")
+            v.c2_w[rb][j], v.c2_b[rb][j] = P(p + f"convs2.{j}.weight"), P(p + f"convs2.{j}.bias")
+        for a in range(6):
+            v.alpha[rb][a] = P(p + f"activations.{a}.act.alpha")
+            v.beta[rb][a] = P(p + f"activations.{a}.act.beta")
+    v.post_alpha = P("decoder.activation_post.act.alpha")
+    v.post_beta = P("decoder.activation_post.act.beta")
+    v.post_filt_up = P("decoder.activation_post.upsample.filter")
+    v.post_filt_down = P("decoder.activation_post.downsample.lowpass.filter")
+    v.conv_post_w = P("decoder.conv_post.weight")
+    return v, keep
+
+
 def _ptr(a):
     if a is None:
         return None
@@ -193,6 +272,35 @@ class Oracle:
                                       C.c_float, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, _fp]
         L.orc_pe_forward.argtypes = [C.POINTER(Pe), _fp, C.c_int, C.c_int, _fp, _fp]
         L.orc_linear_rows.argtypes = [_fp, _fp, C.c_int, _fp, _fp, C.c_int, C.c_int]
+        L.orc_voc_decode.argtypes = [C.POINTER(Voc), _fp, _fp, C.c_int, _fp]
+        L.orc_voc_activation.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp, _fp, C.c_int]
+        L.orc_voc_bottleneck.argtypes = [C.POINTER(Voc), _fp, C.c_int, _fp]
+
+    def voc_decode(self, w, latent, aa=None):
+        """BigVGAN decoder on latent [n_frames][128] -> audio [n_frames * 1920]."""
+        v, keep = make_voc_struct(w)
+        lat = np.ascontiguousarray(latent, np.float32)
+        f = np.ascontiguousarray(aa_filter() if aa is None else aa, np.float32)
+        out = np.zeros(lat.shape[0] * 1920, np.float32)
+        self.lib.orc_voc_decode(C.byref(v), _ptr(f), _ptr(lat), lat.shape[0], _ptr(out))
+        return out
+
+    def voc_activation(self, x, alpha, beta, filt_up, filt_down):
+        """Activation1d on x [len][ch] (returns a new array); filters [12] or [ch][12]."""
+        x = np.array(x, np.float32, copy=True, order="C")
+        fu = np.ascontiguousarray(filt_up, np.float32)
+        fd = np.ascontiguousarray(filt_down, np.float32)
+        fch = 1 if fu.size == 12 else x.shape[1]
+        self.lib.orc_voc_activation(_ptr(x), x.shape[0], x.shape[1], _ptr(np.ascontiguousarray(alpha, np.float32)),
+                                    _ptr(np.ascontiguousarray(beta, np.float32)), _ptr(fu), _ptr(fd), fch)
+        return x
+
+    def voc_bottleneck(self, w, latent):
+        v, keep = make_voc_struct(w)
+        lat = np.ascontiguousarray(latent, np.float32)
+        out = np.zeros((lat.shape[0], 128), np.float32)
+        self.lib.orc_voc_bottleneck(C.byref(v), _ptr(lat), lat.shape[0], _ptr(out))
+        return out
 
     def set_threads(self, n):
         self.lib.orc_set_threads(int(n))
@@ -330,6 +438,17 @@ class Reference:
         L.ref_dit_block.argtypes = [_fp, _fp, _fp, C.POINTER(DitBlock), C.c_int, _u8p, _fp, C.c_int]
         L.ref_dit_velocity.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp, _u8p, _fp, C.c_int, C.c_int, _fp]
         L.ref_llm_run.argtypes = [C.c_int, C.POINTER(_RefLLMLayer), _fp, _fp, C.c_int, _fp, C.c_int, _fp, _fp]
+        L.ref_voc_decode.argtypes = [C.POINTER(Voc), _fp, C.c_int, _fp]
+        L.ref_voc_decode.restype = C.c_int
+
+    def voc_decode(self, w, latent):
+        """The reference's own bigvgan_decode (src/modules/vocoder/bigvgan_cpp.cpp:325)."""
+        v, keep = make_voc_struct(w)
+        lat = np.ascontiguousarray(latent, np.float32)
+        out = np.zeros(lat.shape[0] * 1920, np.float32)
+        n = self.lib.ref_voc_decode(C.byref(v), _ptr(lat), lat.shape[0], _ptr(out))
+        assert n == out.size, (n, out.size)
+        return out
 
     @staticmethod
     def available(path: str = REF_PATH) -> bool:

@@ -1,6 +1,7 @@
 """Comparison helpers.  Tolerances follow the parity bar of this path:
   bf16 paths      max relative error <= 2e-2 and cosine >= 0.999
   fp32 attention  max relative error <= 1e-3
+  vocoder audio   max relative error <= 5e-2 and cosine >= 0.998
 where max relative error = max|got - ref| / max|ref| over the whole tensor."""
 import json
 import struct
@@ -9,6 +10,8 @@ import numpy as np
 
 BF16_REL, BF16_COS = 2e-2, 0.999
 F32_REL = 1e-3
+# vocoder waveform (bf16 convolutions through 6 stages, 54 AMP layers)
+VOC_REL, VOC_COS = 5e-2, 0.998
 
 
 def rel(a, b):
