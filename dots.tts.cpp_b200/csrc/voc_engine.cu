@@ -6,7 +6,8 @@
 // and biases are zero and SnakeBeta(0) = 0.
 //   bottleneck   post_proj, Linear 128->512, 4 x LSTM(512) with skip,
 //                Linear 512->128: fp32 SIMT GEMMs + one cooperative kernel
-//                per LSTM layer (a grid barrier per time step)
+//                running the four LSTM layers as a wavefront (a grid barrier
+//                per step, T + 3 steps)
 //   conv_pre     K = 5, centred: tcgen05 GEMM over taps (bf16 out)
 //   6 stages     causal ConvTranspose1d (K = 2 stride) as `stride` GEMMs, one
 //                per output phase r: out[q s + r] = W_r . [x[q] | x[q-1]],
@@ -39,7 +40,8 @@ constexpr int kUpStride[kStages] = {10, 6, 4, 2, 2, 2};
 constexpr int kRbK[3] = {3, 7, 11};
 constexpr int kRbDil[3] = {1, 3, 5};
 constexpr int kHop = 1920;
-constexpr int kLstmH = 512, kLstmCtas = 64, kLstmUnits = kLstmH / kLstmCtas;   // 8 units per CTA
+constexpr int kLstmH = 512, kLstmCtas = 64, kLstmUnits = kLstmH / kLstmCtas;   // CTAs per layer, 8 units each
+constexpr size_t kLstmSmem = (32 * kLstmH + 2 * kLstmH + 32) * sizeof(float);
 
 inline int cpad(int c) { return c <= 64 ? 64 : (c + 63) / 64 * 64; }
 
@@ -80,13 +82,20 @@ void kaiser_sinc(float *f, double cutoff, double half_width, int K) {
 }
 
 // ------------------------------------------------------------------ kernels
-// Activation1d (bigvgan_cpp.cpp:33-124) on a tile of 64 output times x 32
-// channels: x rows t0-11 .. t0+63 staged in shared memory; then
-//   u[j] = 2 sum_{k = j mod 2, k + 2, .., k <= min(j, 11)} fu[k] x[(j - k) / 2]
-//   s[j] = u + sin^2(a u) * inv_b   (0 for a non-finite u, u for a non-finite s)
-// for j in [2 t0 - 11, 2 t0 + 127] (j < 0 repeats s[0]: the replicate pad),
-// then out[t] = sum_k fd[k] s[2t + k - 11].  Channels >= ch are written as 0.
-constexpr int kActT = 64, kActC = 32;
+// Activation1d (bigvgan_cpp.cpp:33-124).  A warp takes 32 channels (one per
+// lane) and 16 consecutive output times t_w .. t_w + 15, entirely in
+// registers:
+//   x[i]  = x at t_w - 11 + i, i < 27 (zero before t = 0)
+//   s[i]  = SnakeBeta(u) at j = 2 t_w - 11 + i, i < 43, where
+//           u[j] = 2 sum_q f_up[2q + (j mod 2)] x[floor(j / 2) - q], q < 6
+//           (ConvTranspose1d x2 trimmed to 2T; x before 0 contributes 0);
+//           s at j < 0 is s at j = 0 (the replicate pad of the down filter)
+//   out[t_w + o] = sum_k f_down[k] s[2o + k]           (conv1d, stride 2)
+// SnakeBeta: u + sin^2(a u) inv_b with a = e^clamp(alpha), inv_b =
+// 1 / (e^clamp(beta) + 1e-9); a non-finite u gives 0, a non-finite result u.
+// sin is the hardware approximation (__sinf: absolute error about 1e-6 for
+// |a u| < 10).  Lanes of channels >= ch write zeros.
+constexpr int kActTW = 16, kActWarps = 8;
 struct ActArgs {
     const float *x; int ldx;
     void *y; int ldy; int y_bf16;
@@ -96,62 +105,74 @@ struct ActArgs {
 };
 
 __device__ __forceinline__ float snake(float u, float a, float ib) {
-    if (isnan(u) || isinf(u)) return 0.f;
-    const float sn = sinf(a * u);
-    const float v = u + ib * sn * sn;
-    return (isnan(v) || isinf(v)) ? u : v;
+    if (!isfinite(u)) return 0.f;
+    const float sn = __sinf(a * u);
+    const float v = fmaf(ib * sn, sn, u);
+    return isfinite(v) ? v : u;
 }
 
-__global__ void __launch_bounds__(256) voc_act_kernel(const ActArgs p) {
-    __shared__ float xs[kActT + 11][kActC];
-    __shared__ float ss[2 * kActT + 11][kActC];
-    const int c0 = blockIdx.x * kActC, t0 = blockIdx.y * kActT;
-    const int tid = threadIdx.x, cl = tid & 31;
-    const int c = c0 + cl;
+__global__ void __launch_bounds__(kActWarps * 32) voc_act_kernel(const ActArgs p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * 32 + lane;
+    const int tw = (blockIdx.y * kActWarps + warp) * kActTW;
+    if (tw >= p.T) return;
     const bool live = c < p.ch;
-    for (int i = tid; i < (kActT + 11) * kActC; i += 256) {
-        const int r = i / kActC, t = t0 - 11 + r;
-        float v = 0.f;
-        if (t >= 0 && t < p.T && c0 + (i % kActC) < p.ch) v = p.x[(long long)t * p.ldx + c0 + (i % kActC)];
-        xs[r][i % kActC] = v;
-    }
-    __syncthreads();
-    float fu[kTaps], fd[kTaps];
-    const float *fup = p.fu + (p.fch == 1 ? 0 : (long long)(live ? c : 0) * kTaps);
-    const float *fdp = p.fd + (p.fch == 1 ? 0 : (long long)(live ? c : 0) * kTaps);
+    const int n_out = min(kActTW, p.T - tw);
+    float o[kActTW];
+    if (__any_sync(0xffffffffu, live)) {
+        float fu[kTaps], fd[kTaps];
+        const float *fup = p.fu + (p.fch == 1 ? 0 : (long long)(live ? c : 0) * kTaps);
+        const float *fdp = p.fd + (p.fch == 1 ? 0 : (long long)(live ? c : 0) * kTaps);
 #pragma unroll
-    for (int k = 0; k < kTaps; k++) { fu[k] = __ldg(fup + k); fd[k] = __ldg(fdp + k); }
-    const float a = live ? __ldg(p.a + c) : 1.f, ib = live ? __ldg(p.inv_b + c) : 1.f;
-    const int j0 = 2 * t0 - 11;
-    for (int jl = tid >> 5; jl < 2 * kActT + 11; jl += 8) {
-        int j = j0 + jl;
-        if (j < 0) j = 0;   // replicate pad: s[j < 0] = s[0]
-        float u = 0.f;
+        for (int k = 0; k < kTaps; k++) { fu[k] = __ldg(fup + k); fd[k] = __ldg(fdp + k); }
+        const float a = live ? __ldg(p.a + c) : 1.f, ib = live ? __ldg(p.inv_b + c) : 1.f;
+        float x[kActTW + 11];
 #pragma unroll
-        for (int k = 0; k < kTaps; k++) {
-            if ((k & 1) != (j & 1) || k > j) continue;
-            u += xs[(j - k) / 2 - (t0 - 11)][cl] * fu[k] * 2.0f;
+        for (int i = 0; i < kActTW + 11; i++) {
+            const int t = tw - 11 + i;
+            x[i] = (live && t >= 0 && t < p.T) ? __ldg(p.x + (long long)t * p.ldx + c) : 0.f;
         }
-        ss[jl][cl] = snake(u, a, ib);
-    }
-    __syncthreads();
-    for (int tl = tid >> 5; tl < kActT; tl += 8) {
-        const int t = t0 + tl;
-        if (t >= p.T) break;
-        float o = 0.f;
+        float s[2 * kActTW + 11];
 #pragma unroll
-        for (int k = 0; k < kTaps; k++) o += ss[2 * tl + k][cl] * fd[k];
-        if (!live) o = 0.f;
-        if (c < p.ldy) {
-            if (p.y_bf16) reinterpret_cast<bf16 *>(p.y)[(long long)t * p.ldy + c] = __float2bfloat16_rn(o);
-            else reinterpret_cast<float *>(p.y)[(long long)t * p.ldy + c] = o;
+        for (int i = 0; i < 2 * kActTW + 11; i++) {
+            // j = 2 t_w - 11 + i is odd for even i: taps 1, 3, .., 11 on x[i/2 + 5 - q];
+            // even for odd i: taps 0, 2, .., 10 on x[(i - 1)/2 + 6 - q]
+            float u = 0.f;
+#pragma unroll
+            for (int q = 0; q < 6; q++) {
+                if (i % 2 == 0) u = fmaf(x[i / 2 + 5 - q], fu[2 * q + 1], u);
+                else u = fmaf(x[(i - 1) / 2 + 6 - q], fu[2 * q], u);
+            }
+            s[i] = snake(2.0f * u, a, ib);
         }
+        if (tw == 0) {
+#pragma unroll
+            for (int i = 0; i < 11; i++) s[i] = s[11];   // j < 0: replicate s[0]
+        }
+#pragma unroll
+        for (int q = 0; q < kActTW; q++) {
+            float v = 0.f;
+#pragma unroll
+            for (int k = 0; k < kTaps; k++) v = fmaf(s[2 * q + k], fd[k], v);
+            o[q] = live ? v : 0.f;
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < kActTW; q++) o[q] = 0.f;
+    }
+    if (c >= p.ldy) return;
+#pragma unroll
+    for (int q = 0; q < kActTW; q++) {
+        if (q >= n_out) break;
+        const long long off = (long long)(tw + q) * p.ldy + c;
+        if (p.y_bf16) reinterpret_cast<bf16 *>(p.y)[off] = __float2bfloat16_rn(o[q]);
+        else reinterpret_cast<float *>(p.y)[off] = o[q];
     }
 }
 
 void launch_act(const ActArgs &p, int cp, cudaStream_t s) {
-    dim3 grid((cp + kActC - 1) / kActC, (p.T + kActT - 1) / kActT);
-    voc_act_kernel<<<grid, 256, 0, s>>>(p);
+    dim3 grid((cp + 31) / 32, (p.T + kActTW * kActWarps - 1) / (kActTW * kActWarps));
+    voc_act_kernel<<<grid, kActWarps * 32, 0, s>>>(p);
 }
 
 // x = (r0 + r1 + r2) / 3 (bigvgan_cpp.cpp:485-494), as bf16 and optionally fp32
@@ -183,63 +204,89 @@ __global__ void voc_post_kernel(const float *__restrict__ x, int ldx, int T, int
     audio[t] = tanhf(s) * 1.92f;
 }
 
-// One LSTM layer's recurrence (lstm.cpp:12-50): gin [T][2048] holds
-// x W_ih^T + b_ih + b_hh for every step; CTA b owns hidden units 8b .. 8b+7,
-// i.e. W_hh rows g * 512 + 8b + i (gates i, f, g, o), kept in shared memory.
-// Each step reads h[t-1] from L2, writes its 8 units of h[t], then meets the
-// other CTAs at a grid barrier (a counter; bounded wait, error code on expiry).
-// Launched cooperatively so that all CTAs are resident.
+// The 4-layer LSTM (lstm.cpp:12-104) as one wavefront: at global step tau,
+// layer l advances its time step t = tau - l, so the four layers run together
+// and the recurrence takes T + 3 steps instead of 4 T.  CTA b serves layer
+// l = b / 64 and hidden units 8 (b mod 64) .. +7: it keeps their 32 W_hh rows
+// (gates i, f, g, o) in shared memory; layers 1..3 read their 32 W_ih rows
+// from global memory (L2-resident) each step.  Layer 0's input projection
+// (x W_ih^T + b_ih + b_hh for every t) is precomputed in gin0.  Each step
+// reads h^l[t-1] and h^(l-1)[t] from L2 (written the step before), writes its
+// units of h^l[t], then meets every CTA at a grid barrier (a counter; bounded
+// wait, error code on expiry).  Launched cooperatively (all CTAs resident).
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
-__global__ void __launch_bounds__(256) voc_lstm_kernel(const float *__restrict__ gin, const float *__restrict__ w_hh,
-                                                       float *h_out, int T, unsigned *bar, int *err) {
+struct LstmArgs {
+    const float *gin0;                 // [T][2048] layer-0 input projection + biases
+    const float *w_ih[4], *w_hh[4];    // [2048][512]
+    const float *b_g[4];               // [2048] b_ih + b_hh
+    float *h;                          // [4][T][512]
+    int T;
+    unsigned *bar;
+    int *err;
+};
+
+__global__ void __launch_bounds__(256) voc_lstm_kernel(const LstmArgs p) {
     extern __shared__ float sm[];
-    float *w = sm;                        // [32][512]
-    float *hs = sm + 32 * kLstmH;         // [512]
-    float *gs = hs + kLstmH;              // [32]
+    float *w = sm;                        // [32][512] W_hh rows of this CTA
+    float *hs = sm + 32 * kLstmH;         // h^l[t-1]
+    float *xs = hs + kLstmH;              // h^(l-1)[t]
+    float *gs = xs + kLstmH;              // [32] gate pre-activations
     __shared__ int abort_flag;
-    const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int l = blockIdx.x / kLstmCtas, q0 = (blockIdx.x % kLstmCtas) * kLstmUnits;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float *whh = p.w_hh[l], *wih = p.w_ih[l];
     for (int i = tid; i < 32 * kLstmH; i += 256) {
         const int r = i / kLstmH, k = i % kLstmH;   // r = gate * 8 + unit
-        w[i] = w_hh[(long long)((r >> 3) * kLstmH + b * kLstmUnits + (r & 7)) * kLstmH + k];
+        w[i] = whh[(long long)((r >> 3) * kLstmH + q0 + (r & 7)) * kLstmH + k];
     }
     if (tid == 0) abort_flag = 0;
     float cst = 0.f;
-    for (int t = 0; t < T; t++) {
-        for (int k = tid; k < kLstmH; k += 256) hs[k] = t ? __ldcg(h_out + (long long)(t - 1) * kLstmH + k) : 0.f;
-        __syncthreads();
+    float *hl = p.h + (long long)l * p.T * kLstmH;
+    const float *hprev_layer = l ? p.h + (long long)(l - 1) * p.T * kLstmH : nullptr;
+    for (int tau = 0; tau < p.T + 3; tau++) {
+        const int t = tau - l;
+        if (t >= 0 && t < p.T) {
+            for (int k = tid; k < kLstmH; k += 256) {
+                hs[k] = t ? __ldcg(hl + (long long)(t - 1) * kLstmH + k) : 0.f;
+                if (l) xs[k] = __ldcg(hprev_layer + (long long)t * kLstmH + k);
+            }
+            __syncthreads();
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int r = warp * 4 + q;
-            float acc = 0.f;
-            for (int k = lane; k < kLstmH; k += 32) acc += w[r * kLstmH + k] * hs[k];
-            acc = warp_sum(acc);
-            if (lane == 0) gs[r] = acc;
-        }
-        __syncthreads();
-        if (tid < kLstmUnits) {
-            const int j = b * kLstmUnits + tid;
-            const float *g = gin + (long long)t * 4 * kLstmH;
-            const float gi = g[j] + gs[tid], gf = g[kLstmH + j] + gs[8 + tid];
-            const float gg = g[2 * kLstmH + j] + gs[16 + tid], go = g[3 * kLstmH + j] + gs[24 + tid];
-            const float iv = 1.0f / (1.0f + expf(-gi)), fv = 1.0f / (1.0f + expf(-gf));
-            const float gv = tanhf(gg), ov = 1.0f / (1.0f + expf(-go));
-            cst = fv * cst + iv * gv;
-            h_out[(long long)t * kLstmH + j] = ov * tanhf(cst);
+            for (int qq = 0; qq < 4; qq++) {
+                const int r = warp * 4 + qq;
+                const int grow = (r >> 3) * kLstmH + q0 + (r & 7);
+                float acc = 0.f;
+                for (int k = lane; k < kLstmH; k += 32) acc += w[r * kLstmH + k] * hs[k];
+                if (l) {
+                    const float *wr = wih + (long long)grow * kLstmH;
+                    for (int k = lane; k < kLstmH; k += 32) acc += __ldg(wr + k) * xs[k];
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) gs[r] = acc + (l ? __ldg(p.b_g[l] + grow) : p.gin0[(long long)t * 4 * kLstmH + grow]);
+            }
+            __syncthreads();
+            if (tid < kLstmUnits) {
+                const float gi = gs[tid], gf = gs[8 + tid], gg = gs[16 + tid], go = gs[24 + tid];
+                const float iv = 1.0f / (1.0f + expf(-gi)), fv = 1.0f / (1.0f + expf(-gf));
+                const float gv = tanhf(gg), ov = 1.0f / (1.0f + expf(-go));
+                cst = fv * cst + iv * gv;
+                hl[(long long)t * kLstmH + q0 + tid] = ov * tanhf(cst);
+            }
         }
         __syncthreads();
         if (tid == 0) {
             __threadfence();
-            atomicAdd(bar, 1u);
-            const unsigned target = (unsigned)(t + 1) * gridDim.x;
+            atomicAdd(p.bar, 1u);
+            const unsigned target = (unsigned)(tau + 1) * gridDim.x;
             const unsigned long long t0 = globaltimer_ns();
-            while (ld_acquire_u32(bar) < target) {
+            while (ld_acquire_u32(p.bar) < target) {
                 if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                    atomicExch(err, DEVERR_TIMEOUT_BARRIER);
+                    atomicExch(p.err, DEVERR_TIMEOUT_BARRIER);
                     abort_flag = 1;
                     break;
                 }
@@ -304,6 +351,10 @@ GemmOp conv_op(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K
 struct dtts_voc {
     int device = 0, num_sms = 148, max_frames = 0;
     cudaStream_t own_stream = nullptr, stream = nullptr;
+    // the three AMP blocks of a stage are independent until their mean: blocks
+    // 1 and 2 run on side streams, forked from and joined back into `stream`
+    cudaStream_t side[2] = {nullptr, nullptr};
+    cudaEvent_t ev_fork = nullptr, ev_join[2] = {nullptr, nullptr};
     DeviceArena wts, ws;
     int *d_err = nullptr;
     unsigned *d_bar = nullptr;
@@ -313,29 +364,38 @@ struct dtts_voc {
     // convolutions (bf16 B operands [N][taps * cp_in]) and biases (fp32, padded)
     bf16 *w_pre = nullptr; float *b_pre = nullptr; CUtensorMap t_pre;
     bf16 *w_up[kStages] = {}; float *b_up[kStages] = {};
-    std::vector<CUtensorMap> t_up[kStages];               // one per output phase
+    CUtensorMap t_up[kStages][2];                         // all phases stacked along N; boxes of 64 / 128 rows
     bf16 *w_c1[kRb][3] = {}, *w_c2[kRb][3] = {};
     float *b_c1[kRb][3] = {}, *b_c2[kRb][3] = {};
-    CUtensorMap t_c1[kRb][3], t_c2[kRb][3];
+    CUtensorMap t_c1[kRb][3][2], t_c2[kRb][3][2];          // boxes of 64 / 128 rows
     float *act_a[kRb][6] = {}, *act_ib[kRb][6] = {};
     float *aa = nullptr;                                  // [12] AMP filter
     float *post_a = nullptr, *post_ib = nullptr, *post_fu = nullptr, *post_fd = nullptr, *post_w = nullptr;
     // workspace
-    float *lat = nullptr, *pp = nullptr, *z = nullptr, *gin = nullptr, *hl[2] = {}, *bott = nullptr, *audio = nullptr;
+    float *lat = nullptr, *pp = nullptr, *z = nullptr, *gin = nullptr, *hl = nullptr, *sk = nullptr, *bott = nullptr;
+    float *audio = nullptr;
     bf16 *bott16 = nullptr, *x0 = nullptr;                // conv_pre in / out
-    float *r[3] = {}, *y = nullptr, *xf = nullptr;        // stage buffers, fp32
-    bf16 *a16 = nullptr, *xin = nullptr;                  // GEMM A operands
+    float *r[3] = {}, *y[3] = {}, *xf = nullptr;          // stage buffers (one residual + scratch per block), fp32
+    bf16 *a16[3] = {}, *xin = nullptr;                    // GEMM A operands
     size_t stage_elems = 0;
     int maps_T0 = -1;                                     // n_frames the activation maps were encoded for
-    CUtensorMap t_bott, t_x0, t_xin[kStages], t_a[kStages], t_r[kStages][3];
+    CUtensorMap t_bott, t_x0, t_xin[kStages], t_a[kStages][3], t_r[kStages][3];
 
     ~dtts_voc() {
         ws.free_all();
         wts.free_all();
+        for (int i = 0; i < 2; i++) {
+            if (side[i]) cudaStreamDestroy(side[i]);
+            if (ev_join[i]) cudaEventDestroy(ev_join[i]);
+        }
+        if (ev_fork) cudaEventDestroy(ev_fork);
         if (own_stream) cudaStreamDestroy(own_stream);
     }
 
-    static int bn_for(int n) { return n % 128 == 0 ? 128 : 64; }
+    // 128-wide tiles only when they still fill every SM at least twice
+    int bn_for(long long M, int N) const {
+        return (N % 128 == 0 && ((M + 127) / 128) * (N / 128) >= 2LL * num_sms) ? 128 : 64;
+    }
 
     int alloc_ws() {
         const size_t F = (size_t)max_frames;
@@ -350,15 +410,17 @@ struct dtts_voc {
         pp = (float *)ws.alloc(F * 128 * 4);
         z = (float *)ws.alloc(F * kLstmH * 4);
         gin = (float *)ws.alloc(F * 4 * kLstmH * 4);
-        hl[0] = (float *)ws.alloc(F * kLstmH * 4);
-        hl[1] = (float *)ws.alloc(F * kLstmH * 4);
+        hl = (float *)ws.alloc(4 * F * kLstmH * 4);
+        sk = (float *)ws.alloc(F * kLstmH * 4);
         bott = (float *)ws.alloc(F * 128 * 4);
         bott16 = (bf16 *)ws.alloc(F * 128 * 2);
         x0 = (bf16 *)ws.alloc(F * 1536 * 2);
         for (int j = 0; j < 3; j++) r[j] = (float *)ws.alloc(mx * 4);
-        y = (float *)ws.alloc(mx * 4);
+        for (int j = 0; j < 3; j++) {
+            y[j] = (float *)ws.alloc(mx * 4);
+            a16[j] = (bf16 *)ws.alloc(mx * 2);
+        }
         xf = (float *)ws.alloc(mx * 4);
-        a16 = (bf16 *)ws.alloc(mx * 2);
         xin = (bf16 *)ws.alloc(mx * 2);
         audio = (float *)ws.alloc(F * kHop * 4);
         for (void *p : ws.ptrs)
@@ -376,8 +438,8 @@ struct dtts_voc {
             const int cin = s == 0 ? 1536 : cpad(kUpOut[s - 1]), cp = cpad(kUpOut[s]);
             const long long T = Tin * kUpStride[s];
             if (s > 0) ok = ok && make_tmap_bf16(&t_xin[s], xin, Tin, cin, 128);
-            ok = ok && make_tmap_bf16(&t_a[s], a16, T, cp, 128);
-            for (int j = 0; j < 3 && ok; j++) ok = make_tmap_f32_resid(&t_r[s][j], r[j], T, cp);
+            for (int j = 0; j < 3 && ok; j++)
+                ok = make_tmap_bf16(&t_a[s][j], a16[j], T, cp, 128) && make_tmap_f32_resid(&t_r[s][j], r[j], T, cp);
             Tin = T;
         }
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (vocoder activations, %d frames)", T0);
@@ -385,20 +447,47 @@ struct dtts_voc {
         return DTTS_OK;
     }
 
-    int gemm(const GemmOp &op) {
-        DTTS_CUDA(launch_gemm(op, num_sms, stream));
+    int gemm(const GemmOp &op, cudaStream_t s) {
+        DTTS_CUDA(launch_gemm(op, num_sms, s));
         return DTTS_OK;
     }
 
-    int lstm_layer(const float *w_hh_l, float *h_out, int T) {
+    // AMP block j of stage s: r[j] += c2(act(c1(act(r[j])))) for dilations 1, 3, 5 (:427-483)
+    int amp_block(int s, int j, long long T, cudaStream_t strm) {
+        const int cp = cpad(kUpOut[s]), ch = kUpOut[s], rb = s * 3 + j, K = kRbK[j];
+        const int bn = bn_for(T, cp), bi = bn == 128 ? 1 : 0;
+        int st;
+        for (int p = 0; p < 3; p++) {
+            ActArgs aa1{r[j], cp, a16[j], cp, 1, (int)T, ch, act_a[rb][2 * p], act_ib[rb][2 * p], aa, aa, 1};
+            launch_act(aa1, cp, strm);
+            {
+                GemmOp op = conv_op(t_a[s][j], t_c1[rb][p][bi], (int)T, cp, K * cp, EPI_F32, bn, d_err);
+                op.ep.bias = b_c1[rb][p]; op.ep.out = y[j]; op.ep.ldo = cp;
+                op.ep.tap_kb = cp / 64; op.ep.tap_base = -kRbDil[p] * (K - 1); op.ep.tap_step = kRbDil[p];
+                if ((st = gemm(op, strm))) return st;
+            }
+            ActArgs aa2{y[j], cp, a16[j], cp, 1, (int)T, ch, act_a[rb][2 * p + 1], act_ib[rb][2 * p + 1], aa, aa, 1};
+            launch_act(aa2, cp, strm);
+            {
+                GemmOp op = conv_op(t_a[s][j], t_c2[rb][p][bi], (int)T, cp, K * cp, EPI_RESID, bn, d_err);
+                op.tr = t_r[s][j];
+                op.ep.bias = b_c2[rb][p]; op.ep.resid = r[j]; op.ep.ldr = cp;
+                op.ep.tap_kb = cp / 64; op.ep.tap_base = -(K - 1); op.ep.tap_step = 1;
+                if ((st = gemm(op, strm))) return st;
+            }
+        }
+        return DTTS_OK;
+    }
+
+    int lstm(int T) {
         DTTS_CUDA(cudaMemsetAsync(d_bar, 0, sizeof(unsigned), stream));
-        const float *g = gin;
-        unsigned *bar = d_bar;
-        int *err = d_err;
-        void *args[] = {(void *)&g, (void *)&w_hh_l, (void *)&h_out, (void *)&T, (void *)&bar, (void *)&err};
-        const size_t smem = (32 * kLstmH + kLstmH + 32) * sizeof(float);
-        DTTS_CUDA(cudaLaunchCooperativeKernel((const void *)voc_lstm_kernel, dim3(kLstmCtas), dim3(256), args, smem,
-                                              stream));
+        LstmArgs a{};
+        a.gin0 = gin;
+        for (int l = 0; l < 4; l++) { a.w_ih[l] = w_ih[l]; a.w_hh[l] = w_hh[l]; a.b_g[l] = b_g[l]; }
+        a.h = hl; a.T = T; a.bar = d_bar; a.err = d_err;
+        void *args[] = {(void *)&a};
+        DTTS_CUDA(cudaLaunchCooperativeKernel((const void *)voc_lstm_kernel, dim3(4 * kLstmCtas), dim3(256), args,
+                                              kLstmSmem, stream));
         return DTTS_OK;
     }
 
@@ -408,60 +497,45 @@ struct dtts_voc {
         // ---- bottleneck (bigvgan_cpp.cpp:344-377)
         launch_gemm_f32(lat, pp_w, pp_b, pp, T0, 128, 128, stream);
         launch_gemm_f32(pp, mi_w1, mi_b1, z, T0, kLstmH, 128, stream);
-        const float *in = z;
-        for (int l = 0; l < 4; l++) {
-            launch_gemm_f32(in, w_ih[l], b_g[l], gin, T0, 4 * kLstmH, kLstmH, stream);
-            if ((st = lstm_layer(w_hh[l], hl[l & 1], T0))) return st;
-            in = hl[l & 1];
-        }
-        launch_add_f32(z, hl[1], hl[0], (long long)T0 * kLstmH, stream);   // skip: z + h of the last layer
-        launch_gemm_f32(hl[0], mi_w2, mi_b2, bott, T0, 128, kLstmH, stream);
+        launch_gemm_f32(z, w_ih[0], b_g[0], gin, T0, 4 * kLstmH, kLstmH, stream);
+        if ((st = lstm(T0))) return st;
+        // skip: z + h of the last layer
+        launch_add_f32(z, hl + (size_t)3 * T0 * kLstmH, sk, (long long)T0 * kLstmH, stream);
+        launch_gemm_f32(sk, mi_w2, mi_b2, bott, T0, 128, kLstmH, stream);
         launch_f32_to_bf16(bott, bott16, (long long)T0 * 128, stream);
         // ---- conv_pre: centred K = 5 (taps at t - 2 .. t + 2), bf16 out (:384-405)
         {
             GemmOp op = conv_op(t_bott, t_pre, T0, 1536, 5 * 128, EPI_BF16, 128, d_err);
             op.ep.bias = b_pre; op.ep.out = x0; op.ep.ldo = 1536;
             op.ep.tap_kb = 2; op.ep.tap_base = -2; op.ep.tap_step = 1;
-            if ((st = gemm(op))) return st;
+            if ((st = gemm(op, stream))) return st;
         }
         long long Tin = T0;
         for (int s = 0; s < kStages; s++) {
             const int cin = s == 0 ? 1536 : cpad(kUpOut[s - 1]), cp = cpad(kUpOut[s]), ch = kUpOut[s];
             const int str = kUpStride[s];
             const long long T = Tin * str;
-            const int bn = bn_for(cp);
-            // ---- causal ConvTranspose1d, one GEMM per output phase (:176-205, :415-420)
-            for (int ph = 0; ph < str; ph++) {
-                GemmOp op = conv_op(s == 0 ? t_x0 : t_xin[s], t_up[s][ph], (int)Tin, cp, 2 * cin, EPI_F32, bn, d_err);
-                op.ep.bias = b_up[s]; op.ep.out = r[0] + (size_t)ph * cp; op.ep.ldo = (long long)str * cp;
+            // ---- causal ConvTranspose1d as one GEMM: the output phases stacked along N
+            // (row q of [T_in][stride * cp] is rows q stride .. q stride + stride-1 of
+            // [T][cp]), each phase's K = [x[q] | x[q-1]] (:176-205, :415-420)
+            {
+                const int N = str * cp, bn = bn_for(Tin, N);
+                GemmOp op = conv_op(s == 0 ? t_x0 : t_xin[s], t_up[s][bn == 128], (int)Tin, N, 2 * cin, EPI_F32, bn, d_err);
+                op.ep.bias = b_up[s]; op.ep.out = r[0]; op.ep.ldo = N;
                 op.ep.tap_kb = cin / 64; op.ep.tap_base = 0; op.ep.tap_step = -1;
-                if ((st = gemm(op))) return st;
+                if ((st = gemm(op, stream))) return st;
             }
             const size_t n = (size_t)T * cp;
             DTTS_CUDA(cudaMemcpyAsync(r[1], r[0], n * 4, cudaMemcpyDeviceToDevice, stream));
             DTTS_CUDA(cudaMemcpyAsync(r[2], r[0], n * 4, cudaMemcpyDeviceToDevice, stream));
-            // ---- three AMP blocks (:427-483)
-            for (int j = 0; j < 3; j++) {
-                const int rb = s * 3 + j, K = kRbK[j];
-                for (int p = 0; p < 3; p++) {
-                    ActArgs aa1{r[j], cp, a16, cp, 1, (int)T, ch, act_a[rb][2 * p], act_ib[rb][2 * p], aa, aa, 1};
-                    launch_act(aa1, cp, stream);
-                    {
-                        GemmOp op = conv_op(t_a[s], t_c1[rb][p], (int)T, cp, K * cp, EPI_F32, bn, d_err);
-                        op.ep.bias = b_c1[rb][p]; op.ep.out = y; op.ep.ldo = cp;
-                        op.ep.tap_kb = cp / 64; op.ep.tap_base = -kRbDil[p] * (K - 1); op.ep.tap_step = kRbDil[p];
-                        if ((st = gemm(op))) return st;
-                    }
-                    ActArgs aa2{y, cp, a16, cp, 1, (int)T, ch, act_a[rb][2 * p + 1], act_ib[rb][2 * p + 1], aa, aa, 1};
-                    launch_act(aa2, cp, stream);
-                    {
-                        GemmOp op = conv_op(t_a[s], t_c2[rb][p], (int)T, cp, K * cp, EPI_RESID, bn, d_err);
-                        op.tr = t_r[s][j];
-                        op.ep.bias = b_c2[rb][p]; op.ep.resid = r[j]; op.ep.ldr = cp;
-                        op.ep.tap_kb = cp / 64; op.ep.tap_base = -(K - 1); op.ep.tap_step = 1;
-                        if ((st = gemm(op))) return st;
-                    }
-                }
+            // ---- three AMP blocks, concurrently (:427-483)
+            DTTS_CUDA(cudaEventRecord(ev_fork, stream));
+            for (int i = 0; i < 2; i++) DTTS_CUDA(cudaStreamWaitEvent(side[i], ev_fork, 0));
+            for (int j = 0; j < 3; j++)
+                if ((st = amp_block(s, j, T, j == 0 ? stream : side[j - 1]))) return st;
+            for (int i = 0; i < 2; i++) {
+                DTTS_CUDA(cudaEventRecord(ev_join[i], side[i]));
+                DTTS_CUDA(cudaStreamWaitEvent(stream, ev_join[i], 0));
             }
             const long long n4 = (long long)(n / 4);
             const bool last = s == kStages - 1;
@@ -472,9 +546,9 @@ struct dtts_voc {
         }
         // ---- activation_post, conv_post, tanh (:499-521)
         const int cp = cpad(24);
-        ActArgs ap{xf, cp, y, cp, 0, (int)Tin, 24, post_a, post_ib, post_fu, post_fd, 24};
+        ActArgs ap{xf, cp, y[0], cp, 0, (int)Tin, 24, post_a, post_ib, post_fu, post_fd, 24};
         launch_act(ap, cp, stream);
-        voc_post_kernel<<<(unsigned)((Tin + 255) / 256), 256, 0, stream>>>(y, cp, (int)Tin, 24, post_w, audio);
+        voc_post_kernel<<<(unsigned)((Tin + 255) / 256), 256, 0, stream>>>(y[0], cp, (int)Tin, 24, post_w, audio);
         DTTS_CUDA(cudaGetLastError());
         return DTTS_OK;
     }
@@ -540,9 +614,14 @@ int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_
     v->device = device; v->num_sms = nsm; v->max_frames = max_frames;
     DTTS_CUDA(cudaStreamCreateWithFlags(&v->own_stream, cudaStreamNonBlocking));
     v->stream = v->own_stream;
+    for (int i = 0; i < 2; i++) {
+        DTTS_CUDA(cudaStreamCreateWithFlags(&v->side[i], cudaStreamNonBlocking));
+        DTTS_CUDA(cudaEventCreateWithFlags(&v->ev_join[i], cudaEventDisableTiming));
+    }
+    DTTS_CUDA(cudaEventCreateWithFlags(&v->ev_fork, cudaEventDisableTiming));
     DTTS_CUDA(gemm_prepare_attributes());
     DTTS_CUDA(cudaFuncSetAttribute((const void *)voc_lstm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (32 * kLstmH + kLstmH + 32) * (int)sizeof(float)));
+                                   (int)kLstmSmem));
     DeviceArena &A = v->wts;
     v->d_err = (int *)A.alloc(4);
     v->d_bar = (unsigned *)A.alloc(4);
@@ -580,22 +659,27 @@ int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_
                     for (int c = 0; c < ic; c++)
                         bop[(((size_t)ph * cpo + o) * 2 + j) * cpi + c] = w->ups_w[s][((size_t)c * oc + o) * K + ph + j * str];
         if ((st = up_bf16(A, bop, &v->w_up[s]))) return st;
-        if ((st = up_f32_pad(A, w->ups_b[s], oc, cpo, &v->b_up[s]))) return st;
-        v->t_up[s].resize(str);
-        const int bn = dtts_voc::bn_for(cpo);
-        for (int ph = 0; ph < str && ok; ph++)
-            ok = make_tmap_bf16(&v->t_up[s][ph], v->w_up[s] + (size_t)ph * cpo * 2 * cpi, cpo, 2 * cpi, bn);
+        // bias per output column of the stacked phases: b[o] at column ph * cpo + o
+        std::vector<float> bias((size_t)str * cpo, 0.f);
+        for (int ph = 0; ph < str; ph++)
+            for (int o = 0; o < oc; o++) bias[(size_t)ph * cpo + o] = w->ups_b[s] ? w->ups_b[s][o] : 0.f;
+        if ((st = up_f32(A, bias.data(), bias.size(), &v->b_up[s]))) return st;
+        ok = make_tmap_bf16(&v->t_up[s][0], v->w_up[s], (size_t)str * cpo, 2 * cpi, 64) &&
+             make_tmap_bf16(&v->t_up[s][1], v->w_up[s], (size_t)str * cpo, 2 * cpi, 128);
     }
     // AMP blocks
     for (int rb = 0; rb < kRb && ok; rb++) {
-        const int ch = kUpOut[rb / 3], cp = cpad(ch), K = kRbK[rb % 3], bn = dtts_voc::bn_for(cp);
+        const int ch = kUpOut[rb / 3], cp = cpad(ch), K = kRbK[rb % 3];
         for (int j = 0; j < 3 && ok; j++) {
             if ((st = up_bf16(A, conv_b_operand(w->c1_w[rb][j], ch, ch, K, cp, cp), &v->w_c1[rb][j]))) return st;
             if ((st = up_bf16(A, conv_b_operand(w->c2_w[rb][j], ch, ch, K, cp, cp), &v->w_c2[rb][j]))) return st;
             if ((st = up_f32_pad(A, w->c1_b[rb][j], ch, cp, &v->b_c1[rb][j]))) return st;
             if ((st = up_f32_pad(A, w->c2_b[rb][j], ch, cp, &v->b_c2[rb][j]))) return st;
-            ok = make_tmap_bf16(&v->t_c1[rb][j], v->w_c1[rb][j], cp, (size_t)K * cp, bn) &&
-                 make_tmap_bf16(&v->t_c2[rb][j], v->w_c2[rb][j], cp, (size_t)K * cp, bn);
+            for (int bi = 0; bi < 2 && ok; bi++) {
+                const unsigned box = (bi && cp % 128 == 0) ? 128 : 64;   // 128-wide tiles need cp % 128 == 0
+                ok = make_tmap_bf16(&v->t_c1[rb][j][bi], v->w_c1[rb][j], cp, (size_t)K * cp, box) &&
+                     make_tmap_bf16(&v->t_c2[rb][j][bi], v->w_c2[rb][j], cp, (size_t)K * cp, box);
+            }
         }
         for (int a = 0; a < 6; a++) {
             std::vector<float> av, ib;
