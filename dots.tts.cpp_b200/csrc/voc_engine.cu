@@ -189,18 +189,25 @@ __global__ void voc_mean3_kernel(const float4 *__restrict__ r0, const float4 *__
 }
 
 // conv_post (Conv1d(24, 1, 7), causal, no bias) and tanh x 1.92
-// (bigvgan_cpp.cpp:509-521): one thread per output sample
-__global__ void voc_post_kernel(const float *__restrict__ x, int ldx, int T, int ch, const float *__restrict__ w,
-                                float *__restrict__ audio) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+// (bigvgan_cpp.cpp:509-521): a block stages rows t0-6 .. t0+255 of the first
+// 24 channels in shared memory, then one thread per output sample.
+constexpr int kPostT = 256;
+__global__ void __launch_bounds__(kPostT) voc_post_kernel(const float *__restrict__ x, int ldx, int T,
+                                                          const float *__restrict__ w, float *__restrict__ audio) {
+    __shared__ float xs[kPostT + 6][24];
+    __shared__ float ws[24 * 7];
+    const int t0 = blockIdx.x * kPostT;
+    for (int i = threadIdx.x; i < (kPostT + 6) * 24; i += kPostT) {
+        const int r = i / 24, c = i % 24, t = t0 - 6 + r;
+        xs[r][c] = (t >= 0 && t < T) ? x[(long long)t * ldx + c] : 0.f;
+    }
+    if (threadIdx.x < 24 * 7) ws[threadIdx.x] = w[threadIdx.x];
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
     if (t >= T) return;
     float s = 0.f;
-    for (int k = 0; k < 7; k++) {
-        const int ts = t + k - 6;
-        if (ts < 0) continue;
-        const float *xr = x + (long long)ts * ldx;
-        for (int c = 0; c < ch; c++) s += xr[c] * __ldg(w + c * 7 + k);
-    }
+    for (int k = 0; k < 7; k++)
+        for (int c = 0; c < 24; c++) s += xs[threadIdx.x + k][c] * ws[c * 7 + k];
     audio[t] = tanhf(s) * 1.92f;
 }
 
@@ -256,18 +263,33 @@ __global__ void __launch_bounds__(256) voc_lstm_kernel(const LstmArgs p) {
                 if (l) xs[k] = __ldcg(hprev_layer + (long long)t * kLstmH + k);
             }
             __syncthreads();
+            // warp w: rows 4w .. 4w+3, their W_ih loads all issued together
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            int grow[4];
 #pragma unroll
             for (int qq = 0; qq < 4; qq++) {
                 const int r = warp * 4 + qq;
-                const int grow = (r >> 3) * kLstmH + q0 + (r & 7);
-                float acc = 0.f;
-                for (int k = lane; k < kLstmH; k += 32) acc += w[r * kLstmH + k] * hs[k];
-                if (l) {
-                    const float *wr = wih + (long long)grow * kLstmH;
-                    for (int k = lane; k < kLstmH; k += 32) acc += __ldg(wr + k) * xs[k];
+                grow[qq] = (r >> 3) * kLstmH + q0 + (r & 7);
+            }
+            if (l) {
+#pragma unroll
+                for (int k = lane; k < kLstmH; k += 32) {
+                    const float xv = xs[k];
+#pragma unroll
+                    for (int qq = 0; qq < 4; qq++) acc[qq] += __ldg(wih + (long long)grow[qq] * kLstmH + k) * xv;
                 }
-                acc = warp_sum(acc);
-                if (lane == 0) gs[r] = acc + (l ? __ldg(p.b_g[l] + grow) : p.gin0[(long long)t * 4 * kLstmH + grow]);
+            }
+#pragma unroll
+            for (int k = lane; k < kLstmH; k += 32) {
+                const float hv = hs[k];
+#pragma unroll
+                for (int qq = 0; qq < 4; qq++) acc[qq] += w[(warp * 4 + qq) * kLstmH + k] * hv;
+            }
+#pragma unroll
+            for (int qq = 0; qq < 4; qq++) {
+                const float v = warp_sum(acc[qq]);
+                if (lane == 0)
+                    gs[warp * 4 + qq] = v + (l ? __ldg(p.b_g[l] + grow[qq]) : p.gin0[(long long)t * 4 * kLstmH + grow[qq]]);
             }
             __syncthreads();
             if (tid < kLstmUnits) {
@@ -367,7 +389,7 @@ struct dtts_voc {
     CUtensorMap t_up[kStages][2];                         // all phases stacked along N; boxes of 64 / 128 rows
     bf16 *w_c1[kRb][3] = {}, *w_c2[kRb][3] = {};
     float *b_c1[kRb][3] = {}, *b_c2[kRb][3] = {};
-    CUtensorMap t_c1[kRb][3][2], t_c2[kRb][3][2];          // boxes of 64 / 128 rows
+    CUtensorMap t_c1[kRb][3][3], t_c2[kRb][3][3];          // boxes of 64 / 128 / 192 rows (tile widths)
     float *act_a[kRb][6] = {}, *act_ib[kRb][6] = {};
     float *aa = nullptr;                                  // [12] AMP filter
     float *post_a = nullptr, *post_ib = nullptr, *post_fu = nullptr, *post_fd = nullptr, *post_w = nullptr;
@@ -392,9 +414,13 @@ struct dtts_voc {
         if (own_stream) cudaStreamDestroy(own_stream);
     }
 
-    // 128-wide tiles only when they still fill every SM at least twice
+    // the widest tile (192 or 128) that still gives every SM a tile (the three
+    // AMP blocks run concurrently); else 64
     int bn_for(long long M, int N) const {
-        return (N % 128 == 0 && ((M + 127) / 128) * (N / 128) >= 2LL * num_sms) ? 128 : 64;
+        const long long mt = (M + 127) / 128;
+        if (N % 192 == 0 && N % 128 != 0 && mt * (N / 192) * 3 >= num_sms) return 192;
+        if (N % 128 == 0 && mt * (N / 128) * 3 >= num_sms) return 128;
+        return 64;
     }
 
     int alloc_ws() {
@@ -455,7 +481,7 @@ struct dtts_voc {
     // AMP block j of stage s: r[j] += c2(act(c1(act(r[j])))) for dilations 1, 3, 5 (:427-483)
     int amp_block(int s, int j, long long T, cudaStream_t strm) {
         const int cp = cpad(kUpOut[s]), ch = kUpOut[s], rb = s * 3 + j, K = kRbK[j];
-        const int bn = bn_for(T, cp), bi = bn == 128 ? 1 : 0;
+        const int bn = bn_for(T, cp), bi = bn == 192 ? 2 : bn == 128 ? 1 : 0;
         int st;
         for (int p = 0; p < 3; p++) {
             ActArgs aa1{r[j], cp, a16[j], cp, 1, (int)T, ch, act_a[rb][2 * p], act_ib[rb][2 * p], aa, aa, 1};
@@ -548,7 +574,7 @@ struct dtts_voc {
         const int cp = cpad(24);
         ActArgs ap{xf, cp, y[0], cp, 0, (int)Tin, 24, post_a, post_ib, post_fu, post_fd, 24};
         launch_act(ap, cp, stream);
-        voc_post_kernel<<<(unsigned)((Tin + 255) / 256), 256, 0, stream>>>(y[0], cp, (int)Tin, 24, post_w, audio);
+        voc_post_kernel<<<(unsigned)((Tin + kPostT - 1) / kPostT), kPostT, 0, stream>>>(y[0], cp, (int)Tin, post_w, audio);
         DTTS_CUDA(cudaGetLastError());
         return DTTS_OK;
     }
@@ -675,8 +701,9 @@ int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_
             if ((st = up_bf16(A, conv_b_operand(w->c2_w[rb][j], ch, ch, K, cp, cp), &v->w_c2[rb][j]))) return st;
             if ((st = up_f32_pad(A, w->c1_b[rb][j], ch, cp, &v->b_c1[rb][j]))) return st;
             if ((st = up_f32_pad(A, w->c2_b[rb][j], ch, cp, &v->b_c2[rb][j]))) return st;
-            for (int bi = 0; bi < 2 && ok; bi++) {
-                const unsigned box = (bi && cp % 128 == 0) ? 128 : 64;   // 128-wide tiles need cp % 128 == 0
+            for (int bi = 0; bi < 3 && ok; bi++) {
+                const unsigned wide = bi == 2 ? 192 : 128;   // a tile width is usable when it divides cp
+                const unsigned box = (bi && cp % wide == 0) ? wide : 64;
                 ok = make_tmap_bf16(&v->t_c1[rb][j][bi], v->w_c1[rb][j], cp, (size_t)K * cp, box) &&
                      make_tmap_bf16(&v->t_c2[rb][j][bi], v->w_c2[rb][j], cp, (size_t)K * cp, box);
             }
