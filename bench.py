@@ -59,6 +59,7 @@ def parse():
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-pe", action="store_true", help="skip the PatchEncoder stream measurement")
     ap.add_argument("--no-llm", action="store_true", help="skip the LLM decoder step measurement")
+    ap.add_argument("--no-voc", action="store_true", help="skip the BigVGAN decoder measurement")
     return ap.parse_args()
 
 
@@ -436,6 +437,74 @@ def measure_llm(args, local_rank):
             "step_weight_stream_gbs": weight_bytes / (st_ms / 1000.0) / 1e9, "dtype": "bf16"}
 
 
+def measure_voc(args, local_rank, cpu_sample):
+    """BigVGAN decoder on one utterance of 250 latent frames (20 s of 24 kHz
+    audio): device-resident latents, CUDA events on the engine stream, 2
+    warm-up and 5 timed decodes; e2e through host buffers (the C ABI call
+    with its copies), 3 decodes.  cpu_sample: time the reference's own
+    bigvgan_decode on one frame on the host (oracle/_ref), if present."""
+    import time
+    import torch
+    import dtts
+    import synth
+    dev = torch.device("cuda", local_rank)
+    F, reps = 250, 5
+    w = synth.voc_weights(5, aa_filter=dtts.voc_aa_filter())
+    v = dtts.Vocoder(w, max_frames=F, device=local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    v.set_stream(stream.cuda_stream)
+    lat_h = synth.normal(9, "voc.bench", (F, 128), 1.0)
+    lat = torch.from_numpy(lat_h).to(dev)
+    out = torch.empty(F * 1920, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            v.decode(lat, out=out, mem=dtts.MEM_DEVICE)
+        ev[0].record(stream)
+        for _ in range(reps):
+            v.decode(lat, out=out, mem=dtts.MEM_DEVICE)
+        ev[1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / reps
+    audio_s = F * 1920 / 24000.0
+    pin_in = torch.from_numpy(lat_h).pin_memory()
+    pin_out = torch.empty(F * 1920, dtype=torch.float32).pin_memory()
+    t0 = time.perf_counter()
+    for _ in range(3):
+        v.decode(pin_in.numpy(), out=pin_out.numpy(), mem=dtts.MEM_HOST)
+    e2e_ms = (time.perf_counter() - t0) / 3 * 1000.0
+    v.close()
+    res = {"workload": f"BigVGAN decoder, one utterance of {F} latent frames ({audio_s:.0f} s of 24 kHz audio)",
+           "ms_per_decode": ms, "audio_s_per_s": audio_s / (ms / 1000.0),
+           "e2e": {"ms_per_decode": e2e_ms, "audio_s_per_s": audio_s / (e2e_ms / 1000.0),
+                   "h2d_bytes": F * 128 * 4, "d2h_bytes": F * 1920 * 4},
+           "dtype": "bf16 convolutions, fp32 LSTM / activations"}
+    if cpu_sample:
+        sys.path.insert(0, os.path.join(HERE, "oracle"))
+        import oracle as O
+        if O.Reference.available():
+            import ctypes
+            ref = O.Reference()
+            # the reference prints progress lines from C: send fd 1 to /dev/null meanwhile
+            sys.stdout.flush()
+            libc = ctypes.CDLL(None)
+            saved, dn = os.dup(1), os.open(os.devnull, os.O_WRONLY)
+            os.dup2(dn, 1)
+            try:
+                t0 = time.perf_counter()
+                ref.voc_decode(w, lat_h[:1])
+                secs = time.perf_counter() - t0
+                libc.fflush(None)
+            finally:
+                os.dup2(saved, 1)
+                os.close(saved)
+                os.close(dn)
+            res["cpu_reference"] = {"audio_s_per_s": (1920 / 24000.0) / secs, "cores": 1, "kind": "reference",
+                                    "sample": "one latent frame through the reference's bigvgan_decode "
+                                              "(oracle/_ref, single-threaded loops), %.1f s" % secs}
+    return res
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     dist = None
@@ -451,6 +520,8 @@ def run_ours(args, rank, world, local_rank):
     extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
     pe = measure_pe(args, local_rank) if (world == 1 and not args.no_pe) else None
     llm = measure_llm(args, local_rank) if (world == 1 and not args.no_llm) else None
+    voc = measure_voc(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
+        if (world == 1 and not args.no_voc) else None
 
     # ---- CPU baseline: reference code (per-token FFN) on the host, rank 0, N = 1
     cpu = None
@@ -483,6 +554,8 @@ def run_ours(args, rank, world, local_rank):
             line["patch_encoder"] = pe
         if llm:
             line["llm_step"] = llm
+        if voc:
+            line["vocoder"] = voc
         if extra:
             line["fp8"] = {"dtype": "e4m3", "weights": workload_config(args, world, "fp8")["weights"],
                            **{k: extra[k] for k in ("value", "ms_per_step", "e2e", "roofline", "attention_us_per_layer",
