@@ -505,6 +505,47 @@ def measure_voc(args, local_rank, cpu_sample):
     return res
 
 
+def measure_attn_sublayer(args, local_rank, cpu_sample):
+    """Config 1: one DiT self-attention sublayer (manual_attention), X [2][64][1024],
+    fp32 and bf16 engines.  Reports the attention core's device time (post-QKV,
+    pre-O; CUDA events over 50 back-to-back launches) and the whole sublayer call
+    through host buffers (copies included, mean of 20 calls); with cpu_sample,
+    the reference's own manual_attention (oracle/_ref) on the host for the same
+    two rows."""
+    import time
+    import dtts
+    import synth
+    w = synth.dit_weights(0, n_layers=1)
+    p = "velocity_field_predictor.blocks.0."
+    W = [w[p + n] for n in ("attn.q_proj.weight", "attn.k_proj.weight", "attn.v_proj.weight", "attn.o_proj.weight")]
+    bo = np.zeros(1024, np.float32)
+    qn, kn = w[p + "attn.q_norm.weight"], w[p + "attn.k_norm.weight"]
+    x = synth.normal(0, "c1.x", (2, 64, 1024), 1.0)
+    res = {"workload": "attention sublayer, 2 rows x L=64 x 1024, 16 heads, RMS qk-norm, RoPE, no mask"}
+    for name, dt in (("fp32", dtts.DTYPE_F32), ("bf16", dtts.DTYPE_BF16)):
+        a = dtts.Attention(*W, bo, qn, kn, dtype=dt, device=local_rank)
+        for _ in range(3):
+            a.forward(x)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            a.forward(x)
+        call_us = (time.perf_counter() - t0) / 20 * 1e6
+        res[name] = {"core_us": a.profile_core(50), "sublayer_call_us_host_buffers": call_us}
+        a.close()
+    if cpu_sample:
+        sys.path.insert(0, os.path.join(HERE, "oracle"))
+        import oracle as O
+        if O.Reference.available():
+            ref = O.Reference()
+            t0 = time.perf_counter()
+            for i in range(2):
+                ref.manual_attention(x[i], *W, bo, qn, kn)
+            res["cpu_reference_us"] = (time.perf_counter() - t0) * 1e6
+            res["cpu_reference"] = ("the reference's manual_attention (include/dit_manual.h:88) built in "
+                                    "oracle/_ref, both rows, %d threads" % ref.num_threads())
+    return res
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     dist = None
@@ -522,6 +563,8 @@ def run_ours(args, rank, world, local_rank):
     llm = measure_llm(args, local_rank) if (world == 1 and not args.no_llm) else None
     voc = measure_voc(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
         if (world == 1 and not args.no_voc) else None
+    attn1 = measure_attn_sublayer(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
+        if world == 1 else None
 
     # ---- CPU baseline: reference code (per-token FFN) on the host, rank 0, N = 1
     cpu = None
@@ -556,6 +599,8 @@ def run_ours(args, rank, world, local_rank):
             line["llm_step"] = llm
         if voc:
             line["vocoder"] = voc
+        if attn1:
+            line["attention_sublayer"] = attn1
         if extra:
             line["fp8"] = {"dtype": "e4m3", "weights": workload_config(args, world, "fp8")["weights"],
                            **{k: extra[k] for k in ("value", "ms_per_step", "e2e", "roofline", "attention_us_per_layer",
