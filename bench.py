@@ -184,6 +184,42 @@ def cpu_reference_eval(args, w, fc, fu, z0, spk, ffn_mode):
     return time.perf_counter() - t, ref.num_threads()
 
 
+def cpu_batched_eval(args, inputs):
+    """The batched CPU throughput line: one velocity forward of every CFG row of
+    the workload (2 x n_utt rows, step t = 0) through a PyTorch fp32
+    restatement of the reference's arithmetic (oracle/torch_cpu.py) on all
+    host threads; one untimed warm-up forward first."""
+    import torch
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    import torch_cpu
+    w, fc, fu, z0, spk = inputs
+    ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(ncpu)
+    orc = O.Oracle()
+    L = args.fm_len + args.patch
+    mask = orc.fm_mask(L, args.fm_len, args.patch)
+    pos = orc.fm_pos(L, args.fm_len, args.patch)
+    n = args.n_utt
+    x = np.zeros((2 * n, L, 1024), np.float32)
+    cond = np.zeros((2 * n, 1024), np.float32)
+    for u in range(n):
+        c = orc.compute_cond(w, 0.0, spk[u], 1.5, n_layers=args.layers)
+        coord = orc.linear_rows(z0[u], w["coordinate_proj.weight"], w["coordinate_proj.bias"])
+        for r, buf in ((2 * u, fc), (2 * u + 1, fu)):
+            x[r, :args.fm_len] = buf[u]
+            x[r, args.fm_len:] = coord
+            cond[r] = c
+    m = torch_cpu.BatchedDiT(w, args.layers)
+    m.velocity(x[:2], cond[:2], mask, pos, n_out=args.patch)
+    t = time.perf_counter()
+    m.velocity(x, cond, mask, pos, n_out=args.patch)
+    secs = time.perf_counter() - t
+    return {"value": n / secs, "unit": UNIT, "cores": ncpu, "kind": "port",
+            "sample": "one velocity forward of all %d CFG rows (L=%d, %d layers, fp32) batched through "
+                      "PyTorch/MKL on the host (oracle/torch_cpu.py), %.1f s" % (2 * n, L, args.layers, secs)}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference CPU path (as shipped) on the host cores."""
     if rank != 0:
@@ -579,6 +615,11 @@ def run_ours(args, rank, world, local_rank):
                              "include/dit_manual.h (FFN per token) built in oracle/_ref, %.1f s"
                              % (args.fm_len + args.patch, args.layers, secs)}
 
+    # ---- batched CPU line: all 128 rows of the workload through MKL at once
+    cpu_batched = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_batched = cpu_batched_eval(args, inputs)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -591,6 +632,8 @@ def run_ours(args, rank, world, local_rank):
                   "kernels_alone_us"):
             line[k] = head[k]
         line["cpu_baseline"] = cpu
+        if cpu_batched:
+            line["cpu_batched"] = cpu_batched
         line["clocks"] = head["clocks"]
         line["gpu_launches"] = head["gpu_launches"]
         if pe:
