@@ -115,7 +115,9 @@ DTTS_DEV float gelu_tanh_fast(float x) {
     const float c1 = 0.7978845608028654f, c2 = 0.044715f;
     return 0.5f * x * (1.0f + tanh_hw(c1 * (x + c2 * x * x * x)));
 }
-DTTS_DEV float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// x / (1 + e^-x) with the fast divide (2 ulp); for x < -88 the denominator is
+// +inf and the result 0.
+DTTS_DEV float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ---- per-warp staging buffer: 32 rows x 128 bytes, 16-byte chunks swizzled by row
 DTTS_DEV uint32_t stage_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }

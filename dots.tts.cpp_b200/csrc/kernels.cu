@@ -1220,35 +1220,69 @@ void launch_eos_prob(const float *logits, int n, float *prob, cudaStream_t s) {
 // =========================================================================
 // PatchEncoder
 // =========================================================================
-__global__ void __launch_bounds__(128) pe_conv_kernel(const float *__restrict__ frames, int n_frames,
-                                                      const float *__restrict__ tail, const float *__restrict__ w,
+// Causal stride-2 conv (k = 2, taps 2t-1 and 2t, tap 2t-1 of the first token
+// from `tail`): TOK tokens per block (16 for a prefill, 1 for a decode step),
+// their input frames staged in shared memory; thread c computes output
+// channel c of all of them from the transposed weight wt[ic][k][c] (coalesced
+// across threads, 16 input channels of weights loaded ahead).  new_tail: the
+// last frame.
+template <int TOK>
+__global__ void __launch_bounds__(128) pe_conv_kernel(const float *__restrict__ frames, int n_frames, int B,
+                                                      const float *__restrict__ tail, const float *__restrict__ wt,
                                                       const float *__restrict__ bias, bf16 *__restrict__ out,
                                                       float *__restrict__ new_tail) {
     pdl_wait();
     pdl_trigger();
-    __shared__ float f0[kLat], f1[kLat];
+    __shared__ float f[TOK][2][kLat];
     const int T = n_frames / 2;
-    const int b = blockIdx.x / T, t = blockIdx.x % T;
-    const float *fb = frames + (long long)b * n_frames * kLat;
-    const int i0 = 2 * t - 1, i1 = 2 * t;
+    const long long n_tok = (long long)B * T, tok0 = (long long)blockIdx.x * TOK;
     const int c = threadIdx.x;
-    f0[c] = i0 >= 0 ? fb[(long long)i0 * kLat + c] : (tail ? tail[(long long)b * kLat + c] : 0.f);
-    f1[c] = fb[(long long)i1 * kLat + c];
-    __syncthreads();
-    float s = bias ? bias[c] : 0.f;
-    const float *wr = w + (long long)c * kLat * 2;
-    for (int ic = 0; ic < kLat; ic++) {
-        s += f0[ic] * wr[2 * ic + 0];
-        s += f1[ic] * wr[2 * ic + 1];
+    for (int i = 0; i < TOK; i++) {
+        const long long g = tok0 + i;
+        float v0 = 0.f, v1 = 0.f;
+        if (g < n_tok) {
+            const int b = (int)(g / T), t = (int)(g % T);
+            const float *fb = frames + (long long)b * n_frames * kLat;
+            v0 = t > 0 ? fb[(long long)(2 * t - 1) * kLat + c] : (tail ? tail[(long long)b * kLat + c] : 0.f);
+            v1 = fb[(long long)(2 * t) * kLat + c];
+            if (new_tail && t == T - 1) new_tail[(long long)b * kLat + c] = fb[(long long)(n_frames - 1) * kLat + c];
+        }
+        f[i][0][c] = v0;
+        f[i][1][c] = v1;
     }
-    out[((long long)b * T + t) * kLat + c] = __float2bfloat16_rn(s);
-    if (new_tail && t == T - 1) new_tail[(long long)b * kLat + c] = fb[(long long)(n_frames - 1) * kLat + c];
+    __syncthreads();
+    float s[TOK];
+    const float b0 = bias ? bias[c] : 0.f;
+#pragma unroll
+    for (int i = 0; i < TOK; i++) s[i] = b0;
+    for (int ic0 = 0; ic0 < kLat; ic0 += 16) {
+        float w[16][2];
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+            w[u][0] = __ldg(wt + ((ic0 + u) * 2 + 0) * kLat + c);
+            w[u][1] = __ldg(wt + ((ic0 + u) * 2 + 1) * kLat + c);
+        }
+#pragma unroll
+        for (int u = 0; u < 16; u++)
+#pragma unroll
+            for (int i = 0; i < TOK; i++) {
+                s[i] += f[i][0][ic0 + u] * w[u][0];
+                s[i] += f[i][1][ic0 + u] * w[u][1];
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < TOK; i++)
+        if (tok0 + i < n_tok) out[(tok0 + i) * kLat + c] = __float2bfloat16_rn(s[i]);
 }
 
-void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *w, const float *bias,
+void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *wt, const float *bias,
                     bf16 *out, float *new_tail, cudaStream_t s) {
-    const int T = n_frames / 2;
-    pe_conv_kernel<<<B * T, kLat, 0, s>>>(frames, n_frames, tail, w, bias, out, new_tail);
+    const long long n_tok = (long long)B * (n_frames / 2);
+    if (n_tok >= 4096)
+        pe_conv_kernel<16><<<(unsigned)((n_tok + 15) / 16), kLat, 0, s>>>(frames, n_frames, B, tail, wt, bias, out,
+                                                                          new_tail);
+    else
+        pe_conv_kernel<1><<<(unsigned)n_tok, kLat, 0, s>>>(frames, n_frames, B, tail, wt, bias, out, new_tail);
 }
 
 __global__ void pe_pairs_kernel(const float *__restrict__ h, int T, int pair_mode, bf16 *__restrict__ out) {

@@ -137,8 +137,9 @@ void launch_cfg_euler(const float *vel, float *z, int n_utt, int P, float cfg_sc
 // ------------------------------------------------------------ PatchEncoder
 // causal Conv1d(128->128, k=2, s=2); tokens t of sequence b use frames 2t-1, 2t
 // of the concatenation [tail[b] | frames[b]]; writes bf16 [B*T][128] and, if
-// new_tail != nullptr, stores the last frame of each sequence there.
-void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *w, const float *bias,
+// new_tail != nullptr, stores the last frame of each sequence there.  wt is the
+// conv weight transposed to [in 128][tap 2][out 128].
+void launch_pe_conv(const float *frames, int B, int n_frames, const float *tail, const float *wt, const float *bias,
                     bf16 *out, float *new_tail, cudaStream_t s);
 // out[b*n + p] = bf16([h[b, tok0] | h[b, tok1]]) with the pairing rule
 void launch_pe_pairs(const float *h, int B, int T, int pair_mode, bf16 *out, cudaStream_t s, bool pdl = false);

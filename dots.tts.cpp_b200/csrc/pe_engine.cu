@@ -66,8 +66,7 @@ __global__ void pe_silu_kernel(float *__restrict__ x, bf16 *__restrict__ ffn, lo
     if (i >= n4) return;
     float4 v = reinterpret_cast<float4 *>(x)[i];
     reinterpret_cast<float4 *>(x)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    v.x = v.x / (1.0f + __expf(-v.x)); v.y = v.y / (1.0f + __expf(-v.y));
-    v.z = v.z / (1.0f + __expf(-v.z)); v.w = v.w / (1.0f + __expf(-v.w));
+    v.x = silu_f(v.x); v.y = silu_f(v.y); v.z = silu_f(v.z); v.w = silu_f(v.w);
     reinterpret_cast<uint2 *>(ffn)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
 }
 
@@ -389,7 +388,14 @@ int dtts_pe_create(const dtts_pe_weights *w, int dtype, int device, int max_batc
                   make_tmap_bf16(&L.t1_s, L.w1, kF, kD, kBNs) && make_tmap_bf16(&L.t2_s, L.w2, kD, kF, kBNs);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map (PatchEncoder layer %d)", l);
     }
-    if ((st = up_f32(p->wts, w->conv_w, (size_t)kLat * kLat * 2, &p->conv_w))) return st;
+    {
+        // ds conv weight [oc][ic][2] -> [ic][2][oc], read coalesced by pe_conv_kernel
+        std::vector<float> wt((size_t)kLat * kLat * 2);
+        for (int o = 0; o < kLat; o++)
+            for (int i = 0; i < kLat; i++)
+                for (int k = 0; k < 2; k++) wt[((size_t)i * 2 + k) * kLat + o] = w->conv_w[((size_t)o * kLat + i) * 2 + k];
+        if ((st = up_f32(p->wts, wt.data(), wt.size(), &p->conv_w))) return st;
+    }
     if ((st = up_f32(p->wts, w->conv_b, kLat, &p->conv_b))) return st;
     if ((st = up_bf16(p->wts, {w->in_w}, kD, kLat, &p->in_w))) return st;
     if ((st = up_f32(p->wts, w->in_b, kD, &p->in_b))) return st;
