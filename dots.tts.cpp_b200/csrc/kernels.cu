@@ -676,8 +676,17 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl) {
         int dev = 0, nsm = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-        // about 5 resident CTAs per SM, each with a few pairs to pipeline
-        const int target = nsm * 5;
+        // one wave of resident CTAs (48 KB of shared memory each: 4 per SM on
+        // B200), each with a few pairs to pipeline
+        static int occ_cache[64] = {0};
+        int occ = dev < 64 ? occ_cache[dev] : 0;
+        if (occ <= 0) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, attn_short_kernel, 128, kShortSmem) != cudaSuccess ||
+                occ < 1)
+                occ = 1;
+            if (dev < 64) occ_cache[dev] = occ;
+        }
+        const int target = nsm * occ;
         const int per_cta = std::max(1, (n_pairs + target - 1) / target);
         const int grid = (n_pairs + per_cta - 1) / per_cta;
         launch_k(pdl, attn_short_kernel, dim3(grid), dim3(128), (size_t)kShortSmem, s, a, n_pairs, per_cta);
