@@ -538,7 +538,7 @@ struct dtts_voc {
         }
         long long Tin = T0;
         for (int s = 0; s < kStages; s++) {
-            const int cin = s == 0 ? 1536 : cpad(kUpOut[s - 1]), cp = cpad(kUpOut[s]), ch = kUpOut[s];
+            const int cin = s == 0 ? 1536 : cpad(kUpOut[s - 1]), cp = cpad(kUpOut[s]);
             const int str = kUpStride[s];
             const long long T = Tin * str;
             // ---- causal ConvTranspose1d as one GEMM: the output phases stacked along N
