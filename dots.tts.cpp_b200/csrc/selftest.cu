@@ -14,17 +14,33 @@ struct Scratch {
     DeviceArena a;
     ~Scratch() { a.free_all(); }
 };
+
+// One thread waits on an mbarrier that nothing arrives at, through the same
+// bounded wait every GEMM wait uses: after the limit it records the code in
+// the error word, raises the abort flag and returns.
+__global__ void wait_limit_selftest_kernel(int *err) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, &abort_flag, err, DEVERR_TIMEOUT_PRODUCER);
+    __syncthreads();
+}
 }  // namespace
 
 extern "C" {
 
 // C[M][N] = A[M][K] B[N][K]^T (+ bias[N]) through the tcgen05 GEMM kernel with
-// the fp32-output epilogue; bn = 128 or 256.
+// the fp32-output epilogue; bn = 64, 128, 192 or 256.
 int dtts_selftest_gemm(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, int bn,
                        int device) {
     DTTS_CHECK(A && B && C, DTTS_ERR_ARG, "null argument");
-    DTTS_CHECK(M >= 1 && K >= 64 && K % 64 == 0 && (bn == 128 || bn == 256) && N % bn == 0, DTTS_ERR_ARG,
-               "bad GEMM shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
+    DTTS_CHECK(M >= 1 && K >= 64 && K % 64 == 0 && (bn == 64 || bn == 128 || bn == 192 || bn == 256) && N % bn == 0,
+               DTTS_ERR_ARG, "bad GEMM shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
     int nsm = 0, st = check_device(device, &nsm);
     if (st) return st;
     DeviceGuard g(device);
@@ -150,6 +166,73 @@ int dtts_selftest_attention(const float *q, const float *k, const float *v, floa
         std::vector<uint16_t> t(nq);
         DTTS_CUDA(cudaMemcpy(t.data(), dout, nq * 2, cudaMemcpyDeviceToHost));
         for (size_t i = 0; i < nq; i++) { uint32_t u = (uint32_t)t[i] << 16; std::memcpy(&out[i], &u, 4); }
+    }
+    return DTTS_OK;
+}
+
+// Time convolution through the GEMM over taps (EpiParams::tap_*):
+// out[t][o] = bias[o] + sum_k sum_c x[t + k dil - pad_left][c] w[o][c][k], rows
+// outside [0, T) zero; x [T][C] and w [N][C][K] rounded to bf16 as the engine
+// stores them; C % 64 == 0.
+int dtts_selftest_conv(const float *x, int T, int C, const float *w, const float *bias, int N, int K, int dil,
+                       int pad_left, int bn, float *out, int device) {
+    DTTS_CHECK(x && w && out, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(T >= 1 && C >= 64 && C % 64 == 0 && K >= 1 && K <= 32 && dil >= 1 && pad_left >= 0 &&
+                   (bn == 64 || bn == 128 || bn == 192 || bn == 256) && N % bn == 0,
+               DTTS_ERR_ARG, "bad conv shape T=%d C=%d N=%d K=%d bn=%d", T, C, N, K, bn);
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    DTTS_CUDA(gemm_prepare_attributes());
+    Scratch s;
+    std::vector<float> bop((size_t)N * K * C);
+    for (int o = 0; o < N; o++)
+        for (int c = 0; c < C; c++)
+            for (int k = 0; k < K; k++) bop[((size_t)o * K + k) * C + c] = w[((size_t)o * C + c) * K + k];
+    std::vector<uint16_t> ha((size_t)T * C), hb(bop.size());
+    f32_to_bf16_host(x, ha.data(), ha.size());
+    f32_to_bf16_host(bop.data(), hb.data(), hb.size());
+    void *da = s.a.alloc(ha.size() * 2), *db = s.a.alloc(hb.size() * 2), *dc = s.a.alloc((size_t)T * N * 4);
+    void *dbias = bias ? s.a.alloc((size_t)N * 4) : nullptr;
+    int *derr = (int *)s.a.alloc(4);
+    DTTS_CHECK(da && db && dc && derr && (!bias || dbias), DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemcpy(da, ha.data(), ha.size() * 2, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemcpy(db, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice));
+    if (bias) DTTS_CUDA(cudaMemcpy(dbias, bias, (size_t)N * 4, cudaMemcpyHostToDevice));
+    DTTS_CUDA(cudaMemset(derr, 0, 4));
+    GemmOp op;
+    std::memset(&op, 0, sizeof(op));
+    bool ok = make_tmap_bf16(&op.ta, da, T, C, 128) && make_tmap_bf16(&op.tb, db, N, (size_t)K * C, bn);
+    DTTS_CHECK(ok, DTTS_ERR_CUDA, "tensor map encode failed");
+    op.M = T; op.N = N; op.K = K * C; op.bn = bn; op.nw = 4; op.epi = EPI_F32;
+    op.ep.out = dc; op.ep.ldo = N; op.ep.bias = (const float *)dbias; op.ep.err = derr; op.ep.tok_per_row = 1;
+    op.ep.tap_kb = C / 64; op.ep.tap_base = -pad_left; op.ep.tap_step = dil;
+    DTTS_CUDA(launch_gemm(op, nsm, 0));
+    if ((st = stream_wait(0, 60.0))) return st;
+    int err = 0;
+    DTTS_CUDA(cudaMemcpy(&err, derr, 4, cudaMemcpyDeviceToHost));
+    DTTS_CHECK(err == 0, DTTS_ERR_TIMEOUT, "GEMM kernel wait limit reached (code %d)", err);
+    DTTS_CUDA(cudaMemcpy(out, dc, (size_t)T * N * 4, cudaMemcpyDeviceToHost));
+    return DTTS_OK;
+}
+
+int dtts_selftest_wait_limit(int device, int *code) {
+    DTTS_CHECK(code, DTTS_ERR_ARG, "null argument");
+    *code = 0;
+    int nsm = 0, st = check_device(device, &nsm);
+    if (st) return st;
+    DeviceGuard g(device);
+    Scratch s;
+    int *derr = (int *)s.a.alloc(4);
+    DTTS_CHECK(derr, DTTS_ERR_OOM, "cudaMalloc failed");
+    DTTS_CUDA(cudaMemset(derr, 0, 4));
+    wait_limit_selftest_kernel<<<1, 32>>>(derr);
+    DTTS_CUDA(cudaGetLastError());
+    if ((st = stream_wait(0, 30.0))) return st;
+    DTTS_CUDA(cudaMemcpy(code, derr, 4, cudaMemcpyDeviceToHost));
+    if (*code) {
+        set_error("device wait limit reached (code %d)", *code);
+        return DTTS_ERR_TIMEOUT;
     }
     return DTTS_OK;
 }

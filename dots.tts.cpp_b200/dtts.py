@@ -113,7 +113,7 @@ EXPORTS = [
     "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve",
     "dtts_llm_create", "dtts_llm_destroy", "dtts_llm_set_stream", "dtts_llm_prefill", "dtts_llm_step", "dtts_llm_length",
     "dtts_voc_create", "dtts_voc_destroy", "dtts_voc_set_stream", "dtts_voc_decode", "dtts_voc_aa_filter",
-    "dtts_selftest_voc_activation", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
+    "dtts_selftest_voc_activation", "dtts_selftest_wait_limit", "dtts_selftest_conv", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
     "dtts_attn_profile_core", "dtts_attn_forward_f32_noalloc", "dtts_pe_create", "dtts_pe_create_from_safetensors", "dtts_pe_destroy",
     "dtts_pe_set_stream", "dtts_pe_sync", "dtts_pe_forward", "dtts_pe_stream_reset", "dtts_pe_decode",
     "dtts_pe_stream_length", "dtts_selftest_gemm", "dtts_selftest_attention", "dtts_selftest_e4m3",
@@ -231,6 +231,9 @@ def lib(path: str = LIB_PATH):
     L.dtts_voc_decode.argtypes = [_vp, _vp, C.c_int, _vp, C.c_int]
     L.dtts_voc_aa_filter.argtypes = [_fp]
     L.dtts_selftest_voc_activation.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp, _fp, C.c_int, _fp]
+    L.dtts_selftest_wait_limit.argtypes = [C.c_int, C.POINTER(C.c_int)]
+    L.dtts_selftest_conv.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     _fp, C.c_int]
     L.dtts_selftest_e4m3.argtypes = [_fp, _u8p, C.c_int, C.c_int]
     L.dtts_selftest_gemm_e4m3.argtypes = [_u8p, _fp, _u8p, _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
                                           C.c_int]
@@ -620,6 +623,26 @@ class Vocoder:
             out = np.zeros(latent.shape[0] * self.HOP, np.float32) if out is None else out
         check(lib().dtts_voc_decode(self.h, _addr(latent), latent.shape[0], _addr(out), mem))
         return out
+
+
+def selftest_wait_limit(device=0):
+    """(status, code): a kernel wait that nothing completes must give up with
+    DTTS_ERR_TIMEOUT and its code in the error word, leaving the context usable."""
+    code = C.c_int()
+    st = lib().dtts_selftest_wait_limit(device, C.byref(code))
+    return st, code.value
+
+
+def selftest_conv(x, w, bias=None, dil=1, pad_left=None, bn=64, device=0):
+    """Time convolution through the GEMM over taps: x [T][C], w [N][C][K];
+    pad_left defaults to the causal dil (K - 1)."""
+    x, w, bias = _f32(x), _f32(w), _f32(bias)
+    T, Cc = x.shape
+    N, _, K = w.shape
+    pad = dil * (K - 1) if pad_left is None else pad_left
+    out = np.zeros((T, N), np.float32)
+    check(lib().dtts_selftest_conv(_ptr(x), T, Cc, _ptr(w), _ptr(bias), N, K, dil, pad, bn, _ptr(out), device))
+    return out
 
 
 def voc_aa_filter():

@@ -378,9 +378,20 @@ int dtts_selftest_voc_activation(const float *x, int len, int ch, const float *a
                                  const float *filt_up, const float *filt_down, int fch, float *out);
 
 /* ------------------------------------------------------------------ self-test
+ * Failure detection without a fault: one kernel thread waits on an mbarrier that
+ * nothing completes, through the bounded wait of every engine kernel (2 s of
+ * %globaltimer); it must give up, leave its code in *code (1: producer wait) and
+ * return DTTS_ERR_TIMEOUT with the context still usable. */
+int dtts_selftest_wait_limit(int device, int *code);
+/* A time convolution through the tcgen05 GEMM over taps, as the vocoder runs it:
+ * out[t][o] = bias[o] + sum_k sum_c x[t + k dil - pad_left][c] w[o][c][k] (zero outside
+ * [0, T)); x [T][C], w [N][C][K], inputs rounded to bf16; C % 64 == 0, bn | N. */
+int dtts_selftest_conv(const float *x, int T, int C, const float *w, const float *bias, int N, int K, int dil,
+                       int pad_left, int bn, float *out, int device);
+/* ------------------------------------------------------------------ kernel self-tests
  * One engine kernel in isolation on host data (no reference counterpart):
  * inputs are rounded to bf16 on the host exactly as the engine stores them. */
-/* C[M][N] = A[M][K] B[N][K]^T (+ bias) with the tcgen05 GEMM; bn = 128 or 256 */
+/* C[M][N] = A[M][K] B[N][K]^T (+ bias) with the tcgen05 GEMM; bn = 64, 128, 192 or 256 */
 int dtts_selftest_gemm(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, int bn,
                        int device);
 /* C[M][N] = a_scale[m] b_scale[n] sum_k A[m][k] B[n][k] (+ bias) with e4m3 bytes A

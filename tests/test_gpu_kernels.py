@@ -12,6 +12,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K,bn", [
     (128, 256, 64, 256), (128, 128, 64, 128), (1, 256, 128, 256), (200, 512, 1024, 256),
     (1000, 1024, 4096, 256), (8192, 3072, 1024, 256), (64, 1536, 2048, 256), (333, 384, 192, 128),
+    (333, 384, 192, 64), (700, 576, 512, 192),
 ])
 def test_tcgen05_gemm(M, N, K, bn):
     rng = np.random.default_rng(M + N + K)
@@ -75,3 +76,33 @@ def test_attention(rows, Tq, kv, causal, q0, use_mask, use_f32):
     else:
         want = _attn_ref(bf16(q), bf16(k), bf16(v), mask, causal, q0)
         assert rel(got, want) < 1e-2
+
+
+def _conv_ref(x, w, bias, dil, pad):
+    T, N, K = x.shape[0], w.shape[0], w.shape[2]
+    xb, wb = bf16(x).astype(np.float64), bf16(w).astype(np.float64)
+    out = np.zeros((T, N)) + (0 if bias is None else bias)
+    for k in range(K):
+        sh = k * dil - pad
+        src = np.zeros_like(xb)
+        lo, hi = max(0, -sh), min(T, T - sh)
+        if hi > lo:
+            src[lo:hi] = xb[lo + sh:hi + sh]
+        out += src @ wb[:, :, k].T
+    return out
+
+
+@pytest.mark.parametrize("T,C,N,K,dil,pad,bn", [
+    (300, 64, 64, 11, 5, 50, 64),      # causal dilated (AMP c1, 64-channel stages)
+    (200, 128, 128, 7, 1, 6, 128),     # causal, two channel blocks per tap
+    (150, 192, 192, 3, 3, 6, 192),     # 192-wide tiles
+    (77, 128, 256, 5, 1, 2, 128),      # centred K = 5 (conv_pre), rows past T read as zero
+    (130, 64, 128, 2, 1, 0, 64),       # taps x[q], x[q+1]; pad 0
+])
+def test_conv_over_taps(T, C, N, K, dil, pad, bn):
+    rng = np.random.default_rng(T + C + N + K)
+    x = rng.standard_normal((T, C), dtype=np.float32)
+    w = rng.standard_normal((N, C, K), dtype=np.float32)
+    bias = rng.standard_normal(N, dtype=np.float32)
+    got = dtts.selftest_conv(x, w, bias, dil=dil, pad_left=pad, bn=bn)
+    assert rel(got, _conv_ref(x, w, bias, dil, pad)) < 1e-5
