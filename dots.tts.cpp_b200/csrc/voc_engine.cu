@@ -6,8 +6,8 @@
 // and biases are zero and SnakeBeta(0) = 0.
 //   bottleneck   post_proj, Linear 128->512, 4 x LSTM(512) with skip,
 //                Linear 512->128: fp32 SIMT GEMMs + one cooperative kernel
-//                running the four LSTM layers as a wavefront (a grid barrier
-//                per step, T + 3 steps)
+//                running the four LSTM layers as a dataflow wavefront (per-step
+//                counters, T + 3 dependent steps)
 //   conv_pre     K = 5, centred: tcgen05 GEMM over taps (bf16 out)
 //   6 stages     causal ConvTranspose1d (K = 2 stride) as `stride` GEMMs, one
 //                per output phase r: out[q s + r] = W_r . [x[q] | x[q-1]],
@@ -211,16 +211,16 @@ __global__ void __launch_bounds__(kPostT) voc_post_kernel(const float *__restric
     audio[t] = tanhf(s) * 1.92f;
 }
 
-// The 4-layer LSTM (lstm.cpp:12-104) as one wavefront: at global step tau,
-// layer l advances its time step t = tau - l, so the four layers run together
-// and the recurrence takes T + 3 steps instead of 4 T.  CTA b serves layer
-// l = b / 64 and hidden units 8 (b mod 64) .. +7: it keeps their 32 W_hh rows
-// (gates i, f, g, o) in shared memory; layers 1..3 read their 32 W_ih rows
-// from global memory (L2-resident) each step.  Layer 0's input projection
-// (x W_ih^T + b_ih + b_hh for every t) is precomputed in gin0.  Each step
-// reads h^l[t-1] and h^(l-1)[t] from L2 (written the step before), writes its
-// units of h^l[t], then meets every CTA at a grid barrier (a counter; bounded
-// wait, error code on expiry).  Launched cooperatively (all CTAs resident).
+// The 4-layer LSTM (lstm.cpp:12-104) as a dataflow wavefront: CTA b serves
+// layer l = b / 64 and hidden units 8 (b mod 64) .. +7; it keeps their 32 W_hh
+// rows (gates i, f, g, o) in shared memory, and layers 1..3 read their 32 W_ih
+// rows from global memory (L2-resident) each step.  Layer 0's input
+// projection (x W_ih^T + b_ih + b_hh for every t) is precomputed in gin0.
+// Step t of layer l waits until all 64 CTAs of layer l have published h^l[t-1]
+// and all 64 of layer l-1 have published h^(l-1)[t] (counters cnt[l][t],
+// incremented after each CTA's write; bounded wait, error code on expiry), so
+// the layers advance together without a global barrier: T + 3 dependent steps
+// instead of 4 T.  Launched cooperatively (all CTAs resident).
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -233,7 +233,7 @@ struct LstmArgs {
     const float *b_g[4];               // [2048] b_ih + b_hh
     float *h;                          // [4][T][512]
     int T;
-    unsigned *bar;
+    unsigned *cnt;                     // [4][T] CTAs that published h^l[t], zero at launch
     int *err;
 };
 
@@ -255,58 +255,13 @@ __global__ void __launch_bounds__(256) voc_lstm_kernel(const LstmArgs p) {
     float cst = 0.f;
     float *hl = p.h + (long long)l * p.T * kLstmH;
     const float *hprev_layer = l ? p.h + (long long)(l - 1) * p.T * kLstmH : nullptr;
-    for (int tau = 0; tau < p.T + 3; tau++) {
-        const int t = tau - l;
-        if (t >= 0 && t < p.T) {
-            for (int k = tid; k < kLstmH; k += 256) {
-                hs[k] = t ? __ldcg(hl + (long long)(t - 1) * kLstmH + k) : 0.f;
-                if (l) xs[k] = __ldcg(hprev_layer + (long long)t * kLstmH + k);
-            }
-            __syncthreads();
-            // warp w: rows 4w .. 4w+3, their W_ih loads all issued together
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            int grow[4];
-#pragma unroll
-            for (int qq = 0; qq < 4; qq++) {
-                const int r = warp * 4 + qq;
-                grow[qq] = (r >> 3) * kLstmH + q0 + (r & 7);
-            }
-            if (l) {
-#pragma unroll
-                for (int k = lane; k < kLstmH; k += 32) {
-                    const float xv = xs[k];
-#pragma unroll
-                    for (int qq = 0; qq < 4; qq++) acc[qq] += __ldg(wih + (long long)grow[qq] * kLstmH + k) * xv;
-                }
-            }
-#pragma unroll
-            for (int k = lane; k < kLstmH; k += 32) {
-                const float hv = hs[k];
-#pragma unroll
-                for (int qq = 0; qq < 4; qq++) acc[qq] += w[(warp * 4 + qq) * kLstmH + k] * hv;
-            }
-#pragma unroll
-            for (int qq = 0; qq < 4; qq++) {
-                const float v = warp_sum(acc[qq]);
-                if (lane == 0)
-                    gs[warp * 4 + qq] = v + (l ? __ldg(p.b_g[l] + grow[qq]) : p.gin0[(long long)t * 4 * kLstmH + grow[qq]]);
-            }
-            __syncthreads();
-            if (tid < kLstmUnits) {
-                const float gi = gs[tid], gf = gs[8 + tid], gg = gs[16 + tid], go = gs[24 + tid];
-                const float iv = 1.0f / (1.0f + expf(-gi)), fv = 1.0f / (1.0f + expf(-gf));
-                const float gv = tanhf(gg), ov = 1.0f / (1.0f + expf(-go));
-                cst = fv * cst + iv * gv;
-                hl[(long long)t * kLstmH + q0 + tid] = ov * tanhf(cst);
-            }
-        }
-        __syncthreads();
+    for (int t = 0; t < p.T; t++) {
         if (tid == 0) {
-            __threadfence();
-            atomicAdd(p.bar, 1u);
-            const unsigned target = (unsigned)(tau + 1) * gridDim.x;
+            const unsigned *need0 = t ? p.cnt + (long long)l * p.T + (t - 1) : nullptr;
+            const unsigned *need1 = l ? p.cnt + (long long)(l - 1) * p.T + t : nullptr;
             const unsigned long long t0 = globaltimer_ns();
-            while (ld_acquire_u32(p.bar) < target) {
+            while ((need0 && ld_acquire_u32(need0) < (unsigned)kLstmCtas) ||
+                   (need1 && ld_acquire_u32(need1) < (unsigned)kLstmCtas)) {
                 if (globaltimer_ns() - t0 > kWaitLimitNs) {
                     atomicExch(p.err, DEVERR_TIMEOUT_BARRIER);
                     abort_flag = 1;
@@ -316,6 +271,52 @@ __global__ void __launch_bounds__(256) voc_lstm_kernel(const LstmArgs p) {
         }
         __syncthreads();
         if (abort_flag) return;
+        for (int k = tid; k < kLstmH; k += 256) {
+            hs[k] = t ? __ldcg(hl + (long long)(t - 1) * kLstmH + k) : 0.f;
+            if (l) xs[k] = __ldcg(hprev_layer + (long long)t * kLstmH + k);
+        }
+        __syncthreads();
+        // warp w: rows 4w .. 4w+3, their W_ih loads all issued together
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int grow[4];
+#pragma unroll
+        for (int qq = 0; qq < 4; qq++) {
+            const int r = warp * 4 + qq;
+            grow[qq] = (r >> 3) * kLstmH + q0 + (r & 7);
+        }
+        if (l) {
+#pragma unroll
+            for (int k = lane; k < kLstmH; k += 32) {
+                const float xv = xs[k];
+#pragma unroll
+                for (int qq = 0; qq < 4; qq++) acc[qq] += __ldg(wih + (long long)grow[qq] * kLstmH + k) * xv;
+            }
+        }
+#pragma unroll
+        for (int k = lane; k < kLstmH; k += 32) {
+            const float hv = hs[k];
+#pragma unroll
+            for (int qq = 0; qq < 4; qq++) acc[qq] += w[(warp * 4 + qq) * kLstmH + k] * hv;
+        }
+#pragma unroll
+        for (int qq = 0; qq < 4; qq++) {
+            const float v = warp_sum(acc[qq]);
+            if (lane == 0)
+                gs[warp * 4 + qq] = v + (l ? __ldg(p.b_g[l] + grow[qq]) : p.gin0[(long long)t * 4 * kLstmH + grow[qq]]);
+        }
+        __syncthreads();
+        if (tid < kLstmUnits) {
+            const float gi = gs[tid], gf = gs[8 + tid], gg = gs[16 + tid], go = gs[24 + tid];
+            const float iv = 1.0f / (1.0f + expf(-gi)), fv = 1.0f / (1.0f + expf(-gf));
+            const float gv = tanhf(gg), ov = 1.0f / (1.0f + expf(-go));
+            cst = fv * cst + iv * gv;
+            hl[(long long)t * kLstmH + q0 + tid] = ov * tanhf(cst);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(p.cnt + (long long)l * p.T + t, 1u);   // this CTA's units of h^l[t] are out
+        }
     }
 }
 
@@ -379,7 +380,7 @@ struct dtts_voc {
     cudaEvent_t ev_fork = nullptr, ev_join[2] = {nullptr, nullptr};
     DeviceArena wts, ws;
     int *d_err = nullptr;
-    unsigned *d_bar = nullptr;
+    unsigned *d_cnt = nullptr;   // [4][max_frames] LSTM step counters
     // bottleneck (fp32)
     float *pp_w = nullptr, *pp_b = nullptr, *mi_w1 = nullptr, *mi_b1 = nullptr, *mi_w2 = nullptr, *mi_b2 = nullptr;
     float *w_ih[4] = {}, *w_hh[4] = {}, *b_g[4] = {};
@@ -506,11 +507,11 @@ struct dtts_voc {
     }
 
     int lstm(int T) {
-        DTTS_CUDA(cudaMemsetAsync(d_bar, 0, sizeof(unsigned), stream));
+        DTTS_CUDA(cudaMemsetAsync(d_cnt, 0, (size_t)4 * T * sizeof(unsigned), stream));
         LstmArgs a{};
         a.gin0 = gin;
         for (int l = 0; l < 4; l++) { a.w_ih[l] = w_ih[l]; a.w_hh[l] = w_hh[l]; a.b_g[l] = b_g[l]; }
-        a.h = hl; a.T = T; a.bar = d_bar; a.err = d_err;
+        a.h = hl; a.T = T; a.cnt = d_cnt; a.err = d_err;
         void *args[] = {(void *)&a};
         DTTS_CUDA(cudaLaunchCooperativeKernel((const void *)voc_lstm_kernel, dim3(4 * kLstmCtas), dim3(256), args,
                                               kLstmSmem, stream));
@@ -650,8 +651,8 @@ int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_
                                    (int)kLstmSmem));
     DeviceArena &A = v->wts;
     v->d_err = (int *)A.alloc(4);
-    v->d_bar = (unsigned *)A.alloc(4);
-    DTTS_CHECK(v->d_err && v->d_bar, DTTS_ERR_OOM, "cudaMalloc failed");
+    v->d_cnt = (unsigned *)A.alloc((size_t)4 * max_frames * sizeof(unsigned));
+    DTTS_CHECK(v->d_err && v->d_cnt, DTTS_ERR_OOM, "cudaMalloc failed");
     DTTS_CUDA(cudaMemset(v->d_err, 0, 4));
     // bottleneck
     std::vector<float> zero(4 * kLstmH, 0.f);
