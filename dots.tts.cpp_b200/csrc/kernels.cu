@@ -431,12 +431,28 @@ __global__ void __launch_bounds__(128, 5) attn_short_kernel(AttnArgs a, int n_pa
     };
     if (p0 < pend) issue(p0, 0);
     const int qi0 = warp * 16 + g, qi1 = qi0 + 8;
-    // the mask is shared by every (row, head): this thread's two query rows, keys 0..63
-    uint32_t mb[2][2] = {{~0u, ~0u}, {~0u, ~0u}};
-    if (a.mask_bits) {
-        const int mw = (a.kv_len + 31) >> 5;
-        if (qi0 < a.Tq) { mb[0][0] = a.mask_bits[qi0 * mw]; if (mw > 1) mb[0][1] = a.mask_bits[qi0 * mw + 1]; }
-        if (qi1 < a.Tq) { mb[1][0] = a.mask_bits[qi1 * mw]; if (mw > 1) mb[1][1] = a.mask_bits[qi1 * mw + 1]; }
+    // Which of this thread's 32 score slots (nt, c) may attend is the same for
+    // every (row, head): key range, causality and the mask, folded into one word
+    // (bit 4 nt + c) before the pair loop.
+    uint32_t okbits = 0;
+    {
+        uint32_t mb[2][2] = {{~0u, ~0u}, {~0u, ~0u}};
+        if (a.mask_bits) {
+            const int mw = (a.kv_len + 31) >> 5;
+            if (qi0 < a.Tq) { mb[0][0] = a.mask_bits[qi0 * mw]; if (mw > 1) mb[0][1] = a.mask_bits[qi0 * mw + 1]; }
+            if (qi1 < a.Tq) { mb[1][0] = a.mask_bits[qi1 * mw]; if (mw > 1) mb[1][1] = a.mask_bits[qi1 * mw + 1]; }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int key = nt * 8 + 2 * t + (c & 1);
+                const int qi = (c < 2) ? qi0 : qi1;
+                bool ok = key < a.kv_len;
+                if (a.causal) ok = ok && (key <= a.q_pos0 + qi);
+                ok = ok && ((mb[c >> 1][key >> 5] >> (key & 31)) & 1u);
+                okbits |= (ok ? 1u : 0u) << (4 * nt + c);
+            }
     }
     for (int p = p0, it = 0; p < pend; p++, it++) {
         const int buf = it & 1;
@@ -472,12 +488,7 @@ __global__ void __launch_bounds__(128, 5) attn_short_kernel(AttnArgs a, int n_pa
         for (int nt = 0; nt < 8; nt++) {
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                const int key = nt * 8 + 2 * t + (c & 1);
-                const int qi = (c < 2) ? qi0 : qi1;
-                bool ok = key < a.kv_len;
-                if (a.causal) ok = ok && (key <= a.q_pos0 + qi);
-                ok = ok && ((mb[c >> 1][key >> 5] >> (key & 31)) & 1u);
-                const float v = ok ? s[nt][c] * sc : -INFINITY;
+                const float v = ((okbits >> (4 * nt + c)) & 1u) ? s[nt][c] * sc : -INFINITY;
                 s[nt][c] = v;
                 if (c < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
             }
