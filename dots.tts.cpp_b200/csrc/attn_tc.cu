@@ -1,0 +1,243 @@
+// DiT attention at L = 64 on the 5th-generation tensor cores (tcgen05).
+//
+// A work unit is (sequence pair, head): the 128 query rows of two consecutive
+// sequences (rows 64 p .. 64 p + 127 of the [rows * 64][1024] q / k / v
+// buffers) and one head's 64 columns.  Per unit, one CTA of 4 warps:
+//   TMA    Q, K, V tiles 128 rows x 64 columns (128-byte swizzle)
+//   MMA 1  S = Q K^T into TMEM (128 x 128 fp32); only the two 64 x 64 blocks
+//          on the diagonal (each sequence against its own keys) are read
+//   all    thread i holds query row i: its 64 scores from TMEM, scaled by
+//          log2(e)/8, masked (-inf), max, exp2, sum; P (bf16) written K-major
+//          into shared memory with zeros off the diagonal block; meanwhile
+//          V is transposed in shared memory to V^T (dims x keys, K-major)
+//   MMA 2  O = P V (K = 128 keys) into TMEM columns 0..63
+//   all    O / l to bf16, row i of the head's 64 output columns, while the
+//          next unit's Q, K, V load
+// Numerics are those of attn_short_kernel: fp32 scores and softmax, P rounded
+// to bf16 for P V, fp32 accumulation.  Every mbarrier wait is bounded.
+#include "kernels.cuh"
+
+#include <cstdlib>
+
+namespace dtts {
+
+namespace {
+constexpr int kTcThreads = 128;
+constexpr int kTile = 128 * 128;             // bytes of one 128-row x 64-column bf16 tile
+// shared memory: Q | K (later P, two 64-key chunks) | V | V^T (two chunks of 64 rows) | barriers
+constexpr int kSmQ = 0, kSmK = kTile, kSmV = 2 * kTile, kSmVT = 3 * kTile, kSmBar = 3 * kTile + 64 * 128 * 2;
+constexpr int kTcSmem = kSmBar + 64 + 1024;  // + alignment slack
+constexpr uint32_t kIdescS = idesc_bf16(128, 128), kIdescO = idesc_bf16(128, 64);
+
+// byte offset of 16-byte unit u of row r in a K-major tile with 128-byte swizzle
+DTTS_DEV uint32_t sw128(int r, int u) { return (uint32_t)(r * 128 + ((u ^ (r & 7)) << 4)); }
+
+__global__ void __launch_bounds__(kTcThreads, 3)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int rows,
+                   const uint32_t *__restrict__ mask_bits, float scale_log2, int *err) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + kSmBar);
+    uint64_t *mma = full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int n_pairs = (rows + 1) / 2, units = n_pairs * kH;
+
+    if (tid == 0) {
+        mbar_init(full, 1);
+        mbar_init(mma, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tq); tma_prefetch_desc(&tk); tma_prefetch_desc(&tv);
+    }
+    if (warp == 0) { tmem_alloc(tmem_slot, 128); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+
+    // this thread's query row within the pair, its sequence (0 / 1) and its mask words
+    const int i = tid, s = i >> 6, qi = i & 63;
+    uint32_t m0 = ~0u, m1 = ~0u;
+    if (mask_bits) { m0 = mask_bits[qi * 2]; m1 = mask_bits[qi * 2 + 1]; }
+    const uint32_t trow = tbase + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's TMEM lanes
+
+    // Q, K, V of unit v into the tiles, completing on `full`
+    auto issue = [&](int v) {
+        const int pv = v / kH, hv = v % kH;
+        mbar_arrive_expect_tx(full, 3 * kTile);
+        tma_load_2d(sm + kSmQ, &tq, full, hv * kHD, pv * 128);
+        tma_load_2d(sm + kSmK, &tk, full, hv * kHD, pv * 128);
+        tma_load_2d(sm + kSmV, &tv, full, hv * kHD, pv * 128);
+    };
+    bool pending = false;   // a load of phase `ph` has been issued and not yet waited for
+    if (tid == 0 && (int)blockIdx.x < units) { issue(blockIdx.x); pending = true; }
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ph ^= 1u) {
+        const int pr = u / kH, h = u % kH;
+        // every wait is followed by a CTA-wide vote, so that all threads leave the loop together
+        if (__syncthreads_or(!mbar_wait(full, ph, abort_flag, err, DEVERR_TIMEOUT_PRODUCER))) break;
+        pending = false;
+        // ---- MMA 1: S = Q K^T (K = 64 head dims: four 16-element steps of 32 bytes)
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t qa = smem_u32(sm + kSmQ), ka = smem_u32(sm + kSmK);
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                tc_mma_bf16(tbase, sdesc_k128(qa + k * 32), sdesc_k128(ka + k * 32), kIdescS, k ? 1u : 0u);
+            tc_commit(mma);
+        }
+        // ---- meanwhile V^T: thread j holds key row j of V; V^T chunk c = j / 64 is
+        // [64 dims][64 keys] K-major with 128-byte swizzle
+        {
+            const int j = tid, c = j >> 6, kk = j & 63;
+            uint8_t *vt = sm + kSmVT + c * 64 * 128;
+#pragma unroll
+            for (int uu = 0; uu < 8; uu++) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(sm + kSmV + sw128(j, uu));
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int d = uu * 8 + e;
+                    const uint16_t val = static_cast<uint16_t>((ws[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu);
+                    *reinterpret_cast<uint16_t *>(vt + sw128(d, kk >> 3) + (kk & 7) * 2) = val;
+                }
+            }
+        }
+        // the mma barrier completes twice per unit: parity 0 after MMA 1, parity 1 after MMA 2
+        if (__syncthreads_or(!mbar_wait(mma, 0, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        // ---- softmax of query row i over its own sequence's 64 keys
+        float sv[64];
+        {
+            float a[32], b[32];
+            tmem_ld32(trow + s * 64, a);
+            tmem_ld32(trow + s * 64 + 32, b);
+#pragma unroll
+            for (int k = 0; k < 32; k++) { sv[k] = a[k]; sv[32 + k] = b[k]; }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 64; k++) {
+            const bool ok = ((k < 32 ? m0 >> k : m1 >> (k - 32)) & 1u) != 0;
+            sv[k] = ok ? sv[k] * scale_log2 : -INFINITY;
+            mx = fmaxf(mx, sv[k]);
+        }
+        const float mu = mx == -INFINITY ? 0.f : mx;
+        float l = 0.f;
+#pragma unroll
+        for (int k = 0; k < 64; k++) { sv[k] = exp2f(sv[k] - mu); l += sv[k]; }
+        // P row i over 128 keys, in the Q and K tiles (dead after MMA 1): key chunk c
+        // (keys 64 c .. 64 c + 63) at kSmQ + c * 16 KB; this sequence's chunk s holds
+        // the 64 probabilities, chunk 1 - s zeros
+        {
+            uint8_t *pc = sm + kSmQ + s * kTile, *pz = sm + kSmQ + (1 - s) * kTile;
+#pragma unroll
+            for (int uu = 0; uu < 8; uu++) {
+                uint4 w;
+                w.x = pack_bf16x2(sv[8 * uu + 0], sv[8 * uu + 1]);
+                w.y = pack_bf16x2(sv[8 * uu + 2], sv[8 * uu + 3]);
+                w.z = pack_bf16x2(sv[8 * uu + 4], sv[8 * uu + 5]);
+                w.w = pack_bf16x2(sv[8 * uu + 6], sv[8 * uu + 7]);
+                *reinterpret_cast<uint4 *>(pc + sw128(i, uu)) = w;
+                *reinterpret_cast<uint4 *>(pz + sw128(i, uu)) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        // ---- MMA 2: O = P V over 128 keys (eight 16-key steps); O into TMEM columns 0..63
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t pa = smem_u32(sm + kSmQ), va = smem_u32(sm + kSmVT);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t c = k >> 2, o = (k & 3) * 32;
+                tc_mma_bf16(tbase, sdesc_k128(pa + c * kTile + o), sdesc_k128(va + c * 64 * 128 + o), kIdescO,
+                            k ? 1u : 0u);
+            }
+            tc_commit(mma);
+        }
+        if (__syncthreads_or(!mbar_wait(mma, 1, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        // the tiles, P and V^T are free (MMA 2 is done, V was transposed before MMA 1
+        // was waited on): the next unit's tiles load during this unit's output stores
+        if (tid == 0 && u + (int)gridDim.x < units) { issue(u + gridDim.x); pending = true; }
+        // ---- O / l -> bf16, row i of the head's 64 columns
+        {
+            float a[32], b[32];
+            tmem_ld32(trow, a);
+            tmem_ld32(trow + 32, b);
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            if (2 * pr + s < rows) {
+                bf16 *og = out + (long long)(pr * 128 + i) * ldo + h * kHD;
+#pragma unroll
+                for (int uu = 0; uu < 4; uu++) {
+                    uint4 w;
+                    w.x = pack_bf16x2(a[8 * uu + 0] * inv, a[8 * uu + 1] * inv);
+                    w.y = pack_bf16x2(a[8 * uu + 2] * inv, a[8 * uu + 3] * inv);
+                    w.z = pack_bf16x2(a[8 * uu + 4] * inv, a[8 * uu + 5] * inv);
+                    w.w = pack_bf16x2(a[8 * uu + 6] * inv, a[8 * uu + 7] * inv);
+                    reinterpret_cast<uint4 *>(og)[uu] = w;
+                    w.x = pack_bf16x2(b[8 * uu + 0] * inv, b[8 * uu + 1] * inv);
+                    w.y = pack_bf16x2(b[8 * uu + 2] * inv, b[8 * uu + 3] * inv);
+                    w.z = pack_bf16x2(b[8 * uu + 4] * inv, b[8 * uu + 5] * inv);
+                    w.w = pack_bf16x2(b[8 * uu + 6] * inv, b[8 * uu + 7] * inv);
+                    reinterpret_cast<uint4 *>(og)[4 + uu] = w;
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();   // TMEM, P and the tiles are free for the next unit
+    }
+    // after an abort, wait (bounded) for a load still in flight so that no TMA write
+    // lands in shared memory after the CTA has exited
+    if (tid == 0 && pending) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(full, ph))
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 128);
+    }
+}
+}  // namespace
+
+cudaError_t attention_tc_prepare() {
+    return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+}
+
+bool attention_tc_eligible(const AttnArgs &a) {
+    static const bool on = [] {
+        const char *e = std::getenv("DTTS_ATTN_TC");
+        return !(e && e[0] == '0');
+    }();
+    return on && a.Tq == 64 && a.kv_len == 64 && a.kv_cap == 64 && !a.causal && !a.o8 && !a.kv_base_dev &&
+           (!a.mask || a.mask_bits) && a.ldq == kD && a.ldkv == kD && a.rows >= 1;
+}
+
+cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, bool pdl) {
+    if (!attention_tc_eligible(a)) return cudaErrorNotSupported;
+    const unsigned long long R = (unsigned long long)a.rows * 64;
+    CUtensorMap tq, tk, tv;
+    if (!make_tmap_bf16(&tq, a.q, R, kD, 128) || !make_tmap_bf16(&tk, a.k, R, kD, 128) ||
+        !make_tmap_bf16(&tv, a.v, R, kD, 128))
+        return cudaErrorInvalidValue;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int units = (a.rows + 1) / 2 * kH;
+    const int grid = units < 3 * nsm ? units : 3 * nsm;
+    const float sl = a.scale * 1.4426950408889634f;
+    return launch_k(pdl && pdl_enabled(), attn_tc_kernel, dim3(grid), dim3(kTcThreads), (size_t)kTcSmem, s, tq, tk,
+                    tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err);
+}
+
+}  // namespace dtts

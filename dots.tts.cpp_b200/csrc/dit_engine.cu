@@ -409,6 +409,7 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             a.mask = last_mask ? mask : nullptr;
             a.mask_bits = last_mask ? mask_bits : nullptr;
             a.scale = 1.0f / sqrtf(64.0f);
+            a.err = d_err;
             if (fp8()) { a.o8 = att8; a.o_scale = s_att; a.unorm = unorm; a.vbound = Ly.vbound; }
             launches++;
             launch_attention_bf16(a, stream);

@@ -550,7 +550,8 @@ void pack_mask_bits(const uint8_t *mask, int Tq, int kv_len, uint32_t *bits) {
 }
 
 cudaError_t attention_short_prepare() {
-    return cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kShortSmem);
+    cudaError_t e = cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kShortSmem);
+    return e != cudaSuccess ? e : attention_tc_prepare();
 }
 
 // Decode attention (a few queries per sequence against a long cache, causal,
@@ -680,6 +681,10 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl) {
     pdl = pdl && pdl_enabled();
     if (a.Tq <= 8 && !a.mask && !a.mask_bits && !a.o8 && (a.kv_base_dev || a.kv_len > 64)) {
         launch_k(pdl, attn_decode_kernel, dim3(a.rows * a.Tq * kH), dim3(kDecWarps * 32), 0, s, a);
+        return;
+    }
+    if (attention_tc_eligible(a)) {
+        launch_attention_tc(a, a.err, s, pdl);
         return;
     }
     if (a.Tq <= 64 && a.kv_len <= 64 && !a.kv_base_dev) {

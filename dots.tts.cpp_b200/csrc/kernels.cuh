@@ -65,10 +65,17 @@ struct AttnArgs {
     // if set (tiled kernel only): the cache length before this call is read
     // from device memory, q_pos0 = *kv_base_dev and kv_len = *kv_base_dev + Tq
     const int *kv_base_dev;
+    int *err;            // device error word for bounded-wait expiry (tensor-core kernel), or nullptr
 };
 // Tq <= 64 and kv_len <= 64 take the pipelined short-sequence kernel (call
 // attention_short_prepare() once per device first); longer ones the tiled kernel.
 void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl = false);
+// L = 64 on the tensor cores (attn_tc.cu): two sequences x one head per 128-row
+// tile; used by launch_attention_bf16 when eligible (Tq = kv_len = kv_cap = 64,
+// not causal, bf16 out, dense [rows * 64][1024] q/k/v; DTTS_ATTN_TC=0 turns it off).
+bool attention_tc_eligible(const AttnArgs &a);
+cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, bool pdl);
+cudaError_t attention_tc_prepare();
 // *len += add on the device (KV length of a graph-captured decode step)
 void launch_advance_len(int *len, int add, cudaStream_t s, bool pdl = false);
 cudaError_t attention_short_prepare();

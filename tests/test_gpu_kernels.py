@@ -54,6 +54,8 @@ def _attn_ref(q, k, v, mask=None, causal=False, q0=0):
     (2, 64, 64, False, 0, False), (2, 64, 64, False, 0, True), (3, 250, 250, True, 0, False),
     (4, 2, 130, True, 128, False), (2, 100, 100, False, 0, True), (1, 16, 16, False, 0, False),
     (2, 256, 256, False, 0, False),
+    # L = 64 on the tensor cores, an odd number of sequences (the last pair half empty)
+    (3, 64, 64, False, 0, True), (5, 64, 64, False, 0, False),
     # decode shapes (a few queries against a long cache)
     (3, 1, 500, False, 0, False), (2, 8, 1000, True, 992, False), (1, 5, 67, True, 62, False),
 ])
