@@ -8,9 +8,8 @@
 //          on the diagonal (each sequence against its own keys) are read
 //   all    thread i holds query row i: its 64 scores from TMEM, scaled by
 //          log2(e)/8, masked (-inf), max, exp2, sum; P (bf16) written K-major
-//          into shared memory with zeros off the diagonal block; meanwhile
-//          V is transposed in shared memory to V^T (dims x keys, K-major)
-//   MMA 2  O = P V (K = 128 keys) into TMEM columns 0..63
+//          into shared memory with zeros off the diagonal block
+//   MMA 2  O = P V (K = 128 keys; V read MN-major as loaded) into TMEM columns 0..63
 //   all    O / l to bf16, row i of the head's 64 output columns, while the
 //          next unit's Q, K, V load
 // Numerics are those of attn_short_kernel: fp32 scores and softmax, P rounded
@@ -24,15 +23,17 @@ namespace dtts {
 namespace {
 constexpr int kTcThreads = 128;
 constexpr int kTile = 128 * 128;             // bytes of one 128-row x 64-column bf16 tile
-// shared memory: Q | K (later P, two 64-key chunks) | V | V^T (two chunks of 64 rows) | barriers
-constexpr int kSmQ = 0, kSmK = kTile, kSmV = 2 * kTile, kSmVT = 3 * kTile, kSmBar = 3 * kTile + 64 * 128 * 2;
+// shared memory: Q | K (later P, two 64-key chunks) | V | barriers
+constexpr int kSmQ = 0, kSmK = kTile, kSmV = 2 * kTile, kSmBar = 3 * kTile;
 constexpr int kTcSmem = kSmBar + 64 + 1024;  // + alignment slack
-constexpr uint32_t kIdescS = idesc_bf16(128, 128), kIdescO = idesc_bf16(128, 64);
+// O = P V reads B = V in its loaded layout, N (head dims) contiguous: the
+// descriptor's transpose-B bit (16) marks B as MN-major
+constexpr uint32_t kIdescS = idesc_bf16(128, 128), kIdescO = idesc_bf16(128, 64) | (1u << 16);
 
 // byte offset of 16-byte unit u of row r in a K-major tile with 128-byte swizzle
 DTTS_DEV uint32_t sw128(int r, int u) { return (uint32_t)(r * 128 + ((u ^ (r & 7)) << 4)); }
 
-__global__ void __launch_bounds__(kTcThreads, 3)
+__global__ void __launch_bounds__(kTcThreads, 4)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int rows,
                    const uint32_t *__restrict__ mask_bits, float scale_log2, int *err) {
@@ -91,23 +92,6 @@ __global__ void __launch_bounds__(kTcThreads, 3)
                 tc_mma_bf16(tbase, sdesc_k128(qa + k * 32), sdesc_k128(ka + k * 32), kIdescS, k ? 1u : 0u);
             tc_commit(mma);
         }
-        // ---- meanwhile V^T: thread j holds key row j of V; V^T chunk c = j / 64 is
-        // [64 dims][64 keys] K-major with 128-byte swizzle
-        {
-            const int j = tid, c = j >> 6, kk = j & 63;
-            uint8_t *vt = sm + kSmVT + c * 64 * 128;
-#pragma unroll
-            for (int uu = 0; uu < 8; uu++) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(sm + kSmV + sw128(j, uu));
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    const int d = uu * 8 + e;
-                    const uint16_t val = static_cast<uint16_t>((ws[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu);
-                    *reinterpret_cast<uint16_t *>(vt + sw128(d, kk >> 3) + (kk & 7) * 2) = val;
-                }
-            }
-        }
         // the mma barrier completes twice per unit: parity 0 after MMA 1, parity 1 after MMA 2
         if (__syncthreads_or(!mbar_wait(mma, 0, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
         tc_fence_after();
@@ -153,19 +137,20 @@ __global__ void __launch_bounds__(kTcThreads, 3)
         // ---- MMA 2: O = P V over 128 keys (eight 16-key steps); O into TMEM columns 0..63
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t pa = smem_u32(sm + kSmQ), va = smem_u32(sm + kSmVT);
+            const uint32_t pa = smem_u32(sm + kSmQ), va = smem_u32(sm + kSmV);
 #pragma unroll
             for (int k = 0; k < 8; k++) {
+                // A = P, K-major: key chunk k / 4, 32 bytes per 16 keys; B = V as loaded
+                // ([keys][dims], dims contiguous: MN-major), 16 keys = two 1024-byte row groups
                 const uint32_t c = k >> 2, o = (k & 3) * 32;
-                tc_mma_bf16(tbase, sdesc_k128(pa + c * kTile + o), sdesc_k128(va + c * 64 * 128 + o), kIdescO,
-                            k ? 1u : 0u);
+                tc_mma_bf16(tbase, sdesc_k128(pa + c * kTile + o), sdesc_k128(va + k * 2048), kIdescO, k ? 1u : 0u);
             }
             tc_commit(mma);
         }
         if (__syncthreads_or(!mbar_wait(mma, 1, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
         tc_fence_after();
-        // the tiles, P and V^T are free (MMA 2 is done, V was transposed before MMA 1
-        // was waited on): the next unit's tiles load during this unit's output stores
+        // the tiles and P are free (MMA 2 is done): the next unit's tiles load during
+        // this unit's output stores
         if (tid == 0 && u + (int)gridDim.x < units) { issue(u + gridDim.x); pending = true; }
         // ---- O / l -> bf16, row i of the head's 64 columns
         {
@@ -234,7 +219,7 @@ cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, boo
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int units = (a.rows + 1) / 2 * kH;
-    const int grid = units < 3 * nsm ? units : 3 * nsm;
+    const int grid = units < 4 * nsm ? units : 4 * nsm;   // 4 resident CTAs per SM (49 KB, 128 TMEM columns)
     const float sl = a.scale * 1.4426950408889634f;
     return launch_k(pdl && pdl_enabled(), attn_tc_kernel, dim3(grid), dim3(kTcThreads), (size_t)kTcSmem, s, tq, tk,
                     tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err);
