@@ -10,8 +10,9 @@
 //          log2(e)/8, masked (-inf), max, exp2, sum; P (bf16) written K-major
 //          into shared memory with zeros off the diagonal block
 //   MMA 2  O = P V (K = 128 keys; V read MN-major as loaded) into TMEM columns 0..63
-//   all    O / l to bf16, row i of the head's 64 output columns, while the
-//          next unit's Q, K, V load
+//   all    O / l to bf16 (or to e4m3 with the sequence's scale bound, the FP8
+//          engine), row i of the head's 64 output columns, while the next
+//          unit's Q, K, V load
 // Numerics are those of attn_short_kernel: fp32 scores and softmax, P rounded
 // to bf16 for P V, fp32 accumulation.  Every mbarrier wait is bounded.
 #include "kernels.cuh"
@@ -36,7 +37,8 @@ DTTS_DEV uint32_t sw128(int r, int u) { return (uint32_t)(r * 128 + ((u ^ (r & 7
 __global__ void __launch_bounds__(kTcThreads, 4)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int rows,
-                   const uint32_t *__restrict__ mask_bits, float scale_log2, int *err) {
+                   const uint32_t *__restrict__ mask_bits, float scale_log2, int *err, uint8_t *__restrict__ o8,
+                   float *__restrict__ o_scale, const float *__restrict__ unorm, float vbound) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
@@ -152,13 +154,41 @@ __global__ void __launch_bounds__(kTcThreads, 4)
         // the tiles and P are free (MMA 2 is done): the next unit's tiles load during
         // this unit's output stores
         if (tid == 0 && u + (int)gridDim.x < units) { issue(u + gridDim.x); pending = true; }
-        // ---- O / l -> bf16, row i of the head's 64 columns
+        // ---- O / l -> bf16 (or e4m3 with the sequence's bound), row i of the head's 64 columns
         {
             float a[32], b[32];
             tmem_ld32(trow, a);
             tmem_ld32(trow + 32, b);
             const float inv = l > 0.f ? 1.0f / l : 0.f;
-            if (2 * pr + s < rows) {
+            const int r = 2 * pr + s;
+            if (o8) {
+                // |softmax . V| <= 1.02 max_j unorm_j max_d |Wv_d| over the sequence (AttnArgs)
+                float m = 0.f;
+                if (r < rows) {
+                    const int lane = tid & 31;
+                    m = fmaxf(__ldg(unorm + (long long)r * 64 + lane), __ldg(unorm + (long long)r * 64 + 32 + lane));
+                }
+                const float bnd = 1.02f * warp_max(m) * vbound;
+                const float f = inv * (bnd > 0.f ? 448.0f / bnd : 0.f);
+                if (r < rows) {
+                    uint8_t *og = o8 + (long long)(pr * 128 + i) * ldo + h * kHD;
+#pragma unroll
+                    for (int uu = 0; uu < 2; uu++) {
+                        uint4 w;
+                        w.x = pack_e4m3x4(a[16 * uu + 0] * f, a[16 * uu + 1] * f, a[16 * uu + 2] * f, a[16 * uu + 3] * f);
+                        w.y = pack_e4m3x4(a[16 * uu + 4] * f, a[16 * uu + 5] * f, a[16 * uu + 6] * f, a[16 * uu + 7] * f);
+                        w.z = pack_e4m3x4(a[16 * uu + 8] * f, a[16 * uu + 9] * f, a[16 * uu + 10] * f, a[16 * uu + 11] * f);
+                        w.w = pack_e4m3x4(a[16 * uu + 12] * f, a[16 * uu + 13] * f, a[16 * uu + 14] * f, a[16 * uu + 15] * f);
+                        reinterpret_cast<uint4 *>(og)[uu] = w;
+                        w.x = pack_e4m3x4(b[16 * uu + 0] * f, b[16 * uu + 1] * f, b[16 * uu + 2] * f, b[16 * uu + 3] * f);
+                        w.y = pack_e4m3x4(b[16 * uu + 4] * f, b[16 * uu + 5] * f, b[16 * uu + 6] * f, b[16 * uu + 7] * f);
+                        w.z = pack_e4m3x4(b[16 * uu + 8] * f, b[16 * uu + 9] * f, b[16 * uu + 10] * f, b[16 * uu + 11] * f);
+                        w.w = pack_e4m3x4(b[16 * uu + 12] * f, b[16 * uu + 13] * f, b[16 * uu + 14] * f, b[16 * uu + 15] * f);
+                        reinterpret_cast<uint4 *>(og)[2 + uu] = w;
+                    }
+                    if (h == 0) o_scale[(long long)r * 64 + qi] = bnd / 448.0f;
+                }
+            } else if (r < rows) {
                 bf16 *og = out + (long long)(pr * 128 + i) * ldo + h * kHD;
 #pragma unroll
                 for (int uu = 0; uu < 4; uu++) {
@@ -204,8 +234,9 @@ bool attention_tc_eligible(const AttnArgs &a) {
         const char *e = std::getenv("DTTS_ATTN_TC");
         return !(e && e[0] == '0');
     }();
-    return on && a.Tq == 64 && a.kv_len == 64 && a.kv_cap == 64 && !a.causal && !a.o8 && !a.kv_base_dev &&
-           (!a.mask || a.mask_bits) && a.ldq == kD && a.ldkv == kD && a.rows >= 1;
+    return on && a.Tq == 64 && a.kv_len == 64 && a.kv_cap == 64 && !a.causal && !a.kv_base_dev &&
+           (!a.mask || a.mask_bits) && (!a.o8 || (a.o_scale && a.unorm)) && a.ldq == kD && a.ldkv == kD &&
+           a.rows >= 1;
 }
 
 cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, bool pdl) {
@@ -222,7 +253,8 @@ cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, boo
     const int grid = units < 4 * nsm ? units : 4 * nsm;   // 4 resident CTAs per SM (49 KB, 128 TMEM columns)
     const float sl = a.scale * 1.4426950408889634f;
     return launch_k(pdl && pdl_enabled(), attn_tc_kernel, dim3(grid), dim3(kTcThreads), (size_t)kTcSmem, s, tq, tk,
-                    tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err);
+                    tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err, a.o8, a.o_scale,
+                    a.unorm, a.vbound);
 }
 
 }  // namespace dtts
