@@ -101,12 +101,14 @@ __global__ void __launch_bounds__(256) llm_rope_cache_kernel(float *__restrict__
     }
 }
 
-// Grouped-query causal attention, one warp per (token m, query head): lane
-// l owns dims 4l..4l+3; keys 0 .. pos0 + t of the token's sequence, eight at
-// a time (their K and V rows are loaded together and their dot products
-// reduced together, so the memory latency is paid once per eight keys);
-// online softmax in fp32; the output row goes to ao (bf16, the o_proj input).
-__global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__ q, const bf16 *__restrict__ kc,
+// Grouped-query causal attention, one warp per (token m, query head): the
+// lanes form two groups of 16 (g = lane / 16); lane c of group g owns dims
+// 8c .. 8c+7 of key 2u + g, so each 16-byte load instruction reads two whole
+// 256-byte K (or V) rows and a score needs a 4-step shuffle within the group.
+// Keys 0 .. pos0 + t of the token's sequence, 16 per round; online softmax in
+// fp32 (scores pre-scaled by log2(e) / sqrt(128), exp2); the two groups' P.V
+// are merged at the end; the output row goes to ao (bf16, the o_proj input).
+__global__ void __launch_bounds__(256, 2) llm_attn_kernel(const float *__restrict__ q, const bf16 *__restrict__ kc,
                                                        const bf16 *__restrict__ vc, int T, int pos0,
                                                        const int *__restrict__ pos_dev, int cap, int M,
                                                        bf16 *__restrict__ ao) {
@@ -117,55 +119,81 @@ __global__ void __launch_bounds__(256) llm_attn_kernel(const float *__restrict__
     if (wid >= M * kLNH) return;
     const int m = wid / kLNH, h = wid % kLNH, b = m / T, t = m % T;
     const int kvh = h * kLNKV / kLNH;
+    const int g = lane >> 4, c = lane & 15;
     const int n_keys = pos0 + t + 1;
-    const float scale = 1.0f / sqrtf((float)kLHD);
-    const float4 qv = reinterpret_cast<const float4 *>(q + (long long)m * kLH + h * kLHD)[lane];
-    const bf16 *kb = kc + ((long long)b * kLNKV + kvh) * cap * kLHD + 4 * lane;
-    const bf16 *vb = vc + ((long long)b * kLNKV + kvh) * cap * kLHD + 4 * lane;
-    constexpr int U = 8;
-    float mx = -INFINITY, l = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j0 = 0; j0 < n_keys; j0 += U) {
-        uint2 kr[U], vr[U];
+    const float sc = 1.4426950408889634f / sqrtf((float)kLHD);
+    float qv[8];
+    {
+        const float4 *q4 = reinterpret_cast<const float4 *>(q + (long long)m * kLH + h * kLHD + 8 * c);
+        const float4 a = q4[0], bq = q4[1];
+        qv[0] = a.x * sc; qv[1] = a.y * sc; qv[2] = a.z * sc; qv[3] = a.w * sc;
+        qv[4] = bq.x * sc; qv[5] = bq.y * sc; qv[6] = bq.z * sc; qv[7] = bq.w * sc;
+    }
+    const bf16 *kb = kc + ((long long)b * kLNKV + kvh) * cap * kLHD + 8 * c;
+    const bf16 *vb = vc + ((long long)b * kLNKV + kvh) * cap * kLHD + 8 * c;
+    constexpr int U = 8;   // key pairs per round
+    float mx = -INFINITY, l = 0.f, acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.f;
+    for (int j0 = 0; j0 < n_keys; j0 += 2 * U) {
+        uint4 kr[U], vr[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            const int j = min(j0 + u, n_keys - 1);   // past the end: a valid row, masked below
-            kr[u] = *reinterpret_cast<const uint2 *>(kb + (long long)j * kLHD);
-            vr[u] = *reinterpret_cast<const uint2 *>(vb + (long long)j * kLHD);
+            const int j = min(j0 + 2 * u + g, n_keys - 1);   // past the end: a valid row, masked below
+            kr[u] = *reinterpret_cast<const uint4 *>(kb + (long long)j * kLHD);
+            vr[u] = *reinterpret_cast<const uint4 *>(vb + (long long)j * kLHD);
         }
-        float sc[U];
+        float sv[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[u].x));
-            const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[u].y));
-            sc[u] = (qv.x * k01.x + qv.y * k01.y) + (qv.z * k23.x + qv.w * k23.y);
+            const uint32_t w[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+            float d = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                // bf16 pair -> two floats by bit placement (exact)
+                d = fmaf(qv[2 * i], __uint_as_float(w[i] << 16), d);
+                d = fmaf(qv[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u), d);
+            }
+            sv[u] = d;
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+        for (int o = 8; o > 0; o >>= 1)
 #pragma unroll
-            for (int u = 0; u < U; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+            for (int u = 0; u < U; u++) sv[u] += __shfl_xor_sync(0xffffffffu, sv[u], o);
         float bm = mx;
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            sc[u] = (j0 + u < n_keys) ? sc[u] * scale : -INFINITY;
-            bm = fmaxf(bm, sc[u]);
+            if (j0 + 2 * u + g >= n_keys) sv[u] = -INFINITY;
+            bm = fmaxf(bm, sv[u]);
         }
-        const float corr = expf(mx - bm);
-        acc.x *= corr; acc.y *= corr; acc.z *= corr; acc.w *= corr;
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+        const float corr = exp2f(mx - bm);
         l *= corr;
 #pragma unroll
+        for (int i = 0; i < 8; i++) acc[i] *= corr;
+#pragma unroll
         for (int u = 0; u < U; u++) {
-            const float e = expf(sc[u] - bm);
-            const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr[u].x));
-            const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vr[u].y));
-            acc.x += e * v01.x; acc.y += e * v01.y; acc.z += e * v23.x; acc.w += e * v23.y;
-            l += e;
+            const float p = exp2f(sv[u] - bm);
+            l += p;
+            const uint32_t w[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                acc[2 * i] = fmaf(p, __uint_as_float(w[i] << 16), acc[2 * i]);
+                acc[2 * i + 1] = fmaf(p, __uint_as_float(w[i] & 0xFFFF0000u), acc[2 * i + 1]);
+            }
         }
         mx = bm;
     }
-    const float inv = 1.0f / l;
-    reinterpret_cast<uint2 *>(ao + (long long)m * kLH + h * kLHD)[lane] =
-        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+    // merge the two key groups (lanes c and c + 16)
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
+    if (g == 0) {
+        const float inv = 1.0f / l;
+        reinterpret_cast<uint4 *>(ao + (long long)m * kLH + h * kLHD)[c] =
+            make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                       pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    }
 }
 
 // out[m][j] = gate / (1 + e^-gate) * up with gu[m] = gate[8960] | up[8960]
