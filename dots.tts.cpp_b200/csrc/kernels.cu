@@ -581,8 +581,8 @@ __global__ void __launch_bounds__(kDecWarps * 32, 8) attn_decode_kernel(const At
         const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
-            qv[2 * i] = f.x * sc; qv[2 * i + 1] = f.y * sc;
+            // bf16 pair -> two floats by bit placement (exact)
+            qv[2 * i] = __uint_as_float(w[i] << 16) * sc; qv[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u) * sc;
         }
     }
     const long long rbase = (long long)r * a.kv_cap * a.ldkv + h * kHD + 8 * c;
@@ -606,9 +606,8 @@ __global__ void __launch_bounds__(kDecWarps * 32, 8) attn_decode_kernel(const At
             float d = 0.f;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
-                d = fmaf(qv[2 * i], f.x, d);
-                d = fmaf(qv[2 * i + 1], f.y, d);
+                d = fmaf(qv[2 * i], __uint_as_float(w[i] << 16), d);
+                d = fmaf(qv[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u), d);
             }
             s[u] = d;
         }
@@ -635,9 +634,8 @@ __global__ void __launch_bounds__(kDecWarps * 32, 8) attn_decode_kernel(const At
             const uint32_t w[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
-                acc[2 * i] = fmaf(p, f.x, acc[2 * i]);
-                acc[2 * i + 1] = fmaf(p, f.y, acc[2 * i + 1]);
+                acc[2 * i] = fmaf(p, __uint_as_float(w[i] << 16), acc[2 * i]);
+                acc[2 * i + 1] = fmaf(p, __uint_as_float(w[i] & 0xFFFF0000u), acc[2 * i + 1]);
             }
         }
         mx = bm;
