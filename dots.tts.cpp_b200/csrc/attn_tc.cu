@@ -223,10 +223,194 @@ __global__ void __launch_bounds__(kTcThreads, 4)
         tmem_dealloc(tbase, 128);
     }
 }
+
+// Causal attention over a KV cache on tcgen05 (the PatchEncoder prefill, Tq >
+// 64 tokens per sequence): a unit is (sequence r, head h, 128-query tile qt).
+// Q rows r Tq + 128 qt .. (rows past the sequence belong to the next one and
+// are never stored); keys come from the cache rows r cap + 128 kb .. in blocks
+// of 128, as many as the tile's last query can see.  Per key block: S = Q K^T
+// (TMEM columns 0..127), online softmax in fp32 by the thread that owns the
+// query row (running max m, sum l, output O in registers rescaled by
+// exp2(m_old - m_new)), P (bf16) K-major in shared memory, cache rows past the
+// valid keys zeroed in V (they may hold anything), PV = P V (TMEM columns
+// 128..191, V read MN-major) added into O.  O / l to bf16 at the end.
+constexpr int kCaSmem = 5 * kTile + 64 + 1024;   // Q | K | V | P (two 64-key chunks) | barriers
+constexpr uint32_t kIdescPV = idesc_bf16(128, 64) | (1u << 16);
+
+__global__ void __launch_bounds__(kTcThreads, 2)
+    attn_tc_causal_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int B,
+                          int Tq, int cap, int q_pos0, int kv_len, float scale_log2, int *err) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sQ = sm, *sK = sm + kTile, *sV = sm + 2 * kTile, *sP = sm + 3 * kTile;
+    uint64_t *qbar = reinterpret_cast<uint64_t *>(sm + 5 * kTile);
+    uint64_t *kvbar = qbar + 1;
+    uint64_t *mma = qbar + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(qbar + 3);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int n_qt = (Tq + 127) / 128, units = B * kH * n_qt;
+    if (tid == 0) {
+        mbar_init(qbar, 1);
+        mbar_init(kvbar, 1);
+        mbar_init(mma, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tq); tma_prefetch_desc(&tk); tma_prefetch_desc(&tv);
+    }
+    if (warp == 0) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+    const uint32_t trow = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+    const int i = tid;
+    uint32_t qph = 0, kvph = 0;
+    int q_out = -1, kv_out = -1;   // parity of a load issued and not yet seen complete, or -1
+    bool failed = false;
+    for (int u = blockIdx.x; u < units && !failed; u += gridDim.x) {
+        const int qt = u % n_qt, h = (u / n_qt) % kH, r = u / (n_qt * kH);
+        const int q_row0 = qt * 128;                        // first query of the tile (within the sequence)
+        const int q_abs = q_pos0 + q_row0 + i;               // this thread's query position
+        const int last_q = min(Tq - 1, q_row0 + 127);
+        const int n_keys = min(kv_len, q_pos0 + last_q + 1);
+        const int n_kb = (n_keys + 127) / 128;
+        if (tid == 0) {
+            mbar_arrive_expect_tx(qbar, kTile);
+            tma_load_2d(sQ, &tq, qbar, h * kHD, r * Tq + q_row0);
+        }
+        q_out = (int)qph;
+        float o[64];
+#pragma unroll
+        for (int d = 0; d < 64; d++) o[d] = 0.f;
+        float m = -INFINITY, l = 0.f;
+        for (int kb = 0; kb < n_kb; kb++) {
+            if (tid == 0) {
+                mbar_arrive_expect_tx(kvbar, 2 * kTile);
+                tma_load_2d(sK, &tk, kvbar, h * kHD, r * cap + kb * 128);
+                tma_load_2d(sV, &tv, kvbar, h * kHD, r * cap + kb * 128);
+            }
+            kv_out = (int)kvph;
+            bool ok = true;
+            if (kb == 0) {
+                ok = mbar_wait(qbar, qph, abort_flag, err, DEVERR_TIMEOUT_PRODUCER);
+                if (ok) { q_out = -1; qph ^= 1u; }
+            }
+            if (ok) {
+                ok = mbar_wait(kvbar, kvph, abort_flag, err, DEVERR_TIMEOUT_PRODUCER);
+                if (ok) { kv_out = -1; kvph ^= 1u; }
+            }
+            if (__syncthreads_or(!ok)) { failed = true; break; }
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK);
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    tc_mma_bf16(tbase, sdesc_k128(qa + k * 32), sdesc_k128(ka + k * 32), kIdescS, k ? 1u : 0u);
+                tc_commit(mma);
+            }
+            // cache rows past the valid keys may hold anything: zero them in V
+            // (their P is 0, and 0 x NaN would not be)
+            const int valid = n_keys - kb * 128;
+            if (i >= valid) {
+#pragma unroll
+                for (int uu = 0; uu < 8; uu++) *reinterpret_cast<uint4 *>(sV + i * 128 + uu * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            if (__syncthreads_or(!mbar_wait(mma, 0, abort_flag, err, DEVERR_TIMEOUT_MMA))) { failed = true; break; }
+            tc_fence_after();
+            float sv[128];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float t32[32];
+                tmem_ld32(trow + c * 32, t32);
+#pragma unroll
+                for (int k = 0; k < 32; k++) sv[32 * c + k] = t32[k];
+            }
+            float mx = m;
+#pragma unroll
+            for (int k = 0; k < 128; k++) {
+                const int j = kb * 128 + k;
+                sv[k] = (j < n_keys && j <= q_abs) ? sv[k] * scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sv[k]);
+            }
+            const float mu = mx == -INFINITY ? 0.f : mx;
+            const float corr = exp2f(m - mu);   // m = -inf on the first block: 0
+            l *= corr;
+#pragma unroll
+            for (int k = 0; k < 128; k++) { sv[k] = exp2f(sv[k] - mu); l += sv[k]; }
+            m = mx;
+#pragma unroll
+            for (int c = 0; c < 2; c++)
+#pragma unroll
+                for (int uu = 0; uu < 8; uu++) {
+                    const float *pv = sv + 64 * c + 8 * uu;
+                    *reinterpret_cast<uint4 *>(sP + c * kTile + sw128(i, uu)) =
+                        make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
+                                   pack_bf16x2(pv[6], pv[7]));
+                }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t pa = smem_u32(sP), va = smem_u32(sV);
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const uint32_t c = k >> 2, off = (k & 3) * 32;
+                    tc_mma_bf16(tbase + 128, sdesc_k128(pa + c * kTile + off), sdesc_k128(va + k * 2048), kIdescPV,
+                                k ? 1u : 0u);
+                }
+                tc_commit(mma);
+            }
+            if (__syncthreads_or(!mbar_wait(mma, 1, abort_flag, err, DEVERR_TIMEOUT_MMA))) { failed = true; break; }
+            tc_fence_after();
+            {
+                float a[32], b2[32];
+                tmem_ld32(trow + 128, a);
+                tmem_ld32(trow + 160, b2);
+#pragma unroll
+                for (int d = 0; d < 32; d++) { o[d] = o[d] * corr + a[d]; o[32 + d] = o[32 + d] * corr + b2[d]; }
+            }
+            tc_fence_before();
+            __syncthreads();   // K, V, P and TMEM are free for the next key block
+        }
+        if (failed) break;
+        if (q_row0 + i < Tq) {
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            uint4 *og = reinterpret_cast<uint4 *>(out + (long long)(r * Tq + q_row0 + i) * ldo + h * kHD);
+#pragma unroll
+            for (int uu = 0; uu < 8; uu++)
+                og[uu] = make_uint4(pack_bf16x2(o[8 * uu] * inv, o[8 * uu + 1] * inv),
+                                    pack_bf16x2(o[8 * uu + 2] * inv, o[8 * uu + 3] * inv),
+                                    pack_bf16x2(o[8 * uu + 4] * inv, o[8 * uu + 5] * inv),
+                                    pack_bf16x2(o[8 * uu + 6] * inv, o[8 * uu + 7] * inv));
+        }
+    }
+    // after an abort, wait (bounded) for loads still in flight so that no TMA write
+    // lands in shared memory after the CTA has exited
+    if (tid == 0) {
+        const unsigned long long t0 = globaltimer_ns();
+        if (q_out >= 0)
+            while (!mbar_try_wait(qbar, (uint32_t)q_out) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+        if (kv_out >= 0)
+            while (!mbar_try_wait(kvbar, (uint32_t)kv_out) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 256);
+    }
+}
 }  // namespace
 
 cudaError_t attention_tc_prepare() {
-    return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_tc_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCaSmem);
 }
 
 bool attention_tc_eligible(const AttnArgs &a) {
@@ -255,6 +439,32 @@ cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, boo
     return launch_k(pdl && pdl_enabled(), attn_tc_kernel, dim3(grid), dim3(kTcThreads), (size_t)kTcSmem, s, tq, tk,
                     tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err, a.o8, a.o_scale,
                     a.unorm, a.vbound);
+}
+
+bool attention_tc_causal_eligible(const AttnArgs &a) {
+    static const bool on = [] {
+        const char *e = std::getenv("DTTS_ATTN_TC");
+        return !(e && e[0] == '0');
+    }();
+    return on && a.causal && a.Tq > 64 && !a.kv_base_dev && !a.mask && !a.mask_bits && !a.o8 && a.ldq == kD &&
+           a.ldkv == kD && a.rows >= 1 && a.q_pos0 >= 0 && a.kv_len >= a.q_pos0 + a.Tq && a.kv_len <= a.kv_cap;
+}
+
+cudaError_t launch_attention_tc_causal(const AttnArgs &a, int *err, cudaStream_t s, bool pdl) {
+    if (!attention_tc_causal_eligible(a)) return cudaErrorNotSupported;
+    CUtensorMap tq, tk, tv;
+    const unsigned long long RQ = (unsigned long long)a.rows * a.Tq, RK = (unsigned long long)a.rows * a.kv_cap;
+    if (!make_tmap_bf16(&tq, a.q, RQ, kD, 128) || !make_tmap_bf16(&tk, a.k, RK, kD, 128) ||
+        !make_tmap_bf16(&tv, a.v, RK, kD, 128))
+        return cudaErrorInvalidValue;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int units = a.rows * kH * ((a.Tq + 127) / 128);
+    const int grid = units < 2 * nsm ? units : 2 * nsm;   // 2 resident CTAs per SM (81 KB, 256 TMEM columns)
+    return launch_k(pdl && pdl_enabled(), attn_tc_causal_kernel, dim3(grid), dim3(kTcThreads), (size_t)kCaSmem, s, tq,
+                    tk, tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.Tq, a.kv_cap, a.q_pos0, a.kv_len,
+                    a.scale * 1.4426950408889634f, err);
 }
 
 }  // namespace dtts

@@ -75,6 +75,10 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl = false);
 // not causal, bf16 out, dense [rows * 64][1024] q/k/v; DTTS_ATTN_TC=0 turns it off).
 bool attention_tc_eligible(const AttnArgs &a);
 cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, bool pdl);
+// Causal attention of a prefill (Tq > 64) over the KV cache on the tensor cores:
+// 128-query tiles, 128-key blocks with an online softmax (attn_tc.cu).
+bool attention_tc_causal_eligible(const AttnArgs &a);
+cudaError_t launch_attention_tc_causal(const AttnArgs &a, int *err, cudaStream_t s, bool pdl);
 cudaError_t attention_tc_prepare();
 // *len += add on the device (KV length of a graph-captured decode step)
 void launch_advance_len(int *len, int add, cudaStream_t s, bool pdl = false);

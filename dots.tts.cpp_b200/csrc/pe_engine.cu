@@ -231,6 +231,7 @@ struct dtts_pe {
                 a.o = att; a.ldo = kD; a.rows = B; a.Tq = T; a.kv_len = cur_len + T; a.kv_cap = max_tokens;
                 a.q_pos0 = cur_len; a.causal = 1; a.mask = nullptr; a.scale = 1.0f / sqrtf(64.0f);
                 a.kv_base_dev = dev_pos ? d_len : nullptr;
+                a.err = d_err;
                 launches++;
                 launch_attention_bf16(a, stream, true);
             }
