@@ -83,6 +83,10 @@ struct EpiParams {
 __host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || epi == EPI_RESID_GATED; }
 
 constexpr int kRopeSmemRows = 64;   // sequences up to this length read RoPE from shared memory
+// Shared-memory RoPE row stride in float2: 32 pairs + 2 of padding (272 bytes).
+// Each lane reads its own token's row, so with 256-byte rows the 8 lanes of a
+// 16-byte load phase would all hit the same four banks; 272 bytes spreads them.
+constexpr int kRopeRowF2 = 34;
 
 template <int BN, int NW, int EPI, int F8 = 0>
 struct GemmCfg {
@@ -97,7 +101,7 @@ struct GemmCfg {
     static constexpr int BAR_BYTES = 256;
     // EPI_QKV: the q/k RMS gains (128 floats) and up to kRopeSmemRows rows of
     // the RoPE table staged in shared memory once per CTA
-    static constexpr int CONST_BYTES = EPI == EPI_QKV ? 512 + kRopeSmemRows * 256 : 0;
+    static constexpr int CONST_BYTES = EPI == EPI_QKV ? 512 + kRopeSmemRows * kRopeRowF2 * 8 : 0;
     static constexpr int STAGES_FIT = (SMEM_MAX - STAGE_STAGING - CONST_BYTES - BAR_BYTES - 1024) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
@@ -190,7 +194,8 @@ DTTS_DEV void load_bias32(float (&v)[32], const float *bias, int n0) {
 
 // Per-thread head transform for EPI_QKV: lo = head columns [0,32), hi = [32,64).
 // sgain: the q gains then the k gains (shared memory, ones where absent);
-// srope: RoPE rows kv_start.. in shared memory, or nullptr to read ep.rope.
+// srope: RoPE rows kv_start.. in shared memory (kRopeRowF2 float2 apart), or
+// nullptr to read ep.rope (32 float2 apart).
 // The RoPE rows are read with generic loads: they may be shared or global.
 DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&lo)[32], float (&hi)[32],
                                  const float *sgain, const float4 *srope, int kv_start) {
@@ -212,7 +217,7 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
             hi[4 * i + 0] *= inv * b.x; hi[4 * i + 1] *= inv * b.y; hi[4 * i + 2] *= inv * b.z; hi[4 * i + 3] *= inv * b.w;
         }
     }
-    const float4 *cs = srope ? srope + t * 16
+    const float4 *cs = srope ? srope + t * (kRopeRowF2 / 2)
                              : reinterpret_cast<const float4 *>(ep.rope + (long long)(kv_start + t) * 32);
     if (ep.rope_mode == ROPE_HALF) {
         // pairs (d, d + 32), frequency index d
@@ -419,7 +424,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             const bool rope_smem = ep.rope != nullptr && ep.tok_per_row <= kRopeSmemRows;
             if (rope_smem)
                 for (int i = et; i < ep.tok_per_row * 32; i += EPI_THREADS)
-                    rp[i] = __ldg(ep.rope + (long long)kv_start * 32 + i);
+                    rp[(i >> 5) * kRopeRowF2 + (i & 31)] = __ldg(ep.rope + (long long)kv_start * 32 + i);
             asm volatile("bar.sync 1, %0;\n" ::"r"(EPI_THREADS) : "memory");
             if (rope_smem) srope = reinterpret_cast<const float4 *>(rp);
         }
