@@ -47,7 +47,9 @@ cudaError_t launch_one(const GemmOp &op, int num_sms, cudaStream_t s) {
 template <int BN, int NW>
 cudaError_t dispatch_epi_f8(const GemmOp &op, int num_sms, cudaStream_t s) {
     switch (op.epi) {
-        case EPI_QKV: return launch_one<BN, EPI_QKV, NW, 1>(op, num_sms, s);
+        case EPI_QKV:
+            return op.ep.rope_mode == ROPE_ADJACENT ? launch_one<BN, EPI_QKV_ADJ, NW, 1>(op, num_sms, s)
+                                                    : launch_one<BN, EPI_QKV, NW, 1>(op, num_sms, s);
         case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED, NW, 1>(op, num_sms, s);
         case EPI_F32: return launch_one<BN, EPI_F32, NW, 1>(op, num_sms, s);
         case EPI_GELU_F8:
@@ -66,7 +68,9 @@ cudaError_t dispatch_epi(const GemmOp &op, int num_sms, cudaStream_t s) {
         case EPI_F32: return launch_one<BN, EPI_F32, NW>(op, num_sms, s);
         case EPI_RESID: return launch_one<BN, EPI_RESID, NW>(op, num_sms, s);
         case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED, NW>(op, num_sms, s);
-        case EPI_QKV: return launch_one<BN, EPI_QKV, NW>(op, num_sms, s);
+        case EPI_QKV:
+            return op.ep.rope_mode == ROPE_ADJACENT ? launch_one<BN, EPI_QKV_ADJ, NW>(op, num_sms, s)
+                                                    : launch_one<BN, EPI_QKV, NW>(op, num_sms, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -81,6 +85,7 @@ template <int BN, int NW>
 cudaError_t prepare_bn_f8() {
     cudaError_t e;
     if ((e = prepare_one<BN, NW, EPI_QKV, 1>()) != cudaSuccess) return e;
+    if ((e = prepare_one<BN, NW, EPI_QKV_ADJ, 1>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_F32, 1>()) != cudaSuccess) return e;
     if constexpr (BN % 128 == 0)
         if ((e = prepare_one<BN, NW, EPI_GELU_F8, 1>()) != cudaSuccess) return e;
@@ -96,7 +101,8 @@ cudaError_t prepare_bn() {
     if ((e = prepare_one<BN, NW, EPI_F32>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_RESID>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_RESID_GATED>()) != cudaSuccess) return e;
-    return prepare_one<BN, NW, EPI_QKV>();
+    if ((e = prepare_one<BN, NW, EPI_QKV>()) != cudaSuccess) return e;
+    return prepare_one<BN, NW, EPI_QKV_ADJ>();
 }
 
 }  // namespace

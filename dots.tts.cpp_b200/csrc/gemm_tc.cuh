@@ -42,6 +42,11 @@ enum EpiKind : int {
     EPI_RESID_GATED,  // resid   += gate[row] * (acc + bias)       (DiT gated residual)
     EPI_QKV,          // q/k/v split, optional per-head RMS norm, RoPE, bf16 stores
     EPI_GELU_F8,      // out_e4m3 = e4m3(gelu_tanh(acc + bias) * out_inv[row])  (DiT FFN1, FP8 path)
+    // EPI_QKV with adjacent-pair RoPE.  Callers ask for EPI_QKV and set
+    // ep.rope_mode; launch_gemm picks this instance for ROPE_ADJACENT, so each
+    // kernel compiles one rotation (with both in one body, the 8-warp bf16
+    // kernel spilled at its 168-register cap).
+    EPI_QKV_ADJ,
 };
 
 enum RopeMode : int { ROPE_HALF = 0, ROPE_ADJACENT = 1 };
@@ -81,6 +86,7 @@ struct EpiParams {
 };
 
 __host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || epi == EPI_RESID_GATED; }
+__host__ __device__ constexpr bool is_qkv(int epi) { return epi == EPI_QKV || epi == EPI_QKV_ADJ; }
 
 constexpr int kRopeSmemRows = 64;   // sequences up to this length read RoPE from shared memory
 // Shared-memory RoPE row stride in float2: 32 pairs + 2 of padding (272 bytes).
@@ -101,7 +107,7 @@ struct GemmCfg {
     static constexpr int BAR_BYTES = 256;
     // EPI_QKV: the q/k RMS gains (128 floats) and up to kRopeSmemRows rows of
     // the RoPE table staged in shared memory once per CTA
-    static constexpr int CONST_BYTES = EPI == EPI_QKV ? 512 + kRopeSmemRows * kRopeRowF2 * 8 : 0;
+    static constexpr int CONST_BYTES = is_qkv(EPI) ? 512 + kRopeSmemRows * kRopeRowF2 * 8 : 0;
     static constexpr int STAGES_FIT = (SMEM_MAX - STAGE_STAGING - CONST_BYTES - BAR_BYTES - 1024) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
@@ -197,6 +203,7 @@ DTTS_DEV void load_bias32(float (&v)[32], const float *bias, int n0) {
 // srope: RoPE rows kv_start.. in shared memory (kRopeRowF2 float2 apart), or
 // nullptr to read ep.rope (32 float2 apart).
 // The RoPE rows are read with generic loads: they may be shared or global.
+template <int MODE>
 DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&lo)[32], float (&hi)[32],
                                  const float *sgain, const float4 *srope, int kv_start) {
     if (sect == 2) return;  // v: plain
@@ -219,7 +226,7 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
     }
     const float4 *cs = srope ? srope + t * (kRopeRowF2 / 2)
                              : reinterpret_cast<const float4 *>(ep.rope + (long long)(kv_start + t) * 32);
-    if (ep.rope_mode == ROPE_HALF) {
+    if constexpr (MODE == ROPE_HALF) {
         // pairs (d, d + 32), frequency index d
 #pragma unroll
         for (int i = 0; i < 16; i++) {
@@ -413,7 +420,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
         const float4 *srope = nullptr;
         const int kv_start = ep.kv_start_dev ? *ep.kv_start_dev : ep.kv_start;
         const bool kv_dense = ep.kv_cap == ep.tok_per_row && kv_start == 0;
-        if constexpr (EPI == EPI_QKV) {
+        if constexpr (is_qkv(EPI)) {
             sgain = reinterpret_cast<float *>(sConst);
             float2 *rp = reinterpret_cast<float2 *>(sConst + 512);
             const int et = threadIdx.x - 64;
@@ -447,17 +454,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             float rs = 0.f;   // e4m3 row scale of this thread's row
             if constexpr (F8)
                 if (m_base + lane < M) rs = __ldg(ep.row_scale + m_base + lane);
-            if constexpr (EPI == EPI_QKV || EPI == EPI_BF16 || EPI == EPI_GELU_BF16 || EPI == EPI_SILU_BF16) {
+            if constexpr (is_qkv(EPI) || EPI == EPI_BF16 || EPI == EPI_GELU_BF16 || EPI == EPI_SILU_BF16) {
                 // 64 columns (one head / 128 bytes of bf16) per chunk
 #pragma unroll 1
                 for (int c = half; c < BN / 64; c += CSTEP) {
                     const int n0 = nb * BN + c * 64;
                     // the DiT QKV projection has no bias: bf16 QKV needs no column constants
-                    constexpr bool kCols = F8 || EPI != EPI_QKV;
+                    constexpr bool kCols = F8 || !is_qkv(EPI);
                     Col32 cl, ch;
                     if constexpr (kCols) {
-                        col32_load<F8 != 0>(cl, ep.col_scale, EPI == EPI_QKV ? nullptr : ep.bias, n0);
-                        col32_load<F8 != 0>(ch, ep.col_scale, EPI == EPI_QKV ? nullptr : ep.bias, n0 + 32);
+                        col32_load<F8 != 0>(cl, ep.col_scale, is_qkv(EPI) ? nullptr : ep.bias, n0);
+                        col32_load<F8 != 0>(ch, ep.col_scale, is_qkv(EPI) ? nullptr : ep.bias, n0 + 32);
                     }
                     float lo[32], hi[32];
                     tmem_ld32(tbase + c * 64, lo);
@@ -467,8 +474,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                         col32_apply<F8 != 0>(hi, ch, rs);
                     }
                     const int m_self = m_base + lane;
-                    if constexpr (EPI == EPI_QKV) {
-                        if (m_self < M) qkv_head_transform(ep, m_self, n0 >> 10, lo, hi, sgain, srope, kv_start);
+                    if constexpr (is_qkv(EPI)) {
+                        constexpr int kMode = EPI == EPI_QKV_ADJ ? ROPE_ADJACENT : ROPE_HALF;
+                        if (m_self < M) qkv_head_transform<kMode>(ep, m_self, n0 >> 10, lo, hi, sgain, srope, kv_start);
                     } else {
                         if constexpr (EPI == EPI_GELU_BF16) {
 #pragma unroll
@@ -489,7 +497,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                         const uint4 val = *reinterpret_cast<const uint4 *>(wbuf + stage_off(r, chunk));
                         if (m >= M) continue;
                         bf16 *dst;
-                        if constexpr (EPI == EPI_QKV) {
+                        if constexpr (is_qkv(EPI)) {
                             const int sect = n0 >> 10, col = (n0 & 1023) + chunk * 8;
                             if (sect == 0) {
                                 dst = ep.q + (long long)m * ep.ldq + col;
