@@ -467,8 +467,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                         col32_load<F8 != 0>(ch, ep.col_scale, is_qkv(EPI) ? nullptr : ep.bias, n0 + 32);
                     }
                     float lo[32], hi[32];
-                    tmem_ld32(tbase + c * 64, lo);
-                    tmem_ld32(tbase + c * 64 + 32, hi);
+                    tmem_ld32x2(tbase + c * 64, tbase + c * 64 + 32, lo, hi);
                     if constexpr (kCols) {
                         col32_apply<F8 != 0>(lo, cl, rs);
                         col32_apply<F8 != 0>(hi, ch, rs);
