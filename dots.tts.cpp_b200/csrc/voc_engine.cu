@@ -738,7 +738,10 @@ int dtts_voc_create(const dtts_voc_weights *w, int device, int max_frames, dtts_
 int dtts_voc_destroy(dtts_voc *v) {
     if (!v) return DTTS_OK;
     DeviceGuard g(v->device);
+    // a decode that failed between fork and join can leave work on the side streams
     cudaStreamSynchronize(v->stream);
+    for (int i = 0; i < 2; i++)
+        if (v->side[i]) cudaStreamSynchronize(v->side[i]);
     delete v;
     return DTTS_OK;
 }
