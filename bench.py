@@ -435,11 +435,42 @@ def measure_pe(args, local_rank):
             "dtype": "bf16"}
 
 
-def measure_llm(args, local_rank):
+def cpu_llm_reference(w, layers, batch):
+    """The reference's own llm_kv_cache_init / llm_kv_cache_step (oracle/_ref) on
+    one sequence on the host: a 1-token prompt alone, then with one step; the
+    step time is the difference.  None when oracle/_ref is absent."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    import synth
+    if not O.Reference.available():
+        return None
+    try:
+        ref = O.Reference()
+        p1 = synth.normal(4, "llm.cpu_prompt", (1, 1536), 1.0)
+        s1 = synth.normal(4, "llm.cpu_step", (1, 1536), 1.0)
+        t0 = time.perf_counter()
+        ref.llm_run(w, layers, p1, s1[:0])
+        t1 = time.perf_counter()
+        ref.llm_run(w, layers, p1, s1)
+        t2 = time.perf_counter()
+    except Exception as e:   # the device figures stand without the CPU sample
+        return {"error": str(e)[:200]}
+    step_s = max(1e-9, (t2 - t1) - (t1 - t0))
+    return {"step_ms_per_sequence": step_s * 1000.0, "steps_per_s": 1.0 / (step_s * batch), "cores": 1,
+            "kind": "reference",
+            "sample": "one sequence through the reference's llm_kv_cache_init / llm_kv_cache_step "
+                      "(oracle/_ref, single-threaded loops), %d layers: a 1-token prompt alone, then with "
+                      "one step; the step is the difference (%.1f s in all). steps_per_s is for %d "
+                      "sequences, which the reference steps one after another" % (layers, t2 - t0, batch)}
+
+
+def measure_llm(args, local_rank, cpu_sample=False):
     """LLM decoder step at the autoregressive loop's batch: 28 layers of
     Qwen2.5-1.5B (synthetic weights), 64 sequences prefilled with 64-token
     prompts, then 16 steps of one embedding each (device-resident inputs,
-    CUDA events on the engine stream, one host call per step)."""
+    CUDA events on the engine stream, one host call per step).  cpu_sample:
+    time the reference's own llm_kv_cache_init / llm_kv_cache_step on one
+    sequence on the host (oracle/_ref), if present."""
     import torch
     import dtts
     import synth
@@ -447,7 +478,8 @@ def measure_llm(args, local_rank):
     B, n_tok, steps, layers = args.n_utt, 64, 16, 28
     w = synth.llm_weights(3, n_layers=layers)
     llm = dtts.LLM(w, n_layers=layers, max_batch=B, max_seq=n_tok + steps + 1, device=local_rank)
-    del w
+    if not cpu_sample:
+        del w
     stream = torch.cuda.Stream(device=dev)
     llm.set_stream(stream.cuda_stream)
     emb = torch.from_numpy(synth.normal(4, "llm.bench", (B, n_tok + steps, 1536), 1.0)).to(dev)
@@ -468,9 +500,13 @@ def measure_llm(args, local_rank):
     pre_ms, st_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]) / steps
     llm.close()
     weight_bytes = layers * 2 * (1536 * 2048 + 1536 * 1536 + 2 * 8960 * 1536 + 8960 * 1536)
-    return {"workload": f"LLM decoder, {layers} layers, {B} sequences: {n_tok}-token prefill, then {steps} steps",
-            "prefill_ms": pre_ms, "step_ms": st_ms, "steps_per_s": 1000.0 / st_ms,
-            "step_weight_stream_gbs": weight_bytes / (st_ms / 1000.0) / 1e9, "dtype": "bf16"}
+    res = {"workload": f"LLM decoder, {layers} layers, {B} sequences: {n_tok}-token prefill, then {steps} steps",
+           "prefill_ms": pre_ms, "step_ms": st_ms, "steps_per_s": 1000.0 / st_ms,
+           "step_weight_stream_gbs": weight_bytes / (st_ms / 1000.0) / 1e9, "dtype": "bf16"}
+    if cpu_sample:
+        res["cpu_reference"] = cpu_llm_reference(w, layers, B)
+        del w
+    return res
 
 
 def measure_voc(args, local_rank, cpu_sample):
@@ -596,7 +632,8 @@ def run_ours(args, rank, world, local_rank):
     head = measure(args, head_dtype, world, local_rank, dist, inputs)
     extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
     pe = measure_pe(args, local_rank) if (world == 1 and not args.no_pe) else None
-    llm = measure_llm(args, local_rank) if (world == 1 and not args.no_llm) else None
+    llm = measure_llm(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
+        if (world == 1 and not args.no_llm) else None
     voc = measure_voc(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
         if (world == 1 and not args.no_voc) else None
     attn1 = measure_attn_sublayer(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
