@@ -393,12 +393,35 @@ def measure(args, dtype, world, local_rank, dist, inputs):
             "gpu_launches": launches_per_solve * args.steps}
 
 
-def measure_pe(args, local_rank):
+def cpu_pe_port(w, layers, frames):
+    """One stream's prefill through the oracle's fp32 restatement of
+    patchenc_forward (oracle/oracle.c, OpenMP over the host threads): the CPU
+    line for the PatchEncoder, whose reference path (ggml) is not vendored."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    import synth
+    try:
+        orc = O.Oracle()
+        fr = synth.normal(2, "pe.cpu", (frames, 128), 1.0)
+        t0 = time.perf_counter()
+        orc.pe_forward(w, layers, fr)
+        secs = time.perf_counter() - t0
+        cores = orc.num_threads()
+    except Exception as e:   # the device figures stand without the CPU sample
+        return {"error": str(e)[:200]}
+    return {"prefill_frames_per_s": frames / secs, "cores": cores, "kind": "port",
+            "sample": "one stream's %d-frame prefill, %d layers, through oracle/oracle.c (the fp32 "
+                      "restatement of src/modules/backbone/patchenc.cpp; the reference's ggml build is not "
+                      "vendored), %.1f s" % (frames, layers, secs)}
+
+
+def measure_pe(args, local_rank, cpu_sample=False):
     """PatchEncoder stream at the PatchEncoder workload: 32 streams, a 500-frame
     prefill (250 tokens each), then 125 one-patch decode steps against the KV
     cache; 24 layers, bf16, device-resident frames, CUDA events on the engine
     stream.  The decode steps are launched one host call at a time, as a
-    streaming caller would, so launch gaps count."""
+    streaming caller would, so launch gaps count.  cpu_sample: time one
+    stream's prefill through the oracle's restatement on the host."""
     import torch
     import dtts
     import synth
@@ -428,11 +451,14 @@ def measure_pe(args, local_rank):
     pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
     pe.close()
     flop_pre = B * 24 * (prefill // 2) * 2 * (4 * 1024 * 1024 + 2 * 1024 * 4096)
-    return {"workload": "PatchEncoder, 24 layers, 32 streams: 500-frame prefill, then 125 decode steps",
-            "prefill_ms": pre_ms, "prefill_frames_per_s": B * prefill / (pre_ms / 1000.0),
-            "prefill_gemm_tflops": flop_pre / (pre_ms / 1000.0) / 1e12,
-            "decode_ms_per_step": dec_ms / steps, "decode_patches_per_s": B * steps / (dec_ms / 1000.0),
-            "dtype": "bf16"}
+    res = {"workload": "PatchEncoder, 24 layers, 32 streams: 500-frame prefill, then 125 decode steps",
+           "prefill_ms": pre_ms, "prefill_frames_per_s": B * prefill / (pre_ms / 1000.0),
+           "prefill_gemm_tflops": flop_pre / (pre_ms / 1000.0) / 1e12,
+           "decode_ms_per_step": dec_ms / steps, "decode_patches_per_s": B * steps / (dec_ms / 1000.0),
+           "dtype": "bf16"}
+    if cpu_sample:
+        res["cpu_port"] = cpu_pe_port(w, 24, prefill)
+    return res
 
 
 def cpu_llm_reference(w, layers, batch):
@@ -631,7 +657,8 @@ def run_ours(args, rank, world, local_rank):
     head_dtype = "fp8" if args.dtype == "fp8" else "bf16"
     head = measure(args, head_dtype, world, local_rank, dist, inputs)
     extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
-    pe = measure_pe(args, local_rank) if (world == 1 and not args.no_pe) else None
+    pe = measure_pe(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
+        if (world == 1 and not args.no_pe) else None
     llm = measure_llm(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
         if (world == 1 and not args.no_llm) else None
     voc = measure_voc(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
