@@ -1244,4 +1244,14 @@ int dtts_fm_solve(dtts_fm *f, const dtts_solve_args *a) {
     return euler_solve_impl(f->e, &b, f->cap);
 }
 
+int dtts_fm_layout(int total, int fm_len, int patch, int hidden_patch, uint8_t *mask, float *pos) {
+    DTTS_CHECK(mask || pos, DTTS_ERR_ARG, "null argument");
+    DTTS_CHECK(total >= 1 && patch >= 0 && fm_len >= 0 && fm_len + patch <= total && hidden_patch >= 0,
+               DTTS_ERR_ARG, "bad layout total=%d fm_len=%d patch=%d hidden_patch=%d", total, fm_len, patch,
+               hidden_patch);
+    if (mask) fm_mask(mask, total, fm_len, patch, hidden_patch);
+    if (pos) fm_pos(pos, total, fm_len, patch);
+    return DTTS_OK;
+}
+
 }  // extern "C"

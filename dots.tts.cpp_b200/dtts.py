@@ -110,7 +110,7 @@ EXPORTS = [
     "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_solve_timeline",
     "dtts_dit_profile_kernel",
     "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_fm_create", "dtts_fm_destroy", "dtts_fm_start",
-    "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve",
+    "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve", "dtts_fm_layout",
     "dtts_llm_create", "dtts_llm_destroy", "dtts_llm_set_stream", "dtts_llm_prefill", "dtts_llm_step", "dtts_llm_length",
     "dtts_voc_create", "dtts_voc_destroy", "dtts_voc_set_stream", "dtts_voc_decode", "dtts_voc_aa_filter",
     "dtts_selftest_voc_activation", "dtts_selftest_wait_limit", "dtts_selftest_conv", "dtts_attn_create", "dtts_attn_destroy", "dtts_attn_forward",
@@ -238,6 +238,7 @@ def lib(path: str = LIB_PATH):
     L.dtts_selftest_gemm_e4m3.argtypes = [_u8p, _fp, _u8p, _fp, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
                                           C.c_int]
     L.dtts_fp8_quantize_rows.argtypes = [_fp, C.c_int, C.c_int, _u8p, _fp]
+    L.dtts_fm_layout.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u8p, _fp]
     _LIB = L
     return L
 
@@ -796,6 +797,15 @@ def fp8_quantize_rows(w):
     sc = np.zeros(w.shape[0], np.float32)
     check(lib().dtts_fp8_quantize_rows(_ptr(w), w.shape[0], w.shape[1], q.ctypes.data_as(_u8p), _ptr(sc)))
     return q, sc
+
+
+def fm_layout(total, fm_len, patch, hidden_patch=1):
+    """The attention mask (uint8 [total][total]) and position ids ([total]) a solve
+    builds for fm_len history rows and `patch` noise rows (host only)."""
+    m = np.zeros((total, total), np.uint8)
+    p = np.zeros(total, np.float32)
+    check(lib().dtts_fm_layout(total, fm_len, patch, hidden_patch, m.ctypes.data_as(_u8p), _ptr(p)))
+    return m, p
 
 
 class SafeTensors:

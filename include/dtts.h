@@ -221,6 +221,13 @@ int dtts_fm_read(dtts_fm *f, float *cond, float *uncond);
  * taken from f; a->z0, spk, z_out (and a->mem, which describes them) as in dtts_dit_euler_solve. */
 int dtts_fm_solve(dtts_fm *f, const dtts_solve_args *a);
 
+/* Host only (no device needed): the attention mask and position ids a solve builds for
+ * `total` rows of which the first fm_len are history and the last `patch` are noise
+ * (build_fm_attn_mask / build_fm_pos_ids, src/e2e_pipeline_v4.cpp:120-155; the solve uses
+ * total = fm_len + patch and hidden_patch = 1).  mask [total][total] uint8 (1 = attend) and
+ * pos [total], either may be NULL. */
+int dtts_fm_layout(int total, int fm_len, int patch, int hidden_patch, uint8_t *mask, float *pos);
+
 /* Launch kinds of dtts_dit_solve_timeline. */
 #define DTTS_TL_GEMM_QKV       0   /* QKV projection + qk-norm + RoPE epilogue  */
 #define DTTS_TL_GEMM_O         1   /* attention output projection, gated residual */

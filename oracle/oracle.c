@@ -641,25 +641,64 @@ static void rope_adjacent(float *v, int p) {
     }
 }
 
+/* causal Conv1d(128->128, k=2, s=2) with taps at frames 2o-1 and 2o
+ * (patchenc.cpp:19-39): frames [seq][128] -> out [seq/2][128]. */
+void orc_pe_conv(float *out, const float *frames, int seq, const float *w, const float *b) {
+    const int C = ORC_LAT, T = seq / 2;
+    for (int o = 0; o < T; o++)
+        for (int oc = 0; oc < C; oc++) {
+            float s = b ? b[oc] : 0.0f;
+            for (int ic = 0; ic < C; ic++) {
+                int wb = (oc * C + ic) * 2;
+                int i0 = 2 * o - 1;
+                if (i0 >= 0 && i0 < seq) s += frames[(size_t)i0 * C + ic] * w[wb + 0];
+                int i1 = 2 * o;
+                if (i1 >= 0 && i1 < seq) s += frames[(size_t)i1 * C + ic] * w[wb + 1];
+            }
+            out[(size_t)o * C + oc] = s;
+        }
+}
+
+/* causal per-head softmax(QK^T/8)V over 16 heads of 64 (patchenc.cpp:59-101):
+ * q, k, v, ctx [T][1024]. */
+void orc_pe_causal_attention(float *ctx, const float *q, const float *k, const float *v, int T) {
+    const int D = ORC_D;
+    const float scale = 1.0f / sqrtf((float)ORC_HD);
+    #pragma omp parallel
+    {
+        float *s = (float *)malloc((size_t)T * sizeof(float));
+        #pragma omp for collapse(2) schedule(static)
+        for (int hh = 0; hh < ORC_H; hh++)
+            for (int ti = 0; ti < T; ti++) {
+                for (int tj = 0; tj < T; tj++) {
+                    float acc = 0.0f;
+                    for (int d = 0; d < ORC_HD; d++)
+                        acc += q[(size_t)ti * D + hh * ORC_HD + d] * k[(size_t)tj * D + hh * ORC_HD + d];
+                    s[tj] = acc * scale;
+                }
+                for (int tj = ti + 1; tj < T; tj++) s[tj] = -INFINITY;
+                float mx = s[0];
+                for (int tj = 1; tj < T; tj++) if (s[tj] > mx) mx = s[tj];
+                float sum = 0.0f;
+                for (int tj = 0; tj < T; tj++) { s[tj] = expf(s[tj] - mx); sum += s[tj]; }
+                for (int tj = 0; tj < T; tj++) s[tj] /= sum;
+                for (int d = 0; d < ORC_HD; d++) {
+                    float acc = 0.0f;
+                    for (int tj = 0; tj < T; tj++) acc += s[tj] * v[(size_t)tj * D + hh * ORC_HD + d];
+                    ctx[(size_t)ti * D + hh * ORC_HD + d] = acc;
+                }
+            }
+        free(s);
+    }
+}
+
 void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pair_mode,
                     float *out, float *h_last) {
     const int D = ORC_D, C = ORC_LAT;
     int seq = n_patches * 4;
     int T = seq / 2;
-    /* causal Conv1d(128->128, k=2, s=2), taps at frames 2o-1 and 2o (patchenc.cpp:19-39) */
     float *xc = (float *)malloc((size_t)T * C * sizeof(float));
-    for (int o = 0; o < T; o++)
-        for (int oc = 0; oc < C; oc++) {
-            float s = m->conv_b ? m->conv_b[oc] : 0.0f;
-            for (int ic = 0; ic < C; ic++) {
-                int wb = (oc * C + ic) * 2;
-                int i0 = 2 * o - 1;
-                if (i0 >= 0 && i0 < seq) s += frames[(size_t)i0 * C + ic] * m->conv_w[wb + 0];
-                int i1 = 2 * o;
-                if (i1 >= 0 && i1 < seq) s += frames[(size_t)i1 * C + ic] * m->conv_w[wb + 1];
-            }
-            xc[(size_t)o * C + oc] = s;
-        }
+    orc_pe_conv(xc, frames, seq, m->conv_w, m->conv_b);
     size_t n = (size_t)T * D;
     float *h = (float *)malloc(n * sizeof(float));
     orc_linear_rows(h, xc, T, m->in_w, m->in_b, C, D);
@@ -671,7 +710,6 @@ void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pai
     float *ao = (float *)malloc(n * sizeof(float));
     float *f1 = (float *)malloc((size_t)T * ORC_F * sizeof(float));
     float *f2 = (float *)malloc(n * sizeof(float));
-    const float scale = 1.0f / sqrtf((float)ORC_HD);
     for (int li = 0; li < m->n_layers; li++) {
         const orc_pe_layer *l = &m->layers[li];
         for (int t = 0; t < T; t++) rms_norm_w(xn + (size_t)t * D, h + (size_t)t * D, l->attn_norm_w, D, 1e-6f);
@@ -684,33 +722,7 @@ void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pai
                 rope_adjacent(q + (size_t)t * D + hh * ORC_HD, t);
                 rope_adjacent(k + (size_t)t * D + hh * ORC_HD, t);
             }
-        /* causal per-head attention (patchenc.cpp:59-101) */
-        #pragma omp parallel
-        {
-            float *s = (float *)malloc((size_t)T * sizeof(float));
-            #pragma omp for collapse(2) schedule(static)
-            for (int hh = 0; hh < ORC_H; hh++)
-                for (int ti = 0; ti < T; ti++) {
-                    for (int tj = 0; tj < T; tj++) {
-                        float acc = 0.0f;
-                        for (int d = 0; d < ORC_HD; d++)
-                            acc += q[(size_t)ti * D + hh * ORC_HD + d] * k[(size_t)tj * D + hh * ORC_HD + d];
-                        s[tj] = acc * scale;
-                    }
-                    for (int tj = ti + 1; tj < T; tj++) s[tj] = -INFINITY;
-                    float mx = s[0];
-                    for (int tj = 1; tj < T; tj++) if (s[tj] > mx) mx = s[tj];
-                    float sum = 0.0f;
-                    for (int tj = 0; tj < T; tj++) { s[tj] = expf(s[tj] - mx); sum += s[tj]; }
-                    for (int tj = 0; tj < T; tj++) s[tj] /= sum;
-                    for (int d = 0; d < ORC_HD; d++) {
-                        float acc = 0.0f;
-                        for (int tj = 0; tj < T; tj++) acc += s[tj] * v[(size_t)tj * D + hh * ORC_HD + d];
-                        ctx[(size_t)ti * D + hh * ORC_HD + d] = acc;
-                    }
-                }
-            free(s);
-        }
+        orc_pe_causal_attention(ctx, q, k, v, T);
         orc_linear_rows(ao, ctx, T, l->wo, l->bo, D, D);
         for (size_t i = 0; i < n; i++) h[i] += ao[i];
         for (int t = 0; t < T; t++) rms_norm_w(xn + (size_t)t * D, h + (size_t)t * D, l->ffn_norm_w, D, 1e-6f);

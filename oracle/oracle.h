@@ -126,6 +126,11 @@ void orc_euler_solve(const orc_dit *m, int n_utt, int fm_len, int patch,
 
 void orc_pe_forward(const orc_pe *m, const float *frames, int n_patches, int pair_mode,
                     float *out, float *h_last);
+/* The two PatchEncoder pieces the reference writes as plain C (patchenc.cpp:19-39,
+ * :59-101), for comparison with the reference's own: frames [seq][128] -> out
+ * [seq/2][128]; q, k, v, ctx [T][1024]. */
+void orc_pe_conv(float *out, const float *frames, int seq, const float *w, const float *b);
+void orc_pe_causal_attention(float *ctx, const float *q, const float *k, const float *v, int T);
 
 
 /* ---------------------------------------------------------------- vocoder

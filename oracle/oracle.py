@@ -271,6 +271,8 @@ class Oracle:
         L.orc_euler_solve.argtypes = [C.POINTER(Dit), C.c_int, C.c_int, C.c_int, _fp, _fp, _fp, _fp,
                                       C.c_float, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, _fp]
         L.orc_pe_forward.argtypes = [C.POINTER(Pe), _fp, C.c_int, C.c_int, _fp, _fp]
+        L.orc_pe_conv.argtypes = [_fp, _fp, C.c_int, _fp, _fp]
+        L.orc_pe_causal_attention.argtypes = [_fp, _fp, _fp, _fp, C.c_int]
         L.orc_linear_rows.argtypes = [_fp, _fp, C.c_int, _fp, _fp, C.c_int, C.c_int]
         L.orc_voc_decode.argtypes = [C.POINTER(Voc), _fp, _fp, C.c_int, _fp]
         L.orc_voc_activation.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp, _fp, C.c_int]
@@ -413,6 +415,21 @@ class Oracle:
         self.lib.orc_pe_forward(C.byref(m), _ptr(frames), n_patches, pair_mode, _ptr(out), _ptr(h))
         return (out, h) if want_hidden else out
 
+    def pe_conv(self, x, wc, bc=None):
+        """Causal stride-2 conv (patchenc.cpp:19-39): x [T][128] -> [T // 2][128]."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros((x.shape[0] // 2, 128), np.float32)
+        self.lib.orc_pe_conv(_ptr(out), _ptr(x), x.shape[0], _ptr(np.ascontiguousarray(wc, np.float32)),
+                             _ptr(None if bc is None else np.ascontiguousarray(bc, np.float32)))
+        return out
+
+    def pe_causal_attention(self, q, k, v):
+        """Causal per-head attention (patchenc.cpp:59-101): [T][1024] each -> [T][1024]."""
+        q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+        out = np.zeros_like(q)
+        self.lib.orc_pe_causal_attention(_ptr(out), _ptr(q), _ptr(k), _ptr(v), q.shape[0])
+        return out
+
     def linear_rows(self, x, w, b=None):
         x = np.ascontiguousarray(x, np.float32)
         out = np.zeros((x.shape[0], w.shape[0]), np.float32)
@@ -429,7 +446,7 @@ class Reference:
 
     def __init__(self, path: str = REF_PATH):
         if not os.path.exists(path):
-            raise FileNotFoundError(f"{path} missing: run `make -C oracle` where the reference tree exists")
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle REF=<reference tree>`")
         self.lib = C.CDLL(path)
         L = self.lib
         L.ref_num_threads.restype = C.c_int
@@ -440,6 +457,126 @@ class Reference:
         L.ref_llm_run.argtypes = [C.c_int, C.POINTER(_RefLLMLayer), _fp, _fp, C.c_int, _fp, C.c_int, _fp, _fp]
         L.ref_voc_decode.argtypes = [C.POINTER(Voc), _fp, C.c_int, _fp]
         L.ref_voc_decode.restype = C.c_int
+        # pieces of src/e2e_pipeline_v4.cpp and src/modules/backbone/patchenc.cpp (ref_pipeline.cpp)
+        L.ref_gen_ranges.restype = C.c_char_p
+        L.ref_set_solve_ffn.argtypes = [C.c_int]
+        L.ref_compute_cond.argtypes = [C.POINTER(Dit), C.c_float, _fp, C.c_float, _fp]
+        L.ref_fm_mask.argtypes = [_u8p, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.ref_fm_pos.argtypes = [_fp, C.c_int, C.c_int, C.c_int]
+        L.ref_latent_proj.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp]
+        L.ref_hidden_proj.argtypes = [C.POINTER(Dit), _fp, _fp]
+        L.ref_coord_proj.argtypes = [C.POINTER(Dit), _fp, _fp]
+        L.ref_eos_prob.argtypes = [_fp, _fp, _fp, _fp, _fp]
+        L.ref_eos_prob.restype = C.c_float
+        L.ref_solve_patch.argtypes = [C.POINTER(Dit), _fp, _fp, C.c_int, _fp, C.c_int, C.c_float, C.c_int]
+        L.ref_pe_forward.argtypes = [C.POINTER(Pe), _fp, C.c_int, _fp]
+        L.ref_pe_conv.argtypes = [_fp, C.c_int, _fp, _fp, _fp]
+        L.ref_pe_causal_attention.argtypes = [_fp, _fp, _fp, _fp, C.c_int]
+
+    def gen_ranges(self):
+        """{piece: (first, last)}: where the verbatim pieces of src/e2e_pipeline_v4.cpp
+        sit in the reference file the library was built from."""
+        out = {}
+        for part in self.lib.ref_gen_ranges().decode().split(";"):
+            name, rng = part.strip().rsplit(" ", 1)
+            a, b = rng.split("-")
+            out[name] = (int(a), int(b))
+        return out
+
+    def compute_cond(self, w, t, spk=None, spk_scale=1.0):
+        """compute_cond (src/e2e_pipeline_v4.cpp:57-71) -> c [1024]."""
+        m, keep = make_dit_struct(w, 0)
+        out = np.zeros(1024, np.float32)
+        spk = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        self.lib.ref_compute_cond(C.byref(m), C.c_float(t), _ptr(spk), C.c_float(spk_scale), _ptr(out))
+        return out
+
+    def fm_mask(self, total, fm_len, patch, hidden_patch=1):
+        """build_fm_attn_mask (:120-146) as uint8 [total][total]."""
+        m = np.zeros((total, total), np.uint8)
+        self.lib.ref_fm_mask(m.ctypes.data_as(_u8p), total, fm_len, patch, hidden_patch)
+        return m
+
+    def fm_pos(self, total, fm_len, patch):
+        """build_fm_pos_ids (:149-155)."""
+        p = np.zeros(total, np.float32)
+        self.lib.ref_fm_pos(_ptr(p), total, fm_len, patch)
+        return p
+
+    def latent_proj(self, w, z):
+        """apply_latent_proj (:81-91): z [P][128] -> [P][1024]."""
+        m, keep = make_dit_struct(w, 0)
+        z = np.ascontiguousarray(z, np.float32)
+        out = np.zeros((z.shape[0], 1024), np.float32)
+        self.lib.ref_latent_proj(C.byref(m), _ptr(z), z.shape[0], _ptr(out))
+        return out
+
+    def hidden_proj(self, w, h):
+        """apply_hidden_proj (:94-102): h [1536] -> [1024]."""
+        m, keep = make_dit_struct(w, 0)
+        h = np.ascontiguousarray(h, np.float32)
+        out = np.zeros(1024, np.float32)
+        self.lib.ref_hidden_proj(C.byref(m), _ptr(h), _ptr(out))
+        return out
+
+    def coord_proj(self, w, z):
+        """apply_coord_proj (:105-113): z [128] -> [1024]."""
+        m, keep = make_dit_struct(w, 0)
+        z = np.ascontiguousarray(z, np.float32)
+        out = np.zeros(1024, np.float32)
+        self.lib.ref_coord_proj(C.byref(m), _ptr(z), _ptr(out))
+        return out
+
+    def eos_prob(self, w, h):
+        """The EOS head as written (:599-619) on each row of h [n][1536]."""
+        h = np.ascontiguousarray(h, np.float32)
+        a = [np.ascontiguousarray(w[n], np.float32) for n in
+             ("eos_proj.0.weight", "eos_proj.0.bias", "eos_proj.2.weight", "eos_proj.2.bias")]
+        return np.array([self.lib.ref_eos_prob(*[_ptr(x) for x in a], _ptr(h[i])) for i in range(h.shape[0])],
+                        np.float32)
+
+    def solve_patch(self, w, n_layers, fm_cond, fm_uncond, z0, nfe=10, cfg_scale=2.0, fast=False,
+                    ffn_mode=FFN_PER_TOKEN):
+        """One patch of the decode loop's Euler + CFG solve (:381-400, :410-533) for one
+        utterance: histories [fm_len][1024], z0 [4][128] -> z [4][128].  No speaker
+        (the pipeline passes none); ffn_mode picks the block the loop calls."""
+        m, keep = make_dit_struct(w, n_layers)
+        fc = np.ascontiguousarray(fm_cond, np.float32)
+        fu = np.ascontiguousarray(fm_uncond, np.float32)
+        z = np.array(z0, np.float32, copy=True, order="C")
+        assert z.shape == (4, 128)
+        self.lib.ref_set_solve_ffn(int(ffn_mode))
+        try:
+            self.lib.ref_solve_patch(C.byref(m), _ptr(fc), _ptr(fu), fc.shape[0], _ptr(z), int(nfe),
+                                     C.c_float(cfg_scale), int(fast))
+        finally:
+            self.lib.ref_set_solve_ffn(FFN_PER_TOKEN)
+        return z
+
+    def pe_forward(self, w, n_layers, frames):
+        """patchenc_forward (src/modules/backbone/patchenc.cpp:146-239) as written, ggml
+        operators from the eager stand-in: frames [4 n][128] -> [n][1536]."""
+        m, keep = make_pe_struct(w, n_layers)
+        frames = np.ascontiguousarray(frames, np.float32)
+        n_patches = frames.shape[0] // 4
+        out = np.zeros((n_patches, 1536), np.float32)
+        self.lib.ref_pe_forward(C.byref(m), _ptr(frames), n_patches, _ptr(out))
+        return out
+
+    def pe_conv(self, x, wc, bc=None):
+        """causal_conv1d_stride2 (patchenc.cpp:19-39): x [T][128] -> [T // 2][128]."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros((x.shape[0] // 2, 128), np.float32)
+        self.lib.ref_pe_conv(_ptr(x), x.shape[0], _ptr(np.ascontiguousarray(wc, np.float32)),
+                             _ptr(None if bc is None else np.ascontiguousarray(bc, np.float32)), _ptr(out))
+        return out
+
+    def pe_causal_attention(self, q, k, v):
+        """per_head_attention_cpu (patchenc.cpp:59-101): [T][1024] each -> [T][1024]."""
+        q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+        out = np.zeros_like(q)
+        self.lib.ref_pe_causal_attention(_ptr(out), _ptr(q), _ptr(k), _ptr(v), q.shape[0])
+        return out
 
     def voc_decode(self, w, latent):
         """The reference's own bigvgan_decode (src/modules/vocoder/bigvgan_cpp.cpp:325)."""

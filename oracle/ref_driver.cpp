@@ -11,44 +11,11 @@
 //   manual_dit_block   include/dit_manual.h:148-199 (as shipped)
 // plus a per-token-FFN block built from the same primitives, and the
 // velocity forward wired like src/e2e_pipeline_v4.cpp:441-478.
-#include "dit_manual.h"
-#include "../oracle.h"
+#include "ref_views.h"
 #include <vector>
 #include <cstdint>
 #include <cstdlib>
 #include <omp.h>
-
-namespace {
-
-struct TensorView {
-    ggml_tensor t;
-    explicit TensorView(const float *p) { t.ne[0] = t.ne[1] = t.ne[2] = t.ne[3] = 0; t.data = const_cast<float *>(p); t.view_offs = 0; }
-};
-
-struct BlockViews {
-    TensorView q, k, v, o, ob, qn, kn, w1, b1, w2, b2, aw, ab;
-    dit_block blk;
-    explicit BlockViews(const orc_dit_block *b)
-        : q(b->wq), k(b->wk), v(b->wv), o(b->wo), ob(b->bo), qn(b->qn), kn(b->kn),
-          w1(b->w1), b1(b->b1), w2(b->w2), b2(b->b2), aw(b->ada_w), ab(b->ada_b) {
-        blk.attn_q_weight = &q.t; blk.attn_k_weight = &k.t; blk.attn_v_weight = &v.t;
-        blk.attn_o_weight = &o.t; blk.attn_o_bias = b->bo ? &ob.t : nullptr;
-        blk.q_norm_w = b->qn ? &qn.t : nullptr; blk.k_norm_w = b->kn ? &kn.t : nullptr;
-        blk.ffn_w1 = &w1.t; blk.ffn_b1 = b->b1 ? &b1.t : nullptr;
-        blk.ffn_w2 = &w2.t; blk.ffn_b2 = b->b2 ? &b2.t : nullptr;
-        blk.adaln_linear_w = &aw.t; blk.adaln_linear_b = b->ada_b ? &ab.t : nullptr;
-        blk.attn_norm_w = nullptr; blk.ffn_norm_w = nullptr;
-    }
-};
-
-// The reference takes a plain bool array for the mask.
-struct BoolMask {
-    bool *p = nullptr;
-    BoolMask(const uint8_t *mask, int L) {
-        if (mask) { p = new bool[(size_t)L * L]; for (size_t i = 0; i < (size_t)L * L; i++) p[i] = mask[i] != 0; }
-    }
-    ~BoolMask() { delete[] p; }
-};
 
 // Block flow of manual_dit_block with the FFN applied to every token.  The
 // single change from include/dit_manual.h:171-197 is the per-token loop
@@ -98,8 +65,6 @@ void dit_block_per_token_ffn(const float *x_in, const float *cond, const dit_blo
         for (int i = 0; i < hidden; i++) out[(size_t)t * hidden + i] = h[(size_t)t * hidden + i] + gml[i] * fo[i];
     }
 }
-
-}  // namespace
 
 extern "C" {
 

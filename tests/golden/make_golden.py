@@ -1,7 +1,7 @@
 """Generates tests/golden/dit_ref_small.npz from the reference's own DiT math
 (include/dit_manual.h compiled in place into oracle/_ref by oracle/Makefile).
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle REF=<tree> && python tests/golden/make_golden.py
 
 Inputs are regenerated from seeds (dots.tts.cpp_b200/synth.py), so the file
 holds the seeds, shapes and the reference outputs only.  Small sizes keep the

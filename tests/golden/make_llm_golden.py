@@ -4,7 +4,7 @@ compiled in place into oracle/_ref by oracle/Makefile) on seeded random
 weights of the real shapes, 2 layers.  Two cases: a 9-token prompt with 3
 steps, and a 1-token prompt with 2 steps.
 
-    make -C oracle && python tests/golden/make_llm_golden.py
+    make -C oracle REF=<tree> && python tests/golden/make_llm_golden.py
 
 Weights and embeddings are regenerated from seeds (dots.tts.cpp_b200/synth.py),
 so the file holds the seeds, shapes and reference outputs only."""

@@ -4,7 +4,7 @@ oracle/_ref by oracle/Makefile) on seeded random weights of the real shapes,
 plus the 12 filter taps the reference hard-codes for its AMP activations
 (bigvgan_cpp.cpp:27-31), read from the source text.
 
-    make -C oracle && python tests/golden/make_voc_golden.py [REFERENCE_TREE]
+    make -C oracle REF=<tree> && python tests/golden/make_voc_golden.py <tree>
 
 Weights and latents are regenerated from seeds (dots.tts.cpp_b200/synth.py),
 so the file holds the seeds, shapes and reference outputs only."""
@@ -38,7 +38,9 @@ def reference_filter(tree):
 
 
 def main():
-    tree = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DTTS_REFERENCE", "")
+    if not tree:
+        raise SystemExit("usage: make_voc_golden.py REFERENCE_TREE (or set DTTS_REFERENCE)")
     ref = O.Reference()
     w, lat = inputs()
     audio = ref.voc_decode(w, lat)
