@@ -8,11 +8,13 @@
 // pointers the caller already owns, and keeps its intermediates (Q, K, V,
 // attention context, RoPE table) in one file-scope __device__ array compiled
 // into the library.  Limits: rows * L <= DTTS_NOALLOC_MAX_TOKENS (256) and
-// L <= 256; every GPU that loads the library holds the array (4.06 MiB) until
-// the process exits.
+// L <= 256.  The array occupies 4.06 MiB on a device from the first call
+// there (from library load when CUDA_MODULE_LOADING=EAGER) until the process
+// exits.
 #include "kernels.cuh"
 #include "runtime.h"
 
+#include <cuda.h>
 #include <mutex>
 
 using namespace dtts;
@@ -28,10 +30,29 @@ constexpr size_t kScratchFloats = 4 * kActFloats + kRopeFloats;
 // Q, K, V, context, then the RoPE table.  Shared by every call on this GPU.
 static __device__ __align__(256) float g_noalloc_scratch[kScratchFloats];
 
-// Host-side device address of g_noalloc_scratch, looked up once per device.
+// Host-side device address of g_noalloc_scratch, looked up once per device
+// and context: the context it was looked up in is kept beside it, so a device
+// reset (which destroys the primary context, its module and the kernel
+// attribute set below) leads to a fresh set-up instead of a stale address.
 constexpr int kMaxDevices = 64;
 float *g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 std::mutex g_setup_mutex;
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    return fn;
+}
 
 // RoPE (cos, sin) table of the half-split rotation: theta_d = (1e4^(-2/64))^d
 // by repeated multiplication, angle = pos[t] * theta_d (t when pos is null).
@@ -49,16 +70,25 @@ __global__ void noalloc_rope_table_kernel(const float *__restrict__ pos, int L, 
     }
 }
 
-// Once per device, with that device current: find where the array lives and
-// opt the fp32 attention kernel into its shared-memory size.
+// Once per device (and again after the device's context was replaced), with
+// that device current: find where the array lives and opt the fp32 attention
+// kernel into its shared-memory size.
 int setup_device(int dev, float **out) {
+    CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+    DTTS_CHECK(get_ctx, DTTS_ERR_CUDA, "cuCtxGetCurrent is not available from the driver");
+    // NULL when the runtime has not yet made a context current on this thread
+    CUcontext ctx = nullptr;
+    if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_scratch_addr[dev]) { *out = g_scratch_addr[dev]; return DTTS_OK; }
+    if (ctx && g_scratch_addr[dev] && g_scratch_ctx[dev] == ctx) { *out = g_scratch_addr[dev]; return DTTS_OK; }
+    // the lookup makes the device's primary context current when it is not yet
     void *p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    DTTS_CHECK(get_ctx(&ctx) == CUDA_SUCCESS && ctx, DTTS_ERR_CUDA, "no current CUDA context on device %d", dev);
     DTTS_CUDA(attention_f32_prepare());
     g_scratch_addr[dev] = static_cast<float *>(p);
+    g_scratch_ctx[dev] = ctx;
     *out = g_scratch_addr[dev];
     return DTTS_OK;
 }

@@ -706,6 +706,15 @@ class PatchEncoder:
         check(lib().dtts_pe_create(C.byref(s), dtype, device, max_batch, max_tokens, C.byref(h)))
         self.h = h
 
+    @classmethod
+    def from_safetensors(cls, path, n_layers=24, max_batch=32, max_tokens=512, dtype=DTYPE_BF16, device=0):
+        self = cls.__new__(cls)
+        h = _vp()
+        check(lib().dtts_pe_create_from_safetensors(path.encode(), n_layers, dtype, device, max_batch, max_tokens,
+                                                    C.byref(h)))
+        self.h = h
+        return self
+
     def close(self):
         if getattr(self, "h", None):
             lib().dtts_pe_destroy(self.h)

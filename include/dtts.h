@@ -281,14 +281,16 @@ int dtts_attn_profile_core(dtts_attn *a, int iters, float *us_per_launch);
  * an allocation could block -- every argument is a device pointer the caller
  * owns (x, out [rows][L][1024]; weights as in dtts_attn_weights; mask [L][L]
  * and pos [L] or NULL) and the intermediates live in one fixed array compiled
- * into the library (4.06 MiB, held by every GPU that loads it until exit).
+ * into the library: 4.06 MiB on a device from the first call there (from
+ * library load when CUDA_MODULE_LOADING=EAGER) until the process exits.
  * Limits: rows * L <= DTTS_NOALLOC_MAX_TOKENS and L <= 256; larger shapes
  * return DTTS_ERR_ARG.  Work is enqueued on `cuda_stream` (NULL: the default
  * stream) on the current device; the call returns without waiting.  The first
- * call on a device looks up the array's address and sets a kernel attribute,
- * so make that first call before any stream capture.  All calls on a device
- * share the array: calls whose work overlaps on the GPU race and must be
- * serialised by the caller.  Nothing in the array needs to start at zero. */
+ * call on a device (and the first after a device reset) looks up the array's
+ * address and sets a kernel attribute, so make that first call before any
+ * stream capture.  All calls on a device share the array: calls whose work
+ * overlaps on the GPU race and must be serialised by the caller.  Nothing in
+ * the array needs to start at zero. */
 #define DTTS_NOALLOC_MAX_TOKENS 256
 int dtts_attn_forward_f32_noalloc(const float *x, const float *wq, const float *wk, const float *wv, const float *wo,
                                   const float *bo, const float *qn, const float *kn, const uint8_t *mask,

@@ -39,6 +39,17 @@ def assert_bf16_close(got, want, what=""):
     assert r <= BF16_REL and c >= BF16_COS, f"{what}: max rel {r:.3e} (<= {BF16_REL}), cos {c:.6f} (>= {BF16_COS})"
 
 
+def f16_bits(a):
+    """IEEE half bit patterns of a (round to nearest even), as uint16."""
+    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
+
+
+def bf16_bits(a):
+    """bf16 bit patterns of a (round to nearest even), as uint16."""
+    u = np.asarray(a, np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
 def write_safetensors(path, tensors, metadata=None):
     """Minimal writer of the safetensors layout: u64 header length, JSON header,
     raw little-endian data."""

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import dtts
-from helpers import write_safetensors
+from helpers import bf16_bits, f16_bits, write_safetensors
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -68,13 +68,6 @@ def test_no_device_is_an_error_not_a_fallback(dtts_mod):
     assert e.value.status == dtts.ERR_NO_DEVICE
 
 
-def _f16(a):
-    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
-
-
-def _bf16_bits(a):
-    u = np.asarray(a, np.float32).view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
 
 
 def test_safetensors_reader_dtypes(tmp_path, dtts_mod):
@@ -83,7 +76,7 @@ def test_safetensors_reader_dtypes(tmp_path, dtts_mod):
     b = rng.standard_normal((7,), dtype=np.float32)
     c = rng.standard_normal((2, 2, 2), dtype=np.float32)
     p = str(tmp_path / "t.safetensors")
-    write_safetensors(p, {"a.weight": ("F32", a), "b": ("F16", _f16(b)), "c": ("BF16", _bf16_bits(c))},
+    write_safetensors(p, {"a.weight": ("F32", a), "b": ("F16", f16_bits(b)), "c": ("BF16", bf16_bits(c))},
                       metadata={"format": "pt"})
     st = dtts.SafeTensors(p)
     assert st.count() == 3

@@ -102,6 +102,53 @@ def test_euler_solve_18_layers(w18, eng18, orc):
     assert_bf16_close(got - z0, want - z0, "18-layer solve displacement")
 
 
+def _bench_inputs(w18, rank=0, n_utt=64, fm_len=60):
+    """The benchmark's own config-3 inputs (bench.py make_inputs: seed 1000 + rank)."""
+    seed = 1000 + rank
+    fc, fu = synth.fm_history(seed, n_utt, fm_len, w18)
+    z0 = synth.normal(seed, "z0", (n_utt, 4, 128), 1.0)
+    spk = synth.normal(seed, "spk", (n_utt, 512), 1.0 / np.sqrt(512.0))
+    return fc, fu, z0, spk
+
+
+def test_config3_as_benchmarked(w18, eng18, orc):
+    """Config 3 as the benchmark runs it: 64 utterances (128 CFG rows) in one
+    graph-captured solve, L = 64, 18 layers, NFE 10, CFG 2.0, speaker x-vectors.
+    Utterances 0 and 63 against the oracle's solve (whose Euler loop is pinned to
+    the reference's own, tests/test_oracle_ref_pieces.py), on the displacement."""
+    fc, fu, z0, spk = _bench_inputs(w18)
+    got = eng18.solve(fc, fu, z0, spk, nfe=10, cfg_scale=2.0)
+    for u in (0, 63):
+        want = orc.euler_solve(w18, 18, fc[u:u + 1], fu[u:u + 1], z0[u:u + 1], spk[u:u + 1], 1.5, nfe=10,
+                               cfg_scale=2.0)[0]
+        assert_bf16_close(got[u] - z0[u], want - z0[u], f"config 3 utterance {u} displacement")
+
+
+def test_cond_against_reference(w18, eng18, ref):
+    """dtts_dit_cond against the reference's own compute_cond (src/e2e_pipeline_v4.cpp:57-71)."""
+    spk = synth.normal(31, "cond.spk", (512,), 1.0 / np.sqrt(512.0))
+    for t in (0.0, 0.37, 0.9):
+        for s, sc in ((None, 1.5), (spk, 1.5), (spk, 1.0)):
+            got, want = eng18.cond(t, s, sc), ref.compute_cond(w18, t, s, sc)
+            assert rel(got, want) <= 1e-5, (t, s is None, sc, rel(got, want))
+
+
+@pytest.mark.parametrize("L", [16, 256])
+def test_velocity_config5_lengths(w18, eng18, orc, ref, L):
+    """Config 5's sequence lengths through the 18-layer velocity forward with the
+    v4 mask and position ids (L - 4 history rows, 4 noise rows): L = 16 against
+    the reference build itself, L = 256 against the oracle (the reference's
+    per-token GEMVs take minutes there)."""
+    rows = 4
+    x = synth.normal(40 + L, "c5.x", (rows, L, 1024), 1.0)
+    cond = synth.normal(40 + L, "c5.c", (rows, 1024), 1.0)
+    mask, pos = orc.fm_mask(L, L - 4, 4), orc.fm_pos(L, L - 4, 4)
+    got = eng18.velocity(x, cond, mask, pos, n_out=4)
+    src = ref if L <= 16 else orc
+    want = np.stack([src.dit_velocity(w18, 18, x[i], cond[i], mask, pos, n_out=4) for i in range(rows)])
+    assert_bf16_close(got, want, f"18-layer velocity L={L}")
+
+
 def test_graph_and_eager_solve_identical(eng18, w18):
     fc, fu = synth.fm_history(5, 4, 28, w18)
     z0 = synth.normal(5, "z0", (4, 4, 128), 1.0)

@@ -109,6 +109,29 @@ def test_fp8_solve_18_layers(orc, fp8_oracle):
     assert_no_worse_than_recipe(got - z0, want8 - z0, want32 - z0, "FP8 18-layer solve")
 
 
+def test_fp8_config3_as_benchmarked(orc, fp8_oracle):
+    """The FP8 twin of config 3 as benchmarked (64 utterances, NFE 10, CFG 2.0):
+    utterances 0 and 63 against the FP8 recipe oracle and against fp32."""
+    w = synth.dit_weights(1, n_layers=18)
+    seed = 1000
+    fc, fu = synth.fm_history(seed, 64, 60, w)
+    z0 = synth.normal(seed, "z0", (64, 4, 128), 1.0)
+    spk = synth.normal(seed, "spk", (64, 512), 1.0 / np.sqrt(512.0))
+    eng = dtts.DiT(w, n_layers=18, dtype=dtts.DTYPE_FP8)
+    got = eng.solve(fc, fu, z0, spk, nfe=10, cfg_scale=2.0)
+    eng.close()
+    for u in (0, 63):
+        sl = slice(u, u + 1)
+        fp8_oracle.set_dit_fp8(1)
+        want8 = fp8_oracle.euler_solve(w, 18, fc[sl], fu[sl], z0[sl], spk[sl], 1.5, nfe=10, cfg_scale=2.0)[0]
+        orc.set_dit_fp8(0)
+        want32 = orc.euler_solve(w, 18, fc[sl], fu[sl], z0[sl], spk[sl], 1.5, nfe=10, cfg_scale=2.0)[0]
+        d = got[u] - z0[u]
+        assert_fp8_solve_close(d, want8 - z0[u], f"FP8 config 3 utterance {u} vs FP8 oracle")
+        assert_fp8_solve_close(d, want32 - z0[u], f"FP8 config 3 utterance {u} vs fp32")
+        assert_no_worse_than_recipe(d, want8 - z0[u], want32 - z0[u], f"FP8 config 3 utterance {u}")
+
+
 def test_fp8_batch_independence_and_graph(orc):
     """Per-row scales keep utterances independent: one utterance solved alone is
     bit-identical to its row of a 16-utterance batch; graph == eager."""

@@ -72,6 +72,39 @@ def test_decode_batch_of_32_against_oracle(w24, pe24, orc):
         assert_bf16_close(got[i], orc.pe_forward(w24, 24, fr[i]), f"stream {i}")
 
 
+def test_prefill_against_reference_patchenc(w24, pe24, ref):
+    """The engine's prefill with the as-written pairing against the reference's own
+    patchenc_forward (src/modules/backbone/patchenc.cpp:146-239, compiled in
+    oracle/_ref over the eager ggml stand-in): 500 frames, 24 layers."""
+    fr = synth.normal(3, "pe.ref", (1, 500, 128), 1.0)
+    got = pe24.forward(fr, dtts.PAIR_AS_WRITTEN)
+    assert_bf16_close(got[0], ref.pe_forward(w24, 24, fr[0]), "PE prefill vs the reference's patchenc_forward")
+
+
+def test_decode_at_benchmark_depth(w24, pe24, orc):
+    """Config 4 as benchmarked: 32 streams, a 500-frame prefill (250 tokens), then
+    125 one-patch decode steps, filling the cache to 500 tokens.  Outputs of
+    steps 1, 60 and 125 for streams 0 and 31 against the oracle's stateless
+    forward over the whole 1000 frames (causal, so its output for patch q is
+    the output over the prefix ending there; the incremental == full pattern of
+    the reference's test/test_kv_cache_correctness.cpp)."""
+    B, pre, steps = 32, 500, 125
+    fr = synth.normal(9, "pe.deep", (B, pre + 4 * steps, 128), 1.0)
+    pe24.reset(B)
+    first = pe24.decode(fr[:, :pre])
+    got = {}
+    for s in range(1, steps + 1):
+        o = pe24.decode(fr[:, pre + 4 * (s - 1):pre + 4 * s])
+        if s in (1, 60, 125):
+            got[s] = o[:, 0]
+    assert pe24.length() == (pre + 4 * steps) // 2
+    for i in (0, 31):
+        want = orc.pe_forward(w24, 24, fr[i])
+        assert_bf16_close(first[i], want[:pre // 4], f"stream {i} prefill")
+        for s, o in got.items():
+            assert_bf16_close(o[i], want[pre // 4 + s - 1], f"stream {i} step {s}")
+
+
 def test_cache_capacity_and_batch_errors(w24):
     p = dtts.PatchEncoder(w24, n_layers=24, max_batch=2, max_tokens=8)
     p.reset(2)
