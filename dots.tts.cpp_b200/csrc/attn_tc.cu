@@ -224,6 +224,234 @@ __global__ void __launch_bounds__(kTcThreads, 4)
     }
 }
 
+// Bidirectional (optionally masked) attention for 64 < L <= 256 on tcgen05: a
+// unit is (sequence r, head h, 128-query tile qt), the whole key range in one
+// tile of NK = 128 or 256 keys.  Per unit, one CTA of 4 warps:
+//   TMA    Q (128 rows), K and V (NK rows from the sequence's first token;
+//          rows past L belong to the next sequence or are the zero fill)
+//   MMA 1  S = Q K^T into TMEM columns 0..NK-1
+//   all    thread i owns query row i: pass 1 reads S from TMEM in 32-column
+//          chunks for the row maximum, pass 2 reads it again for exp2 and the
+//          sum and writes P (bf16) K-major over the Q and K tiles (dead after
+//          MMA 1); keys past L and masked keys get P = 0, and V rows past L
+//          are zeroed
+//   MMA 2  O = P V (K = NK keys, V read MN-major as loaded) into TMEM
+//          columns 0..63 (S is dead by then)
+//   all    O / l to bf16 (or e4m3 with the sequence's bound) while the next
+//          unit's tiles load
+// No running rescale is needed: the whole row is in TMEM.  Numerics are those
+// of the L = 64 kernel (fp32 scores and softmax, P rounded to bf16).
+template <int NK>
+struct LongCfg {
+    static constexpr int kSQ = 0;
+    static constexpr int kSK = kTile;                                         // NK rows of 128 bytes
+    static constexpr int kPBytes = NK * 256;                                  // 128 rows x NK keys bf16
+    static constexpr int kSV = (kTile + NK * 128 > kPBytes) ? kTile + NK * 128 : kPBytes;
+    static constexpr int kSBar = kSV + NK * 128;
+    static constexpr int kSmem = kSBar + 64 + 1024;
+    static constexpr uint32_t kIdescS = idesc_bf16(128, NK);
+    static constexpr int kOcc = NK == 256 ? 2 : 4;                            // resident CTAs per SM
+};
+
+template <int NK>
+__global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
+    attn_tc_long_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int rows, int L,
+                        const uint32_t *__restrict__ mask_bits, float scale_log2, int *err, uint8_t *__restrict__ o8,
+                        float *__restrict__ o_scale, const float *__restrict__ unorm, float vbound) {
+    using Cfg = LongCfg<NK>;
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sQ = sm + Cfg::kSQ, *sK = sm + Cfg::kSK, *sV = sm + Cfg::kSV, *sP = sm;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + Cfg::kSBar);
+    uint64_t *mma = full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *red = reinterpret_cast<float *>(tmem_slot + 2);   // 4 per-warp maxima of the FP8 bound
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int n_qt = (L + 127) / 128, units = rows * kH * n_qt;
+    const int W = (L + 31) / 32;   // mask words per query row
+
+    if (tid == 0) {
+        mbar_init(full, 1);
+        mbar_init(mma, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tq); tma_prefetch_desc(&tk); tma_prefetch_desc(&tv);
+    }
+    if (warp == 0) { tmem_alloc(tmem_slot, NK); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+    const uint32_t trow = tbase + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's TMEM lanes
+    const int i = tid;
+
+    auto issue = [&](int v) {
+        const int qv = v % n_qt, hv = (v / n_qt) % kH, rv = v / (n_qt * kH);
+        mbar_arrive_expect_tx(full, kTile + 2 * NK * 128);
+        tma_load_2d(sQ, &tq, full, hv * kHD, rv * L + qv * 128);
+        tma_load_2d(sK, &tk, full, hv * kHD, rv * L);
+        tma_load_2d(sV, &tv, full, hv * kHD, rv * L);
+    };
+    bool pending = false;
+    if (tid == 0 && (int)blockIdx.x < units) { issue(blockIdx.x); pending = true; }
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ph ^= 1u) {
+        const int qt = u % n_qt, h = (u / n_qt) % kH, r = u / (n_qt * kH);
+        const int q = qt * 128 + i;   // this thread's query within the sequence
+        if (__syncthreads_or(!mbar_wait(full, ph, abort_flag, err, DEVERR_TIMEOUT_PRODUCER))) break;
+        pending = false;
+        // ---- MMA 1: S = Q K^T (K = 64 head dims: four 16-element steps of 32 bytes)
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK);
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                tc_mma_bf16(tbase, sdesc_k128(qa + k * 32), sdesc_k128(ka + k * 32), Cfg::kIdescS, k ? 1u : 0u);
+            tc_commit(mma);
+        }
+        // V rows past the sequence: zeroed (their P is 0, and 0 x NaN would not be)
+        for (int j = i; j < NK; j += 128)
+            if (j >= L) {
+#pragma unroll
+                for (int uu = 0; uu < 8; uu++) *reinterpret_cast<uint4 *>(sV + j * 128 + uu * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        if (o8) {
+            float m = 0.f;
+            if (i < L) m = __ldg(unorm + (long long)r * L + i);
+            if (128 + i < L) m = fmaxf(m, __ldg(unorm + (long long)r * L + 128 + i));
+            m = warp_max(m);
+            if ((tid & 31) == 0) red[warp] = m;
+        }
+        if (__syncthreads_or(!mbar_wait(mma, 0, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        // key-validity word of 32-key chunk c for this row: mask bits and keys < L
+        auto valid_word = [&](int c) -> uint32_t {
+            const int left = L - 32 * c;
+            if (left <= 0) return 0u;
+            uint32_t w = left >= 32 ? ~0u : ((1u << left) - 1u);
+            if (mask_bits && q < L) w &= __ldg(mask_bits + (long long)q * W + c);
+            return w;
+        };
+        // ---- pass 1: row maximum
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < NK / 32; c += 2) {
+            float a[32], b[32];
+            tmem_ld32x2(trow + c * 32, trow + c * 32 + 32, a, b);
+            const uint32_t wa = valid_word(c), wb = valid_word(c + 1);
+#pragma unroll
+            for (int k = 0; k < 32; k++) {
+                if ((wa >> k) & 1u) mx = fmaxf(mx, a[k]);
+                if ((wb >> k) & 1u) mx = fmaxf(mx, b[k]);
+            }
+        }
+        // scores are scaled after the maximum: max(s) * c = max(s * c) for c > 0
+        const float mu = mx == -INFINITY ? 0.f : mx * scale_log2;
+        // ---- pass 2: P = exp2(s c - max) (bf16, K-major over the dead Q | K tiles), row sum
+        float l = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < NK / 32; c += 2) {
+            float a[32], b[32];
+            tmem_ld32x2(trow + c * 32, trow + c * 32 + 32, a, b);
+            const uint32_t wa = valid_word(c), wb = valid_word(c + 1);
+#pragma unroll
+            for (int k = 0; k < 32; k++) {
+                a[k] = ((wa >> k) & 1u) ? exp2f(a[k] * scale_log2 - mu) : 0.f;
+                b[k] = ((wb >> k) & 1u) ? exp2f(b[k] * scale_log2 - mu) : 0.f;
+                l += a[k] + b[k];
+            }
+            // keys 32 c .. 32 c + 63 are 16-byte units 0..7 of row i in chunk c / 2
+            uint8_t *pc = sP + (c >> 1) * kTile;
+#pragma unroll
+            for (int uu = 0; uu < 4; uu++) {
+                *reinterpret_cast<uint4 *>(pc + sw128(i, uu)) =
+                    make_uint4(pack_bf16x2(a[8 * uu], a[8 * uu + 1]), pack_bf16x2(a[8 * uu + 2], a[8 * uu + 3]),
+                               pack_bf16x2(a[8 * uu + 4], a[8 * uu + 5]), pack_bf16x2(a[8 * uu + 6], a[8 * uu + 7]));
+                *reinterpret_cast<uint4 *>(pc + sw128(i, 4 + uu)) =
+                    make_uint4(pack_bf16x2(b[8 * uu], b[8 * uu + 1]), pack_bf16x2(b[8 * uu + 2], b[8 * uu + 3]),
+                               pack_bf16x2(b[8 * uu + 4], b[8 * uu + 5]), pack_bf16x2(b[8 * uu + 6], b[8 * uu + 7]));
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        // ---- MMA 2: O = P V over NK keys (NK / 16 steps); O into TMEM columns 0..63
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t pa = smem_u32(sP), va = smem_u32(sV);
+#pragma unroll
+            for (int k = 0; k < NK / 16; k++) {
+                const uint32_t c = k >> 2, o = (k & 3) * 32;
+                tc_mma_bf16(tbase, sdesc_k128(pa + c * kTile + o), sdesc_k128(va + k * 2048), kIdescO, k ? 1u : 0u);
+            }
+            tc_commit(mma);
+        }
+        if (__syncthreads_or(!mbar_wait(mma, 1, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        // P and the tiles are free: the next unit's tiles load during this unit's stores
+        if (tid == 0 && u + (int)gridDim.x < units) { issue(u + gridDim.x); pending = true; }
+        {
+            float a[32], b[32];
+            tmem_ld32x2(trow, trow + 32, a, b);
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            const long long row = (long long)r * L + q;
+            if (o8) {
+                // |softmax . V| <= 1.02 max_j unorm_j max_d |Wv_d| over the sequence (AttnArgs)
+                const float bnd = 1.02f * fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])) * vbound;
+                const float f = inv * (bnd > 0.f ? 448.0f / bnd : 0.f);
+                if (q < L) {
+                    uint8_t *og = o8 + row * ldo + h * kHD;
+#pragma unroll
+                    for (int uu = 0; uu < 2; uu++) {
+                        uint4 w;
+                        w.x = pack_e4m3x4(a[16 * uu + 0] * f, a[16 * uu + 1] * f, a[16 * uu + 2] * f, a[16 * uu + 3] * f);
+                        w.y = pack_e4m3x4(a[16 * uu + 4] * f, a[16 * uu + 5] * f, a[16 * uu + 6] * f, a[16 * uu + 7] * f);
+                        w.z = pack_e4m3x4(a[16 * uu + 8] * f, a[16 * uu + 9] * f, a[16 * uu + 10] * f, a[16 * uu + 11] * f);
+                        w.w = pack_e4m3x4(a[16 * uu + 12] * f, a[16 * uu + 13] * f, a[16 * uu + 14] * f, a[16 * uu + 15] * f);
+                        reinterpret_cast<uint4 *>(og)[uu] = w;
+                        w.x = pack_e4m3x4(b[16 * uu + 0] * f, b[16 * uu + 1] * f, b[16 * uu + 2] * f, b[16 * uu + 3] * f);
+                        w.y = pack_e4m3x4(b[16 * uu + 4] * f, b[16 * uu + 5] * f, b[16 * uu + 6] * f, b[16 * uu + 7] * f);
+                        w.z = pack_e4m3x4(b[16 * uu + 8] * f, b[16 * uu + 9] * f, b[16 * uu + 10] * f, b[16 * uu + 11] * f);
+                        w.w = pack_e4m3x4(b[16 * uu + 12] * f, b[16 * uu + 13] * f, b[16 * uu + 14] * f, b[16 * uu + 15] * f);
+                        reinterpret_cast<uint4 *>(og)[2 + uu] = w;
+                    }
+                    if (h == 0) o_scale[row] = bnd / 448.0f;
+                }
+            } else if (q < L) {
+                uint4 *og = reinterpret_cast<uint4 *>(out + row * ldo + h * kHD);
+#pragma unroll
+                for (int uu = 0; uu < 4; uu++) {
+                    og[uu] = make_uint4(pack_bf16x2(a[8 * uu] * inv, a[8 * uu + 1] * inv),
+                                        pack_bf16x2(a[8 * uu + 2] * inv, a[8 * uu + 3] * inv),
+                                        pack_bf16x2(a[8 * uu + 4] * inv, a[8 * uu + 5] * inv),
+                                        pack_bf16x2(a[8 * uu + 6] * inv, a[8 * uu + 7] * inv));
+                    og[4 + uu] = make_uint4(pack_bf16x2(b[8 * uu] * inv, b[8 * uu + 1] * inv),
+                                            pack_bf16x2(b[8 * uu + 2] * inv, b[8 * uu + 3] * inv),
+                                            pack_bf16x2(b[8 * uu + 4] * inv, b[8 * uu + 5] * inv),
+                                            pack_bf16x2(b[8 * uu + 6] * inv, b[8 * uu + 7] * inv));
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();   // TMEM, P, the tiles and red[] are free for the next unit
+    }
+    if (tid == 0 && pending) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(full, ph))
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tbase, NK);
+    }
+}
+
 // Causal attention over a KV cache on tcgen05 (the PatchEncoder prefill, Tq >
 // 64 tokens per sequence): a unit is (sequence r, head h, 128-query tile qt).
 // Q rows r Tq + 128 qt .. (rows past the sequence belong to the next one and
@@ -410,6 +638,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 cudaError_t attention_tc_prepare() {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_tc_long_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             LongCfg<128>::kSmem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_tc_long_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             LongCfg<256>::kSmem);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(attn_tc_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCaSmem);
 }
 
@@ -439,6 +673,41 @@ cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, boo
     return launch_k(pdl && pdl_enabled(), attn_tc_kernel, dim3(grid), dim3(kTcThreads), (size_t)kTcSmem, s, tq, tk,
                     tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err, a.o8, a.o_scale,
                     a.unorm, a.vbound);
+}
+
+bool attention_tc_long_eligible(const AttnArgs &a) {
+    static const bool on = [] {
+        const char *e = std::getenv("DTTS_ATTN_TC");
+        return !(e && e[0] == '0');
+    }();
+    return on && !a.causal && a.Tq > 64 && a.Tq <= 256 && a.kv_len == a.Tq && a.kv_cap == a.Tq && !a.kv_base_dev &&
+           (!a.mask || a.mask_bits) && (!a.o8 || (a.o_scale && a.unorm)) && a.ldq == kD && a.ldkv == kD &&
+           a.rows >= 1;
+}
+
+cudaError_t launch_attention_tc_long(const AttnArgs &a, int *err, cudaStream_t s, bool pdl) {
+    if (!attention_tc_long_eligible(a)) return cudaErrorNotSupported;
+    const int L = a.Tq, nk = L <= 128 ? 128 : 256;
+    const unsigned long long R = (unsigned long long)a.rows * L;
+    CUtensorMap tq, tk, tv;
+    if (!make_tmap_bf16(&tq, a.q, R, kD, 128) || !make_tmap_bf16(&tk, a.k, R, kD, nk) ||
+        !make_tmap_bf16(&tv, a.v, R, kD, nk))
+        return cudaErrorInvalidValue;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int units = a.rows * kH * ((L + 127) / 128);
+    const float sl = a.scale * 1.4426950408889634f;
+    if (nk == 128) {
+        const int grid = units < LongCfg<128>::kOcc * nsm ? units : LongCfg<128>::kOcc * nsm;
+        return launch_k(pdl && pdl_enabled(), attn_tc_long_kernel<128>, dim3(grid), dim3(kTcThreads),
+                        (size_t)LongCfg<128>::kSmem, s, tq, tk, tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo,
+                        a.rows, L, a.mask_bits, sl, err, a.o8, a.o_scale, a.unorm, a.vbound);
+    }
+    const int grid = units < LongCfg<256>::kOcc * nsm ? units : LongCfg<256>::kOcc * nsm;
+    return launch_k(pdl && pdl_enabled(), attn_tc_long_kernel<256>, dim3(grid), dim3(kTcThreads),
+                    (size_t)LongCfg<256>::kSmem, s, tq, tk, tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo,
+                    a.rows, L, a.mask_bits, sl, err, a.o8, a.o_scale, a.unorm, a.vbound);
 }
 
 bool attention_tc_causal_eligible(const AttnArgs &a) {

@@ -706,6 +706,10 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl) {
         launch_k(pdl, attn_short_kernel, dim3(grid), dim3(128), (size_t)kShortSmem, s, a, n_pairs, per_cta);
         return;
     }
+    if (attention_tc_long_eligible(a)) {
+        launch_attention_tc_long(a, a.err, s, pdl);
+        return;
+    }
     if (attention_tc_causal_eligible(a)) {
         launch_attention_tc_causal(a, a.err, s, pdl);
         return;

@@ -75,6 +75,12 @@ void launch_attention_bf16(const AttnArgs &a, cudaStream_t s, bool pdl = false);
 // not causal, bf16 out, dense [rows * 64][1024] q/k/v; DTTS_ATTN_TC=0 turns it off).
 bool attention_tc_eligible(const AttnArgs &a);
 cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, bool pdl);
+// Bidirectional (optionally masked) attention for 64 < L <= 256 on the tensor
+// cores (attn_tc.cu): 128-query tiles against the whole key range in TMEM; used by
+// launch_attention_bf16 when eligible (Tq = kv_len = kv_cap, not causal, dense
+// [rows * L][1024] q/k/v, bf16 or e4m3 out).
+bool attention_tc_long_eligible(const AttnArgs &a);
+cudaError_t launch_attention_tc_long(const AttnArgs &a, int *err, cudaStream_t s, bool pdl);
 // Causal attention of a prefill (Tq > 64) over the KV cache on the tensor cores:
 // 128-query tiles, 128-key blocks with an online softmax (attn_tc.cu).
 bool attention_tc_causal_eligible(const AttnArgs &a);

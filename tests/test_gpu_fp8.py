@@ -78,7 +78,7 @@ def test_fp8_velocity_two_layers(orc, fp8_oracle):
     assert_no_worse_than_recipe(got, want8, want32, "FP8 velocity")
 
 
-@pytest.mark.parametrize("L", [17, 100])
+@pytest.mark.parametrize("L", [17, 100, 256])
 def test_fp8_blocks_ragged_and_long(orc, fp8_oracle, L):
     """One block at a ragged length (partial tiles) and past the short-attention
     limit (the tiled attention kernel's e4m3 output)."""

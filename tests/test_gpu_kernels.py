@@ -54,6 +54,10 @@ def _attn_ref(q, k, v, mask=None, causal=False, q0=0):
     (2, 64, 64, False, 0, False), (2, 64, 64, False, 0, True), (3, 250, 250, True, 0, False),
     (4, 2, 130, True, 128, False), (2, 100, 100, False, 0, True), (1, 16, 16, False, 0, False),
     (2, 256, 256, False, 0, False),
+    # 64 < L <= 256 bidirectional on the tensor cores (whole key range in TMEM):
+    # 128- and 256-key tiles, a second query tile, L not a multiple of 32 or 128
+    (3, 256, 256, False, 0, True), (2, 130, 130, False, 0, True), (1, 65, 65, False, 0, False),
+    (5, 200, 200, False, 0, True), (2, 128, 128, False, 0, True), (3, 97, 97, False, 0, False),
     # L = 64 on the tensor cores, an odd number of sequences (the last pair half empty)
     (3, 64, 64, False, 0, True), (5, 64, 64, False, 0, False),
     # decode shapes (a few queries against a long cache)
