@@ -226,53 +226,64 @@ __global__ void __launch_bounds__(kTcThreads, 4)
 
 // Bidirectional (optionally masked) attention for 64 < L <= 256 on tcgen05: a
 // unit is (sequence r, head h, 128-query tile qt), the whole key range in one
-// tile of NK = 128 or 256 keys.  Per unit, one CTA of 4 warps:
+// tile of NK = 128 or 256 keys.  Per unit, one CTA of 8 warps:
 //   TMA    Q (128 rows), K and V (NK rows from the sequence's first token;
 //          rows past L belong to the next sequence or are the zero fill)
 //   MMA 1  S = Q K^T into TMEM columns 0..NK-1
-//   all    thread i owns query row i: pass 1 reads S from TMEM in 32-column
-//          chunks for the row maximum, pass 2 reads it again for exp2 and the
-//          sum and writes P (bf16) K-major over the Q and K tiles (dead after
-//          MMA 1); keys past L and masked keys get P = 0, and V rows past L
+//   all    query row i is owned by two threads, warps w and w + 4 (the TMEM
+//          lanes of a warp are fixed by w mod 4), each over half of the keys:
+//          pass 1 reads its half of S from TMEM for the row maximum, the two
+//          halves meet in shared memory, pass 2 reads S again for exp2 and
+//          the sum and writes P (bf16) K-major over the Q and K tiles (dead
+//          after MMA 1); keys past L and masked keys get P = 0, V rows past L
 //          are zeroed
 //   MMA 2  O = P V (K = NK keys, V read MN-major as loaded) into TMEM
 //          columns 0..63 (S is dead by then)
-//   all    O / l to bf16 (or e4m3 with the sequence's bound) while the next
-//          unit's tiles load
+//   all    each thread of a row stores 32 of its 64 output columns, O / l in
+//          bf16 (or e4m3 with the sequence's bound), while the next unit's
+//          tiles load
 // No running rescale is needed: the whole row is in TMEM.  Numerics are those
 // of the L = 64 kernel (fp32 scores and softmax, P rounded to bf16).
+constexpr int kLongThreads = 256;
+
 template <int NK>
 struct LongCfg {
     static constexpr int kSQ = 0;
     static constexpr int kSK = kTile;                                         // NK rows of 128 bytes
     static constexpr int kPBytes = NK * 256;                                  // 128 rows x NK keys bf16
     static constexpr int kSV = (kTile + NK * 128 > kPBytes) ? kTile + NK * 128 : kPBytes;
-    static constexpr int kSBar = kSV + NK * 128;
+    static constexpr int kSRed = kSV + NK * 128;                              // row max / sum halves, FP8 bound
+    static constexpr int kSBar = kSRed + (2 * 128 + 2 * 128 + 8) * 4;
     static constexpr int kSmem = kSBar + 64 + 1024;
     static constexpr uint32_t kIdescS = idesc_bf16(128, NK);
-    static constexpr int kOcc = NK == 256 ? 2 : 4;                            // resident CTAs per SM
+    static constexpr int kHalfChunks = NK / 64;                               // 32-key chunks per thread
 };
 
 template <int NK>
-__global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
+__global__ void __launch_bounds__(kLongThreads, 2)
     attn_tc_long_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int rows, int L,
                         const uint32_t *__restrict__ mask_bits, float scale_log2, int *err, uint8_t *__restrict__ o8,
                         float *__restrict__ o_scale, const float *__restrict__ unorm, float vbound) {
     using Cfg = LongCfg<NK>;
+    constexpr int HC = Cfg::kHalfChunks;
     pdl_wait();
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = sm + Cfg::kSQ, *sK = sm + Cfg::kSK, *sV = sm + Cfg::kSV, *sP = sm;
+    float *red_mx = reinterpret_cast<float *>(sm + Cfg::kSRed);   // [2][128] partial row maxima
+    float *red_l = red_mx + 256;                                  // [2][128] partial row sums
+    float *red_b = red_l + 256;                                   // [8] per-warp maxima of the FP8 bound
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + Cfg::kSBar);
     uint64_t *mma = full + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    float *red = reinterpret_cast<float *>(tmem_slot + 2);   // 4 per-warp maxima of the FP8 bound
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int sub = warp & 3, hf = warp >> 2;     // TMEM lane quarter, key half
+    const int i = sub * 32 + lane;                // query row within the tile
     const int n_qt = (L + 127) / 128, units = rows * kH * n_qt;
-    const int W = (L + 31) / 32;   // mask words per query row
+    const int W = (L + 31) / 32;                  // mask words per query row
 
     if (tid == 0) {
         mbar_init(full, 1);
@@ -286,8 +297,7 @@ __global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
-    const uint32_t trow = tbase + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's TMEM lanes
-    const int i = tid;
+    const uint32_t trow = tbase + (static_cast<uint32_t>(sub * 32) << 16);   // this warp's TMEM lanes
 
     auto issue = [&](int v) {
         const int qv = v % n_qt, hv = (v / n_qt) % kH, rv = v / (n_qt * kH);
@@ -302,6 +312,20 @@ __global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ph ^= 1u) {
         const int qt = u % n_qt, h = (u / n_qt) % kH, r = u / (n_qt * kH);
         const int q = qt * 128 + i;   // this thread's query within the sequence
+        // validity words of this thread's 32-key chunks: mask bits and keys < L
+        uint32_t vw[HC];
+#pragma unroll
+        for (int c = 0; c < HC; c++) {
+            const int cc = hf * HC + c, left = L - 32 * cc;
+            uint32_t w = left <= 0 ? 0u : (left >= 32 ? ~0u : ((1u << left) - 1u));
+            if (mask_bits && q < L && left > 0) w &= __ldg(mask_bits + (long long)q * W + cc);
+            vw[c] = w;
+        }
+        float bmax = 0.f;
+        if (o8) {
+            if (tid < L) bmax = __ldg(unorm + (long long)r * L + tid);
+            bmax = warp_max(bmax);
+        }
         if (__syncthreads_or(!mbar_wait(full, ph, abort_flag, err, DEVERR_TIMEOUT_PRODUCER))) break;
         pending = false;
         // ---- MMA 1: S = Q K^T (K = 64 head dims: four 16-element steps of 32 bytes)
@@ -314,58 +338,48 @@ __global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
             tc_commit(mma);
         }
         // V rows past the sequence: zeroed (their P is 0, and 0 x NaN would not be)
-        for (int j = i; j < NK; j += 128)
-            if (j >= L) {
+        if (tid >= L && tid < NK) {
 #pragma unroll
-                for (int uu = 0; uu < 8; uu++) *reinterpret_cast<uint4 *>(sV + j * 128 + uu * 16) = make_uint4(0u, 0u, 0u, 0u);
-            }
-        if (o8) {
-            float m = 0.f;
-            if (i < L) m = __ldg(unorm + (long long)r * L + i);
-            if (128 + i < L) m = fmaxf(m, __ldg(unorm + (long long)r * L + 128 + i));
-            m = warp_max(m);
-            if ((tid & 31) == 0) red[warp] = m;
+            for (int uu = 0; uu < 8; uu++) *reinterpret_cast<uint4 *>(sV + tid * 128 + uu * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
+        if (o8 && lane == 0) red_b[warp] = bmax;
         if (__syncthreads_or(!mbar_wait(mma, 0, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
         tc_fence_after();
-        // key-validity word of 32-key chunk c for this row: mask bits and keys < L
-        auto valid_word = [&](int c) -> uint32_t {
-            const int left = L - 32 * c;
-            if (left <= 0) return 0u;
-            uint32_t w = left >= 32 ? ~0u : ((1u << left) - 1u);
-            if (mask_bits && q < L) w &= __ldg(mask_bits + (long long)q * W + c);
-            return w;
-        };
-        // ---- pass 1: row maximum
-        float mx = -INFINITY;
+        // ---- pass 1: maximum of this thread's half of the row (four independent chains)
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-        for (int c = 0; c < NK / 32; c += 2) {
+        for (int c = 0; c < HC; c += 2) {
             float a[32], b[32];
-            tmem_ld32x2(trow + c * 32, trow + c * 32 + 32, a, b);
-            const uint32_t wa = valid_word(c), wb = valid_word(c + 1);
+            const uint32_t col = (uint32_t)(hf * HC + c) * 32;
+            tmem_ld32x2(trow + col, trow + col + 32, a, b);
+            const uint32_t wa = c == 0 ? vw[0] : vw[HC - 2], wb = c == 0 ? vw[1] : vw[HC - 1];
 #pragma unroll
             for (int k = 0; k < 32; k++) {
-                if ((wa >> k) & 1u) mx = fmaxf(mx, a[k]);
-                if ((wb >> k) & 1u) mx = fmaxf(mx, b[k]);
+                m4[k & 3] = fmaxf(m4[k & 3], ((wa >> k) & 1u) ? a[k] : -INFINITY);
+                m4[k & 3] = fmaxf(m4[k & 3], ((wb >> k) & 1u) ? b[k] : -INFINITY);
             }
         }
+        red_mx[hf * 128 + i] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        __syncthreads();   // both halves of every row
+        const float mx = fmaxf(red_mx[i], red_mx[128 + i]);
         // scores are scaled after the maximum: max(s) * c = max(s * c) for c > 0
         const float mu = mx == -INFINITY ? 0.f : mx * scale_log2;
         // ---- pass 2: P = exp2(s c - max) (bf16, K-major over the dead Q | K tiles), row sum
-        float l = 0.f;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-        for (int c = 0; c < NK / 32; c += 2) {
+        for (int c = 0; c < HC; c += 2) {
             float a[32], b[32];
-            tmem_ld32x2(trow + c * 32, trow + c * 32 + 32, a, b);
-            const uint32_t wa = valid_word(c), wb = valid_word(c + 1);
+            const int cc = hf * HC + c;
+            tmem_ld32x2(trow + (uint32_t)cc * 32, trow + (uint32_t)cc * 32 + 32, a, b);
+            const uint32_t wa = c == 0 ? vw[0] : vw[HC - 2], wb = c == 0 ? vw[1] : vw[HC - 1];
 #pragma unroll
             for (int k = 0; k < 32; k++) {
-                a[k] = ((wa >> k) & 1u) ? exp2f(a[k] * scale_log2 - mu) : 0.f;
-                b[k] = ((wb >> k) & 1u) ? exp2f(b[k] * scale_log2 - mu) : 0.f;
-                l += a[k] + b[k];
+                a[k] = ((wa >> k) & 1u) ? ex2_hw(fmaf(a[k], scale_log2, -mu)) : 0.f;
+                b[k] = ((wb >> k) & 1u) ? ex2_hw(fmaf(b[k], scale_log2, -mu)) : 0.f;
+                l4[k & 3] += a[k] + b[k];
             }
-            // keys 32 c .. 32 c + 63 are 16-byte units 0..7 of row i in chunk c / 2
-            uint8_t *pc = sP + (c >> 1) * kTile;
+            // keys 32 cc .. 32 cc + 63 are 16-byte units 0..7 of row i in 64-key chunk cc / 2
+            uint8_t *pc = sP + (cc >> 1) * kTile;
 #pragma unroll
             for (int uu = 0; uu < 4; uu++) {
                 *reinterpret_cast<uint4 *>(pc + sw128(i, uu)) =
@@ -376,6 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
                                pack_bf16x2(b[8 * uu + 4], b[8 * uu + 5]), pack_bf16x2(b[8 * uu + 6], b[8 * uu + 7]));
             }
         }
+        red_l[hf * 128 + i] = (l4[0] + l4[1]) + (l4[2] + l4[3]);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -395,49 +410,41 @@ __global__ void __launch_bounds__(kTcThreads, LongCfg<NK>::kOcc)
         // P and the tiles are free: the next unit's tiles load during this unit's stores
         if (tid == 0 && u + (int)gridDim.x < units) { issue(u + gridDim.x); pending = true; }
         {
-            float a[32], b[32];
-            tmem_ld32x2(trow, trow + 32, a, b);
+            float a[32];
+            tmem_ld32(trow + hf * 32, a);   // output columns 32 hf .. 32 hf + 31
+            const float l = red_l[i] + red_l[128 + i];
             const float inv = l > 0.f ? 1.0f / l : 0.f;
             const long long row = (long long)r * L + q;
             if (o8) {
                 // |softmax . V| <= 1.02 max_j unorm_j max_d |Wv_d| over the sequence (AttnArgs)
-                const float bnd = 1.02f * fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])) * vbound;
+                float bm = red_b[0];
+#pragma unroll
+                for (int w2 = 1; w2 < 8; w2++) bm = fmaxf(bm, red_b[w2]);
+                const float bnd = 1.02f * bm * vbound;
                 const float f = inv * (bnd > 0.f ? 448.0f / bnd : 0.f);
                 if (q < L) {
-                    uint8_t *og = o8 + row * ldo + h * kHD;
+                    uint4 *og = reinterpret_cast<uint4 *>(o8 + row * ldo + h * kHD + hf * 32);
 #pragma unroll
-                    for (int uu = 0; uu < 2; uu++) {
-                        uint4 w;
-                        w.x = pack_e4m3x4(a[16 * uu + 0] * f, a[16 * uu + 1] * f, a[16 * uu + 2] * f, a[16 * uu + 3] * f);
-                        w.y = pack_e4m3x4(a[16 * uu + 4] * f, a[16 * uu + 5] * f, a[16 * uu + 6] * f, a[16 * uu + 7] * f);
-                        w.z = pack_e4m3x4(a[16 * uu + 8] * f, a[16 * uu + 9] * f, a[16 * uu + 10] * f, a[16 * uu + 11] * f);
-                        w.w = pack_e4m3x4(a[16 * uu + 12] * f, a[16 * uu + 13] * f, a[16 * uu + 14] * f, a[16 * uu + 15] * f);
-                        reinterpret_cast<uint4 *>(og)[uu] = w;
-                        w.x = pack_e4m3x4(b[16 * uu + 0] * f, b[16 * uu + 1] * f, b[16 * uu + 2] * f, b[16 * uu + 3] * f);
-                        w.y = pack_e4m3x4(b[16 * uu + 4] * f, b[16 * uu + 5] * f, b[16 * uu + 6] * f, b[16 * uu + 7] * f);
-                        w.z = pack_e4m3x4(b[16 * uu + 8] * f, b[16 * uu + 9] * f, b[16 * uu + 10] * f, b[16 * uu + 11] * f);
-                        w.w = pack_e4m3x4(b[16 * uu + 12] * f, b[16 * uu + 13] * f, b[16 * uu + 14] * f, b[16 * uu + 15] * f);
-                        reinterpret_cast<uint4 *>(og)[2 + uu] = w;
-                    }
-                    if (h == 0) o_scale[row] = bnd / 448.0f;
+                    for (int uu = 0; uu < 2; uu++)
+                        og[uu] = make_uint4(
+                            pack_e4m3x4(a[16 * uu + 0] * f, a[16 * uu + 1] * f, a[16 * uu + 2] * f, a[16 * uu + 3] * f),
+                            pack_e4m3x4(a[16 * uu + 4] * f, a[16 * uu + 5] * f, a[16 * uu + 6] * f, a[16 * uu + 7] * f),
+                            pack_e4m3x4(a[16 * uu + 8] * f, a[16 * uu + 9] * f, a[16 * uu + 10] * f, a[16 * uu + 11] * f),
+                            pack_e4m3x4(a[16 * uu + 12] * f, a[16 * uu + 13] * f, a[16 * uu + 14] * f, a[16 * uu + 15] * f));
+                    if (h == 0 && hf == 0) o_scale[row] = bnd / 448.0f;
                 }
             } else if (q < L) {
-                uint4 *og = reinterpret_cast<uint4 *>(out + row * ldo + h * kHD);
+                uint4 *og = reinterpret_cast<uint4 *>(out + row * ldo + h * kHD + hf * 32);
 #pragma unroll
-                for (int uu = 0; uu < 4; uu++) {
+                for (int uu = 0; uu < 4; uu++)
                     og[uu] = make_uint4(pack_bf16x2(a[8 * uu] * inv, a[8 * uu + 1] * inv),
                                         pack_bf16x2(a[8 * uu + 2] * inv, a[8 * uu + 3] * inv),
                                         pack_bf16x2(a[8 * uu + 4] * inv, a[8 * uu + 5] * inv),
                                         pack_bf16x2(a[8 * uu + 6] * inv, a[8 * uu + 7] * inv));
-                    og[4 + uu] = make_uint4(pack_bf16x2(b[8 * uu] * inv, b[8 * uu + 1] * inv),
-                                            pack_bf16x2(b[8 * uu + 2] * inv, b[8 * uu + 3] * inv),
-                                            pack_bf16x2(b[8 * uu + 4] * inv, b[8 * uu + 5] * inv),
-                                            pack_bf16x2(b[8 * uu + 6] * inv, b[8 * uu + 7] * inv));
-                }
             }
         }
         tc_fence_before();
-        __syncthreads();   // TMEM, P, the tiles and red[] are free for the next unit
+        __syncthreads();   // TMEM, P, the tiles and the row halves are free for the next unit
     }
     if (tid == 0 && pending) {
         const unsigned long long t0 = globaltimer_ns();
@@ -699,13 +706,13 @@ cudaError_t launch_attention_tc_long(const AttnArgs &a, int *err, cudaStream_t s
     const int units = a.rows * kH * ((L + 127) / 128);
     const float sl = a.scale * 1.4426950408889634f;
     if (nk == 128) {
-        const int grid = units < LongCfg<128>::kOcc * nsm ? units : LongCfg<128>::kOcc * nsm;
-        return launch_k(pdl && pdl_enabled(), attn_tc_long_kernel<128>, dim3(grid), dim3(kTcThreads),
+        const int grid = units < 2 * nsm ? units : 2 * nsm;   // 2 resident CTAs per SM
+        return launch_k(pdl && pdl_enabled(), attn_tc_long_kernel<128>, dim3(grid), dim3(kLongThreads),
                         (size_t)LongCfg<128>::kSmem, s, tq, tk, tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo,
                         a.rows, L, a.mask_bits, sl, err, a.o8, a.o_scale, a.unorm, a.vbound);
     }
-    const int grid = units < LongCfg<256>::kOcc * nsm ? units : LongCfg<256>::kOcc * nsm;
-    return launch_k(pdl && pdl_enabled(), attn_tc_long_kernel<256>, dim3(grid), dim3(kTcThreads),
+    const int grid = units < 2 * nsm ? units : 2 * nsm;   // 2 resident CTAs per SM (97 KB, 256 TMEM columns)
+    return launch_k(pdl && pdl_enabled(), attn_tc_long_kernel<256>, dim3(grid), dim3(kLongThreads),
                     (size_t)LongCfg<256>::kSmem, s, tq, tk, tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo,
                     a.rows, L, a.mask_bits, sl, err, a.o8, a.o_scale, a.unorm, a.vbound);
 }

@@ -271,6 +271,13 @@ DTTS_DEV float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+// 2^x by the hardware approximation (MUFU ex2, subnormal results flushed to
+// zero), for softmax numerators whose argument is <= 0.
+DTTS_DEV float ex2_hw(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 // tanh by the hardware approximation (MUFU), used in the bf16 GELU epilogue.
 DTTS_DEV float tanh_hw(float x) {
     float y;
