@@ -345,18 +345,29 @@ __global__ void __launch_bounds__(kLongThreads, 2)
         if (o8 && lane == 0) red_b[warp] = bmax;
         if (__syncthreads_or(!mbar_wait(mma, 0, abort_flag, err, DEVERR_TIMEOUT_MMA))) break;
         tc_fence_after();
-        // ---- pass 1: maximum of this thread's half of the row (four independent chains)
+        // ---- pass 1: maximum of this thread's half of the row (four independent chains).
+        // A chunk pair no row of the warp may see is not read at all (the TMEM load is
+        // warp-collective); fully visible chunks skip the per-key tests.
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
         for (int c = 0; c < HC; c += 2) {
+            const uint32_t wa = c == 0 ? vw[0] : vw[HC - 2], wb = c == 0 ? vw[1] : vw[HC - 1];
+            if (!__any_sync(0xffffffffu, (wa | wb) != 0u)) continue;
             float a[32], b[32];
             const uint32_t col = (uint32_t)(hf * HC + c) * 32;
             tmem_ld32x2(trow + col, trow + col + 32, a, b);
-            const uint32_t wa = c == 0 ? vw[0] : vw[HC - 2], wb = c == 0 ? vw[1] : vw[HC - 1];
+            if ((wa & wb) == 0xffffffffu) {
 #pragma unroll
-            for (int k = 0; k < 32; k++) {
-                m4[k & 3] = fmaxf(m4[k & 3], ((wa >> k) & 1u) ? a[k] : -INFINITY);
-                m4[k & 3] = fmaxf(m4[k & 3], ((wb >> k) & 1u) ? b[k] : -INFINITY);
+                for (int k = 0; k < 32; k++) {
+                    m4[k & 3] = fmaxf(m4[k & 3], a[k]);
+                    m4[k & 3] = fmaxf(m4[k & 3], b[k]);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 32; k++) {
+                    m4[k & 3] = fmaxf(m4[k & 3], ((wa >> k) & 1u) ? a[k] : -INFINITY);
+                    m4[k & 3] = fmaxf(m4[k & 3], ((wb >> k) & 1u) ? b[k] : -INFINITY);
+                }
             }
         }
         red_mx[hf * 128 + i] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
@@ -368,15 +379,29 @@ __global__ void __launch_bounds__(kLongThreads, 2)
         float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
         for (int c = 0; c < HC; c += 2) {
-            float a[32], b[32];
             const int cc = hf * HC + c;
-            tmem_ld32x2(trow + (uint32_t)cc * 32, trow + (uint32_t)cc * 32 + 32, a, b);
             const uint32_t wa = c == 0 ? vw[0] : vw[HC - 2], wb = c == 0 ? vw[1] : vw[HC - 1];
+            float a[32], b[32];
+            if (__any_sync(0xffffffffu, (wa | wb) != 0u)) {
+                tmem_ld32x2(trow + (uint32_t)cc * 32, trow + (uint32_t)cc * 32 + 32, a, b);
+                if ((wa & wb) == 0xffffffffu) {
 #pragma unroll
-            for (int k = 0; k < 32; k++) {
-                a[k] = ((wa >> k) & 1u) ? ex2_hw(fmaf(a[k], scale_log2, -mu)) : 0.f;
-                b[k] = ((wb >> k) & 1u) ? ex2_hw(fmaf(b[k], scale_log2, -mu)) : 0.f;
-                l4[k & 3] += a[k] + b[k];
+                    for (int k = 0; k < 32; k++) {
+                        a[k] = ex2_hw(fmaf(a[k], scale_log2, -mu));
+                        b[k] = ex2_hw(fmaf(b[k], scale_log2, -mu));
+                        l4[k & 3] += a[k] + b[k];
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 32; k++) {
+                        a[k] = ((wa >> k) & 1u) ? ex2_hw(fmaf(a[k], scale_log2, -mu)) : 0.f;
+                        b[k] = ((wb >> k) & 1u) ? ex2_hw(fmaf(b[k], scale_log2, -mu)) : 0.f;
+                        l4[k & 3] += a[k] + b[k];
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 32; k++) a[k] = b[k] = 0.f;
             }
             // keys 32 cc .. 32 cc + 63 are 16-byte units 0..7 of row i in 64-key chunk cc / 2
             uint8_t *pc = sP + (cc >> 1) * kTile;
