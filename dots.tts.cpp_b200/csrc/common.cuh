@@ -39,21 +39,59 @@ DTTS_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_
 DTTS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 DTTS_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
+// L2 access-policy window that launch_k attaches to every launch made by the
+// calling thread while it is set (bytes > 0): accesses inside [base, base +
+// bytes) are marked persisting with probability hit_ratio, so a buffer that
+// every kernel of a forward reads and writes (the DiT's fp32 residual stream)
+// stays in L2 between kernels instead of being evicted by the streams of
+// weights and activations around it.  Launches captured into a CUDA graph keep
+// the window as a kernel-node attribute.
+struct L2Window {
+    void *base = nullptr;
+    size_t bytes = 0;
+    float hit_ratio = 0.f;
+};
+inline L2Window &l2_window() {
+    static thread_local L2Window w;
+    return w;
+}
+// Sets the calling thread's window for the scope and restores the previous one.
+struct L2WindowScope {
+    L2Window prev;
+    explicit L2WindowScope(const L2Window &w) : prev(l2_window()) { l2_window() = w; }
+    ~L2WindowScope() { l2_window() = prev; }
+};
+
 // k<<<grid, block, smem, s>>>(args...), with programmatic stream
 // serialization when pdl is set (the kernel must follow the pdl_wait rule)
+// and the calling thread's L2 window, if any
 template <typename... P, typename... A>
 inline cudaError_t launch_k(bool pdl, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                             A &&...args) {
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
+    const L2Window &w = l2_window();
+    if (w.bytes > 0) {
+        attr[n].id = cudaLaunchAttributeAccessPolicyWindow;
+        attr[n].val.accessPolicyWindow.base_ptr = w.base;
+        attr[n].val.accessPolicyWindow.num_bytes = w.bytes;
+        attr[n].val.accessPolicyWindow.hitRatio = w.hit_ratio;
+        attr[n].val.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+        attr[n].val.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+        n++;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, k, static_cast<A &&>(args)...);
 }
 

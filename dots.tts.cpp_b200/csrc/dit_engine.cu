@@ -12,6 +12,8 @@
 // update and the coordinate projection of z into the noise tokens, all on the
 // device, and the whole solve is captured once into a CUDA graph.
 #include "kernels.cuh"
+
+#include <cstdlib>
 #include "runtime.h"
 
 #include <algorithm>
@@ -262,8 +264,14 @@ struct dtts_dit {
         ~TlScope() { if (idx >= 0) e->tl_end(idx); }
     };
 
+    // the fp32 residual stream h is kept in L2 across the kernels of a forward
+    // (DTTS_L2_PERSIST=0 turns it off)
+    L2Window l2w;
+    bool l2_held = false;
+
     ~dtts_dit() {
         if (gexec) cudaGraphExecDestroy(gexec);
+        if (l2_held) l2_persist_release(device);
         ws.free_all();
         wts.free_all();
         if (own_stream) cudaStreamDestroy(own_stream);
@@ -272,8 +280,12 @@ struct dtts_dit {
 
     int ensure_workspace(int rows, int L, int nfe);
     int build_weight_maps();
-    int gemm(const GemmOp &op) {
+    // Every kernel of a forward is launched with programmatic stream
+    // serialization (DTTS_PDL=0 turns it off): a GEMM requests its first weight
+    // tiles and every kernel sets up while the kernel before it finishes.
+    int gemm(GemmOp op) {
         launches++;
+        op.pdl = 1;
         DTTS_CUDA(launch_gemm(op, num_sms, stream));
         return DTTS_OK;
     }
@@ -344,6 +356,30 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
              make_tmap_e4m3(&t_ffn8, ffn8, T, kF, 128);
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for an e4m3 workspace buffer");
     }
+    // L2 residency of h: a set-aside of h's size (capped by the device) and a
+    // window over h whose hit ratio is the fraction of it the set-aside holds
+    l2w = L2Window{};
+    static const bool l2_on = [] {
+        const char *e = std::getenv("DTTS_L2_PERSIST");
+        return !(e && e[0] == '0');
+    }();
+    if (l2_on) {
+        const size_t hb = T * kD * 4;
+        int max_win = 0;
+        cudaDeviceGetAttribute(&max_win, cudaDevAttrMaxAccessPolicyWindowSize, device);
+        cudaGetLastError();
+        if (max_win > 0) {
+            const size_t granted = l2_persist_acquire(device, hb);
+            if (granted > 0) {
+                if (l2_held) l2_persist_release(device);   // one reference per engine
+                l2_held = true;
+                const size_t win = std::min(hb, (size_t)max_win);
+                l2w.base = h;
+                l2w.bytes = win;
+                l2w.hit_ratio = granted >= win ? 1.0f : (float)granted / (float)win;
+            }
+        }
+    }
     return DTTS_OK;
 }
 
@@ -383,13 +419,13 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             if (fp8()) {
                 if (kind == 5)
                     launch_ln_modulate_f8(h, act8, M, ada_l + off, ada_l + off + kD, n_ada, tpr, s_act, unorm, nullptr,
-                                          nullptr, 0.f, 0.f, stream);
+                                          nullptr, 0.f, 0.f, stream, true);
                 else
                     launch_ln_modulate_f8(h, act8, M, ada_l + off, ada_l + off + kD, n_ada, tpr, s_act, nullptr, s_ffn,
-                                          inv_ffn, Ly.w1n, Ly.b1max, stream);
+                                          inv_ffn, Ly.w1n, Ly.b1max, stream, true);
                 return DTTS_OK;
             }
-            launch_ln_modulate(h, act, M, ada_l + off, ada_l + off + kD, n_ada, tpr, stream);
+            launch_ln_modulate(h, act, M, ada_l + off, ada_l + off + kD, n_ada, tpr, stream, true);
             return DTTS_OK;
         }
         case 0: {
@@ -412,7 +448,7 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             a.err = d_err;
             if (fp8()) { a.o8 = att8; a.o_scale = s_att; a.unorm = unorm; a.vbound = Ly.vbound; }
             launches++;
-            launch_attention_bf16(a, stream);
+            launch_attention_bf16(a, stream, true);
             return DTTS_OK;
         }
         case 1: {
@@ -451,6 +487,7 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
 int dtts_dit::enqueue_forward(int rows, int L, int P) {
     const int M = rows * L;
     last_rows = rows; last_L = L; last_P = P;
+    L2WindowScope l2_scope(l2w);
     {   // input layer
         TlScope tl_scope(this, TL_GEMM_INPUT);
         GemmOp op = make_op(t_x_in, t_in, M, kD, kD, EPI_F32, d_err, tu_in);

@@ -13,6 +13,8 @@ __global__ void __launch_bounds__(256, 3) ln_modulate_kernel(const float *__rest
                                                              const float *__restrict__ shift,
                                                              const float *__restrict__ scale, long long ada_ld,
                                                              int tok_per_row) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -47,8 +49,9 @@ __global__ void __launch_bounds__(256, 3) ln_modulate_kernel(const float *__rest
 }
 
 void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale, long long ada_ld,
-                        int tok_per_row, cudaStream_t s) {
-    ln_modulate_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, shift, scale, ada_ld, tok_per_row);
+                        int tok_per_row, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), ln_modulate_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, shift, scale,
+             ada_ld, tok_per_row);
 }
 
 // The same LayerNorm + modulation with an e4m3 output row: the row is scaled
@@ -62,6 +65,8 @@ __global__ void __launch_bounds__(256, 3) ln_modulate_f8_kernel(const float *__r
                                                                 int tok_per_row, float *__restrict__ row_scale,
                                                                 float *__restrict__ unorm, float *__restrict__ g_scale,
                                                                 float *__restrict__ g_inv, float w1n, float b1max) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -114,9 +119,9 @@ __global__ void __launch_bounds__(256, 3) ln_modulate_f8_kernel(const float *__r
 
 void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
-                           float *g_inv, float w1n, float b1max, cudaStream_t s) {
-    ln_modulate_f8_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, y, M, shift, scale, ada_ld, tok_per_row, row_scale, unorm,
-                                                      g_scale, g_inv, w1n, b1max);
+                           float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), ln_modulate_f8_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, shift, scale,
+             ada_ld, tok_per_row, row_scale, unorm, g_scale, g_inv, w1n, b1max);
 }
 
 // e4m3 conversion of n values (device self-test of the rounding).

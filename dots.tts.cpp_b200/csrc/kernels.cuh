@@ -37,7 +37,7 @@ cudaError_t gemm_prepare_attributes();
 // ------------------------------------------------------------ norms
 // y = bf16( LN(x) * (1 + scale[row]) + shift[row] ), LN without affine, eps 1e-5.
 void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale,
-                        long long ada_ld, int tok_per_row, cudaStream_t s);
+                        long long ada_ld, int tok_per_row, cudaStream_t s, bool pdl = false);
 // y = bf16( x / sqrt(mean(x^2) + 1e-6) * w )
 void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s, bool pdl = false);
 
@@ -128,7 +128,7 @@ void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf1
 // LayerNorm + modulation to e4m3 rows (DiT FP8 path), see kernels.cu.
 void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
-                           float *g_inv, float w1n, float b1max, cudaStream_t s);
+                           float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl = false);
 void launch_e4m3_selftest(const float *x, uint8_t *y, int n, cudaStream_t s);
 
 // ------------------------------------------------------------ FM history

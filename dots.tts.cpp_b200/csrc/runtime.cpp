@@ -7,6 +7,7 @@
 #include <chrono>
 #include <cstdarg>
 #include <cstring>
+#include <mutex>
 #include <thread>
 
 namespace dtts {
@@ -161,6 +162,59 @@ int stream_wait(cudaStream_t s, double limit_s) {
             return DTTS_ERR_TIMEOUT;
         }
         if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+namespace {
+struct L2Persist {
+    int refs = 0;
+    size_t orig = 0, cur = 0;
+};
+std::mutex g_l2_mutex;
+L2Persist g_l2[64];
+}  // namespace
+
+size_t l2_persist_acquire(int dev, size_t want) {
+    if (dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(g_l2_mutex);
+    L2Persist &p = g_l2[dev];
+    int max_persist = 0;
+    if (cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, dev) != cudaSuccess ||
+        max_persist <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (p.refs == 0) {
+        size_t orig = 0;
+        if (cudaDeviceGetLimit(&orig, cudaLimitPersistingL2CacheSize) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        p.orig = p.cur = orig;
+    }
+    const size_t target = std::min(want, (size_t)max_persist);
+    if (target > p.cur) {
+        if (cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, target) != cudaSuccess) {
+            cudaGetLastError();
+            if (p.refs == 0) return 0;
+        } else {
+            p.cur = target;
+        }
+    }
+    p.refs++;
+    return p.cur;
+}
+
+void l2_persist_release(int dev) {
+    if (dev < 0 || dev >= 64) return;
+    std::lock_guard<std::mutex> lock(g_l2_mutex);
+    L2Persist &p = g_l2[dev];
+    if (p.refs <= 0) return;
+    if (--p.refs == 0) {
+        cudaCtxResetPersistingL2Cache();
+        cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, p.orig);
+        cudaGetLastError();
+        p.cur = p.orig;
     }
 }
 

@@ -86,4 +86,14 @@ int check_device(int device, int *num_sms);
 // Bounded host wait on a stream: polls cudaStreamQuery until done or limit.
 int stream_wait(cudaStream_t s, double limit_s);
 
+// L2 set-aside for persisting accesses on the current device, shared by the
+// engines of this process: l2_persist_acquire raises the set-aside to at least
+// `want` bytes (capped by the device maximum) and takes a reference;
+// l2_persist_release drops it, and the last release flushes the persisting
+// lines and restores the limit the process had before.  Returns the bytes set
+// aside (0 where the device or the driver offers none).  The limit belongs to
+// this process's context and ends with it.
+size_t l2_persist_acquire(int dev, size_t want);
+void l2_persist_release(int dev);
+
 }  // namespace dtts
