@@ -60,6 +60,14 @@ def parse():
     ap.add_argument("--no-pe", action="store_true", help="skip the PatchEncoder stream measurement")
     ap.add_argument("--no-llm", action="store_true", help="skip the LLM decoder step measurement")
     ap.add_argument("--no-voc", action="store_true", help="skip the BigVGAN decoder measurement")
+    ap.add_argument("--global-utt", type=int, default=2048,
+                    help="strong-scaling line (key global_solve): this many utterances split evenly over the "
+                         "ranks, each rank solving its shard in batches of at most --max-batch; 0 skips it")
+    ap.add_argument("--max-batch", type=int, default=256, help="utterances per solve in the global_solve line")
+    ap.add_argument("--global-steps", type=int, default=2, help="timed passes over the global workload")
+    ap.add_argument("--sweep", action="store_true",
+                    help="per-GPU sweep instead of the benchmark line: batch 16..256 at L = 64 and L = 16/64/256 "
+                         "at batch 64, bf16 and e4m3, one JSON line per point")
     return ap.parse_args()
 
 
@@ -317,13 +325,13 @@ def measure(args, dtype, world, local_rank, dist, inputs):
             if dist:
                 dist.barrier()
             torch.cuda.synchronize()
-            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e2.record(stream)
+            # each call copies in, solves and copies out before it returns: the
+            # host clock around the loop is what the API costs a caller
+            t0 = time.perf_counter()
             for _ in range(args.steps):
                 eng.solve(hfc, hfu, hz0, hspk, z_out=hz, mem=dtts.MEM_HOST, **kw)
-            e3.record(stream)
             torch.cuda.synchronize()
-            e2e_ms = e2.elapsed_time(e3)
+            e2e_ms = (time.perf_counter() - t0) * 1000.0
             if dist:
                 dist.barrier()
 
@@ -391,6 +399,100 @@ def measure(args, dtype, world, local_rank, dist, inputs):
             "roofline": roof, "attention_us_per_layer": attn_us, "kernels_in_place": kernels,
             "timeline_solve_ms": timeline_ms, "kernels_alone_us": alone, "clocks": clocks,
             "gpu_launches": launches_per_solve * args.steps}
+
+
+def measure_global(args, world, rank, local_rank, dist):
+    """Config 5: args.global_utt utterances (one config-3 patch solve each) split
+    evenly over the ranks (shard.shard_range), every rank solving its shard in
+    batches of at most args.max_batch utterances with inputs resident on its
+    GPU; bf16 and, with --dtype both, e4m3.  Whole-job evals/s over the max of
+    the ranks' device times (strong scaling: the total work is fixed)."""
+    import torch
+    import dtts
+    import shard
+    import synth
+    dev = torch.device("cuda", local_rank)
+    lo, hi = shard.shard_range(args.global_utt, world, rank)
+    n_local = hi - lo
+    chunks = []
+    u = lo
+    while u < hi:
+        chunks.append(min(args.max_batch, hi - u))
+        u += chunks[-1]
+    # one seeded batch of inputs, reused by every chunk of the same size: the
+    # work of a solve does not depend on the values
+    w = synth.dit_weights(1, n_layers=args.layers)
+    nb = max(chunks) if chunks else 0
+    res = {}
+    for dtype in (("bf16", "fp8") if args.dtype == "both" else (args.dtype,)):
+        eng = dtts.DiT(w, n_layers=args.layers, device=local_rank,
+                       dtype=dtts.DTYPE_FP8 if dtype == "fp8" else dtts.DTYPE_BF16)
+        stream = torch.cuda.Stream(device=dev)
+        eng.set_stream(stream.cuda_stream)
+        kw = dict(spk_scale=1.5, nfe=args.nfe, cfg_scale=args.cfg_scale, cfg_form=dtts.CFG_V4,
+                  layout=dtts.LAYOUT_FM_MASK, use_graph=True)
+        d = {}
+        if nb:
+            fc, fu = synth.fm_history(5000, nb, args.fm_len, w)
+            z0 = synth.normal(5000, "z0", (nb, args.patch, 128), 1.0)
+            spk = synth.normal(5000, "spk", (nb, 512), 1.0 / np.sqrt(512.0))
+            d = {k: torch.from_numpy(v).to(dev) for k, v in (("fc", fc), ("fu", fu), ("z0", z0), ("spk", spk))}
+            d["z"] = torch.empty_like(d["z0"])
+
+        def one_pass():
+            for c in chunks:
+                eng.solve(d["fc"][:c], d["fu"][:c], d["z0"][:c], d["spk"][:c], z_out=d["z"][:c], mem=dtts.MEM_DEVICE,
+                          **kw)
+
+        with torch.cuda.stream(stream):
+            one_pass()
+            eng.sync()
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.global_steps):
+                one_pass()
+            e1.record(stream)
+            eng.sync()
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        evals = args.global_utt * args.nfe * args.global_steps
+        res[dtype] = {"value": evals / (ms / 1000.0), "unit": UNIT, "ms_per_pass": ms / args.global_steps,
+                      "gpu_launches": eng.last_launch_count() * len(chunks) * args.global_steps}
+        eng.close()
+        if dist:
+            dist.barrier()
+    return {"global_utterances": args.global_utt, "utterances_per_rank": n_local, "batches_per_rank": chunks,
+            "scaling": "strong", "passes": args.global_steps,
+            "inputs": "one seeded batch of the largest solve size, reused by every batch of the shard",
+            **res}
+
+
+def run_sweep(args, local_rank):
+    """Per-GPU sweep of config 5: batch (utterances per solve) 16..256 at L = 64
+    and sequence length L = 16 / 64 / 256 at 64 utterances, bf16 and e4m3; one
+    JSON line per point with the solve's evals/s and the in-place kernel times."""
+    import torch
+    torch.cuda.set_device(local_rank)
+    points = [(b, 60) for b in (16, 32, 64, 128, 256)] + [(64, 12), (64, 252)]
+    for n_utt, fm_len in points:
+        a = argparse.Namespace(**vars(args))
+        a.n_utt, a.fm_len, a.no_e2e = n_utt, fm_len, True
+        inputs = make_inputs(a, 0)
+        for dtype in (("bf16", "fp8") if args.dtype == "both" else (args.dtype,)):
+            r = measure(a, dtype, 1, local_rank, None, inputs)
+            k = r["kernels_in_place"]
+            print(json.dumps({"sweep": "config5", "dtype": dtype, "n_utt": n_utt, "seq_len": fm_len + args.patch,
+                              "value": r["value"], "unit": UNIT, "ms_per_step": r["ms_per_step"],
+                              "roofline_frac": r["roofline"]["frac"] if r["roofline"] else None,
+                              "us_per_launch": {n: v["us_per_launch"] for n, v in k.items()},
+                              "clocks": r["clocks"]}), flush=True)
 
 
 def cpu_pe_port(w, layers, frames):
@@ -657,6 +759,7 @@ def run_ours(args, rank, world, local_rank):
     head_dtype = "fp8" if args.dtype == "fp8" else "bf16"
     head = measure(args, head_dtype, world, local_rank, dist, inputs)
     extra = measure(args, "fp8", world, local_rank, dist, inputs) if args.dtype == "both" else None
+    glob = measure_global(args, world, rank, local_rank, dist) if args.global_utt > 0 else None
     pe = measure_pe(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
         if (world == 1 and not args.no_pe) else None
     llm = measure_llm(args, local_rank, rank == 0 and not args.no_cpu_baseline) \
@@ -708,6 +811,8 @@ def run_ours(args, rank, world, local_rank):
             line["vocoder"] = voc
         if attn1:
             line["attention_sublayer"] = attn1
+        if glob:
+            line["global_solve"] = glob
         if extra:
             line["fp8"] = {"dtype": "e4m3", "weights": workload_config(args, world, "fp8")["weights"],
                            **{k: extra[k] for k in ("value", "ms_per_step", "e2e", "roofline", "attention_us_per_layer",
@@ -725,6 +830,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.sweep:
+        run_sweep(args, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 
