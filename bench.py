@@ -63,7 +63,8 @@ def parse():
     ap.add_argument("--global-utt", type=int, default=2048,
                     help="strong-scaling line (key global_solve): this many utterances split evenly over the "
                          "ranks, each rank solving its shard in batches of at most --max-batch; 0 skips it")
-    ap.add_argument("--max-batch", type=int, default=256, help="utterances per solve in the global_solve line")
+    ap.add_argument("--max-batch", type=int, default=128,
+                    help="utterances per solve in the global_solve line (throughput peaks at 64-128)")
     ap.add_argument("--global-steps", type=int, default=2, help="timed passes over the global workload")
     ap.add_argument("--sweep", action="store_true",
                     help="per-GPU sweep instead of the benchmark line: batch 16..256 at L = 64 and L = 16/64/256 "

@@ -357,13 +357,21 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
         DTTS_CHECK(ok, DTTS_ERR_CUDA, "cuTensorMapEncodeTiled failed for an e4m3 workspace buffer");
     }
     // L2 residency of h: a set-aside of h's size (capped by the device) and a
-    // window over h whose hit ratio is the fraction of it the set-aside holds
+    // window over h whose hit ratio is the fraction of it the set-aside holds.
+    // Only while h takes at most 40% of L2: a larger set-aside starves the
+    // q/k/v and FFN activations that each kernel hands to the next (at 128 MB
+    // of h, 256 utterances x 64 tokens, every block kernel ran 1.3-3x slower).
     l2w = L2Window{};
     static const bool l2_on = [] {
         const char *e = std::getenv("DTTS_L2_PERSIST");
         return !(e && e[0] == '0');
     }();
-    if (l2_on) {
+    int l2_size = 0;
+    cudaDeviceGetAttribute(&l2_size, cudaDevAttrL2CacheSize, device);
+    cudaGetLastError();
+    const bool l2_fits = (double)T * kD * 4 <= 0.4 * (double)l2_size;
+    if (l2_held && !l2_fits) { l2_persist_release(device); l2_held = false; }
+    if (l2_on && l2_fits) {
         const size_t hb = T * kD * 4;
         int max_win = 0;
         cudaDeviceGetAttribute(&max_win, cudaDevAttrMaxAccessPolicyWindowSize, device);
