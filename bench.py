@@ -66,6 +66,11 @@ def parse():
     ap.add_argument("--max-batch", type=int, default=128,
                     help="utterances per solve in the global_solve line (throughput peaks at 64-128)")
     ap.add_argument("--global-steps", type=int, default=2, help="timed passes over the global workload")
+    ap.add_argument("--part", choices=["all", "dit", "pe", "llm", "voc", "attn"], default="all",
+                    help="run one part alone and print its JSON object (profiling drivers): dit = the DiT solve "
+                         "(bf16 unless --dtype fp8), pe = PatchEncoder prefill + decode, llm = LLM steps, "
+                         "voc = BigVGAN decode, attn = the attention sublayer")
+    ap.add_argument("--pe-steps", type=int, default=125, help="PatchEncoder decode steps per pass")
     ap.add_argument("--sweep", action="store_true",
                     help="per-GPU sweep instead of the benchmark line: batch 16..256 at L = 64 and L = 16/64/256 "
                          "at batch 64, bf16 and e4m3, one JSON line per point")
@@ -529,7 +534,7 @@ def measure_pe(args, local_rank, cpu_sample=False):
     import dtts
     import synth
     dev = torch.device("cuda", local_rank)
-    B, prefill, steps = 32, 500, 125
+    B, prefill, steps = 32, 500, args.pe_steps
     w = synth.pe_weights(2, n_layers=24)
     pe = dtts.PatchEncoder(w, n_layers=24, max_batch=B, max_tokens=512, device=local_rank)
     stream = torch.cuda.Stream(device=dev)
@@ -554,7 +559,7 @@ def measure_pe(args, local_rank, cpu_sample=False):
     pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
     pe.close()
     flop_pre = B * 24 * (prefill // 2) * 2 * (4 * 1024 * 1024 + 2 * 1024 * 4096)
-    res = {"workload": "PatchEncoder, 24 layers, 32 streams: 500-frame prefill, then 125 decode steps",
+    res = {"workload": f"PatchEncoder, 24 layers, 32 streams: 500-frame prefill, then {steps} decode steps",
            "prefill_ms": pre_ms, "prefill_frames_per_s": B * prefill / (pre_ms / 1000.0),
            "prefill_gemm_tflops": flop_pre / (pre_ms / 1000.0) / 1e12,
            "decode_ms_per_step": dec_ms / steps, "decode_patches_per_s": B * steps / (dec_ms / 1000.0),
@@ -747,6 +752,25 @@ def measure_attn_sublayer(args, local_rank, cpu_sample):
     return res
 
 
+def run_part(args, local_rank):
+    """One part of the benchmark alone (a profiling driver): its JSON object on one line."""
+    import torch
+    torch.cuda.set_device(local_rank)
+    cpu = not args.no_cpu_baseline
+    if args.part == "dit":
+        dtype = "fp8" if args.dtype == "fp8" else "bf16"
+        r = measure(args, dtype, 1, local_rank, None, make_inputs(args, 0))
+    elif args.part == "pe":
+        r = measure_pe(args, local_rank, cpu)
+    elif args.part == "llm":
+        r = measure_llm(args, local_rank, cpu)
+    elif args.part == "voc":
+        r = measure_voc(args, local_rank, cpu)
+    else:
+        r = measure_attn_sublayer(args, local_rank, cpu)
+    print(json.dumps({"part": args.part, **r}))
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     dist = None
@@ -833,6 +857,8 @@ def main():
         run_reference(args, rank, world)
     elif args.sweep:
         run_sweep(args, local_rank)
+    elif args.part != "all":
+        run_part(args, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 
