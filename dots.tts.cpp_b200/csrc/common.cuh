@@ -152,14 +152,6 @@ DTTS_DEV void tma_load_2d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, 
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
-// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
-// aligned) from global memory into shared memory, completing on `bar`.
-DTTS_DEV void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(smem_dst)),
-                 "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
 DTTS_DEV void tma_prefetch_desc(const CUtensorMap *tm) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }

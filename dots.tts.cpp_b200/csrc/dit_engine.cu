@@ -427,13 +427,13 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             if (fp8()) {
                 if (kind == 5)
                     launch_ln_modulate_f8(h, act8, M, ada_l + off, ada_l + off + kD, n_ada, tpr, s_act, unorm, nullptr,
-                                          nullptr, 0.f, 0.f, stream, true, d_err);
+                                          nullptr, 0.f, 0.f, stream, true);
                 else
                     launch_ln_modulate_f8(h, act8, M, ada_l + off, ada_l + off + kD, n_ada, tpr, s_act, nullptr, s_ffn,
-                                          inv_ffn, Ly.w1n, Ly.b1max, stream, true, d_err);
+                                          inv_ffn, Ly.w1n, Ly.b1max, stream, true);
                 return DTTS_OK;
             }
-            launch_ln_modulate(h, act, M, ada_l + off, ada_l + off + kD, n_ada, tpr, stream, true, d_err);
+            launch_ln_modulate(h, act, M, ada_l + off, ada_l + off + kD, n_ada, tpr, stream, true);
             return DTTS_OK;
         }
         case 0: {
@@ -665,7 +665,6 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     e->stream = e->own_stream;
     DTTS_CUDA(gemm_prepare_attributes());
     DTTS_CUDA(attention_short_prepare());
-    DTTS_CUDA(ln_prepare());
     cudaStream_t s = e->stream;
     e->d_err = (int *)e->wts.alloc(sizeof(int));
     DTTS_CHECK(e->d_err, DTTS_ERR_OOM, "cudaMalloc failed");

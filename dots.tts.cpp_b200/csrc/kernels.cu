@@ -7,188 +7,121 @@
 namespace dtts {
 
 // =========================================================================
-// LayerNorm + modulation: one warp per token row of 1024 fp32 values.
-// Rows reach shared memory by bulk copies: one persistent CTA per SM walks
-// chunks of 8 consecutive rows (32 KB), a producer warp keeps kLnStages chunks
-// in flight (128 KB per SM), and each of the 8 consumer warps normalises one
-// row of a chunk from shared memory (8 x float4 per lane) and writes it out.
-// With 1024 chunks at 8192 tokens, every SM takes 6 or 7.
+// norms: one warp per token row of 1024 fp32 values (8 x float4 per lane)
 // =========================================================================
-constexpr int kLnStages = 4;
-constexpr int kLnChunk = 8 * kD * 4;                       // bytes of 8 rows
-constexpr int kLnSmem = kLnStages * kLnChunk + 2 * kLnStages * 8 + 16;
-constexpr int kLnThreads = 9 * 32;                         // 8 consumer warps + the producer
-
-// LayerNorm statistics of one row held as 8 float4 per lane (no affine, eps
-// 1e-5): the mean, then the mean of the squared deviations.
-DTTS_DEV void ln_stats(const float4 (&v)[8], float &mean, float &inv) {
+__global__ void __launch_bounds__(256, 3) ln_modulate_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
+                                                             const float *__restrict__ shift,
+                                                             const float *__restrict__ scale, long long ada_ld,
+                                                             int tok_per_row) {
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const long long r = row / tok_per_row;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
+    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
+    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    mean = warp_sum(s) * (1.0f / kD);
+    const float mean = warp_sum(s) * (1.0f / kD);
     float q = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
         q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
     }
-    inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
+    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
+    uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
+        const float o0 = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
+        const float o1 = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
+        const float o2 = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
+        const float o3 = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
+        yr[lane + 32 * j] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+    }
 }
 
-// y = bf16(LN(x) (1 + scale) + shift) of one row
-struct LnRowBf16 {
-    bf16 *y;
-    DTTS_DEV void operator()(float4 (&v)[8], int row, int lane, const float4 *sh, const float4 *sc) const {
-        float mean, inv;
-        ln_stats(v, mean, inv);
-        uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
-            const float o0 = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
-            const float o1 = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
-            const float o2 = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
-            const float o3 = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
-            yr[lane + 32 * j] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
-        }
-    }
-};
+void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale, long long ada_ld,
+                        int tok_per_row, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), ln_modulate_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, shift, scale,
+             ada_ld, tok_per_row);
+}
 
 // The same LayerNorm + modulation with an e4m3 output row: the row is scaled
 // by 448 / absmax before the conversion and row_scale = absmax / 448 is
 // written beside it.  unorm (if given) receives 1.08 |u| and, when g_scale is
 // given, the row's bound on |gelu(W1 u + b1)|, B = 1.02 max(1.08 |u| w1n +
 // b1max, 0.17), is stored as g_scale = B / 448 and g_inv = 448 / B.
-struct LnRowE4m3 {
-    uint8_t *y;
-    float *row_scale, *unorm, *g_scale, *g_inv;
-    float w1n, b1max;
-    DTTS_DEV void operator()(float4 (&v)[8], int row, int lane, const float4 *sh, const float4 *sc) const {
-        float mean, inv;
-        ln_stats(v, mean, inv);
-        float amax = 0.f, ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
-            v[j].x = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
-            v[j].y = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
-            v[j].z = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
-            v[j].w = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
-            ss += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
-        }
-        amax = warp_max(amax);
-        const float qinv = amax > 0.f ? 448.0f / amax : 0.f;
-        uint32_t *yr = reinterpret_cast<uint32_t *>(y + (long long)row * kD);
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-            yr[lane + 32 * j] = pack_e4m3x4(v[j].x * qinv, v[j].y * qinv, v[j].z * qinv, v[j].w * qinv);
-        const float nrm = sqrtf(warp_sum(ss));
-        if (lane == 0) {
-            row_scale[row] = amax / 448.0f;
-            if (unorm) unorm[row] = 1.08f * nrm;
-            if (g_scale) {
-                const float bnd = 1.02f * fmaxf(1.08f * nrm * w1n + b1max, 0.17f);
-                g_scale[row] = bnd / 448.0f;
-                g_inv[row] = 448.0f / bnd;
-            }
-        }
-    }
-};
-
-template <typename RowOp>
-__global__ void __launch_bounds__(kLnThreads, 1)
-    ln_modulate_kernel(const float *__restrict__ x, int M, const float *__restrict__ shift,
-                       const float *__restrict__ scale, long long ada_ld, int tok_per_row, RowOp op, int *err) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + kLnStages * kLnChunk);
-    uint64_t *empty = full + kLnStages;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kLnStages);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_chunks = (M + 7) / 8;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kLnStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 8); }
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
+__global__ void __launch_bounds__(256, 3) ln_modulate_f8_kernel(const float *__restrict__ x, uint8_t *__restrict__ y,
+                                                                int M, const float *__restrict__ shift,
+                                                                const float *__restrict__ scale, long long ada_ld,
+                                                                int tok_per_row, float *__restrict__ row_scale,
+                                                                float *__restrict__ unorm, float *__restrict__ g_scale,
+                                                                float *__restrict__ g_inv, float w1n, float b1max) {
     pdl_wait();
     pdl_trigger();
-    if (warp == 8) {
-        // ---- producer: chunk k of this CTA (global chunk blockIdx.x + k gridDim.x) into stage k mod kLnStages
-        if (lane == 0) {
-            int k = 0;
-            for (int c = blockIdx.x; c < n_chunks; c += gridDim.x, k++) {
-                const int s = k % kLnStages;
-                if (k >= kLnStages && !mbar_wait(&empty[s], ((k / kLnStages) - 1) & 1, abort_flag, err,
-                                                 DEVERR_TIMEOUT_PRODUCER))
-                    break;
-                const int rows = min(8, M - 8 * c);
-                const uint32_t bytes = (uint32_t)rows * kD * 4;
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_load(sm + s * kLnChunk, x + (long long)8 * c * kD, bytes, &full[s]);
-            }
-            // drain (bounded): no bulk copy may land after the CTA has exited
-            const int issued = k;
-            for (int j = issued - kLnStages < 0 ? 0 : issued - kLnStages; j < issued; j++) {
-                const int s = j % kLnStages;
-                const unsigned long long t0 = globaltimer_ns();
-                while (!mbar_try_wait(&full[s], (j / kLnStages) & 1))
-                    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-            }
-        }
-        return;
-    }
-    // ---- consumers: warp w takes row w of every chunk
-    int k = 0;
-    for (int c = blockIdx.x; c < n_chunks; c += gridDim.x, k++) {
-        const int s = k % kLnStages;
-        if (!mbar_wait(&full[s], (k / kLnStages) & 1, abort_flag, err, DEVERR_TIMEOUT_EPILOGUE)) break;
-        const int row = 8 * c + warp;
-        if (row < M) {
-            const float4 *xr = reinterpret_cast<const float4 *>(sm + s * kLnChunk + warp * kD * 4);
-            float4 v[8];
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const long long r = row / tok_per_row;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
+    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
+    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
+    float4 v[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
-            const long long r = row / tok_per_row;
-            op(v, row, lane, reinterpret_cast<const float4 *>(shift + r * ada_ld),
-               reinterpret_cast<const float4 *>(scale + r * ada_ld));
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+    for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    const float mean = warp_sum(s) * (1.0f / kD);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
+        q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
     }
-}
-
-cudaError_t ln_prepare() {
-    cudaError_t e = cudaFuncSetAttribute(ln_modulate_kernel<LnRowBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kLnSmem + 128);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(ln_modulate_kernel<LnRowE4m3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kLnSmem + 128);
-}
-
-static int ln_grid(int M) {
-    int dev = 0, nsm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const int chunks = (M + 7) / 8;
-    return chunks < nsm ? chunks : nsm;
-}
-
-void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale, long long ada_ld,
-                        int tok_per_row, cudaStream_t s, bool pdl, int *err) {
-    LnRowBf16 op{y};
-    launch_k(pdl && pdl_enabled(), ln_modulate_kernel<LnRowBf16>, dim3(ln_grid(M)), dim3(kLnThreads),
-             (size_t)kLnSmem + 128, s, x, M, shift, scale, ada_ld, tok_per_row, op, err);
+    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
+    float amax = 0.f, ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
+        v[j].x = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
+        v[j].y = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
+        v[j].z = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
+        v[j].w = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+        ss += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
+    }
+    amax = warp_max(amax);
+    const float qinv = amax > 0.f ? 448.0f / amax : 0.f;
+    uint32_t *yr = reinterpret_cast<uint32_t *>(y + (long long)row * kD);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        yr[lane + 32 * j] = pack_e4m3x4(v[j].x * qinv, v[j].y * qinv, v[j].z * qinv, v[j].w * qinv);
+    const float nrm = sqrtf(warp_sum(ss));
+    if (lane == 0) {
+        row_scale[row] = amax / 448.0f;
+        if (unorm) unorm[row] = 1.08f * nrm;
+        if (g_scale) {
+            const float bnd = 1.02f * fmaxf(1.08f * nrm * w1n + b1max, 0.17f);
+            g_scale[row] = bnd / 448.0f;
+            g_inv[row] = 448.0f / bnd;
+        }
+    }
 }
 
 void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
-                           float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl, int *err) {
-    LnRowE4m3 op{y, row_scale, unorm, g_scale, g_inv, w1n, b1max};
-    launch_k(pdl && pdl_enabled(), ln_modulate_kernel<LnRowE4m3>, dim3(ln_grid(M)), dim3(kLnThreads),
-             (size_t)kLnSmem + 128, s, x, M, shift, scale, ada_ld, tok_per_row, op, err);
+                           float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl) {
+    launch_k(pdl && pdl_enabled(), ln_modulate_f8_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, shift, scale,
+             ada_ld, tok_per_row, row_scale, unorm, g_scale, g_inv, w1n, b1max);
 }
 
 // e4m3 conversion of n values (device self-test of the rounding).

@@ -36,11 +36,8 @@ cudaError_t gemm_prepare_attributes();
 
 // ------------------------------------------------------------ norms
 // y = bf16( LN(x) * (1 + scale[row]) + shift[row] ), LN without affine, eps 1e-5.
-// Rows are staged through shared memory by bulk copies (call ln_prepare() once
-// per device first); err receives a code if a bounded wait expires.
 void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale,
-                        long long ada_ld, int tok_per_row, cudaStream_t s, bool pdl = false, int *err = nullptr);
-cudaError_t ln_prepare();
+                        long long ada_ld, int tok_per_row, cudaStream_t s, bool pdl = false);
 // y = bf16( x / sqrt(mean(x^2) + 1e-6) * w )
 void launch_rms_norm(const float *x, bf16 *y, int M, const float *w, cudaStream_t s, bool pdl = false);
 
@@ -131,8 +128,7 @@ void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf1
 // LayerNorm + modulation to e4m3 rows (DiT FP8 path), see kernels.cu.
 void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
-                           float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl = false,
-                           int *err = nullptr);
+                           float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl = false);
 void launch_e4m3_selftest(const float *x, uint8_t *y, int n, cudaStream_t s);
 
 // ------------------------------------------------------------ FM history
