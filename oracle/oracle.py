@@ -461,6 +461,7 @@ class Reference:
         L.ref_gen_ranges.restype = C.c_char_p
         L.ref_set_solve_ffn.argtypes = [C.c_int]
         L.ref_compute_cond.argtypes = [C.POINTER(Dit), C.c_float, _fp, C.c_float, _fp]
+        L.ref_compute_cond_raw.argtypes = [C.POINTER(Dit), C.c_float, _fp, _fp]
         L.ref_fm_mask.argtypes = [_u8p, C.c_int, C.c_int, C.c_int, C.c_int]
         L.ref_fm_pos.argtypes = [_fp, C.c_int, C.c_int, C.c_int]
         L.ref_latent_proj.argtypes = [C.POINTER(Dit), _fp, C.c_int, _fp]
@@ -489,6 +490,14 @@ class Reference:
         out = np.zeros(1024, np.float32)
         spk = None if spk is None else np.ascontiguousarray(spk, np.float32)
         self.lib.ref_compute_cond(C.byref(m), C.c_float(t), _ptr(spk), C.c_float(spk_scale), _ptr(out))
+        return out
+
+    def compute_cond_raw(self, w, t, spk=None):
+        """compute_cond of the ggml DiT path (src/modules/backbone/dit_forward.cpp:22-36)."""
+        m, keep = make_dit_struct(w, 0)
+        out = np.zeros(1024, np.float32)
+        spk = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        self.lib.ref_compute_cond_raw(C.byref(m), C.c_float(t), _ptr(spk), _ptr(out))
         return out
 
     def fm_mask(self, total, fm_len, patch, hidden_patch=1):

@@ -131,6 +131,9 @@ def test_cond_against_reference(w18, eng18, ref):
         for s, sc in ((None, 1.5), (spk, 1.5), (spk, 1.0)):
             got, want = eng18.cond(t, s, sc), ref.compute_cond(w18, t, s, sc)
             assert rel(got, want) <= 1e-5, (t, s is None, sc, rel(got, want))
+        # the conditioning of the ggml DiT path behind dit_forward_raw
+        # (src/modules/backbone/dit_forward.cpp:22-36): speaker term unscaled
+        assert rel(eng18.cond(t, spk, 1.0), ref.compute_cond_raw(w18, t, spk)) <= 1e-5
 
 
 @pytest.mark.parametrize("L", [16, 256])

@@ -52,7 +52,8 @@ def test_pieces_come_from_the_cited_lines(ref):
         "HIDDEN_PATCH_SIZE": (39, 39), "LATENT_PATCH_SIZE": (40, 40), "compute_cond": (57, 71),
         "apply_latent_proj": (81, 91), "apply_hidden_proj": (94, 102), "apply_coord_proj": (105, 113),
         "build_fm_attn_mask": (120, 146), "build_fm_pos_ids": (149, 155), "solver_locals": (246, 249),
-        "fm_input": (381, 400), "euler_loop": (410, 533), "eos_head": (599, 619)}
+        "fm_input": (381, 400), "euler_loop": (410, 533), "eos_head": (599, 619),
+        "raw_compute_cond": (22, 36)}
 
 
 def test_fm_mask_and_pos_golden(orc, gold, dtts_mod):
@@ -89,6 +90,15 @@ def test_compute_cond_live(orc, ref, dit_in):
     for t in (0.05, 0.5, 0.99):
         for s, sc in ((None, 1.0), (spk, 1.0), (spk, 1.5), (spk * 3.0, 0.25)):
             assert rel(orc.compute_cond(w, t, s, sc), ref.compute_cond(w, t, s, sc)) <= F32
+
+
+def test_compute_cond_of_the_ggml_path_live(orc, ref, dit_in):
+    """dit_forward_raw's own compute_cond (src/modules/backbone/dit_forward.cpp:22-36) is the
+    pipeline's with the speaker term unscaled."""
+    w, spk = dit_in[0], dit_in[1]
+    for t in (0.0, 0.4):
+        for s in (None, spk):
+            assert rel(orc.compute_cond(w, t, s, 1.0), ref.compute_cond_raw(w, t, s)) <= F32
 
 
 def test_projections_and_eos_golden(orc, gold, dit_in):
