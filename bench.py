@@ -501,16 +501,28 @@ def run_sweep(args, local_rank):
                               "clocks": r["clocks"]}), flush=True)
 
 
-def cpu_pe_port(w, layers, frames):
-    """One stream's prefill through the oracle's fp32 restatement of
-    patchenc_forward (oracle/oracle.c, OpenMP over the host threads): the CPU
-    line for the PatchEncoder, whose reference path (ggml) is not vendored."""
+def cpu_pe_baseline(w, layers, frames):
+    """One stream's prefill on the host cores: the reference's own patchenc_forward
+    (src/modules/backbone/patchenc.cpp, built in oracle/_ref over the eager ggml
+    stand-in, OpenMP matrix products) where that build exists, else the oracle's
+    fp32 restatement (oracle/oracle.c)."""
     sys.path.insert(0, os.path.join(HERE, "oracle"))
     import oracle as O
     import synth
     try:
-        orc = O.Oracle()
         fr = synth.normal(2, "pe.cpu", (frames, 128), 1.0)
+        if O.Reference.available():
+            ref = O.Reference()
+            ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+            ref.set_threads(ncpu)
+            t0 = time.perf_counter()
+            ref.pe_forward(w, layers, fr)
+            secs = time.perf_counter() - t0
+            return {"prefill_frames_per_s": frames / secs, "cores": ref.num_threads(), "kind": "reference",
+                    "sample": "one stream's %d-frame prefill, %d layers, through the reference's patchenc_forward "
+                              "(src/modules/backbone/patchenc.cpp) built in oracle/_ref, its ggml operators from "
+                              "the eager stand-in oracle/shim/ggml_eager.cpp, %.1f s" % (frames, layers, secs)}
+        orc = O.Oracle()
         t0 = time.perf_counter()
         orc.pe_forward(w, layers, fr)
         secs = time.perf_counter() - t0
@@ -519,8 +531,7 @@ def cpu_pe_port(w, layers, frames):
         return {"error": str(e)[:200]}
     return {"prefill_frames_per_s": frames / secs, "cores": cores, "kind": "port",
             "sample": "one stream's %d-frame prefill, %d layers, through oracle/oracle.c (the fp32 "
-                      "restatement of src/modules/backbone/patchenc.cpp; the reference's ggml build is not "
-                      "vendored), %.1f s" % (frames, layers, secs)}
+                      "restatement of src/modules/backbone/patchenc.cpp), %.1f s" % (frames, layers, secs)}
 
 
 def measure_pe(args, local_rank, cpu_sample=False):
@@ -565,7 +576,7 @@ def measure_pe(args, local_rank, cpu_sample=False):
            "decode_ms_per_step": dec_ms / steps, "decode_patches_per_s": B * steps / (dec_ms / 1000.0),
            "dtype": "bf16"}
     if cpu_sample:
-        res["cpu_port"] = cpu_pe_port(w, 24, prefill)
+        res["cpu_baseline"] = cpu_pe_baseline(w, 24, prefill)
     return res
 
 
