@@ -13,6 +13,9 @@ namespace dtts {
 
 typedef __nv_bfloat16 bf16;
 
+// model widths: hidden, heads, head dim, FFN, latent, LLM hidden, speaker
+constexpr int kD = 1024, kH = 16, kHD = 64, kF = 4096, kLat = 128, kLLM = 1536, kSpk = 512;
+
 // Error codes that kernels write into the engine's device error word.
 enum DeviceError : int {
     DEVERR_NONE = 0,
@@ -62,15 +65,23 @@ struct L2WindowScope {
     ~L2WindowScope() { l2_window() = prev; }
 };
 
-// k<<<grid, block, smem, s>>>(args...), with programmatic stream
-// serialization when pdl is set (the kernel must follow the pdl_wait rule)
-// and the calling thread's L2 window, if any
+// k<<<grid, block, smem, s>>>(args...) with the calling thread's L2 window, if
+// any.  flags: kLaunchPdl (the value of `true`), programmatic stream
+// serialization (the kernel must follow the pdl_wait rule); kLaunchCoop, a
+// cooperative launch (every CTA resident at once, so its CTAs may wait on one
+// another).
+constexpr unsigned kLaunchPdl = 1u, kLaunchCoop = 2u;
 template <typename... P, typename... A>
-inline cudaError_t launch_k(bool pdl, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+inline cudaError_t launch_k(unsigned flags, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                             A &&...args) {
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     int n = 0;
-    if (pdl) {
+    if (flags & kLaunchCoop) {
+        attr[n].id = cudaLaunchAttributeCooperative;
+        attr[n].val.cooperative = 1;
+        n++;
+    }
+    if (flags & kLaunchPdl) {
         attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[n].val.programmaticStreamSerializationAllowed = 1;
         n++;
@@ -152,6 +163,14 @@ DTTS_DEV void tma_load_2d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, 
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// 1-D bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from global into this CTA's shared memory, completing on `bar`.
+DTTS_DEV void bulk_load_1d(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
 DTTS_DEV void tma_prefetch_desc(const CUtensorMap *tm) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
@@ -173,6 +192,14 @@ template <int N>
 DTTS_DEV void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory"); }
 // orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads
 DTTS_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// orders this thread's completed async-proxy (bulk) global writes before its later generic-proxy accesses
+DTTS_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// acquire load of a counter that other CTAs raise (bounded inter-CTA waits)
+DTTS_DEV unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // ----------------------------------------------------------------- tcgen05
 DTTS_DEV void tmem_alloc(uint32_t *slot, uint32_t ncols) {

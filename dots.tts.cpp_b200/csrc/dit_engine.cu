@@ -232,6 +232,16 @@ struct dtts_dit {
     uint8_t *act8 = nullptr, *att8 = nullptr, *ffn8 = nullptr;
     float *s_act = nullptr, *s_att = nullptr, *s_ffn = nullptr, *inv_ffn = nullptr, *unorm = nullptr;
     CUtensorMap t_act8, t_att8, t_ffn8;
+    // Optionally (DTTS_FUSE_LN=1 or dtts_dit_set_fused_ln) the LayerNorm +
+    // modulation after each residual GEMM runs in that GEMM's epilogue
+    // (EPI_RESID_GATED_LN): LN2 in the O projection, the next block's LN1 in
+    // FFN2.  Needs ksplit 1 and a tile width of 128 or 256.  Both forms give the
+    // same bits; the standalone kernels are the default because they are faster
+    // on B200 (the GEMM's 4-8 epilogue warps per SM normalise rows at a fraction
+    // of the rate of the LayerNorm kernel's 24).
+    bool fuse_ln = false;
+    unsigned *ln_cnt = nullptr;   // one arrival counter per 128-token block, zero at rest
+    bool ln_fused(const GemmTune &t) const { return fuse_ln && t.ks == 1 && t.bn % 128 == 0; }
     bool fp8() const { return dtype == DTTS_DTYPE_FP8; }
 
     // shapes of the last forward (for profiling) and launch accounting
@@ -326,6 +336,7 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
     ada = (float *)A(R * (size_t)cap_nfe * n_ada * 4);
     vel = (float *)A(T * kLat * 4);
     z = (float *)A(T * kLat * 4);
+    ln_cnt = (unsigned *)A((T / 128 + 1) * sizeof(unsigned));
     cond_f32 = (float *)A(R * kD * 4);
     spk_c = (float *)A(R * kD * 4);
     spk_in = (float *)A(R * kSpk * 4);
@@ -347,6 +358,7 @@ int dtts_dit::ensure_workspace(int rows, int L, int nfe) {
     }
     for (void *p : ws.ptrs)
         if (!p) { set_error("workspace allocation failed (%lld tokens)", tok); cap_tok = cap_rows = cap_L = 0; ws.free_all(); return DTTS_ERR_OOM; }
+    DTTS_CUDA(cudaMemsetAsync(ln_cnt, 0, (T / 128 + 1) * sizeof(unsigned), stream));
     bool ok = make_tmap_bf16(&t_x_in, x_in, T, kD, 128) && make_tmap_bf16(&t_act, act, T, kD, 128) &&
               make_tmap_bf16(&t_att, att, T, kD, 128) && make_tmap_bf16(&t_ffn, ffn, T, kF, 128) &&
               make_tmap_bf16(&t_acond, a_cond, R * (size_t)cap_nfe, kD, 128) && make_tmap_f32_resid(&t_h, h, T, kD);
@@ -418,6 +430,9 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
     const Layer &Ly = layers[l];
     const float *ada_l = ada_cur + (long long)l * kAdaPerLayer;
     const int tpr = L * rows_per_ada;   // tokens sharing one modulation row
+    // LN2 runs inside the O projection and LN1 of blocks after the first inside
+    // the previous block's FFN2 when those are fused
+    if ((kind == 6 && ln_fused(tu_o)) || (kind == 5 && l > 0 && ln_fused(tu_ffn2))) return DTTS_OK;
     TlScope tl_scope(this, kind == 6 ? TL_LN : kind);
     switch (kind) {
         case 5:
@@ -465,6 +480,15 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             op.tr = t_h;
             op.ep.bias = Ly.bo; op.ep.resid = h; op.ep.ldr = kD;
             op.ep.gate = ada_l + 2 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = tpr;
+            if (ln_fused(tu_o)) {   // + LN2 of this block
+                op.epi = EPI_RESID_GATED_LN;
+                op.ep.ln_count = ln_cnt;
+                op.ep.ln = ln_params(ada_l + 3 * kD, ada_l + 4 * kD, n_ada, tpr, fp8() ? (void *)act8 : (void *)act);
+                if (fp8()) {
+                    op.ep.ln.row_scale = s_act; op.ep.ln.g_scale = s_ffn; op.ep.ln.g_inv = inv_ffn;
+                    op.ep.ln.w1n = Ly.w1n; op.ep.ln.b1max = Ly.b1max;
+                }
+            }
             return gemm(op);
         }
         case 2: {
@@ -484,6 +508,13 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             op.tr = t_h;
             op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
             op.ep.gate = ada_l + 5 * kD; op.ep.gate_ld = n_ada; op.ep.tok_per_row = tpr;
+            if (l + 1 < n_layers && ln_fused(tu_ffn2)) {   // + LN1 of the next block
+                const float *ada_n = ada_l + kAdaPerLayer;
+                op.epi = EPI_RESID_GATED_LN;
+                op.ep.ln_count = ln_cnt;
+                op.ep.ln = ln_params(ada_n, ada_n + kD, n_ada, tpr, fp8() ? (void *)act8 : (void *)act);
+                if (fp8()) { op.ep.ln.row_scale = s_act; op.ep.ln.unorm = unorm; }
+            }
             return gemm(op);
         }
     }
@@ -583,6 +614,8 @@ int dtts_dit::finish(bool host_wait) {
     DTTS_CUDA(cudaMemcpy(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err) {
         cudaMemset(d_err, 0, sizeof(int));
+        // a fused LayerNorm wait that gave up leaves its block counters raised
+        if (ln_cnt) cudaMemset(ln_cnt, 0, ((size_t)cap_tok / 128 + 1) * sizeof(unsigned));
         if (err == DEVERR_NONFINITE) { set_error("non-finite velocity"); return DTTS_ERR_NONFINITE; }
         set_error("device wait limit reached (code %d)", err);
         return DTTS_ERR_TIMEOUT;
@@ -655,6 +688,10 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     DeviceGuard g(device);
     std::unique_ptr<dtts_dit> e(new dtts_dit());
     e->device = device; e->dtype = dtype; e->num_sms = nsm; e->n_layers = w->n_layers;
+    {
+        const char *fl = std::getenv("DTTS_FUSE_LN");
+        e->fuse_ln = fl && fl[0] == '1';
+    }
     if (dtype == DTTS_DTYPE_FP8) {
         // e4m3 mainloops take half the time, so the epilogue decides: eight
         // epilogue warps for the O and FFN1 tiles (sweep at 8192 tokens)
@@ -1015,6 +1052,16 @@ int dtts_dit_tune(dtts_dit *e, const char *gemm, int bn, int epi_warps, int kspl
     if (e->gexec) { cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
     e->gkey.clear();
     return e->build_weight_maps();
+}
+
+int dtts_dit_set_fused_ln(dtts_dit *e, int on) {
+    DTTS_CHECK(e, DTTS_ERR_ARG, "null argument");
+    DeviceGuard gd(e->device);
+    DTTS_CUDA(cudaStreamSynchronize(e->stream));
+    e->fuse_ln = on != 0;
+    if (e->gexec) { cudaGraphExecDestroy(e->gexec); e->gexec = nullptr; }
+    e->gkey.clear();
+    return DTTS_OK;
 }
 
 int dtts_dit_last_launch_count(dtts_dit *e, int *n) {

@@ -39,7 +39,11 @@ cudaError_t launch_one(const GemmOp &op, int num_sms, cudaStream_t s) {
     using Cfg = GemmCfg<BN, NW, EPI, F8>;
     const int units = ((op.M + Cfg::BM - 1) / Cfg::BM) * (op.N / BN) * (op.ep.ksplit > 0 ? op.ep.ksplit : 1);
     const int grid = units < num_sms ? units : num_sms;
-    return launch_k(op.pdl && pdl_enabled(), gemm_tc_kernel<BN, EPI, NW, F8>, dim3(grid), dim3(Cfg::THREADS),
+    unsigned flags = op.pdl && pdl_enabled() ? kLaunchPdl : 0u;
+    // the CTAs of the fused LayerNorm wait on one another's arrivals, so they
+    // must all be resident: a cooperative launch (without the programmatic overlap)
+    if constexpr (EPI == EPI_RESID_GATED_LN) flags = kLaunchCoop;
+    return launch_k(flags, gemm_tc_kernel<BN, EPI, NW, F8>, dim3(grid), dim3(Cfg::THREADS),
                     (size_t)Cfg::SMEM_BYTES, s, op.ta, op.tb, op.tr, op.M, op.N, op.K, op.ep);
 }
 
@@ -51,6 +55,9 @@ cudaError_t dispatch_epi_f8(const GemmOp &op, int num_sms, cudaStream_t s) {
             return op.ep.rope_mode == ROPE_ADJACENT ? launch_one<BN, EPI_QKV_ADJ, NW, 1>(op, num_sms, s)
                                                     : launch_one<BN, EPI_QKV, NW, 1>(op, num_sms, s);
         case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED, NW, 1>(op, num_sms, s);
+        case EPI_RESID_GATED_LN:
+            if constexpr (BN % 128 == 0) return launch_one<BN, EPI_RESID_GATED_LN, NW, 1>(op, num_sms, s);
+            return cudaErrorInvalidValue;
         case EPI_F32: return launch_one<BN, EPI_F32, NW, 1>(op, num_sms, s);
         case EPI_GELU_F8:
             if constexpr (BN % 128 == 0) return launch_one<BN, EPI_GELU_F8, NW, 1>(op, num_sms, s);
@@ -68,6 +75,9 @@ cudaError_t dispatch_epi(const GemmOp &op, int num_sms, cudaStream_t s) {
         case EPI_F32: return launch_one<BN, EPI_F32, NW>(op, num_sms, s);
         case EPI_RESID: return launch_one<BN, EPI_RESID, NW>(op, num_sms, s);
         case EPI_RESID_GATED: return launch_one<BN, EPI_RESID_GATED, NW>(op, num_sms, s);
+        case EPI_RESID_GATED_LN:
+            if constexpr (BN % 128 == 0) return launch_one<BN, EPI_RESID_GATED_LN, NW>(op, num_sms, s);
+            return cudaErrorInvalidValue;
         case EPI_QKV:
             return op.ep.rope_mode == ROPE_ADJACENT ? launch_one<BN, EPI_QKV_ADJ, NW>(op, num_sms, s)
                                                     : launch_one<BN, EPI_QKV, NW>(op, num_sms, s);
@@ -87,8 +97,10 @@ cudaError_t prepare_bn_f8() {
     if ((e = prepare_one<BN, NW, EPI_QKV, 1>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_QKV_ADJ, 1>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_F32, 1>()) != cudaSuccess) return e;
-    if constexpr (BN % 128 == 0)
+    if constexpr (BN % 128 == 0) {
         if ((e = prepare_one<BN, NW, EPI_GELU_F8, 1>()) != cudaSuccess) return e;
+        if ((e = prepare_one<BN, NW, EPI_RESID_GATED_LN, 1>()) != cudaSuccess) return e;
+    }
     return prepare_one<BN, NW, EPI_RESID_GATED, 1>();
 }
 
@@ -101,6 +113,8 @@ cudaError_t prepare_bn() {
     if ((e = prepare_one<BN, NW, EPI_F32>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_RESID>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_RESID_GATED>()) != cudaSuccess) return e;
+    if constexpr (BN % 128 == 0)
+        if ((e = prepare_one<BN, NW, EPI_RESID_GATED_LN>()) != cudaSuccess) return e;
     if ((e = prepare_one<BN, NW, EPI_QKV>()) != cudaSuccess) return e;
     return prepare_one<BN, NW, EPI_QKV_ADJ>();
 }
@@ -175,6 +189,14 @@ cudaError_t launch_gemm(const GemmOp &op, int num_sms, cudaStream_t s) {
     const int bk = op.f8 ? 128 : 64;
     if (op.M < 1 || op.K < bk * ks || op.K % (bk * ks) != 0 || op.N % op.bn != 0) return cudaErrorInvalidValue;
     if (ks > 1 && !is_resid(op.epi)) return cudaErrorInvalidValue;
+    if (op.epi == EPI_RESID_GATED_LN) {
+        // whole kD-wide rows, one arrival per warp of each tile, rows split evenly
+        const int num_n = op.N / op.bn;
+        if (op.N != kD || op.ep.ldr != kD || ks != 1 || op.bn % 128 != 0 || 128 % num_n != 0 || num_n > num_sms ||
+            !op.ep.ln_count || !op.ep.err || !op.ep.ln.out || !op.ep.ln.shift || !op.ep.ln.scale || op.ep.ln.tok_per_row < 1 ||
+            (op.f8 && !op.ep.ln.row_scale))
+            return cudaErrorInvalidValue;
+    }
     const int nw = op.nw == 8 ? 8 : 4;
     if (op.f8) {
         if (!op.ep.row_scale || !op.ep.col_scale) return cudaErrorInvalidValue;

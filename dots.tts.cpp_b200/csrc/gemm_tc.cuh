@@ -25,11 +25,22 @@
 // mbarrier wait is bounded (common.cuh); on expiry the CTA drains and returns
 // with an error code in the device error word.
 //
+// EPI_RESID_GATED_LN also applies the next LayerNorm + modulation to the
+// residual rows it completes.  When an epilogue warp's reduce-adds for a tile
+// have landed it arrives on the tile's 128-row block counter; arrivals wait on
+// nothing.  After its last tile the CTA's mainloop buffers are free: each
+// epilogue warp then waits (bounded) until its blocks show every arrival,
+// copies its share of their rows into those buffers with bulk copies, and
+// normalises them (ln_rows.cuh).  The launch is cooperative, so every CTA whose
+// arrivals are awaited is resident.
+//
 // Shape rules (checked on the host): N % BN == 0, K % (BK * ksplit) == 0,
 // ksplit > 1 only for EPI_RESID / EPI_RESID_GATED; rows past M are
-// zero-filled by TMA and never stored.
+// zero-filled by TMA and never stored.  EPI_RESID_GATED_LN: N = kD, ksplit 1,
+// BN 128 or 256.
 #pragma once
 #include "common.cuh"
+#include "ln_rows.cuh"
 
 namespace dtts {
 
@@ -47,6 +58,9 @@ enum EpiKind : int {
     // kernel compiles one rotation (with both in one body, the 8-warp bf16
     // kernel spilled at its 168-register cap).
     EPI_QKV_ADJ,
+    // EPI_RESID_GATED, then y = LN(resid) * (1 + scale) + shift of the rows
+    // the launch completes (ep.ln; bf16 rows, e4m3 rows when F8)
+    EPI_RESID_GATED_LN,
 };
 
 enum RopeMode : int { ROPE_HALF = 0, ROPE_ADJACENT = 1 };
@@ -83,9 +97,15 @@ struct EpiParams {
     // outside [0, M) read as zero (TMA fill), which is the zero padding of a
     // causal (or centred) time convolution over A = [time][channels].
     int tap_kb, tap_base, tap_step;
+    // EPI_RESID_GATED_LN: the LayerNorm's modulation rows and output, and one
+    // arrival counter per 128-row block (zero between launches; the last warp
+    // to leave a block's wait puts it back to zero)
+    LnParams ln;
+    unsigned *ln_count;
 };
 
-__host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || epi == EPI_RESID_GATED; }
+__host__ __device__ constexpr bool is_gated(int epi) { return epi == EPI_RESID_GATED || epi == EPI_RESID_GATED_LN; }
+__host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID || is_gated(epi); }
 __host__ __device__ constexpr bool is_qkv(int epi) { return epi == EPI_QKV || epi == EPI_QKV_ADJ; }
 
 constexpr int kRopeSmemRows = 64;   // sequences up to this length read RoPE from shared memory
@@ -263,6 +283,15 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
     }
 }
 
+// Tile index -> (M block, N block): N-block-major (consecutive CTAs share the
+// weight tile), except for EPI_RESID_GATED_LN, whose blocks then complete in
+// order (their N tiles adjacent).
+template <int EPI>
+DTTS_DEV void tile_coords(int tile, int num_m, int num_n, int &mb, int &nb) {
+    if constexpr (EPI == EPI_RESID_GATED_LN) { mb = tile / num_n; nb = tile - mb * num_n; }
+    else { nb = tile / num_m; mb = tile - nb * num_m; }
+}
+
 template <int BN, int EPI, int NW, int F8 = 0>
 __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -284,6 +313,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
     uint64_t *fin_bar = tempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    uint64_t *ln_bar = fin_bar + 2;   // EPI_RESID_GATED_LN: one per epilogue warp
+    static_assert((2 * STAGES + 6 + (EPI == EPI_RESID_GATED_LN ? NW : 0)) * 8 <= Cfg::BAR_BYTES, "barrier area");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
@@ -297,6 +328,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int a = 0; a < 2; a++) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], EPI_THREADS); }
         mbar_init(fin_bar, 1);
+        if constexpr (EPI == EPI_RESID_GATED_LN)
+            for (int w = 0; w < NW; w++) mbar_init(&ln_bar[w], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -323,7 +356,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             int npre = 0;
             if (blockIdx.x < num_units) {
                 const int tile = blockIdx.x % num_tiles, split = blockIdx.x / num_tiles;
-                const int nb = tile / num_m, kb0 = split * kblocks;
+                int mb, nb;
+                tile_coords<EPI>(tile, num_m, num_n, mb, nb);
+                const int kb0 = split * kblocks;
                 npre = kblocks < STAGES ? kblocks : STAGES;
                 for (int kb = 0; kb < npre; kb++) {
                     mbar_arrive_expect_tx(&full[kb], Cfg::STAGE_BYTES);   // B now, A after the wait
@@ -336,7 +371,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             bool ok = true;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int tile = u % num_tiles, split = u / num_tiles;
-                const int mb = tile % num_m, nb = tile / num_m;
+                int mb, nb;
+                tile_coords<EPI>(tile, num_m, num_n, mb, nb);
                 const int kb0 = split * kblocks;
                 for (int kb = 0; kb < kblocks; kb++) {
                     const bool pre = u == (int)blockIdx.x && kb < npre;   // stage == kb, phase 0, B in flight
@@ -448,7 +484,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.err, DEVERR_TIMEOUT_EPILOGUE)) break;
             tc_fence_after();
             const int tile = u % num_tiles, split = u / num_tiles;
-            const int mb = tile % num_m, nb = tile / num_m;
+            int mb, nb;
+            tile_coords<EPI>(tile, num_m, num_n, mb, nb);
             const int m_base = mb * Cfg::BM + quad * 32;
             const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(quad * 32) << 16);
             float rs = 0.f;   // e4m3 row scale of this thread's row
@@ -588,7 +625,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                 // fp32 residual (32 rows x 32 columns per warp per chunk)
                 const int m_self = m_base + lane;
                 const float4 *g4 = nullptr;
-                if constexpr (EPI == EPI_RESID_GATED)
+                if constexpr (is_gated(EPI))
                     if (m_self < M) g4 = reinterpret_cast<const float4 *>(ep.gate + (long long)(m_self / ep.tok_per_row) * ep.gate_ld);
 #pragma unroll 1
                 for (int c = half; c < BN / 32; c += CSTEP, cc++) {
@@ -596,7 +633,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                     Col32 cv;
                     col32_load<F8 != 0>(cv, ep.col_scale, split == 0 ? ep.bias : nullptr, n0);
                     float4 gq[8];
-                    if constexpr (EPI == EPI_RESID_GATED) {
+                    if constexpr (is_gated(EPI)) {
 #pragma unroll
                         for (int i = 0; i < 8; i++) gq[i] = g4 ? __ldg(g4 + (n0 >> 2) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
@@ -606,7 +643,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                     if (m_self >= M) {
 #pragma unroll
                         for (int i = 0; i < 32; i++) v[i] = 0.f;
-                    } else if constexpr (EPI == EPI_RESID_GATED) {
+                    } else if constexpr (is_gated(EPI)) {
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
                             v[4 * i + 0] *= gq[i].x; v[4 * i + 1] *= gq[i].y; v[4 * i + 2] *= gq[i].z; v[4 * i + 3] *= gq[i].w;
@@ -626,6 +663,88 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+            if constexpr (EPI == EPI_RESID_GATED_LN) {
+                // Once this warp's reduce-adds have landed, publish them and
+                // arrive on the M block's counter (one arrival per warp of each
+                // of the block's tiles).  Nothing here waits on another CTA.
+                if (lane == 0) {
+                    bulk_wait<0>();
+                    fence_proxy_async_global();
+                    __threadfence();
+                    atomicAdd(ep.ln_count + mb, 1u);
+                }
+                __syncwarp();
+            }
+        }
+        if constexpr (EPI == EPI_RESID_GATED_LN) {
+            // LayerNorm of this CTA's share of each block it worked on: rows
+            // [nb * per, (nb + 1) * per) of the block, rows_w of them per warp.
+            // Every MMA of the CTA has completed (its last accumulator was
+            // full), so the mainloop's stage buffers are free: each warp copies
+            // its rows there with bulk copies (which need no L1, unlike loads
+            // through the SM's small L1) after the block's counter shows every
+            // arrival.  The warp's staging buffers hold the modulation row.
+            constexpr int num_n_c = kD / BN;
+            constexpr int per = Cfg::BM / num_n_c;
+            constexpr int rows_w = (per + NW - 1) / NW;
+            static_assert(NW * rows_w * kD * 4 <= STAGES * Cfg::STAGE_BYTES, "LayerNorm rows fit in the stage buffers");
+            static_assert(Cfg::STAGE_BUFS * 32 * 128 >= 2 * kD * 4, "a warp's staging holds one modulation row");
+            float *rows_s = reinterpret_cast<float *>(smem) + (size_t)ew * rows_w * kD;
+            float *mod_s = reinterpret_cast<float *>(wbuf);   // [2][kD]: shift, scale
+            ModRow st{-1, mod_s, mod_s + kD};
+            const unsigned need = static_cast<unsigned>(num_n * NW);
+            uint32_t lphase = 0;
+            bool ok = !*abort_flag;
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                int mb, nb;
+                tile_coords<EPI>(u % num_tiles, num_m, num_n, mb, nb);
+                const int r_lo = mb * Cfg::BM + nb * per + ew * rows_w;
+                const int r_hi = min(min(r_lo + rows_w, mb * Cfg::BM + (nb + 1) * per), M);
+                const int nrows = r_hi - r_lo;   // may be <= 0 for a ragged last block
+                unsigned *cnt = ep.ln_count + mb;
+                int wok = 1;
+                if (lane == 0) {
+                    const unsigned long long t0 = globaltimer_ns();
+                    while (ld_acquire_u32(cnt) < need)
+                        if (globaltimer_ns() - t0 > kWaitLimitNs || *reinterpret_cast<volatile int *>(ep.err)) {
+                            wok = 0;
+                            atomicCAS(ep.err, 0, DEVERR_TIMEOUT_BARRIER);
+                            break;
+                        }
+                    if (wok) {
+                        if (nrows > 0) {
+                            fence_proxy_async_global();
+                            mbar_arrive_expect_tx(&ln_bar[ew], static_cast<uint32_t>(nrows) * kD * 4);
+                            for (int i = 0; i < nrows; i++)
+                                bulk_load_1d(rows_s + i * kD, ep.resid + (long long)(r_lo + i) * kD, kD * 4, &ln_bar[ew]);
+                        }
+                        // the last of the block's warps to leave re-arms the counter
+                        if (atomicAdd(cnt, 1u) == 2u * need - 1u) atomicExch(cnt, 0u);
+                    }
+                }
+                wok = __shfl_sync(0xffffffffu, wok, 0);
+                if (!wok) { ok = false; break; }
+                if (nrows <= 0) continue;
+                const long long mr = r_lo / ep.ln.tok_per_row;
+                if (mr != st.mr) {
+                    ln_stage_mod(ep.ln, mr, mod_s, mod_s + kD, lane);
+                    __syncwarp();
+                    st.mr = mr;
+                }
+                if (!mbar_wait(&ln_bar[ew], lphase, abort_flag, ep.err, DEVERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+                lphase ^= 1u;
+                ln_rows_smem<rows_w, F8 != 0>(rows_s, nrows, r_lo, ep.ln, st, lane);
+                // these rows' shared-memory reads before the next bulk copies overwrite them
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+            if (!ok && lane == 0) {
+                // a copy may still be in flight into shared memory: wait for it
+                // (bounded) before the CTA exits
+                const unsigned long long t0 = globaltimer_ns();
+                while (!mbar_try_wait(&ln_bar[ew], lphase))
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            }
         }
         if constexpr (is_resid(EPI)) {
             if (lane == 0) bulk_wait<0>();   // every reduce of this warp has landed

@@ -7,121 +7,46 @@
 namespace dtts {
 
 // =========================================================================
-// norms: one warp per token row of 1024 fp32 values (8 x float4 per lane)
+// norms: one warp per token row of 1024 fp32 values (8 x float4 per lane);
+// the row arithmetic is ln_rows.cuh's, shared with the fused GEMM epilogue
 // =========================================================================
-__global__ void __launch_bounds__(256, 3) ln_modulate_kernel(const float *__restrict__ x, bf16 *__restrict__ y, int M,
-                                                             const float *__restrict__ shift,
-                                                             const float *__restrict__ scale, long long ada_ld,
-                                                             int tok_per_row) {
+__global__ void __launch_bounds__(256, 3) ln_modulate_kernel(const float *__restrict__ x, int M, LnParams p) {
     pdl_wait();
     pdl_trigger();
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= M) return;
-    const long long r = row / tok_per_row;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
-    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
-    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
-    float4 v[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    const float mean = warp_sum(s) * (1.0f / kD);
-    float q = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
-        q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
-    }
-    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
-    uint2 *yr = reinterpret_cast<uint2 *>(y + (long long)row * kD);
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
-        const float o0 = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
-        const float o1 = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
-        const float o2 = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
-        const float o3 = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
-        yr[lane + 32 * j] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
-    }
+    const int row[1] = {static_cast<int>(blockIdx.x * 8 + (threadIdx.x >> 5))};
+    if (row[0] >= M) return;
+    const bool live[1] = {true};
+    ln_rows_bf16<1>(x, p, row, live, threadIdx.x & 31);
+}
+
+LnParams ln_params(const float *shift, const float *scale, long long ada_ld, int tok_per_row, void *out) {
+    LnParams p{};
+    p.shift = shift; p.scale = scale; p.ada_ld = ada_ld; p.tok_per_row = tok_per_row; p.out = out;
+    return p;
 }
 
 void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale, long long ada_ld,
                         int tok_per_row, cudaStream_t s, bool pdl) {
-    launch_k(pdl && pdl_enabled(), ln_modulate_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, shift, scale,
-             ada_ld, tok_per_row);
+    launch_k(pdl && pdl_enabled(), ln_modulate_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, M,
+             ln_params(shift, scale, ada_ld, tok_per_row, y));
 }
 
-// The same LayerNorm + modulation with an e4m3 output row: the row is scaled
-// by 448 / absmax before the conversion and row_scale = absmax / 448 is
-// written beside it.  unorm (if given) receives 1.08 |u| and, when g_scale is
-// given, the row's bound on |gelu(W1 u + b1)|, B = 1.02 max(1.08 |u| w1n +
-// b1max, 0.17), is stored as g_scale = B / 448 and g_inv = 448 / B.
-__global__ void __launch_bounds__(256, 3) ln_modulate_f8_kernel(const float *__restrict__ x, uint8_t *__restrict__ y,
-                                                                int M, const float *__restrict__ shift,
-                                                                const float *__restrict__ scale, long long ada_ld,
-                                                                int tok_per_row, float *__restrict__ row_scale,
-                                                                float *__restrict__ unorm, float *__restrict__ g_scale,
-                                                                float *__restrict__ g_inv, float w1n, float b1max) {
+// The same LayerNorm + modulation with an e4m3 output row (ln_rows_f8).
+__global__ void __launch_bounds__(256, 3) ln_modulate_f8_kernel(const float *__restrict__ x, int M, LnParams p) {
     pdl_wait();
     pdl_trigger();
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= M) return;
-    const long long r = row / tok_per_row;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (long long)row * kD);
-    const float4 *sh = reinterpret_cast<const float4 *>(shift + r * ada_ld);
-    const float4 *sc = reinterpret_cast<const float4 *>(scale + r * ada_ld);
-    float4 v[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = xr[lane + 32 * j];
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    const float mean = warp_sum(s) * (1.0f / kD);
-    float q = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
-        q += (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
-    }
-    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / kD) + 1e-5f);
-    float amax = 0.f, ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float4 a = __ldg(sh + lane + 32 * j), b = __ldg(sc + lane + 32 * j);
-        v[j].x = (v[j].x - mean) * inv * (1.0f + b.x) + a.x;
-        v[j].y = (v[j].y - mean) * inv * (1.0f + b.y) + a.y;
-        v[j].z = (v[j].z - mean) * inv * (1.0f + b.z) + a.z;
-        v[j].w = (v[j].w - mean) * inv * (1.0f + b.w) + a.w;
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
-        ss += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
-    }
-    amax = warp_max(amax);
-    const float qinv = amax > 0.f ? 448.0f / amax : 0.f;
-    uint32_t *yr = reinterpret_cast<uint32_t *>(y + (long long)row * kD);
-#pragma unroll
-    for (int j = 0; j < 8; j++)
-        yr[lane + 32 * j] = pack_e4m3x4(v[j].x * qinv, v[j].y * qinv, v[j].z * qinv, v[j].w * qinv);
-    const float nrm = sqrtf(warp_sum(ss));
-    if (lane == 0) {
-        row_scale[row] = amax / 448.0f;
-        if (unorm) unorm[row] = 1.08f * nrm;
-        if (g_scale) {
-            const float bnd = 1.02f * fmaxf(1.08f * nrm * w1n + b1max, 0.17f);
-            g_scale[row] = bnd / 448.0f;
-            g_inv[row] = 448.0f / bnd;
-        }
-    }
+    const int row[1] = {static_cast<int>(blockIdx.x * 8 + (threadIdx.x >> 5))};
+    if (row[0] >= M) return;
+    const bool live[1] = {true};
+    ln_rows_f8<1>(x, p, row, live, threadIdx.x & 31);
 }
 
 void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
                            float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl) {
-    launch_k(pdl && pdl_enabled(), ln_modulate_f8_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, y, M, shift, scale,
-             ada_ld, tok_per_row, row_scale, unorm, g_scale, g_inv, w1n, b1max);
+    LnParams p = ln_params(shift, scale, ada_ld, tok_per_row, y);
+    p.row_scale = row_scale; p.unorm = unorm; p.g_scale = g_scale; p.g_inv = g_inv; p.w1n = w1n; p.b1max = b1max;
+    launch_k(pdl && pdl_enabled(), ln_modulate_f8_kernel, dim3((M + 7) / 8), dim3(256), 0, s, x, M, p);
 }
 
 // e4m3 conversion of n values (device self-test of the rounding).

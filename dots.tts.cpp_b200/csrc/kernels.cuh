@@ -5,8 +5,6 @@
 
 namespace dtts {
 
-constexpr int kD = 1024, kH = 16, kHD = 64, kF = 4096, kLat = 128, kLLM = 1536, kSpk = 512;
-
 // ------------------------------------------------------------ GEMM (tcgen05)
 struct GemmOp {
     CUtensorMap ta, tb;
@@ -36,6 +34,7 @@ cudaError_t gemm_prepare_attributes();
 
 // ------------------------------------------------------------ norms
 // y = bf16( LN(x) * (1 + scale[row]) + shift[row] ), LN without affine, eps 1e-5.
+LnParams ln_params(const float *shift, const float *scale, long long ada_ld, int tok_per_row, void *out);
 void launch_ln_modulate(const float *x, bf16 *y, int M, const float *shift, const float *scale,
                         long long ada_ld, int tok_per_row, cudaStream_t s, bool pdl = false);
 // y = bf16( x / sqrt(mean(x^2) + 1e-6) * w )
@@ -125,7 +124,7 @@ void launch_speaker_cond(const float *spk, int n_utt, const float *w, const floa
 // a_cond[k*n + u] = bf16(SiLU(temb[k] + spk_c[u])) for k < n_t, u < n  (spk_c may be null)
 void launch_cond_rows(const float *temb, int n_t, const float *spk_c, int n, bf16 *a_cond, cudaStream_t s);
 
-// LayerNorm + modulation to e4m3 rows (DiT FP8 path), see kernels.cu.
+// LayerNorm + modulation to e4m3 rows (DiT FP8 path), see ln_rows.cuh.
 void launch_ln_modulate_f8(const float *x, uint8_t *y, int M, const float *shift, const float *scale,
                            long long ada_ld, int tok_per_row, float *row_scale, float *unorm, float *g_scale,
                            float *g_inv, float w1n, float b1max, cudaStream_t s, bool pdl = false);

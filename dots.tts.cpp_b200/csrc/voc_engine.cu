@@ -221,11 +221,6 @@ __global__ void __launch_bounds__(kPostT) voc_post_kernel(const float *__restric
 // incremented after each CTA's write; bounded wait, error code on expiry), so
 // the layers advance together without a global barrier: T + 3 dependent steps
 // instead of 4 T.  Launched cooperatively (all CTAs resident).
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 struct LstmArgs {
     const float *gin0;                 // [T][2048] layer-0 input projection + biases

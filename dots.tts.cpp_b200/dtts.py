@@ -109,7 +109,7 @@ EXPORTS = [
     "dtts_dit_create", "dtts_dit_create_from_safetensors", "dtts_dit_destroy", "dtts_dit_set_stream",
     "dtts_dit_sync", "dtts_dit_velocity", "dtts_dit_blocks", "dtts_dit_cond", "dtts_dit_set_rope", "dtts_dit_euler_solve", "dtts_dit_solve_timeline",
     "dtts_dit_profile_kernel",
-    "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_fm_create", "dtts_fm_destroy", "dtts_fm_start",
+    "dtts_dit_last_launch_count", "dtts_dit_tune", "dtts_dit_set_fused_ln", "dtts_fm_create", "dtts_fm_destroy", "dtts_fm_start",
     "dtts_fm_append_latents", "dtts_fm_append_hidden", "dtts_fm_length", "dtts_fm_read", "dtts_fm_solve", "dtts_fm_layout",
     "dtts_llm_create", "dtts_llm_destroy", "dtts_llm_set_stream", "dtts_llm_prefill", "dtts_llm_step", "dtts_llm_length",
     "dtts_voc_create", "dtts_voc_destroy", "dtts_voc_set_stream", "dtts_voc_decode", "dtts_voc_aa_filter",
@@ -186,6 +186,7 @@ def lib(path: str = LIB_PATH):
                                           C.POINTER(C.c_double)]
     L.dtts_dit_last_launch_count.argtypes = [_vp, C.POINTER(C.c_int)]
     L.dtts_dit_tune.argtypes = [_vp, C.c_char_p, C.c_int, C.c_int, C.c_int]
+    L.dtts_dit_set_fused_ln.argtypes = [_vp, C.c_int]
     L.dtts_attn_create.argtypes = [C.POINTER(AttnW), C.c_int, C.c_int, C.POINTER(_vp)]
     L.dtts_attn_destroy.argtypes = [_vp]
     L.dtts_attn_forward.argtypes = [_vp, _fp, C.c_int, C.c_int, _u8p, _fp, _fp]
@@ -417,6 +418,10 @@ class DiT:
 
     def tune(self, gemm, bn, epi_warps=4, ksplit=1):
         check(lib().dtts_dit_tune(self.h, gemm.encode(), bn, epi_warps, ksplit))
+
+    def set_fused_ln(self, on):
+        """LayerNorm + modulation in the residual GEMMs' epilogue (True) or as separate kernels."""
+        check(lib().dtts_dit_set_fused_ln(self.h, 1 if on else 0))
 
     def last_launch_count(self):
         n = C.c_int()

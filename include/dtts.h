@@ -262,6 +262,16 @@ int dtts_dit_profile_kernel(dtts_dit *e, int kind, int iters, float *us_per_laun
  * partial sums reach the residual in run-dependent order, so repeated runs
  * may differ in the last bits.  Defaults (ksplit 1) are tuned for B200. */
 int dtts_dit_tune(dtts_dit *e, const char *gemm, int bn, int epi_warps, int ksplit);
+/* on = 1: the LayerNorm + adaLN modulation that follows each gated residual
+ * (dit_manual.h:158-168) runs in the epilogue of the residual GEMM itself, LN2
+ * in the O projection and the next block's LN1 in FFN2.  on = 0 (the default,
+ * unless DTTS_FUSE_LN=1 is set when the engine is created): standalone
+ * LayerNorm kernels, which are faster on B200.  Both give identical results.
+ * The fused form needs the residual GEMMs at ksplit 1 with a tile width of 128
+ * or 256 (dtts_dit_tune) and falls back to the standalone kernels otherwise.
+ * It is a cooperative launch whose CTAs wait on one another's arrivals
+ * (bounded, DTTS_ERR_TIMEOUT on expiry). */
+int dtts_dit_set_fused_ln(dtts_dit *e, int on);
 /* Kernel launches enqueued by the last solve / velocity call (all engine kernels). */
 int dtts_dit_last_launch_count(dtts_dit *e, int *n);
 
