@@ -38,7 +38,8 @@ __global__ void __launch_bounds__(kTcThreads, 4)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, bf16 *__restrict__ out, long long ldo, int rows,
                    const uint32_t *__restrict__ mask_bits, float scale_log2, int *err, uint8_t *__restrict__ o8,
-                   float *__restrict__ o_scale, const float *__restrict__ unorm, float vbound) {
+                   float *__restrict__ o_scale, const float *__restrict__ unorm, float vbound, const bf16 *dq,
+                   const bf16 *dk, const bf16 *dv) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
@@ -85,6 +86,14 @@ __global__ void __launch_bounds__(kTcThreads, 4)
         // every wait is followed by a CTA-wide vote, so that all threads leave the loop together
         if (__syncthreads_or(!mbar_wait(full, ph, abort_flag, err, DEVERR_TIMEOUT_PRODUCER))) break;
         pending = false;
+        if (dq && pr * 128 + tid < rows * 64) {
+            // this unit is the only reader of its rows' head slices (one 128-byte
+            // line each): drop them from L2 without a write-back
+            const long long off = (long long)(pr * 128 + tid) * kD + h * kHD;
+            l2_discard_line(dq + off);
+            l2_discard_line(dk + off);
+            l2_discard_line(dv + off);
+        }
         // ---- MMA 1: S = Q K^T (K = 64 head dims: four 16-element steps of 32 bytes)
         if (tid == 0) {
             tc_fence_after();
@@ -702,9 +711,12 @@ cudaError_t launch_attention_tc(const AttnArgs &a, int *err, cudaStream_t s, boo
     const int units = (a.rows + 1) / 2 * kH;
     const int grid = units < 4 * nsm ? units : 4 * nsm;   // 4 resident CTAs per SM (49 KB, 128 TMEM columns)
     const float sl = a.scale * 1.4426950408889634f;
+    const bf16 *dq = a.discard_qkv ? reinterpret_cast<const bf16 *>(a.q) : nullptr;
+    const bf16 *dk = a.discard_qkv ? reinterpret_cast<const bf16 *>(a.k) : nullptr;
+    const bf16 *dv = a.discard_qkv ? reinterpret_cast<const bf16 *>(a.v) : nullptr;
     return launch_k(pdl && pdl_enabled(), attn_tc_kernel, dim3(grid), dim3(kTcThreads), (size_t)kTcSmem, s, tq, tk,
                     tv, reinterpret_cast<bf16 *>(a.o), (long long)a.ldo, a.rows, a.mask_bits, sl, err, a.o8, a.o_scale,
-                    a.unorm, a.vbound);
+                    a.unorm, a.vbound, dq, dk, dv);
 }
 
 bool attention_tc_long_eligible(const AttnArgs &a) {

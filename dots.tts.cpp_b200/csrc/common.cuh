@@ -194,6 +194,9 @@ DTTS_DEV void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N)
 DTTS_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // orders this thread's completed async-proxy (bulk) global writes before its later generic-proxy accesses
 DTTS_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// Invalidates the 128-byte L2 line at p (128-byte aligned) without writing it
+// back: for data no kernel will read again before it is overwritten.
+DTTS_DEV void l2_discard_line(const void *p) { asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory"); }
 // acquire load of a counter that other CTAs raise (bounded inter-CTA waits)
 DTTS_DEV unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;

@@ -242,6 +242,7 @@ struct dtts_dit {
     // on B200 (the GEMM's 4-8 epilogue warps per SM normalise rows at a fraction
     // of the rate of the LayerNorm kernel's 24).
     bool fuse_ln = false;
+    bool discard_qkv = true;   // DTTS_L2_DISCARD=0: keep the dead q / k / v lines (see AttnArgs)
     unsigned *ln_cnt = nullptr;   // one arrival counter per 128-token block, zero at rest
     bool ln_fused(const GemmTune &t) const { return fuse_ln && t.ks == 1 && t.bn % 128 == 0; }
     bool fp8() const { return dtype == DTTS_DTYPE_FP8; }
@@ -471,6 +472,7 @@ int dtts_dit::enqueue_block_op(int kind, int l, int rows, int L) {
             a.mask_bits = last_mask ? mask_bits : nullptr;
             a.scale = 1.0f / sqrtf(64.0f);
             a.err = d_err;
+            a.discard_qkv = discard_qkv;   // q, k, v are rewritten by the next block's QKV GEMM
             if (fp8()) { a.o8 = att8; a.o_scale = s_att; a.unorm = unorm; a.vbound = Ly.vbound; }
             launches++;
             launch_attention_bf16(a, stream, true);
@@ -693,6 +695,8 @@ int dtts_dit_create(const dtts_dit_weights *w, int dtype, int device, dtts_dit *
     {
         const char *fl = std::getenv("DTTS_FUSE_LN");
         e->fuse_ln = fl && fl[0] == '1';
+        const char *dl = std::getenv("DTTS_L2_DISCARD");
+        e->discard_qkv = !(dl && dl[0] == '0');
     }
     if (dtype == DTTS_DTYPE_FP8) {
         // e4m3 mainloops take half the time, so the epilogue decides: eight

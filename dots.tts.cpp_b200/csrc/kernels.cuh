@@ -64,6 +64,10 @@ struct AttnArgs {
     // if set (tiled kernel only): the cache length before this call is read
     // from device memory, q_pos0 = *kv_base_dev and kv_len = *kv_base_dev + Tq
     const int *kv_base_dev;
+    // the q / k / v rows are dead after this call (the DiT forward's own
+    // workspace): the tcgen05 L = 64 kernel drops their L2 lines once it has
+    // loaded them, so they are never written back to DRAM
+    int discard_qkv;
     int *err;            // device error word for bounded-wait expiry (tensor-core kernel), or nullptr
 };
 // Tq <= 64 and kv_len <= 64 take the pipelined short-sequence kernel (call
