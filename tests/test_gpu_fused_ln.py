@@ -4,7 +4,7 @@ FFN2; dtts_dit_set_fused_ln) against the standalone LayerNorm kernels
 (include/dit_manual.h:158-168 of the reference, checked against the reference
 itself by the velocity tests).  Both paths run the same per-row arithmetic, so
 the solves must be bit-identical, in bf16 and with e4m3 block weights, at batch
-shapes whose 128-token blocks take one round of the persistent GEMM, two (the
+shapes whose 128-token blocks take one wave of the persistent GEMM, two (the
 benchmark), several, a ragged last block, and with 128-wide tiles (8 tiles per
 block instead of 4).  A second fused solve checks that the per-block arrival
 counters are re-armed."""
@@ -24,9 +24,9 @@ def w18():
 
 # (utterances, FM history length, O / FFN2 tile width); L = history + 4 tokens
 CASES = [
-    (2, 60, 256),     # 256 tokens: 2 blocks, one round
-    (64, 60, 256),    # 8192 tokens (the benchmark): 64 blocks, two rounds
-    (160, 60, 256),   # 20480 tokens: 160 blocks, five rounds
+    (2, 60, 256),     # 256 tokens: 2 blocks, one wave
+    (64, 60, 256),    # 8192 tokens (the benchmark): 64 blocks, two waves
+    (160, 60, 256),   # 20480 tokens: 160 blocks, five waves
     (3, 45, 256),     # 294 tokens: the last block holds 38 rows
     (64, 60, 128),    # 8 tiles of 128 columns per block
 ]
