@@ -102,6 +102,10 @@ struct EpiParams {
     // to leave a block's wait puts it back to zero)
     LnParams ln;
     unsigned *ln_count;
+    // 1: tiles M block by M block (the N tiles of a block on neighbouring
+    // CTAs, sharing its A rows through L2), for a GEMM whose A does not stay in
+    // L2 across N passes; 0: N block by N block (neighbours share a weight tile)
+    int mb_major;
 };
 
 __host__ __device__ constexpr bool is_gated(int epi) { return epi == EPI_RESID_GATED || epi == EPI_RESID_GATED_LN; }
@@ -284,11 +288,11 @@ DTTS_DEV void qkv_head_transform(const EpiParams &ep, int m, int sect, float (&l
 }
 
 // Tile index -> (M block, N block): N-block-major (consecutive CTAs share the
-// weight tile), except for EPI_RESID_GATED_LN, whose blocks then complete in
-// order (their N tiles adjacent).
+// weight tile) or, with ep.mb_major and always for EPI_RESID_GATED_LN (whose
+// blocks then complete in order), M-block-major.
 template <int EPI>
-DTTS_DEV void tile_coords(int tile, int num_m, int num_n, int &mb, int &nb) {
-    if constexpr (EPI == EPI_RESID_GATED_LN) { mb = tile / num_n; nb = tile - mb * num_n; }
+DTTS_DEV void tile_coords(int tile, int num_m, int num_n, int mb_major, int &mb, int &nb) {
+    if (EPI == EPI_RESID_GATED_LN || mb_major) { mb = tile / num_n; nb = tile - mb * num_n; }
     else { nb = tile / num_m; mb = tile - nb * num_m; }
 }
 
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             if (blockIdx.x < num_units) {
                 const int tile = blockIdx.x % num_tiles, split = blockIdx.x / num_tiles;
                 int mb, nb;
-                tile_coords<EPI>(tile, num_m, num_n, mb, nb);
+                tile_coords<EPI>(tile, num_m, num_n, ep.mb_major, mb, nb);
                 const int kb0 = split * kblocks;
                 npre = kblocks < STAGES ? kblocks : STAGES;
                 for (int kb = 0; kb < npre; kb++) {
@@ -372,7 +376,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const int tile = u % num_tiles, split = u / num_tiles;
                 int mb, nb;
-                tile_coords<EPI>(tile, num_m, num_n, mb, nb);
+                tile_coords<EPI>(tile, num_m, num_n, ep.mb_major, mb, nb);
                 const int kb0 = split * kblocks;
                 for (int kb = 0; kb < kblocks; kb++) {
                     const bool pre = u == (int)blockIdx.x && kb < npre;   // stage == kb, phase 0, B in flight
@@ -485,7 +489,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             tc_fence_after();
             const int tile = u % num_tiles, split = u / num_tiles;
             int mb, nb;
-            tile_coords<EPI>(tile, num_m, num_n, mb, nb);
+            tile_coords<EPI>(tile, num_m, num_n, ep.mb_major, mb, nb);
             const int m_base = mb * Cfg::BM + quad * 32;
             const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(quad * 32) << 16);
             float rs = 0.f;   // e4m3 row scale of this thread's row
@@ -697,7 +701,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             bool ok = !*abort_flag;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 int mb, nb;
-                tile_coords<EPI>(u % num_tiles, num_m, num_n, mb, nb);
+                tile_coords<EPI>(u % num_tiles, num_m, num_n, ep.mb_major, mb, nb);
                 const int r_lo = mb * Cfg::BM + nb * per + ew * rows_w;
                 const int r_hi = min(min(r_lo + rows_w, mb * Cfg::BM + (nb + 1) * per), M);
                 const int nrows = r_hi - r_lo;   // may be <= 0 for a ragged last block
