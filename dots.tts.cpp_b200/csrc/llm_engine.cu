@@ -370,6 +370,9 @@ struct dtts_llm {
                 GemmOp o = op(t_ffn, small ? L.td_s : L.td, M, kLH, kLF, EPI_RESID, bn);
                 o.tr = t_h; o.ep.resid = h; o.ep.ldr = kLH;
                 o.ep.ksplit = small ? 10 : 1;
+                // prefill: the 17.5 KB-per-token activations are read once from DRAM,
+                // not once per N pass (M-block-major tiles)
+                o.ep.mb_major = small ? 0 : 1;
                 DTTS_CUDA(launch_gemm(o, num_sms, stream));
             }
         }

@@ -263,6 +263,9 @@ struct dtts_pe {
                 GemmOp op = op0(t_ffn, small ? Ly.t2_s : Ly.t2, M, kD, kF, EPI_RESID, d_err);
                 op.bn = bn;
                 op.ep.ksplit = small ? kKsF2 : 1;
+                // prefill: the 8 KB-per-token activations are read once from DRAM,
+                // not once per N pass (M-block-major tiles)
+                op.ep.mb_major = small ? 0 : 1;
                 op.tr = t_h;
                 op.ep.bias = Ly.b2; op.ep.resid = h; op.ep.ldr = kD;
                 if ((st = gemm(op))) return st;
