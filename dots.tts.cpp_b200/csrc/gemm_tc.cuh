@@ -698,6 +698,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
             ModRow st{-1, mod_s, mod_s + kD};
             const unsigned need = static_cast<unsigned>(num_n * NW);
             uint32_t lphase = 0;
+            bool pending = false;   // lane 0: copies of phase lphase issued and not yet waited for
             bool ok = !*abort_flag;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 int mb, nb;
@@ -721,6 +722,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                             mbar_arrive_expect_tx(&ln_bar[ew], static_cast<uint32_t>(nrows) * kD * 4);
                             for (int i = 0; i < nrows; i++)
                                 bulk_load_1d(rows_s + i * kD, ep.resid + (long long)(r_lo + i) * kD, kD * 4, &ln_bar[ew]);
+                            pending = true;
                         }
                         // the last of the block's warps to leave re-arms the counter
                         if (atomicAdd(cnt, 1u) == 2u * need - 1u) atomicExch(cnt, 0u);
@@ -736,14 +738,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, NW, EPI, F8>::THREADS, 1)
                     st.mr = mr;
                 }
                 if (!mbar_wait(&ln_bar[ew], lphase, abort_flag, ep.err, DEVERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+                pending = false;
                 lphase ^= 1u;
                 ln_rows_smem<rows_w, F8 != 0>(rows_s, nrows, r_lo, ep.ln, st, lane);
                 // these rows' shared-memory reads before the next bulk copies overwrite them
                 fence_proxy_async_smem();
                 __syncwarp();
             }
-            if (!ok && lane == 0) {
-                // a copy may still be in flight into shared memory: wait for it
+            if (pending && lane == 0) {
+                // copies may still be in flight into shared memory: wait for them
                 // (bounded) before the CTA exits
                 const unsigned long long t0 = globaltimer_ns();
                 while (!mbar_try_wait(&ln_bar[ew], lphase))
