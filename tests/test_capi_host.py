@@ -52,6 +52,8 @@ def test_argument_validation_without_device(dtts_mod):
     assert L.dtts_dit_velocity(None, None, None, None, None, 1, 1, 1, None, 0) == dtts.ERR_ARG
     assert L.dtts_pe_decode(None, None, 1, 4, None, 0) == dtts.ERR_ARG
     assert L.dtts_dit_euler_solve(None, None) == dtts.ERR_ARG
+    assert L.dtts_dit_set_fused_ln(None, 1) == dtts.ERR_ARG
+    assert L.dtts_dit_tune(None, b"o", 256, 8, 1) == dtts.ERR_ARG
     w = dtts.DitW()
     w.n_layers = 0
     assert L.dtts_dit_create(C.byref(w), 0, 0, C.byref(h)) == dtts.ERR_ARG
